@@ -1,0 +1,114 @@
+"""ctypes binding of libcuinf.so (include/cuinf.h).
+
+The library is loaded from this package directory only.  There is no
+fallback: if the shared library is missing or fails to load, importing the
+ops raises.
+"""
+import ctypes
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libcuinf.so")
+
+c_void_p = ctypes.c_void_p
+c_int = ctypes.c_int
+c_float = ctypes.c_float
+c_size_t = ctypes.c_size_t
+c_int64 = ctypes.c_int64
+
+
+class CuinfConfig(ctypes.Structure):
+    """Mirror of cuinf_config (include/cuinf.h)."""
+    _fields_ = [
+        ("hidden", ctypes.c_int32), ("n_layers", ctypes.c_int32), ("n_heads", ctypes.c_int32),
+        ("n_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("vocab", ctypes.c_int32),
+        ("n_dense", ctypes.c_int32), ("n_experts", ctypes.c_int32), ("top_k", ctypes.c_int32),
+        ("moe_inter", ctypes.c_int32), ("dense_inter", ctypes.c_int32), ("conv_k", ctypes.c_int32),
+        ("rope_theta", ctypes.c_float), ("norm_eps", ctypes.c_float),
+        ("attn_layer", ctypes.c_uint8 * 64),
+    ]
+
+
+# name -> (restype, argtypes)
+_SIGS = {
+    "cuinf_last_error": (ctypes.c_char_p, []),
+    "cuinf_version": (ctypes.c_char_p, []),
+    "cuinf_gemv_int4": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "cuinf_gemv_fp16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "cuinf_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]),
+    "cuinf_rope": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_void_p]),
+    "cuinf_kv_write_tail": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                                    c_void_p]),
+    "cuinf_kv_commit_group": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      c_int, c_int, c_int, c_void_p]),
+    "cuinf_attn_decode_workspace_size": (c_size_t, [c_int, c_int, c_int]),
+    "cuinf_attn_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_int, c_int, c_float, c_void_p, c_int, c_int, c_void_p,
+                                  c_size_t, c_void_p]),
+    "cuinf_conv_pre": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "cuinf_conv_apply": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                 c_void_p]),
+    "cuinf_conv_update_state": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "cuinf_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    "cuinf_acc_scaled": (c_int, [c_void_p, c_void_p, c_float, c_int, c_void_p]),
+    "cuinf_add_inplace": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+    "cuinf_add_f32_inplace": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+    "cuinf_f32_to_f16": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+    "cuinf_embed_gather": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "cuinf_argmax": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "cuinf_moe_route": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
+                                c_void_p]),
+    "cuinf_moe_ffn": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                              c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "cuinf_quantize_int4": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
+    "cuinf_quantize_int4_host": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
+    "cuinf_default_config": (None, [ctypes.POINTER(CuinfConfig)]),
+    "cuinf_model_load": (c_int, [ctypes.c_char_p, ctypes.POINTER(CuinfConfig),
+                                 ctypes.POINTER(c_void_p)]),
+    "cuinf_model_from_device_blob": (c_int, [ctypes.POINTER(CuinfConfig), c_void_p, c_size_t,
+                                             c_void_p, c_size_t, ctypes.POINTER(c_void_p)]),
+    "cuinf_model_free": (c_int, [c_void_p]),
+    "cuinf_session_create": (c_int, [c_void_p, c_int, c_void_p, ctypes.POINTER(c_void_p)]),
+    "cuinf_session_free": (c_int, [c_void_p]),
+    "cuinf_session_reset": (c_int, [c_void_p]),
+    "cuinf_session_pos": (c_int, [c_void_p]),
+    "cuinf_decode_step": (c_int, [c_void_p, c_int, ctypes.POINTER(c_int)]),
+    "cuinf_generate": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
+                               ctypes.POINTER(c_int)]),
+    "cuinf_session_keep_logits": (c_int, [c_void_p, c_int]),
+    "cuinf_session_logits": (c_void_p, [c_void_p]),
+    "cuinf_session_hidden": (c_void_p, [c_void_p]),
+    "cuinf_session_routes": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "cuinf_session_kernels_per_step": (c_int, [c_void_p]),
+}
+
+EXPORTS = tuple(_SIGS)
+_lib = None
+
+
+def lib():
+    """Load libcuinf.so (once).  Raises if it is absent: there is no fallback."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing; build it with `python -m cuda_inf_b200.build` "
+                "(there is no CPU fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+class CuinfError(RuntimeError):
+    pass
+
+
+def check(rc):
+    if rc != 0:
+        msg = lib().cuinf_last_error().decode(errors="replace")
+        raise CuinfError(f"cuinf error {rc}: {msg}")
+    return rc

@@ -1,0 +1,278 @@
+// Single-token flash-decoding attention over the FP8 E4M3 group-64 KV cache and
+// its fp16 tail (attn_decode_split + attn_decode_combine, src/engine.cu:396-480).
+//
+// Layout (the reference's, engine.cu:185-187, 599-603):
+//   kc8/vc8  u8   [T, nkv, 64]    committed tokens [0, committed)
+//   ksc/vsc  fp16 [T/64, nkv]     one scale per (64-token group, kv head)
+//   ktail/vtail fp16 [64, nkv, 64] tokens [committed, qpos] at t - committed
+//
+// Work decomposition: grid (nkv, nsplit), 4 warps.  A "unit" is one 64-token
+// group (the tail is the last unit).  CTA (h, sp) takes a contiguous run of
+// units of kv head h; its warps take units round-robin.  Each warp handles
+// all GQA query heads of h at once, so every K/V byte is read once.
+//   S = Q K^T : mma m16n8k16, rows = query heads (<= 16), cols = 8 keys,
+//               k = 64 dims; K converted FP8->f16 in registers (exact).
+//   O += P V  : rows = query heads, k = 16 keys, cols = 8 dims; P in f16.
+// Online softmax in base 2 with finite sentinels; per-unit V scale applied
+// to a fresh accumulator.  Partials (m, l, O) per (h, sp, query head) go to
+// the workspace; the last CTA of each kv head (atomic ticket) merges them.
+#pragma once
+#include "common.cuh"
+
+struct AttnParams {
+    const __half* q;
+    const uint8_t* kc8;
+    const uint8_t* vc8;
+    const __half* ksc;
+    const __half* vsc;
+    const __half* ktail;
+    const __half* vtail;
+    const int* pos_dev;  // when set: qpos = *pos_dev, committed = 64*((qpos+1)/64)
+    int committed, qpos;
+    float scale;
+    __half* out;
+    float* part;          // [nkv][nsplit][gqa][68]
+    unsigned* counters;   // [nkv], zero before the first launch; left zero
+    int nh, nkv, nsplit;
+};
+
+#define ATTN_PART_STRIDE 68
+#define ATTN_THREADS 128
+#define ATTN_NEG (-1.0e30f)
+
+__device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t two_bytes) {
+    __half2_raw r = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(two_bytes & 0xFFFFu), __NV_E4M3);
+    return (uint32_t)r.x | ((uint32_t)r.y << 16);
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
+    __shared__ __align__(16) float sm[4][16][ATTN_PART_STRIDE];
+    __shared__ int s_last;
+    const int h = blockIdx.x, sp = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int nkv = P.nkv, gqa = P.nh / P.nkv;
+    int qpos = P.qpos, committed = P.committed;
+    if (P.pos_dev) {
+        qpos = *P.pos_dev;
+        committed = ((qpos + 1) / CUINF_KVGROUP) * CUINF_KVGROUP;
+    }
+    const int total = qpos + 1;
+    const int tail_len = total - committed;
+    const int n_fp8 = committed / CUINF_KVGROUP;
+    const int nunits = n_fp8 + (tail_len > 0 ? 1 : 0);
+    const int ups = (nunits + P.nsplit - 1) / P.nsplit;
+    const int u0 = sp * ups, u1 = min(u0 + ups, nunits);
+    const float kfac = P.scale * 1.4426950408889634f;  // scores in base 2
+
+    // Q as the A operand: row g = query head h*gqa+g (rows >= gqa are zero).
+    uint32_t aq[4][2];
+    {
+        const bool real = g < gqa;
+        const __half* qh = P.q + (size_t)(h * gqa + (real ? g : 0)) * CUINF_HD + 16 * c;
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            uint32_t lo = *reinterpret_cast<const uint32_t*>(qh + 4 * s);
+            uint32_t hi = *reinterpret_cast<const uint32_t*>(qh + 4 * s + 2);
+            aq[s][0] = real ? lo : 0u;
+            aq[s][1] = real ? hi : 0u;
+        }
+    }
+
+    float m_run = ATTN_NEG, l_run = 0.f;
+    float O[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; j++) O[j][0] = O[j][1] = O[j][2] = O[j][3] = 0.f;
+
+    for (int u = u0 + warp; u < u1; u += 4) {
+        const bool tail = u >= n_fp8;
+        const int valid = tail ? tail_len : CUINF_KVGROUP;
+        const int kbase = u * CUINF_KVGROUP;
+        // ---- S = Q K^T for 64 keys (8 n-tiles of 8 keys) ----
+        float S[8][4];
+#pragma unroll
+        for (int jn = 0; jn < 8; jn++) {
+            S[jn][0] = S[jn][1] = S[jn][2] = S[jn][3] = 0.f;
+            const int kk = 8 * jn + g;  // key within the unit
+            uint32_t kb[8];
+            if (!tail) {
+                uint4 raw = ldg_stream(P.kc8 + ((size_t)(kbase + kk) * nkv + h) * CUINF_HD + 16 * c);
+                const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    kb[2 * i] = fp8x2_to_h2(w4[i]);
+                    kb[2 * i + 1] = fp8x2_to_h2(w4[i] >> 16);
+                }
+            } else {
+                const __half* kp = P.ktail + ((size_t)kk * nkv + h) * CUINF_HD + 16 * c;
+                uint4 r0 = *reinterpret_cast<const uint4*>(kp);
+                uint4 r1 = *reinterpret_cast<const uint4*>(kp + 8);
+                kb[0] = r0.x; kb[1] = r0.y; kb[2] = r0.z; kb[3] = r0.w;
+                kb[4] = r1.x; kb[5] = r1.y; kb[6] = r1.z; kb[7] = r1.w;
+            }
+#pragma unroll
+            for (int s = 0; s < 4; s++)
+                mma_16816(S[jn], aq[s][0], 0u, aq[s][1], 0u, kb[2 * s], kb[2 * s + 1]);
+        }
+        const float kscale = tail ? 1.0f : __half2float(P.ksc[(size_t)u * nkv + h]);
+        const float f = kscale * kfac;
+        float mx = ATTN_NEG;
+#pragma unroll
+        for (int jn = 0; jn < 8; jn++) {
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int key = 8 * jn + 2 * c + i;
+                float s = S[jn][i] * f;
+                s = key < valid ? s : ATTN_NEG;
+                S[jn][i] = s;
+                mx = fmaxf(mx, s);
+            }
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        const float alpha = exp2f(m_run - m_new);
+        float lsum = 0.f;
+#pragma unroll
+        for (int jn = 0; jn < 8; jn++) {
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int key = 8 * jn + 2 * c + i;
+                float p = key < valid ? exp2f(S[jn][i] - m_new) : 0.f;
+                S[jn][i] = p;
+                lsum += p;
+            }
+        }
+        l_run = l_run * alpha + lsum;
+        m_run = m_new;
+        // ---- tmp = P V (4 k-steps of 16 keys, 8 n-tiles of 8 dims) ----
+        float T[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; j++) T[j][0] = T[j][1] = T[j][2] = T[j][3] = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < 4; s2++) {
+            const uint32_t pa0 = pack_h2(S[2 * s2][0], S[2 * s2][1]);
+            const uint32_t pa2 = pack_h2(S[2 * s2 + 1][0], S[2 * s2 + 1][1]);
+            const int ka = 16 * s2 + 2 * c;  // keys ka, ka+1, ka+8, ka+9
+            uint32_t b0[8], b1[8];
+            if (!tail) {
+                const uint8_t* vp = P.vc8 + ((size_t)(kbase + ka) * nkv + h) * CUINF_HD + 8 * g;
+                const size_t kstride = (size_t)nkv * CUINF_HD;
+                uint2 va = ldg_stream8(vp), vb = ldg_stream8(vp + kstride);
+                uint2 vc = ldg_stream8(vp + 8 * kstride), vd = ldg_stream8(vp + 9 * kstride);
+                uint32_t r;
+                r = prmt(va.x, vb.x, 0x5140u); b0[0] = fp8x2_to_h2(r); b0[1] = fp8x2_to_h2(r >> 16);
+                r = prmt(va.x, vb.x, 0x7362u); b0[2] = fp8x2_to_h2(r); b0[3] = fp8x2_to_h2(r >> 16);
+                r = prmt(va.y, vb.y, 0x5140u); b0[4] = fp8x2_to_h2(r); b0[5] = fp8x2_to_h2(r >> 16);
+                r = prmt(va.y, vb.y, 0x7362u); b0[6] = fp8x2_to_h2(r); b0[7] = fp8x2_to_h2(r >> 16);
+                r = prmt(vc.x, vd.x, 0x5140u); b1[0] = fp8x2_to_h2(r); b1[1] = fp8x2_to_h2(r >> 16);
+                r = prmt(vc.x, vd.x, 0x7362u); b1[2] = fp8x2_to_h2(r); b1[3] = fp8x2_to_h2(r >> 16);
+                r = prmt(vc.y, vd.y, 0x5140u); b1[4] = fp8x2_to_h2(r); b1[5] = fp8x2_to_h2(r >> 16);
+                r = prmt(vc.y, vd.y, 0x7362u); b1[6] = fp8x2_to_h2(r); b1[7] = fp8x2_to_h2(r >> 16);
+            } else {
+                const __half* vp = P.vtail + ((size_t)ka * nkv + h) * CUINF_HD + 8 * g;
+                const size_t kstride = (size_t)nkv * CUINF_HD;
+                const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+                // keys beyond the tail hold stale data: zero them
+                uint4 va = ka < valid ? *reinterpret_cast<const uint4*>(vp) : z;
+                uint4 vb = ka + 1 < valid ? *reinterpret_cast<const uint4*>(vp + kstride) : z;
+                uint4 vc = ka + 8 < valid ? *reinterpret_cast<const uint4*>(vp + 8 * kstride) : z;
+                uint4 vd = ka + 9 < valid ? *reinterpret_cast<const uint4*>(vp + 9 * kstride) : z;
+                const uint32_t A4[4] = {va.x, va.y, va.z, va.w}, B4[4] = {vb.x, vb.y, vb.z, vb.w};
+                const uint32_t C4[4] = {vc.x, vc.y, vc.z, vc.w}, D4[4] = {vd.x, vd.y, vd.z, vd.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    b0[2 * i] = prmt(A4[i], B4[i], 0x5410u);
+                    b0[2 * i + 1] = prmt(A4[i], B4[i], 0x7632u);
+                    b1[2 * i] = prmt(C4[i], D4[i], 0x5410u);
+                    b1[2 * i + 1] = prmt(C4[i], D4[i], 0x7632u);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) mma_16816(T[j], pa0, 0u, pa2, 0u, b0[j], b1[j]);
+        }
+        const float vscale = tail ? 1.0f : __half2float(P.vsc[(size_t)u * nkv + h]);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            O[j][0] = O[j][0] * alpha + vscale * T[j][0];
+            O[j][1] = O[j][1] * alpha + vscale * T[j][1];
+        }
+    }
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+
+    // ---- merge the 4 warps (rows g < gqa are real) ----
+    if (g < gqa) {
+        float* row = sm[warp][g];
+        if (c == 0) { row[0] = m_run; row[1] = l_run; }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            row[4 + 16 * c + j] = O[j][0];
+            row[4 + 16 * c + 8 + j] = O[j][1];
+        }
+    }
+    __syncthreads();
+    float* part = P.part + ((size_t)(h * P.nsplit + sp) * gqa) * ATTN_PART_STRIDE;
+    for (int it = threadIdx.x; it < gqa * 64; it += blockDim.x) {
+        const int r = it >> 6, d = it & 63;
+        float mm = ATTN_NEG;
+#pragma unroll
+        for (int w = 0; w < 4; w++) mm = fmaxf(mm, sm[w][r][0]);
+        float l = 0.f, o = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const float e = exp2f(sm[w][r][0] - mm);
+            l += sm[w][r][1] * e;
+            o += sm[w][r][4 + d] * e;
+        }
+        float* pr = part + (size_t)r * ATTN_PART_STRIDE;
+        pr[4 + d] = o;
+        if (d == 0) { pr[0] = mm; pr[1] = l; }
+    }
+    // ---- last CTA of kv head h merges the splits ----
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned prev = atomicAdd(&P.counters[h], 1u);
+        s_last = prev == (unsigned)(P.nsplit - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float* hp = P.part + (size_t)h * P.nsplit * gqa * ATTN_PART_STRIDE;
+    for (int it = threadIdx.x; it < gqa * 64; it += blockDim.x) {
+        const int r = it >> 6, d = it & 63;
+        float gm = ATTN_NEG;
+        for (int s = 0; s < P.nsplit; s++) {
+            const float* pr = hp + ((size_t)s * gqa + r) * ATTN_PART_STRIDE;
+            if (__ldcg(pr + 1) > 0.f) gm = fmaxf(gm, __ldcg(pr));
+        }
+        float l = 0.f, o = 0.f;
+        for (int s = 0; s < P.nsplit; s++) {
+            const float* pr = hp + ((size_t)s * gqa + r) * ATTN_PART_STRIDE;
+            const float pl = __ldcg(pr + 1);
+            if (pl <= 0.f) continue;
+            const float e = exp2f(__ldcg(pr) - gm);
+            l += pl * e;
+            o += __ldcg(pr + 4 + d) * e;
+        }
+        P.out[(size_t)(h * gqa + r) * CUINF_HD + d] = __float2half_rn(o / l);
+    }
+    if (threadIdx.x == 0) P.counters[h] = 0u;
+}
+
+// Splits that fill the GPU: about two CTAs per SM over all kv heads.
+static inline int attn_default_nsplit(int nkv, int max_units, int num_sms) {
+    int ns = (2 * num_sms + nkv - 1) / nkv;
+    if (ns > max_units) ns = max_units;
+    if (ns < 1) ns = 1;
+    return ns;
+}

@@ -1,0 +1,275 @@
+// Shared device helpers for the sm_100a decode hot path.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/cuinf.h"
+
+#define CUINF_HD 64       // head_dim (fixed by the reference: HEAD_DIM, engine.cu:35)
+#define CUINF_KVGROUP 64  // FP8 KV commit group (KVGROUP, engine.cu:23)
+#define CUINF_QGROUP 128  // INT4 scale group along K (GROUP, engine.cu:46)
+
+// ---------------------------------------------------------------------------
+// host-side status helpers
+// ---------------------------------------------------------------------------
+#define CUINF_TRY(expr)                                         \
+    do {                                                        \
+        cudaError_t e_ = (expr);                                \
+        if (e_ != cudaSuccess) return cuinf_set_cuda_error(e_); \
+    } while (0)
+
+int cuinf_set_cuda_error(cudaError_t e);
+int cuinf_set_arg_error(const char* what);
+int cuinf_launch_status();
+
+// ---------------------------------------------------------------------------
+// loads
+// ---------------------------------------------------------------------------
+// Streaming 16-byte load of weights: read-only path, no L1 allocation.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint2 ldg_stream8(const void* p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n"
+                 : "=r"(r.x), "=r"(r.y)
+                 : "l"(p));
+    return r;
+}
+// Bulk prefetch of [p, p+bytes) into L2 (TMA unit, no completion tracking).
+// p must be 16-byte aligned and bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tensor-core fragment math (mma.sync m16n8k16, f16 in, f32 accumulate)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));  // (a & b) | c
+    return d;
+}
+__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.f16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Dequantize one 32-bit word of packed INT4 (8 nibbles, k0..k7; byte j holds
+// k=2j in its low nibble, tools/export_weights.py:74-77) into four f16x2
+// registers holding (nibble - 8), exact in fp16:
+//   h[0] = (k0,k4)  h[1] = (k1,k5)  h[2] = (k2,k6)  h[3] = (k3,k7)
+// Low nibbles are OR-ed into the mantissa of 1024.0 and 1032 is subtracted;
+// high nibbles land as 1024 + 16n and are mapped by n/16*... = t/16 - 72.
+__device__ __forceinline__ void dequant8(uint32_t w, uint32_t (&h)[4]) {
+    const uint32_t LO = 0x000F000Fu, HI = 0x00F000F0u, EX = 0x64006400u;
+    const uint32_t NEG1032 = 0xE408E408u;  // -1032.0 in both halves
+    const uint32_t SIXTEENTH = 0x2C002C00u; // 1/16
+    const uint32_t NEG72 = 0xD480D480u;     // -72.0
+    uint32_t w8 = w >> 8;
+    h[0] = hadd2_u(lop3_and_or(w, LO, EX), NEG1032);
+    h[1] = hfma2_u(lop3_and_or(w, HI, EX), SIXTEENTH, NEG72);
+    h[2] = hadd2_u(lop3_and_or(w8, LO, EX), NEG1032);
+    h[3] = hfma2_u(lop3_and_or(w8, HI, EX), SIXTEENTH, NEG72);
+}
+
+// x in "B-fragment order" for the INT4 tile core.  For group G (128 k values),
+// mma m (0..7) and lane quad c (0..3) the 4 halves at index ((G*8+m)*4+c)*4 are
+//   m even: x[k], x[k+4], x[k+1], x[k+5]     m odd: x[k+2], x[k+6], x[k+3], x[k+7]
+// with k = 128G + 32c + 8(m/2).  This matches the A-fragment slots that
+// dequant8 produces from the 16-byte chunk c of a row's group G.
+__device__ __forceinline__ void build_xB_entry(const __half* x, __half* xB, int e) {
+    int c = e & 3, m = (e >> 2) & 7, G = e >> 5;
+    int k = 128 * G + 32 * c + 8 * (m >> 1) + ((m & 1) ? 2 : 0);
+    __half* o = xB + (size_t)e * 4;
+    o[0] = x[k];
+    o[1] = x[k + 4];
+    o[2] = x[k + 1];
+    o[3] = x[k + 5];
+}
+// Same, reading x from shared memory with a float source.
+__device__ __forceinline__ void build_xB_entry_f(const float* x, __half* xB, int e) {
+    int c = e & 3, m = (e >> 2) & 7, G = e >> 5;
+    int k = 128 * G + 32 * c + 8 * (m >> 1) + ((m & 1) ? 2 : 0);
+    __half* o = xB + (size_t)e * 4;
+    o[0] = __float2half_rn(x[k]);
+    o[1] = __float2half_rn(x[k + 4]);
+    o[2] = __float2half_rn(x[k + 1]);
+    o[3] = __float2half_rn(x[k + 5]);
+}
+
+// INT4 tile core.  One warp, 16 rows [row0, row0+16) of W[N,K] (INT4 G=128
+// layout of tools/export_weights.py), groups gbeg, gbeg+gstep, ... < gend.
+// Lane (g = lane/4, c = lane%4) returns partial dot products for rows row0+g
+// (y0) and row0+g+8 (y1); all four lanes of a quad hold the same values.
+// Rows >= N are clamped for loading (their results must be discarded).
+// Per group: two 16-byte loads per lane, 8 mma.m16n8k16 with fp32
+// accumulation of (nibble-8)*x, then one fp32 FMA with the group's scale.
+template <int UNROLL>
+__device__ __forceinline__ void int4_tile_dot(const uint8_t* __restrict__ packed,
+                                              const __half* __restrict__ scales, int N, int K,
+                                              int row0, int gbeg, int gend, int gstep,
+                                              const uint2* __restrict__ xB, float& y0, float& y1) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int ra = min(row0 + g, N - 1), rb = min(row0 + g + 8, N - 1);
+    const int KG = K >> 7;
+    const uint8_t* pa = packed + (size_t)ra * (K >> 1) + c * 16;
+    const uint8_t* pb = packed + (size_t)rb * (K >> 1) + c * 16;
+    const __half* sa = scales + (size_t)ra * KG;
+    const __half* sb = scales + (size_t)rb * KG;
+    for (int G0 = gbeg; G0 < gend; G0 += gstep * UNROLL) {
+        uint4 wa[UNROLL], wb[UNROLL];
+        float fa[UNROLL], fb[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            int G = G0 + u * gstep;
+            if (G < gend) {
+                wa[u] = ldg_stream(pa + (size_t)G * 64);
+                wb[u] = ldg_stream(pb + (size_t)G * 64);
+                fa[u] = __half2float(sa[G]);
+                fb[u] = __half2float(sb[G]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            int G = G0 + u * gstep;
+            if (G < gend) {
+                float d[4] = {0.f, 0.f, 0.f, 0.f};
+                const uint2* xg = xB + (size_t)G * 32 + c;
+                const uint32_t wav[4] = {wa[u].x, wa[u].y, wa[u].z, wa[u].w};
+                const uint32_t wbv[4] = {wb[u].x, wb[u].y, wb[u].z, wb[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    uint32_t ha[4], hb[4];
+                    dequant8(wav[j], ha);
+                    dequant8(wbv[j], hb);
+                    uint2 b0 = xg[(2 * j) * 4];
+                    uint2 b1 = xg[(2 * j + 1) * 4];
+                    mma_16816(d, ha[0], hb[0], ha[1], hb[1], b0.x, b0.y);
+                    mma_16816(d, ha[2], hb[2], ha[3], hb[3], b1.x, b1.y);
+                }
+                y0 = fmaf(fa[u], d[0], y0);
+                y1 = fmaf(fb[u], d[2], y1);
+            }
+        }
+    }
+}
+
+// fp16-weight tile core (router gate, tied lm_head).  One warp, 16 rows,
+// k-blocks of 32 (kb = 32*i for i in [ibeg, iend) step istep).  x is in natural
+// order (fp16, shared memory).  Lane quad c loads 16 bytes = halves
+// [kb+8c, kb+8c+8) of rows g and g+8; the mma slot order equals x's order.
+template <int UNROLL>
+__device__ __forceinline__ void f16_tile_dot(const __half* __restrict__ W, int N, int K, int row0,
+                                             int ibeg, int iend, int istep,
+                                             const __half* __restrict__ xs, float& y0, float& y1) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int ra = min(row0 + g, N - 1), rb = min(row0 + g + 8, N - 1);
+    const __half* pa = W + (size_t)ra * K + c * 8;
+    const __half* pb = W + (size_t)rb * K + c * 8;
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int i0 = ibeg; i0 < iend; i0 += istep * UNROLL) {
+        uint4 wa[UNROLL], wb[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            int i = i0 + u * istep;
+            if (i < iend) {
+                wa[u] = ldg_stream(pa + (size_t)i * 32);
+                wb[u] = ldg_stream(pb + (size_t)i * 32);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            int i = i0 + u * istep;
+            if (i < iend) {
+                const uint2* xv = reinterpret_cast<const uint2*>(xs + i * 32 + c * 8);
+                uint2 b0 = xv[0], b1 = xv[1];
+                mma_16816(d, wa[u].x, wb[u].x, wa[u].y, wb[u].y, b0.x, b0.y);
+                mma_16816(d, wa[u].z, wb[u].z, wa[u].w, wb[u].w, b1.x, b1.y);
+            }
+        }
+    }
+    y0 += d[0];
+    y1 += d[2];
+}
+
+// ---------------------------------------------------------------------------
+// reductions
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide sum of one float per thread; red must hold blockDim.x/32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; i++) t += red[i];
+    return t;
+}
+
+// RMSNorm of an fp16 row held in shared memory (rmsnorm, engine.cu:131-144):
+// out[i] = half(x[i] * rsqrt(mean(x^2) + eps) * w[i]).
+__device__ __forceinline__ void rmsnorm_smem(const __half* x, const __half* __restrict__ w,
+                                             __half* out, int D, float eps, float* red) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        float v = __half2float(x[i]);
+        ss += v * v;
+    }
+    ss = block_sum(ss, red);
+    float inv = rsqrtf(ss / (float)D + eps);
+    for (int i = threadIdx.x; i < D; i += blockDim.x)
+        out[i] = __float2half_rn(__half2float(x[i]) * inv * __half2float(w[i]));
+}
+
+__device__ __forceinline__ unsigned long long umax64_dev(unsigned long long a,
+                                                        unsigned long long b) {
+    return a > b ? a : b;
+}
+
+// Order-preserving key for (value, index) argmax that reproduces argmax_kernel
+// (engine.cu:562-572, 256 threads): among equal maxima the winner has the
+// smallest index mod 256, then the smallest index.  Larger key wins.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+    uint32_t b = __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    uint32_t tie = ((uint32_t)(i & 255) << 23) | ((uint32_t)i >> 8);
+    return ((unsigned long long)b << 32) | (0xFFFFFFFFu - tie);
+}
+__device__ __forceinline__ int argmax_key_index(unsigned long long key) {
+    uint32_t tie = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu);
+    return (int)(((tie & 0x7FFFFFu) << 8) | (tie >> 23));
+}

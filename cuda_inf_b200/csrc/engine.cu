@@ -1,0 +1,797 @@
+// Decode engine: model (one device blob in the tools/export_weights.py
+// layout), session (KV cache, conv state, activations) and the per-token
+// launch chain, captured once as a CUDA graph.  Host orchestration of the
+// reference: main() in src/engine.cu:637-975 (load 664-692, buffers 711-770,
+// layer_forward 784-908, logits 932-940, decode loop 954-963).
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "attn.cuh"
+#include "engine_kernels.cuh"
+
+#define REQUIRE(cond, msg) \
+    do {                   \
+        if (!(cond)) return cuinf_set_arg_error(msg); \
+    } while (0)
+#define ST(s) ((cudaStream_t)(s))
+
+// ---------------------------------------------------------------------------
+// standalone flash-decoding attention (attn_decode_split/combine, 396-480)
+// ---------------------------------------------------------------------------
+extern "C" size_t cuinf_attn_decode_workspace_size(int nh, int nkv, int max_ctx) {
+    if (nh <= 0 || nkv <= 0 || max_ctx <= 0) return 0;
+    int units = (max_ctx + CUINF_KVGROUP - 1) / CUINF_KVGROUP + 1;
+    int ns = attn_default_nsplit(nkv, units, 148);
+    return (size_t)nkv * ns * (nh / nkv) * ATTN_PART_STRIDE * 4 + 256;
+}
+
+static std::mutex g_ws_mu;
+static void* g_ws = nullptr;
+static size_t g_ws_bytes = 0;
+
+// Library-owned scratch for calls that pass no workspace (grown on demand;
+// its first 256 bytes are the zero-initialised per-kv-head tickets).
+static int shared_workspace(size_t need, void** out, cudaStream_t st) {
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    if (g_ws_bytes < need) {
+        if (g_ws) {
+            CUINF_TRY(cudaStreamSynchronize(st));
+            CUINF_TRY(cudaFree(g_ws));
+            g_ws = nullptr;
+            g_ws_bytes = 0;
+        }
+        CUINF_TRY(cudaMalloc(&g_ws, need));
+        CUINF_TRY(cudaMemsetAsync(g_ws, 0, 256, st));
+        g_ws_bytes = need;
+    }
+    *out = g_ws;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_t* vc8,
+                                 const void* ksc, const void* vsc, const void* ktail,
+                                 const void* vtail, int committed, int qpos, float scale, void* out,
+                                 int nh, int nkv, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+    REQUIRE(q && ktail && vtail && out, "null pointer");
+    REQUIRE(nh > 0 && nkv > 0 && nh % nkv == 0 && nh / nkv <= 8, "need nh % nkv == 0, nh/nkv <= 8");
+    REQUIRE(qpos >= 0 && committed >= 0 && committed % CUINF_KVGROUP == 0, "committed % 64 == 0");
+    REQUIRE(committed <= qpos + 1 && qpos + 1 - committed <= CUINF_KVGROUP,
+            "tail length must be in [0, 64]");
+    REQUIRE(committed == 0 || (kc8 && vc8 && ksc && vsc), "null FP8 cache");
+    REQUIRE(((uintptr_t)ktail & 15) == 0 && ((uintptr_t)vtail & 15) == 0 &&
+                ((uintptr_t)kc8 & 15) == 0 && ((uintptr_t)vc8 & 15) == 0 && ((uintptr_t)q & 3) == 0,
+            "cache pointers must be 16-byte aligned");
+    const int units = committed / CUINF_KVGROUP + (qpos + 1 > committed ? 1 : 0);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int ns = attn_default_nsplit(nkv, units, sms);
+    const size_t need = (size_t)nkv * ns * (nh / nkv) * ATTN_PART_STRIDE * 4 + 256;
+    void* ws = workspace;
+    if (!ws) {
+        int rc = shared_workspace(need, &ws, ST(stream));
+        if (rc) return rc;
+    } else {
+        REQUIRE(workspace_bytes >= need, "workspace too small");
+        REQUIRE(((uintptr_t)ws & 15) == 0, "workspace must be 16-byte aligned");
+    }
+    AttnParams P;
+    P.q = (const __half*)q;
+    P.kc8 = kc8;
+    P.vc8 = vc8;
+    P.ksc = (const __half*)ksc;
+    P.vsc = (const __half*)vsc;
+    P.ktail = (const __half*)ktail;
+    P.vtail = (const __half*)vtail;
+    P.pos_dev = nullptr;
+    P.committed = committed;
+    P.qpos = qpos;
+    P.scale = scale;
+    P.out = (__half*)out;
+    P.counters = (unsigned*)ws;
+    P.part = (float*)((char*)ws + 256);
+    P.nh = nh;
+    P.nkv = nkv;
+    P.nsplit = ns;
+    if (workspace) CUINF_TRY(cudaMemsetAsync(ws, 0, 256, ST(stream)));
+    k_attn_decode<<<dim3(nkv, ns), ATTN_THREADS, 0, ST(stream)>>>(P);
+    return cuinf_launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// standalone fused MoE FFN for one token (engine.cu:877-905)
+// ---------------------------------------------------------------------------
+static size_t moe_up_smem(int H) { return (size_t)H * 4 + (160 + 32 + 256 + 32) * 4; }
+static size_t moe_down_smem(int I, int topk) { return (size_t)topk * I * 2 + 8 * topk * 16 * 4; }
+
+extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* expert_bias,
+                             const void* const* experts, void* h, int H, int I, int n_exp, int topk,
+                             int* idx, float* w, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+    REQUIRE(xn && gate && expert_bias && experts && h, "null pointer");
+    REQUIRE(H > 0 && H % 128 == 0 && I > 0 && I % 128 == 0, "H and I must be multiples of 128");
+    REQUIRE(n_exp > 0 && n_exp <= 256 && topk > 0 && topk <= 8 && topk <= n_exp,
+            "n_exp <= 256, topk <= 8");
+    const size_t need = (size_t)topk * I * 2 + 256;
+    void* ws = workspace;
+    if (!ws) {
+        int rc = shared_workspace(need + 256, &ws, ST(stream));
+        if (rc) return rc;
+        ws = (char*)ws + 256;
+    } else {
+        REQUIRE(workspace_bytes >= need, "workspace too small");
+    }
+    __half* mid = (__half*)ws;
+    int* ridx = idx ? idx : (int*)((char*)ws + (size_t)topk * I * 2);
+    float* rw = w ? w : (float*)((char*)ws + (size_t)topk * I * 2 + 128);
+    MoeUpParams U;
+    U.h = nullptr;
+    U.xn = (const __half*)xn;
+    U.norm_w = nullptr;
+    U.gate = (const __half*)gate;
+    U.bias = (const __half*)expert_bias;
+    U.experts = experts;
+    U.xn_store = nullptr;
+    U.mid = mid;
+    U.route_idx = ridx;
+    U.route_w = rw;
+    U.H = H;
+    U.I = I;
+    U.E = n_exp;
+    U.topk = topk;
+    U.eps = 0.f;
+    const int tiles = I / 16;
+    const int grid_up = ((topk * tiles + 7) / 8) * 8;
+    k_moe_up<<<grid_up, 256, moe_up_smem(H), ST(stream)>>>(U);
+    int rc = cuinf_launch_status();
+    if (rc) return rc;
+    MoeDownParams D;
+    D.mid = mid;
+    D.experts = experts;
+    D.route_idx = ridx;
+    D.route_w = rw;
+    D.h = (__half*)h;
+    D.H = H;
+    D.I = I;
+    D.topk = topk;
+    const size_t sd = moe_down_smem(I, topk);
+    if (sd > 48 * 1024)
+        CUINF_TRY(cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sd));
+    k_moe_down<<<(H + 15) / 16, 256, sd, ST(stream)>>>(D);
+    return cuinf_launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// model
+// ---------------------------------------------------------------------------
+struct TDesc {
+    uint8_t kind;
+    uint64_t offset, packed, scales;
+    int64_t d0, d1;
+};
+struct Q4 {
+    const uint8_t* p = nullptr;
+    const __half* s = nullptr;
+};
+struct LayerW {
+    const __half *op_norm = nullptr, *ffn_norm = nullptr;
+    Q4 wq, wk, wv, wo, in_proj, out_proj, w1, w3, w2;
+    const __half *q_ln = nullptr, *k_ln = nullptr, *conv_w = nullptr, *gate = nullptr,
+                 *ebias = nullptr;
+    int moe_index = -1;  // index into the expert table / route buffers
+};
+
+struct cuinf_model {
+    cuinf_config cfg;
+    uint8_t* d_blob = nullptr;
+    size_t blob_bytes = 0;
+    bool own_blob = false;
+    std::unordered_map<std::string, TDesc> idx;
+    std::vector<LayerW> L;
+    const __half *embed = nullptr, *emb_norm = nullptr;
+    void** d_experts = nullptr;  // [n_moe][E][6]
+    int n_moe = 0;
+};
+
+extern "C" void cuinf_default_config(cuinf_config* c) {
+    memset(c, 0, sizeof(*c));
+    c->hidden = 2048;
+    c->n_layers = 24;
+    c->n_heads = 32;
+    c->n_kv_heads = 8;
+    c->head_dim = 64;
+    c->vocab = 128000;
+    c->n_dense = 2;
+    c->n_experts = 32;
+    c->top_k = 4;
+    c->moe_inter = 1792;
+    c->dense_inter = 7168;
+    c->conv_k = 3;
+    c->rope_theta = 5000000.0f;
+    c->norm_eps = 1e-5f;
+    const int attn[] = {2, 6, 10, 14, 18, 21};  // ATTN_LAYER, engine.cu:50
+    for (int i : attn) c->attn_layer[i] = 1;
+}
+
+static int parse_index(cuinf_model* m, const uint8_t* b, size_t len) {
+    size_t p = 0;
+    uint32_t n;
+    if (len < 4) return cuinf_set_arg_error("index.bin truncated");
+    memcpy(&n, b, 4);
+    p = 4;
+    for (uint32_t i = 0; i < n; i++) {
+        if (p + 1 > len) return cuinf_set_arg_error("index.bin truncated");
+        uint8_t nl = b[p++];
+        if (p + nl + 1 + 40 > len) return cuinf_set_arg_error("index.bin truncated");
+        std::string name((const char*)b + p, nl);
+        p += nl;
+        TDesc t;
+        t.kind = b[p++];
+        memcpy(&t.offset, b + p, 8); p += 8;
+        memcpy(&t.packed, b + p, 8); p += 8;
+        memcpy(&t.scales, b + p, 8); p += 8;
+        memcpy(&t.d0, b + p, 8); p += 8;
+        memcpy(&t.d1, b + p, 8); p += 8;
+        m->idx[name] = t;
+    }
+    return CUINF_OK;
+}
+
+namespace {
+struct Resolver {
+    cuinf_model* m;
+    std::string err;
+    const TDesc* get(const std::string& n, int kind, int64_t d0, int64_t d1) {
+        auto it = m->idx.find(n);
+        if (it == m->idx.end()) { if (err.empty()) err = "missing tensor " + n; return nullptr; }
+        const TDesc& t = it->second;
+        if (t.kind != kind) { if (err.empty()) err = "wrong kind for " + n; return nullptr; }
+        if (t.d0 != d0 || t.d1 != d1) {
+            if (err.empty())
+                err = "shape mismatch for " + n + ": got [" + std::to_string(t.d0) + "," +
+                      std::to_string(t.d1) + "] want [" + std::to_string(d0) + "," + std::to_string(d1) + "]";
+            return nullptr;
+        }
+        if (t.offset + t.packed + t.scales > m->blob_bytes) {
+            if (err.empty()) err = "tensor " + n + " beyond weights.bin";
+            return nullptr;
+        }
+        if (t.offset % 16 != 0 || (kind == 1 && (t.offset + t.packed) % 4 != 0)) {
+            if (err.empty()) err = "tensor " + n + " not 16-byte aligned";
+            return nullptr;
+        }
+        if (kind == 1 && (t.packed != (uint64_t)(d0 * d1 / 2) || t.scales != (uint64_t)(d0 * (d1 / 128) * 2))) {
+            if (err.empty()) err = "bad INT4 sizes for " + n;
+            return nullptr;
+        }
+        return &t;
+    }
+    const __half* f16(const std::string& n, int64_t d0, int64_t d1 = 0) {
+        const TDesc* t = get(n, 0, d0, d1);
+        return t ? (const __half*)(m->d_blob + t->offset) : nullptr;
+    }
+    Q4 q4(const std::string& n, int64_t N, int64_t K) {
+        Q4 w;
+        const TDesc* t = get(n, 1, N, K);
+        if (t) {
+            w.p = m->d_blob + t->offset;
+            w.s = (const __half*)(m->d_blob + t->offset + t->packed);
+        }
+        return w;
+    }
+};
+}  // namespace
+
+static int check_config(const cuinf_config* c) {
+    REQUIRE(c->head_dim == 64, "head_dim must be 64");
+    REQUIRE(c->hidden > 0 && c->hidden % 128 == 0 && c->hidden <= 16384, "hidden % 128 == 0");
+    REQUIRE(c->n_layers > 0 && c->n_layers <= 64, "1 <= n_layers <= 64");
+    REQUIRE(c->n_heads > 0 && c->n_kv_heads > 0 && c->n_heads % c->n_kv_heads == 0 &&
+                c->n_heads / c->n_kv_heads <= 8, "GQA group must divide and be <= 8");
+    REQUIRE(c->vocab > 0, "vocab > 0");
+    REQUIRE(c->n_dense >= 0 && c->n_dense <= c->n_layers, "n_dense");
+    REQUIRE(c->n_dense == c->n_layers || (c->n_experts > 0 && c->n_experts <= 256 &&
+                                          c->top_k > 0 && c->top_k <= 8 && c->top_k <= c->n_experts),
+            "n_experts <= 256, top_k <= 8");
+    REQUIRE(c->moe_inter % 128 == 0 && c->dense_inter % 128 == 0, "inter sizes % 128 == 0");
+    REQUIRE(c->conv_k == 3, "conv kernel size must be 3");
+    return CUINF_OK;
+}
+
+static int resolve_model(cuinf_model* m) {
+    const cuinf_config& c = m->cfg;
+    const int H = c.hidden, hd = c.head_dim;
+    Resolver R{m, ""};
+    m->embed = R.f16("model.embed_tokens.weight", c.vocab, H);
+    m->emb_norm = R.f16("model.embedding_norm.weight", H);
+    m->L.assign(c.n_layers, LayerW());
+    std::vector<void*> table;
+    for (int l = 0; l < c.n_layers; l++) {
+        LayerW& L = m->L[l];
+        const std::string p = "model.layers." + std::to_string(l) + ".";
+        L.op_norm = R.f16(p + "operator_norm.weight", H);
+        L.ffn_norm = R.f16(p + "ffn_norm.weight", H);
+        if (c.attn_layer[l]) {
+            L.wq = R.q4(p + "self_attn.q_proj.weight", c.n_heads * hd, H);
+            L.wk = R.q4(p + "self_attn.k_proj.weight", c.n_kv_heads * hd, H);
+            L.wv = R.q4(p + "self_attn.v_proj.weight", c.n_kv_heads * hd, H);
+            L.wo = R.q4(p + "self_attn.out_proj.weight", H, c.n_heads * hd);
+            L.q_ln = R.f16(p + "self_attn.q_layernorm.weight", hd);
+            L.k_ln = R.f16(p + "self_attn.k_layernorm.weight", hd);
+        } else {
+            L.in_proj = R.q4(p + "conv.in_proj.weight", 3 * H, H);
+            L.out_proj = R.q4(p + "conv.out_proj.weight", H, H);
+            L.conv_w = R.f16(p + "conv.conv.weight", H, 3);
+        }
+        if (l < c.n_dense) {
+            L.w1 = R.q4(p + "feed_forward.w1.weight", c.dense_inter, H);
+            L.w3 = R.q4(p + "feed_forward.w3.weight", c.dense_inter, H);
+            L.w2 = R.q4(p + "feed_forward.w2.weight", H, c.dense_inter);
+        } else {
+            L.gate = R.f16(p + "feed_forward.gate.weight", c.n_experts, H);
+            L.ebias = R.f16(p + "feed_forward.expert_bias", c.n_experts);
+            L.moe_index = m->n_moe++;
+            for (int e = 0; e < c.n_experts; e++) {
+                const std::string ep = p + "feed_forward.experts." + std::to_string(e) + ".";
+                Q4 a = R.q4(ep + "w1.weight", c.moe_inter, H);
+                Q4 b = R.q4(ep + "w3.weight", c.moe_inter, H);
+                Q4 d = R.q4(ep + "w2.weight", H, c.moe_inter);
+                table.push_back((void*)a.p); table.push_back((void*)a.s);
+                table.push_back((void*)b.p); table.push_back((void*)b.s);
+                table.push_back((void*)d.p); table.push_back((void*)d.s);
+            }
+        }
+    }
+    if (!R.err.empty()) return cuinf_set_arg_error(R.err.c_str());
+    if (!table.empty()) {
+        CUINF_TRY(cudaMalloc(&m->d_experts, table.size() * sizeof(void*)));
+        CUINF_TRY(cudaMemcpy(m->d_experts, table.data(), table.size() * sizeof(void*),
+                             cudaMemcpyHostToDevice));
+    }
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_model_from_device_blob(const cuinf_config* cfg, void* d_blob, size_t blob_bytes,
+                                            const uint8_t* index, size_t index_bytes,
+                                            cuinf_model** out) {
+    REQUIRE(d_blob && index && out, "null pointer");
+    cuinf_config c;
+    if (cfg) c = *cfg; else cuinf_default_config(&c);
+    int rc = check_config(&c);
+    if (rc) return rc;
+    cuinf_model* m = new cuinf_model();
+    m->cfg = c;
+    m->d_blob = (uint8_t*)d_blob;
+    m->blob_bytes = blob_bytes;
+    rc = parse_index(m, index, index_bytes);
+    if (!rc) rc = resolve_model(m);
+    if (rc) { cuinf_model_free(m); return rc; }
+    *out = m;
+    return CUINF_OK;
+}
+
+static int read_file(const std::string& path, std::vector<uint8_t>& buf) {
+    FILE* f = fopen(path.c_str(), "rb");
+    if (!f) { cuinf_set_arg_error(("cannot open " + path).c_str()); return CUINF_ERR_IO; }
+    fseek(f, 0, SEEK_END);
+    long sz = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    buf.resize((size_t)sz);
+    size_t r = fread(buf.data(), 1, (size_t)sz, f);
+    fclose(f);
+    if (r != (size_t)sz) { cuinf_set_arg_error(("short read " + path).c_str()); return CUINF_ERR_IO; }
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_model_load(const char* dir, const cuinf_config* cfg, cuinf_model** out) {
+    REQUIRE(dir && out, "null pointer");
+    std::vector<uint8_t> index;
+    int rc = read_file(std::string(dir) + "/index.bin", index);
+    if (rc) return rc;
+    const std::string wp = std::string(dir) + "/weights.bin";
+    FILE* f = fopen(wp.c_str(), "rb");
+    if (!f) { cuinf_set_arg_error(("cannot open " + wp).c_str()); return CUINF_ERR_IO; }
+    fseek(f, 0, SEEK_END);
+    size_t sz = (size_t)ftell(f);
+    fseek(f, 0, SEEK_SET);
+    uint8_t* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, sz);
+    if (e != cudaSuccess) { fclose(f); return cuinf_set_cuda_error(e); }
+    const size_t chunk = 256ull << 20;  // the reference uploads in 256 MB chunks too
+    uint8_t* host = nullptr;
+    e = cudaMallocHost(&host, chunk);
+    if (e != cudaSuccess) { fclose(f); cudaFree(d); return cuinf_set_cuda_error(e); }
+    size_t done = 0;
+    while (done < sz) {
+        size_t n = fread(host, 1, std::min(chunk, sz - done), f);
+        if (n == 0) break;
+        e = cudaMemcpy(d + done, host, n, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) break;
+        done += n;
+    }
+    fclose(f);
+    cudaFreeHost(host);
+    if (e != cudaSuccess) { cudaFree(d); return cuinf_set_cuda_error(e); }
+    if (done != sz) { cudaFree(d); cuinf_set_arg_error("short read of weights.bin"); return CUINF_ERR_IO; }
+    rc = cuinf_model_from_device_blob(cfg, d, sz, index.data(), index.size(), out);
+    if (rc) { cudaFree(d); return rc; }
+    (*out)->own_blob = true;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_model_free(cuinf_model* m) {
+    if (!m) return CUINF_OK;
+    if (m->d_experts) cudaFree(m->d_experts);
+    if (m->own_blob && m->d_blob) cudaFree(m->d_blob);
+    delete m;
+    return CUINF_OK;
+}
+
+// ---------------------------------------------------------------------------
+// session
+// ---------------------------------------------------------------------------
+struct AttnState {
+    uint8_t *kc8 = nullptr, *vc8 = nullptr;
+    __half *ksc = nullptr, *vsc = nullptr, *ktail = nullptr, *vtail = nullptr;
+};
+
+struct cuinf_session {
+    cuinf_model* m = nullptr;
+    int max_ctx = 0;
+    cudaStream_t st = nullptr;
+    bool own_stream = false;
+    std::vector<void*> allocs;
+    __half *h = nullptr, *q = nullptr, *attn_out = nullptr, *conv_y = nullptr, *mid = nullptr,
+           *hidden = nullptr;
+    int *pos = nullptr, *tok = nullptr, *route_idx = nullptr, *out_ring = nullptr;
+    float *route_w = nullptr, *logits = nullptr, *attn_part = nullptr;
+    unsigned* attn_cnt = nullptr;
+    unsigned long long* am_key = nullptr;
+    unsigned* am_ticket = nullptr;
+    std::vector<AttnState> attn;
+    std::vector<__half*> conv_state;
+    int nsplit = 1;
+    int kernels_per_step = 0;
+    bool keep_logits = false;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int* pinned = nullptr;  // [0] token in, [1] token out
+    int host_pos = 0;
+    int num_sms = 148;
+};
+
+template <class T>
+static int dalloc(cuinf_session* s, T** p, size_t bytes) {
+    void* d = nullptr;
+    CUINF_TRY(cudaMalloc(&d, bytes < 16 ? 16 : bytes));
+    CUINF_TRY(cudaMemset(d, 0, bytes < 16 ? 16 : bytes));
+    s->allocs.push_back(d);
+    *p = (T*)d;
+    return CUINF_OK;
+}
+
+static size_t smem_norm_gemv(int H, int warps) { return (size_t)H * 4 + (warps * 16 + 32) * 4; }
+
+// Records one decode step into the session stream (used under capture).
+static int record_step(cuinf_session* s) {
+    const cuinf_model* m = s->m;
+    const cuinf_config& c = m->cfg;
+    const int H = c.hidden;
+    cudaStream_t st = s->st;
+    int kernels = 0;
+    for (int l = 0; l < c.n_layers; l++) {
+        const LayerW& L = m->L[l];
+        const bool first = l == 0;
+        if (c.attn_layer[l]) {
+            AttnState& A = s->attn[l];
+            QkvParams Q;
+            Q.h = s->h;
+            Q.embed = first ? m->embed : nullptr;
+            Q.tok = s->tok;
+            Q.h_store = s->h;
+            Q.norm_w = L.op_norm;
+            Q.wq_p = L.wq.p; Q.wq_s = L.wq.s;
+            Q.wk_p = L.wk.p; Q.wk_s = L.wk.s;
+            Q.wv_p = L.wv.p; Q.wv_s = L.wv.s;
+            Q.q_ln = L.q_ln;
+            Q.k_ln = L.k_ln;
+            Q.pos = s->pos;
+            Q.q_out = s->q;
+            Q.ktail = A.ktail; Q.vtail = A.vtail;
+            Q.kc8 = A.kc8; Q.vc8 = A.vc8;
+            Q.ksc = A.ksc; Q.vsc = A.vsc;
+            Q.H = H; Q.nh = c.n_heads; Q.nkv = c.n_kv_heads;
+            Q.eps = c.norm_eps; Q.theta = c.rope_theta;
+            const int heads = c.n_heads + 2 * c.n_kv_heads;
+            k_attn_qkv<<<heads * 4, 256, smem_norm_gemv(H, 8) + (16 + 64) * 4 + 128, st>>>(Q);
+            kernels++;
+            AttnParams P;
+            P.q = s->q;
+            P.kc8 = A.kc8; P.vc8 = A.vc8; P.ksc = A.ksc; P.vsc = A.vsc;
+            P.ktail = A.ktail; P.vtail = A.vtail;
+            P.pos_dev = s->pos;
+            P.committed = 0; P.qpos = 0;
+            P.scale = 1.0f / sqrtf((float)c.head_dim);
+            P.out = s->attn_out;
+            P.part = s->attn_part;
+            P.counters = s->attn_cnt;
+            P.nh = c.n_heads; P.nkv = c.n_kv_heads; P.nsplit = s->nsplit;
+            k_attn_decode<<<dim3(c.n_kv_heads, s->nsplit), ATTN_THREADS, 0, st>>>(P);
+            kernels++;
+            k_gemv_residual<<<H / 16, 256, (size_t)c.n_heads * 64 * 2 + 8 * 16 * 4, st>>>(
+                s->attn_out, L.wo.p, L.wo.s, s->h, H, c.n_heads * 64);
+            kernels++;
+        } else {
+            ConvParams C;
+            C.h = s->h;
+            C.embed = first ? m->embed : nullptr;
+            C.tok = s->tok;
+            C.h_store = s->h;
+            C.norm_w = L.op_norm;
+            C.wp = L.in_proj.p; C.ws = L.in_proj.s;
+            C.conv_w = L.conv_w;
+            C.state = s->conv_state[l];
+            C.y = s->conv_y;
+            C.H = H; C.eps = c.norm_eps;
+            k_conv_in<<<H / 16, 384, smem_norm_gemv(H, 12), st>>>(C);
+            kernels++;
+            k_gemv_residual<<<H / 16, 256, (size_t)H * 2 + 8 * 16 * 4, st>>>(s->conv_y, L.out_proj.p,
+                                                                           L.out_proj.s, s->h, H, H);
+            kernels++;
+        }
+        if (l < c.n_dense) {
+            FfnUpParams F;
+            F.h = s->h; F.norm_w = L.ffn_norm;
+            F.w1p = L.w1.p; F.w1s = L.w1.s; F.w3p = L.w3.p; F.w3s = L.w3.s;
+            F.mid = s->mid; F.H = H; F.I = c.dense_inter; F.eps = c.norm_eps;
+            k_ffn_up<<<(c.dense_inter + 15) / 16, 256, smem_norm_gemv(H, 8), st>>>(F);
+            kernels++;
+            size_t sm = (size_t)c.dense_inter * 2 + 8 * 16 * 4;
+            k_gemv_residual<<<H / 16, 256, sm, st>>>(s->mid, L.w2.p, L.w2.s, s->h, H, c.dense_inter);
+            kernels++;
+        } else {
+            const int mi = L.moe_index;
+            MoeUpParams U;
+            U.h = s->h; U.xn = nullptr; U.norm_w = L.ffn_norm;
+            U.gate = L.gate; U.bias = L.ebias;
+            U.experts = (const void* const*)(m->d_experts + (size_t)mi * c.n_experts * 6);
+            U.xn_store = nullptr;
+            U.mid = s->mid;
+            U.route_idx = s->route_idx + mi * c.top_k;
+            U.route_w = s->route_w + mi * c.top_k;
+            U.H = H; U.I = c.moe_inter; U.E = c.n_experts; U.topk = c.top_k; U.eps = c.norm_eps;
+            const int tiles = c.moe_inter / 16;
+            const int grid_up = ((c.top_k * tiles + 7) / 8) * 8;
+            k_moe_up<<<grid_up, 256, moe_up_smem(H), st>>>(U);
+            kernels++;
+            MoeDownParams D;
+            D.mid = s->mid; D.experts = U.experts;
+            D.route_idx = U.route_idx; D.route_w = U.route_w;
+            D.h = s->h; D.H = H; D.I = c.moe_inter; D.topk = c.top_k;
+            k_moe_down<<<H / 16, 256, moe_down_smem(c.moe_inter, c.top_k), st>>>(D);
+            kernels++;
+        }
+    }
+    LmHeadParams LM;
+    LM.h = s->h;
+    LM.norm_w = m->emb_norm;
+    LM.W = m->embed;
+    LM.logits = s->keep_logits ? s->logits : nullptr;
+    LM.hidden_out = s->hidden;
+    LM.key = s->am_key;
+    LM.ticket = s->am_ticket;
+    LM.tok = s->tok;
+    LM.pos = s->pos;
+    LM.out_ring = s->out_ring;
+    LM.ring = s->max_ctx;
+    LM.H = H;
+    LM.V = c.vocab;
+    LM.eps = c.norm_eps;
+    const int lm_tiles = (c.vocab + 15) / 16;
+    k_lmhead<<<(lm_tiles + 7) / 8, 256, (size_t)H * 2 + 64 * 4, st>>>(LM);
+    kernels++;
+    s->kernels_per_step = kernels;
+    return cuinf_launch_status();
+}
+
+static int build_graph(cuinf_session* s) {
+    if (s->exec) { cudaGraphExecDestroy(s->exec); s->exec = nullptr; }
+    if (s->graph) { cudaGraphDestroy(s->graph); s->graph = nullptr; }
+    CUINF_TRY(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+    int rc = record_step(s);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(s->st, &g);
+    if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+    if (e != cudaSuccess) return cuinf_set_cuda_error(e);
+    s->graph = g;
+    CUINF_TRY(cudaGraphInstantiate(&s->exec, g, 0));
+    return CUINF_OK;
+}
+
+static int set_kernel_attrs(const cuinf_config& c) {
+    const size_t sd = moe_down_smem(c.moe_inter, c.top_k);
+    if (sd > 48 * 1024)
+        CUINF_TRY(cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sd));
+    const size_t sr = (size_t)std::max(c.dense_inter, std::max(c.hidden, c.n_heads * 64)) * 2 + 8 * 16 * 4;
+    if (sr > 48 * 1024)
+        CUINF_TRY(cudaFuncSetAttribute(k_gemv_residual, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sr));
+    const size_t sn = smem_norm_gemv(c.hidden, 12) + 512;
+    if (sn > 48 * 1024) {
+        CUINF_TRY(cudaFuncSetAttribute(k_conv_in, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sn));
+        CUINF_TRY(cudaFuncSetAttribute(k_attn_qkv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sn));
+        CUINF_TRY(cudaFuncSetAttribute(k_ffn_up, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sn));
+        CUINF_TRY(cudaFuncSetAttribute(k_moe_up, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)moe_up_smem(c.hidden)));
+    }
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_session_free(cuinf_session* s) {
+    if (!s) return CUINF_OK;
+    if (s->st) cudaStreamSynchronize(s->st);
+    if (s->exec) cudaGraphExecDestroy(s->exec);
+    if (s->graph) cudaGraphDestroy(s->graph);
+    for (void* p : s->allocs) cudaFree(p);
+    if (s->pinned) cudaFreeHost(s->pinned);
+    if (s->own_stream && s->st) cudaStreamDestroy(s->st);
+    delete s;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_session_create(cuinf_model* m, int max_ctx, void* stream, cuinf_session** out) {
+    REQUIRE(m && out, "null pointer");
+    REQUIRE(max_ctx > 0 && max_ctx <= (1 << 24), "max_ctx out of range");
+    const cuinf_config& c = m->cfg;
+    cuinf_session* s = new cuinf_session();
+    s->m = m;
+    s->max_ctx = max_ctx;
+    int rc = CUINF_OK;
+#define TRYS(x) do { rc = (x); if (rc) { cuinf_session_free(s); return rc; } } while (0)
+#define TRYC(x) do { cudaError_t e_ = (x); if (e_ != cudaSuccess) { rc = cuinf_set_cuda_error(e_); cuinf_session_free(s); return rc; } } while (0)
+    if (stream) s->st = ST(stream);
+    else { TRYC(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking)); s->own_stream = true; }
+    int dev = 0;
+    TRYC(cudaGetDevice(&dev));
+    TRYC(cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, dev));
+    TRYS(set_kernel_attrs(c));
+    const int H = c.hidden, nkv = c.n_kv_heads, gqa = c.n_heads / c.n_kv_heads;
+    const size_t maxI = std::max((size_t)c.dense_inter, (size_t)c.top_k * c.moe_inter);
+    TRYS(dalloc(s, &s->h, (size_t)H * 2));
+    TRYS(dalloc(s, &s->q, (size_t)c.n_heads * 64 * 2));
+    TRYS(dalloc(s, &s->attn_out, (size_t)c.n_heads * 64 * 2));
+    TRYS(dalloc(s, &s->conv_y, (size_t)H * 2));
+    TRYS(dalloc(s, &s->mid, maxI * 2));
+    TRYS(dalloc(s, &s->hidden, (size_t)H * 2));
+    TRYS(dalloc(s, &s->pos, 16));
+    TRYS(dalloc(s, &s->tok, 16));
+    TRYS(dalloc(s, &s->out_ring, (size_t)max_ctx * 4));
+    TRYS(dalloc(s, &s->route_idx, (size_t)std::max(1, m->n_moe * c.top_k) * 4));
+    TRYS(dalloc(s, &s->route_w, (size_t)std::max(1, m->n_moe * c.top_k) * 4));
+    TRYS(dalloc(s, &s->logits, (size_t)c.vocab * 4));
+    TRYS(dalloc(s, &s->am_key, 16));
+    TRYS(dalloc(s, &s->am_ticket, 16));
+    const int units = max_ctx / CUINF_KVGROUP + 1;
+    s->nsplit = attn_default_nsplit(nkv, units, s->num_sms);
+    TRYS(dalloc(s, &s->attn_part, (size_t)nkv * s->nsplit * gqa * ATTN_PART_STRIDE * 4));
+    TRYS(dalloc(s, &s->attn_cnt, (size_t)nkv * 4));
+    s->attn.assign(c.n_layers, AttnState());
+    s->conv_state.assign(c.n_layers, nullptr);
+    const size_t row = (size_t)nkv * 64;
+    const size_t groups = (size_t)max_ctx / CUINF_KVGROUP + 2;
+    for (int l = 0; l < c.n_layers; l++) {
+        if (c.attn_layer[l]) {
+            AttnState& A = s->attn[l];
+            TRYS(dalloc(s, &A.kc8, (size_t)max_ctx * row));
+            TRYS(dalloc(s, &A.vc8, (size_t)max_ctx * row));
+            TRYS(dalloc(s, &A.ksc, groups * nkv * 2));
+            TRYS(dalloc(s, &A.vsc, groups * nkv * 2));
+            TRYS(dalloc(s, &A.ktail, (size_t)CUINF_KVGROUP * row * 2));
+            TRYS(dalloc(s, &A.vtail, (size_t)CUINF_KVGROUP * row * 2));
+        } else {
+            TRYS(dalloc(s, &s->conv_state[l], (size_t)2 * H * 2));
+        }
+    }
+    TRYC(cudaMallocHost(&s->pinned, 64));
+    TRYS(build_graph(s));
+#undef TRYS
+#undef TRYC
+    *out = s;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_session_reset(cuinf_session* s) {
+    REQUIRE(s, "null session");
+    const cuinf_config& c = s->m->cfg;
+    const size_t row = (size_t)c.n_kv_heads * 64;
+    const size_t groups = (size_t)s->max_ctx / CUINF_KVGROUP + 2;
+    for (int l = 0; l < c.n_layers; l++) {
+        if (c.attn_layer[l]) {
+            AttnState& A = s->attn[l];
+            CUINF_TRY(cudaMemsetAsync(A.kc8, 0, (size_t)s->max_ctx * row, s->st));
+            CUINF_TRY(cudaMemsetAsync(A.vc8, 0, (size_t)s->max_ctx * row, s->st));
+            CUINF_TRY(cudaMemsetAsync(A.ksc, 0, groups * c.n_kv_heads * 2, s->st));
+            CUINF_TRY(cudaMemsetAsync(A.vsc, 0, groups * c.n_kv_heads * 2, s->st));
+            CUINF_TRY(cudaMemsetAsync(A.ktail, 0, CUINF_KVGROUP * row * 2, s->st));
+            CUINF_TRY(cudaMemsetAsync(A.vtail, 0, CUINF_KVGROUP * row * 2, s->st));
+        } else {
+            CUINF_TRY(cudaMemsetAsync(s->conv_state[l], 0, (size_t)2 * c.hidden * 2, s->st));
+        }
+    }
+    CUINF_TRY(cudaMemsetAsync(s->pos, 0, 4, s->st));
+    CUINF_TRY(cudaStreamSynchronize(s->st));
+    s->host_pos = 0;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_session_pos(const cuinf_session* s) { return s ? s->host_pos : -1; }
+
+extern "C" int cuinf_decode_step(cuinf_session* s, int token, int* out_token) {
+    REQUIRE(s && s->exec, "null session");
+    REQUIRE(s->host_pos < s->max_ctx, "context full (max_ctx reached)");
+    REQUIRE(token < s->m->cfg.vocab, "token out of range");
+    if (token >= 0) {
+        s->pinned[0] = token;
+        CUINF_TRY(cudaMemcpyAsync(s->tok, &s->pinned[0], 4, cudaMemcpyHostToDevice, s->st));
+    }
+    CUINF_TRY(cudaGraphLaunch(s->exec, s->st));
+    s->host_pos++;
+    if (out_token) {
+        CUINF_TRY(cudaMemcpyAsync(&s->pinned[1], s->tok, 4, cudaMemcpyDeviceToHost, s->st));
+        CUINF_TRY(cudaStreamSynchronize(s->st));
+        *out_token = s->pinned[1];
+    }
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_generate(cuinf_session* s, const int* prompt, int n_prompt, int n_new, int eos,
+                              int* out_ids, int* n_out) {
+    REQUIRE(s && prompt && out_ids && n_out && n_prompt > 0 && n_new > 0, "bad arguments");
+    REQUIRE(s->host_pos + n_prompt + n_new - 1 <= s->max_ctx, "context too long for max_ctx");
+    int next = -1, rc;
+    for (int i = 0; i < n_prompt; i++) {
+        rc = cuinf_decode_step(s, prompt[i], i == n_prompt - 1 ? &next : nullptr);
+        if (rc) return rc;
+    }
+    int n = 0;
+    out_ids[n++] = next;
+    // engine.cu:954-963: stop after n_new tokens or at EOS
+    for (int step = 0; step < n_new - 1 && next != eos; step++) {
+        rc = cuinf_decode_step(s, -1, &next);
+        if (rc) return rc;
+        out_ids[n++] = next;
+        if (next == eos) break;
+    }
+    *n_out = n;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_session_keep_logits(cuinf_session* s, int on) {
+    REQUIRE(s, "null session");
+    if ((bool)on == s->keep_logits) return CUINF_OK;
+    CUINF_TRY(cudaStreamSynchronize(s->st));
+    s->keep_logits = on != 0;
+    return build_graph(s);
+}
+
+extern "C" const float* cuinf_session_logits(const cuinf_session* s) { return s ? s->logits : nullptr; }
+extern "C" const void* cuinf_session_hidden(const cuinf_session* s) { return s ? s->hidden : nullptr; }
+
+extern "C" int cuinf_session_routes(cuinf_session* s, int* idx, float* w) {
+    REQUIRE(s && idx && w, "null pointer");
+    const size_t n = (size_t)std::max(1, s->m->n_moe * s->m->cfg.top_k);
+    CUINF_TRY(cudaMemcpyAsync(idx, s->route_idx, n * 4, cudaMemcpyDeviceToHost, s->st));
+    CUINF_TRY(cudaMemcpyAsync(w, s->route_w, n * 4, cudaMemcpyDeviceToHost, s->st));
+    CUINF_TRY(cudaStreamSynchronize(s->st));
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_session_kernels_per_step(const cuinf_session* s) {
+    return s ? s->kernels_per_step : -1;
+}

@@ -1,0 +1,63 @@
+// MoE routing on the device, following the host loop of src/engine.cu:883-892.
+#pragma once
+#include "common.cuh"
+
+// sigmoid as the reference's host computes it: 1.f / (1.f + expf(-z)) in
+// float, with expf evaluated in double and rounded once to float.
+__device__ __forceinline__ float route_sigmoid(float z) {
+    float e = (float)exp(-(double)z);
+    return 1.0f / (1.0f + e);
+}
+
+// One warp per token; n_exp <= 32*8, topk <= 16.
+__device__ __forceinline__ void route_select_warp(const float* logits, const __half* bias, int n_exp, int topk,
+                                  int* idx, float* w) {
+    const int lane = threadIdx.x & 31;
+    float sig[8], score[8];
+    bool used[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        int e = lane + 32 * j;
+        used[j] = e >= n_exp;
+        if (e < n_exp) {
+            sig[j] = route_sigmoid(logits[e]);
+            score[j] = sig[j] + __half2float(bias[e]);
+        } else {
+            sig[j] = 0.f;
+            score[j] = -INFINITY;
+        }
+    }
+    float wsel[16];
+    int isel[16];
+    for (int t = 0; t < topk; t++) {
+        // max score, lowest index on ties (the reference scans e ascending with '>')
+        float bv = -1e30f;
+        int be = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            int e = lane + 32 * j;
+            if (!used[j] && score[j] > bv) { bv = score[j]; be = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+        }
+        float sv = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            if (lane + 32 * j == be) { used[j] = true; sv = sig[j]; }
+        sv = __shfl_sync(0xffffffffu, sv, be & 31);
+        isel[t] = be;
+        wsel[t] = sv;
+    }
+    float wsum = 0.f;
+    for (int t = 0; t < topk; t++) wsum += wsel[t];
+    if (lane == 0)
+        for (int t = 0; t < topk; t++) {
+            idx[t] = isel[t];
+            w[t] = wsel[t] / (wsum + 1e-6f);
+        }
+}
+

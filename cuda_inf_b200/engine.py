@@ -1,0 +1,117 @@
+"""Decode engine handles: Model (one device blob) and Session (KV cache,
+conv state, CUDA-graph decode step).  Mirrors main() of src/engine.cu
+(load 664-692, decode loop 928-963) over the C ABI."""
+import ctypes
+
+import torch
+
+from ._lib import CuinfConfig, check, lib
+from .weights import default_config
+
+
+class _DevArray:
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr,
+                                         "data": (ptr, False), "version": 3}
+
+
+class Model:
+    def __init__(self, handle, cfg, keepalive=None):
+        self._h = handle
+        self.cfg = cfg
+        self._keep = keepalive
+
+    @classmethod
+    def load(cls, directory, cfg=None):
+        cfg = cfg or default_config()
+        h = ctypes.c_void_p()
+        check(lib().cuinf_model_load(directory.encode(), ctypes.byref(cfg), ctypes.byref(h)))
+        return cls(h, cfg)
+
+    @classmethod
+    def from_device_blob(cls, blob, index, cfg=None):
+        cfg = cfg or default_config()
+        h = ctypes.c_void_p()
+        ib = (ctypes.c_uint8 * len(index)).from_buffer_copy(index)
+        check(lib().cuinf_model_from_device_blob(ctypes.byref(cfg), ctypes.c_void_p(blob.data_ptr()),
+                                                 blob.numel(), ib, len(index), ctypes.byref(h)))
+        return cls(h, cfg, keepalive=blob)
+
+    def close(self):
+        if self._h:
+            lib().cuinf_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Session:
+    def __init__(self, model, max_ctx, stream=None):
+        self.model = model
+        self.max_ctx = max_ctx
+        h = ctypes.c_void_p()
+        st = ctypes.c_void_p(stream.cuda_stream) if stream is not None else None
+        check(lib().cuinf_session_create(model._h, max_ctx, st, ctypes.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            lib().cuinf_session_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def pos(self):
+        return lib().cuinf_session_pos(self._h)
+
+    def reset(self):
+        check(lib().cuinf_session_reset(self._h))
+
+    def step(self, token=-1, want=True):
+        """One decode step; token < 0 feeds back the previous argmax on the
+        device.  Returns the argmax (synchronizes) when want is true."""
+        out = ctypes.c_int(-1)
+        check(lib().cuinf_decode_step(self._h, int(token), ctypes.byref(out) if want else None))
+        return out.value if want else None
+
+    def generate(self, prompt, n_new, eos=-1):
+        p = (ctypes.c_int * len(prompt))(*prompt)
+        o = (ctypes.c_int * n_new)()
+        n = ctypes.c_int(0)
+        check(lib().cuinf_generate(self._h, p, len(prompt), n_new, eos, o, ctypes.byref(n)))
+        return list(o[:n.value])
+
+    def keep_logits(self, on=True):
+        check(lib().cuinf_session_keep_logits(self._h, 1 if on else 0))
+
+    def logits(self):
+        """Device view (fp32 [vocab]) of the last step's logits (keep_logits on)."""
+        ptr = lib().cuinf_session_logits(self._h)
+        return torch.as_tensor(_DevArray(ptr, (self.model.cfg.vocab,), "<f4"), device="cuda")
+
+    def hidden(self):
+        """Device view (fp16 [hidden]) of the last step's final pre-norm hidden state."""
+        ptr = lib().cuinf_session_hidden(self._h)
+        return torch.as_tensor(_DevArray(ptr, (self.model.cfg.hidden,), "<f2"), device="cuda")
+
+    def routes(self):
+        c = self.model.cfg
+        n_moe = c.n_layers - c.n_dense
+        n = max(1, n_moe * c.top_k)
+        idx = (ctypes.c_int * n)()
+        w = (ctypes.c_float * n)()
+        check(lib().cuinf_session_routes(self._h, idx, w))
+        return list(idx), list(w)
+
+    @property
+    def kernels_per_step(self):
+        return lib().cuinf_session_kernels_per_step(self._h)

@@ -1,0 +1,201 @@
+/*
+ * cuinf — B200-native (sm_100a) quantized decode hot path of g023/cuda_inf.
+ *
+ * C ABI.  Plain pointers and sizes only.  Device pointers are CUDA device
+ * addresses owned by the caller unless stated otherwise; `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).
+ *
+ * Every function returns 0 on success, CUINF_ERR_ARG for a rejected argument
+ * or CUINF_ERR_CUDA for a CUDA error; cuinf_last_error() gives the message.
+ * Nothing here exits the process (the reference's CK() macro calls exit(1),
+ * src/engine.cu:52-53).  Launches are asynchronous on `stream`.
+ *
+ * Reference citations are src/engine.cu of g023/cuda_inf unless a tools/ file
+ * is named.  Where the reference hard-codes a dimension with a #define
+ * (H, NH, NKV, HEAD_DIM, ...; engine.cu:33-50) the entry point takes it as an
+ * argument; HEAD_DIM is fixed at 64 and the KV group at 64 tokens.
+ *
+ * fp16 data is IEEE binary16; FP8 is OCP E4M3 (the __NV_E4M3 of the reference).
+ */
+#ifndef CUINF_H
+#define CUINF_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CUINF_OK 0
+#define CUINF_ERR_ARG 1
+#define CUINF_ERR_CUDA 2
+#define CUINF_ERR_IO 3
+
+/* Message of the most recent error on the calling thread ("" if none). */
+const char* cuinf_last_error(void);
+/* Library version string. */
+const char* cuinf_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* Operators: the kernel-level signatures of src/engine.cu, plus a stream.     */
+/* ------------------------------------------------------------------------ */
+
+/* y[m,n] = sum_k x[m,k] * (nib(W[n,k]) - 8) * scale[n, k/128], fp32 out.
+ * x fp16 [M,K]; packed u8 [N,K/2] (low nibble = even k); scales fp16 [N,K/128]
+ * (tools/export_weights.py:64-79 layout); K % 128 == 0.
+ * Replaces gemv_int4 (engine.cu:83-109) + run_gemv_int4 (engine.cu:626-630). */
+int cuinf_gemv_int4(const void* x, const uint8_t* packed, const void* scales, float* y,
+                    int M, int N, int K, void* stream);
+
+/* y[m,n] = sum_k x[m,k] * W[n,k], fp16 weights, fp32 out; K % 32 == 0.
+ * Replaces gemv_fp16 (engine.cu:112-128) + run_gemv_fp16 (engine.cu:631-635). */
+int cuinf_gemv_fp16(const void* x, const void* W, float* y, int M, int N, int K, void* stream);
+
+/* out[m,:] = half(in[m,:] * rsqrt(mean(in^2) + eps) * w), in/out fp16 [M,D]
+ * (may alias).  Replaces rmsnorm (engine.cu:131-144) and, with D = 64,
+ * rmsnorm_head (engine.cu:148-158). */
+int cuinf_rmsnorm(const void* in, const void* w, void* out, int M, int D, float eps, void* stream);
+
+/* In-place NEOX RoPE on q fp16 [S,nq,64] and k fp16 [S,nk,64] at absolute
+ * positions pos (device int [S]); inv_freq = theta^(-2d/64).
+ * Replaces rope (engine.cu:161-182; theta = ROPE_THETA 5e6). */
+int cuinf_rope(void* q, void* k, const int* pos, int S, int nq, int nk, float theta, void* stream);
+
+/* Copy cnt tokens of k,v fp16 [cnt,nkv,64] into the tail at slot..slot+cnt-1.
+ * Replaces kv_write_tail (engine.cu:190-198). */
+int cuinf_kv_write_tail(const void* k, const void* v, void* ktail, void* vtail, int slot, int cnt,
+                        int nkv, void* stream);
+
+/* Commit the full 64-token tail to FP8 E4M3 at tokens dst_tok_base..+63 with
+ * one fp16 scale per kv head: scale = absmax/448 + 1e-12, stored at
+ * ksc/vsc[grp*nkv + h]; values quantized with the fp32 scale, satfinite.
+ * kc8/vc8 u8 [T,nkv,64]; ktail/vtail fp16 [64,nkv,64].
+ * Replaces kv_commit_group (engine.cu:202-228). */
+int cuinf_kv_commit_group(const void* ktail, const void* vtail, uint8_t* kc8, uint8_t* vc8,
+                          void* ksc, void* vsc, int dst_tok_base, int grp, int nkv, void* stream);
+
+/* Workspace bytes cuinf_attn_decode needs for nh query heads. */
+size_t cuinf_attn_decode_workspace_size(int nh, int nkv, int max_ctx);
+
+/* Single-token flash-decoding attention over the FP8 cache [0, committed)
+ * and the fp16 tail [committed, qpos]: out[h,:] = softmax(q_h . K^T * scale) V.
+ * q/out fp16 [nh,64]; GQA group nh/nkv.  workspace: device scratch of
+ * cuinf_attn_decode_workspace_size(nh, nkv, qpos+1) bytes, or NULL to use a
+ * library-owned buffer (allocated on first use).
+ * Replaces attn_decode_split + attn_decode_combine (engine.cu:396-480). */
+int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_t* vc8, const void* ksc,
+                      const void* vsc, const void* ktail, const void* vtail, int committed,
+                      int qpos, float scale, void* out, int nh, int nkv, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Short-conv pieces (H channels): inproj fp32 [S,3H] = B | C | x.
+ * conv_pre: C = half(C), Bx = half(B*x)            (engine.cu:483-494)
+ * conv_apply: y = half(C * (Bx[s-2]w0 + Bx[s-1]w1 + Bx[s]w2)), history from
+ *             state fp16 [2,H], w fp16 [H,3]     (engine.cu:498-512)
+ * conv_update_state: state <- last two Bx      (engine.cu:514-525) */
+int cuinf_conv_pre(const float* inproj, void* C, void* Bx, int S, int H, void* stream);
+int cuinf_conv_apply(const void* Bx, const void* C, const void* w, const void* state, void* y,
+                     int S, int H, void* stream);
+int cuinf_conv_update_state(const void* Bx, void* state, int S, int H, void* stream);
+
+/* Elementwise (engine.cu:527-559). */
+int cuinf_swiglu(const float* g, const float* u, void* out, int n, void* stream);      /* 542 */
+int cuinf_acc_scaled(void* dst, const float* src, float w, int n, void* stream);      /* 556 */
+int cuinf_add_inplace(void* a, const void* b, int n, void* stream);                   /* 527 */
+int cuinf_add_f32_inplace(void* a, const float* b, int n, void* stream);              /* 532 */
+int cuinf_f32_to_f16(const float* src, void* dst, int n, void* stream);               /* 537 */
+int cuinf_embed_gather(const void* embed, const int* ids, void* out, int S, int H,
+                       void* stream);                                                 /* 549 */
+
+/* Index of the maximum of logits[n] with argmax_kernel's tie rule
+ * (engine.cu:562-572).  out: device int. */
+int cuinf_argmax(const float* logits, int n, int* out, void* stream);
+
+/* MoE selection on the device for S tokens: sig = sigmoid(logit);
+ * score = sig + bias; top-k by score (strict '>', lowest index on ties);
+ * w = sig[sel] / (sum + 1e-6).  logits fp32 [S,n_exp], bias fp16 [n_exp];
+ * idx int [S,topk], w fp32 [S,topk].  Replaces the host loop at
+ * engine.cu:883-892 (which needs a D2H copy and a sync per MoE layer). */
+int cuinf_moe_route(const float* logits, const void* bias, int S, int n_exp, int topk, int* idx,
+                    float* w, void* stream);
+
+/* Fused MoE FFN for one token (engine.cu:877-905): xn = the ffn-normed hidden
+ * state fp16 [H]; router gate fp16 [n_exp,H]; expert_bias fp16 [n_exp];
+ * experts: device array of n_exp*6 pointers {w1.packed, w1.scales,
+ * w3.packed, w3.scales, w2.packed, w2.scales} (w1,w3 [I,H], w2 [H,I]).
+ * h fp16 [H] is updated in place: h = half(h + acc), acc accumulated in fp16
+ * over the selected experts in rank order.  idx/w (device, may be NULL)
+ * receive the routing decision.  workspace: 2*topk*I*2 bytes or NULL. */
+int cuinf_moe_ffn(const void* xn, const void* gate, const void* expert_bias,
+                  const void* const* experts, void* h, int H, int I, int n_exp, int topk,
+                  int* idx, float* w, void* workspace, size_t workspace_bytes, void* stream);
+
+/* INT4 G=128 quantizer of tools/export_weights.py:64-79, bit-exact:
+ * scale = amax/7 (fp32), q = rint(w/scale) clipped to [-7,7], nibble q+8,
+ * scale stored fp16.  Device version (w, packed, scales device pointers) and
+ * host version (host pointers).  K % 128 == 0. */
+int cuinf_quantize_int4(const float* w, int64_t N, int64_t K, uint8_t* packed, void* scales,
+                        void* stream);
+int cuinf_quantize_int4_host(const float* w, int64_t N, int64_t K, uint8_t* packed,
+                             uint16_t* scales);
+
+/* ------------------------------------------------------------------------ */
+/* Decode engine (replaces main's layer_forward / decode loop,                 */
+/* engine.cu:784-963): the model of tools/export_weights.py in one device      */
+/* blob, per-session KV/conv state, one decode step = one CUDA graph launch.   */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+    int32_t hidden, n_layers, n_heads, n_kv_heads, head_dim, vocab;
+    int32_t n_dense, n_experts, top_k, moe_inter, dense_inter, conv_k;
+    float rope_theta, norm_eps;
+    uint8_t attn_layer[64]; /* 1 = attention layer, 0 = short-conv layer */
+} cuinf_config;
+
+/* The LFM2.5-8B-A1B configuration of engine.cu:33-50. */
+void cuinf_default_config(cuinf_config* cfg);
+
+typedef struct cuinf_model cuinf_model;
+typedef struct cuinf_session cuinf_session;
+
+/* Load dir/index.bin + dir/weights.bin (tools/make_index.py format) into one
+ * device blob (engine.cu:664-692).  cfg NULL = cuinf_default_config. */
+int cuinf_model_load(const char* dir, const cuinf_config* cfg, cuinf_model** out);
+/* Wrap an existing device blob laid out like weights.bin; index = index.bin
+ * bytes (host).  The blob is not copied and must outlive the model. */
+int cuinf_model_from_device_blob(const cuinf_config* cfg, void* d_blob, size_t blob_bytes,
+                                 const uint8_t* index, size_t index_bytes, cuinf_model** out);
+int cuinf_model_free(cuinf_model* m);
+
+/* Session: KV cache (FP8 + fp16 tail) and conv state for max_ctx tokens, on
+ * `stream` (NULL = a new stream owned by the session). */
+int cuinf_session_create(cuinf_model* m, int max_ctx, void* stream, cuinf_session** out);
+int cuinf_session_free(cuinf_session* s);
+/* Clear the KV cache and conv state; position back to 0. */
+int cuinf_session_reset(cuinf_session* s);
+int cuinf_session_pos(const cuinf_session* s);
+
+/* One token through all layers + final norm + lm_head + argmax, at the
+ * session's position (then position + 1).  token >= 0 is the input token
+ * (copied host->device); token < 0 feeds back the previous step's argmax,
+ * which never leaves the device.  out_token (host, nullable) receives the
+ * argmax after a stream sync.  Asynchronous when out_token == NULL. */
+int cuinf_decode_step(cuinf_session* s, int token, int* out_token);
+/* Greedy generation like the reference's main: feed n_prompt ids, then
+ * n_new tokens (stop early on eos >= 0).  out_ids host [n_new]; returns the
+ * number generated in *n_out. */
+int cuinf_generate(cuinf_session* s, const int* prompt, int n_prompt, int n_new, int eos,
+                   int* out_ids, int* n_out);
+/* Device pointer to this session's last fp32 logits [vocab] (filled only while
+ * cuinf_session_keep_logits(s, 1) is set) and its final hidden state fp16 [H]. */
+int cuinf_session_keep_logits(cuinf_session* s, int on);
+const float* cuinf_session_logits(const cuinf_session* s);
+const void* cuinf_session_hidden(const cuinf_session* s);
+/* Host copy of the last step's routing decisions [n_moe_layers*top_k]. */
+int cuinf_session_routes(cuinf_session* s, int* idx, float* w);
+/* Number of kernels one decode step launches (for the bench's accounting). */
+int cuinf_session_kernels_per_step(const cuinf_session* s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
