@@ -76,10 +76,14 @@ _SIGS = {
     "cuinf_generate": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
                                ctypes.POINTER(c_int)]),
     "cuinf_session_keep_logits": (c_int, [c_void_p, c_int]),
+    "cuinf_session_set_option": (c_int, [c_void_p, c_int, c_int]),
+    "cuinf_device_error": (c_int, [ctypes.POINTER(ctypes.c_uint)]),
     "cuinf_session_logits": (c_void_p, [c_void_p]),
     "cuinf_session_hidden": (c_void_p, [c_void_p]),
     "cuinf_session_routes": (c_int, [c_void_p, c_void_p, c_void_p]),
     "cuinf_session_kernels_per_step": (c_int, [c_void_p]),
+    "cuinf_session_profile_step": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                           c_int, ctypes.POINTER(c_int)]),
 }
 
 EXPORTS = tuple(_SIGS)

@@ -33,12 +33,14 @@ struct AttnParams {
     __half* out;
     float* part;          // [nkv][nsplit][gqa][68]
     unsigned* counters;   // [nkv], zero before the first launch; left zero
-    int nh, nkv, nsplit;
+    int nh, nkv, nsplit;  // nsplit * (nh/nkv) <= ATTN_MAX_PARTS
+    L2Ranges next;        // weights of the following kernels, prefetched to L2
 };
 
 #define ATTN_PART_STRIDE 68
 #define ATTN_THREADS 128
 #define ATTN_NEG (-1.0e30f)
+#define ATTN_MAX_PARTS 1024
 
 __device__ __forceinline__ uint32_t fp8x2_to_h2(uint32_t two_bytes) {
     __half2_raw r = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(two_bytes & 0xFFFFu), __NV_E4M3);
@@ -60,6 +62,10 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     const int h = blockIdx.x, sp = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const int nkv = P.nkv, gqa = P.nh / P.nkv;
+    if (threadIdx.x == 0 && P.next.count)
+        l2_prefetch_share(P.next, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+    pdl_trigger();
+    pdl_wait();  // q and the cache come from the previous kernel
     int qpos = P.qpos, committed = P.committed;
     if (P.pos_dev) {
         qpos = *P.pos_dev;
@@ -247,32 +253,50 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // stage (m, l) of every split in shared memory, then one weight per split
     const float* hp = P.part + (size_t)h * P.nsplit * gqa * ATTN_PART_STRIDE;
+    float* s_m = &sm[0][0][0];                 // [nsplit*gqa]
+    float* s_l = s_m + ATTN_MAX_PARTS;         // [nsplit*gqa]
+    float* s_g = s_l + ATTN_MAX_PARTS;         // [gqa] max, [gqa] sum (at +8)
+    const int np = P.nsplit * gqa;
+    for (int i = threadIdx.x; i < np; i += blockDim.x) {
+        s_m[i] = __ldcg(hp + (size_t)i * ATTN_PART_STRIDE);
+        s_l[i] = __ldcg(hp + (size_t)i * ATTN_PART_STRIDE + 1);
+    }
+    __syncthreads();
+    if (threadIdx.x < gqa) {
+        const int r = threadIdx.x;
+        float gm = ATTN_NEG;
+        for (int sp2 = 0; sp2 < P.nsplit; sp2++)
+            if (s_l[sp2 * gqa + r] > 0.f) gm = fmaxf(gm, s_m[sp2 * gqa + r]);
+        float L = 0.f;
+        for (int sp2 = 0; sp2 < P.nsplit; sp2++) {
+            const int i = sp2 * gqa + r;
+            const float e = s_l[i] > 0.f ? exp2f(s_m[i] - gm) : 0.f;
+            s_m[i] = e;  // now the split's weight
+            L += s_l[i] * e;
+        }
+        s_g[8 + r] = L;
+    }
+    __syncthreads();
     for (int it = threadIdx.x; it < gqa * 64; it += blockDim.x) {
         const int r = it >> 6, d = it & 63;
-        float gm = ATTN_NEG;
-        for (int s = 0; s < P.nsplit; s++) {
-            const float* pr = hp + ((size_t)s * gqa + r) * ATTN_PART_STRIDE;
-            if (__ldcg(pr + 1) > 0.f) gm = fmaxf(gm, __ldcg(pr));
+        float o = 0.f;
+        for (int sp2 = 0; sp2 < P.nsplit; sp2++) {
+            const int i = sp2 * gqa + r;
+            o += s_m[i] * __ldcg(hp + (size_t)i * ATTN_PART_STRIDE + 4 + d);
         }
-        float l = 0.f, o = 0.f;
-        for (int s = 0; s < P.nsplit; s++) {
-            const float* pr = hp + ((size_t)s * gqa + r) * ATTN_PART_STRIDE;
-            const float pl = __ldcg(pr + 1);
-            if (pl <= 0.f) continue;
-            const float e = exp2f(__ldcg(pr) - gm);
-            l += pl * e;
-            o += __ldcg(pr + 4 + d) * e;
-        }
-        P.out[(size_t)(h * gqa + r) * CUINF_HD + d] = __float2half_rn(o / l);
+        P.out[(size_t)(h * gqa + r) * CUINF_HD + d] = __float2half_rn(o / s_g[8 + r]);
     }
     if (threadIdx.x == 0) P.counters[h] = 0u;
 }
 
-// Splits that fill the GPU: about two CTAs per SM over all kv heads.
-static inline int attn_default_nsplit(int nkv, int max_units, int num_sms) {
+// Splits that fill the GPU: about two CTAs per SM over all kv heads, at most
+// ATTN_MAX_PARTS (split, query head) partials per kv head.
+static inline int attn_default_nsplit(int nkv, int gqa, int max_units, int num_sms) {
     int ns = (2 * num_sms + nkv - 1) / nkv;
     if (ns > max_units) ns = max_units;
+    if (ns * gqa > ATTN_MAX_PARTS) ns = ATTN_MAX_PARTS / gqa;
     if (ns < 1) ns = 1;
     return ns;
 }

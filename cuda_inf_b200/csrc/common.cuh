@@ -49,6 +49,129 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) 
 }
 
 // ---------------------------------------------------------------------------
+// TMA bulk copies (global -> this CTA's shared memory) tracked by an mbarrier,
+// and programmatic dependent launch.  No multicast anywhere.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// dst (shared) and src (global) 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for phase `parity` of bar with an iteration limit.  On time-out the
+// flag word (if given) is set and false returned; the caller then skips its
+// math but still waits (bounded) before exiting so no copy targets freed smem.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* flag) {
+    for (int i = 0; i < (1 << 22); i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    if (flag) atomicOr(flag, 1u);
+    return false;
+}
+// PDL: let the next kernel in the stream start launching, and wait until the
+// previous kernel has completed and its writes are visible.  Both are no-ops
+// when the launch carries no programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+// Bytes of one 16-row INT4 tile staged in shared memory: packed rows then
+// their scales (K % 64 == 0 keeps every tile 16-byte aligned).
+__host__ __device__ __forceinline__ uint32_t int4_tile_bytes(int K) {
+    return 16u * (uint32_t)(K >> 1) + 16u * (uint32_t)(K >> 6);
+}
+// Thread-0 helper: TMA one full 16-row tile (rows row0..row0+15 of W[N,K])
+// into dst; returns the bytes it will deliver to bar.
+__device__ __forceinline__ uint32_t tma_tile_int4(const uint8_t* packed, const __half* scales, int K,
+                                                  int row0, uint8_t* dst, uint64_t* bar) {
+    const uint32_t pb = 16u * (uint32_t)(K >> 1), sb = 16u * (uint32_t)(K >> 6);
+    tma_load_1d(dst, packed + (size_t)row0 * (K >> 1), pb, bar);
+    tma_load_1d(dst + pb, (const uint8_t*)scales + (size_t)row0 * (K >> 6), sb, bar);
+    return pb + sb;
+}
+
+// Up to 8 byte ranges (16-byte aligned starts and sizes) to pull into L2.
+struct L2Ranges {
+    const char* p[8];
+    unsigned long long n[8];
+    int count;
+};
+
+// Part `part` of `nparts` of the concatenated ranges is prefetched into L2
+// by the calling thread, in bulk pieces of at most 64 KB.
+__device__ __forceinline__ void l2_prefetch_share(const L2Ranges& R, int part, int nparts) {
+    unsigned long long total = 0;
+    for (int i = 0; i < R.count; i++) total += R.n[i];
+    if (total == 0) return;
+    unsigned long long per = ((total + nparts - 1) / nparts + 15) & ~15ull;
+    unsigned long long beg = (unsigned long long)part * per, end = beg + per;
+    if (end > total) end = total;
+    unsigned long long base = 0;
+    for (int i = 0; i < R.count && beg < end; i++) {
+        const unsigned long long rb = base, re = base + R.n[i];
+        base = re;
+        if (re <= beg || rb >= end) continue;
+        unsigned long long a = beg > rb ? beg : rb, b = end < re ? end : re;
+        const char* p = R.p[i] + (a - rb);
+        unsigned long long len = b - a;
+        if (((uintptr_t)p & 15) != 0) continue;
+        while (len >= 16) {
+            unsigned piece = len > 65536 ? 65536u : (unsigned)(len & ~15ull);
+            prefetch_l2_bulk(p, piece);
+            p += piece;
+            len -= piece;
+        }
+    }
+}
+
+// L2 prefetch of one 16-row INT4 tile (rows are contiguous, scales follow
+// the same row order).
+__device__ __forceinline__ void l2_prefetch_tile_int4(const uint8_t* packed, const __half* scales,
+                                                      int K, int row0, int rows) {
+    const char* p = (const char*)packed + (size_t)row0 * (K >> 1);
+    const char* s = (const char*)scales + (size_t)row0 * (K >> 6);
+    const unsigned pb = (unsigned)rows * (K >> 1), sb = (unsigned)rows * (K >> 6);
+    if ((((uintptr_t)p | pb) & 15) == 0) prefetch_l2_bulk(p, pb);
+    if ((((uintptr_t)s | sb) & 15) == 0) prefetch_l2_bulk(s, sb);
+}
+
+// L2 prefetch of rows [row0, row0+rows) of an fp16 matrix [N,K] (clamped to N).
+__device__ __forceinline__ void l2_prefetch_bulk_rows(const __half* W, int N, int K, int row0, int rows) {
+    const int r1 = min(row0 + rows, N);
+    if (r1 <= row0) return;
+    const char* p = (const char*)(W + (size_t)row0 * K);
+    unsigned long long len = (unsigned long long)(r1 - row0) * K * 2;
+    if (((uintptr_t)p & 15) != 0) return;
+    while (len >= 16) {
+        unsigned piece = len > 65536 ? 65536u : (unsigned)(len & ~15ull);
+        prefetch_l2_bulk(p, piece);
+        p += piece;
+        len -= piece;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // tensor-core fragment math (mma.sync m16n8k16, f16 in, f32 accumulate)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -176,6 +299,58 @@ __device__ __forceinline__ void int4_tile_dot(const uint8_t* __restrict__ packed
     }
 }
 
+// INT4 tile core over a tile staged in shared memory by tma_tile_int4:
+// packed [16][K/2] then scales [16][K/128].  Same lane mapping and math as
+// int4_tile_dot.
+template <int UNROLL>
+__device__ __forceinline__ void int4_tile_dot_smem(const uint8_t* tile, int K, int gbeg, int gend,
+                                                   int gstep, const uint2* __restrict__ xB, float& y0,
+                                                   float& y1) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int KH = K >> 1, KG = K >> 7;
+    const uint8_t* pa = tile + g * KH + c * 16;
+    const uint8_t* pb = tile + (g + 8) * KH + c * 16;
+    const __half* sc = reinterpret_cast<const __half*>(tile + 16 * KH);
+    const __half* sa = sc + g * KG;
+    const __half* sb = sc + (g + 8) * KG;
+    for (int G0 = gbeg; G0 < gend; G0 += gstep * UNROLL) {
+        uint4 wa[UNROLL], wb[UNROLL];
+        float fa[UNROLL], fb[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            int G = G0 + u * gstep;
+            if (G < gend) {
+                wa[u] = *reinterpret_cast<const uint4*>(pa + G * 64);
+                wb[u] = *reinterpret_cast<const uint4*>(pb + G * 64);
+                fa[u] = __half2float(sa[G]);
+                fb[u] = __half2float(sb[G]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            int G = G0 + u * gstep;
+            if (G < gend) {
+                float d[4] = {0.f, 0.f, 0.f, 0.f};
+                const uint2* xg = xB + (size_t)G * 32 + c;
+                const uint32_t wav[4] = {wa[u].x, wa[u].y, wa[u].z, wa[u].w};
+                const uint32_t wbv[4] = {wb[u].x, wb[u].y, wb[u].z, wb[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    uint32_t ha[4], hb[4];
+                    dequant8(wav[j], ha);
+                    dequant8(wbv[j], hb);
+                    uint2 b0 = xg[(2 * j) * 4];
+                    uint2 b1 = xg[(2 * j + 1) * 4];
+                    mma_16816(d, ha[0], hb[0], ha[1], hb[1], b0.x, b0.y);
+                    mma_16816(d, ha[2], hb[2], ha[3], hb[3], b1.x, b1.y);
+                }
+                y0 = fmaf(fa[u], d[0], y0);
+                y1 = fmaf(fb[u], d[2], y1);
+            }
+        }
+    }
+}
+
 // fp16-weight tile core (router gate, tied lm_head).  One warp, 16 rows,
 // k-blocks of 32 (kb = 32*i for i in [ibeg, iend) step istep).  x is in natural
 // order (fp16, shared memory).  Lane quad c loads 16 bytes = halves
@@ -261,15 +436,19 @@ __device__ __forceinline__ unsigned long long umax64_dev(unsigned long long a,
 }
 
 // Order-preserving key for (value, index) argmax that reproduces argmax_kernel
-// (engine.cu:562-572, 256 threads): among equal maxima the winner has the
-// smallest index mod 256, then the smallest index.  Larger key wins.
+// (engine.cu:562-572, 256 threads, tree reduction keeping the lower slot on
+// ties).  Each thread keeps its first maximum (lowest index of its residue
+// i mod 256); two equal values from residues a and b meet at the lowest bit
+// where a and b differ and the one with a 0 there survives, i.e. the winner
+// has the smallest bit-reversed residue.  Larger key wins.
+__device__ __forceinline__ uint32_t brev8(uint32_t r) { return __brev(r) >> 24; }
 __device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
     uint32_t b = __float_as_uint(v);
     b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-    uint32_t tie = ((uint32_t)(i & 255) << 23) | ((uint32_t)i >> 8);
+    uint32_t tie = (brev8((uint32_t)i & 255u) << 23) | ((uint32_t)i >> 8);
     return ((unsigned long long)b << 32) | (0xFFFFFFFFu - tie);
 }
 __device__ __forceinline__ int argmax_key_index(unsigned long long key) {
     uint32_t tie = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu);
-    return (int)(((tie & 0x7FFFFFu) << 8) | (tie >> 23));
+    return (int)(((tie & 0x7FFFFFu) << 8) | brev8(tie >> 23));
 }

@@ -7,6 +7,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <functional>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -27,7 +28,7 @@
 extern "C" size_t cuinf_attn_decode_workspace_size(int nh, int nkv, int max_ctx) {
     if (nh <= 0 || nkv <= 0 || max_ctx <= 0) return 0;
     int units = (max_ctx + CUINF_KVGROUP - 1) / CUINF_KVGROUP + 1;
-    int ns = attn_default_nsplit(nkv, units, 148);
+    int ns = attn_default_nsplit(nkv, nh / nkv, units, 148);
     return (size_t)nkv * ns * (nh / nkv) * ATTN_PART_STRIDE * 4 + 256;
 }
 
@@ -60,7 +61,8 @@ extern "C" int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_
                                  int nh, int nkv, void* workspace, size_t workspace_bytes,
                                  void* stream) {
     REQUIRE(q && ktail && vtail && out, "null pointer");
-    REQUIRE(nh > 0 && nkv > 0 && nh % nkv == 0 && nh / nkv <= 8, "need nh % nkv == 0, nh/nkv <= 8");
+    REQUIRE(nh > 0 && nkv > 0 && nkv <= 64 && nh % nkv == 0 && nh / nkv <= 8,
+            "need nkv <= 64, nh % nkv == 0, nh/nkv <= 8");
     REQUIRE(qpos >= 0 && committed >= 0 && committed % CUINF_KVGROUP == 0, "committed % 64 == 0");
     REQUIRE(committed <= qpos + 1 && qpos + 1 - committed <= CUINF_KVGROUP,
             "tail length must be in [0, 64]");
@@ -72,7 +74,7 @@ extern "C" int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int ns = attn_default_nsplit(nkv, units, sms);
+    const int ns = attn_default_nsplit(nkv, nh / nkv, units, sms);
     const size_t need = (size_t)nkv * ns * (nh / nkv) * ATTN_PART_STRIDE * 4 + 256;
     void* ws = workspace;
     if (!ws) {
@@ -100,6 +102,7 @@ extern "C" int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_
     P.nh = nh;
     P.nkv = nkv;
     P.nsplit = ns;
+    P.next.count = 0;
     if (workspace) CUINF_TRY(cudaMemsetAsync(ws, 0, 256, ST(stream)));
     k_attn_decode<<<dim3(nkv, ns), ATTN_THREADS, 0, ST(stream)>>>(P);
     return cuinf_launch_status();
@@ -108,8 +111,26 @@ extern "C" int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_
 // ---------------------------------------------------------------------------
 // standalone fused MoE FFN for one token (engine.cu:877-905)
 // ---------------------------------------------------------------------------
-static size_t moe_up_smem(int H) { return (size_t)H * 4 + (160 + 32 + 256 + 32) * 4; }
-static size_t moe_down_smem(int I, int topk) { return (size_t)topk * I * 2 + 8 * topk * 16 * 4; }
+// Launch with programmatic stream serialization (PDL) when pdl is set: the
+// kernel may start while its predecessor runs and orders itself with
+// griddepcontrol.wait before touching its predecessor's outputs.
+template <typename Kern, typename Par>
+static cudaError_t launch_k(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                            const Par& params) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
+static int set_kernel_attrs(const cuinf_config& c);
 
 extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* expert_bias,
                              const void* const* experts, void* h, int H, int I, int n_exp, int topk,
@@ -138,7 +159,6 @@ extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* exper
     U.gate = (const __half*)gate;
     U.bias = (const __half*)expert_bias;
     U.experts = experts;
-    U.xn_store = nullptr;
     U.mid = mid;
     U.route_idx = ridx;
     U.route_w = rw;
@@ -147,9 +167,19 @@ extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* exper
     U.E = n_exp;
     U.topk = topk;
     U.eps = 0.f;
+    U.next.count = 0;
+    {   // TMA sources must be 16-byte aligned
+        std::vector<uintptr_t> tab((size_t)n_exp * 6);
+        CUINF_TRY(cudaMemcpy(tab.data(), experts, tab.size() * sizeof(uintptr_t), cudaMemcpyDeviceToHost));
+        for (uintptr_t a : tab) REQUIRE(a && (a & 15) == 0, "expert tensors must be 16-byte aligned");
+    }
+    const size_t su = moe_up_smem(H, n_exp);
+    REQUIRE(su <= 227 * 1024 && moe_down_smem(I, topk) <= 227 * 1024, "H/I too large for shared memory");
+    if (su > 48 * 1024)
+        CUINF_TRY(cudaFuncSetAttribute(k_moe_up, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)su));
     const int tiles = I / 16;
     const int grid_up = ((topk * tiles + 7) / 8) * 8;
-    k_moe_up<<<grid_up, 256, moe_up_smem(H), ST(stream)>>>(U);
+    k_moe_up<<<grid_up, 256, su, ST(stream)>>>(U);
     int rc = cuinf_launch_status();
     if (rc) return rc;
     MoeDownParams D;
@@ -161,6 +191,7 @@ extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* exper
     D.H = H;
     D.I = I;
     D.topk = topk;
+    D.next.count = 0;
     const size_t sd = moe_down_smem(I, topk);
     if (sd > 48 * 1024)
         CUINF_TRY(cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sd));
@@ -465,6 +496,8 @@ struct cuinf_session {
     int* pinned = nullptr;  // [0] token in, [1] token out
     int host_pos = 0;
     int num_sms = 148;
+    bool prefetch = true;  // L2 prefetch plans (cross-kernel weight streaming)
+    bool pdl = true;       // programmatic dependent launch between the step's kernels
 };
 
 template <class T>
@@ -479,13 +512,79 @@ static int dalloc(cuinf_session* s, T** p, size_t bytes) {
 
 static size_t smem_norm_gemv(int H, int warps) { return (size_t)H * 4 + (warps * 16 + 32) * 4; }
 
-// Records one decode step into the session stream (used under capture).
-static int record_step(cuinf_session* s) {
+// Per-kernel timing of an eagerly launched step: an event after each launch
+// plus the kernel's algorithmic bytes (weights + activations it must move).
+struct Prof {
+    std::vector<cudaEvent_t> ev;
+    std::vector<const char*> name;
+    std::vector<double> bytes;
+};
+static void prof_mark(Prof* p, cudaStream_t st, const char* name, double bytes) {
+    if (!p) return;
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    cudaEventRecord(e, st);
+    p->ev.push_back(e);
+    p->name.push_back(name);
+    p->bytes.push_back(bytes);
+}
+static double q4_bytes(int64_t N, int64_t K) { return (double)(N * K / 2 + N * (K / 128) * 2); }
+
+// One kernel of the step: how to launch it given its L2 prefetch plan, and
+// the static weight ranges it reads (for the plans of the kernels before it).
+struct Launch {
+    const char* name;
+    double bytes;
+    std::vector<std::pair<const char*, unsigned long long>> weights;
+    std::function<cudaError_t(const L2Ranges&, bool)> fire;
+};
+
+static std::pair<const char*, unsigned long long> q4_range(const Q4& w, int64_t N, int64_t K) {
+    return {(const char*)w.p, (unsigned long long)(N * K / 2 + N * (K / 128) * 2)};
+}
+
+// Weight bytes a kernel prefetches for the kernels after it: each static
+// range is scheduled once, as early as the budget allows.
+static const unsigned long long kPrefetchBudget = 12ull << 20;
+
+static void plan_prefetch(const std::vector<Launch>& L, std::vector<L2Ranges>& plans) {
+    const int n = (int)L.size();
+    plans.assign(n, L2Ranges());
+    // (kernel, range) in execution order, wrapping once into the next step
+    std::vector<std::pair<int, std::pair<const char*, unsigned long long>>> q;
+    for (int r = 0; r < 2; r++)
+        for (int i = 0; i < n; i++)
+            for (auto& w : L[i].weights) q.push_back({i + r * n, w});
+    size_t next = 0;
+    unsigned long long off = 0;  // bytes of q[next] already scheduled
+    for (int i = 0; i < n; i++) {
+        L2Ranges& R = plans[i];
+        R.count = 0;
+        while (next < q.size() && q[next].first <= i) { next++; off = 0; }  // too late
+        unsigned long long acc = 0;
+        while (next < q.size() && R.count < 8 && acc < kPrefetchBudget && q[next].first <= i + 3) {
+            const unsigned long long left = q[next].second.second - off;
+            unsigned long long len = std::min(left, kPrefetchBudget - acc);
+            len = (len + 15) & ~15ull;
+            if (len > left) len = left;
+            R.p[R.count] = q[next].second.first + off;
+            R.n[R.count++] = len;
+            acc += len;
+            off += len;
+            if (off >= q[next].second.second) { next++; off = 0; }
+        }
+    }
+}
+
+// Records one decode step into the session stream (under capture, or eagerly
+// with per-kernel events when prof is set).
+static int record_step(cuinf_session* s, Prof* prof = nullptr) {
     const cuinf_model* m = s->m;
     const cuinf_config& c = m->cfg;
     const int H = c.hidden;
     cudaStream_t st = s->st;
-    int kernels = 0;
+    const int nh = c.n_heads, nkv = c.n_kv_heads;
+    std::vector<Launch> Ls;
     for (int l = 0; l < c.n_layers; l++) {
         const LayerW& L = m->L[l];
         const bool first = l == 0;
@@ -507,11 +606,16 @@ static int record_step(cuinf_session* s) {
             Q.ktail = A.ktail; Q.vtail = A.vtail;
             Q.kc8 = A.kc8; Q.vc8 = A.vc8;
             Q.ksc = A.ksc; Q.vsc = A.vsc;
-            Q.H = H; Q.nh = c.n_heads; Q.nkv = c.n_kv_heads;
+            Q.H = H; Q.nh = nh; Q.nkv = nkv;
             Q.eps = c.norm_eps; Q.theta = c.rope_theta;
-            const int heads = c.n_heads + 2 * c.n_kv_heads;
-            k_attn_qkv<<<heads * 4, 256, smem_norm_gemv(H, 8) + (16 + 64) * 4 + 128, st>>>(Q);
-            kernels++;
+            const int heads = nh + 2 * nkv;
+            const size_t sq = qkv_smem(H);
+            Ls.push_back({"attn_qkv", q4_bytes((nh + 2 * nkv) * 64, H) + 2.0 * H + nh * 128 + 4 * nkv * 64,
+                          {q4_range(L.wq, nh * 64, H), q4_range(L.wk, nkv * 64, H), q4_range(L.wv, nkv * 64, H)},
+                          [=](const L2Ranges& nx, bool pdl) mutable {
+                              Q.next = nx;
+                              return launch_k(k_attn_qkv, dim3(heads * 4), dim3(256), sq, st, pdl, Q);
+                          }});
             AttnParams P;
             P.q = s->q;
             P.kc8 = A.kc8; P.vc8 = A.vc8; P.ksc = A.ksc; P.vsc = A.vsc;
@@ -522,12 +626,23 @@ static int record_step(cuinf_session* s) {
             P.out = s->attn_out;
             P.part = s->attn_part;
             P.counters = s->attn_cnt;
-            P.nh = c.n_heads; P.nkv = c.n_kv_heads; P.nsplit = s->nsplit;
-            k_attn_decode<<<dim3(c.n_kv_heads, s->nsplit), ATTN_THREADS, 0, st>>>(P);
-            kernels++;
-            k_gemv_residual<<<H / 16, 256, (size_t)c.n_heads * 64 * 2 + 8 * 16 * 4, st>>>(
-                s->attn_out, L.wo.p, L.wo.s, s->h, H, c.n_heads * 64);
-            kernels++;
+            P.nh = nh; P.nkv = nkv; P.nsplit = s->nsplit;
+            const double ctx = s->host_pos + 1, cm = 64.0 * floor(ctx / 64.0);
+            const int nsplit = s->nsplit;
+            Ls.push_back({"attn_decode", cm * nkv * 128 + cm / 64 * nkv * 4 + (ctx - cm) * nkv * 256 + nh * 256.0,
+                          {},
+                          [=](const L2Ranges& nx, bool pdl) mutable {
+                              P.next = nx;
+                              return launch_k(k_attn_decode, dim3(nkv, nsplit), dim3(ATTN_THREADS), 0, st, pdl, P);
+                          }});
+            ResParams R;
+            R.act = s->attn_out; R.wp = L.wo.p; R.ws = L.wo.s; R.h = s->h; R.N = H; R.K = nh * 64;
+            Ls.push_back({"attn_out_proj", q4_bytes(H, nh * 64) + nh * 128 + 4.0 * H,
+                          {q4_range(L.wo, H, nh * 64)},
+                          [=](const L2Ranges& nx, bool pdl) mutable {
+                              R.next = nx;
+                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), res_smem(nh * 64), st, pdl, R);
+                          }});
         } else {
             ConvParams C;
             C.h = s->h;
@@ -540,43 +655,68 @@ static int record_step(cuinf_session* s) {
             C.state = s->conv_state[l];
             C.y = s->conv_y;
             C.H = H; C.eps = c.norm_eps;
-            k_conv_in<<<H / 16, 384, smem_norm_gemv(H, 12), st>>>(C);
-            kernels++;
-            k_gemv_residual<<<H / 16, 256, (size_t)H * 2 + 8 * 16 * 4, st>>>(s->conv_y, L.out_proj.p,
-                                                                           L.out_proj.s, s->h, H, H);
-            kernels++;
+            Ls.push_back({"conv_in", q4_bytes(3 * H, H) + 18.0 * H, {q4_range(L.in_proj, 3 * H, H)},
+                          [=](const L2Ranges& nx, bool pdl) mutable {
+                              C.next = nx;
+                              return launch_k(k_conv_in, dim3(H / 16), dim3(384), conv_smem(H), st, pdl, C);
+                          }});
+            ResParams R;
+            R.act = s->conv_y; R.wp = L.out_proj.p; R.ws = L.out_proj.s; R.h = s->h; R.N = H; R.K = H;
+            Ls.push_back({"conv_out_proj", q4_bytes(H, H) + 6.0 * H, {q4_range(L.out_proj, H, H)},
+                          [=](const L2Ranges& nx, bool pdl) mutable {
+                              R.next = nx;
+                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), res_smem(H), st, pdl, R);
+                          }});
         }
         if (l < c.n_dense) {
             FfnUpParams F;
             F.h = s->h; F.norm_w = L.ffn_norm;
             F.w1p = L.w1.p; F.w1s = L.w1.s; F.w3p = L.w3.p; F.w3s = L.w3.s;
             F.mid = s->mid; F.H = H; F.I = c.dense_inter; F.eps = c.norm_eps;
-            k_ffn_up<<<(c.dense_inter + 15) / 16, 256, smem_norm_gemv(H, 8), st>>>(F);
-            kernels++;
-            size_t sm = (size_t)c.dense_inter * 2 + 8 * 16 * 4;
-            k_gemv_residual<<<H / 16, 256, sm, st>>>(s->mid, L.w2.p, L.w2.s, s->h, H, c.dense_inter);
-            kernels++;
+            const int I = c.dense_inter;
+            Ls.push_back({"dense_up", 2 * q4_bytes(I, H) + 4.0 * H + 2.0 * I,
+                          {q4_range(L.w1, I, H), q4_range(L.w3, I, H)},
+                          [=](const L2Ranges& nx, bool pdl) mutable {
+                              F.next = nx;
+                              return launch_k(k_ffn_up, dim3((I + 15) / 16), dim3(256), ffn_up_smem(H), st, pdl, F);
+                          }});
+            ResParams R;
+            R.act = s->mid; R.wp = L.w2.p; R.ws = L.w2.s; R.h = s->h; R.N = H; R.K = I;
+            Ls.push_back({"dense_down", q4_bytes(H, I) + 2.0 * I + 4.0 * H, {q4_range(L.w2, H, I)},
+                          [=](const L2Ranges& nx, bool pdl) mutable {
+                              R.next = nx;
+                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), res_smem(I), st, pdl, R);
+                          }});
         } else {
             const int mi = L.moe_index;
             MoeUpParams U;
             U.h = s->h; U.xn = nullptr; U.norm_w = L.ffn_norm;
             U.gate = L.gate; U.bias = L.ebias;
             U.experts = (const void* const*)(m->d_experts + (size_t)mi * c.n_experts * 6);
-            U.xn_store = nullptr;
             U.mid = s->mid;
             U.route_idx = s->route_idx + mi * c.top_k;
             U.route_w = s->route_w + mi * c.top_k;
             U.H = H; U.I = c.moe_inter; U.E = c.n_experts; U.topk = c.top_k; U.eps = c.norm_eps;
             const int tiles = c.moe_inter / 16;
             const int grid_up = ((c.top_k * tiles + 7) / 8) * 8;
-            k_moe_up<<<grid_up, 256, moe_up_smem(H), st>>>(U);
-            kernels++;
+            Ls.push_back({"moe_up", 2.0 * c.top_k * q4_bytes(c.moe_inter, H) + (double)c.n_experts * H * 2 +
+                                        c.n_experts * 2 + 4.0 * H + 2.0 * c.top_k * c.moe_inter,
+                          {{(const char*)L.gate, (unsigned long long)c.n_experts * H * 2}},
+                          [=](const L2Ranges& nx, bool pdl) mutable {
+                              U.next = nx;
+                              return launch_k(k_moe_up, dim3(grid_up), dim3(256), moe_up_smem(H, c.n_experts), st, pdl, U);
+                          }});
             MoeDownParams D;
             D.mid = s->mid; D.experts = U.experts;
             D.route_idx = U.route_idx; D.route_w = U.route_w;
             D.h = s->h; D.H = H; D.I = c.moe_inter; D.topk = c.top_k;
-            k_moe_down<<<H / 16, 256, moe_down_smem(c.moe_inter, c.top_k), st>>>(D);
-            kernels++;
+            const size_t sd = moe_down_smem(c.moe_inter, c.top_k);
+            Ls.push_back({"moe_down", c.top_k * q4_bytes(H, c.moe_inter) + 2.0 * c.top_k * c.moe_inter + 4.0 * H,
+                          {},
+                          [=](const L2Ranges& nx, bool pdl) mutable {
+                              D.next = nx;
+                              return launch_k(k_moe_down, dim3(H / 16), dim3(256), sd, st, pdl, D);
+                          }});
         }
     }
     LmHeadParams LM;
@@ -594,10 +734,25 @@ static int record_step(cuinf_session* s) {
     LM.H = H;
     LM.V = c.vocab;
     LM.eps = c.norm_eps;
-    const int lm_tiles = (c.vocab + 15) / 16;
-    k_lmhead<<<(lm_tiles + 7) / 8, 256, (size_t)H * 2 + 64 * 4, st>>>(LM);
-    kernels++;
-    s->kernels_per_step = kernels;
+    const int lm_grid = ((c.vocab + 15) / 16 + 7) / 8;
+    Ls.push_back({"lm_head_argmax", (double)c.vocab * H * 2 + 6.0 * H,
+                  {{(const char*)m->embed, (unsigned long long)c.vocab * H * 2}},
+                  [=](const L2Ranges& nx, bool pdl) mutable {
+                      LM.next = nx;
+                      return launch_k(k_lmhead, dim3(lm_grid), dim3(256), (size_t)H * 2 + 64 * 4, st, pdl, LM);
+                  }});
+
+    std::vector<L2Ranges> plans;
+    if (s->prefetch) plan_prefetch(Ls, plans);
+    else plans.assign(Ls.size(), L2Ranges{{}, {}, 0});
+    prof_mark(prof, st, "start", 0);
+    for (size_t i = 0; i < Ls.size(); i++) {
+        // the step's first kernel follows host copies / the previous graph: no PDL
+        cudaError_t e = Ls[i].fire(plans[i], s->pdl && i > 0);
+        if (e != cudaSuccess) return cuinf_set_cuda_error(e);
+        prof_mark(prof, st, Ls[i].name, Ls[i].bytes);
+    }
+    s->kernels_per_step = (int)Ls.size();
     return cuinf_launch_status();
 }
 
@@ -616,19 +771,20 @@ static int build_graph(cuinf_session* s) {
 }
 
 static int set_kernel_attrs(const cuinf_config& c) {
-    const size_t sd = moe_down_smem(c.moe_inter, c.top_k);
-    if (sd > 48 * 1024)
-        CUINF_TRY(cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sd));
-    const size_t sr = (size_t)std::max(c.dense_inter, std::max(c.hidden, c.n_heads * 64)) * 2 + 8 * 16 * 4;
-    if (sr > 48 * 1024)
-        CUINF_TRY(cudaFuncSetAttribute(k_gemv_residual, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sr));
-    const size_t sn = smem_norm_gemv(c.hidden, 12) + 512;
-    if (sn > 48 * 1024) {
-        CUINF_TRY(cudaFuncSetAttribute(k_conv_in, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sn));
-        CUINF_TRY(cudaFuncSetAttribute(k_attn_qkv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sn));
-        CUINF_TRY(cudaFuncSetAttribute(k_ffn_up, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sn));
-        CUINF_TRY(cudaFuncSetAttribute(k_moe_up, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)moe_up_smem(c.hidden)));
+    const int H = c.hidden;
+    struct { const void* k; size_t bytes; } need[] = {
+        {(const void*)k_attn_qkv, qkv_smem(H)},
+        {(const void*)k_conv_in, conv_smem(H)},
+        {(const void*)k_ffn_up, ffn_up_smem(H)},
+        {(const void*)k_moe_up, moe_up_smem(H, std::max(1, c.n_experts))},
+        {(const void*)k_moe_down, moe_down_smem(c.moe_inter, std::max(1, c.top_k))},
+        {(const void*)k_gemv_residual,
+         std::max(res_smem(H), std::max(res_smem(c.n_heads * 64), res_smem(c.dense_inter)))},
+    };
+    for (auto& n : need) {
+        if (n.bytes > 227 * 1024) return cuinf_set_arg_error("model dims too large for shared memory");
+        if (n.bytes > 48 * 1024)
+            CUINF_TRY(cudaFuncSetAttribute(n.k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)n.bytes));
     }
     return CUINF_OK;
 }
@@ -678,7 +834,7 @@ extern "C" int cuinf_session_create(cuinf_model* m, int max_ctx, void* stream, c
     TRYS(dalloc(s, &s->am_key, 16));
     TRYS(dalloc(s, &s->am_ticket, 16));
     const int units = max_ctx / CUINF_KVGROUP + 1;
-    s->nsplit = attn_default_nsplit(nkv, units, s->num_sms);
+    s->nsplit = attn_default_nsplit(nkv, gqa, units, s->num_sms);
     TRYS(dalloc(s, &s->attn_part, (size_t)nkv * s->nsplit * gqa * ATTN_PART_STRIDE * 4));
     TRYS(dalloc(s, &s->attn_cnt, (size_t)nkv * 4));
     s->attn.assign(c.n_layers, AttnState());
@@ -780,6 +936,24 @@ extern "C" int cuinf_session_keep_logits(cuinf_session* s, int on) {
     return build_graph(s);
 }
 
+extern "C" int cuinf_session_set_option(cuinf_session* s, int option, int value) {
+    REQUIRE(s, "null session");
+    bool* f = option == CUINF_OPT_PREFETCH ? &s->prefetch : option == CUINF_OPT_PDL ? &s->pdl : nullptr;
+    REQUIRE(f, "unknown option");
+    if ((bool)value == *f) return CUINF_OK;
+    CUINF_TRY(cudaStreamSynchronize(s->st));
+    *f = value != 0;
+    return build_graph(s);
+}
+
+extern "C" int cuinf_device_error(unsigned* flags) {
+    REQUIRE(flags, "null pointer");
+    unsigned v = 0;
+    CUINF_TRY(cudaMemcpyFromSymbol(&v, g_engine_err, sizeof(v)));
+    *flags = v;
+    return CUINF_OK;
+}
+
 extern "C" const float* cuinf_session_logits(const cuinf_session* s) { return s ? s->logits : nullptr; }
 extern "C" const void* cuinf_session_hidden(const cuinf_session* s) { return s ? s->hidden : nullptr; }
 
@@ -794,4 +968,33 @@ extern "C" int cuinf_session_routes(cuinf_session* s, int* idx, float* w) {
 
 extern "C" int cuinf_session_kernels_per_step(const cuinf_session* s) {
     return s ? s->kernels_per_step : -1;
+}
+
+extern "C" int cuinf_session_profile_step(cuinf_session* s, int token, int max_kernels, float* ms,
+                                          double* bytes, char* names, int name_len, int* n_kernels) {
+    REQUIRE(s && ms && bytes && n_kernels, "null pointer");
+    REQUIRE(s->host_pos < s->max_ctx, "context full (max_ctx reached)");
+    CUINF_TRY(cudaStreamSynchronize(s->st));
+    if (token >= 0) {
+        s->pinned[0] = token;
+        CUINF_TRY(cudaMemcpyAsync(s->tok, &s->pinned[0], 4, cudaMemcpyHostToDevice, s->st));
+    }
+    Prof prof;
+    int rc = record_step(s, &prof);
+    CUINF_TRY(cudaStreamSynchronize(s->st));
+    s->host_pos++;
+    const int n = (int)prof.ev.size() - 1;
+    for (int i = 0; i < n && i < max_kernels; i++) {
+        float t = 0.f;
+        cudaEventElapsedTime(&t, prof.ev[i], prof.ev[i + 1]);
+        ms[i] = t;
+        bytes[i] = prof.bytes[i + 1];
+        if (names && name_len > 0) {
+            strncpy(names + (size_t)i * name_len, prof.name[i + 1], name_len - 1);
+            names[(size_t)i * name_len + name_len - 1] = 0;
+        }
+    }
+    for (cudaEvent_t e : prof.ev) cudaEventDestroy(e);
+    *n_kernels = n;
+    return rc;
 }

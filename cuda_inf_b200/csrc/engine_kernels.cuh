@@ -1,10 +1,22 @@
-// Fused decode-step kernels.  One token (batch 1) per launch chain; every
-// kernel streams its INT4 weights once with 16-byte loads and dequantizes in
-// registers (int4_tile_dot), and fuses the reference's small kernels
-// (rmsnorm, f32_to_f16, qk-norm, rope, kv_write_tail, kv_commit_group,
-// conv_pre/apply/update, swiglu, acc_scaled, add_*, argmax) into its
-// prologue or epilogue.  Per step: 3 kernels per attention layer, 2 per conv
-// layer, 2 per FFN, 1 lm_head (src/engine.cu:784-940 launches ~760).
+// Fused decode-step kernels.  One token (batch 1) per launch chain.
+//
+// Every weight-streaming kernel follows the same schedule:
+//   1. thread 0 stages the CTA's weight tiles (16 rows x full K, packed
+//      nibbles + fp16 scales, the tools/export_weights.py layout) into
+//      shared memory with TMA bulk copies tracked by one mbarrier, and pulls
+//      the weights of the kernels after it into L2;
+//   2. griddepcontrol.launch_dependents, so the next kernel of the step
+//      (launched with programmatic serialization) can start its own step 1
+//      while this one runs;
+//   3. griddepcontrol.wait: only now read what earlier kernels wrote;
+//   4. prologue (RMSNorm of the residual, x permuted to B-fragment order),
+//      wait for the tiles, dequantize in registers and run mma.m16n8k16
+//      (fp32 accumulate) per 128-wide group, scale, reduce across warps;
+//   5. fused epilogue replacing the reference's small kernels (f32_to_f16,
+//      rmsnorm_head, rope, kv_write_tail, kv_commit_group, conv_pre/apply/
+//      update_state, swiglu, acc_scaled, add_*, argmax).
+// Per step: 3 kernels per attention layer, 2 per conv layer, 2 per FFN and
+// one lm_head (src/engine.cu:784-940 launches ~760 plus 24 host syncs).
 #pragma once
 #include <cooperative_groups.h>
 
@@ -12,6 +24,10 @@
 #include "route.cuh"
 
 namespace cg = cooperative_groups;
+
+// Device-side error word of this translation unit: bit 0 = an mbarrier wait
+// timed out (its kernel then skipped its math).
+static __device__ unsigned g_engine_err;
 
 // Norm prologue: x = rmsnorm(src, w) into shared memory (fp16, natural order)
 // and its B-fragment permutation xB.  src is the residual h, or the embedding
@@ -27,12 +43,31 @@ __device__ __forceinline__ void norm_prologue(const __half* __restrict__ h,
         if (blockIdx.x == 0 && blockIdx.y == 0)
             for (int i = threadIdx.x; i < H; i += blockDim.x) h_store[i] = src[i];
     }
-    for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = src[i];
+    for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8)
+        *reinterpret_cast<uint4*>(xs + i) = *reinterpret_cast<const uint4*>(src + i);
     __syncthreads();
     rmsnorm_smem(xs, w, xs, H, eps, red);
     __syncthreads();
     for (int e = threadIdx.x; e < H / 4; e += blockDim.x) build_xB_entry(xs, xB, e);
     __syncthreads();
+}
+
+// Stage begin: mbarrier init by thread 0, made visible to the CTA.
+__device__ __forceinline__ void stage_begin(uint64_t* bar) {
+    if (threadIdx.x == 0) mbar_init(bar, 1);
+    __syncthreads();
+}
+// Wait for the staged tiles; false (and the error bit) on time-out.
+__device__ __forceinline__ bool stage_wait(uint64_t* bar) {
+    return mbar_wait_bounded(bar, 0, &g_engine_err);
+}
+
+__device__ __forceinline__ void warp_partials(float* red, int warp, float y0, float y1) {
+    const int lane = threadIdx.x & 31;
+    if ((lane & 3) == 0) {
+        red[warp * 16 + (lane >> 2)] = y0;
+        red[warp * 16 + (lane >> 2) + 8] = y1;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -59,36 +94,48 @@ struct QkvParams {
     __half *ksc, *vsc;
     int H, nh, nkv;
     float eps, theta;
+    L2Ranges next;
 };
 
+__host__ __device__ inline size_t qkv_smem(int H) {
+    return int4_tile_bytes(H) + (size_t)H * 4 + (160 + 16 + 64) * 4 + 128;
+}
+
 __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256) k_attn_qkv(QkvParams P) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __half* xs = reinterpret_cast<__half*>(smem);
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar;
+    uint8_t* tile = smem;
+    __half* xs = reinterpret_cast<__half*>(smem + int4_tile_bytes(P.H));
     __half* xB = xs + P.H;
     float* red = reinterpret_cast<float*>(xB + P.H);  // [8][16] + 32
-    float* res = red + 8 * 16 + 32;                   // [16] this CTA's rows
+    float* res = red + 160;                           // [16] this CTA's rows
     float* head = res + 16;                           // [64] rank 0 only
     __half* hv = reinterpret_cast<__half*>(head + 64);  // [64]
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
     const int hh = blockIdx.x >> 2;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    norm_prologue(P.h, P.embed, P.tok, P.h_store, P.norm_w, P.H, P.eps, xs, xB, red + 128);
+    const int warp = threadIdx.x >> 5;
 
     const uint8_t* wp;
     const __half* ws;
-    int N, row0;
-    if (hh < P.nh) { wp = P.wq_p; ws = P.wq_s; N = P.nh * CUINF_HD; row0 = hh * CUINF_HD; }
-    else if (hh < P.nh + P.nkv) { wp = P.wk_p; ws = P.wk_s; N = P.nkv * CUINF_HD; row0 = (hh - P.nh) * CUINF_HD; }
-    else { wp = P.wv_p; ws = P.wv_s; N = P.nkv * CUINF_HD; row0 = (hh - P.nh - P.nkv) * CUINF_HD; }
+    int row0;
+    if (hh < P.nh) { wp = P.wq_p; ws = P.wq_s; row0 = hh * CUINF_HD; }
+    else if (hh < P.nh + P.nkv) { wp = P.wk_p; ws = P.wk_s; row0 = (hh - P.nh) * CUINF_HD; }
+    else { wp = P.wv_p; ws = P.wv_s; row0 = (hh - P.nh - P.nkv) * CUINF_HD; }
     row0 += rank * 16;
-    float y0 = 0.f, y1 = 0.f;
-    int4_tile_dot<2>(wp, ws, N, P.H, row0, warp, P.H >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
-    if ((lane & 3) == 0) {
-        red[warp * 16 + (lane >> 2)] = y0;
-        red[warp * 16 + (lane >> 2) + 8] = y1;
+    stage_begin(&bar);
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar, int4_tile_bytes(P.H));
+        tma_tile_int4(wp, ws, P.H, row0, tile, &bar);
+        l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
     }
+    pdl_trigger();
+    pdl_wait();
+    norm_prologue(P.h, P.embed, P.tok, P.h_store, P.norm_w, P.H, P.eps, xs, xB, red + 128);
+    float y0 = 0.f, y1 = 0.f;
+    if (stage_wait(&bar))
+        int4_tile_dot_smem<2>(tile, P.H, warp, P.H >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
+    warp_partials(red, warp, y0, y1);
     __syncthreads();
     if (threadIdx.x < 16) {
         float s = 0.f;
@@ -112,7 +159,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256) k_attn_qkv(QkvP
     if (d < 64) hv[d] = __float2half_rn(head[d]);  // f32_to_f16
     __syncthreads();
     if (is_q || is_k) {
-        // rmsnorm_head (engine.cu:148-158), 64 threads
+        // rmsnorm_head (engine.cu:148-158)
         float v = d < 64 ? __half2float(hv[d]) : 0.f;
         float ss = block_sum(v * v, red + 128);
         float inv = rsqrtf(ss / 64.f + P.eps);
@@ -171,31 +218,49 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256) k_attn_qkv(QkvP
 // ---------------------------------------------------------------------------
 // Residual GEMV: h[n] = half(h[n] + (W . act)[n])  (out_proj of attention and
 // conv layers, dense w2; engine.cu:858-859, 866-867, 875-876).  One 16-row
-// tile per CTA, 8 warps interleaved over K groups.
+// tile per CTA, 8 warps interleaved over the K groups.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_gemv_residual(const __half* __restrict__ act,
-                                                       const uint8_t* __restrict__ wp,
-                                                       const __half* __restrict__ ws,
-                                                       __half* h, int N, int K) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __half* xB = reinterpret_cast<__half*>(smem);
-    float* red = reinterpret_cast<float*>(xB + K);
-    for (int e = threadIdx.x; e < K / 4; e += blockDim.x) build_xB_entry(act, xB, e);
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row0 = blockIdx.x * 16;
-    float y0 = 0.f, y1 = 0.f;
-    int4_tile_dot<2>(wp, ws, N, K, row0, warp, K >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
-    if ((lane & 3) == 0) {
-        red[warp * 16 + (lane >> 2)] = y0;
-        red[warp * 16 + (lane >> 2) + 8] = y1;
+struct ResParams {
+    const __half* act;
+    const uint8_t* wp;
+    const __half* ws;
+    __half* h;
+    int N, K;
+    L2Ranges next;
+};
+
+__host__ __device__ inline size_t res_smem(int K) {
+    return int4_tile_bytes(K) + (size_t)K * 2 + 8 * 16 * 4;
+}
+
+__global__ void __launch_bounds__(256) k_gemv_residual(ResParams P) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar;
+    uint8_t* tile = smem;
+    __half* xB = reinterpret_cast<__half*>(smem + int4_tile_bytes(P.K));
+    float* red = reinterpret_cast<float*>(xB + P.K);
+    const int warp = threadIdx.x >> 5, row0 = blockIdx.x * 16;
+    stage_begin(&bar);
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar, int4_tile_bytes(P.K));
+        tma_tile_int4(P.wp, P.ws, P.K, row0, tile, &bar);
+        l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
     }
+    pdl_trigger();
+    pdl_wait();
+    for (int e = threadIdx.x; e < P.K / 4; e += blockDim.x) build_xB_entry(P.act, xB, e);
+    __syncthreads();
+    float y0 = 0.f, y1 = 0.f;
+    if (stage_wait(&bar))
+        int4_tile_dot_smem<2>(tile, P.K, warp, P.K >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
+    warp_partials(red, warp, y0, y1);
     __syncthreads();
     if (threadIdx.x < 16) {
         float s = 0.f;
 #pragma unroll
         for (int w = 0; w < 8; w++) s += red[w * 16 + threadIdx.x];
         const int n = row0 + threadIdx.x;
-        if (n < N) h[n] = __float2half_rn(__half2float(h[n]) + s);
+        if (n < P.N) P.h[n] = __float2half_rn(__half2float(P.h[n]) + s);
     }
 }
 
@@ -217,23 +282,37 @@ struct ConvParams {
     __half* y;             // [H]
     int H;
     float eps;
+    L2Ranges next;
 };
 
+__host__ __device__ inline size_t conv_smem(int H) {
+    return 3 * (size_t)int4_tile_bytes(H) + (size_t)H * 4 + (192 + 32) * 4;
+}
+
 __global__ void __launch_bounds__(384) k_conv_in(ConvParams P) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __half* xs = reinterpret_cast<__half*>(smem);
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar;
+    const uint32_t TB = int4_tile_bytes(P.H);
+    uint8_t* tiles = smem;
+    __half* xs = reinterpret_cast<__half*>(smem + 3 * TB);
     __half* xB = xs + P.H;
     float* red = reinterpret_cast<float*>(xB + P.H);  // [12][16] + 32
-    norm_prologue(P.h, P.embed, P.tok, P.h_store, P.norm_w, P.H, P.eps, xs, xB, red + 192);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
     const int tile = warp >> 2, c0 = blockIdx.x * 16;
-    float y0 = 0.f, y1 = 0.f;
-    int4_tile_dot<2>(P.wp, P.ws, 3 * P.H, P.H, tile * P.H + c0, warp & 3, P.H >> 7, 4,
-                     reinterpret_cast<const uint2*>(xB), y0, y1);
-    if ((lane & 3) == 0) {
-        red[warp * 16 + (lane >> 2)] = y0;
-        red[warp * 16 + (lane >> 2) + 8] = y1;
+    stage_begin(&bar);
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar, 3 * TB);
+        for (int t = 0; t < 3; t++) tma_tile_int4(P.wp, P.ws, P.H, t * P.H + c0, tiles + t * TB, &bar);
+        l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
     }
+    pdl_trigger();
+    pdl_wait();
+    norm_prologue(P.h, P.embed, P.tok, P.h_store, P.norm_w, P.H, P.eps, xs, xB, red + 192);
+    float y0 = 0.f, y1 = 0.f;
+    if (stage_wait(&bar))
+        int4_tile_dot_smem<2>(tiles + tile * TB, P.H, warp & 3, P.H >> 7, 4,
+                              reinterpret_cast<const uint2*>(xB), y0, y1);
+    warp_partials(red, warp, y0, y1);
     __syncthreads();
     if (threadIdx.x < 16) {
         const int i = threadIdx.x, c = c0 + i;
@@ -266,25 +345,40 @@ struct FfnUpParams {
     __half* mid;
     int H, I;
     float eps;
+    L2Ranges next;
 };
+
+__host__ __device__ inline size_t ffn_up_smem(int H) {
+    return 2 * (size_t)int4_tile_bytes(H) + (size_t)H * 4 + (128 + 32) * 4;
+}
 
 __device__ __forceinline__ float silu_fast(float x) { return x / (1.f + __expf(-x)); }
 
 __global__ void __launch_bounds__(256) k_ffn_up(FfnUpParams P) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __half* xs = reinterpret_cast<__half*>(smem);
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar;
+    const uint32_t TB = int4_tile_bytes(P.H);
+    uint8_t* tiles = smem;
+    __half* xs = reinterpret_cast<__half*>(smem + 2 * TB);
     __half* xB = xs + P.H;
     float* red = reinterpret_cast<float*>(xB + P.H);
-    norm_prologue(P.h, nullptr, nullptr, nullptr, P.norm_w, P.H, P.eps, xs, xB, red + 128);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row0 = blockIdx.x * 16;
+    const int warp = threadIdx.x >> 5, row0 = blockIdx.x * 16;
     const int tile = warp & 1;
-    float y0 = 0.f, y1 = 0.f;
-    int4_tile_dot<2>(tile ? P.w3p : P.w1p, tile ? P.w3s : P.w1s, P.I, P.H, row0, warp >> 1,
-                     P.H >> 7, 4, reinterpret_cast<const uint2*>(xB), y0, y1);
-    if ((lane & 3) == 0) {
-        red[warp * 16 + (lane >> 2)] = y0;
-        red[warp * 16 + (lane >> 2) + 8] = y1;
+    stage_begin(&bar);
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar, 2 * TB);
+        tma_tile_int4(P.w1p, P.w1s, P.H, row0, tiles, &bar);
+        tma_tile_int4(P.w3p, P.w3s, P.H, row0, tiles + TB, &bar);
+        l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
     }
+    pdl_trigger();
+    pdl_wait();
+    norm_prologue(P.h, nullptr, nullptr, nullptr, P.norm_w, P.H, P.eps, xs, xB, red + 128);
+    float y0 = 0.f, y1 = 0.f;
+    if (stage_wait(&bar))
+        int4_tile_dot_smem<2>(tiles + tile * TB, P.H, warp >> 1, P.H >> 7, 4,
+                              reinterpret_cast<const uint2*>(xB), y0, y1);
+    warp_partials(red, warp, y0, y1);
     __syncthreads();
     if (threadIdx.x < 16) {
         const int i = threadIdx.x, r = row0 + i;
@@ -299,10 +393,12 @@ __global__ void __launch_bounds__(256) k_ffn_up(FfnUpParams P) {
 }
 
 // ---------------------------------------------------------------------------
-// MoE up: router (gate fp16 [E,H] . x) computed cooperatively by a cluster
-// of 8 CTAs (DSMEM exchange of logits), device-side selection with the
-// reference's rules (engine.cu:879-892), then this CTA's (rank slot t,
-// 16-row tile) of experts' w1 and w3 -> mid[t*I + i] = half(silu(g) * u).
+// MoE up: the router gate (fp16 [E,H]) is split over a cluster of 8 CTAs
+// (each stages its rows with TMA before the dependency wait) and the logits
+// are exchanged over DSMEM; device-side selection with the reference's rules
+// (engine.cu:879-892); then this CTA's (rank slot t, 16-row tile) of the
+// selected expert's w1 and w3 -> mid[t*I + i] = half(silu(g) * u).  The
+// selected experts' w2 (for moe_down) is pulled into L2 across the grid.
 // ---------------------------------------------------------------------------
 struct MoeUpParams {
     const __half* h;       // residual (normalized here) or, if xn != null, ignored
@@ -311,18 +407,32 @@ struct MoeUpParams {
     const __half* gate;    // [E,H]
     const __half* bias;    // [E]
     const void* const* experts;  // [E][6]
-    __half* xn_store;      // if set, CTA 0 stores the normalized x here
     __half* mid;           // [topk, I]
     int* route_idx;        // [topk]
     float* route_w;        // [topk]
     int H, I, E, topk;
     float eps;
+    L2Ranges next;         // static weights of the kernels after moe_down
 };
 
+// The gate rows are consumed before the expert tiles arrive, so both share
+// the first region (keeps 448 CTAs resident in one wave on 148 SMs).
+__host__ __device__ inline size_t moe_up_stage_bytes(int H, int E) {
+    const size_t gate = (size_t)((E + 7) / 8) * H * 2, tiles = 2 * (size_t)int4_tile_bytes(H);
+    return gate > tiles ? gate : tiles;
+}
+__host__ __device__ inline size_t moe_up_smem(int H, int E) {
+    return moe_up_stage_bytes(H, E) + (size_t)H * 4 + (160 + 32 + 256 + 32) * 4;
+}
 
 __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpParams P) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __half* xs = reinterpret_cast<__half*>(smem);
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar[2];
+    const int rpc = (P.E + 7) / 8;
+    const uint32_t TB = int4_tile_bytes(P.H);
+    uint8_t* tiles = smem;
+    __half* gs = reinterpret_cast<__half*>(smem);  // [rpc][H] gate rows, then the tiles
+    __half* xs = reinterpret_cast<__half*>(smem + moe_up_stage_bytes(P.H, P.E));
     __half* xB = xs + P.H;
     float* red = reinterpret_cast<float*>(xB + P.H);  // [8][16] + 32
     float* lg_mine = red + 160;                       // [32]
@@ -332,7 +442,20 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e0 = rank * rpc, ne = max(0, min(P.E - e0, rpc));
 
+    if (threadIdx.x == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar[0], (uint32_t)ne * P.H * 2);
+        if (ne > 0) tma_load_1d(gs, P.gate + (size_t)e0 * P.H, (uint32_t)ne * P.H * 2, &bar[0]);
+        l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
+    }
+    pdl_trigger();
+    pdl_wait();
     if (P.xn) {
         for (int i = threadIdx.x; i < P.H; i += blockDim.x) xs[i] = P.xn[i];
         __syncthreads();
@@ -341,29 +464,33 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     } else {
         norm_prologue(P.h, nullptr, nullptr, nullptr, P.norm_w, P.H, P.eps, xs, xB, red + 128);
     }
-    // router rows [rank*rpc, rank*rpc + rpc): one warp per row, CUDA cores
-    const int rpc = (P.E + 7) / 8;
-    for (int j = warp; j < rpc; j += 8) {
-        const int e = rank * rpc + j;
+    // router rows of this cluster member: one warp per half row, from smem
+    const bool gate_ok = stage_wait(&bar[0]);
+    float* lgp = lg_all;  // [2*rpc] half-row partials (lg_all is filled later)
+    for (int item = warp; item < 2 * rpc; item += 8) {
+        const int j = item >> 1;
         float acc = 0.f;
-        if (e < P.E) {
-            const __half* gr = P.gate + (size_t)e * P.H;
-            for (int k = lane * 8; k < P.H; k += 256) {
+        if (j < ne && gate_ok) {
+            const int half = P.H >> 1, k0 = (item & 1) * half;
+            const __half* gr = gs + (size_t)j * P.H + k0;
+            for (int k = lane * 8; k < half; k += 256) {
                 uint4 wv = *reinterpret_cast<const uint4*>(gr + k);
-                uint4 xv = *reinterpret_cast<const uint4*>(xs + k);
+                uint4 xv = *reinterpret_cast<const uint4*>(xs + k0 + k);
                 const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
                 const __half2* x2 = reinterpret_cast<const __half2*>(&xv);
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    float2 a = __half22float2(w2[i]), b = __half22float2(x2[i]);
+                for (int q = 0; q < 4; q++) {
+                    float2 a = __half22float2(w2[q]), b = __half22float2(x2[q]);
                     acc = fmaf(a.x, b.x, acc);
                     acc = fmaf(a.y, b.y, acc);
                 }
             }
             acc = warp_sum(acc);
         }
-        if (lane == 0) lg_mine[j] = acc;
+        if (lane == 0) lgp[item] = acc;
     }
+    __syncthreads();
+    for (int j = threadIdx.x; j < rpc; j += blockDim.x) lg_mine[j] = lgp[2 * j] + lgp[2 * j + 1];
     cluster.sync();
     for (int e = threadIdx.x; e < P.E; e += blockDim.x) {
         const float* src = cluster.map_shared_rank(lg_mine, e / rpc);
@@ -376,26 +503,37 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
         P.route_idx[threadIdx.x] = sidx[threadIdx.x];
         P.route_w[threadIdx.x] = sw[threadIdx.x];
     }
-    if (blockIdx.x == 0 && P.xn_store)
-        for (int i = threadIdx.x; i < P.H; i += blockDim.x) P.xn_store[i] = xs[i];
-
-    const int tiles = P.I / 16;
+    const int tiles_per = P.I / 16;
     const int item = blockIdx.x;
-    if (item >= P.topk * tiles) return;
-    const int t = item / tiles, row0 = (item % tiles) * 16;
-    const int e = sidx[t];
-    const void* const* ex = P.experts + (size_t)e * 6;
-    const int tile = warp & 1;
-    const uint8_t* wp = (const uint8_t*)ex[tile ? 2 : 0];
-    const __half* ws = (const __half*)ex[tile ? 3 : 1];
-    float y0 = 0.f, y1 = 0.f;
-    int4_tile_dot<2>(wp, ws, P.I, P.H, row0, warp >> 1, P.H >> 7, 4,
-                     reinterpret_cast<const uint2*>(xB), y0, y1);
-    __syncthreads();
-    if ((lane & 3) == 0) {
-        red[warp * 16 + (lane >> 2)] = y0;
-        red[warp * 16 + (lane >> 2) + 8] = y1;
+    const bool active = item < P.topk * tiles_per;
+    const int t = active ? item / tiles_per : 0, row0 = active ? (item % tiles_per) * 16 : 0;
+    const void* const* ex = P.experts + (size_t)sidx[t] * 6;
+    if (threadIdx.x == 0) {
+        if (active) {
+            mbar_arrive_expect_tx(&bar[1], 2 * TB);
+            tma_tile_int4((const uint8_t*)ex[0], (const __half*)ex[1], P.H, row0, tiles, &bar[1]);
+            tma_tile_int4((const uint8_t*)ex[2], (const __half*)ex[3], P.H, row0, tiles + TB, &bar[1]);
+        }
+        // the selected experts' w2 (read by moe_down next) into L2, over the grid
+        L2Ranges R;
+        R.count = 0;
+        for (int k = 0; k < P.topk && R.count < 7; k++) {
+            const void* const* e2 = P.experts + (size_t)sidx[k] * 6;
+            R.p[R.count] = (const char*)e2[4];
+            R.n[R.count++] = (unsigned long long)P.H * (P.I >> 1);
+            R.p[R.count] = (const char*)e2[5];
+            R.n[R.count++] = (unsigned long long)P.H * (P.I >> 6);
+        }
+        l2_prefetch_share(R, blockIdx.x, gridDim.x);
     }
+    if (!active) return;
+    const int tile = warp & 1;
+    float y0 = 0.f, y1 = 0.f;
+    if (stage_wait(&bar[1]))
+        int4_tile_dot_smem<2>(tiles + tile * TB, P.H, warp >> 1, P.H >> 7, 4,
+                              reinterpret_cast<const uint2*>(xB), y0, y1);
+    __syncthreads();
+    warp_partials(red, warp, y0, y1);
     __syncthreads();
     if (threadIdx.x < 16) {
         const int i = threadIdx.x;
@@ -412,7 +550,8 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
 // ---------------------------------------------------------------------------
 // MoE down: rows [16b, 16b+16) of every selected expert's w2 . mid[t], then
 // acc = half(acc + w_t * o_t) in rank order and h = half(h + acc)
-// (engine.cu:900-904, acc_scaled 556-559, add_inplace 527-530).
+// (engine.cu:900-904, acc_scaled 556-559, add_inplace 527-530).  The expert
+// ids come from moe_up, so the tiles are staged after the dependency wait.
 // ---------------------------------------------------------------------------
 struct MoeDownParams {
     const __half* mid;  // [topk, I]
@@ -421,24 +560,45 @@ struct MoeDownParams {
     const float* route_w;
     __half* h;
     int H, I, topk;
+    L2Ranges next;
 };
 
+__host__ __device__ inline size_t moe_down_smem(int I, int topk) {
+    return (size_t)topk * int4_tile_bytes(I) + (size_t)topk * I * 2 + 8 * topk * 16 * 4;
+}
+
 __global__ void __launch_bounds__(256) k_moe_down(MoeDownParams P) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __half* xB = reinterpret_cast<__half*>(smem);          // [topk][I]
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar;
+    const uint32_t TB = int4_tile_bytes(P.I);
+    uint8_t* tiles = smem;
+    __half* xB = reinterpret_cast<__half*>(smem + (size_t)P.topk * TB);  // [topk][I]
     float* red = reinterpret_cast<float*>(xB + (size_t)P.topk * P.I);  // [8][topk][16]
+    const int warp = threadIdx.x >> 5, row0 = blockIdx.x * 16;
+    stage_begin(&bar);
+    if (threadIdx.x == 0) l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar, (uint32_t)P.topk * TB);
+        for (int t = 0; t < P.topk; t++) {
+            const void* const* ex = P.experts + (size_t)P.route_idx[t] * 6;
+            tma_tile_int4((const uint8_t*)ex[4], (const __half*)ex[5], P.I, row0, tiles + t * TB, &bar);
+        }
+    }
     for (int e = threadIdx.x; e < P.topk * (P.I / 4); e += blockDim.x) {
         const int t = e / (P.I / 4), r = e % (P.I / 4);
         build_xB_entry(P.mid + (size_t)t * P.I, xB + (size_t)t * P.I, r);
     }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row0 = blockIdx.x * 16;
     const int KG = P.I >> 7;
+    const bool ok = stage_wait(&bar);
+    const int lane = threadIdx.x & 31;
     for (int t = 0; t < P.topk; t++) {
-        const void* const* ex = P.experts + (size_t)P.route_idx[t] * 6;
         float y0 = 0.f, y1 = 0.f;
-        int4_tile_dot<2>((const uint8_t*)ex[4], (const __half*)ex[5], P.H, P.I, row0, warp, KG, 8,
-                         reinterpret_cast<const uint2*>(xB + (size_t)t * P.I), y0, y1);
+        if (ok)
+            int4_tile_dot_smem<2>(tiles + t * TB, P.I, warp, KG, 8,
+                                  reinterpret_cast<const uint2*>(xB + (size_t)t * P.I), y0, y1);
         if ((lane & 3) == 0) {
             red[(warp * P.topk + t) * 16 + (lane >> 2)] = y0;
             red[(warp * P.topk + t) * 16 + (lane >> 2) + 8] = y1;
@@ -461,8 +621,10 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeDownParams P) {
 // ---------------------------------------------------------------------------
 // Final norm + tied lm_head (fp16 [V,H]) + argmax + next-token bookkeeping
 // (engine.cu:932-940).  One 16-row tile per warp, all tiles resident in one
-// wave.  Argmax: 64-bit keys (argmax_key) reduced per CTA, then atomicMax;
-// the last CTA (atomic ticket) publishes the token, advances pos and resets.
+// wave, weights streamed with 16-byte loads (their first rows pulled into L2
+// before the dependency wait).  Argmax: 64-bit keys (argmax_key) reduced per
+// CTA, then atomicMax; the last CTA (atomic ticket) publishes the token,
+// advances pos and resets.
 // ---------------------------------------------------------------------------
 struct LmHeadParams {
     const __half* h;
@@ -478,6 +640,7 @@ struct LmHeadParams {
     int ring;
     int H, V;
     float eps;
+    L2Ranges next;  // the first kernels of the next step
 };
 
 __global__ void __launch_bounds__(256) k_lmhead(LmHeadParams P) {
@@ -486,16 +649,21 @@ __global__ void __launch_bounds__(256) k_lmhead(LmHeadParams P) {
     float* red = reinterpret_cast<float*>(xs + P.H);
     __shared__ unsigned long long kred[8];
     __shared__ int s_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = (P.V + 15) / 16;
+    const int tile0 = blockIdx.x * 8 + warp;
+    if (threadIdx.x == 0) l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
+    if (tile0 < ntiles && lane == 0) l2_prefetch_bulk_rows(P.W, P.V, P.H, tile0 * 16, 16);
+    pdl_trigger();
+    pdl_wait();
     for (int i = threadIdx.x; i < P.H; i += blockDim.x) xs[i] = P.h[i];
     __syncthreads();
     if (blockIdx.x == 0 && P.hidden_out)
         for (int i = threadIdx.x; i < P.H; i += blockDim.x) P.hidden_out[i] = xs[i];
     rmsnorm_smem(xs, P.norm_w, xs, P.H, P.eps, red);
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntiles = (P.V + 15) / 16;
     unsigned long long best = 0ull;
-    for (int tile = blockIdx.x * 8 + warp; tile < ntiles; tile += gridDim.x * 8) {
+    for (int tile = tile0; tile < ntiles; tile += gridDim.x * 8) {
         float y0 = 0.f, y1 = 0.f;
         f16_tile_dot<4>(P.W, P.V, P.H, tile * 16, 0, P.H >> 5, 1, xs, y0, y1);
         const int r0 = tile * 16 + (lane >> 2), r1 = r0 + 8;

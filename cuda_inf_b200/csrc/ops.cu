@@ -10,6 +10,10 @@
 #include "common.cuh"
 #include "route.cuh"
 
+// Device-side error word of this translation unit (bit 0: a bounded wait on
+// a weight-staging barrier timed out).
+static __device__ unsigned g_ops_err;
+
 // ---------------------------------------------------------------------------
 // status
 // ---------------------------------------------------------------------------
@@ -40,25 +44,42 @@ extern "C" const char* cuinf_version(void) { return "cuinf-b200 0.1 (sm_100a)"; 
 
 // ---------------------------------------------------------------------------
 // INT4 GEMV (gemv_int4, engine.cu:83-109)
-// grid (ceil(N/16), M), 256 threads.  Each CTA: one 16-row tile, the 8 warps
-// interleave over the K groups (warp w takes groups w, w+8, ...), so at any
-// time the CTA streams 512 contiguous bytes of each of its 16 rows.
+// grid (ceil(N/16), M), 256 threads.  Each CTA owns one 16-row tile: thread 0
+// stages the tile (packed rows + scales) into shared memory with TMA bulk
+// copies while the CTA permutes x into B-fragment order; the 8 warps then
+// take the K groups w, w+8, ... (ragged or unaligned tiles use direct loads).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_gemv_int4(const __half* __restrict__ x,
                                                    const uint8_t* __restrict__ packed,
                                                    const __half* __restrict__ scales,
-                                                   float* __restrict__ y, int N, int K) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __half* xB = reinterpret_cast<__half*>(smem);
-    float* red = reinterpret_cast<float*>(smem + (size_t)K * 2);  // [8][16]
+                                                   float* __restrict__ y, int N, int K, int use_tma) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar;
     const int m = blockIdx.y, row0 = blockIdx.x * 16;
+    const bool tma = use_tma && row0 + 16 <= N;
+    uint8_t* tile = smem;
+    __half* xB = reinterpret_cast<__half*>(smem + (use_tma ? int4_tile_bytes(K) : 0));
+    float* red = reinterpret_cast<float*>(xB + K);  // [8][16]
+    if (tma) {
+        if (threadIdx.x == 0) mbar_init(&bar, 1);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            mbar_arrive_expect_tx(&bar, int4_tile_bytes(K));
+            tma_tile_int4(packed, scales, K, row0, tile, &bar);
+        }
+    }
     const __half* xm = x + (size_t)m * K;
     for (int e = threadIdx.x; e < K / 4; e += blockDim.x) build_xB_entry(xm, xB, e);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float y0 = 0.f, y1 = 0.f;
-    int4_tile_dot<2>(packed, scales, N, K, row0, warp, K >> 7, 8,
-                     reinterpret_cast<const uint2*>(xB), y0, y1);
+    if (tma) {
+        if (mbar_wait_bounded(&bar, 0, &g_ops_err))
+            int4_tile_dot_smem<2>(tile, K, warp, K >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
+    } else {
+        int4_tile_dot<2>(packed, scales, N, K, row0, warp, K >> 7, 8,
+                         reinterpret_cast<const uint2*>(xB), y0, y1);
+    }
     if ((lane & 3) == 0) {
         red[warp * 16 + (lane >> 2)] = y0;
         red[warp * 16 + (lane >> 2) + 8] = y1;
@@ -81,14 +102,15 @@ extern "C" int cuinf_gemv_int4(const void* x, const uint8_t* packed, const void*
     REQUIRE(((uintptr_t)packed & 15) == 0, "packed must be 16-byte aligned");
     REQUIRE(((uintptr_t)scales & 1) == 0 && ((uintptr_t)x & 1) == 0, "misaligned fp16 pointer");
     REQUIRE(M <= 65535, "M too large");
-    size_t smem = (size_t)K * 2 + 8 * 16 * 4;
-    REQUIRE(smem <= 200 * 1024, "K too large");
+    const int use_tma = ((uintptr_t)scales & 15) == 0;
+    size_t smem = (size_t)K * 2 + 8 * 16 * 4 + (use_tma ? int4_tile_bytes(K) : 0);
+    REQUIRE(smem <= 227 * 1024, "K too large");
     if (smem > 48 * 1024)
         CUINF_TRY(cudaFuncSetAttribute(k_gemv_int4, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem));
     dim3 grid((N + 15) / 16, M);
     k_gemv_int4<<<grid, 256, smem, ST(stream)>>>((const __half*)x, packed, (const __half*)scales,
-                                                 y, N, K);
+                                                 y, N, K, use_tma);
     return cuinf_launch_status();
 }
 

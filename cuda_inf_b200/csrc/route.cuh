@@ -44,6 +44,17 @@ __device__ __forceinline__ void route_select_warp(const float* logits, const __h
             int oe = __shfl_xor_sync(0xffffffffu, be, o);
             if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
         }
+        if (be == 0x7fffffff) {
+            // no candidate above -1e30 (NaN logits): take the smallest unused
+            // index so the id is always a valid expert
+            int cand = 0x7fffffff;
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (!used[j]) cand = min(cand, lane + 32 * j);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) cand = min(cand, __shfl_xor_sync(0xffffffffu, cand, o));
+            be = cand;
+        }
         float sv = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; j++)

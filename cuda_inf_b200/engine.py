@@ -9,6 +9,13 @@ from ._lib import CuinfConfig, check, lib
 from .weights import default_config
 
 
+def device_error():
+    """Engine kernels' device error flags (0 = none)."""
+    v = ctypes.c_uint(0)
+    check(lib().cuinf_device_error(ctypes.byref(v)))
+    return v.value
+
+
 class _DevArray:
     def __init__(self, ptr, shape, typestr):
         self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr,
@@ -90,6 +97,13 @@ class Session:
         check(lib().cuinf_generate(self._h, p, len(prompt), n_new, eos, o, ctypes.byref(n)))
         return list(o[:n.value])
 
+    OPT_PREFETCH, OPT_PDL = 1, 2
+
+    def set_option(self, option, value):
+        """OPT_PREFETCH: L2 prefetch of upcoming weights; OPT_PDL: programmatic
+        dependent launch between the step's kernels (both default on)."""
+        check(lib().cuinf_session_set_option(self._h, int(option), int(value)))
+
     def keep_logits(self, on=True):
         check(lib().cuinf_session_keep_logits(self._h, 1 if on else 0))
 
@@ -115,3 +129,16 @@ class Session:
     @property
     def kernels_per_step(self):
         return lib().cuinf_session_kernels_per_step(self._h)
+
+    def profile_step(self, token=-1):
+        """One step launched kernel by kernel with events: list of
+        (name, ms, algorithmic bytes) per kernel."""
+        cap, nl = 1024, 32
+        ms = (ctypes.c_float * cap)()
+        by = (ctypes.c_double * cap)()
+        names = ctypes.create_string_buffer(cap * nl)
+        n = ctypes.c_int(0)
+        check(lib().cuinf_session_profile_step(self._h, int(token), cap, ms, by, names, nl,
+                                               ctypes.byref(n)))
+        return [(names.raw[i * nl:(i + 1) * nl].split(b"\0")[0].decode(), ms[i], by[i])
+                for i in range(n.value)]

@@ -124,15 +124,15 @@ def quantize_int4_host(w):
 
 
 def write_model(out_dir, c, get_tensor):
-    """Write weights.bin + index.bin from float32 tensors get_tensor(name)
-    (the conv kernel may be given as [H,1,3] like the checkpoint).  Returns
-    the sha256 of weights.bin."""
+    """Write weights.bin + index.bin from float32 tensors get_tensor(name,
+    shape) (shape as stored; the conv kernel may come as [H,1,3] like the
+    checkpoint).  Returns the sha256 of weights.bin."""
     os.makedirs(out_dir, exist_ok=True)
     ents = layout(c)
     h = hashlib.sha256()
     with open(os.path.join(out_dir, "weights.bin"), "wb") as f:
         for e in ents:
-            w = np.asarray(get_tensor(e.name), dtype=np.float32)
+            w = np.asarray(get_tensor(e.name, e.shape), dtype=np.float32)
             if e.kind == FP16:
                 b = w.reshape(e.shape).astype(np.float16).tobytes()
             else:

@@ -188,12 +188,28 @@ int cuinf_generate(cuinf_session* s, const int* prompt, int n_prompt, int n_new,
 /* Device pointer to this session's last fp32 logits [vocab] (filled only while
  * cuinf_session_keep_logits(s, 1) is set) and its final hidden state fp16 [H]. */
 int cuinf_session_keep_logits(cuinf_session* s, int on);
+/* Session options (rebuild the step graph; both default to 1):
+ * CUINF_OPT_PREFETCH: each kernel pulls the next kernels' weights into L2;
+ * CUINF_OPT_PDL: kernels launch with programmatic stream serialization so a
+ * kernel's weight staging overlaps its predecessor. */
+#define CUINF_OPT_PREFETCH 1
+#define CUINF_OPT_PDL 2
+int cuinf_session_set_option(cuinf_session* s, int option, int value);
+/* Device error flags of the engine kernels (bit 0: a bounded wait on a
+ * weight-staging barrier timed out and the kernel skipped its math). */
+int cuinf_device_error(unsigned* flags);
 const float* cuinf_session_logits(const cuinf_session* s);
 const void* cuinf_session_hidden(const cuinf_session* s);
 /* Host copy of the last step's routing decisions [n_moe_layers*top_k]. */
 int cuinf_session_routes(cuinf_session* s, int* idx, float* w);
 /* Number of kernels one decode step launches (for the bench's accounting). */
 int cuinf_session_kernels_per_step(const cuinf_session* s);
+/* One decode step launched kernel by kernel (not as the graph) with a CUDA
+ * event after each launch: ms[i] = duration of kernel i, bytes[i] = its
+ * algorithmic bytes (weights + activations), names[i*name_len] its name.
+ * Advances the session like cuinf_decode_step. */
+int cuinf_session_profile_step(cuinf_session* s, int token, int max_kernels, float* ms,
+                               double* bytes, char* names, int name_len, int* n_kernels);
 
 #ifdef __cplusplus
 }

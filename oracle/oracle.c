@@ -598,9 +598,17 @@ int orc_state_pos(const orc_state* s) { return s->pos; }
 const int* orc_state_route_idx(const orc_state* s) { return s->route_idx; }
 const float* orc_state_route_w(const orc_state* s) { return s->route_w; }
 
-/* layer_forward for S == 1 (engine.cu:784-908) + compute_logits_last (932-940) */
 int orc_forward_token(const orc_model* m, orc_state* s, int token, float* logits_out,
                       uint16_t* hidden_out) {
+    return orc_forward_token_ex(m, s, token, NULL, NULL, logits_out, hidden_out);
+}
+
+/* layer_forward for S == 1 (engine.cu:784-908) + compute_logits_last (932-940).
+ * forced_idx [n_moe][top_k] (nullable) replaces the selected experts (the
+ * weights are still the oracle's sigmoid of those experts, normalized);
+ * scores_out [n_moe][n_experts] (nullable) receives sigmoid+bias scores. */
+int orc_forward_token_ex(const orc_model* m, orc_state* s, int token, const int* forced_idx,
+                         float* scores_out, float* logits_out, uint16_t* hidden_out) {
     const orc_config* c = &m->cfg;
     const int H = c->hidden, hd = c->head_dim, nh = c->n_heads, nkv = c->n_kv_heads;
     const float eps = c->norm_eps;
@@ -675,6 +683,18 @@ int orc_forward_token(const orc_model* m, orc_state* s, int token, float* logits
             orc_gemv_fp16(xn, L->gate, rl, 1, E, H);
             for (int e = 0; e < E; e++) eb[e] = orc_h2f(L->ebias[e]);
             orc_moe_select(rl, eb, E, K, idx, w);
+            if (scores_out)
+                for (int e = 0; e < E; e++)
+                    scores_out[moe_i * E + e] = 1.0f / (1.0f + expf(-rl[e])) + eb[e];
+            if (forced_idx) {  /* same weight rule (engine.cu:890-892) on the given experts */
+                float wsum = 0.0f;
+                for (int t = 0; t < K; t++) {
+                    idx[t] = forced_idx[moe_i * K + t];
+                    w[t] = 1.0f / (1.0f + expf(-rl[idx[t]]));
+                }
+                for (int t = 0; t < K; t++) wsum += w[t];
+                for (int t = 0; t < K; t++) w[t] /= (wsum + 1e-6f);
+            }
             for (int t = 0; t < K; t++) {
                 s->route_idx[moe_i * K + t] = idx[t];
                 s->route_w[moe_i * K + t] = w[t];

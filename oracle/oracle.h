@@ -99,6 +99,12 @@ int        orc_state_pos(const orc_state* s);
  * hidden state (pre-norm, fp16) when hidden != NULL.  Returns the argmax. */
 int        orc_forward_token(const orc_model* m, orc_state* s, int token,
                              float* logits, uint16_t* hidden);
+/* Same, with optional forced expert choices [n_moe][top_k] (the weights are
+ * recomputed from the oracle's router for those experts) and the oracle's
+ * own selection scores sigmoid(logit)+bias written to scores [n_moe][E]. */
+int        orc_forward_token_ex(const orc_model* m, orc_state* s, int token,
+                                const int* forced_idx, float* scores,
+                                float* logits, uint16_t* hidden);
 /* Router decisions of the last forward_token: [n_moe_layers][top_k]. */
 const int*   orc_state_route_idx(const orc_state* s);
 const float* orc_state_route_w(const orc_state* s);

@@ -58,6 +58,7 @@ _SIGS = {
     "orc_state_free": (None, [P]),
     "orc_state_pos": (I, [P]),
     "orc_forward_token": (I, [P, P, I, P, P]),
+    "orc_forward_token_ex": (I, [P, P, I, P, P, P, P]),
     "orc_state_route_idx": (P, [P]),
     "orc_state_route_w": (P, [P]),
     "orc_set_threads": (None, [I]),
@@ -275,6 +276,19 @@ class State:
         hid = np.empty(c.hidden, np.float16) if want_hidden else None
         nxt = lib().orc_forward_token(self.model._h, self._h, int(token), _ptr(lg), _ptr(hid))
         return nxt, lg, hid
+
+    def forward_ex(self, token, forced_idx=None):
+        """Forward with optional forced experts [n_moe*top_k]; returns
+        (argmax, logits, hidden, scores [n_moe, E])."""
+        c = self.model.cfg
+        n_moe = c.n_layers - c.n_dense
+        lg = np.empty(c.vocab, np.float32)
+        hid = np.empty(c.hidden, np.float16)
+        sc = np.empty((max(1, n_moe), max(1, c.n_experts)), np.float32)
+        fi = None if forced_idx is None else np.ascontiguousarray(forced_idx, np.int32)
+        nxt = lib().orc_forward_token_ex(self.model._h, self._h, int(token), _ptr(fi), _ptr(sc),
+                                         _ptr(lg), _ptr(hid))
+        return nxt, lg, hid, sc
 
     def routes(self):
         c = self.model.cfg

@@ -50,7 +50,9 @@ def shape_of(name, c=SMALL):
     raise KeyError(name)
 
 
-def fake_tensor(name, c=SMALL, base_seed=20261201):
+def fake_tensor(name, stored_shape=None, c=SMALL, base_seed=20261201):
+    """stored_shape (as the writer stores it) is accepted and ignored: the
+    checkpoint shape comes from the name."""
     shape = shape_of(name, c)
     rng = np.random.default_rng((zlib.crc32(name.encode()) + base_seed) & 0xFFFFFFFF)
     if name.endswith("norm.weight") or name.endswith("layernorm.weight"):

@@ -163,3 +163,26 @@ def test_oracle_moe_select():
         sel, ww = _select_ref(lg, b, 4)
         assert list(idx) == sel
         np.testing.assert_allclose(w, ww, rtol=2e-7)
+
+
+def test_argmax_key_rule_matches_reference_tree():
+    """The device argmax encodes ties as 'smallest bit-reversed index mod 256,
+    then smallest index' (argmax_key in csrc/common.cuh); that rule equals the
+    result of argmax_kernel's tree reduction on heavy-tie inputs."""
+    def brev8(r):
+        return int("{:08b}".format(r)[::-1], 2)
+
+    def key_argmax(v):
+        best = None
+        for i, x in enumerate(v):
+            if x > -1e30:
+                k = (float(x), -((brev8(i & 255) << 23) | (i >> 8)))
+                if best is None or k > best[0]:
+                    best = (k, i)
+        return best[1] if best else 0
+
+    rng = np.random.default_rng(4)
+    for _ in range(60):
+        n = int(rng.integers(1, 3000))
+        v = rng.integers(0, int(rng.integers(1, 6)), n).astype(np.float32)
+        assert key_argmax(v) == _argmax_ref_kernel(v)

@@ -1,0 +1,139 @@
+"""GPU decode engine vs the whole-model CPU oracle on a small model that
+exercises every layer kind (conv, attention with GQA 4, dense and MoE FFN),
+FP8 KV commits at tokens 64 and 128, and a vocab that is not a multiple of 16.
+
+Routing is compared, not inherited: two faithful implementations round the
+fp16 activations identically but sum in different orders, so the residual can
+differ by an fp16 ulp, which moves router logits by ~1e-4 and can flip the
+top-k when two expert scores are that close.  Each step therefore
+  * runs the oracle with the engine's expert choices (both states stay on
+    the same experts), and
+  * asserts the engine chose exactly the oracle's own top-k whenever the
+    oracle's k-th vs (k+1)-th score margin exceeds ROUTE_MARGIN.
+Logits must agree within LOGIT_TOL (max-abs error / max-abs logit; the
+recurrent KV/conv state carries fp16 one-ulp differences from step to step)
+and the argmax must agree whenever the oracle's top-2 logit margin exceeds
+TIE_MARGIN.
+"""
+import zlib
+
+import numpy as np
+import pytest
+
+from oracle import pyoracle as orc
+from cuda_inf_b200 import weights
+from cuda_inf_b200.engine import Model, Session, device_error
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-2
+TIE_MARGIN = 1e-3
+ROUTE_MARGIN = 1e-3
+
+TINY = dict(hidden=256, n_layers=6, n_heads=4, n_kv_heads=1, vocab=1000, n_dense=1, n_experts=8,
+            top_k=2, moe_inter=256, dense_inter=384, attn_layers=(1, 4))
+
+
+def tiny_tensor(name, shape):
+    rng = np.random.default_rng(zlib.crc32(name.encode()))
+    k = weights.init_kind(name)
+    if k == "norm":
+        return (1 + 0.02 * rng.standard_normal(shape)).astype(np.float32)
+    if k == "bias":
+        return (0.1 * rng.standard_normal(shape)).astype(np.float32)
+    if k == "conv":
+        return rng.uniform(-0.577, 0.577, shape).astype(np.float32)
+    return (0.05 * rng.standard_normal(shape)).astype(np.float32)
+
+
+@pytest.fixture(scope="module")
+def tiny(tmp_path_factory, cuda):
+    d = tmp_path_factory.mktemp("tiny")
+    cfg = weights.make_config(**TINY)
+    weights.write_model(str(d), cfg, tiny_tensor)
+    blob = np.fromfile(d / "weights.bin", np.uint8)
+    index = open(d / "index.bin", "rb").read()
+    om = orc.Model(weights.config_dict(cfg), blob, index)
+    gm = Model.load(str(d), cfg)
+    return cfg, om, gm
+
+
+def own_topk(scores, k):
+    """The reference's selection on given scores (strict '>', lowest index)."""
+    order = sorted(range(len(scores)), key=lambda e: (-scores[e], e))
+    return order[:k], (scores[order[k - 1]] - scores[order[k]]) if len(scores) > k else np.inf
+
+
+def run_compare(cfg, om, s, tokens, max_ctx):
+    st = om.state(max_ctx)
+    worst, near_ties, checked = 0.0, 0, 0
+    got_tokens = []
+    for i, t in enumerate(tokens):
+        got = s.step(int(t))
+        got_tokens.append(got)
+        gi, _ = s.routes()
+        gi = np.array(gi, np.int32).reshape(-1, cfg.top_k)
+        ref, lg, _, sc = st.forward_ex(int(t), forced_idx=gi.ravel())
+        for l in range(gi.shape[0]):
+            sel, margin = own_topk(sc[l], cfg.top_k)
+            if margin > ROUTE_MARGIN:
+                assert list(gi[l]) == sel, (i, l, list(gi[l]), sel, margin)
+                checked += 1
+            else:
+                near_ties += 1
+        glog = s.logits().cpu().numpy()
+        e = float(np.max(np.abs(glog - lg)) / np.max(np.abs(lg)))
+        worst = max(worst, e)
+        assert e < LOGIT_TOL, (i, e)
+        top = np.sort(lg)[::-1]
+        if top[0] - top[1] > TIE_MARGIN * max(1.0, abs(top[0])):
+            assert got == ref, (i, got, ref)
+    return worst, near_ties, checked, got_tokens
+
+
+def test_engine_matches_oracle_teacher_forced(tiny):
+    cfg, om, gm = tiny
+    s = Session(gm, max_ctx=160)
+    s.keep_logits(True)
+    toks = np.random.default_rng(123).integers(0, cfg.vocab, 140)
+    worst, near, checked, _ = run_compare(cfg, om, s, toks, 160)
+    print(f"worst logits rel err {worst:.2e}; routing checked {checked}, near-ties {near}")
+    assert checked > 0.9 * (checked + near)
+    assert device_error() == 0
+
+
+def test_engine_greedy_matches_oracle(tiny):
+    """Free-running greedy generation: the oracle follows the engine's tokens
+    and confirms each one is its own argmax (outside logit near-ties)."""
+    cfg, om, gm = tiny
+    s = Session(gm, max_ctx=96)
+    s.keep_logits(True)
+    prompt = [5, 17, 999, 0, 42]
+    gen = s.generate(prompt, 40)
+    s2 = Session(gm, max_ctx=96)
+    s2.keep_logits(True)
+    seq = prompt + gen[:-1]
+    worst, near, checked, got = run_compare(cfg, om, s2, seq, 96)
+    assert got[len(prompt) - 1:] == gen  # generate() == step-by-step
+    s.reset()
+    assert s.generate(prompt, 40) == gen  # reset restores the initial state
+
+
+def test_kernels_per_step(tiny):
+    cfg, om, gm = tiny
+    s = Session(gm, max_ctx=64)
+    assert s.kernels_per_step == 2 * 4 + 3 * 2 + 2 * 6 + 1
+
+
+@pytest.mark.parametrize("opt", [(1, 0), (2, 0)])
+def test_engine_options_do_not_change_results(tiny, opt):
+    """Turning the L2 prefetch plan or PDL off changes scheduling only."""
+    cfg, om, gm = tiny
+    a = Session(gm, max_ctx=80)
+    b = Session(gm, max_ctx=80)
+    b.set_option(*opt)
+    a.keep_logits(True)
+    b.keep_logits(True)
+    for t in np.random.default_rng(9).integers(0, cfg.vocab, 70):
+        assert a.step(int(t)) == b.step(int(t))
+        assert np.array_equal(a.logits().cpu().numpy(), b.logits().cpu().numpy())
