@@ -78,6 +78,10 @@ _SIGS = {
     "cuinf_session_keep_logits": (c_int, [c_void_p, c_int]),
     "cuinf_session_set_option": (c_int, [c_void_p, c_int, c_int]),
     "cuinf_device_error": (c_int, [ctypes.POINTER(ctypes.c_uint)]),
+    "cuinf_session_uses_megakernel": (c_int, [c_void_p]),
+    "cuinf_session_trace": (c_int, [c_void_p, c_void_p, c_int, c_void_p, ctypes.POINTER(c_int),
+                                    ctypes.POINTER(c_int)]),
+    "cuinf_session_error": (c_int, [c_void_p, c_void_p]),
     "cuinf_session_logits": (c_void_p, [c_void_p]),
     "cuinf_session_hidden": (c_void_p, [c_void_p]),
     "cuinf_session_routes": (c_int, [c_void_p, c_void_p, c_void_p]),

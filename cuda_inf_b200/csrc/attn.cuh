@@ -56,6 +56,137 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// One warp: online-softmax attention of its query heads (A-fragment rows,
+// aq) over units u_begin, u_begin+u_step, ... < u_end of kv head h.  Keeps
+// the running max m_run (base 2, per row), the per-lane partial sum l_run and
+// the output accumulators O (n-tile j holds dims 16c+j and 16c+8+j of row g).
+__device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
+                                                const uint8_t* __restrict__ vc8,
+                                                const __half* __restrict__ ksc,
+                                                const __half* __restrict__ vsc,
+                                                const __half* __restrict__ ktail,
+                                                const __half* __restrict__ vtail, int nkv, int h,
+                                                int n_fp8, int tail_len, float kfac,
+                                                const uint32_t (&aq)[4][2], int u_begin, int u_end,
+                                                int u_step, float& m_run, float& l_run,
+                                                float (&O)[8][4]) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    for (int u = u_begin; u < u_end; u += u_step) {
+        const bool tail = u >= n_fp8;
+        const int valid = tail ? tail_len : CUINF_KVGROUP;
+        const int kbase = u * CUINF_KVGROUP;
+        // ---- S = Q K^T for 64 keys (8 n-tiles of 8 keys) ----
+        float S[8][4];
+#pragma unroll
+        for (int jn = 0; jn < 8; jn++) {
+            S[jn][0] = S[jn][1] = S[jn][2] = S[jn][3] = 0.f;
+            const int kk = 8 * jn + g;  // key within the unit
+            uint32_t kb[8];
+            if (!tail) {
+                uint4 raw = ldg_stream(kc8 + ((size_t)(kbase + kk) * nkv + h) * CUINF_HD + 16 * c);
+                const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    kb[2 * i] = fp8x2_to_h2(w4[i]);
+                    kb[2 * i + 1] = fp8x2_to_h2(w4[i] >> 16);
+                }
+            } else {
+                const __half* kp = ktail + ((size_t)kk * nkv + h) * CUINF_HD + 16 * c;
+                uint4 r0 = *reinterpret_cast<const uint4*>(kp);
+                uint4 r1 = *reinterpret_cast<const uint4*>(kp + 8);
+                kb[0] = r0.x; kb[1] = r0.y; kb[2] = r0.z; kb[3] = r0.w;
+                kb[4] = r1.x; kb[5] = r1.y; kb[6] = r1.z; kb[7] = r1.w;
+            }
+#pragma unroll
+            for (int s = 0; s < 4; s++)
+                mma_16816(S[jn], aq[s][0], 0u, aq[s][1], 0u, kb[2 * s], kb[2 * s + 1]);
+        }
+        const float kscale = tail ? 1.0f : __half2float(ksc[(size_t)u * nkv + h]);
+        const float f = kscale * kfac;
+        float mx = ATTN_NEG;
+#pragma unroll
+        for (int jn = 0; jn < 8; jn++) {
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int key = 8 * jn + 2 * c + i;
+                float s = S[jn][i] * f;
+                s = key < valid ? s : ATTN_NEG;
+                S[jn][i] = s;
+                mx = fmaxf(mx, s);
+            }
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        const float alpha = exp2f(m_run - m_new);
+        float lsum = 0.f;
+#pragma unroll
+        for (int jn = 0; jn < 8; jn++) {
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int key = 8 * jn + 2 * c + i;
+                float p = key < valid ? exp2f(S[jn][i] - m_new) : 0.f;
+                S[jn][i] = p;
+                lsum += p;
+            }
+        }
+        l_run = l_run * alpha + lsum;
+        m_run = m_new;
+        // ---- tmp = P V (4 k-steps of 16 keys, 8 n-tiles of 8 dims) ----
+        float T[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; j++) T[j][0] = T[j][1] = T[j][2] = T[j][3] = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < 4; s2++) {
+            const uint32_t pa0 = pack_h2(S[2 * s2][0], S[2 * s2][1]);
+            const uint32_t pa2 = pack_h2(S[2 * s2 + 1][0], S[2 * s2 + 1][1]);
+            const int ka = 16 * s2 + 2 * c;  // keys ka, ka+1, ka+8, ka+9
+            uint32_t b0[8], b1[8];
+            if (!tail) {
+                const uint8_t* vp = vc8 + ((size_t)(kbase + ka) * nkv + h) * CUINF_HD + 8 * g;
+                const size_t kstride = (size_t)nkv * CUINF_HD;
+                uint2 va = ldg_stream8(vp), vb = ldg_stream8(vp + kstride);
+                uint2 vc = ldg_stream8(vp + 8 * kstride), vd = ldg_stream8(vp + 9 * kstride);
+                uint32_t r;
+                r = prmt(va.x, vb.x, 0x5140u); b0[0] = fp8x2_to_h2(r); b0[1] = fp8x2_to_h2(r >> 16);
+                r = prmt(va.x, vb.x, 0x7362u); b0[2] = fp8x2_to_h2(r); b0[3] = fp8x2_to_h2(r >> 16);
+                r = prmt(va.y, vb.y, 0x5140u); b0[4] = fp8x2_to_h2(r); b0[5] = fp8x2_to_h2(r >> 16);
+                r = prmt(va.y, vb.y, 0x7362u); b0[6] = fp8x2_to_h2(r); b0[7] = fp8x2_to_h2(r >> 16);
+                r = prmt(vc.x, vd.x, 0x5140u); b1[0] = fp8x2_to_h2(r); b1[1] = fp8x2_to_h2(r >> 16);
+                r = prmt(vc.x, vd.x, 0x7362u); b1[2] = fp8x2_to_h2(r); b1[3] = fp8x2_to_h2(r >> 16);
+                r = prmt(vc.y, vd.y, 0x5140u); b1[4] = fp8x2_to_h2(r); b1[5] = fp8x2_to_h2(r >> 16);
+                r = prmt(vc.y, vd.y, 0x7362u); b1[6] = fp8x2_to_h2(r); b1[7] = fp8x2_to_h2(r >> 16);
+            } else {
+                const __half* vp = vtail + ((size_t)ka * nkv + h) * CUINF_HD + 8 * g;
+                const size_t kstride = (size_t)nkv * CUINF_HD;
+                const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+                // keys beyond the tail hold stale data: zero them
+                uint4 va = ka < valid ? *reinterpret_cast<const uint4*>(vp) : z;
+                uint4 vb = ka + 1 < valid ? *reinterpret_cast<const uint4*>(vp + kstride) : z;
+                uint4 vc = ka + 8 < valid ? *reinterpret_cast<const uint4*>(vp + 8 * kstride) : z;
+                uint4 vd = ka + 9 < valid ? *reinterpret_cast<const uint4*>(vp + 9 * kstride) : z;
+                const uint32_t A4[4] = {va.x, va.y, va.z, va.w}, B4[4] = {vb.x, vb.y, vb.z, vb.w};
+                const uint32_t C4[4] = {vc.x, vc.y, vc.z, vc.w}, D4[4] = {vd.x, vd.y, vd.z, vd.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    b0[2 * i] = prmt(A4[i], B4[i], 0x5410u);
+                    b0[2 * i + 1] = prmt(A4[i], B4[i], 0x7632u);
+                    b1[2 * i] = prmt(C4[i], D4[i], 0x5410u);
+                    b1[2 * i + 1] = prmt(C4[i], D4[i], 0x7632u);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) mma_16816(T[j], pa0, 0u, pa2, 0u, b0[j], b1[j]);
+        }
+        const float vscale = tail ? 1.0f : __half2float(vsc[(size_t)u * nkv + h]);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            O[j][0] = O[j][0] * alpha + vscale * T[j][0];
+            O[j][1] = O[j][1] * alpha + vscale * T[j][1];
+        }
+    }
+}
+
 __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     __shared__ __align__(16) float sm[4][16][ATTN_PART_STRIDE];
     __shared__ int s_last;
@@ -98,120 +229,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
 #pragma unroll
     for (int j = 0; j < 8; j++) O[j][0] = O[j][1] = O[j][2] = O[j][3] = 0.f;
 
-    for (int u = u0 + warp; u < u1; u += 4) {
-        const bool tail = u >= n_fp8;
-        const int valid = tail ? tail_len : CUINF_KVGROUP;
-        const int kbase = u * CUINF_KVGROUP;
-        // ---- S = Q K^T for 64 keys (8 n-tiles of 8 keys) ----
-        float S[8][4];
-#pragma unroll
-        for (int jn = 0; jn < 8; jn++) {
-            S[jn][0] = S[jn][1] = S[jn][2] = S[jn][3] = 0.f;
-            const int kk = 8 * jn + g;  // key within the unit
-            uint32_t kb[8];
-            if (!tail) {
-                uint4 raw = ldg_stream(P.kc8 + ((size_t)(kbase + kk) * nkv + h) * CUINF_HD + 16 * c);
-                const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    kb[2 * i] = fp8x2_to_h2(w4[i]);
-                    kb[2 * i + 1] = fp8x2_to_h2(w4[i] >> 16);
-                }
-            } else {
-                const __half* kp = P.ktail + ((size_t)kk * nkv + h) * CUINF_HD + 16 * c;
-                uint4 r0 = *reinterpret_cast<const uint4*>(kp);
-                uint4 r1 = *reinterpret_cast<const uint4*>(kp + 8);
-                kb[0] = r0.x; kb[1] = r0.y; kb[2] = r0.z; kb[3] = r0.w;
-                kb[4] = r1.x; kb[5] = r1.y; kb[6] = r1.z; kb[7] = r1.w;
-            }
-#pragma unroll
-            for (int s = 0; s < 4; s++)
-                mma_16816(S[jn], aq[s][0], 0u, aq[s][1], 0u, kb[2 * s], kb[2 * s + 1]);
-        }
-        const float kscale = tail ? 1.0f : __half2float(P.ksc[(size_t)u * nkv + h]);
-        const float f = kscale * kfac;
-        float mx = ATTN_NEG;
-#pragma unroll
-        for (int jn = 0; jn < 8; jn++) {
-#pragma unroll
-            for (int i = 0; i < 2; i++) {
-                const int key = 8 * jn + 2 * c + i;
-                float s = S[jn][i] * f;
-                s = key < valid ? s : ATTN_NEG;
-                S[jn][i] = s;
-                mx = fmaxf(mx, s);
-            }
-        }
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m_run, mx);
-        const float alpha = exp2f(m_run - m_new);
-        float lsum = 0.f;
-#pragma unroll
-        for (int jn = 0; jn < 8; jn++) {
-#pragma unroll
-            for (int i = 0; i < 2; i++) {
-                const int key = 8 * jn + 2 * c + i;
-                float p = key < valid ? exp2f(S[jn][i] - m_new) : 0.f;
-                S[jn][i] = p;
-                lsum += p;
-            }
-        }
-        l_run = l_run * alpha + lsum;
-        m_run = m_new;
-        // ---- tmp = P V (4 k-steps of 16 keys, 8 n-tiles of 8 dims) ----
-        float T[8][4];
-#pragma unroll
-        for (int j = 0; j < 8; j++) T[j][0] = T[j][1] = T[j][2] = T[j][3] = 0.f;
-#pragma unroll
-        for (int s2 = 0; s2 < 4; s2++) {
-            const uint32_t pa0 = pack_h2(S[2 * s2][0], S[2 * s2][1]);
-            const uint32_t pa2 = pack_h2(S[2 * s2 + 1][0], S[2 * s2 + 1][1]);
-            const int ka = 16 * s2 + 2 * c;  // keys ka, ka+1, ka+8, ka+9
-            uint32_t b0[8], b1[8];
-            if (!tail) {
-                const uint8_t* vp = P.vc8 + ((size_t)(kbase + ka) * nkv + h) * CUINF_HD + 8 * g;
-                const size_t kstride = (size_t)nkv * CUINF_HD;
-                uint2 va = ldg_stream8(vp), vb = ldg_stream8(vp + kstride);
-                uint2 vc = ldg_stream8(vp + 8 * kstride), vd = ldg_stream8(vp + 9 * kstride);
-                uint32_t r;
-                r = prmt(va.x, vb.x, 0x5140u); b0[0] = fp8x2_to_h2(r); b0[1] = fp8x2_to_h2(r >> 16);
-                r = prmt(va.x, vb.x, 0x7362u); b0[2] = fp8x2_to_h2(r); b0[3] = fp8x2_to_h2(r >> 16);
-                r = prmt(va.y, vb.y, 0x5140u); b0[4] = fp8x2_to_h2(r); b0[5] = fp8x2_to_h2(r >> 16);
-                r = prmt(va.y, vb.y, 0x7362u); b0[6] = fp8x2_to_h2(r); b0[7] = fp8x2_to_h2(r >> 16);
-                r = prmt(vc.x, vd.x, 0x5140u); b1[0] = fp8x2_to_h2(r); b1[1] = fp8x2_to_h2(r >> 16);
-                r = prmt(vc.x, vd.x, 0x7362u); b1[2] = fp8x2_to_h2(r); b1[3] = fp8x2_to_h2(r >> 16);
-                r = prmt(vc.y, vd.y, 0x5140u); b1[4] = fp8x2_to_h2(r); b1[5] = fp8x2_to_h2(r >> 16);
-                r = prmt(vc.y, vd.y, 0x7362u); b1[6] = fp8x2_to_h2(r); b1[7] = fp8x2_to_h2(r >> 16);
-            } else {
-                const __half* vp = P.vtail + ((size_t)ka * nkv + h) * CUINF_HD + 8 * g;
-                const size_t kstride = (size_t)nkv * CUINF_HD;
-                const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-                // keys beyond the tail hold stale data: zero them
-                uint4 va = ka < valid ? *reinterpret_cast<const uint4*>(vp) : z;
-                uint4 vb = ka + 1 < valid ? *reinterpret_cast<const uint4*>(vp + kstride) : z;
-                uint4 vc = ka + 8 < valid ? *reinterpret_cast<const uint4*>(vp + 8 * kstride) : z;
-                uint4 vd = ka + 9 < valid ? *reinterpret_cast<const uint4*>(vp + 9 * kstride) : z;
-                const uint32_t A4[4] = {va.x, va.y, va.z, va.w}, B4[4] = {vb.x, vb.y, vb.z, vb.w};
-                const uint32_t C4[4] = {vc.x, vc.y, vc.z, vc.w}, D4[4] = {vd.x, vd.y, vd.z, vd.w};
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    b0[2 * i] = prmt(A4[i], B4[i], 0x5410u);
-                    b0[2 * i + 1] = prmt(A4[i], B4[i], 0x7632u);
-                    b1[2 * i] = prmt(C4[i], D4[i], 0x5410u);
-                    b1[2 * i + 1] = prmt(C4[i], D4[i], 0x7632u);
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 8; j++) mma_16816(T[j], pa0, 0u, pa2, 0u, b0[j], b1[j]);
-        }
-        const float vscale = tail ? 1.0f : __half2float(P.vsc[(size_t)u * nkv + h]);
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            O[j][0] = O[j][0] * alpha + vscale * T[j][0];
-            O[j][1] = O[j][1] * alpha + vscale * T[j][1];
-        }
-    }
+    attn_warp_units(P.kc8, P.vc8, P.ksc, P.vsc, P.ktail, P.vtail, nkv, h, n_fp8, tail_len, kfac, aq,
+                    u0 + warp, u1, 4, m_run, l_run, O);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
 

@@ -72,21 +72,36 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+// Non-blocking test of phase `parity` of bar.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
 }
-// Wait for phase `parity` of bar with an iteration limit.  On time-out the
-// flag word (if given) is set and false returned; the caller then skips its
-// math but still waits (bounded) before exiting so no copy targets freed smem.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
+    return t;
+}
+// Every wait in these kernels gives up after this long (wall time), sets an
+// error flag and lets the kernel finish.
+#define CUINF_WAIT_LIMIT_NS 4000000000ull
+// Wait for phase `parity` of bar, at most CUINF_WAIT_LIMIT_NS.  On time-out
+// the flag word (if given) is set and false returned; the caller then skips
+// its math but still waits (bounded) before exiting so no copy targets freed
+// shared memory.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* flag) {
-    for (int i = 0; i < (1 << 22); i++)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) break;
+        __nanosleep(32);
+    }
     if (flag) atomicOr(flag, 1u);
     return false;
 }

@@ -15,6 +15,7 @@
 
 #include "attn.cuh"
 #include "engine_kernels.cuh"
+#include "megakernel.cuh"
 
 #define REQUIRE(cond, msg) \
     do {                   \
@@ -493,11 +494,26 @@ struct cuinf_session {
     bool keep_logits = false;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
-    int* pinned = nullptr;  // [0] token in, [1] token out
+    // Pinned staging for the per-step token copies: input tokens go through a
+    // ring of slots, each reused only after the event of its last copy
+    // (asynchronous steps may be queued far ahead of the device).
+    static const int kTokRing = 64;
+    int* pinned = nullptr;  // [0, kTokRing) token in, [kTokRing] token out
+    cudaEvent_t tok_ev[kTokRing] = {};
+    int tok_slot = 0;
     int host_pos = 0;
     int num_sms = 148;
     bool prefetch = true;  // L2 prefetch plans (cross-kernel weight streaming)
     bool pdl = true;       // programmatic dependent launch between the step's kernels
+    // persistent megakernel (one cooperative launch per step)
+    bool mk_ok = false, use_mk = true;
+    MkParams mk;
+    size_t mk_smem = 0;
+    int mk_grid = 0;
+    unsigned* mk_words = nullptr;  // [0] gbar [1] abort [2] err [3] lm_tick [4..6] failure info
+    unsigned long long* mk_trace = nullptr;  // per-stage timestamps when tracing is on
+    bool trace = false;
+    std::vector<int> mk_kinds;  // stage kinds, for trace reports
 };
 
 template <class T>
@@ -576,9 +592,139 @@ static void plan_prefetch(const std::vector<Launch>& L, std::vector<L2Ranges>& p
     }
 }
 
+// Builds the megakernel's device tables (layer pointers, stage program) and
+// buffers; leaves s->mk_ok false when the device or the model does not fit
+// (the multi-kernel step is then used).
+static int setup_megakernel(cuinf_session* s) {
+    const cuinf_model* m = s->m;
+    const cuinf_config& c = m->cfg;
+    const int H = c.hidden, nh = c.n_heads, nkv = c.n_kv_heads, gqa = nh / nkv;
+    int dev = 0, coop = 0;
+    CUINF_TRY(cudaGetDevice(&dev));
+    CUINF_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+    int max_smem = 0;
+    CUINF_TRY(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    if (!coop || c.top_k > 5 || c.n_experts > 256) return CUINF_OK;
+    const int xbn = std::max(std::max(H, nh * 64), std::max(c.dense_inter, c.top_k * c.moe_inter));
+    const size_t fixed = mk_layout(H, xbn, 0, gqa).total;
+    const size_t static_smem = sizeof(MkHeader) + 256;
+    if ((size_t)max_smem < fixed + static_smem + 64 * 1024) return CUINF_OK;
+    int ring = (int)(((size_t)max_smem - fixed - static_smem) / 1024 * 1024);
+    // the largest slab must fit the ring
+    const size_t slab_max = std::max(
+        std::max((size_t)c.n_experts * H * 2, (size_t)16 * H * 2),
+        std::max((size_t)3 * int4_tile_bytes(H),
+                 std::max((size_t)c.top_k * int4_tile_bytes(c.moe_inter),
+                          (size_t)int4_tile_bytes(std::max(c.dense_inter, nh * 64)))));
+    if (slab_max > (size_t)ring) return CUINF_OK;
+    const size_t smem = mk_layout(H, xbn, ring, gqa).total;
+    CUINF_TRY(cudaFuncSetAttribute(k_decode_mk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int per_sm = 0;
+    CUINF_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mk, MK_THREADS, smem));
+    if (per_sm < 1) return CUINF_OK;
+    const int G = s->num_sms;
+
+    std::vector<MkLayer> layers(c.n_layers);
+    std::vector<MkStage> stages;
+    for (int l = 0; l < c.n_layers; l++) {
+        const LayerW& L = m->L[l];
+        MkLayer& Y = layers[l];
+        memset(&Y, 0, sizeof(Y));
+        Y.op_norm = L.op_norm;
+        Y.ffn_norm = L.ffn_norm;
+        if (c.attn_layer[l]) {
+            AttnState& A = s->attn[l];
+            Y.wq = L.wq.p; Y.sq = L.wq.s; Y.wk = L.wk.p; Y.sk = L.wk.s; Y.wv = L.wv.p; Y.sv = L.wv.s;
+            Y.q_ln = L.q_ln; Y.k_ln = L.k_ln;
+            Y.kc8 = A.kc8; Y.vc8 = A.vc8; Y.ksc = A.ksc; Y.vsc = A.vsc; Y.ktail = A.ktail; Y.vtail = A.vtail;
+            stages.push_back({MK_QKV, l, (nh + 2 * nkv) * 4, H, nullptr, nullptr, nullptr});
+            stages.push_back({MK_ATTN, l, 0, 0, nullptr, nullptr, nullptr});
+            stages.push_back({MK_RES, l, H / 16, nh * 64, L.wo.p, L.wo.s, s->attn_out});
+        } else {
+            Y.win = L.in_proj.p; Y.sin = L.in_proj.s; Y.conv_w = L.conv_w; Y.conv_state = s->conv_state[l];
+            stages.push_back({MK_CONV_IN, l, H / 16, H, nullptr, nullptr, nullptr});
+            stages.push_back({MK_RES, l, H / 16, H, L.out_proj.p, L.out_proj.s, s->conv_y});
+        }
+        if (l < c.n_dense) {
+            Y.w1 = L.w1.p; Y.s1 = L.w1.s; Y.w3 = L.w3.p; Y.s3 = L.w3.s;
+            stages.push_back({MK_DENSE_UP, l, c.dense_inter / 16, H, nullptr, nullptr, nullptr});
+            stages.push_back({MK_RES, l, H / 16, c.dense_inter, L.w2.p, L.w2.s, s->mid});
+        } else {
+            Y.gate = L.gate; Y.ebias = L.ebias;
+            Y.experts = (const void* const*)(m->d_experts + (size_t)L.moe_index * c.n_experts * 6);
+            Y.route_idx = s->route_idx + L.moe_index * c.top_k;
+            Y.route_w = s->route_w + L.moe_index * c.top_k;
+            stages.push_back({MK_MOE_UP, l, c.top_k * c.moe_inter / 16, H, nullptr, nullptr, nullptr});
+            stages.push_back({MK_MOE_DOWN, l, H / 16, c.moe_inter, nullptr, nullptr, nullptr});
+        }
+    }
+    stages.push_back({MK_LMHEAD, -1, (c.vocab + 15) / 16, H, nullptr, nullptr, nullptr});
+    s->mk_kinds.clear();
+    for (auto& st : stages) s->mk_kinds.push_back(st.kind);
+    MkLayer* dL = nullptr;
+    MkStage* dS = nullptr;
+    int rc = dalloc(s, &dL, layers.size() * sizeof(MkLayer));
+    if (!rc) rc = dalloc(s, &dS, stages.size() * sizeof(MkStage));
+    if (rc) return rc;
+    CUINF_TRY(cudaMemcpy(dL, layers.data(), layers.size() * sizeof(MkLayer), cudaMemcpyHostToDevice));
+    CUINF_TRY(cudaMemcpy(dS, stages.data(), stages.size() * sizeof(MkStage), cudaMemcpyHostToDevice));
+    MkParams& P = s->mk;
+    memset(&P, 0, sizeof(P));
+    P.L = dL;
+    P.S = dS;
+    P.n_stages = (int)stages.size();
+    P.H = H; P.nh = nh; P.nkv = nkv; P.I = c.moe_inter; P.E = c.n_experts; P.topk = c.top_k; P.V = c.vocab;
+    P.ring_bytes = ring;
+    P.xbn = xbn;
+    P.attn_chunks = std::max(1, G / nkv);
+    P.eps = c.norm_eps; P.theta = c.rope_theta; P.scale = 1.0f / sqrtf((float)c.head_dim);
+    P.h = s->h; P.q = s->q; P.attn_out = s->attn_out; P.conv_y = s->conv_y; P.mid = s->mid;
+    P.hidden_out = s->hidden;
+    if ((rc = dalloc(s, &P.qkv_f32, (size_t)(nh + 2 * nkv) * 64 * 4))) return rc;
+    if ((rc = dalloc(s, &P.qkv_tick, (size_t)(nh + 2 * nkv) * 4))) return rc;
+    if ((rc = dalloc(s, &P.attn_part, (size_t)nkv * P.attn_chunks * gqa * ATTN_PART_STRIDE * 4))) return rc;
+    if ((rc = dalloc(s, &P.attn_tick, (size_t)nkv * 4))) return rc;
+    if ((rc = dalloc(s, &s->mk_words, 64))) return rc;
+    P.gbar = s->mk_words + 0;
+    P.abort_flag = s->mk_words + 1;
+    P.err = s->mk_words + 2;
+    P.lm_tick = s->mk_words + 3;
+    P.am_key = s->am_key;
+    P.embed = m->embed; P.emb_norm = m->emb_norm;
+    P.tok = s->tok; P.pos = s->pos; P.out_ring = s->out_ring; P.ring = s->max_ctx;
+    if ((rc = dalloc(s, &s->mk_trace, (size_t)P.n_stages * G * 4 * 8))) return rc;
+    // the attention merge scratch also stages (m, l) of every chunk
+    if ((size_t)(2 * P.attn_chunks * gqa + gqa) * 4 > mk_layout(H, xbn, ring, gqa).out - mk_layout(H, xbn, ring, gqa).xs)
+        return CUINF_OK;
+    s->mk_smem = smem;
+    s->mk_grid = G;
+    s->mk_ok = true;
+    return CUINF_OK;
+}
+
+static int record_step_mk(cuinf_session* s) {
+    MkParams P = s->mk;
+    P.logits = s->keep_logits ? s->logits : nullptr;
+    P.trace = s->trace ? s->mk_trace : nullptr;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(s->mk_grid);
+    cfg.blockDim = dim3(MK_THREADS);
+    cfg.dynamicSmemBytes = s->mk_smem;
+    cfg.stream = s->st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUINF_TRY(cudaLaunchKernelEx(&cfg, k_decode_mk, P));
+    s->kernels_per_step = 1;
+    return CUINF_OK;
+}
+
 // Records one decode step into the session stream (under capture, or eagerly
 // with per-kernel events when prof is set).
 static int record_step(cuinf_session* s, Prof* prof = nullptr) {
+    if (s->use_mk && s->mk_ok && !prof) return record_step_mk(s);
     const cuinf_model* m = s->m;
     const cuinf_config& c = m->cfg;
     const int H = c.hidden;
@@ -795,6 +941,8 @@ extern "C" int cuinf_session_free(cuinf_session* s) {
     if (s->exec) cudaGraphExecDestroy(s->exec);
     if (s->graph) cudaGraphDestroy(s->graph);
     for (void* p : s->allocs) cudaFree(p);
+    for (int i = 0; i < cuinf_session::kTokRing; i++)
+        if (s->tok_ev[i]) cudaEventDestroy(s->tok_ev[i]);
     if (s->pinned) cudaFreeHost(s->pinned);
     if (s->own_stream && s->st) cudaStreamDestroy(s->st);
     delete s;
@@ -854,7 +1002,10 @@ extern "C" int cuinf_session_create(cuinf_model* m, int max_ctx, void* stream, c
             TRYS(dalloc(s, &s->conv_state[l], (size_t)2 * H * 2));
         }
     }
-    TRYC(cudaMallocHost(&s->pinned, 64));
+    TRYC(cudaMallocHost(&s->pinned, (cuinf_session::kTokRing + 1) * sizeof(int)));
+    for (int i = 0; i < cuinf_session::kTokRing; i++)
+        TRYC(cudaEventCreateWithFlags(&s->tok_ev[i], cudaEventDisableTiming));
+    TRYS(setup_megakernel(s));
     TRYS(build_graph(s));
 #undef TRYS
 #undef TRYC
@@ -881,6 +1032,7 @@ extern "C" int cuinf_session_reset(cuinf_session* s) {
         }
     }
     CUINF_TRY(cudaMemsetAsync(s->pos, 0, 4, s->st));
+    if (s->mk_words) CUINF_TRY(cudaMemsetAsync(s->mk_words, 0, 64, s->st));
     CUINF_TRY(cudaStreamSynchronize(s->st));
     s->host_pos = 0;
     return CUINF_OK;
@@ -893,15 +1045,20 @@ extern "C" int cuinf_decode_step(cuinf_session* s, int token, int* out_token) {
     REQUIRE(s->host_pos < s->max_ctx, "context full (max_ctx reached)");
     REQUIRE(token < s->m->cfg.vocab, "token out of range");
     if (token >= 0) {
-        s->pinned[0] = token;
-        CUINF_TRY(cudaMemcpyAsync(s->tok, &s->pinned[0], 4, cudaMemcpyHostToDevice, s->st));
+        const int k = s->tok_slot;
+        s->tok_slot = (k + 1) % cuinf_session::kTokRing;
+        CUINF_TRY(cudaEventSynchronize(s->tok_ev[k]));  // its previous copy has run
+        s->pinned[k] = token;
+        CUINF_TRY(cudaMemcpyAsync(s->tok, &s->pinned[k], 4, cudaMemcpyHostToDevice, s->st));
+        CUINF_TRY(cudaEventRecord(s->tok_ev[k], s->st));
     }
     CUINF_TRY(cudaGraphLaunch(s->exec, s->st));
     s->host_pos++;
     if (out_token) {
-        CUINF_TRY(cudaMemcpyAsync(&s->pinned[1], s->tok, 4, cudaMemcpyDeviceToHost, s->st));
+        int* o = &s->pinned[cuinf_session::kTokRing];
+        CUINF_TRY(cudaMemcpyAsync(o, s->tok, 4, cudaMemcpyDeviceToHost, s->st));
         CUINF_TRY(cudaStreamSynchronize(s->st));
-        *out_token = s->pinned[1];
+        *out_token = *o;
     }
     return CUINF_OK;
 }
@@ -938,12 +1095,49 @@ extern "C" int cuinf_session_keep_logits(cuinf_session* s, int on) {
 
 extern "C" int cuinf_session_set_option(cuinf_session* s, int option, int value) {
     REQUIRE(s, "null session");
-    bool* f = option == CUINF_OPT_PREFETCH ? &s->prefetch : option == CUINF_OPT_PDL ? &s->pdl : nullptr;
+    bool* f = option == CUINF_OPT_PREFETCH ? &s->prefetch
+            : option == CUINF_OPT_PDL      ? &s->pdl
+            : option == CUINF_OPT_MEGAKERNEL ? &s->use_mk
+            : option == CUINF_OPT_TRACE      ? &s->trace
+                                             : nullptr;
     REQUIRE(f, "unknown option");
     if ((bool)value == *f) return CUINF_OK;
     CUINF_TRY(cudaStreamSynchronize(s->st));
     *f = value != 0;
     return build_graph(s);
+}
+
+extern "C" int cuinf_session_trace(cuinf_session* s, unsigned long long* buf, int cap, int* kinds,
+                                   int* n_stages, int* n_ctas) {
+    REQUIRE(s && buf && n_stages && n_ctas, "null pointer");
+    REQUIRE(s->mk_ok && s->mk_trace, "no megakernel trace recorded (set CUINF_OPT_TRACE)");
+    const int n = s->mk.n_stages, G = s->mk_grid;
+    REQUIRE(cap >= n * G * 4, "trace buffer too small");
+    CUINF_TRY(cudaStreamSynchronize(s->st));
+    CUINF_TRY(cudaMemcpy(buf, s->mk_trace, (size_t)n * G * 4 * 8, cudaMemcpyDeviceToHost));
+    if (kinds)
+        for (int i = 0; i < n; i++) kinds[i] = s->mk_kinds[i];
+    *n_stages = n;
+    *n_ctas = G;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_session_uses_megakernel(const cuinf_session* s) {
+    return s && s->use_mk && s->mk_ok ? 1 : 0;
+}
+
+extern "C" int cuinf_session_error(cuinf_session* s, unsigned* flags) {
+    REQUIRE(s && flags, "null pointer");
+    unsigned w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (s->mk_words) {
+        CUINF_TRY(cudaStreamSynchronize(s->st));
+        CUINF_TRY(cudaMemcpy(w, s->mk_words, sizeof(w), cudaMemcpyDeviceToHost));
+    }
+    flags[0] = w[2] | (w[1] ? 1u : 0u);
+    flags[1] = w[4];  // stage of the first failure
+    flags[2] = w[5];  // CTA
+    flags[3] = w[6];  // slab number
+    return CUINF_OK;
 }
 
 extern "C" int cuinf_device_error(unsigned* flags) {
@@ -976,7 +1170,7 @@ extern "C" int cuinf_session_profile_step(cuinf_session* s, int token, int max_k
     REQUIRE(s->host_pos < s->max_ctx, "context full (max_ctx reached)");
     CUINF_TRY(cudaStreamSynchronize(s->st));
     if (token >= 0) {
-        s->pinned[0] = token;
+        s->pinned[0] = token;  // the stream was synchronized above
         CUINF_TRY(cudaMemcpyAsync(s->tok, &s->pinned[0], 4, cudaMemcpyHostToDevice, s->st));
     }
     Prof prof;

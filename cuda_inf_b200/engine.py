@@ -97,7 +97,35 @@ class Session:
         check(lib().cuinf_generate(self._h, p, len(prompt), n_new, eos, o, ctypes.byref(n)))
         return list(o[:n.value])
 
-    OPT_PREFETCH, OPT_PDL = 1, 2
+    OPT_PREFETCH, OPT_PDL, OPT_MEGAKERNEL, OPT_TRACE = 1, 2, 3, 4
+    STAGE_KINDS = ("conv_in", "residual", "qkv", "attention", "dense_up", "moe_up", "moe_down",
+                   "lm_head")
+
+    def trace(self):
+        """Per-stage timestamps of the last traced megakernel step: returns
+        (kinds [S], t [S, G, 4]) with t = start, prologue end, slab-wait ns, end."""
+        import numpy as np
+        c = self.model.cfg
+        max_stages = 5 * c.n_layers + 1
+        cap = max_stages * 1024 * 4
+        buf = np.zeros(cap, np.uint64)
+        kinds = np.zeros(max_stages, np.int32)
+        ns, ng = ctypes.c_int(0), ctypes.c_int(0)
+        check(lib().cuinf_session_trace(self._h, buf.ctypes.data, cap, kinds.ctypes.data,
+                                        ctypes.byref(ns), ctypes.byref(ng)))
+        t = buf[:ns.value * ng.value * 4].reshape(ns.value, ng.value, 4)
+        return [self.STAGE_KINDS[k] for k in kinds[:ns.value]], t
+
+    @property
+    def uses_megakernel(self):
+        return bool(lib().cuinf_session_uses_megakernel(self._h))
+
+    def error(self, detail=False):
+        """Megakernel error flags (0 = none); synchronizes the session stream.
+        detail=True returns (flags, stage, cta, slab) of the first failure."""
+        v = (ctypes.c_uint * 4)()
+        check(lib().cuinf_session_error(self._h, v))
+        return tuple(v) if detail else v[0]
 
     def set_option(self, option, value):
         """OPT_PREFETCH: L2 prefetch of upcoming weights; OPT_PDL: programmatic

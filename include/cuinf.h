@@ -194,10 +194,29 @@ int cuinf_session_keep_logits(cuinf_session* s, int on);
  * kernel's weight staging overlaps its predecessor. */
 #define CUINF_OPT_PREFETCH 1
 #define CUINF_OPT_PDL 2
+/* CUINF_OPT_MEGAKERNEL: run the step as one persistent cooperative kernel
+ * (one CTA per SM, TMA weight ring, grid barriers between stages); falls back
+ * to the multi-kernel graph when the device or model does not fit. */
+#define CUINF_OPT_MEGAKERNEL 3
+/* CUINF_OPT_TRACE: the megakernel records %globaltimer at every stage start
+ * and end of every CTA (read with cuinf_session_trace; default 0). */
+#define CUINF_OPT_TRACE 4
 int cuinf_session_set_option(cuinf_session* s, int option, int value);
 /* Device error flags of the engine kernels (bit 0: a bounded wait on a
  * weight-staging barrier timed out and the kernel skipped its math). */
 int cuinf_device_error(unsigned* flags);
+/* Per-stage timestamps of the last traced megakernel step: buf receives
+ * [n_stages][n_ctas][4] (start, prologue end, ns spent waiting for weight
+ * slabs, end), times in ns; kinds (nullable) [n_stages]. */
+int cuinf_session_trace(cuinf_session* s, unsigned long long* buf, int cap, int* kinds, int* n_stages,
+                        int* n_ctas);
+/* 1 when this session's step runs as the persistent megakernel. */
+int cuinf_session_uses_megakernel(const cuinf_session* s);
+/* Megakernel error state of this session (synchronizes its stream), 4 words:
+ * flags[0] bits: 0 abort, 1 grid-barrier time-out, 2 producer ring time-out,
+ * 3 producer routing time-out, 4 consumer slab time-out (0 = none);
+ * flags[1..3]: stage, CTA and slab number of the first failure. */
+int cuinf_session_error(cuinf_session* s, unsigned* flags);
 const float* cuinf_session_logits(const cuinf_session* s);
 const void* cuinf_session_hidden(const cuinf_session* s);
 /* Host copy of the last step's routing decisions [n_moe_layers*top_k]. */

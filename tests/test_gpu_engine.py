@@ -91,15 +91,18 @@ def run_compare(cfg, om, s, tokens, max_ctx):
     return worst, near_ties, checked, got_tokens
 
 
-def test_engine_matches_oracle_teacher_forced(tiny):
+@pytest.mark.parametrize("mk", [1, 0], ids=["megakernel", "multikernel"])
+def test_engine_matches_oracle_teacher_forced(tiny, mk):
     cfg, om, gm = tiny
     s = Session(gm, max_ctx=160)
+    s.set_option(Session.OPT_MEGAKERNEL, mk)
+    assert s.uses_megakernel == bool(mk)
     s.keep_logits(True)
     toks = np.random.default_rng(123).integers(0, cfg.vocab, 140)
     worst, near, checked, _ = run_compare(cfg, om, s, toks, 160)
     print(f"worst logits rel err {worst:.2e}; routing checked {checked}, near-ties {near}")
     assert checked > 0.9 * (checked + near)
-    assert device_error() == 0
+    assert device_error() == 0 and s.error() == 0
 
 
 def test_engine_greedy_matches_oracle(tiny):
@@ -122,15 +125,20 @@ def test_engine_greedy_matches_oracle(tiny):
 def test_kernels_per_step(tiny):
     cfg, om, gm = tiny
     s = Session(gm, max_ctx=64)
+    assert s.kernels_per_step == 1  # one persistent launch
+    s.set_option(Session.OPT_MEGAKERNEL, 0)
     assert s.kernels_per_step == 2 * 4 + 3 * 2 + 2 * 6 + 1
 
 
 @pytest.mark.parametrize("opt", [(1, 0), (2, 0)])
 def test_engine_options_do_not_change_results(tiny, opt):
-    """Turning the L2 prefetch plan or PDL off changes scheduling only."""
+    """On the multi-kernel path, turning the L2 prefetch plan or PDL off
+    changes scheduling only: results are bit-identical."""
     cfg, om, gm = tiny
     a = Session(gm, max_ctx=80)
     b = Session(gm, max_ctx=80)
+    a.set_option(Session.OPT_MEGAKERNEL, 0)
+    b.set_option(Session.OPT_MEGAKERNEL, 0)
     b.set_option(*opt)
     a.keep_logits(True)
     b.keep_logits(True)
