@@ -260,7 +260,8 @@ class Model:
         return State(self, max_ctx)
 
     def __del__(self):
-        if getattr(self, "_h", None):
+        # at interpreter exit the module globals may already be gone
+        if getattr(self, "_h", None) and callable(lib):
             lib().orc_model_free(self._h)
             self._h = None
 
@@ -304,6 +305,7 @@ class State:
         return lib().orc_state_pos(self._h)
 
     def __del__(self):
-        if getattr(self, "_h", None):
+        # at interpreter exit the module globals may already be gone
+        if getattr(self, "_h", None) and callable(lib):
             lib().orc_state_free(self._h)
             self._h = None

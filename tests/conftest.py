@@ -6,9 +6,9 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
-GOLDEN = os.path.join(ROOT, "tests", "golden")
-if GOLDEN not in sys.path:
-    sys.path.insert(0, GOLDEN)
+for _d in (os.path.join(ROOT, "tests"), os.path.join(ROOT, "tests", "golden")):
+    if _d not in sys.path:
+        sys.path.insert(0, _d)
 
 
 def pytest_configure(config):

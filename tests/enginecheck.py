@@ -1,0 +1,52 @@
+"""Teacher-forced comparison of a decode Session with the whole-model CPU
+oracle, shared by the engine GPU tests.
+
+Each step runs the oracle with the engine's expert choices and asserts the
+engine chose the oracle's own top-k set whenever the oracle's k-th vs (k+1)-th
+score margin exceeds ROUTE_MARGIN, in the oracle's order up to swaps of
+scores within that margin; logits agree within LOGIT_TOL (max-abs
+error / max-abs logit) and the argmax agrees outside TIE_MARGIN near-ties.
+"""
+import numpy as np
+
+LOGIT_TOL = 1e-2
+TIE_MARGIN = 1e-3
+ROUTE_MARGIN = 1e-3
+
+
+def own_topk(scores, k):
+    """The reference's selection on given scores (strict '>', lowest index)."""
+    order = sorted(range(len(scores)), key=lambda e: (-scores[e], e))
+    return order[:k], (scores[order[k - 1]] - scores[order[k]]) if len(scores) > k else np.inf
+
+
+def run_compare(cfg, om, s, tokens, max_ctx, logit_tol=LOGIT_TOL, route_margin=ROUTE_MARGIN):
+    st = om.state(max_ctx)
+    worst, near_ties, checked = 0.0, 0, 0
+    got_tokens = []
+    for i, t in enumerate(tokens):
+        got = s.step(int(t))
+        got_tokens.append(got)
+        gi, _ = s.routes()
+        gi = np.array(gi, np.int32).reshape(-1, cfg.top_k)
+        ref, lg, _, sc = st.forward_ex(int(t), forced_idx=gi.ravel())
+        for l in range(gi.shape[0]):
+            sel, margin = own_topk(sc[l], cfg.top_k)
+            if margin > route_margin:
+                # same expert set; each slot holds an expert whose score is
+                # within route_margin of the oracle's expert for that slot
+                # (the order is descending score, so near-equal scores may swap)
+                assert sorted(gi[l].tolist()) == sorted(sel), (i, l, list(gi[l]), sel, margin)
+                for j, e in enumerate(gi[l]):
+                    assert abs(sc[l][e] - sc[l][sel[j]]) <= route_margin, (i, l, j, list(gi[l]), sel)
+                checked += 1
+            else:
+                near_ties += 1
+        glog = s.logits().cpu().numpy()
+        e = float(np.max(np.abs(glog - lg)) / np.max(np.abs(lg)))
+        worst = max(worst, e)
+        assert e < logit_tol, (i, e)
+        top = np.sort(lg)[::-1]
+        if top[0] - top[1] > TIE_MARGIN * max(1.0, abs(top[0])):
+            assert got == ref, (i, got, ref)
+    return worst, near_ties, checked, got_tokens

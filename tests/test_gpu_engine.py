@@ -23,12 +23,9 @@ import pytest
 from oracle import pyoracle as orc
 from cuda_inf_b200 import weights
 from cuda_inf_b200.engine import Model, Session, device_error
+from enginecheck import run_compare
 
 pytestmark = pytest.mark.gpu
-
-LOGIT_TOL = 1e-2
-TIE_MARGIN = 1e-3
-ROUTE_MARGIN = 1e-3
 
 TINY = dict(hidden=256, n_layers=6, n_heads=4, n_kv_heads=1, vocab=1000, n_dense=1, n_experts=8,
             top_k=2, moe_inter=256, dense_inter=384, attn_layers=(1, 4))
@@ -56,39 +53,6 @@ def tiny(tmp_path_factory, cuda):
     om = orc.Model(weights.config_dict(cfg), blob, index)
     gm = Model.load(str(d), cfg)
     return cfg, om, gm
-
-
-def own_topk(scores, k):
-    """The reference's selection on given scores (strict '>', lowest index)."""
-    order = sorted(range(len(scores)), key=lambda e: (-scores[e], e))
-    return order[:k], (scores[order[k - 1]] - scores[order[k]]) if len(scores) > k else np.inf
-
-
-def run_compare(cfg, om, s, tokens, max_ctx):
-    st = om.state(max_ctx)
-    worst, near_ties, checked = 0.0, 0, 0
-    got_tokens = []
-    for i, t in enumerate(tokens):
-        got = s.step(int(t))
-        got_tokens.append(got)
-        gi, _ = s.routes()
-        gi = np.array(gi, np.int32).reshape(-1, cfg.top_k)
-        ref, lg, _, sc = st.forward_ex(int(t), forced_idx=gi.ravel())
-        for l in range(gi.shape[0]):
-            sel, margin = own_topk(sc[l], cfg.top_k)
-            if margin > ROUTE_MARGIN:
-                assert list(gi[l]) == sel, (i, l, list(gi[l]), sel, margin)
-                checked += 1
-            else:
-                near_ties += 1
-        glog = s.logits().cpu().numpy()
-        e = float(np.max(np.abs(glog - lg)) / np.max(np.abs(lg)))
-        worst = max(worst, e)
-        assert e < LOGIT_TOL, (i, e)
-        top = np.sort(lg)[::-1]
-        if top[0] - top[1] > TIE_MARGIN * max(1.0, abs(top[0])):
-            assert got == ref, (i, got, ref)
-    return worst, near_ties, checked, got_tokens
 
 
 @pytest.mark.parametrize("mk", [1, 0], ids=["megakernel", "multikernel"])
