@@ -45,6 +45,10 @@ _SIGS = {
     "cuinf_attn_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_void_p, c_int, c_int, c_float, c_void_p, c_int, c_int, c_void_p,
                                   c_size_t, c_void_p]),
+    "cuinf_attn_decode_static_scratch_bytes": (c_size_t, []),
+    "cuinf_attn_decode_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_void_p, c_int, c_int, c_float, c_void_p,
+                                          c_int, c_int, c_void_p]),
     "cuinf_conv_pre": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "cuinf_conv_apply": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                  c_void_p]),

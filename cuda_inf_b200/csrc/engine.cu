@@ -110,6 +110,100 @@ extern "C" int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_
 }
 
 // ---------------------------------------------------------------------------
+// attention with library-static scratch: a variant for callers that may not
+// allocate device memory at all (an allocator hook that re-enters this
+// library, a pool that forbids cudaMalloc, or a caller that pre-reserves all
+// HBM).  The split-K partials and tickets live in one file-scope __device__
+// array; its address is taken once per device at set-up.
+// ---------------------------------------------------------------------------
+#define ATTN_STATIC_SCRATCH_BYTES (512u << 10)  // 256 B of tickets + partials
+#define ATTN_STATIC_MAX_DEVICES 64
+
+static __device__ __align__(256) unsigned char g_attn_static_scratch[ATTN_STATIC_SCRATCH_BYTES];
+
+static std::mutex g_static_mu;
+static void* g_static_ptr[ATTN_STATIC_MAX_DEVICES];
+static int g_static_sms[ATTN_STATIC_MAX_DEVICES];
+
+// Address of g_attn_static_scratch and the SM count on the current device.
+// The first call on a device resolves the symbol (module load, no allocation);
+// later calls only read the cached table.
+static int static_scratch(void** ptr, int* sms) {
+    int dev = 0;
+    CUINF_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= ATTN_STATIC_MAX_DEVICES)
+        return cuinf_set_arg_error("device ordinal beyond the static scratch table");
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_ptr[dev]) {
+        void* p = nullptr;
+        int n = 0;
+        CUINF_TRY(cudaGetSymbolAddress(&p, g_attn_static_scratch));
+        CUINF_TRY(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        if (!p || ((uintptr_t)p & 255)) return cuinf_set_arg_error("static scratch misaligned");
+        g_static_sms[dev] = n;
+        g_static_ptr[dev] = p;
+    }
+    *ptr = g_static_ptr[dev];
+    *sms = g_static_sms[dev];
+    return CUINF_OK;
+}
+
+extern "C" size_t cuinf_attn_decode_static_scratch_bytes(void) { return ATTN_STATIC_SCRATCH_BYTES; }
+
+extern "C" int cuinf_attn_decode_noalloc(const void* q, const uint8_t* kc8, const uint8_t* vc8,
+                                         const void* ksc, const void* vsc, const void* ktail,
+                                         const void* vtail, int committed, int qpos, float scale,
+                                         void* out, int nh, int nkv, void* stream) {
+    REQUIRE(q && ktail && vtail && out, "null pointer");
+    REQUIRE(nh > 0 && nkv > 0 && nkv <= 64 && nh % nkv == 0 && nh / nkv <= 8,
+            "need nkv <= 64, nh % nkv == 0, nh/nkv <= 8");
+    REQUIRE(qpos >= 0 && committed >= 0 && committed % CUINF_KVGROUP == 0, "committed % 64 == 0");
+    REQUIRE(committed <= qpos + 1 && qpos + 1 - committed <= CUINF_KVGROUP,
+            "tail length must be in [0, 64]");
+    REQUIRE(committed == 0 || (kc8 && vc8 && ksc && vsc), "null FP8 cache");
+    REQUIRE(((uintptr_t)ktail & 15) == 0 && ((uintptr_t)vtail & 15) == 0 &&
+                ((uintptr_t)kc8 & 15) == 0 && ((uintptr_t)vc8 & 15) == 0 && ((uintptr_t)q & 3) == 0,
+            "cache pointers must be 16-byte aligned");
+    void* ws = nullptr;
+    int sms = 0;
+    int rc = static_scratch(&ws, &sms);
+    if (rc) return rc;
+    const int units = committed / CUINF_KVGROUP + (qpos + 1 > committed ? 1 : 0);
+    const int ns = attn_default_nsplit(nkv, nh / nkv, units, sms);
+    const size_t need = (size_t)nkv * ns * (nh / nkv) * ATTN_PART_STRIDE * 4 + 256;
+    if (need > ATTN_STATIC_SCRATCH_BYTES)
+        return cuinf_set_arg_error(
+            "cuinf_attn_decode_noalloc: split-K partials exceed the 512 KiB static scratch; "
+            "use cuinf_attn_decode with a workspace");
+    AttnParams P;
+    P.q = (const __half*)q;
+    P.kc8 = kc8;
+    P.vc8 = vc8;
+    P.ksc = (const __half*)ksc;
+    P.vsc = (const __half*)vsc;
+    P.ktail = (const __half*)ktail;
+    P.vtail = (const __half*)vtail;
+    P.pos_dev = nullptr;
+    P.committed = committed;
+    P.qpos = qpos;
+    P.scale = scale;
+    P.out = (__half*)out;
+    P.counters = (unsigned*)ws;
+    P.part = (float*)((char*)ws + 256);
+    P.nh = nh;
+    P.nkv = nkv;
+    P.nsplit = ns;
+    P.next.count = 0;
+    // The per-kv-head tickets must read zero when the kernel starts.  The array
+    // is zero at module load and every completed launch returns its tickets to
+    // zero; clearing them here on the stream (a memset, no allocation) also
+    // covers a launch that an earlier error cut short.
+    CUINF_TRY(cudaMemsetAsync(ws, 0, 256, ST(stream)));
+    k_attn_decode<<<dim3(nkv, ns), ATTN_THREADS, 0, ST(stream)>>>(P);
+    return cuinf_launch_status();
+}
+
+// ---------------------------------------------------------------------------
 // standalone fused MoE FFN for one token (engine.cu:877-905)
 // ---------------------------------------------------------------------------
 // Launch with programmatic stream serialization (PDL) when pdl is set: the

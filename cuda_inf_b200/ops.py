@@ -14,7 +14,7 @@ from ._lib import check, lib
 
 __all__ = [
     "gemv_int4", "gemv_fp16", "rmsnorm", "rmsnorm_head", "rope", "kv_write_tail",
-    "kv_commit_group", "attn_decode", "conv_pre", "conv_apply", "conv_update_state", "swiglu",
+    "kv_commit_group", "attn_decode", "attn_decode_noalloc", "conv_pre", "conv_apply", "conv_update_state", "swiglu",
     "acc_scaled", "add_inplace", "add_f32_inplace", "f32_to_f16", "embed_gather", "argmax",
     "moe_route", "moe_ffn", "quantize_int4", "expert_table",
 ]
@@ -111,6 +111,21 @@ def attn_decode(q, kc8, vc8, ksc, vsc, ktail, vtail, committed, qpos, scale=0.12
     check(lib().cuinf_attn_decode(_p(q), _p(kc8), _p(vc8), _p(ksc), _p(vsc), _p(ktail), _p(vtail),
                                   committed, qpos, scale, _p(out), nh, nkv, _p(workspace), ws_bytes,
                                   _stream()))
+    return out
+
+
+def attn_decode_noalloc(q, kc8, vc8, ksc, vsc, ktail, vtail, committed, qpos, scale=0.125,
+                        out=None):
+    """attn_decode with the library's static 512 KiB scratch: the C call allocates
+    no device memory (out is allocated here only when not given).  Calls on
+    one device must not overlap."""
+    nh = q.numel() // 64
+    nkv = ktail.shape[1]
+    if out is None:
+        out = torch.empty_like(q)
+    check(lib().cuinf_attn_decode_noalloc(_p(q), _p(kc8), _p(vc8), _p(ksc), _p(vsc), _p(ktail),
+                                          _p(vtail), committed, qpos, scale, _p(out), nh, nkv,
+                                          _stream()))
     return out
 
 

@@ -88,6 +88,28 @@ int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_t* vc8, con
                       int qpos, float scale, void* out, int nh, int nkv, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* Same attention as cuinf_attn_decode, for callers that must not allocate
+ * device memory (an allocator callback that calls back into this library, a
+ * memory pool that forbids cudaMalloc, a host that has reserved all HBM up
+ * front).  It allocates nothing: its split-K scratch is a static device array
+ * of cuinf_attn_decode_static_scratch_bytes() (512 KiB) bytes inside the
+ * library.  The first call on a device sets up (looks up that array's
+ * address) and should come before any stream capture on that device.  Shapes
+ * whose scratch would exceed 512 KiB are rejected with CUINF_ERR_ARG: on a
+ * B200, 8 kv heads x 4 query heads each (the model's shape) need at most
+ * 0.31 MiB; 8 kv heads x 8 query heads need more than 512 KiB past 1920
+ * tokens and are rejected there.
+ * The scratch is shared by every call on a device, so calls on one device
+ * must not overlap: issue them on one stream or order them with events;
+ * overlapping calls race on the scratch.  The scratch's 256-byte ticket area
+ * must start at zero; each call clears it on the stream before its launch.
+ * No counterpart in the reference. */
+size_t cuinf_attn_decode_static_scratch_bytes(void);
+int cuinf_attn_decode_noalloc(const void* q, const uint8_t* kc8, const uint8_t* vc8,
+                              const void* ksc, const void* vsc, const void* ktail,
+                              const void* vtail, int committed, int qpos, float scale, void* out,
+                              int nh, int nkv, void* stream);
+
 /* Short-conv pieces (H channels): inproj fp32 [S,3H] = B | C | x.
  * conv_pre: C = half(C), Bx = half(B*x)            (engine.cu:483-494)
  * conv_apply: y = half(C * (Bx[s-2]w0 + Bx[s-1]w1 + Bx[s]w2)), history from
