@@ -72,6 +72,22 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// L2 cache policy for data read once per step (weights streamed from HBM):
+// evict those lines first so they do not push out activations, the KV cache
+// or kernel code that is reused.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void tma_load_1d_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                 uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+        "%4;\n" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
 // Non-blocking test of phase `parity` of bar.
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
@@ -117,12 +133,14 @@ __host__ __device__ __forceinline__ uint32_t int4_tile_bytes(int K) {
     return 16u * (uint32_t)(K >> 1) + 16u * (uint32_t)(K >> 6);
 }
 // Thread-0 helper: TMA one full 16-row tile (rows row0..row0+15 of W[N,K])
-// into dst; returns the bytes it will deliver to bar.
+// into dst; returns the bytes it will deliver to bar.  Weights are read once
+// per step, so their L2 lines are marked evict-first.
 __device__ __forceinline__ uint32_t tma_tile_int4(const uint8_t* packed, const __half* scales, int K,
                                                   int row0, uint8_t* dst, uint64_t* bar) {
     const uint32_t pb = 16u * (uint32_t)(K >> 1), sb = 16u * (uint32_t)(K >> 6);
-    tma_load_1d(dst, packed + (size_t)row0 * (K >> 1), pb, bar);
-    tma_load_1d(dst + pb, (const uint8_t*)scales + (size_t)row0 * (K >> 6), sb, bar);
+    const uint64_t pol = l2_policy_evict_first();
+    tma_load_1d_hint(dst, packed + (size_t)row0 * (K >> 1), pb, bar, pol);
+    tma_load_1d_hint(dst + pb, (const uint8_t*)scales + (size_t)row0 * (K >> 6), sb, bar, pol);
     return pb + sb;
 }
 

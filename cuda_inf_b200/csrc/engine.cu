@@ -698,7 +698,7 @@ static int setup_megakernel(cuinf_session* s) {
     CUINF_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
     int max_smem = 0;
     CUINF_TRY(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-    if (!coop || c.top_k > 5 || c.n_experts > 256) return CUINF_OK;
+    if (!coop || c.top_k > 5 || c.n_experts > 256 || c.n_experts % 8) return CUINF_OK;
     const int xbn = std::max(std::max(H, nh * 64), std::max(c.dense_inter, c.top_k * c.moe_inter));
     const size_t fixed = mk_layout(H, xbn, 0, gqa).total;
     const size_t static_smem = sizeof(MkHeader) + 256;
@@ -706,8 +706,8 @@ static int setup_megakernel(cuinf_session* s) {
     int ring = (int)(((size_t)max_smem - fixed - static_smem) / 1024 * 1024);
     // the largest slab must fit the ring
     const size_t slab_max = std::max(
-        std::max((size_t)c.n_experts * H * 2, (size_t)16 * H * 2),
-        std::max((size_t)3 * int4_tile_bytes(H),
+        std::max((size_t)(c.n_experts + 1) * H * 2 + c.n_experts * 2, (size_t)16 * H * 2),
+        std::max((size_t)3 * int4_tile_bytes(H) + 160,
                  std::max((size_t)c.top_k * int4_tile_bytes(c.moe_inter),
                           (size_t)int4_tile_bytes(std::max(c.dense_inter, nh * 64)))));
     if (slab_max > (size_t)ring) return CUINF_OK;
@@ -717,6 +717,18 @@ static int setup_megakernel(cuinf_session* s) {
     CUINF_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mk, MK_THREADS, smem));
     if (per_sm < 1) return CUINF_OK;
     const int G = s->num_sms;
+
+    // every TMA source of the stage program must be 16-byte aligned
+    auto a16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+    bool aligned = a16(m->emb_norm) && a16(m->embed);
+    for (int l = 0; l < c.n_layers; l++) {
+        const LayerW& L = m->L[l];
+        aligned = aligned && a16(L.op_norm) && a16(L.ffn_norm);
+        if (c.attn_layer[l]) aligned = aligned && a16(L.q_ln) && a16(L.k_ln);
+        else aligned = aligned && a16(L.conv_w) && a16(s->conv_state[l]);
+        if (l >= c.n_dense) aligned = aligned && a16(L.gate) && a16(L.ebias);
+    }
+    if (!aligned) return CUINF_OK;
 
     std::vector<MkLayer> layers(c.n_layers);
     std::vector<MkStage> stages;
@@ -786,7 +798,7 @@ static int setup_megakernel(cuinf_session* s) {
     P.am_key = s->am_key;
     P.embed = m->embed; P.emb_norm = m->emb_norm;
     P.tok = s->tok; P.pos = s->pos; P.out_ring = s->out_ring; P.ring = s->max_ctx;
-    if ((rc = dalloc(s, &s->mk_trace, (size_t)P.n_stages * G * 4 * 8))) return rc;
+    if ((rc = dalloc(s, &s->mk_trace, (size_t)P.n_stages * G * MK_TRACE_W * 8))) return rc;
     // the attention merge scratch also stages (m, l) of every chunk
     if ((size_t)(2 * P.attn_chunks * gqa + gqa) * 4 > mk_layout(H, xbn, ring, gqa).out - mk_layout(H, xbn, ring, gqa).xs)
         return CUINF_OK;
@@ -1206,9 +1218,9 @@ extern "C" int cuinf_session_trace(cuinf_session* s, unsigned long long* buf, in
     REQUIRE(s && buf && n_stages && n_ctas, "null pointer");
     REQUIRE(s->mk_ok && s->mk_trace, "no megakernel trace recorded (set CUINF_OPT_TRACE)");
     const int n = s->mk.n_stages, G = s->mk_grid;
-    REQUIRE(cap >= n * G * 4, "trace buffer too small");
+    REQUIRE(cap >= n * G * MK_TRACE_W, "trace buffer too small");
     CUINF_TRY(cudaStreamSynchronize(s->st));
-    CUINF_TRY(cudaMemcpy(buf, s->mk_trace, (size_t)n * G * 4 * 8, cudaMemcpyDeviceToHost));
+    CUINF_TRY(cudaMemcpy(buf, s->mk_trace, (size_t)n * G * MK_TRACE_W * 8, cudaMemcpyDeviceToHost));
     if (kinds)
         for (int i = 0; i < n; i++) kinds[i] = s->mk_kinds[i];
     *n_stages = n;

@@ -23,11 +23,14 @@
 #include "common.cuh"
 #include "route.cuh"
 
+#ifndef MK_CW
 #define MK_CW 12                  // consumer warps
+#endif
 #define MK_CT (MK_CW * 32)        // consumer threads
 #define MK_THREADS (MK_CT + 32)   // + producer warp (one lane issues TMA)
 #define MK_QN 32                  // slabs in flight (one mbarrier each)
 #define MK_MAXPC 10               // TMA pieces per slab
+#define MK_TRACE_W 16             // trace words per (stage, CTA)
 
 enum MkKind : int {
     MK_CONV_IN = 0,  // in_proj (B|C|x) + short conv epilogue
@@ -77,7 +80,15 @@ struct MkParams {
     const __half *embed, *emb_norm;
     int *tok, *pos, *out_ring;
     int ring;
-    unsigned long long* trace;  // optional [n_stages][G][4]: start, prologue end, slab-wait ns, end
+    // optional [n_stages][G][MK_TRACE_W]: %globaltimer at start, prologue end
+    // and end (words 0, 1, 3), ns spent in slab waits (2), then SM cycles
+    // since the stage start (%clock64): pre-slab ready (4), first item slab
+    // ready (5), dot done (6), epilogue done (7), MoE-up norm done (8),
+    // router dots done (9), selection done (10); word 11 = %clock64 at start;
+    // producer %clock64 at: pre-slab issue (12), first item slab ready to
+    // place (13, after any routing wait), first item slab issue (14); SM
+    // cycles from the stage start to the prologue end (15)
+    unsigned long long* trace;
 };
 
 // Shared-memory carve-up (identical on host and device).
@@ -201,6 +212,16 @@ __device__ __forceinline__ void mk_item_pieces(const MkParams& P, const MkStage&
     switch (st.kind) {
         case MK_CONV_IN:
             for (int t = 0; t < 3; t++) mk_add_tile(pc, L.win, L.sin, H, t * H + 16 * j);
+            // conv taps [16][3] and the two history rows of the item's channels
+            // (written only by this stage, in the previous step)
+            pc.src[pc.n] = L.conv_w + (size_t)48 * j;
+            pc.bytes[pc.n++] = 96u;
+            pc.src[pc.n] = L.conv_state + (size_t)16 * j;
+            pc.bytes[pc.n++] = 32u;
+            pc.src[pc.n] = L.conv_state + (size_t)H + 16 * j;
+            pc.bytes[pc.n++] = 32u;
+            pc.total += 160u;
+            pc.tx += 160u;
             break;
         case MK_RES:
             mk_add_tile(pc, st.wres, st.sres, st.K, 16 * j);
@@ -210,6 +231,12 @@ __device__ __forceinline__ void mk_item_pieces(const MkParams& P, const MkStage&
             if (hh < P.nh) mk_add_tile(pc, L.wq, L.sq, H, hh * 64 + r * 16);
             else if (hh < P.nh + P.nkv) mk_add_tile(pc, L.wk, L.sk, H, (hh - P.nh) * 64 + r * 16);
             else mk_add_tile(pc, L.wv, L.sv, H, (hh - P.nh - P.nkv) * 64 + r * 16);
+            if (hh < P.nh + P.nkv) {  // q/k-norm weight for whichever tile finishes the head
+                pc.src[pc.n] = hh < P.nh ? L.q_ln : L.k_ln;
+                pc.bytes[pc.n++] = 128u;
+                pc.total += 128u;
+                pc.tx += 128u;
+            }
             break;
         }
         case MK_DENSE_UP:
@@ -243,12 +270,39 @@ __device__ __forceinline__ void mk_item_pieces(const MkParams& P, const MkStage&
     }
 }
 
+// Stages whose prologue normalises the residual get a per-CTA "pre-slab" at
+// their head: the RMSNorm weight, and for MoE-up also the router gate and the
+// expert bias, so no prologue waits on a DRAM miss for a small static vector.
+__device__ __forceinline__ bool mk_has_pre(int kind) {
+    return kind == MK_CONV_IN || kind == MK_QKV || kind == MK_DENSE_UP || kind == MK_MOE_UP ||
+           kind == MK_LMHEAD;
+}
+__device__ __forceinline__ void mk_pre_pieces(const MkParams& P, const MkStage& st, MkPieces& pc) {
+    const MkLayer& L = P.L[st.layer < 0 ? 0 : st.layer];
+    const unsigned hb = 2u * (unsigned)P.H;
+    pc.src[0] = st.kind == MK_LMHEAD ? P.emb_norm
+              : (st.kind == MK_CONV_IN || st.kind == MK_QKV) ? L.op_norm : L.ffn_norm;
+    pc.bytes[0] = hb;
+    pc.n = 1;
+    pc.total = pc.tx = hb;
+    if (st.kind == MK_MOE_UP) {
+        const unsigned gb = 2u * (unsigned)(P.E * P.H), bb = 2u * (unsigned)P.E;  // E % 8 == 0
+        pc.src[1] = L.gate;
+        pc.bytes[1] = gb;
+        pc.src[2] = L.ebias;
+        pc.bytes[2] = bb;
+        pc.n = 3;
+        pc.total = pc.tx = hb + gb + bb;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // producer
 // ---------------------------------------------------------------------------
 __device__ __noinline__ void mk_producer(const MkParams& P, MkHeader& S, uint8_t* ring, int pos) {
     const int G = gridDim.x, b = blockIdx.x;
     const unsigned RING = (unsigned)P.ring_bytes;
+    const uint64_t pol_ef = l2_policy_evict_first();
     unsigned head = 0, nslab = 0;
     bool ok = true;
     for (int s = 0; s < P.n_stages && ok; s++) {
@@ -256,14 +310,10 @@ __device__ __noinline__ void mk_producer(const MkParams& P, MkHeader& S, uint8_t
         if (st.kind == MK_ATTN) continue;
         const int n = mk_items(P, st, pos);
         const bool moe = st.kind == MK_MOE_UP || st.kind == MK_MOE_DOWN;
-        // the router gate is a per-CTA slab at the head of the MoE-up stage
-        for (int j = (st.kind == MK_MOE_UP ? -1 : b); j < n && ok; j = (j < 0 ? b : j + G)) {
+        for (int j = (mk_has_pre(st.kind) ? -1 : b); j < n && ok; j = (j < 0 ? b : j + G)) {
             MkPieces pc;
             if (j < 0) {
-                const MkLayer& L = P.L[st.layer];
-                pc.src[0] = L.gate;
-                pc.bytes[0] = pc.total = pc.tx = (unsigned)P.E * P.H * 2;
-                pc.n = 1;
+                mk_pre_pieces(P, st, pc);
             } else {
                 if (moe) {  // expert slabs need this CTA's routing of this layer
                     const int want = st.kind == MK_MOE_UP ? s : s - 1;
@@ -282,6 +332,8 @@ __device__ __noinline__ void mk_producer(const MkParams& P, MkHeader& S, uint8_t
                 }
                 mk_item_pieces(P, st, j, S.sidx, pc);
             }
+            unsigned long long* ptrace = (P.trace && j <= b) ? P.trace + ((size_t)s * G + b) * MK_TRACE_W : nullptr;
+            if (ptrace && j >= 0) ptrace[13] = clock64();
             // Place the slab contiguously; if it does not fit before the end of
             // the ring it starts at offset 0 (the skipped bytes stay unused).
             // It may be written once the bytes it overwrites were consumed:
@@ -308,15 +360,20 @@ __device__ __noinline__ void mk_producer(const MkParams& P, MkHeader& S, uint8_t
             S.meta_end[q] = head + pc.total;
             mbar_arrive_expect_tx(&S.full[q], pc.tx);
             unsigned doff = off;
-            for (int k = 0; k < pc.n; k++) {  // bulk copies of at most 32 KB each
+            // bulk copies of at most 32 KB each; item slabs (weights read once
+            // per step) are evict-first in L2, pre-slabs (norm weights and the
+            // router gate, read by every CTA) keep the default policy
+            for (int k = 0; k < pc.n; k++) {
                 const uint8_t* src = (const uint8_t*)pc.src[k];
                 for (unsigned done = 0; done < pc.bytes[k];) {
                     const unsigned len = min(pc.bytes[k] - done, 32768u);
-                    tma_load_1d(ring + doff + done, src + done, len, &S.full[q]);
+                    if (j >= 0) tma_load_1d_hint(ring + doff + done, src + done, len, &S.full[q], pol_ef);
+                    else tma_load_1d(ring + doff + done, src + done, len, &S.full[q]);
                     done += len;
                 }
                 doff += pc.bytes[k];
             }
+            if (ptrace) ptrace[j < 0 ? 12 : 14] = clock64();
             head += pc.total;
             nslab++;
         }
@@ -383,7 +440,7 @@ __device__ __forceinline__ void mk_grid_arrive(const MkParams& P) {
 }
 
 // x = rmsnorm(src) into xs (fp16) and, when xB != null, its B-fragment order.
-__device__ __forceinline__ void mk_norm(const __half* src, const __half* w, int H, float eps,
+__device__ __noinline__ void mk_norm(const __half* src, const __half* w, int H, float eps,
                                         __half* xs, __half* xB, float* red) {
     for (int i = threadIdx.x * 8; i < H; i += MK_CT * 8)
         *reinterpret_cast<uint4*>(xs + i) = *reinterpret_cast<const uint4*>(src + i);
@@ -404,9 +461,33 @@ __device__ __forceinline__ void mk_norm(const __half* src, const __half* w, int 
     }
 }
 
+// Router logits lg[e] = gate[e,:] . xs for the E experts (gate fp16 [E][H]
+// in shared memory); ends with a consumer barrier.
+__device__ __noinline__ void mk_router_logits(const __half* gw, const __half* xs, int E, int H, float* lg) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = warp; e < E; e += MK_CW) {
+        float acc = 0.f;
+        for (int k = lane * 8; k < H; k += 256) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(gw + (size_t)e * H + k);
+            const uint4 xv = *reinterpret_cast<const uint4*>(xs + k);
+            const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
+            const __half2* x2 = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+            for (int qq = 0; qq < 4; qq++) {
+                const float2 a = __half22float2(w2[qq]), bb = __half22float2(x2[qq]);
+                acc = fmaf(a.x, bb.x, acc);
+                acc = fmaf(a.y, bb.y, acc);
+            }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) lg[e] = acc;
+    }
+    cbar();
+}
+
 // T INT4 tiles (K wide, consecutive in the slab) times x (B-fragment order,
 // tile t uses xB + t*xstride): out[t*16 + r] = row r of tile t.
-__device__ __forceinline__ void mk_dot_tiles(const uint8_t* slab, int T, int K, const __half* xB,
+__device__ __noinline__ void mk_dot_tiles(const uint8_t* slab, int T, int K, const __half* xB,
                                              int xstride, float* red, float* out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KG = K >> 7;
@@ -441,7 +522,7 @@ __device__ __forceinline__ void mk_dot_tiles(const uint8_t* slab, int T, int K, 
 }
 
 // 16 fp16 rows (row stride H, in the slab) times x (fp16, natural order).
-__device__ __forceinline__ void mk_dot_f16_tile(const uint8_t* slab, int H, const __half* xs, float* red,
+__device__ __noinline__ void mk_dot_f16_tile(const uint8_t* slab, int H, const __half* xs, float* red,
                                                 float* out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const __half* Wt = reinterpret_cast<const __half*>(slab);
@@ -470,9 +551,10 @@ __device__ __forceinline__ void mk_dot_f16_tile(const uint8_t* slab, int H, cons
 
 // QK-RMSNorm + RoPE + KV append (+ FP8 commit) of one head's 64 values
 // (engine.cu:792-845), run by the consumers of the CTA that finished the
-// head's last tile.  hv: 64 halves of scratch.
+// head's last tile.  lw: the head's q/k-norm weight (shared memory, unused
+// for v heads); hv: 64 halves of scratch.
 __device__ __noinline__ void mk_qkv_head(const MkParams& P, const MkLayer& L, int hh, const float* vals,
-                                         __half* hv, float* red, int pos) {
+                                         const __half* lw, __half* hv, float* red, int pos) {
     const int d = threadIdx.x;
     const int committed = (pos / CUINF_KVGROUP) * CUINF_KVGROUP, slot = pos - committed;
     const bool is_q = hh < P.nh, is_k = !is_q && hh < P.nh + P.nkv;
@@ -482,7 +564,6 @@ __device__ __noinline__ void mk_qkv_head(const MkParams& P, const MkLayer& L, in
         const float v = d < 64 ? __half2float(hv[d]) : 0.f;
         const float ss = cblock_sum(v * v, red);
         const float inv = rsqrtf(ss / 64.f + P.eps);
-        const __half* lw = is_q ? L.q_ln : L.k_ln;
         const __half nv = __float2half_rn(v * inv * __half2float(lw[d < 64 ? d : 0]));
         cbar();
         if (d < 64) hv[d] = nv;
@@ -631,7 +712,7 @@ __device__ __noinline__ void mk_attn_item(const MkParams& P, const MkLayer& L, i
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(MkParams P) {
+__global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const __grid_constant__ MkParams P) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ MkHeader S;
     const int G = gridDim.x, b = blockIdx.x;
@@ -667,11 +748,24 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(MkParams P) {
         const MkStage st = P.S[s];
         const MkLayer& L = P.L[st.layer < 0 ? 0 : st.layer];
         if (s > 0 && !mk_grid_wait(P, S, (unsigned)s * G)) { alive = false; break; }
+        long long clk0 = 0;
         if (P.trace && tid == 0) {
-            P.trace[((size_t)s * G + b) * 4] = globaltimer_ns();
+            unsigned long long* tr = P.trace + ((size_t)s * G + b) * MK_TRACE_W;
+            tr[0] = globaltimer_ns();
+            clk0 = clock64();
+            for (int w = 4; w <= 10; w++) tr[w] = 0ull;
+            tr[11] = (unsigned long long)clk0;
             S.wait_ns = 0ull;
         }
+        unsigned long long* trs = (P.trace && tid == 0) ? P.trace + ((size_t)s * G + b) * MK_TRACE_W : nullptr;
         // ---- stage prologue ----
+        const uint8_t* pre = nullptr;
+        if (mk_has_pre(st.kind)) {
+            pre = mk_slab_wait(P, S, ring, slabno, s);
+            if (!pre) { alive = false; break; }
+            if (trs) trs[4] = clock64() - clk0;
+        }
+        const __half* nw = reinterpret_cast<const __half*>(pre);
         switch (st.kind) {
             case MK_CONV_IN:
             case MK_QKV: {
@@ -681,7 +775,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(MkParams P) {
                     if (b == 0)
                         for (int i = tid; i < H; i += MK_CT) P.h[i] = src[i];
                 }
-                mk_norm(src, L.op_norm, H, P.eps, xs, xB, red);
+                mk_norm(src, nw, H, P.eps, xs, xB, red);
                 break;
             }
             case MK_RES:
@@ -689,34 +783,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(MkParams P) {
                 cbar();
                 break;
             case MK_DENSE_UP:
-                mk_norm(P.h, L.ffn_norm, H, P.eps, xs, xB, red);
+                mk_norm(P.h, nw, H, P.eps, xs, xB, red);
                 break;
             case MK_MOE_UP: {
-                mk_norm(P.h, L.ffn_norm, H, P.eps, xs, xB, red);
-                const uint8_t* gs = mk_slab_wait(P, S, ring, slabno, s);
-                if (!gs) { alive = false; break; }
-                const __half* gw = reinterpret_cast<const __half*>(gs);
-                const int warp = tid >> 5, lane = tid & 31;
-                for (int e = warp; e < P.E; e += MK_CW) {
-                    float acc = 0.f;
-                    for (int k = lane * 8; k < H; k += 256) {
-                        const uint4 wv = *reinterpret_cast<const uint4*>(gw + (size_t)e * H + k);
-                        const uint4 xv = *reinterpret_cast<const uint4*>(xs + k);
-                        const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
-                        const __half2* x2 = reinterpret_cast<const __half2*>(&xv);
-#pragma unroll
-                        for (int qq = 0; qq < 4; qq++) {
-                            const float2 a = __half22float2(w2[qq]), bb = __half22float2(x2[qq]);
-                            acc = fmaf(a.x, bb.x, acc);
-                            acc = fmaf(a.y, bb.y, acc);
-                        }
-                    }
-                    acc = warp_sum(acc);
-                    if (lane == 0) lg[e] = acc;
-                }
-                mk_slab_free(S, slabno++);
-                if (warp == 0) route_select_warp(lg, L.ebias, P.E, P.topk, S.sidx, S.sw);
+                mk_norm(P.h, nw, H, P.eps, xs, xB, red);
+                if (trs) trs[8] = clock64() - clk0;
+                const __half* gw = nw + H;
+                mk_router_logits(gw, xs, P.E, H, lg);
+                if (trs) trs[9] = clock64() - clk0;
+                if (tid < 32) route_select_warp(lg, gw + (size_t)P.E * H, P.E, P.topk, S.sidx, S.sw);
                 cbar();
+                if (trs) trs[10] = clock64() - clk0;
                 if (tid == 0) {
                     __threadfence_block();
                     S.route_stage = s;
@@ -737,13 +814,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(MkParams P) {
             case MK_LMHEAD:
                 if (b == 0 && P.hidden_out)
                     for (int i = tid; i < H; i += MK_CT) P.hidden_out[i] = P.h[i];
-                mk_norm(P.h, P.emb_norm, H, P.eps, xs, nullptr, red);
+                mk_norm(P.h, nw, H, P.eps, xs, nullptr, red);
                 break;
             default:
                 break;
         }
+        if (pre) mk_slab_free(S, slabno++);
         if (!alive) break;
-        if (P.trace && tid == 0) P.trace[((size_t)s * G + b) * 4 + 1] = globaltimer_ns();
+        if (trs) {
+            trs[1] = globaltimer_ns();
+            trs[15] = clock64() - clk0;
+        }
         // ---- items ----
         const int n = mk_items(P, st, pos);
         for (int j = b; j < n; j += G) {
@@ -754,33 +835,43 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(MkParams P) {
             }
             const uint8_t* slab = mk_slab_wait(P, S, ring, slabno, s);
             if (!slab) { alive = false; break; }
+            const bool tr_item = trs && j == b;
+            unsigned long long* tr = trs;
+            if (tr_item) tr[5] = clock64() - clk0;
+            // the residual rows this item updates, read before the dot so the
+            // load latency hides behind it (only this CTA writes them)
+            float hres = 0.f;
+            if ((st.kind == MK_RES || st.kind == MK_MOE_DOWN) && tid < 16)
+                hres = __half2float(P.h[16 * j + tid]);
             switch (st.kind) {
                 case MK_CONV_IN: {
                     mk_dot_tiles(slab, 3, H, xB, 0, red, out);
+                    if (tr_item) tr[6] = clock64() - clk0;
                     if (tid < 16) {
                         const int c = 16 * j + tid;
+                        const __half* ex = reinterpret_cast<const __half*>(slab + 3 * int4_tile_bytes(H));
                         const __half Cb = __float2half_rn(out[16 + tid]);
                         const __half Bx = __float2half_rn(out[tid] * out[32 + tid]);
-                        const float s0 = __half2float(L.conv_state[c]), s1 = __half2float(L.conv_state[H + c]);
-                        const float w0 = __half2float(L.conv_w[c * 3 + 0]), w1 = __half2float(L.conv_w[c * 3 + 1]),
-                                    w2 = __half2float(L.conv_w[c * 3 + 2]);
+                        const __half s1h = ex[64 + tid];
+                        const float s0 = __half2float(ex[48 + tid]), s1 = __half2float(s1h);
+                        const float w0 = __half2float(ex[tid * 3 + 0]), w1 = __half2float(ex[tid * 3 + 1]),
+                                    w2 = __half2float(ex[tid * 3 + 2]);
                         const float co = s0 * w0 + s1 * w1 + __half2float(Bx) * w2;
                         P.conv_y[c] = __float2half_rn(__half2float(Cb) * co);
-                        L.conv_state[c] = L.conv_state[H + c];
+                        L.conv_state[c] = s1h;
                         L.conv_state[H + c] = Bx;
                     }
                     break;
                 }
                 case MK_RES: {
                     mk_dot_tiles(slab, 1, st.K, xB, 0, red, out);
-                    if (tid < 16) {
-                        const int nrow = 16 * j + tid;
-                        P.h[nrow] = __float2half_rn(__half2float(P.h[nrow]) + out[tid]);
-                    }
+                    if (tr_item) tr[6] = clock64() - clk0;
+                    if (tid < 16) P.h[16 * j + tid] = __float2half_rn(hres + out[tid]);
                     break;
                 }
                 case MK_QKV: {
                     mk_dot_tiles(slab, 1, H, xB, 0, red, out);
+                    if (tr_item) tr[6] = clock64() - clk0;
                     const int hh = j >> 2;
                     if (tid < 16) P.qkv_f32[16 * j + tid] = out[tid];
                     __threadfence();
@@ -792,13 +883,16 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(MkParams P) {
                         if (tid < 64) out[tid] = __ldcg(P.qkv_f32 + 64 * hh + tid);
                         if (tid == 0) P.qkv_tick[hh] = 0u;
                         cbar();
-                        mk_qkv_head(P, L, hh, out, reinterpret_cast<__half*>(lg), red, pos);
+                        mk_qkv_head(P, L, hh, out,
+                                    reinterpret_cast<const __half*>(slab + int4_tile_bytes(H)),
+                                    reinterpret_cast<__half*>(lg), red, pos);
                     }
                     break;
                 }
                 case MK_DENSE_UP:
                 case MK_MOE_UP: {
                     mk_dot_tiles(slab, 2, H, xB, 0, red, out);
+                    if (tr_item) tr[6] = clock64() - clk0;
                     if (tid < 16) {
                         const float gg = out[tid], u = out[16 + tid];
                         const float sv = gg / (1.f + __expf(-gg)) * u;
@@ -813,17 +907,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(MkParams P) {
                 }
                 case MK_MOE_DOWN: {
                     mk_dot_tiles(slab, P.topk, P.I, xB, P.I, red, out);
+                    if (tr_item) tr[6] = clock64() - clk0;
                     if (tid < 16) {
                         __half acc = __float2half_rn(0.f);
                         for (int t = 0; t < P.topk; t++)
                             acc = __float2half_rn(__half2float(acc) + S.sw[t] * out[t * 16 + tid]);
-                        const int nrow = 16 * j + tid;
-                        P.h[nrow] = __float2half_rn(__half2float(P.h[nrow]) + __half2float(acc));
+                        P.h[16 * j + tid] = __float2half_rn(hres + __half2float(acc));
                     }
                     break;
                 }
                 case MK_LMHEAD: {
                     mk_dot_f16_tile(slab, H, xs, red, out);
+                    if (tr_item) tr[6] = clock64() - clk0;
                     if (tid < 16) {
                         const int r = 16 * j + tid;
                         if (r < P.V) {
@@ -837,14 +932,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(MkParams P) {
                 default:
                     break;
             }
+            if (tr_item) tr[7] = clock64() - clk0;
             mk_slab_free(S, slabno++);
         }
         if (!alive) break;
         if (P.trace) {
             cbar();
             if (tid == 0) {
-                P.trace[((size_t)s * G + b) * 4 + 2] = S.wait_ns;
-                P.trace[((size_t)s * G + b) * 4 + 3] = globaltimer_ns();
+                P.trace[((size_t)s * G + b) * MK_TRACE_W + 2] = S.wait_ns;
+                P.trace[((size_t)s * G + b) * MK_TRACE_W + 3] = globaltimer_ns();
             }
         }
         if (st.kind != MK_LMHEAD) mk_grid_arrive(P);

@@ -8,10 +8,14 @@ __device__ __forceinline__ float route_sigmoid(float z) {
     float e = (float)exp(-(double)z);
     return 1.0f / (1.0f + e);
 }
+// One out-of-line copy: the double-precision exp is long code, and the
+// selection below calls it from an unrolled loop.
+static __device__ __noinline__ float route_sigmoid_call(float z) { return route_sigmoid(z); }
 
-// One warp per token; n_exp <= 32*8, topk <= 16.
+// One warp per token; n_exp <= 32*8.  idx/w receive the topk choices
+// (written by lane 0; w is normalised in place at the end).
 __device__ __forceinline__ void route_select_warp(const float* logits, const __half* bias, int n_exp, int topk,
-                                  int* idx, float* w) {
+                                                  int* idx, float* w) {
     const int lane = threadIdx.x & 31;
     float sig[8], score[8];
     bool used[8];
@@ -19,16 +23,15 @@ __device__ __forceinline__ void route_select_warp(const float* logits, const __h
     for (int j = 0; j < 8; j++) {
         int e = lane + 32 * j;
         used[j] = e >= n_exp;
+        sig[j] = 0.f;
+        score[j] = -INFINITY;
         if (e < n_exp) {
-            sig[j] = route_sigmoid(logits[e]);
+            sig[j] = route_sigmoid_call(logits[e]);
             score[j] = sig[j] + __half2float(bias[e]);
-        } else {
-            sig[j] = 0.f;
-            score[j] = -INFINITY;
         }
     }
-    float wsel[16];
-    int isel[16];
+    float wsum = 0.f;  // summed in selection order, as the reference does
+#pragma unroll 1
     for (int t = 0; t < topk; t++) {
         // max score, lowest index on ties (the reference scans e ascending with '>')
         float bv = -1e30f;
@@ -60,15 +63,13 @@ __device__ __forceinline__ void route_select_warp(const float* logits, const __h
         for (int j = 0; j < 8; j++)
             if (lane + 32 * j == be) { used[j] = true; sv = sig[j]; }
         sv = __shfl_sync(0xffffffffu, sv, be & 31);
-        isel[t] = be;
-        wsel[t] = sv;
-    }
-    float wsum = 0.f;
-    for (int t = 0; t < topk; t++) wsum += wsel[t];
-    if (lane == 0)
-        for (int t = 0; t < topk; t++) {
-            idx[t] = isel[t];
-            w[t] = wsel[t] / (wsum + 1e-6f);
+        wsum += sv;
+        if (lane == 0) {
+            idx[t] = be;
+            w[t] = sv;
         }
+    }
+    if (lane == 0)
+        for (int t = 0; t < topk; t++) w[t] = w[t] / (wsum + 1e-6f);
+    __syncwarp();
 }
-

@@ -103,17 +103,24 @@ class Session:
 
     def trace(self):
         """Per-stage timestamps of the last traced megakernel step: returns
-        (kinds [S], t [S, G, 4]) with t = start, prologue end, slab-wait ns, end."""
+        (kinds [S], t [S, G, 16]): %globaltimer ns at start, prologue end and
+        end (0, 1, 3), slab-wait ns (2); SM cycles since the stage start for
+        pre-slab ready (4), the first item's slab ready, dot done and
+        epilogue done (5-7), MoE-up norm, router dots and selection done
+        (8-10); %clock64 at the stage start (11); producer %clock64 at the
+        pre-slab issue (12), first item ready to place (13) and issued (14);
+        SM cycles from the stage start to the prologue end (15).
+        0 = no such point."""
         import numpy as np
         c = self.model.cfg
         max_stages = 5 * c.n_layers + 1
-        cap = max_stages * 1024 * 4
+        cap = max_stages * 1024 * 16
         buf = np.zeros(cap, np.uint64)
         kinds = np.zeros(max_stages, np.int32)
         ns, ng = ctypes.c_int(0), ctypes.c_int(0)
         check(lib().cuinf_session_trace(self._h, buf.ctypes.data, cap, kinds.ctypes.data,
                                         ctypes.byref(ns), ctypes.byref(ng)))
-        t = buf[:ns.value * ng.value * 4].reshape(ns.value, ng.value, 4)
+        t = buf[:ns.value * ng.value * 16].reshape(ns.value, ng.value, 16)
         return [self.STAGE_KINDS[k] for k in kinds[:ns.value]], t
 
     @property

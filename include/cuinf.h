@@ -228,8 +228,14 @@ int cuinf_session_set_option(cuinf_session* s, int option, int value);
  * weight-staging barrier timed out and the kernel skipped its math). */
 int cuinf_device_error(unsigned* flags);
 /* Per-stage timestamps of the last traced megakernel step: buf receives
- * [n_stages][n_ctas][4] (start, prologue end, ns spent waiting for weight
- * slabs, end), times in ns; kinds (nullable) [n_stages]. */
+ * [n_stages][n_ctas][16]: %globaltimer ns at the stage start, prologue end
+ * and end (words 0, 1, 3); ns spent waiting for weight slabs (2); SM cycles
+ * since the stage start for: pre-slab ready (4), the first item's slab
+ * ready, dot done, epilogue done (5-7), MoE-up norm, router dots and expert
+ * selection done (8-10); %clock64 at the stage start (11); the producer's
+ * %clock64 at its pre-slab issue (12), first item ready to place (13) and
+ * first item issue (14); SM cycles from the stage start to the prologue end
+ * (15).  0 where a stage has no such point.  kinds (nullable) [n_stages]. */
 int cuinf_session_trace(cuinf_session* s, unsigned long long* buf, int cap, int* kinds, int* n_stages,
                         int* n_ctas);
 /* 1 when this session's step runs as the persistent megakernel. */
