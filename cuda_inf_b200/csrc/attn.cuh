@@ -60,6 +60,10 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 // aq) over units u_begin, u_begin+u_step, ... < u_end of kv head h.  Keeps
 // the running max m_run (base 2, per row), the per-lane partial sum l_run and
 // the output accumulators O (n-tile j holds dims 16c+j and 16c+8+j of row g).
+// CG: read the cache with ld.global.cg (coherent at L2) because the caller's
+// own launch may have written it (the persistent kernel); otherwise the
+// cache is read through the non-coherent streaming path.
+template <bool CG>
 __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
                                                 const uint8_t* __restrict__ vc8,
                                                 const __half* __restrict__ ksc,
@@ -83,7 +87,8 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
             const int kk = 8 * jn + g;  // key within the unit
             uint32_t kb[8];
             if (!tail) {
-                uint4 raw = ldg_stream(kc8 + ((size_t)(kbase + kk) * nkv + h) * CUINF_HD + 16 * c);
+                const uint8_t* kp8 = kc8 + ((size_t)(kbase + kk) * nkv + h) * CUINF_HD + 16 * c;
+                uint4 raw = CG ? __ldcg(reinterpret_cast<const uint4*>(kp8)) : ldg_stream(kp8);
                 const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
@@ -92,8 +97,8 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
                 }
             } else {
                 const __half* kp = ktail + ((size_t)kk * nkv + h) * CUINF_HD + 16 * c;
-                uint4 r0 = *reinterpret_cast<const uint4*>(kp);
-                uint4 r1 = *reinterpret_cast<const uint4*>(kp + 8);
+                uint4 r0 = CG ? __ldcg(reinterpret_cast<const uint4*>(kp)) : *reinterpret_cast<const uint4*>(kp);
+                uint4 r1 = CG ? __ldcg(reinterpret_cast<const uint4*>(kp + 8)) : *reinterpret_cast<const uint4*>(kp + 8);
                 kb[0] = r0.x; kb[1] = r0.y; kb[2] = r0.z; kb[3] = r0.w;
                 kb[4] = r1.x; kb[5] = r1.y; kb[6] = r1.z; kb[7] = r1.w;
             }
@@ -101,7 +106,7 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
             for (int s = 0; s < 4; s++)
                 mma_16816(S[jn], aq[s][0], 0u, aq[s][1], 0u, kb[2 * s], kb[2 * s + 1]);
         }
-        const float kscale = tail ? 1.0f : __half2float(ksc[(size_t)u * nkv + h]);
+        const float kscale = tail ? 1.0f : __half2float(CG ? __ldcg(ksc + (size_t)u * nkv + h) : ksc[(size_t)u * nkv + h]);
         const float f = kscale * kfac;
         float mx = ATTN_NEG;
 #pragma unroll
@@ -145,8 +150,18 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
             if (!tail) {
                 const uint8_t* vp = vc8 + ((size_t)(kbase + ka) * nkv + h) * CUINF_HD + 8 * g;
                 const size_t kstride = (size_t)nkv * CUINF_HD;
-                uint2 va = ldg_stream8(vp), vb = ldg_stream8(vp + kstride);
-                uint2 vc = ldg_stream8(vp + 8 * kstride), vd = ldg_stream8(vp + 9 * kstride);
+                uint2 va, vb, vc, vd;
+                if (CG) {
+                    va = __ldcg(reinterpret_cast<const uint2*>(vp));
+                    vb = __ldcg(reinterpret_cast<const uint2*>(vp + kstride));
+                    vc = __ldcg(reinterpret_cast<const uint2*>(vp + 8 * kstride));
+                    vd = __ldcg(reinterpret_cast<const uint2*>(vp + 9 * kstride));
+                } else {
+                    va = ldg_stream8(vp);
+                    vb = ldg_stream8(vp + kstride);
+                    vc = ldg_stream8(vp + 8 * kstride);
+                    vd = ldg_stream8(vp + 9 * kstride);
+                }
                 uint32_t r;
                 r = prmt(va.x, vb.x, 0x5140u); b0[0] = fp8x2_to_h2(r); b0[1] = fp8x2_to_h2(r >> 16);
                 r = prmt(va.x, vb.x, 0x7362u); b0[2] = fp8x2_to_h2(r); b0[3] = fp8x2_to_h2(r >> 16);
@@ -161,10 +176,13 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
                 const size_t kstride = (size_t)nkv * CUINF_HD;
                 const uint4 z = make_uint4(0u, 0u, 0u, 0u);
                 // keys beyond the tail hold stale data: zero them
-                uint4 va = ka < valid ? *reinterpret_cast<const uint4*>(vp) : z;
-                uint4 vb = ka + 1 < valid ? *reinterpret_cast<const uint4*>(vp + kstride) : z;
-                uint4 vc = ka + 8 < valid ? *reinterpret_cast<const uint4*>(vp + 8 * kstride) : z;
-                uint4 vd = ka + 9 < valid ? *reinterpret_cast<const uint4*>(vp + 9 * kstride) : z;
+                auto ld16 = [](const __half* q) {
+                    return CG ? __ldcg(reinterpret_cast<const uint4*>(q)) : *reinterpret_cast<const uint4*>(q);
+                };
+                uint4 va = ka < valid ? ld16(vp) : z;
+                uint4 vb = ka + 1 < valid ? ld16(vp + kstride) : z;
+                uint4 vc = ka + 8 < valid ? ld16(vp + 8 * kstride) : z;
+                uint4 vd = ka + 9 < valid ? ld16(vp + 9 * kstride) : z;
                 const uint32_t A4[4] = {va.x, va.y, va.z, va.w}, B4[4] = {vb.x, vb.y, vb.z, vb.w};
                 const uint32_t C4[4] = {vc.x, vc.y, vc.z, vc.w}, D4[4] = {vd.x, vd.y, vd.z, vd.w};
 #pragma unroll
@@ -178,7 +196,7 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
 #pragma unroll
             for (int j = 0; j < 8; j++) mma_16816(T[j], pa0, 0u, pa2, 0u, b0[j], b1[j]);
         }
-        const float vscale = tail ? 1.0f : __half2float(vsc[(size_t)u * nkv + h]);
+        const float vscale = tail ? 1.0f : __half2float(CG ? __ldcg(vsc + (size_t)u * nkv + h) : vsc[(size_t)u * nkv + h]);
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             O[j][0] = O[j][0] * alpha + vscale * T[j][0];
@@ -229,7 +247,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
 #pragma unroll
     for (int j = 0; j < 8; j++) O[j][0] = O[j][1] = O[j][2] = O[j][3] = 0.f;
 
-    attn_warp_units(P.kc8, P.vc8, P.ksc, P.vsc, P.ktail, P.vtail, nkv, h, n_fp8, tail_len, kfac, aq,
+    attn_warp_units<false>(P.kc8, P.vc8, P.ksc, P.vsc, P.ktail, P.vtail, nkv, h, n_fp8, tail_len, kfac, aq,
                     u0 + warp, u1, 4, m_run, l_run, O);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);

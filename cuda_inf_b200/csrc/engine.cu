@@ -600,7 +600,7 @@ struct cuinf_session {
     bool prefetch = true;  // L2 prefetch plans (cross-kernel weight streaming)
     bool pdl = true;       // programmatic dependent launch between the step's kernels
     // persistent megakernel (one cooperative launch per step)
-    bool mk_ok = false, use_mk = true;
+    bool mk_ok = false, use_mk = false;  // the multi-kernel graph is the default
     MkParams mk;
     size_t mk_smem = 0;
     int mk_grid = 0;
@@ -698,7 +698,10 @@ static int setup_megakernel(cuinf_session* s) {
     CUINF_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
     int max_smem = 0;
     CUINF_TRY(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-    if (!coop || c.top_k > 5 || c.n_experts > 256 || c.n_experts % 8) return CUINF_OK;
+    // stage program limits: at most 4 router tiles of 16 experts, norm of at
+    // most 16 elements per consumer thread
+    if (!coop || c.top_k > 5 || c.n_experts > 64 || c.n_experts % 8 || H % 64 || H > 16 * MK_CT)
+        return CUINF_OK;
     const int xbn = std::max(std::max(H, nh * 64), std::max(c.dense_inter, c.top_k * c.moe_inter));
     const size_t fixed = mk_layout(H, xbn, 0, gqa).total;
     const size_t static_smem = sizeof(MkHeader) + 256;
@@ -706,7 +709,7 @@ static int setup_megakernel(cuinf_session* s) {
     int ring = (int)(((size_t)max_smem - fixed - static_smem) / 1024 * 1024);
     // the largest slab must fit the ring
     const size_t slab_max = std::max(
-        std::max((size_t)(c.n_experts + 1) * H * 2 + c.n_experts * 2, (size_t)16 * H * 2),
+        std::max((size_t)H * 2 + c.n_experts * 2, (size_t)16 * mk_f16_pitch(H)),
         std::max((size_t)3 * int4_tile_bytes(H) + 160,
                  std::max((size_t)c.top_k * int4_tile_bytes(c.moe_inter),
                           (size_t)int4_tile_bytes(std::max(c.dense_inter, nh * 64)))));

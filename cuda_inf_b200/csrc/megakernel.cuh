@@ -81,7 +81,7 @@ struct MkParams {
     int *tok, *pos, *out_ring;
     int ring;
     // optional [n_stages][G][MK_TRACE_W]: %globaltimer at start, prologue end
-    // and end (words 0, 1, 3), ns spent in slab waits (2), then SM cycles
+    // and end (words 0, 1, 3), SM cycles spent in slab waits (2), then SM cycles
     // since the stage start (%clock64): pre-slab ready (4), first item slab
     // ready (5), dot done (6), epilogue done (7), MoE-up norm done (8),
     // router dots done (9), selection done (10); word 11 = %clock64 at start;
@@ -123,7 +123,7 @@ struct MkHeader {
     float sw[16];
     int flag;                    // consumer-broadcast scratch
     unsigned long long kred[16];
-    unsigned long long wait_ns;  // trace: time thread 0 spent waiting for slabs
+    unsigned long long wait_cyc;  // trace: SM cycles thread 0 spent waiting for slabs
 };
 
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;\n" ::"n"(MK_CT) : "memory"); }
@@ -185,23 +185,50 @@ __device__ __forceinline__ int mk_items(const MkParams& P, const MkStage& st, in
     return st.n_items;
 }
 
-// TMA pieces of item j of stage st (dst offsets are consecutive in the slab).
-// total = ring bytes the slab occupies; tx = bytes actually copied.
+// TMA pieces of item j of stage st, placed one after another in the slab.
+// Piece k copies rows[k] rows of bytes[k] bytes, source rows sstride[k]
+// apart, into slab rows dstride[k] apart (rows = 1 for a plain range), and
+// occupies span[k] bytes of the slab.  total = ring bytes the slab occupies;
+// tx = bytes actually copied.
 struct MkPieces {
     const void* src[MK_MAXPC];
-    unsigned bytes[MK_MAXPC];
+    unsigned bytes[MK_MAXPC], rows[MK_MAXPC], sstride[MK_MAXPC], dstride[MK_MAXPC], span[MK_MAXPC];
     int n;
     unsigned total, tx;
 };
+__device__ __forceinline__ void mk_add_piece(MkPieces& pc, const void* src, unsigned bytes) {
+    pc.src[pc.n] = src;
+    pc.bytes[pc.n] = bytes;
+    pc.rows[pc.n] = 1;
+    pc.sstride[pc.n] = pc.dstride[pc.n] = pc.span[pc.n] = bytes;
+    pc.n++;
+    pc.total += bytes;
+    pc.tx += bytes;
+}
+// fp16 rows of H halves staged with a row pitch of mk_f16_pitch(H) bytes:
+// 64 mod 128, so the 16-byte loads of two neighbouring rows by one 8-lane
+// phase of a warp fall in different shared-memory banks.
+__host__ __device__ __forceinline__ unsigned mk_f16_pitch(int H) {
+    const unsigned b = 2u * (unsigned)H;
+    return b + ((64u - (b & 127u)) & 127u);
+}
+__device__ __forceinline__ void mk_add_f16_rows(MkPieces& pc, const __half* src, int rows, int H,
+                                                int slab_rows) {
+    const unsigned pitch = mk_f16_pitch(H);
+    pc.src[pc.n] = src;
+    pc.bytes[pc.n] = 2u * (unsigned)H;
+    pc.rows[pc.n] = (unsigned)rows;
+    pc.sstride[pc.n] = 2u * (unsigned)H;
+    pc.dstride[pc.n] = pitch;
+    pc.span[pc.n] = (unsigned)slab_rows * pitch;
+    pc.n++;
+    pc.total += (unsigned)slab_rows * pitch;
+    pc.tx += (unsigned)rows * 2u * (unsigned)H;
+}
 __device__ __forceinline__ void mk_add_tile(MkPieces& pc, const uint8_t* packed, const __half* scales,
                                             int K, int row0) {
-    const unsigned pb = 16u * (unsigned)(K >> 1), sb = 16u * (unsigned)(K >> 6);
-    pc.src[pc.n] = packed + (size_t)row0 * (K >> 1);
-    pc.bytes[pc.n++] = pb;
-    pc.src[pc.n] = (const uint8_t*)scales + (size_t)row0 * (K >> 6);
-    pc.bytes[pc.n++] = sb;
-    pc.total += pb + sb;
-    pc.tx += pb + sb;
+    mk_add_piece(pc, packed + (size_t)row0 * (K >> 1), 16u * (unsigned)(K >> 1));
+    mk_add_piece(pc, (const uint8_t*)scales + (size_t)row0 * (K >> 6), 16u * (unsigned)(K >> 6));
 }
 __device__ __forceinline__ void mk_item_pieces(const MkParams& P, const MkStage& st, int j,
                                                const int* sidx, MkPieces& pc) {
@@ -214,14 +241,9 @@ __device__ __forceinline__ void mk_item_pieces(const MkParams& P, const MkStage&
             for (int t = 0; t < 3; t++) mk_add_tile(pc, L.win, L.sin, H, t * H + 16 * j);
             // conv taps [16][3] and the two history rows of the item's channels
             // (written only by this stage, in the previous step)
-            pc.src[pc.n] = L.conv_w + (size_t)48 * j;
-            pc.bytes[pc.n++] = 96u;
-            pc.src[pc.n] = L.conv_state + (size_t)16 * j;
-            pc.bytes[pc.n++] = 32u;
-            pc.src[pc.n] = L.conv_state + (size_t)H + 16 * j;
-            pc.bytes[pc.n++] = 32u;
-            pc.total += 160u;
-            pc.tx += 160u;
+            mk_add_piece(pc, L.conv_w + (size_t)48 * j, 96u);
+            mk_add_piece(pc, L.conv_state + (size_t)16 * j, 32u);
+            mk_add_piece(pc, L.conv_state + (size_t)H + 16 * j, 32u);
             break;
         case MK_RES:
             mk_add_tile(pc, st.wres, st.sres, st.K, 16 * j);
@@ -231,12 +253,8 @@ __device__ __forceinline__ void mk_item_pieces(const MkParams& P, const MkStage&
             if (hh < P.nh) mk_add_tile(pc, L.wq, L.sq, H, hh * 64 + r * 16);
             else if (hh < P.nh + P.nkv) mk_add_tile(pc, L.wk, L.sk, H, (hh - P.nh) * 64 + r * 16);
             else mk_add_tile(pc, L.wv, L.sv, H, (hh - P.nh - P.nkv) * 64 + r * 16);
-            if (hh < P.nh + P.nkv) {  // q/k-norm weight for whichever tile finishes the head
-                pc.src[pc.n] = hh < P.nh ? L.q_ln : L.k_ln;
-                pc.bytes[pc.n++] = 128u;
-                pc.total += 128u;
-                pc.tx += 128u;
-            }
+            if (hh < P.nh + P.nkv)  // q/k-norm weight for whichever tile finishes the head
+                mk_add_piece(pc, hh < P.nh ? L.q_ln : L.k_ln, 128u);
             break;
         }
         case MK_DENSE_UP:
@@ -257,12 +275,9 @@ __device__ __forceinline__ void mk_item_pieces(const MkParams& P, const MkStage&
             }
             break;
         case MK_LMHEAD: {
-            const int r0 = 16 * j, rows = min(16, P.V - r0);
-            pc.src[0] = P.embed + (size_t)r0 * H;
-            pc.bytes[0] = (unsigned)rows * H * 2;
-            pc.n = 1;
-            pc.tx = pc.bytes[0];
-            pc.total = 16u * H * 2;  // slab spans 16 rows; rows past V are never used
+            // the slab spans 16 pitched rows; rows past V are never read
+            const int r0 = 16 * j;
+            mk_add_f16_rows(pc, P.embed + (size_t)r0 * H, min(16, P.V - r0), H, 16);
             break;
         }
         default:
@@ -279,21 +294,12 @@ __device__ __forceinline__ bool mk_has_pre(int kind) {
 }
 __device__ __forceinline__ void mk_pre_pieces(const MkParams& P, const MkStage& st, MkPieces& pc) {
     const MkLayer& L = P.L[st.layer < 0 ? 0 : st.layer];
-    const unsigned hb = 2u * (unsigned)P.H;
-    pc.src[0] = st.kind == MK_LMHEAD ? P.emb_norm
-              : (st.kind == MK_CONV_IN || st.kind == MK_QKV) ? L.op_norm : L.ffn_norm;
-    pc.bytes[0] = hb;
-    pc.n = 1;
-    pc.total = pc.tx = hb;
-    if (st.kind == MK_MOE_UP) {
-        const unsigned gb = 2u * (unsigned)(P.E * P.H), bb = 2u * (unsigned)P.E;  // E % 8 == 0
-        pc.src[1] = L.gate;
-        pc.bytes[1] = gb;
-        pc.src[2] = L.ebias;
-        pc.bytes[2] = bb;
-        pc.n = 3;
-        pc.total = pc.tx = hb + gb + bb;
-    }
+    pc.n = 0;
+    pc.total = pc.tx = 0;
+    mk_add_piece(pc, st.kind == MK_LMHEAD ? P.emb_norm
+                     : (st.kind == MK_CONV_IN || st.kind == MK_QKV) ? L.op_norm : L.ffn_norm,
+                 2u * (unsigned)P.H);
+    if (st.kind == MK_MOE_UP) mk_add_piece(pc, L.ebias, 2u * (unsigned)P.E);  // norm [H] | bias [E]
 }
 
 // ---------------------------------------------------------------------------
@@ -314,18 +320,28 @@ __device__ __noinline__ void mk_producer(const MkParams& P, MkHeader& S, uint8_t
             MkPieces pc;
             if (j < 0) {
                 mk_pre_pieces(P, st, pc);
+                const MkLayer& L = P.L[st.layer < 0 ? 0 : st.layer];
+                if ((st.kind == MK_CONV_IN || st.kind == MK_QKV) && L.gate) {
+                    // pull this layer's router gate into L2 ahead of its MoE
+                    // stage, each CTA one slice
+                    const unsigned gbytes = 2u * (unsigned)(P.E * P.H);
+                    const unsigned chunk = ((gbytes + G - 1) / G + 15u) & ~15u;
+                    const unsigned o = (unsigned)b * chunk;
+                    if (o < gbytes) prefetch_l2_bulk(reinterpret_cast<const char*>(L.gate) + o, min(chunk, gbytes - o));
+                }
             } else {
                 if (moe) {  // expert slabs need this CTA's routing of this layer
                     const int want = st.kind == MK_MOE_UP ? s : s - 1;
                     const uint64_t t0 = globaltimer_ns();
-                    while (S.route_stage != want) {
-                        if (S.stop) { ok = false; break; }
-                        if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) {
-                            mk_fail(P, 8u, s, nslab);
-                            ok = false;
-                            break;
+                    for (unsigned it = 1; S.route_stage != want; it++) {
+                        if ((it & 15) == 0) {  // the clock and the stop word every 16th poll
+                            if (S.stop) { ok = false; break; }
+                            if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) {
+                                mk_fail(P, 8u, s, nslab);
+                                ok = false;
+                                break;
+                            }
                         }
-                        __nanosleep(64);
                     }
                     if (!ok) break;
                     __threadfence_block();
@@ -345,14 +361,15 @@ __device__ __noinline__ void mk_producer(const MkParams& P, MkHeader& S, uint8_t
             const unsigned need = head + pc.total <= RING ? 0u : min(head + pc.total - RING, h0);
             // wait for ring space and a free mbarrier
             const uint64_t t0 = globaltimer_ns();
-            while ((int)(S.tail - need) < 0 || nslab - S.consumed >= MK_QN) {
-                if (S.stop) { ok = false; break; }
-                if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) {
-                    mk_fail(P, 4u, s, nslab);
-                    ok = false;
-                    break;
+            for (unsigned it = 1; (int)(S.tail - need) < 0 || nslab - S.consumed >= MK_QN; it++) {
+                if ((it & 15) == 0) {
+                    if (S.stop) { ok = false; break; }
+                    if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) {
+                        mk_fail(P, 4u, s, nslab);
+                        ok = false;
+                        break;
+                    }
                 }
-                __nanosleep(32);
             }
             if (!ok) break;
             const unsigned q = nslab % MK_QN;
@@ -364,14 +381,17 @@ __device__ __noinline__ void mk_producer(const MkParams& P, MkHeader& S, uint8_t
             // per step) are evict-first in L2, pre-slabs (norm weights and the
             // router gate, read by every CTA) keep the default policy
             for (int k = 0; k < pc.n; k++) {
-                const uint8_t* src = (const uint8_t*)pc.src[k];
-                for (unsigned done = 0; done < pc.bytes[k];) {
-                    const unsigned len = min(pc.bytes[k] - done, 32768u);
-                    if (j >= 0) tma_load_1d_hint(ring + doff + done, src + done, len, &S.full[q], pol_ef);
-                    else tma_load_1d(ring + doff + done, src + done, len, &S.full[q]);
-                    done += len;
+                for (unsigned r = 0; r < pc.rows[k]; r++) {
+                    const uint8_t* src = (const uint8_t*)pc.src[k] + (size_t)r * pc.sstride[k];
+                    uint8_t* dst = ring + doff + r * pc.dstride[k];
+                    for (unsigned done = 0; done < pc.bytes[k];) {
+                        const unsigned len = min(pc.bytes[k] - done, 32768u);
+                        if (j >= 0) tma_load_1d_hint(dst + done, src + done, len, &S.full[q], pol_ef);
+                        else tma_load_1d(dst + done, src + done, len, &S.full[q]);
+                        done += len;
+                    }
                 }
-                doff += pc.bytes[k];
+                doff += pc.span[k];
             }
             if (ptrace) ptrace[j < 0 ? 12 : 14] = clock64();
             head += pc.total;
@@ -393,12 +413,12 @@ __device__ __noinline__ void mk_producer(const MkParams& P, MkHeader& S, uint8_t
 __device__ __forceinline__ const uint8_t* mk_slab_wait(const MkParams& P, MkHeader& S, uint8_t* ring,
                                                        unsigned slabno, int stage) {
     const unsigned q = slabno % MK_QN;
-    const uint64_t tw = (P.trace && threadIdx.x == 0) ? globaltimer_ns() : 0ull;
+    const long long tw = (P.trace && threadIdx.x == 0) ? clock64() : 0ll;
     if (!mbar_wait_bounded(&S.full[q], (slabno / MK_QN) & 1, nullptr)) {
         mk_fail(P, 16u, stage, slabno);
         S.stop = 1;
     }
-    if (P.trace && threadIdx.x == 0) S.wait_ns += globaltimer_ns() - tw;
+    if (P.trace && threadIdx.x == 0) S.wait_cyc += (unsigned long long)(clock64() - tw);
     cbar();  // a time-out in any consumer stops all of them (and the producer)
     return S.stop ? nullptr : ring + S.meta_off[q];
 }
@@ -415,72 +435,111 @@ __device__ __forceinline__ void mk_slab_free(MkHeader& S, unsigned slabno) {
 __device__ __forceinline__ bool mk_grid_wait(const MkParams& P, MkHeader& S, unsigned target) {
     if (threadIdx.x == 0) {
         int ok = 1;
-        const uint64_t t0 = globaltimer_ns();
-        while (ld_acquire_u32(P.gbar) < target) {
-            if (ld_volatile_u32(P.abort_flag)) { ok = 0; break; }
-            if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) {
-                mk_fail(P, 2u, (int)(target / gridDim.x), 0u);
-                ok = 0;
-                break;
+        uint64_t t0 = 0;
+        // tight acquire polls of the counter; the abort word and the clock are
+        // checked every 16th poll (each poll is an L2 round trip)
+        for (unsigned it = 1; ld_acquire_u32(P.gbar) < target; it++) {
+            if ((it & 15) == 0) {
+                if (ld_volatile_u32(P.abort_flag)) { ok = 0; break; }
+                const uint64_t now = globaltimer_ns();
+                if (!t0) t0 = now;
+                else if (now - t0 > CUINF_WAIT_LIMIT_NS) {
+                    mk_fail(P, 2u, (int)(target / gridDim.x), 0u);
+                    ok = 0;
+                    break;
+                }
             }
-            __nanosleep(20);
         }
-        __threadfence();
         S.flag = ok;
     }
     cbar();
     return S.flag != 0;
 }
+// Arrival: the consumer barrier orders every consumer's writes before thread
+// 0's release-add (bar.sync is cumulative), so a CTA that acquires the count
+// sees them.
 __device__ __forceinline__ void mk_grid_arrive(const MkParams& P) {
     cbar();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(P.gbar, 1u);
-    }
+    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;\n" ::"l"(P.gbar) : "memory");
 }
 
-// x = rmsnorm(src) into xs (fp16) and, when xB != null, its B-fragment order.
+// Data that other CTAs write during the launch (the residual, activation
+// vectors, q, the KV tail, attention partials) is read with ld.global.cg: the
+// SM's L1 is not coherent with other SMs' stores, and a line cached by an
+// earlier stage of the same launch would be stale.
+
+// x = rmsnorm(src) into xs (fp16) and, when xB != null, its B-fragment order
+// (rmsnorm, engine.cu:131-144: half(x * rsqrt(mean(x^2) + eps) * w)).  Each
+// thread owns 8 consecutive elements (H % 8 == 0, H <= 16 * MK_CT), which are
+// exactly the two B-fragment entries m = 2j, 2j+1 of quad c of their group, so
+// the whole norm takes one load of src and two consumer barriers.  red[0..11]
+// must not be read by anyone after the caller's last barrier.
 __device__ __noinline__ void mk_norm(const __half* src, const __half* w, int H, float eps,
-                                        __half* xs, __half* xB, float* red) {
-    for (int i = threadIdx.x * 8; i < H; i += MK_CT * 8)
-        *reinterpret_cast<uint4*>(xs + i) = *reinterpret_cast<const uint4*>(src + i);
-    cbar();
+                                     __half* xs, __half* xB, float* red) {
+    const int tid = threadIdx.x;
+    const int n8 = H >> 3;
+    uint4 v[2];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += MK_CT) {
-        const float v = __half2float(xs[i]);
-        ss += v * v;
-    }
-    ss = cblock_sum(ss, red);
-    const float inv = rsqrtf(ss / (float)H + eps);
-    for (int i = threadIdx.x; i < H; i += MK_CT)
-        xs[i] = __float2half_rn(__half2float(xs[i]) * inv * __half2float(w[i]));
-    cbar();
-    if (xB) {
-        for (int e = threadIdx.x; e < H / 4; e += MK_CT) build_xB_entry(xs, xB, e);
-        cbar();
-    }
-}
-
-// Router logits lg[e] = gate[e,:] . xs for the E experts (gate fp16 [E][H]
-// in shared memory); ends with a consumer barrier.
-__device__ __noinline__ void mk_router_logits(const __half* gw, const __half* xs, int E, int H, float* lg) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int e = warp; e < E; e += MK_CW) {
-        float acc = 0.f;
-        for (int k = lane * 8; k < H; k += 256) {
-            const uint4 wv = *reinterpret_cast<const uint4*>(gw + (size_t)e * H + k);
-            const uint4 xv = *reinterpret_cast<const uint4*>(xs + k);
-            const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
-            const __half2* x2 = reinterpret_cast<const __half2*>(&xv);
 #pragma unroll
-            for (int qq = 0; qq < 4; qq++) {
-                const float2 a = __half22float2(w2[qq]), bb = __half22float2(x2[qq]);
-                acc = fmaf(a.x, bb.x, acc);
-                acc = fmaf(a.y, bb.y, acc);
+    for (int r = 0; r < 2; r++) {
+        const int i = tid + r * MK_CT;
+        if (i < n8) {
+            v[r] = __ldcg(reinterpret_cast<const uint4*>(src + 8 * i));
+            const __half2* h2 = reinterpret_cast<const __half2*>(&v[r]);
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float2 f = __half22float2(h2[q]);
+                ss = fmaf(f.x, f.x, ss);
+                ss = fmaf(f.y, f.y, ss);
             }
         }
-        acc = warp_sum(acc);
-        if (lane == 0) lg[e] = acc;
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    cbar();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < MK_CW; i++) tot += red[i];
+    const float inv = rsqrtf(tot / (float)H + eps);
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int i = tid + r * MK_CT;
+        if (i < n8) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(w + 8 * i);
+            const __half* xh = reinterpret_cast<const __half*>(&v[r]);
+            const __half* wh = reinterpret_cast<const __half*>(&wv);
+            __align__(16) __half o[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) o[q] = __float2half_rn(__half2float(xh[q]) * inv * __half2float(wh[q]));
+            *reinterpret_cast<uint4*>(xs + 8 * i) = *reinterpret_cast<const uint4*>(o);
+            if (xB) {
+                // k0 = 8i = 128G + 32c + 8j: entries (G, 2j, c) and (G, 2j+1, c)
+                const int G = i >> 4, c = (i >> 2) & 3, j = i & 3;
+                __half2* e0 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j) * 4 + c) * 4);
+                __half2* e1 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j + 1) * 4 + c) * 4);
+                e0[0] = __halves2half2(o[0], o[4]);
+                e0[1] = __halves2half2(o[1], o[5]);
+                e1[0] = __halves2half2(o[2], o[6]);
+                e1[1] = __halves2half2(o[3], o[7]);
+            }
+        }
+    }
+    cbar();
+}
+
+// xB = B-fragment order of the fp16 vector src[K] (K % 128 == 0), eight
+// elements per thread; ends with a consumer barrier.
+__device__ __noinline__ void mk_build_xB(const __half* src, int K, __half* xB) {
+    for (int i = threadIdx.x; i < (K >> 3); i += MK_CT) {
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src + 8 * i));
+        const __half* o = reinterpret_cast<const __half*>(&v);
+        const int G = i >> 4, c = (i >> 2) & 3, j = i & 3;
+        __half2* e0 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j) * 4 + c) * 4);
+        __half2* e1 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j + 1) * 4 + c) * 4);
+        e0[0] = __halves2half2(o[0], o[4]);
+        e0[1] = __halves2half2(o[1], o[5]);
+        e1[0] = __halves2half2(o[2], o[6]);
+        e1[1] = __halves2half2(o[3], o[7]);
     }
     cbar();
 }
@@ -521,30 +580,133 @@ __device__ __noinline__ void mk_dot_tiles(const uint8_t* slab, int T, int K, con
     cbar();
 }
 
-// 16 fp16 rows (row stride H, in the slab) times x (fp16, natural order).
-__device__ __noinline__ void mk_dot_f16_tile(const uint8_t* slab, int H, const __half* xs, float* red,
-                                                float* out) {
+// T tiles of 16 fp16 rows (H halves each, rows mk_f16_pitch(H) bytes apart,
+// tiles consecutive) times x (fp16, natural order): out[t*16 + r].  The
+// 32-wide k blocks of each tile are spread over the consumer warps; a block is
+// two mma.m16n8k16 whose A slots follow the 16-byte row chunk a lane loads,
+// with x read in the same order.  T <= 4.
+__device__ __noinline__ void mk_dot_f16_tiles(const uint8_t* slab, int T, int H, const __half* xs, float* red,
+                                              float* out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-    const __half* Wt = reinterpret_cast<const __half*>(slab);
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int i = warp; i < (H >> 5); i += MK_CW) {
-        const uint4 wa = *reinterpret_cast<const uint4*>(Wt + (size_t)g * H + i * 32 + c * 8);
-        const uint4 wb = *reinterpret_cast<const uint4*>(Wt + (size_t)(g + 8) * H + i * 32 + c * 8);
-        const uint2* xv = reinterpret_cast<const uint2*>(xs + i * 32 + c * 8);
-        const uint2 b0 = xv[0], b1 = xv[1];
-        mma_16816(d, wa.x, wb.x, wa.y, wb.y, b0.x, b0.y);
-        mma_16816(d, wa.z, wb.z, wa.w, wb.w, b1.x, b1.y);
-    }
-    if ((lane & 3) == 0) {
-        red[warp * 16 + g] = d[0];
-        red[warp * 16 + g + 8] = d[2];
+    const unsigned pitch = mk_f16_pitch(H);
+    const int KB = H >> 5;
+    for (int t = 0; t < T; t++) {
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint8_t* tb = slab + (size_t)t * 16 * pitch + c * 16;
+        for (int i = warp; i < KB; i += MK_CW) {
+            const uint4 wa = *reinterpret_cast<const uint4*>(tb + g * pitch + i * 64);
+            const uint4 wb = *reinterpret_cast<const uint4*>(tb + (g + 8) * pitch + i * 64);
+            const uint2* xv = reinterpret_cast<const uint2*>(xs + i * 32 + c * 8);
+            const uint2 b0 = xv[0], b1 = xv[1];
+            mma_16816(d0, wa.x, wb.x, wa.y, wb.y, b0.x, b0.y);
+            mma_16816(d1, wa.z, wb.z, wa.w, wb.w, b1.x, b1.y);
+        }
+        if (c == 0) {
+            red[(warp * 4 + t) * 16 + g] = d0[0] + d1[0];
+            red[(warp * 4 + t) * 16 + g + 8] = d0[2] + d1[2];
+        }
     }
     cbar();
-    if (threadIdx.x < 16) {
-        float s = 0.f;
+    for (int i = threadIdx.x; i < T * 16; i += MK_CT) {
+        const int t = i >> 4, r = i & 15;
+        float sum = 0.f;
 #pragma unroll
-        for (int w = 0; w < MK_CW; w++) s += red[w * 16 + threadIdx.x];
-        out[threadIdx.x] = s;
+        for (int w = 0; w < MK_CW; w++) sum += red[(w * 4 + t) * 16 + r];
+        out[i] = sum;
+    }
+    cbar();
+}
+
+// Router logits lg[e] = gate[e,:] . xs (gate fp16 [E][H] in global memory, E
+// % 8 == 0).  The gate is read straight from L2: it is small, every CTA reads
+// it, and it is fetched with the default L2 policy while the streamed weights
+// are evict-first, so it stays resident across steps.  Units are (16-expert
+// tile, 32-wide k block) pairs; rows past E are clamped and discarded.
+__device__ __noinline__ void mk_router_l2(const __half* gate, int E, int H, const __half* xs, float* red,
+                                          float* lg) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int KB = H >> 5, T = (E + 15) >> 4;
+    for (int t = 0; t < T; t++) {
+        const int ra = min(16 * t + g, E - 1), rb = min(16 * t + g + 8, E - 1);
+        const __half* pa = gate + (size_t)ra * H + c * 8;
+        const __half* pb = gate + (size_t)rb * H + c * 8;
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+        int i = warp;
+        for (; i + 3 * MK_CW < KB; i += 4 * MK_CW) {  // four k blocks in flight
+            uint4 wa[4], wb[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                wa[u] = __ldcg(reinterpret_cast<const uint4*>(pa + (i + u * MK_CW) * 32));
+                wb[u] = __ldcg(reinterpret_cast<const uint4*>(pb + (i + u * MK_CW) * 32));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint2* xv = reinterpret_cast<const uint2*>(xs + (i + u * MK_CW) * 32 + c * 8);
+                const uint2 b0 = xv[0], b1 = xv[1];
+                mma_16816(d0, wa[u].x, wb[u].x, wa[u].y, wb[u].y, b0.x, b0.y);
+                mma_16816(d1, wa[u].z, wb[u].z, wa[u].w, wb[u].w, b1.x, b1.y);
+            }
+        }
+        for (; i < KB; i += MK_CW) {
+            const uint4 wa = __ldcg(reinterpret_cast<const uint4*>(pa + i * 32));
+            const uint4 wb = __ldcg(reinterpret_cast<const uint4*>(pb + i * 32));
+            const uint2* xv = reinterpret_cast<const uint2*>(xs + i * 32 + c * 8);
+            const uint2 b0 = xv[0], b1 = xv[1];
+            mma_16816(d0, wa.x, wb.x, wa.y, wb.y, b0.x, b0.y);
+            mma_16816(d1, wa.z, wb.z, wa.w, wb.w, b1.x, b1.y);
+        }
+        if (c == 0) {
+            red[(warp * 4 + t) * 16 + g] = d0[0] + d1[0];
+            red[(warp * 4 + t) * 16 + g + 8] = d0[2] + d1[2];
+        }
+    }
+    cbar();
+    for (int i = threadIdx.x; i < T * 16; i += MK_CT) {
+        const int t = i >> 4, r = i & 15;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < MK_CW; w++) sum += red[(w * 4 + t) * 16 + r];
+        lg[i] = sum;
+    }
+    cbar();
+}
+
+// Expert selection of the reference's host loop (engine.cu:883-892) by rank:
+// expert e is picked in slot rank(e) = #{e' : s' > s, or s' == s and e' < e}
+// when that rank is below topk, which is the order of the reference's repeated
+// strict-'>' scan.  Scores that are NaN or <= -1e30 rank last (by index), as
+// the scan never picks them before the smallest unused index.  Weights are
+// the unbiased sigmoids of the picks over (their sum in slot order + 1e-6).
+// All consumer threads call it; E <= MK_CT; scratch: 2*E floats.
+__device__ __noinline__ void mk_route_select(const float* lg, const __half* bias, int E, int topk, int* idx,
+                                             float* w, float* scratch) {
+    const int e = threadIdx.x;
+    float* sc = scratch;
+    float* sg = scratch + E;
+    float sig = 0.f, key = -INFINITY;
+    if (e < E) {
+        sig = route_sigmoid_call(lg[e]);
+        const float score = sig + __half2float(bias[e]);
+        key = (score > -1e30f) ? score : -INFINITY;  // NaN compares false
+        sc[e] = key;
+    }
+    cbar();
+    if (e < E) {
+        int rank = 0;
+        for (int o = 0; o < E; o++) {
+            const float ko = sc[o];
+            rank += (ko > key || (ko == key && o < e)) ? 1 : 0;
+        }
+        if (rank < topk) {
+            idx[rank] = e;
+            sg[rank] = sig;
+        }
+    }
+    cbar();
+    if (e == 0) {
+        float wsum = 0.f;
+        for (int t = 0; t < topk; t++) wsum += sg[t];
+        for (int t = 0; t < topk; t++) w[t] = sg[t] / (wsum + 1e-6f);
     }
     cbar();
 }
@@ -627,8 +789,8 @@ __device__ __noinline__ void mk_attn_item(const MkParams& P, const MkLayer& L, i
         const __half* qh = P.q + (size_t)(h * gqa + (real ? g : 0)) * CUINF_HD + 16 * c;
 #pragma unroll
         for (int s = 0; s < 4; s++) {
-            const uint32_t lo = *reinterpret_cast<const uint32_t*>(qh + 4 * s);
-            const uint32_t hi = *reinterpret_cast<const uint32_t*>(qh + 4 * s + 2);
+            const uint32_t lo = __ldcg(reinterpret_cast<const unsigned int*>(qh + 4 * s));
+            const uint32_t hi = __ldcg(reinterpret_cast<const unsigned int*>(qh + 4 * s + 2));
             aq[s][0] = real ? lo : 0u;
             aq[s][1] = real ? hi : 0u;
         }
@@ -636,7 +798,7 @@ __device__ __noinline__ void mk_attn_item(const MkParams& P, const MkLayer& L, i
     float m_run = ATTN_NEG, l_run = 0.f, O[8][4];
 #pragma unroll
     for (int t = 0; t < 8; t++) O[t][0] = O[t][1] = O[t][2] = O[t][3] = 0.f;
-    attn_warp_units(L.kc8, L.vc8, L.ksc, L.vsc, L.ktail, L.vtail, nkv, h, n_fp8, tail_len, kfac, aq,
+    attn_warp_units<true>(L.kc8, L.vc8, L.ksc, L.vsc, L.ktail, L.vtail, nkv, h, n_fp8, tail_len, kfac, aq,
                     u0 + warp, u1, MK_CW, m_run, l_run, O);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
@@ -755,7 +917,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const __grid_consta
             clk0 = clock64();
             for (int w = 4; w <= 10; w++) tr[w] = 0ull;
             tr[11] = (unsigned long long)clk0;
-            S.wait_ns = 0ull;
+            S.wait_cyc = 0ull;
         }
         unsigned long long* trs = (P.trace && tid == 0) ? P.trace + ((size_t)s * G + b) * MK_TRACE_W : nullptr;
         // ---- stage prologue ----
@@ -779,8 +941,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const __grid_consta
                 break;
             }
             case MK_RES:
-                for (int e = tid; e < st.K / 4; e += MK_CT) build_xB_entry(st.act, xB, e);
-                cbar();
+                mk_build_xB(st.act, st.K, xB);
                 break;
             case MK_DENSE_UP:
                 mk_norm(P.h, nw, H, P.eps, xs, xB, red);
@@ -788,11 +949,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const __grid_consta
             case MK_MOE_UP: {
                 mk_norm(P.h, nw, H, P.eps, xs, xB, red);
                 if (trs) trs[8] = clock64() - clk0;
-                const __half* gw = nw + H;
-                mk_router_logits(gw, xs, P.E, H, lg);
+                mk_router_l2(L.gate, P.E, H, xs, red, lg);
                 if (trs) trs[9] = clock64() - clk0;
-                if (tid < 32) route_select_warp(lg, gw + (size_t)P.E * H, P.E, P.topk, S.sidx, S.sw);
-                cbar();
+                mk_route_select(lg, reinterpret_cast<const __half*>(pre + 2 * H), P.E, P.topk, S.sidx, S.sw,
+                                red + MK_CW * 4 * 16 - 2 * P.E);
                 if (trs) trs[10] = clock64() - clk0;
                 if (tid == 0) {
                     __threadfence_block();
@@ -805,15 +965,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const __grid_consta
                 break;
             }
             case MK_MOE_DOWN:
-                for (int e = tid; e < P.topk * (P.I / 4); e += MK_CT) {
-                    const int t = e / (P.I / 4), r = e - t * (P.I / 4);
-                    build_xB_entry(P.mid + (size_t)t * P.I, xB + (size_t)t * P.I, r);
-                }
-                cbar();
+                mk_build_xB(P.mid, P.topk * P.I, xB);  // the expert slices are consecutive
                 break;
             case MK_LMHEAD:
                 if (b == 0 && P.hidden_out)
-                    for (int i = tid; i < H; i += MK_CT) P.hidden_out[i] = P.h[i];
+                    for (int i = tid; i < H; i += MK_CT) P.hidden_out[i] = __ldcg(P.h + i);
                 mk_norm(P.h, nw, H, P.eps, xs, nullptr, red);
                 break;
             default:
@@ -842,7 +998,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const __grid_consta
             // load latency hides behind it (only this CTA writes them)
             float hres = 0.f;
             if ((st.kind == MK_RES || st.kind == MK_MOE_DOWN) && tid < 16)
-                hres = __half2float(P.h[16 * j + tid]);
+                hres = __half2float(__ldcg(P.h + 16 * j + tid));
             switch (st.kind) {
                 case MK_CONV_IN: {
                     mk_dot_tiles(slab, 3, H, xB, 0, red, out);
@@ -917,7 +1073,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const __grid_consta
                     break;
                 }
                 case MK_LMHEAD: {
-                    mk_dot_f16_tile(slab, H, xs, red, out);
+                    mk_dot_f16_tiles(slab, 1, H, xs, red, out);
                     if (tr_item) tr[6] = clock64() - clk0;
                     if (tid < 16) {
                         const int r = 16 * j + tid;
@@ -939,7 +1095,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mk(const __grid_consta
         if (P.trace) {
             cbar();
             if (tid == 0) {
-                P.trace[((size_t)s * G + b) * MK_TRACE_W + 2] = S.wait_ns;
+                P.trace[((size_t)s * G + b) * MK_TRACE_W + 2] = S.wait_cyc;
                 P.trace[((size_t)s * G + b) * MK_TRACE_W + 3] = globaltimer_ns();
             }
         }

@@ -104,7 +104,7 @@ class Session:
     def trace(self):
         """Per-stage timestamps of the last traced megakernel step: returns
         (kinds [S], t [S, G, 16]): %globaltimer ns at start, prologue end and
-        end (0, 1, 3), slab-wait ns (2); SM cycles since the stage start for
+        end (0, 1, 3), slab-wait SM cycles (2); SM cycles since the stage start for
         pre-slab ready (4), the first item's slab ready, dot done and
         epilogue done (5-7), MoE-up norm, router dots and selection done
         (8-10); %clock64 at the stage start (11); producer %clock64 at the

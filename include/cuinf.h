@@ -217,8 +217,9 @@ int cuinf_session_keep_logits(cuinf_session* s, int on);
 #define CUINF_OPT_PREFETCH 1
 #define CUINF_OPT_PDL 2
 /* CUINF_OPT_MEGAKERNEL: run the step as one persistent cooperative kernel
- * (one CTA per SM, TMA weight ring, grid barriers between stages); falls back
- * to the multi-kernel graph when the device or model does not fit. */
+ * (one CTA per SM, TMA weight ring, grid barriers between stages) instead of
+ * the captured multi-kernel graph (default 0); falls back to the graph when
+ * the device or model does not fit. */
 #define CUINF_OPT_MEGAKERNEL 3
 /* CUINF_OPT_TRACE: the megakernel records %globaltimer at every stage start
  * and end of every CTA (read with cuinf_session_trace; default 0). */
@@ -229,7 +230,7 @@ int cuinf_session_set_option(cuinf_session* s, int option, int value);
 int cuinf_device_error(unsigned* flags);
 /* Per-stage timestamps of the last traced megakernel step: buf receives
  * [n_stages][n_ctas][16]: %globaltimer ns at the stage start, prologue end
- * and end (words 0, 1, 3); ns spent waiting for weight slabs (2); SM cycles
+ * and end (words 0, 1, 3); SM cycles spent waiting for weight slabs (2); SM cycles
  * since the stage start for: pre-slab ready (4), the first item's slab
  * ready, dot done, epilogue done (5-7), MoE-up norm, router dots and expert
  * selection done (8-10); %clock64 at the stage start (11); the producer's

@@ -89,9 +89,10 @@ def test_engine_greedy_matches_oracle(tiny):
 def test_kernels_per_step(tiny):
     cfg, om, gm = tiny
     s = Session(gm, max_ctx=64)
-    assert s.kernels_per_step == 1  # one persistent launch
-    s.set_option(Session.OPT_MEGAKERNEL, 0)
+    assert not s.uses_megakernel  # the captured multi-kernel graph is the default
     assert s.kernels_per_step == 2 * 4 + 3 * 2 + 2 * 6 + 1
+    s.set_option(Session.OPT_MEGAKERNEL, 1)
+    assert s.kernels_per_step == 1  # one persistent launch
 
 
 @pytest.mark.parametrize("opt", [(1, 0), (2, 0)])
