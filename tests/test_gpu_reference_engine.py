@@ -1,0 +1,88 @@
+"""Greedy tokens against the reference engine itself (src/engine.cu of
+g023/cuda_inf, built unmodified for sm_100a by oracle/Makefile into
+oracle/_ref/ref_engine), on the same random-init full-size weights.
+
+The prompt is one token.  For a longer prompt the reference runs a batched
+prefill whose attention reads the prompt's own keys from the FP8 group that
+the prefill has just committed (attention_fused, engine.cu:236-308, with the
+placement at 831-855), while this engine decodes prompt tokens one by one
+(fp16 tail until a group is full); the two are different computations, so a
+batched prefill is what greedy parity on long prompts needs.  With a
+one-token prompt the reference's first step is its decode step
+(attn_decode_split/combine), and every later step is decode in both engines.
+
+80 tokens are generated, crossing the FP8 commit of the first KV group.  The
+CPU oracle, teacher-forced along the reference's tokens, gives each
+decision's top-2 logit margin.  This engine's tokens must equal the
+reference's up to the first difference, that difference may only fall on a
+near-tie (margin below TIE_MARGIN of the top logit), and wherever the margin
+is clear the reference's token must be the oracle's argmax.
+"""
+import os
+import shutil
+import subprocess
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import pyoracle as orc
+from cuda_inf_b200 import weights
+from cuda_inf_b200.engine import Model, Session
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_ENGINE = os.path.join(ROOT, "oracle", "_ref", "ref_engine")
+N_PROMPT = 1
+N_NEW = 80
+TIE_MARGIN = 1e-2  # relative top-2 logit margin below which a greedy pick is a near-tie
+
+
+@pytest.mark.skipif(not os.path.exists(REF_ENGINE), reason="reference engine not built (oracle/_ref)")
+def test_greedy_matches_reference_engine(cuda):
+    cfg = weights.default_config()
+    blob, index = weights.synth_device_blob(cfg, seed=97, device=cuda)
+    prompt = [int(t) for t in np.random.default_rng(5).integers(0, cfg.vocab, N_PROMPT)]
+    base = "/dev/shm" if shutil.disk_usage("/dev/shm").free > 6e9 else None
+    with tempfile.TemporaryDirectory(dir=base) as d:
+        weights.save_blob(blob, index, d)
+        np.array(prompt, np.int32).tofile(os.path.join(d, "ids.i32"))
+        os.makedirs(os.path.join(d, "scratch"), exist_ok=True)
+        r = subprocess.run([REF_ENGINE, "--dir", d, "--ids", os.path.join(d, "ids.i32"), "--n", str(N_NEW),
+                            "--no-stream"], cwd=d, capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stderr[-500:]
+        ref = np.fromfile(os.path.join(d, "scratch", "engine_out_ids.i32"), np.int32).tolist()
+        host = np.fromfile(os.path.join(d, "weights.bin"), np.uint8)
+    assert 1 <= len(ref) <= N_NEW
+
+    gm = Model.from_device_blob(blob, index, cfg)
+    s = Session(gm, max_ctx=N_PROMPT + N_NEW + 8)
+    ours = s.generate(prompt, len(ref))
+    s.close()
+    gm.close()
+    del blob
+    torch.cuda.empty_cache()
+
+    orc.set_threads(os.cpu_count() or 1)
+    om = orc.Model(weights.config_dict(cfg), host, index)
+    st = om.state(N_PROMPT + N_NEW + 8)
+    for t in prompt[:-1]:
+        st.forward(t, want_logits=False)
+    matched = 0
+    feed = prompt[-1]
+    for i, tok in enumerate(ref):
+        nxt, lg, _ = st.forward(feed)
+        top = np.sort(lg)[::-1]
+        near_tie = top[0] - top[1] <= TIE_MARGIN * max(1.0, abs(float(top[0])))
+        if not near_tie:
+            assert tok == nxt, (i, tok, nxt)
+        if ours[i] != tok:
+            assert near_tie, (i, ours[: i + 1], ref[: i + 1])
+            break
+        matched += 1
+        feed = tok
+    print(f"greedy tokens equal to the reference engine's: first {matched} of {len(ref)}; "
+          f"ours {ours[:matched + 1]}, reference {ref[:matched + 1]}")
+    assert matched >= 1
