@@ -12,11 +12,17 @@ one-token prompt the reference's first step is its decode step
 (attn_decode_split/combine), and every later step is decode in both engines.
 
 80 tokens are generated, crossing the FP8 commit of the first KV group.  The
-CPU oracle, teacher-forced along the reference's tokens, gives each
-decision's top-2 logit margin.  This engine's tokens must equal the
-reference's up to the first difference, that difference may only fall on a
-near-tie (margin below TIE_MARGIN of the top logit), and wherever the margin
-is clear the reference's token must be the oracle's argmax.
+CPU oracle, teacher-forced along the reference's tokens, gives at every
+position the top-2 logit margin and, for each of the 22 MoE layers, the
+margin between the 4th and 5th expert scores.  Two faithful implementations
+differ by fp16 ulps in the residual stream, which moves router scores by up
+to ~1.5e-3; a flipped expert then changes the logits by far more than any
+rounding, so the two greedy trajectories can part at such a routing
+near-tie.  The test walks the reference's tokens: this engine's tokens must
+equal them up to the first difference, that difference must sit on a
+near-tie (logit margin below TIE_MARGIN of the top logit, or a routing
+margin below ROUTE_MARGIN in some layer), and at every clear position the
+reference's token must be the oracle's argmax.  The matched prefix is printed.
 """
 import os
 import shutil
@@ -38,6 +44,7 @@ REF_ENGINE = os.path.join(ROOT, "oracle", "_ref", "ref_engine")
 N_PROMPT = 1
 N_NEW = 80
 TIE_MARGIN = 1e-2  # relative top-2 logit margin below which a greedy pick is a near-tie
+ROUTE_MARGIN = 2e-3  # 4th-vs-5th expert score margin below which routing is a near-tie
 
 
 @pytest.mark.skipif(not os.path.exists(REF_ENGINE), reason="reference engine not built (oracle/_ref)")
@@ -73,14 +80,17 @@ def test_greedy_matches_reference_engine(cuda):
     matched = 0
     feed = prompt[-1]
     for i, tok in enumerate(ref):
-        nxt, lg, _ = st.forward(feed)
+        nxt, lg, _, sc = st.forward_ex(feed)
         top = np.sort(lg)[::-1]
-        near_tie = top[0] - top[1] <= TIE_MARGIN * max(1.0, abs(float(top[0])))
+        srt = -np.sort(-sc, axis=1)
+        route_margin = float(np.min(srt[:, cfg.top_k - 1] - srt[:, cfg.top_k]))
+        logit_tie = top[0] - top[1] <= TIE_MARGIN * max(1.0, abs(float(top[0])))
+        near_tie = logit_tie or route_margin <= ROUTE_MARGIN
+        if ours[i] != tok:
+            assert near_tie, (i, float(top[0] - top[1]), route_margin, ours[: i + 1], ref[: i + 1])
+            break
         if not near_tie:
             assert tok == nxt, (i, tok, nxt)
-        if ours[i] != tok:
-            assert near_tie, (i, ours[: i + 1], ref[: i + 1])
-            break
         matched += 1
         feed = tok
     print(f"greedy tokens equal to the reference engine's: first {matched} of {len(ref)}; "
