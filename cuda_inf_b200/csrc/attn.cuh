@@ -79,6 +79,28 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
         const bool tail = u >= n_fp8;
         const int valid = tail ? tail_len : CUINF_KVGROUP;
         const int kbase = u * CUINF_KVGROUP;
+        // An FP8 unit's K (8 x 16 B per lane) and V (16 x 8 B per lane) are
+        // all requested before any math, so the unit costs one memory round
+        // trip instead of one per 8-key block.
+        uint4 kraw[8];
+        uint2 vraw[4][4];
+        if (!tail) {
+            const size_t kstride = (size_t)nkv * CUINF_HD;
+#pragma unroll
+            for (int jn = 0; jn < 8; jn++) {
+                const uint8_t* kp8 = kc8 + ((size_t)(kbase + 8 * jn + g) * nkv + h) * CUINF_HD + 16 * c;
+                kraw[jn] = CG ? __ldcg(reinterpret_cast<const uint4*>(kp8)) : ldg_stream(kp8);
+            }
+#pragma unroll
+            for (int s2 = 0; s2 < 4; s2++) {
+                const uint8_t* vp = vc8 + ((size_t)(kbase + 16 * s2 + 2 * c) * nkv + h) * CUINF_HD + 8 * g;
+                const int off[4] = {0, 1, 8, 9};
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    vraw[s2][i] = CG ? __ldcg(reinterpret_cast<const uint2*>(vp + off[i] * kstride))
+                                     : ldg_stream8(vp + off[i] * kstride);
+            }
+        }
         // ---- S = Q K^T for 64 keys (8 n-tiles of 8 keys) ----
         float S[8][4];
 #pragma unroll
@@ -87,8 +109,7 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
             const int kk = 8 * jn + g;  // key within the unit
             uint32_t kb[8];
             if (!tail) {
-                const uint8_t* kp8 = kc8 + ((size_t)(kbase + kk) * nkv + h) * CUINF_HD + 16 * c;
-                uint4 raw = CG ? __ldcg(reinterpret_cast<const uint4*>(kp8)) : ldg_stream(kp8);
+                const uint4 raw = kraw[jn];
                 const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
@@ -148,20 +169,7 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
             const int ka = 16 * s2 + 2 * c;  // keys ka, ka+1, ka+8, ka+9
             uint32_t b0[8], b1[8];
             if (!tail) {
-                const uint8_t* vp = vc8 + ((size_t)(kbase + ka) * nkv + h) * CUINF_HD + 8 * g;
-                const size_t kstride = (size_t)nkv * CUINF_HD;
-                uint2 va, vb, vc, vd;
-                if (CG) {
-                    va = __ldcg(reinterpret_cast<const uint2*>(vp));
-                    vb = __ldcg(reinterpret_cast<const uint2*>(vp + kstride));
-                    vc = __ldcg(reinterpret_cast<const uint2*>(vp + 8 * kstride));
-                    vd = __ldcg(reinterpret_cast<const uint2*>(vp + 9 * kstride));
-                } else {
-                    va = ldg_stream8(vp);
-                    vb = ldg_stream8(vp + kstride);
-                    vc = ldg_stream8(vp + 8 * kstride);
-                    vd = ldg_stream8(vp + 9 * kstride);
-                }
+                const uint2 va = vraw[s2][0], vb = vraw[s2][1], vc = vraw[s2][2], vd = vraw[s2][3];
                 uint32_t r;
                 r = prmt(va.x, vb.x, 0x5140u); b0[0] = fp8x2_to_h2(r); b0[1] = fp8x2_to_h2(r >> 16);
                 r = prmt(va.x, vb.x, 0x7362u); b0[2] = fp8x2_to_h2(r); b0[3] = fp8x2_to_h2(r >> 16);
@@ -326,6 +334,16 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
         P.out[(size_t)(h * gqa + r) * CUINF_HD + d] = __float2half_rn(o / s_g[8 + r]);
     }
     if (threadIdx.x == 0) P.counters[h] = 0u;
+}
+
+// Splits for the decode engine: one 64-token unit per warp at the session's
+// longest context (ATTN_THREADS/32 units per CTA), so every warp of every CTA
+// has a unit and the combine merges as few partials as that allows; at most
+// ATTN_MAX_PARTS (split, query head) partials per kv head.
+static inline int attn_engine_nsplit(int gqa, int max_units) {
+    int ns = (max_units + ATTN_THREADS / 32 - 1) / (ATTN_THREADS / 32);
+    if (ns * gqa > ATTN_MAX_PARTS) ns = ATTN_MAX_PARTS / gqa;
+    return ns < 1 ? 1 : ns;
 }
 
 // Splits that fill the GPU: about two CTAs per SM over all kv heads, at most

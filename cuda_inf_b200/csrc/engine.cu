@@ -225,6 +225,27 @@ static cudaError_t launch_k(Kern kernel, dim3 grid, dim3 block, size_t smem, cud
     return cudaLaunchKernelEx(&cfg, kernel, params);
 }
 
+// Same, with thread-block clusters of cluster_x CTAs along x.
+template <typename Kern, typename Par>
+static cudaError_t launch_kc(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                             int cluster_x, const Par& params) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cluster_x;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
 static int set_kernel_attrs(const cuinf_config& c);
 
 extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* expert_bias,
@@ -290,7 +311,7 @@ extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* exper
     const size_t sd = moe_down_smem(I, topk);
     if (sd > 48 * 1024)
         CUINF_TRY(cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sd));
-    k_moe_down<<<(H + 15) / 16, 256, sd, ST(stream)>>>(D);
+    CUINF_TRY(launch_kc(k_moe_down, dim3((H / 16) * topk), dim3(256), sd, ST(stream), false, topk, D));
     return cuinf_launch_status();
 }
 
@@ -970,7 +991,8 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
                           {},
                           [=](const L2Ranges& nx, bool pdl) mutable {
                               D.next = nx;
-                              return launch_k(k_moe_down, dim3(H / 16), dim3(256), sd, st, pdl, D);
+                              return launch_kc(k_moe_down, dim3((H / 16) * c.top_k), dim3(256), sd, st, pdl,
+                                               c.top_k, D);
                           }});
         }
     }
@@ -1091,7 +1113,7 @@ extern "C" int cuinf_session_create(cuinf_model* m, int max_ctx, void* stream, c
     TRYS(dalloc(s, &s->am_key, 16));
     TRYS(dalloc(s, &s->am_ticket, 16));
     const int units = max_ctx / CUINF_KVGROUP + 1;
-    s->nsplit = attn_default_nsplit(nkv, gqa, units, s->num_sms);
+    s->nsplit = attn_engine_nsplit(gqa, units);
     TRYS(dalloc(s, &s->attn_part, (size_t)nkv * s->nsplit * gqa * ATTN_PART_STRIDE * 4));
     TRYS(dalloc(s, &s->attn_cnt, (size_t)nkv * 4));
     s->attn.assign(c.n_layers, AttnState());

@@ -29,26 +29,80 @@ namespace cg = cooperative_groups;
 // timed out (its kernel then skipped its math).
 static __device__ unsigned g_engine_err;
 
-// Norm prologue: x = rmsnorm(src, w) into shared memory (fp16, natural order)
-// and its B-fragment permutation xB.  src is the residual h, or the embedding
-// row embed[*tok] for the first layer (then CTA 0 also stores it into h).
-__device__ __forceinline__ void norm_prologue(const __half* __restrict__ h,
-                                              const __half* __restrict__ embed,
-                                              const int* __restrict__ tok, __half* h_store,
-                                              const __half* __restrict__ w, int H, float eps,
-                                              __half* xs, __half* xB, float* red) {
+// Norm prologue: x = rmsnorm(src, w) (rmsnorm, engine.cu:131-144) into shared
+// memory (fp16, natural order) and its B-fragment permutation xB.  src is the
+// residual h, or the embedding row embed[*tok] for the first layer (then CTA 0
+// also stores it into h).
+// The norm weight is a static tensor, so each thread
+// loads its 8-element chunks of it before the dependency wait (norm_w_load);
+// after the wait, norm_prologue_fast reads its chunks of src once, reduces the
+// sum of squares with one block barrier, and writes both xs and the two
+// B-fragment entries its chunk forms (8 consecutive elements k0..k0+7 are
+// entries m = 2j, 2j+1 of quad c of group G for k0 = 128G + 32c + 8j).
+// H % 8 == 0 and H <= 16 * blockDim.x.
+struct NormW {
+    uint4 w[2];
+};
+__device__ __forceinline__ void norm_w_load(NormW& nw, const __half* __restrict__ w, int H) {
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int i = threadIdx.x + r * blockDim.x;
+        nw.w[r] = i < (H >> 3) ? ldg_stream(w + 8 * i) : make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+__device__ __forceinline__ void norm_prologue_fast(const NormW& nw, const __half* __restrict__ h,
+                                                   const __half* __restrict__ embed,
+                                                   const int* __restrict__ tok, __half* h_store, int H,
+                                                   float eps, __half* xs, __half* xB, float* red) {
     const __half* src = h;
     if (embed) {
         src = embed + (size_t)(*tok) * H;
         if (blockIdx.x == 0 && blockIdx.y == 0)
-            for (int i = threadIdx.x; i < H; i += blockDim.x) h_store[i] = src[i];
+            for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8)
+                *reinterpret_cast<uint4*>(h_store + i) = *reinterpret_cast<const uint4*>(src + i);
     }
-    for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8)
-        *reinterpret_cast<uint4*>(xs + i) = *reinterpret_cast<const uint4*>(src + i);
+    const int n8 = H >> 3;
+    uint4 v[2];
+    float ss = 0.f;
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int i = threadIdx.x + r * blockDim.x;
+        if (i < n8) {
+            v[r] = *reinterpret_cast<const uint4*>(src + 8 * i);
+            const __half2* h2 = reinterpret_cast<const __half2*>(&v[r]);
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float2 f = __half22float2(h2[q]);
+                ss = fmaf(f.x, f.x, ss);
+                ss = fmaf(f.y, f.y, ss);
+            }
+        }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
-    rmsnorm_smem(xs, w, xs, H, eps, red);
-    __syncthreads();
-    for (int e = threadIdx.x; e < H / 4; e += blockDim.x) build_xB_entry(xs, xB, e);
+    float tot = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += red[i];
+    const float inv = rsqrtf(tot / (float)H + eps);
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int i = threadIdx.x + r * blockDim.x;
+        if (i < n8) {
+            const __half* xh = reinterpret_cast<const __half*>(&v[r]);
+            const __half* wh = reinterpret_cast<const __half*>(&nw.w[r]);
+            __align__(16) __half o[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) o[q] = __float2half_rn(__half2float(xh[q]) * inv * __half2float(wh[q]));
+            *reinterpret_cast<uint4*>(xs + 8 * i) = *reinterpret_cast<const uint4*>(o);
+            const int G = i >> 4, c = (i >> 2) & 3, j = i & 3;
+            __half2* e0 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j) * 4 + c) * 4);
+            __half2* e1 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j + 1) * 4 + c) * 4);
+            e0[0] = __halves2half2(o[0], o[4]);
+            e0[1] = __halves2half2(o[1], o[5]);
+            e1[0] = __halves2half2(o[2], o[6]);
+            e1[1] = __halves2half2(o[3], o[7]);
+        }
+    }
     __syncthreads();
 }
 
@@ -129,9 +183,11 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256) k_attn_qkv(QkvP
         tma_tile_int4(wp, ws, P.H, row0, tile, &bar);
         l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
     }
+    NormW nw;
+    norm_w_load(nw, P.norm_w, P.H);
     pdl_trigger();
     pdl_wait();
-    norm_prologue(P.h, P.embed, P.tok, P.h_store, P.norm_w, P.H, P.eps, xs, xB, red + 128);
+    norm_prologue_fast(nw, P.h, P.embed, P.tok, P.h_store, P.H, P.eps, xs, xB, red + 128);
     float y0 = 0.f, y1 = 0.f;
     if (stage_wait(&bar))
         int4_tile_dot_smem<2>(tile, P.H, warp, P.H >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
@@ -305,9 +361,24 @@ __global__ void __launch_bounds__(384) k_conv_in(ConvParams P) {
         for (int t = 0; t < 3; t++) tma_tile_int4(P.wp, P.ws, P.H, t * P.H + c0, tiles + t * TB, &bar);
         l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
     }
+    NormW nw;
+    norm_w_load(nw, P.norm_w, P.H);
+    // the conv taps and the two history rows of this CTA's 16 channels are
+    // read before the dependency wait: the taps are static and the state was
+    // last written by this layer's conv_in of the previous step
+    float cw0 = 0.f, cw1 = 0.f, cw2 = 0.f, cs0 = 0.f;
+    __half cs1 = __float2half_rn(0.f);
+    if (threadIdx.x < 16) {
+        const int c = c0 + threadIdx.x;
+        cw0 = __half2float(P.conv_w[c * 3 + 0]);
+        cw1 = __half2float(P.conv_w[c * 3 + 1]);
+        cw2 = __half2float(P.conv_w[c * 3 + 2]);
+        cs0 = __half2float(P.state[c]);
+        cs1 = P.state[P.H + c];
+    }
     pdl_trigger();
     pdl_wait();
-    norm_prologue(P.h, P.embed, P.tok, P.h_store, P.norm_w, P.H, P.eps, xs, xB, red + 192);
+    norm_prologue_fast(nw, P.h, P.embed, P.tok, P.h_store, P.H, P.eps, xs, xB, red + 192);
     float y0 = 0.f, y1 = 0.f;
     if (stage_wait(&bar))
         int4_tile_dot_smem<2>(tiles + tile * TB, P.H, warp & 3, P.H >> 7, 4,
@@ -323,12 +394,9 @@ __global__ void __launch_bounds__(384) k_conv_in(ConvParams P) {
                    red[(4 * t + 3) * 16 + i];
         const __half Cb = __float2half_rn(v[1]);
         const __half Bx = __float2half_rn(v[0] * v[2]);
-        const float s0 = __half2float(P.state[c]), s1 = __half2float(P.state[P.H + c]);
-        const float w0 = __half2float(P.conv_w[c * 3 + 0]), w1 = __half2float(P.conv_w[c * 3 + 1]),
-                    w2 = __half2float(P.conv_w[c * 3 + 2]);
-        const float co = s0 * w0 + s1 * w1 + __half2float(Bx) * w2;
+        const float co = cs0 * cw0 + __half2float(cs1) * cw1 + __half2float(Bx) * cw2;
         P.y[c] = __float2half_rn(__half2float(Cb) * co);
-        P.state[c] = P.state[P.H + c];
+        P.state[c] = cs1;
         P.state[P.H + c] = Bx;
     }
 }
@@ -371,9 +439,11 @@ __global__ void __launch_bounds__(256) k_ffn_up(FfnUpParams P) {
         tma_tile_int4(P.w3p, P.w3s, P.H, row0, tiles + TB, &bar);
         l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
     }
+    NormW nw;
+    norm_w_load(nw, P.norm_w, P.H);
     pdl_trigger();
     pdl_wait();
-    norm_prologue(P.h, nullptr, nullptr, nullptr, P.norm_w, P.H, P.eps, xs, xB, red + 128);
+    norm_prologue_fast(nw, P.h, nullptr, nullptr, nullptr, P.H, P.eps, xs, xB, red + 128);
     float y0 = 0.f, y1 = 0.f;
     if (stage_wait(&bar))
         int4_tile_dot_smem<2>(tiles + tile * TB, P.H, warp >> 1, P.H >> 7, 4,
@@ -454,6 +524,8 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
         if (ne > 0) tma_load_1d(gs, P.gate + (size_t)e0 * P.H, (uint32_t)ne * P.H * 2, &bar[0]);
         l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
     }
+    NormW nw;
+    if (!P.xn) norm_w_load(nw, P.norm_w, P.H);
     pdl_trigger();
     pdl_wait();
     if (P.xn) {
@@ -462,7 +534,7 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
         for (int e = threadIdx.x; e < P.H / 4; e += blockDim.x) build_xB_entry(xs, xB, e);
         __syncthreads();
     } else {
-        norm_prologue(P.h, nullptr, nullptr, nullptr, P.norm_w, P.H, P.eps, xs, xB, red + 128);
+        norm_prologue_fast(nw, P.h, nullptr, nullptr, nullptr, P.H, P.eps, xs, xB, red + 128);
     }
     // router rows of this cluster member: one warp per half row, from smem
     const bool gate_ok = stage_wait(&bar[0]);
@@ -563,58 +635,69 @@ struct MoeDownParams {
     L2Ranges next;
 };
 
+// One cluster of topk CTAs per 16 output rows: CTA t (cluster rank t) stages
+// and multiplies only expert t's w2 tile against mid[t], and sends its 16
+// outputs to rank 0 over DSMEM; rank 0 adds them in rank order.  The four
+// tiles are fetched and multiplied by four SMs at once instead of one after
+// another.  Launch: grid (H/16)*topk, cluster (topk, 1, 1), topk <= 8.
 __host__ __device__ inline size_t moe_down_smem(int I, int topk) {
-    return (size_t)topk * int4_tile_bytes(I) + (size_t)topk * I * 2 + 8 * topk * 16 * 4;
+    return (size_t)int4_tile_bytes(I) + (size_t)I * 2 + (8 * 16 + 8 * 16) * 4;
 }
 
 __global__ void __launch_bounds__(256) k_moe_down(MoeDownParams P) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t bar;
     const uint32_t TB = int4_tile_bytes(P.I);
-    uint8_t* tiles = smem;
-    __half* xB = reinterpret_cast<__half*>(smem + (size_t)P.topk * TB);  // [topk][I]
-    float* red = reinterpret_cast<float*>(xB + (size_t)P.topk * P.I);  // [8][topk][16]
-    const int warp = threadIdx.x >> 5, row0 = blockIdx.x * 16;
+    uint8_t* tile = smem;
+    __half* xB = reinterpret_cast<__half*>(smem + TB);          // [I]
+    float* red = reinterpret_cast<float*>(xB + P.I);            // [8][16]
+    float* slots = red + 8 * 16;                                // [topk][16], used in rank 0
+    cg::cluster_group cluster = cg::this_cluster();
+    const int t = (int)cluster.block_rank();
+    const int row0 = (blockIdx.x / P.topk) * 16;
+    const int warp = threadIdx.x >> 5;
     stage_begin(&bar);
     if (threadIdx.x == 0) l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
     pdl_trigger();
     pdl_wait();
     if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(&bar, (uint32_t)P.topk * TB);
-        for (int t = 0; t < P.topk; t++) {
-            const void* const* ex = P.experts + (size_t)P.route_idx[t] * 6;
-            tma_tile_int4((const uint8_t*)ex[4], (const __half*)ex[5], P.I, row0, tiles + t * TB, &bar);
-        }
+        mbar_arrive_expect_tx(&bar, TB);
+        const void* const* ex = P.experts + (size_t)P.route_idx[t] * 6;
+        tma_tile_int4((const uint8_t*)ex[4], (const __half*)ex[5], P.I, row0, tile, &bar);
     }
-    for (int e = threadIdx.x; e < P.topk * (P.I / 4); e += blockDim.x) {
-        const int t = e / (P.I / 4), r = e % (P.I / 4);
-        build_xB_entry(P.mid + (size_t)t * P.I, xB + (size_t)t * P.I, r);
+    // mid[t] into B-fragment order, 8 consecutive elements per thread
+    const __half* src = P.mid + (size_t)t * P.I;
+    for (int i = threadIdx.x; i < (P.I >> 3); i += blockDim.x) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src + 8 * i);
+        const __half* o = reinterpret_cast<const __half*>(&v);
+        const int G = i >> 4, c = (i >> 2) & 3, j = i & 3;
+        __half2* e0 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j) * 4 + c) * 4);
+        __half2* e1 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j + 1) * 4 + c) * 4);
+        e0[0] = __halves2half2(o[0], o[4]);
+        e0[1] = __halves2half2(o[1], o[5]);
+        e1[0] = __halves2half2(o[2], o[6]);
+        e1[1] = __halves2half2(o[3], o[7]);
     }
     __syncthreads();
-    const int KG = P.I >> 7;
-    const bool ok = stage_wait(&bar);
-    const int lane = threadIdx.x & 31;
-    for (int t = 0; t < P.topk; t++) {
-        float y0 = 0.f, y1 = 0.f;
-        if (ok)
-            int4_tile_dot_smem<2>(tiles + t * TB, P.I, warp, KG, 8,
-                                  reinterpret_cast<const uint2*>(xB + (size_t)t * P.I), y0, y1);
-        if ((lane & 3) == 0) {
-            red[(warp * P.topk + t) * 16 + (lane >> 2)] = y0;
-            red[(warp * P.topk + t) * 16 + (lane >> 2) + 8] = y1;
-        }
-    }
+    float y0 = 0.f, y1 = 0.f;
+    if (stage_wait(&bar))
+        int4_tile_dot_smem<2>(tile, P.I, warp, P.I >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
+    warp_partials(red, warp, y0, y1);
     __syncthreads();
     if (threadIdx.x < 16) {
-        const int i = threadIdx.x, n = row0 + i;
-        __half acc = __float2half_rn(0.f);
-        for (int t = 0; t < P.topk; t++) {
-            float o = 0.f;
+        float o = 0.f;
 #pragma unroll
-            for (int w = 0; w < 8; w++) o += red[(w * P.topk + t) * 16 + i];
-            acc = __float2half_rn(__half2float(acc) + P.route_w[t] * o);
-        }
-        if (n < P.H) P.h[n] = __float2half_rn(__half2float(P.h[n]) + __half2float(acc));
+        for (int w = 0; w < 8; w++) o += red[w * 16 + threadIdx.x];
+        float* dst = cluster.map_shared_rank(slots, 0);
+        dst[t * 16 + threadIdx.x] = o;
+    }
+    cluster.sync();
+    if (t == 0 && threadIdx.x < 16) {
+        const int n = row0 + threadIdx.x;
+        __half acc = __float2half_rn(0.f);
+        for (int k = 0; k < P.topk; k++)
+            acc = __float2half_rn(__half2float(acc) + P.route_w[k] * slots[k * 16 + threadIdx.x]);
+        P.h[n] = __float2half_rn(__half2float(P.h[n]) + __half2float(acc));
     }
 }
 
