@@ -106,6 +106,17 @@ __device__ __forceinline__ void norm_prologue_fast(const NormW& nw, const __half
     __syncthreads();
 }
 
+// A CTA may touch another cluster member's shared memory only once that member
+// has started: every CTA arrives (relaxed) on the cluster barrier at its
+// start, and waits on it right before its first remote access; by then the
+// wait is normally already satisfied.
+__device__ __forceinline__ void cluster_arrive_started() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_started() {
+    asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+}
+
 // Stage begin: mbarrier init by thread 0, made visible to the CTA.
 __device__ __forceinline__ void stage_begin(uint64_t* bar) {
     if (threadIdx.x == 0) mbar_init(bar, 1);
@@ -513,6 +524,7 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     const int rank = (int)cluster.block_rank();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e0 = rank * rpc, ne = max(0, min(P.E - e0, rpc));
+    cluster_arrive_started();
 
     if (threadIdx.x == 0) {
         mbar_init(&bar[0], 1);
@@ -538,7 +550,7 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     }
     // router rows of this cluster member: one warp per half row, from smem
     const bool gate_ok = stage_wait(&bar[0]);
-    float* lgp = lg_all;  // [2*rpc] half-row partials (lg_all is filled later)
+    float* lgp = red;  // [2*rpc] half-row partials
     for (int item = warp; item < 2 * rpc; item += 8) {
         const int j = item >> 1;
         float acc = 0.f;
@@ -562,15 +574,17 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
         if (lane == 0) lgp[item] = acc;
     }
     __syncthreads();
-    for (int j = threadIdx.x; j < rpc; j += blockDim.x) lg_mine[j] = lgp[2 * j] + lgp[2 * j + 1];
-    cluster.sync();
-    for (int e = threadIdx.x; e < P.E; e += blockDim.x) {
-        const float* src = cluster.map_shared_rank(lg_mine, e / rpc);
-        lg_all[e] = src[e % rpc];
+    // scatter this member's logits into every member's lg_all (DSMEM), then
+    // one cluster barrier: every member then holds all E logits
+    cluster_wait_started();
+    for (int i = threadIdx.x; i < rpc * 8; i += blockDim.x) {
+        const int j = i % rpc, r = i / rpc;
+        if (j < ne) cluster.map_shared_rank(lg_all, r)[e0 + j] = lgp[2 * j] + lgp[2 * j + 1];
     }
     cluster.sync();
-    if (warp == 0) route_select_warp(lg_all, P.bias, P.E, P.topk, sidx, sw);
-    __syncthreads();
+    // scratch for the selection: the gate rows' region, consumed by now (the
+    // expert tiles are staged into it only after the selection)
+    route_select_block(lg_all, P.bias, P.E, P.topk, sidx, sw, reinterpret_cast<float*>(gs));
     if (blockIdx.x == 0 && threadIdx.x < P.topk) {
         P.route_idx[threadIdx.x] = sidx[threadIdx.x];
         P.route_w[threadIdx.x] = sw[threadIdx.x];
@@ -580,13 +594,14 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     const bool active = item < P.topk * tiles_per;
     const int t = active ? item / tiles_per : 0, row0 = active ? (item % tiles_per) * 16 : 0;
     const void* const* ex = P.experts + (size_t)sidx[t] * 6;
-    if (threadIdx.x == 0) {
-        if (active) {
-            mbar_arrive_expect_tx(&bar[1], 2 * TB);
-            tma_tile_int4((const uint8_t*)ex[0], (const __half*)ex[1], P.H, row0, tiles, &bar[1]);
-            tma_tile_int4((const uint8_t*)ex[2], (const __half*)ex[3], P.H, row0, tiles + TB, &bar[1]);
-        }
-        // the selected experts' w2 (read by moe_down next) into L2, over the grid
+    if (threadIdx.x == 0 && active) {
+        mbar_arrive_expect_tx(&bar[1], 2 * TB);
+        tma_tile_int4((const uint8_t*)ex[0], (const __half*)ex[1], P.H, row0, tiles, &bar[1]);
+        tma_tile_int4((const uint8_t*)ex[2], (const __half*)ex[3], P.H, row0, tiles + TB, &bar[1]);
+    }
+    // the selected experts' w2 (read by moe_down next) into L2, over the grid
+    auto prefetch_w2 = [&]() {
+        if (threadIdx.x != 0) return;
         L2Ranges R;
         R.count = 0;
         for (int k = 0; k < P.topk && R.count < 7; k++) {
@@ -597,11 +612,13 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
             R.n[R.count++] = (unsigned long long)P.H * (P.I >> 6);
         }
         l2_prefetch_share(R, blockIdx.x, gridDim.x);
-    }
+    };
+    prefetch_w2();
     if (!active) return;
     const int tile = warp & 1;
     float y0 = 0.f, y1 = 0.f;
-    if (stage_wait(&bar[1]))
+    const bool tiles_ok = stage_wait(&bar[1]);
+    if (tiles_ok)
         int4_tile_dot_smem<2>(tiles + tile * TB, P.H, warp >> 1, P.H >> 7, 4,
                               reinterpret_cast<const uint2*>(xB), y0, y1);
     __syncthreads();
@@ -656,6 +673,7 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeDownParams P) {
     const int t = (int)cluster.block_rank();
     const int row0 = (blockIdx.x / P.topk) * 16;
     const int warp = threadIdx.x >> 5;
+    cluster_arrive_started();
     stage_begin(&bar);
     if (threadIdx.x == 0) l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
     pdl_trigger();
@@ -684,6 +702,7 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeDownParams P) {
         int4_tile_dot_smem<2>(tile, P.I, warp, P.I >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
     warp_partials(red, warp, y0, y1);
     __syncthreads();
+    cluster_wait_started();
     if (threadIdx.x < 16) {
         float o = 0.f;
 #pragma unroll

@@ -73,3 +73,70 @@ __device__ __forceinline__ void route_select_warp(const float* logits, const __h
         for (int t = 0; t < topk; t++) w[t] = w[t] / (wsum + 1e-6f);
     __syncwarp();
 }
+
+// Block-wide selection by rank, for E <= blockDim.x (all threads call it):
+// expert e is picked in slot rank(e) = #{e' : s' > s, or s' == s and e' < e}
+// when that rank is below topk, which is the order of the reference's
+// repeated strict-'>' scan.  Scores that are NaN or <= -1e30 rank last (by
+// index), as the scan never picks them before the smallest unused index.
+// Weights are the unbiased sigmoids over (their sum in slot order + 1e-6).
+// scratch: 2*E floats of shared memory.  Ends with a block barrier.
+__device__ __forceinline__ void route_select_block(const float* logits, const __half* bias, int n_exp, int topk,
+                                                   int* idx, float* w, float* scratch) {
+    const int e = threadIdx.x;
+    if (n_exp <= 32) {  // one warp: the keys travel by shuffle, one block barrier
+        if (e < 32) {
+            float sig = 0.f, key = -INFINITY;
+            if (e < n_exp) {
+                sig = route_sigmoid_call(logits[e]);
+                const float score = sig + __half2float(bias[e]);
+                key = (score > -1e30f) ? score : -INFINITY;
+            }
+            int rank = 0;
+            for (int o = 0; o < n_exp; o++) {
+                const float ko = __shfl_sync(0xffffffffu, key, o);
+                rank += (ko > key || (ko == key && o < e)) ? 1 : 0;
+            }
+            if (e < n_exp && rank < topk) {
+                idx[rank] = e;
+                scratch[rank] = sig;
+            }
+            __syncwarp();
+            if (e == 0) {
+                float wsum = 0.f;
+                for (int t = 0; t < topk; t++) wsum += scratch[t];
+                for (int t = 0; t < topk; t++) w[t] = scratch[t] / (wsum + 1e-6f);
+            }
+        }
+        __syncthreads();
+        return;
+    }
+    float* sc = scratch;
+    float* sg = scratch + n_exp;
+    float sig = 0.f, key = -INFINITY;
+    if (e < n_exp) {
+        sig = route_sigmoid_call(logits[e]);
+        const float score = sig + __half2float(bias[e]);
+        key = (score > -1e30f) ? score : -INFINITY;  // NaN compares false
+        sc[e] = key;
+    }
+    __syncthreads();
+    if (e < n_exp) {
+        int rank = 0;
+        for (int o = 0; o < n_exp; o++) {
+            const float ko = sc[o];
+            rank += (ko > key || (ko == key && o < e)) ? 1 : 0;
+        }
+        if (rank < topk) {
+            idx[rank] = e;
+            sg[rank] = sig;
+        }
+    }
+    __syncthreads();
+    if (e == 0) {
+        float wsum = 0.f;
+        for (int t = 0; t < topk; t++) wsum += sg[t];
+        for (int t = 0; t < topk; t++) w[t] = sg[t] / (wsum + 1e-6f);
+    }
+    __syncthreads();
+}
