@@ -38,7 +38,8 @@ struct AttnParams {
 };
 
 #define ATTN_PART_STRIDE 68
-#define ATTN_THREADS 128
+#define ATTN_THREADS 256  // 8 warps
+#define ATTN_PARTS 2      // each warp takes half a 64-token unit
 #define ATTN_NEG (-1.0e30f)
 #define ATTN_MAX_PARTS 1024
 
@@ -57,13 +58,16 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 }
 
 // One warp: online-softmax attention of its query heads (A-fragment rows,
-// aq) over units u_begin, u_begin+u_step, ... < u_end of kv head h.  Keeps
-// the running max m_run (base 2, per row), the per-lane partial sum l_run and
-// the output accumulators O (n-tile j holds dims 16c+j and 16c+8+j of row g).
+// aq) over unit parts pi = p_begin, p_begin+p_step, ... < p_end of kv head h,
+// where part pi is keys [64/PARTS * (pi % PARTS), +64/PARTS) of the 64-token
+// unit pi / PARTS.  Keeps the running max m_run (base 2, per row), the
+// per-lane partial sum l_run and the output accumulators O (n-tile j holds
+// dims 16c+j and 16c+8+j of row g).  An FP8 part's K and V are all requested
+// before any math, so a part costs one memory round trip.
 // CG: read the cache with ld.global.cg (coherent at L2) because the caller's
 // own launch may have written it (the persistent kernel); otherwise the
 // cache is read through the non-coherent streaming path.
-template <bool CG>
+template <bool CG, int PARTS>
 __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
                                                 const uint8_t* __restrict__ vc8,
                                                 const __half* __restrict__ ksc,
@@ -71,42 +75,42 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
                                                 const __half* __restrict__ ktail,
                                                 const __half* __restrict__ vtail, int nkv, int h,
                                                 int n_fp8, int tail_len, float kfac,
-                                                const uint32_t (&aq)[4][2], int u_begin, int u_end,
-                                                int u_step, float& m_run, float& l_run,
+                                                const uint32_t (&aq)[4][2], int p_begin, int p_end,
+                                                int p_step, float& m_run, float& l_run,
                                                 float (&O)[8][4]) {
+    constexpr int NJ = 8 / PARTS;  // 8-key n-tiles per part (QK)
+    constexpr int NS = 4 / PARTS;  // 16-key k-steps per part (PV)
     const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-    for (int u = u_begin; u < u_end; u += u_step) {
+    const size_t kstride = (size_t)nkv * CUINF_HD;
+    for (int pi = p_begin; pi < p_end; pi += p_step) {
+        const int u = pi / PARTS, k0 = (pi % PARTS) * (64 / PARTS);
         const bool tail = u >= n_fp8;
         const int valid = tail ? tail_len : CUINF_KVGROUP;
         const int kbase = u * CUINF_KVGROUP;
-        // An FP8 unit's K (8 x 16 B per lane) and V (16 x 8 B per lane) are
-        // all requested before any math, so the unit costs one memory round
-        // trip instead of one per 8-key block.
-        uint4 kraw[8];
-        uint2 vraw[4][4];
+        uint4 kraw[NJ];
+        uint2 vraw[NS][4];
+        const int off[4] = {0, 1, 8, 9};
         if (!tail) {
-            const size_t kstride = (size_t)nkv * CUINF_HD;
 #pragma unroll
-            for (int jn = 0; jn < 8; jn++) {
-                const uint8_t* kp8 = kc8 + ((size_t)(kbase + 8 * jn + g) * nkv + h) * CUINF_HD + 16 * c;
+            for (int jn = 0; jn < NJ; jn++) {
+                const uint8_t* kp8 = kc8 + ((size_t)(kbase + k0 + 8 * jn + g) * nkv + h) * CUINF_HD + 16 * c;
                 kraw[jn] = CG ? __ldcg(reinterpret_cast<const uint4*>(kp8)) : ldg_stream(kp8);
             }
 #pragma unroll
-            for (int s2 = 0; s2 < 4; s2++) {
-                const uint8_t* vp = vc8 + ((size_t)(kbase + 16 * s2 + 2 * c) * nkv + h) * CUINF_HD + 8 * g;
-                const int off[4] = {0, 1, 8, 9};
+            for (int s2 = 0; s2 < NS; s2++) {
+                const uint8_t* vp = vc8 + ((size_t)(kbase + k0 + 16 * s2 + 2 * c) * nkv + h) * CUINF_HD + 8 * g;
 #pragma unroll
                 for (int i = 0; i < 4; i++)
                     vraw[s2][i] = CG ? __ldcg(reinterpret_cast<const uint2*>(vp + off[i] * kstride))
                                      : ldg_stream8(vp + off[i] * kstride);
             }
         }
-        // ---- S = Q K^T for 64 keys (8 n-tiles of 8 keys) ----
-        float S[8][4];
+        // ---- S = Q K^T for the part's keys (NJ n-tiles of 8 keys) ----
+        float S[NJ][4];
 #pragma unroll
-        for (int jn = 0; jn < 8; jn++) {
+        for (int jn = 0; jn < NJ; jn++) {
             S[jn][0] = S[jn][1] = S[jn][2] = S[jn][3] = 0.f;
-            const int kk = 8 * jn + g;  // key within the unit
+            const int kk = k0 + 8 * jn + g;  // key within the unit
             uint32_t kb[8];
             if (!tail) {
                 const uint4 raw = kraw[jn];
@@ -131,14 +135,14 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
         const float f = kscale * kfac;
         float mx = ATTN_NEG;
 #pragma unroll
-        for (int jn = 0; jn < 8; jn++) {
+        for (int jn = 0; jn < NJ; jn++) {
 #pragma unroll
             for (int i = 0; i < 2; i++) {
-                const int key = 8 * jn + 2 * c + i;
-                float s = S[jn][i] * f;
-                s = key < valid ? s : ATTN_NEG;
-                S[jn][i] = s;
-                mx = fmaxf(mx, s);
+                const int key = k0 + 8 * jn + 2 * c + i;
+                float sv = S[jn][i] * f;
+                sv = key < valid ? sv : ATTN_NEG;
+                S[jn][i] = sv;
+                mx = fmaxf(mx, sv);
             }
         }
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -147,26 +151,26 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
         const float alpha = exp2f(m_run - m_new);
         float lsum = 0.f;
 #pragma unroll
-        for (int jn = 0; jn < 8; jn++) {
+        for (int jn = 0; jn < NJ; jn++) {
 #pragma unroll
             for (int i = 0; i < 2; i++) {
-                const int key = 8 * jn + 2 * c + i;
-                float p = key < valid ? exp2f(S[jn][i] - m_new) : 0.f;
-                S[jn][i] = p;
-                lsum += p;
+                const int key = k0 + 8 * jn + 2 * c + i;
+                float pv = key < valid ? exp2f(S[jn][i] - m_new) : 0.f;
+                S[jn][i] = pv;
+                lsum += pv;
             }
         }
         l_run = l_run * alpha + lsum;
         m_run = m_new;
-        // ---- tmp = P V (4 k-steps of 16 keys, 8 n-tiles of 8 dims) ----
+        // ---- tmp = P V (NS k-steps of 16 keys, 8 n-tiles of 8 dims) ----
         float T[8][4];
 #pragma unroll
         for (int j = 0; j < 8; j++) T[j][0] = T[j][1] = T[j][2] = T[j][3] = 0.f;
 #pragma unroll
-        for (int s2 = 0; s2 < 4; s2++) {
+        for (int s2 = 0; s2 < NS; s2++) {
             const uint32_t pa0 = pack_h2(S[2 * s2][0], S[2 * s2][1]);
             const uint32_t pa2 = pack_h2(S[2 * s2 + 1][0], S[2 * s2 + 1][1]);
-            const int ka = 16 * s2 + 2 * c;  // keys ka, ka+1, ka+8, ka+9
+            const int ka = k0 + 16 * s2 + 2 * c;  // keys ka, ka+1, ka+8, ka+9
             uint32_t b0[8], b1[8];
             if (!tail) {
                 const uint2 va = vraw[s2][0], vb = vraw[s2][1], vc = vraw[s2][2], vd = vraw[s2][3];
@@ -181,7 +185,6 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
                 r = prmt(vc.y, vd.y, 0x7362u); b1[6] = fp8x2_to_h2(r); b1[7] = fp8x2_to_h2(r >> 16);
             } else {
                 const __half* vp = vtail + ((size_t)ka * nkv + h) * CUINF_HD + 8 * g;
-                const size_t kstride = (size_t)nkv * CUINF_HD;
                 const uint4 z = make_uint4(0u, 0u, 0u, 0u);
                 // keys beyond the tail hold stale data: zero them
                 auto ld16 = [](const __half* q) {
@@ -214,7 +217,7 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
 }
 
 __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
-    __shared__ __align__(16) float sm[4][16][ATTN_PART_STRIDE];
+    __shared__ __align__(16) float sm[ATTN_THREADS / 32][16][ATTN_PART_STRIDE];
     __shared__ int s_last;
     const int h = blockIdx.x, sp = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
@@ -255,8 +258,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
 #pragma unroll
     for (int j = 0; j < 8; j++) O[j][0] = O[j][1] = O[j][2] = O[j][3] = 0.f;
 
-    attn_warp_units<false>(P.kc8, P.vc8, P.ksc, P.vsc, P.ktail, P.vtail, nkv, h, n_fp8, tail_len, kfac, aq,
-                    u0 + warp, u1, 4, m_run, l_run, O);
+    attn_warp_units<false, ATTN_PARTS>(P.kc8, P.vc8, P.ksc, P.vsc, P.ktail, P.vtail, nkv, h, n_fp8, tail_len,
+                                       kfac, aq, u0 * ATTN_PARTS + warp, u1 * ATTN_PARTS, ATTN_THREADS / 32,
+                                       m_run, l_run, O);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
 
@@ -276,10 +280,10 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
         const int r = it >> 6, d = it & 63;
         float mm = ATTN_NEG;
 #pragma unroll
-        for (int w = 0; w < 4; w++) mm = fmaxf(mm, sm[w][r][0]);
+        for (int w = 0; w < ATTN_THREADS / 32; w++) mm = fmaxf(mm, sm[w][r][0]);
         float l = 0.f, o = 0.f;
 #pragma unroll
-        for (int w = 0; w < 4; w++) {
+        for (int w = 0; w < ATTN_THREADS / 32; w++) {
             const float e = exp2f(sm[w][r][0] - mm);
             l += sm[w][r][1] * e;
             o += sm[w][r][4 + d] * e;
@@ -327,21 +331,28 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     for (int it = threadIdx.x; it < gqa * 64; it += blockDim.x) {
         const int r = it >> 6, d = it & 63;
         float o = 0.f;
-        for (int sp2 = 0; sp2 < P.nsplit; sp2++) {
-            const int i = sp2 * gqa + r;
-            o += s_m[i] * __ldcg(hp + (size_t)i * ATTN_PART_STRIDE + 4 + d);
+        // eight splits' values requested at a time, then summed in split order
+        for (int sp0 = 0; sp0 < P.nsplit; sp0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                v[k] = sp0 + k < P.nsplit ? __ldcg(hp + (size_t)((sp0 + k) * gqa + r) * ATTN_PART_STRIDE + 4 + d) : 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (sp0 + k < P.nsplit) o += s_m[(sp0 + k) * gqa + r] * v[k];
         }
         P.out[(size_t)(h * gqa + r) * CUINF_HD + d] = __float2half_rn(o / s_g[8 + r]);
     }
     if (threadIdx.x == 0) P.counters[h] = 0u;
 }
 
-// Splits for the decode engine: one 64-token unit per warp at the session's
-// longest context (ATTN_THREADS/32 units per CTA), so every warp of every CTA
-// has a unit and the combine merges as few partials as that allows; at most
-// ATTN_MAX_PARTS (split, query head) partials per kv head.
+// Splits for the decode engine: one unit part per warp at the session's
+// longest context (ATTN_THREADS/32/ATTN_PARTS units per CTA), so every warp of
+// every CTA has work and the combine merges as few partials as that allows;
+// at most ATTN_MAX_PARTS (split, query head) partials per kv head.
 static inline int attn_engine_nsplit(int gqa, int max_units) {
-    int ns = (max_units + ATTN_THREADS / 32 - 1) / (ATTN_THREADS / 32);
+    const int upc = ATTN_THREADS / 32 / ATTN_PARTS;
+    int ns = (max_units + upc - 1) / upc;
     if (ns * gqa > ATTN_MAX_PARTS) ns = ATTN_MAX_PARTS / gqa;
     return ns < 1 ? 1 : ns;
 }

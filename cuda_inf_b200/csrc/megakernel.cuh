@@ -798,7 +798,7 @@ __device__ __noinline__ void mk_attn_item(const MkParams& P, const MkLayer& L, i
     float m_run = ATTN_NEG, l_run = 0.f, O[8][4];
 #pragma unroll
     for (int t = 0; t < 8; t++) O[t][0] = O[t][1] = O[t][2] = O[t][3] = 0.f;
-    attn_warp_units<true>(L.kc8, L.vc8, L.ksc, L.vsc, L.ktail, L.vtail, nkv, h, n_fp8, tail_len, kfac, aq,
+    attn_warp_units<true, 1>(L.kc8, L.vc8, L.ksc, L.vsc, L.ktail, L.vtail, nkv, h, n_fp8, tail_len, kfac, aq,
                     u0 + warp, u1, MK_CW, m_run, l_run, O);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
