@@ -35,6 +35,13 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
                  : "l"(p));
     return r;
 }
+__device__ __forceinline__ uint4 ldg_stream256(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
 __device__ __forceinline__ uint2 ldg_stream8(const void* p) {
     uint2 r;
     asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n"
@@ -142,6 +149,14 @@ __device__ __forceinline__ uint32_t tma_tile_int4(const uint8_t* packed, const _
     tma_load_1d_hint(dst, packed + (size_t)row0 * (K >> 1), pb, bar, pol);
     tma_load_1d_hint(dst + pb, (const uint8_t*)scales + (size_t)row0 * (K >> 6), sb, bar, pol);
     return pb + sb;
+}
+
+// Shared-memory pitch for rows of H fp16 values: 64 mod 128 bytes, so the
+// 16-byte loads of two neighbouring rows by one 8-lane phase of a warp fall
+// in different banks (rows H*2 = 4096 bytes apart would all hit the same).
+__host__ __device__ __forceinline__ unsigned f16_row_pitch(int H) {
+    const unsigned b = 2u * (unsigned)H;
+    return b + ((64u - (b & 127u)) & 127u);
 }
 
 // Up to 8 byte ranges (16-byte aligned starts and sizes) to pull into L2.
@@ -403,8 +418,8 @@ __device__ __forceinline__ void f16_tile_dot(const __half* __restrict__ W, int N
         for (int u = 0; u < UNROLL; u++) {
             int i = i0 + u * istep;
             if (i < iend) {
-                wa[u] = ldg_stream(pa + (size_t)i * 32);
-                wb[u] = ldg_stream(pb + (size_t)i * 32);
+                wa[u] = ldg_stream256(pa + (size_t)i * 32);
+                wb[u] = ldg_stream256(pb + (size_t)i * 32);
             }
         }
 #pragma unroll

@@ -1049,6 +1049,7 @@ static int build_graph(cuinf_session* s) {
 
 static int set_kernel_attrs(const cuinf_config& c) {
     const int H = c.hidden;
+
     struct { const void* k; size_t bytes; } need[] = {
         {(const void*)k_attn_qkv, qkv_smem(H)},
         {(const void*)k_conv_in, conv_smem(H)},

@@ -94,13 +94,15 @@ __device__ __forceinline__ void norm_prologue_fast(const NormW& nw, const __half
 #pragma unroll
             for (int q = 0; q < 8; q++) o[q] = __float2half_rn(__half2float(xh[q]) * inv * __half2float(wh[q]));
             *reinterpret_cast<uint4*>(xs + 8 * i) = *reinterpret_cast<const uint4*>(o);
-            const int G = i >> 4, c = (i >> 2) & 3, j = i & 3;
-            __half2* e0 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j) * 4 + c) * 4);
-            __half2* e1 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j + 1) * 4 + c) * 4);
-            e0[0] = __halves2half2(o[0], o[4]);
-            e0[1] = __halves2half2(o[1], o[5]);
-            e1[0] = __halves2half2(o[2], o[6]);
-            e1[1] = __halves2half2(o[3], o[7]);
+            if (xB) {
+                const int G = i >> 4, c = (i >> 2) & 3, j = i & 3;
+                __half2* e0 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j) * 4 + c) * 4);
+                __half2* e1 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j + 1) * 4 + c) * 4);
+                e0[0] = __halves2half2(o[0], o[4]);
+                e0[1] = __halves2half2(o[1], o[5]);
+                e1[0] = __halves2half2(o[2], o[6]);
+                e1[1] = __halves2half2(o[3], o[7]);
+            }
         }
     }
     __syncthreads();
@@ -723,8 +725,9 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeDownParams P) {
 // ---------------------------------------------------------------------------
 // Final norm + tied lm_head (fp16 [V,H]) + argmax + next-token bookkeeping
 // (engine.cu:932-940).  One 16-row tile per warp, all tiles resident in one
-// wave, weights streamed with 16-byte loads (their first rows pulled into L2
-// before the dependency wait).  Argmax: 64-bit keys (argmax_key) reduced per
+// wave, weights streamed with 16-byte loads that ask L2 for 256-byte blocks
+// (each row is read front to back, so the rest of the block is used by the
+// same warp's next loads).  Argmax: 64-bit keys (argmax_key) reduced per
 // CTA, then atomicMax; the last CTA (atomic ticket) publishes the token,
 // advances pos and resets.
 // ---------------------------------------------------------------------------
@@ -755,7 +758,6 @@ __global__ void __launch_bounds__(256) k_lmhead(LmHeadParams P) {
     const int ntiles = (P.V + 15) / 16;
     const int tile0 = blockIdx.x * 8 + warp;
     if (threadIdx.x == 0) l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
-    if (tile0 < ntiles && lane == 0) l2_prefetch_bulk_rows(P.W, P.V, P.H, tile0 * 16, 16);
     pdl_trigger();
     pdl_wait();
     for (int i = threadIdx.x; i < P.H; i += blockDim.x) xs[i] = P.h[i];

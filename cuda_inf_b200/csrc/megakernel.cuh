@@ -208,10 +208,7 @@ __device__ __forceinline__ void mk_add_piece(MkPieces& pc, const void* src, unsi
 // fp16 rows of H halves staged with a row pitch of mk_f16_pitch(H) bytes:
 // 64 mod 128, so the 16-byte loads of two neighbouring rows by one 8-lane
 // phase of a warp fall in different shared-memory banks.
-__host__ __device__ __forceinline__ unsigned mk_f16_pitch(int H) {
-    const unsigned b = 2u * (unsigned)H;
-    return b + ((64u - (b & 127u)) & 127u);
-}
+__host__ __device__ __forceinline__ unsigned mk_f16_pitch(int H) { return f16_row_pitch(H); }
 __device__ __forceinline__ void mk_add_f16_rows(MkPieces& pc, const __half* src, int rows, int H,
                                                 int slab_rows) {
     const unsigned pitch = mk_f16_pitch(H);
