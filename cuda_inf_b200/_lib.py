@@ -81,6 +81,7 @@ _SIGS = {
                                ctypes.POINTER(c_int)]),
     "cuinf_session_keep_logits": (c_int, [c_void_p, c_int]),
     "cuinf_session_set_option": (c_int, [c_void_p, c_int, c_int]),
+    "cuinf_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "cuinf_device_error": (c_int, [ctypes.POINTER(ctypes.c_uint)]),
     "cuinf_session_uses_megakernel": (c_int, [c_void_p]),
     "cuinf_session_trace": (c_int, [c_void_p, c_void_p, c_int, c_void_p, ctypes.POINTER(c_int),

@@ -346,6 +346,53 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     if (threadIdx.x == 0) P.counters[h] = 0u;
 }
 
+// Prefill attention (attention_fused, engine.cu:236-308): query token i of
+// S (position past + i) attends to keys [0, past + i]; keys below
+// `committed` (the count after all S tokens were placed) come from the FP8
+// cache with their group scale, the rest from the fp16 tail at index
+// t - committed.  One warp per (token, query head); lane d holds dims 2d and
+// 2d+1; online softmax in fp32.  q/out fp16 [S][nh][64].
+__global__ void __launch_bounds__(32) k_attn_prefill(const __half* __restrict__ q, const uint8_t* __restrict__ kc8,
+                                                     const uint8_t* __restrict__ vc8,
+                                                     const __half* __restrict__ ksc,
+                                                     const __half* __restrict__ vsc,
+                                                     const __half* __restrict__ ktail,
+                                                     const __half* __restrict__ vtail, int committed,
+                                                     int past, float scale, __half* __restrict__ out, int nh,
+                                                     int nkv) {
+    const int i = blockIdx.x, hq = blockIdx.y, d = threadIdx.x;
+    const int kvh = hq / (nh / nkv), qpos = past + i;
+    const __half2 qv = reinterpret_cast<const __half2*>(q + ((size_t)i * nh + hq) * CUINF_HD)[d];
+    const float q0 = __low2float(qv), q1 = __high2float(qv);
+    const int cend = committed < qpos + 1 ? committed : qpos + 1;
+    float m = -1e30f, l = 0.f, o0 = 0.f, o1 = 0.f;
+    for (int t = 0; t <= qpos; t++) {
+        float k0, k1, v0, v1;
+        if (t < cend) {
+            const float ks = __half2float(ksc[(t / CUINF_KVGROUP) * nkv + kvh]);
+            const float vs = __half2float(vsc[(t / CUINF_KVGROUP) * nkv + kvh]);
+            const uint32_t kb = fp8x2_to_h2(reinterpret_cast<const uint16_t*>(kc8 + ((size_t)t * nkv + kvh) * CUINF_HD)[d]);
+            const uint32_t vb = fp8x2_to_h2(reinterpret_cast<const uint16_t*>(vc8 + ((size_t)t * nkv + kvh) * CUINF_HD)[d]);
+            const __half2 kh = *reinterpret_cast<const __half2*>(&kb), vh = *reinterpret_cast<const __half2*>(&vb);
+            k0 = __low2float(kh) * ks; k1 = __high2float(kh) * ks;
+            v0 = __low2float(vh) * vs; v1 = __high2float(vh) * vs;
+        } else {
+            const size_t row = ((size_t)(t - committed) * nkv + kvh) * CUINF_HD;
+            const __half2 kh = reinterpret_cast<const __half2*>(ktail + row)[d];
+            const __half2 vh = reinterpret_cast<const __half2*>(vtail + row)[d];
+            k0 = __low2float(kh); k1 = __high2float(kh);
+            v0 = __low2float(vh); v1 = __high2float(vh);
+        }
+        const float sc = warp_sum(q0 * k0 + q1 * k1) * scale;
+        const float mn = fmaxf(m, sc), cf = __expf(m - mn), p = __expf(sc - mn);
+        l = l * cf + p;
+        o0 = o0 * cf + p * v0;
+        o1 = o1 * cf + p * v1;
+        m = mn;
+    }
+    reinterpret_cast<__half2*>(out + ((size_t)i * nh + hq) * CUINF_HD)[d] = __floats2half2_rn(o0 / l, o1 / l);
+}
+
 // Splits for the decode engine: one unit part per warp at the session's
 // longest context (ATTN_THREADS/32/ATTN_PARTS units per CTA), so every warp of
 // every CTA has work and the combine merges as few partials as that allows;

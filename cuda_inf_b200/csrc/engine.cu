@@ -248,6 +248,53 @@ static cudaError_t launch_kc(Kern kernel, dim3 grid, dim3 block, size_t smem, cu
 
 static int set_kernel_attrs(const cuinf_config& c);
 
+// k_moe_up + k_moe_down for one token: xn already normalized, h += the
+// rank-ordered expert mix; mid [topk*I] fp16 and the routes are scratch.
+static int moe_ffn_launch(const __half* xn, const __half* gate, const __half* bias, const void* const* experts,
+                          __half* h, int H, int I, int n_exp, int topk, __half* mid, int* ridx, float* rw,
+                          cudaStream_t st) {
+    MoeUpParams U;
+    U.h = nullptr;
+    U.xn = xn;
+    U.norm_w = nullptr;
+    U.gate = gate;
+    U.bias = bias;
+    U.experts = experts;
+    U.mid = mid;
+    U.route_idx = ridx;
+    U.route_w = rw;
+    U.H = H;
+    U.I = I;
+    U.E = n_exp;
+    U.topk = topk;
+    U.eps = 0.f;
+    U.next.count = 0;
+    const size_t su = moe_up_smem(H, n_exp);
+    REQUIRE(su <= 227 * 1024 && moe_down_smem(I, topk) <= 227 * 1024, "H/I too large for shared memory");
+    if (su > 48 * 1024)
+        CUINF_TRY(cudaFuncSetAttribute(k_moe_up, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)su));
+    const int tiles = I / 16;
+    const int grid_up = ((topk * tiles + 7) / 8) * 8;
+    k_moe_up<<<grid_up, 256, su, st>>>(U);
+    int rc = cuinf_launch_status();
+    if (rc) return rc;
+    MoeDownParams D;
+    D.mid = mid;
+    D.experts = experts;
+    D.route_idx = ridx;
+    D.route_w = rw;
+    D.h = h;
+    D.H = H;
+    D.I = I;
+    D.topk = topk;
+    D.next.count = 0;
+    const size_t sd = moe_down_smem(I, topk);
+    if (sd > 48 * 1024)
+        CUINF_TRY(cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sd));
+    CUINF_TRY(launch_kc(k_moe_down, dim3((H / 16) * topk), dim3(256), sd, st, false, topk, D));
+    return cuinf_launch_status();
+}
+
 extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* expert_bias,
                              const void* const* experts, void* h, int H, int I, int n_exp, int topk,
                              int* idx, float* w, void* workspace, size_t workspace_bytes,
@@ -268,51 +315,13 @@ extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* exper
     __half* mid = (__half*)ws;
     int* ridx = idx ? idx : (int*)((char*)ws + (size_t)topk * I * 2);
     float* rw = w ? w : (float*)((char*)ws + (size_t)topk * I * 2 + 128);
-    MoeUpParams U;
-    U.h = nullptr;
-    U.xn = (const __half*)xn;
-    U.norm_w = nullptr;
-    U.gate = (const __half*)gate;
-    U.bias = (const __half*)expert_bias;
-    U.experts = experts;
-    U.mid = mid;
-    U.route_idx = ridx;
-    U.route_w = rw;
-    U.H = H;
-    U.I = I;
-    U.E = n_exp;
-    U.topk = topk;
-    U.eps = 0.f;
-    U.next.count = 0;
     {   // TMA sources must be 16-byte aligned
         std::vector<uintptr_t> tab((size_t)n_exp * 6);
         CUINF_TRY(cudaMemcpy(tab.data(), experts, tab.size() * sizeof(uintptr_t), cudaMemcpyDeviceToHost));
         for (uintptr_t a : tab) REQUIRE(a && (a & 15) == 0, "expert tensors must be 16-byte aligned");
     }
-    const size_t su = moe_up_smem(H, n_exp);
-    REQUIRE(su <= 227 * 1024 && moe_down_smem(I, topk) <= 227 * 1024, "H/I too large for shared memory");
-    if (su > 48 * 1024)
-        CUINF_TRY(cudaFuncSetAttribute(k_moe_up, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)su));
-    const int tiles = I / 16;
-    const int grid_up = ((topk * tiles + 7) / 8) * 8;
-    k_moe_up<<<grid_up, 256, su, ST(stream)>>>(U);
-    int rc = cuinf_launch_status();
-    if (rc) return rc;
-    MoeDownParams D;
-    D.mid = mid;
-    D.experts = experts;
-    D.route_idx = ridx;
-    D.route_w = rw;
-    D.h = (__half*)h;
-    D.H = H;
-    D.I = I;
-    D.topk = topk;
-    D.next.count = 0;
-    const size_t sd = moe_down_smem(I, topk);
-    if (sd > 48 * 1024)
-        CUINF_TRY(cudaFuncSetAttribute(k_moe_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sd));
-    CUINF_TRY(launch_kc(k_moe_down, dim3((H / 16) * topk), dim3(256), sd, ST(stream), false, topk, D));
-    return cuinf_launch_status();
+    return moe_ffn_launch((const __half*)xn, (const __half*)gate, (const __half*)expert_bias, experts,
+                          (__half*)h, H, I, n_exp, topk, mid, ridx, rw, ST(stream));
 }
 
 // ---------------------------------------------------------------------------
@@ -620,6 +629,7 @@ struct cuinf_session {
     int num_sms = 148;
     bool prefetch = true;  // L2 prefetch plans (cross-kernel weight streaming)
     bool pdl = true;       // programmatic dependent launch between the step's kernels
+    bool prefill = true;   // cuinf_generate prefills its prompt
     // persistent megakernel (one cooperative launch per step)
     bool mk_ok = false, use_mk = false;  // the multi-kernel graph is the default
     MkParams mk;
@@ -629,6 +639,9 @@ struct cuinf_session {
     unsigned long long* mk_trace = nullptr;  // per-stage timestamps when tracing is on
     bool trace = false;
     std::vector<int> mk_kinds;  // stage kinds, for trace reports
+    // prefill scratch, grown to the longest prompt seen (freed with the session)
+    int pf_cap = 0;
+    void* pf_buf = nullptr;
 };
 
 template <class T>
@@ -1070,6 +1083,7 @@ static int set_kernel_attrs(const cuinf_config& c) {
 extern "C" int cuinf_session_free(cuinf_session* s) {
     if (!s) return CUINF_OK;
     if (s->st) cudaStreamSynchronize(s->st);
+    if (s->pf_buf) cudaFree(s->pf_buf);
     if (s->exec) cudaGraphExecDestroy(s->exec);
     if (s->graph) cudaGraphDestroy(s->graph);
     for (void* p : s->allocs) cudaFree(p);
@@ -1195,14 +1209,164 @@ extern "C" int cuinf_decode_step(cuinf_session* s, int token, int* out_token) {
     return CUINF_OK;
 }
 
+// ---------------------------------------------------------------------------
+// prefill: the reference's batched layer_forward(S) (engine.cu:784-908, 910-917) for
+// the S prompt tokens at positions pos..pos+S-1, then compute_logits_last
+// (932-940).  Per attention layer all S tokens' K/V are placed first (tail up
+// to each group boundary, full groups committed, 831-845) and then every
+// query attends over what is committed (attention_fused, 236-308) -- which is
+// why a prompt prefilled here differs from the same prompt decoded token by
+// token.  Kernel by kernel on the session stream (not captured); afterwards
+// the session continues with decode steps from position pos + S.
+// ---------------------------------------------------------------------------
+extern "C" int cuinf_prefill(cuinf_session* s, const int* ids, int S, int* out_token, int* routes_out) {
+    REQUIRE(s && ids && S > 0, "bad arguments");
+    const cuinf_model* m = s->m;
+    const cuinf_config& c = m->cfg;
+    REQUIRE(s->host_pos + S <= s->max_ctx, "context too long for max_ctx");
+    for (int i = 0; i < S; i++) REQUIRE(ids[i] >= 0 && ids[i] < c.vocab, "token out of range");
+    const int H = c.hidden, nh = c.n_heads, nkv = c.n_kv_heads, hd = 64, E = c.n_experts, K = c.top_k;
+    const int NQ = nh * hd, NK = nkv * hd;
+    const int maxN = std::max(std::max(3 * H, NQ), std::max(c.dense_inter, c.moe_inter));
+    const int n_moe = c.n_layers - c.n_dense;
+    cudaStream_t st = s->st;
+    // scratch: ids, pos, hs, xn, q, k, v, ao, t16, t16b, acc (fp16), fa, fb (fp32), mid, routes
+    auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t b_int = al((size_t)S * 4), b_h = al((size_t)S * H * 2), b_q = al((size_t)S * NQ * 2),
+                 b_k = al((size_t)S * NK * 2), b_t = al((size_t)S * maxN * 2), b_f = al((size_t)S * maxN * 4),
+                 b_mid = al((size_t)K * c.moe_inter * 2), b_r = al((size_t)S * std::max(1, n_moe) * K * 4);
+    const size_t total = 2 * b_int + 3 * b_h + 2 * b_q + 2 * b_k + 2 * b_t + 2 * b_f + b_mid + 2 * b_r + al(4 * c.vocab);
+    if (S > s->pf_cap) {
+        if (s->pf_buf) {
+            CUINF_TRY(cudaStreamSynchronize(st));
+            CUINF_TRY(cudaFree(s->pf_buf));
+            s->pf_buf = nullptr;
+        }
+        CUINF_TRY(cudaMalloc(&s->pf_buf, total));
+        s->pf_cap = S;
+    }
+    char* b = (char*)s->pf_buf;
+    auto take = [&](size_t n) { char* p = b; b += n; return p; };
+    int* d_ids = (int*)take(b_int);
+    int* d_pos = (int*)take(b_int);
+    __half* hs = (__half*)take(b_h);
+    __half* xn = (__half*)take(b_h);
+    __half* acc = (__half*)take(b_h);
+    __half* q16 = (__half*)take(b_q);
+    __half* ao = (__half*)take(b_q);
+    __half* k16 = (__half*)take(b_k);
+    __half* v16 = (__half*)take(b_k);
+    __half* t16 = (__half*)take(b_t);
+    __half* t16b = (__half*)take(b_t);
+    float* fa = (float*)take(b_f);
+    float* fb = (float*)take(b_f);
+    __half* mid = (__half*)take(b_mid);
+    int* ridx = (int*)take(b_r);
+    float* rw = (float*)take(b_r);
+    float* logits = (float*)take(al(4 * c.vocab));
+    const int past = s->host_pos;
+    std::vector<int> hpos(S);
+    for (int i = 0; i < S; i++) hpos[i] = past + i;
+    CUINF_TRY(cudaMemcpyAsync(d_ids, ids, (size_t)S * 4, cudaMemcpyHostToDevice, st));
+    CUINF_TRY(cudaMemcpyAsync(d_pos, hpos.data(), (size_t)S * 4, cudaMemcpyHostToDevice, st));
+    int rc;
+#define PF(call) do { if ((rc = (call)) != CUINF_OK) return rc; } while (0)
+    void* vs = (void*)st;
+    PF(cuinf_embed_gather(m->embed, d_ids, hs, S, H, vs));
+    for (int l = 0; l < c.n_layers; l++) {
+        const LayerW& L = m->L[l];
+        PF(cuinf_rmsnorm(hs, L.op_norm, xn, S, H, c.norm_eps, vs));
+        if (c.attn_layer[l]) {
+            AttnState& A = s->attn[l];
+            PF(cuinf_gemv_int4(xn, L.wq.p, L.wq.s, fa, S, NQ, H, vs));
+            PF(cuinf_f32_to_f16(fa, q16, S * NQ, vs));
+            PF(cuinf_gemv_int4(xn, L.wk.p, L.wk.s, fa, S, NK, H, vs));
+            PF(cuinf_f32_to_f16(fa, k16, S * NK, vs));
+            PF(cuinf_gemv_int4(xn, L.wv.p, L.wv.s, fa, S, NK, H, vs));
+            PF(cuinf_f32_to_f16(fa, v16, S * NK, vs));
+            PF(cuinf_rmsnorm(q16, L.q_ln, q16, S * nh, hd, c.norm_eps, vs));
+            PF(cuinf_rmsnorm(k16, L.k_ln, k16, S * nkv, hd, c.norm_eps, vs));
+            PF(cuinf_rope(q16, k16, d_pos, S, nh, nkv, c.rope_theta, vs));
+            int committed = (past / CUINF_KVGROUP) * CUINF_KVGROUP;
+            for (int placed = 0; placed < S;) {
+                const int slot = past + placed - committed;
+                const int can = std::min(S - placed, CUINF_KVGROUP - slot);
+                PF(cuinf_kv_write_tail(k16 + (size_t)placed * NK, v16 + (size_t)placed * NK, A.ktail, A.vtail,
+                                       slot, can, nkv, vs));
+                placed += can;
+                if (slot + can == CUINF_KVGROUP) {
+                    PF(cuinf_kv_commit_group(A.ktail, A.vtail, A.kc8, A.vc8, A.ksc, A.vsc, committed,
+                                             committed / CUINF_KVGROUP, nkv, vs));
+                    committed += CUINF_KVGROUP;
+                }
+            }
+            k_attn_prefill<<<dim3(S, nh), 32, 0, st>>>(q16, A.kc8, A.vc8, A.ksc, A.vsc, A.ktail, A.vtail,
+                                                       committed, past, 1.0f / sqrtf((float)hd), ao, nh, nkv);
+            PF(cuinf_launch_status());
+            PF(cuinf_gemv_int4(ao, L.wo.p, L.wo.s, fa, S, H, NQ, vs));
+            PF(cuinf_add_f32_inplace(hs, fa, S * H, vs));
+        } else {
+            PF(cuinf_gemv_int4(xn, L.in_proj.p, L.in_proj.s, fa, S, 3 * H, H, vs));
+            PF(cuinf_conv_pre(fa, t16, t16b, S, H, vs));
+            PF(cuinf_conv_apply(t16b, t16, L.conv_w, s->conv_state[l], acc, S, H, vs));
+            PF(cuinf_conv_update_state(t16b, s->conv_state[l], S, H, vs));
+            PF(cuinf_gemv_int4(acc, L.out_proj.p, L.out_proj.s, fa, S, H, H, vs));
+            PF(cuinf_add_f32_inplace(hs, fa, S * H, vs));
+        }
+        PF(cuinf_rmsnorm(hs, L.ffn_norm, xn, S, H, c.norm_eps, vs));
+        if (l < c.n_dense) {
+            const int I = c.dense_inter;
+            PF(cuinf_gemv_int4(xn, L.w1.p, L.w1.s, fa, S, I, H, vs));
+            PF(cuinf_gemv_int4(xn, L.w3.p, L.w3.s, fb, S, I, H, vs));
+            PF(cuinf_swiglu(fa, fb, t16, S * I, vs));
+            PF(cuinf_gemv_int4(t16, L.w2.p, L.w2.s, fa, S, H, I, vs));
+            PF(cuinf_add_f32_inplace(hs, fa, S * H, vs));
+        } else {
+            const void* const* ex = (const void* const*)(m->d_experts + (size_t)L.moe_index * E * 6);
+            for (int i = 0; i < S; i++) {  // one token at a time, h_i += its expert mix (882-904)
+                int* ri = ridx + ((size_t)i * n_moe + L.moe_index) * K;
+                float* wi = rw + ((size_t)i * n_moe + L.moe_index) * K;
+                PF(moe_ffn_launch(xn + (size_t)i * H, L.gate, L.ebias, ex, hs + (size_t)i * H, H, c.moe_inter,
+                                  E, K, mid, ri, wi, st));
+            }
+        }
+    }
+    // compute_logits_last: final norm, lm_head and argmax of the last row
+    const __half* last = hs + (size_t)(S - 1) * H;
+    PF(cuinf_rmsnorm(last, m->emb_norm, xn, 1, H, c.norm_eps, vs));
+    PF(cuinf_gemv_fp16(xn, m->embed, logits, 1, c.vocab, H, vs));
+    PF(cuinf_argmax(logits, c.vocab, s->tok, vs));
+    CUINF_TRY(cudaMemcpyAsync(s->out_ring + (past + S - 1) % s->max_ctx, s->tok, 4, cudaMemcpyDeviceToDevice, st));
+    // session state for the decode steps that follow
+    CUINF_TRY(cudaMemcpyAsync(s->h, last, (size_t)H * 2, cudaMemcpyDeviceToDevice, st));
+    CUINF_TRY(cudaMemcpyAsync(s->hidden, last, (size_t)H * 2, cudaMemcpyDeviceToDevice, st));
+    if (s->keep_logits)
+        CUINF_TRY(cudaMemcpyAsync(s->logits, logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToDevice, st));
+    const int newpos = past + S;
+    int* pin = &s->pinned[cuinf_session::kTokRing];
+    *pin = newpos;
+    CUINF_TRY(cudaMemcpyAsync(s->pos, pin, 4, cudaMemcpyHostToDevice, st));
+    CUINF_TRY(cudaStreamSynchronize(st));
+    s->host_pos = newpos;
+    if (routes_out && n_moe > 0)
+        CUINF_TRY(cudaMemcpy(routes_out, ridx, (size_t)S * n_moe * K * 4, cudaMemcpyDeviceToHost));
+    if (out_token) CUINF_TRY(cudaMemcpy(out_token, s->tok, 4, cudaMemcpyDeviceToHost));
+#undef PF
+    return CUINF_OK;
+}
+
 extern "C" int cuinf_generate(cuinf_session* s, const int* prompt, int n_prompt, int n_new, int eos,
                               int* out_ids, int* n_out) {
     REQUIRE(s && prompt && out_ids && n_out && n_prompt > 0 && n_new > 0, "bad arguments");
     REQUIRE(s->host_pos + n_prompt + n_new - 1 <= s->max_ctx, "context too long for max_ctx");
     int next = -1, rc;
-    for (int i = 0; i < n_prompt; i++) {
-        rc = cuinf_decode_step(s, prompt[i], i == n_prompt - 1 ? &next : nullptr);
-        if (rc) return rc;
+    if (s->prefill) {
+        if ((rc = cuinf_prefill(s, prompt, n_prompt, &next, nullptr))) return rc;
+    } else {
+        for (int i = 0; i < n_prompt; i++) {
+            rc = cuinf_decode_step(s, prompt[i], i == n_prompt - 1 ? &next : nullptr);
+            if (rc) return rc;
+        }
     }
     int n = 0;
     out_ids[n++] = next;
@@ -1227,6 +1391,10 @@ extern "C" int cuinf_session_keep_logits(cuinf_session* s, int on) {
 
 extern "C" int cuinf_session_set_option(cuinf_session* s, int option, int value) {
     REQUIRE(s, "null session");
+    if (option == CUINF_OPT_PREFILL) {  // host-side only, no graph rebuild
+        s->prefill = value != 0;
+        return CUINF_OK;
+    }
     bool* f = option == CUINF_OPT_PREFETCH ? &s->prefetch
             : option == CUINF_OPT_PDL      ? &s->pdl
             : option == CUINF_OPT_MEGAKERNEL ? &s->use_mk

@@ -90,6 +90,20 @@ class Session:
         check(lib().cuinf_decode_step(self._h, int(token), ctypes.byref(out) if want else None))
         return out.value if want else None
 
+    def prefill(self, ids, routes=False):
+        """Batched prompt processing (the reference's prefill): returns the
+        argmax after the last id, and with routes=True also the expert ids
+        each token chose, int32 [S, n_moe_layers, top_k]."""
+        import numpy as np
+        S = len(ids)
+        p = (ctypes.c_int * S)(*[int(t) for t in ids])
+        out = ctypes.c_int(-1)
+        c = self.model.cfg
+        r = np.zeros((S, max(1, c.n_layers - c.n_dense), c.top_k), np.int32) if routes else None
+        check(lib().cuinf_prefill(self._h, p, S, ctypes.byref(out),
+                                  r.ctypes.data if routes else None))
+        return (out.value, r) if routes else out.value
+
     def generate(self, prompt, n_new, eos=-1):
         p = (ctypes.c_int * len(prompt))(*prompt)
         o = (ctypes.c_int * n_new)()
@@ -97,7 +111,7 @@ class Session:
         check(lib().cuinf_generate(self._h, p, len(prompt), n_new, eos, o, ctypes.byref(n)))
         return list(o[:n.value])
 
-    OPT_PREFETCH, OPT_PDL, OPT_MEGAKERNEL, OPT_TRACE = 1, 2, 3, 4
+    OPT_PREFETCH, OPT_PDL, OPT_MEGAKERNEL, OPT_TRACE, OPT_PREFILL = 1, 2, 3, 4, 5
     STAGE_KINDS = ("conv_in", "residual", "qkv", "attention", "dense_up", "moe_up", "moe_down",
                    "lm_head")
 

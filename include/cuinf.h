@@ -202,9 +202,22 @@ int cuinf_session_pos(const cuinf_session* s);
  * which never leaves the device.  out_token (host, nullable) receives the
  * argmax after a stream sync.  Asynchronous when out_token == NULL. */
 int cuinf_decode_step(cuinf_session* s, int token, int* out_token);
-/* Greedy generation like the reference's main: feed n_prompt ids, then
- * n_new tokens (stop early on eos >= 0).  out_ids host [n_new]; returns the
- * number generated in *n_out. */
+/* Batched prompt processing, replacing the reference's prefill
+ * (src/engine.cu:910-917: layer_forward with S = n_ids, 784-908): every layer
+ * runs on all S tokens at positions pos..pos+S-1; each attention layer first
+ * places all S keys/values (FP8-committing every full 64-token group,
+ * 831-845), then every query attends over them (attention_fused, 236-308);
+ * then the last row's logits and argmax (compute_logits_last, 932-940).
+ * Synchronous; the session continues with cuinf_decode_step(s, -1, ...) from
+ * position pos + S.  out_token (host, nullable) receives the argmax;
+ * routes_out (host, nullable) [S][n_layers - n_dense][top_k] the expert ids
+ * each token chose in each MoE layer.  Results differ from feeding the same
+ * ids through decode steps exactly as the reference's prefill does. */
+int cuinf_prefill(cuinf_session* s, const int* ids, int n_ids, int* out_token, int* routes_out);
+/* Greedy generation like the reference's main (engine.cu:910-965): the prompt
+ * through cuinf_prefill (or, with CUINF_OPT_PREFILL off, one decode step per
+ * prompt id), then n_new tokens (stop early on eos >= 0).  out_ids host
+ * [n_new]; returns the number generated in *n_out. */
 int cuinf_generate(cuinf_session* s, const int* prompt, int n_prompt, int n_new, int eos,
                    int* out_ids, int* n_out);
 /* Device pointer to this session's last fp32 logits [vocab] (filled only while
@@ -224,6 +237,9 @@ int cuinf_session_keep_logits(cuinf_session* s, int on);
 /* CUINF_OPT_TRACE: the megakernel records %globaltimer at every stage start
  * and end of every CTA (read with cuinf_session_trace; default 0). */
 #define CUINF_OPT_TRACE 4
+/* CUINF_OPT_PREFILL: cuinf_generate consumes its prompt with cuinf_prefill,
+ * as the reference does (default 1); 0 feeds it through decode steps. */
+#define CUINF_OPT_PREFILL 5
 int cuinf_session_set_option(cuinf_session* s, int option, int value);
 /* Device error flags of the engine kernels (bit 0: a bounded wait on a
  * weight-staging barrier timed out and the kernel skipped its math). */

@@ -725,6 +725,150 @@ int orc_forward_token_ex(const orc_model* m, orc_state* s, int token, const int*
     return next;
 }
 
+/* Prefill: layer_forward for S tokens at positions pos..pos+S-1
+ * (engine.cu:784-908) followed by compute_logits_last (932-940).  Per layer,
+ * all S tokens' K/V are placed first (the placement loop at 831-845 writes
+ * the tail up to each group boundary and commits every full group), and only
+ * then does each query attend (attention_fused, 236-308): query i sees keys
+ * [0, pos+i], those below the post-placement committed count from FP8.
+ * Routing is per token (883-892).  Returns the argmax of the last row's
+ * logits; logits_out (nullable) receives them. */
+int orc_prefill(const orc_model* m, orc_state* s, const int* tokens, int S, float* logits_out) {
+    return orc_prefill_ex(m, s, tokens, S, NULL, NULL, logits_out);
+}
+
+/* Same, with optional forced expert choices forced_idx [S][n_moe][top_k]
+ * (weights recomputed from the oracle's router for those experts) and the
+ * oracle's own scores sigmoid+bias written to scores_out [S][n_moe][E]. */
+int orc_prefill_ex(const orc_model* m, orc_state* s, const int* tokens, int S, const int* forced_idx,
+                   float* scores_out, float* logits_out) {
+    const orc_config* c = &m->cfg;
+    const int H = c->hidden, hd = c->head_dim, nh = c->n_heads, nkv = c->n_kv_heads;
+    const float eps = c->norm_eps;
+    const int past = s->pos;
+    int maxI = c->dense_inter > c->moe_inter ? c->dense_inter : c->moe_inter;
+    int maxN = 3 * H;
+    if (maxI > maxN) maxN = maxI;
+    if (nh * hd > maxN) maxN = nh * hd;
+    uint16_t* hs = (uint16_t*)malloc((size_t)S * H * 2);
+    uint16_t* xn = (uint16_t*)malloc((size_t)S * H * 2);
+    uint16_t* q16 = (uint16_t*)malloc((size_t)S * nh * hd * 2);
+    uint16_t* k16 = (uint16_t*)malloc((size_t)S * nkv * hd * 2);
+    uint16_t* v16 = (uint16_t*)malloc((size_t)S * nkv * hd * 2);
+    uint16_t* ao = (uint16_t*)malloc((size_t)S * nh * hd * 2);
+    uint16_t* t16 = (uint16_t*)malloc((size_t)S * maxN * 2);
+    uint16_t* t16b = (uint16_t*)malloc((size_t)S * maxN * 2);
+    uint16_t* acc = (uint16_t*)malloc((size_t)S * H * 2);
+    float* fa = (float*)malloc((size_t)S * maxN * 4);
+    float* fb = (float*)malloc((size_t)S * maxN * 4);
+    int* pos = (int*)malloc((size_t)S * sizeof(int));
+    for (int i = 0; i < S; i++) {
+        memcpy(hs + (size_t)i * H, m->embed + (size_t)tokens[i] * H, (size_t)H * 2);  /* embed_gather */
+        pos[i] = past + i;
+    }
+    int moe_i = 0;
+    for (int l = 0; l < c->n_layers; l++) {
+        const orc_layer* L = &m->L[l];
+        orc_rmsnorm(hs, L->op_norm, xn, S, H, eps);
+        if (c->attn_layer[l]) {
+            orc_gemv_int4(xn, L->wq.p, L->wq.s, fa, S, L->wq.N, H);
+            orc_f32_to_f16(fa, q16, S * nh * hd);
+            orc_gemv_int4(xn, L->wk.p, L->wk.s, fa, S, L->wk.N, H);
+            orc_f32_to_f16(fa, k16, S * nkv * hd);
+            orc_gemv_int4(xn, L->wv.p, L->wv.s, fa, S, L->wv.N, H);
+            orc_f32_to_f16(fa, v16, S * nkv * hd);
+            orc_rmsnorm(q16, L->q_ln, q16, S * nh, hd, eps);
+            orc_rmsnorm(k16, L->k_ln, k16, S * nkv, hd, eps);
+            orc_rope(q16, k16, pos, S, nh, nkv, hd, c->rope_theta);
+            int placed = 0;
+            while (placed < S) {  /* engine.cu:831-845 */
+                int slot = past + placed - s->committed[l];
+                int can = S - placed < 64 - slot ? S - placed : 64 - slot;
+                orc_kv_write_tail(k16 + (size_t)placed * nkv * hd, v16 + (size_t)placed * nkv * hd,
+                                  s->ktail[l], s->vtail[l], slot, can, nkv, hd);
+                placed += can;
+                if (slot + can == 64) {
+                    orc_kv_commit_group(s->ktail[l], s->vtail[l], s->kc8[l], s->vc8[l], s->ksc[l],
+                                        s->vsc[l], s->committed[l], s->committed[l] / 64, nkv, hd);
+                    s->committed[l] += 64;
+                }
+            }
+            float scale = 1.0f / sqrtf((float)hd);
+            for (int i = 0; i < S; i++)
+                orc_attn_decode(q16 + (size_t)i * nh * hd, s->kc8[l], s->vc8[l], s->ksc[l], s->vsc[l],
+                                s->ktail[l], s->vtail[l], s->committed[l], past + i, scale,
+                                ao + (size_t)i * nh * hd, nh, nkv, hd);
+            orc_gemv_int4(ao, L->wo.p, L->wo.s, fa, S, H, nh * hd);
+            orc_add_f32_inplace(hs, fa, S * H);
+        } else {
+            orc_gemv_int4(xn, L->in_proj.p, L->in_proj.s, fa, S, 3 * H, H);
+            orc_conv_pre(fa, t16, t16b, S, H);
+            orc_conv_apply(t16b, t16, L->conv_w, s->conv_state[l], acc, S, H);
+            orc_conv_update_state(t16b, s->conv_state[l], S, H);
+            orc_gemv_int4(acc, L->out_proj.p, L->out_proj.s, fa, S, H, H);
+            orc_add_f32_inplace(hs, fa, S * H);
+        }
+        orc_rmsnorm(hs, L->ffn_norm, xn, S, H, eps);
+        if (l < c->n_dense) {
+            int I = c->dense_inter;
+            orc_gemv_int4(xn, L->w1.p, L->w1.s, fa, S, I, H);
+            orc_gemv_int4(xn, L->w3.p, L->w3.s, fb, S, I, H);
+            orc_swiglu(fa, fb, t16, S * I);
+            orc_gemv_int4(t16, L->w2.p, L->w2.s, fa, S, H, I);
+            orc_add_f32_inplace(hs, fa, S * H);
+        } else {
+            int E = c->n_experts, K = c->top_k, I = c->moe_inter;
+            float rl[256], eb[256], w[16];
+            int idx[16];
+            for (int e = 0; e < E; e++) eb[e] = orc_h2f(L->ebias[e]);
+            memset(acc, 0, (size_t)S * H * 2);  /* expert_out_acc, engine.cu:882 */
+            const int n_moe = c->n_layers - c->n_dense;
+            for (int i = 0; i < S; i++) {
+                const uint16_t* xi = xn + (size_t)i * H;
+                orc_gemv_fp16(xi, L->gate, rl, 1, E, H);
+                orc_moe_select(rl, eb, E, K, idx, w);
+                if (scores_out)
+                    for (int e = 0; e < E; e++)
+                        scores_out[((size_t)i * n_moe + moe_i) * E + e] = 1.0f / (1.0f + expf(-rl[e])) + eb[e];
+                if (forced_idx) {
+                    float wsum = 0.0f;
+                    for (int t = 0; t < K; t++) {
+                        idx[t] = forced_idx[((size_t)i * n_moe + moe_i) * K + t];
+                        w[t] = 1.0f / (1.0f + expf(-rl[idx[t]]));
+                    }
+                    for (int t = 0; t < K; t++) wsum += w[t];
+                    for (int t = 0; t < K; t++) w[t] /= (wsum + 1e-6f);
+                }
+                for (int t = 0; t < K; t++) {
+                    s->route_idx[moe_i * K + t] = idx[t];
+                    s->route_w[moe_i * K + t] = w[t];
+                }
+                for (int t = 0; t < K; t++) {
+                    int e = idx[t];
+                    orc_gemv_int4(xi, L->ew1[e].p, L->ew1[e].s, fa, 1, I, H);
+                    orc_gemv_int4(xi, L->ew3[e].p, L->ew3[e].s, fb, 1, I, H);
+                    orc_swiglu(fa, fb, t16, I);
+                    orc_gemv_int4(t16, L->ew2[e].p, L->ew2[e].s, fa, 1, H, I);
+                    orc_acc_scaled(acc + (size_t)i * H, fa, w[t], H);
+                }
+            }
+            orc_add_inplace(hs, acc, S * H);
+            moe_i++;
+        }
+    }
+    memcpy(s->h, hs + (size_t)(S - 1) * H, (size_t)H * 2);
+    orc_rmsnorm(s->h, m->emb_norm, xn, 1, H, eps);
+    float* lg = (float*)malloc((size_t)c->vocab * 4);
+    orc_gemv_fp16(xn, m->embed, lg, 1, c->vocab, H);
+    int next = orc_argmax(lg, c->vocab);
+    if (logits_out) memcpy(logits_out, lg, (size_t)c->vocab * 4);
+    free(lg);
+    s->pos += S;
+    free(hs); free(xn); free(q16); free(k16); free(v16); free(ao); free(t16); free(t16b);
+    free(acc); free(fa); free(fb); free(pos);
+    return next;
+}
+
 void orc_set_threads(int n) {
 #ifdef _OPENMP
     if (n > 0) omp_set_num_threads(n);

@@ -105,6 +105,15 @@ int        orc_forward_token(const orc_model* m, orc_state* s, int token,
 int        orc_forward_token_ex(const orc_model* m, orc_state* s, int token,
                                 const int* forced_idx, float* scores,
                                 float* logits, uint16_t* hidden);
+/* Prefill of S tokens at positions pos..pos+S-1 the way the reference's
+ * batched layer_forward(S) does it (all of a layer's K/V placed and full
+ * groups committed before any query attends), then the last row's logits.
+ * Returns their argmax; state->pos advances by S. */
+int        orc_prefill(const orc_model* m, orc_state* s, const int* tokens, int S, float* logits_out);
+/* Same, with optional forced experts [S][n_moe][top_k] and the oracle's own
+ * selection scores written to scores [S][n_moe][E]. */
+int        orc_prefill_ex(const orc_model* m, orc_state* s, const int* tokens, int S,
+                          const int* forced_idx, float* scores, float* logits_out);
 /* Router decisions of the last forward_token: [n_moe_layers][top_k]. */
 const int*   orc_state_route_idx(const orc_state* s);
 const float* orc_state_route_w(const orc_state* s);

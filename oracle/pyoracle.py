@@ -59,6 +59,8 @@ _SIGS = {
     "orc_state_pos": (I, [P]),
     "orc_forward_token": (I, [P, P, I, P, P]),
     "orc_forward_token_ex": (I, [P, P, I, P, P, P, P]),
+    "orc_prefill": (I, [P, P, P, I, P]),
+    "orc_prefill_ex": (I, [P, P, P, I, P, P, P]),
     "orc_state_route_idx": (P, [P]),
     "orc_state_route_w": (P, [P]),
     "orc_set_threads": (None, [I]),
@@ -277,6 +279,19 @@ class State:
         hid = np.empty(c.hidden, np.float16) if want_hidden else None
         nxt = lib().orc_forward_token(self.model._h, self._h, int(token), _ptr(lg), _ptr(hid))
         return nxt, lg, hid
+
+    def prefill(self, tokens, forced_idx=None):
+        """Batched prefill of `tokens` (the reference's layer_forward(S));
+        returns (argmax, logits of the last row, scores [S, n_moe, E])."""
+        c = self.model.cfg
+        ids = np.ascontiguousarray(tokens, np.int32)
+        n_moe = max(1, c.n_layers - c.n_dense)
+        lg = np.empty(c.vocab, np.float32)
+        sc = np.empty((ids.size, n_moe, max(1, c.n_experts)), np.float32)
+        fi = None if forced_idx is None else np.ascontiguousarray(forced_idx, np.int32)
+        nxt = lib().orc_prefill_ex(self.model._h, self._h, ids.ctypes.data, int(ids.size), _ptr(fi),
+                                   _ptr(sc), _ptr(lg))
+        return nxt, lg, sc
 
     def forward_ex(self, token, forced_idx=None):
         """Forward with optional forced experts [n_moe*top_k]; returns

@@ -20,8 +20,39 @@ def own_topk(scores, k):
     return order[:k], (scores[order[k - 1]] - scores[order[k]]) if len(scores) > k else np.inf
 
 
-def run_compare(cfg, om, s, tokens, max_ctx, logit_tol=LOGIT_TOL, route_margin=ROUTE_MARGIN):
-    st = om.state(max_ctx)
+def check_routes(gi, sc, k, route_margin, where):
+    """gi [n_moe, k] the engine's experts, sc [n_moe, E] the oracle's scores
+    on the same inputs; returns (checked, near_ties)."""
+    checked = near = 0
+    for l in range(gi.shape[0]):
+        sel, margin = own_topk(sc[l], k)
+        if margin > route_margin:
+            # same expert set; each slot holds an expert whose score is
+            # within route_margin of the oracle's expert for that slot
+            # (the order is descending score, so near-equal scores may swap)
+            assert sorted(gi[l].tolist()) == sorted(sel), (where, l, list(gi[l]), sel, margin)
+            for j, e in enumerate(gi[l]):
+                assert abs(sc[l][e] - sc[l][sel[j]]) <= route_margin, (where, l, j, list(gi[l]), sel)
+            checked += 1
+        else:
+            near += 1
+    return checked, near
+
+
+def check_logits(glog, lg, got, ref, logit_tol, where):
+    """Relative max-abs logit error below logit_tol; the argmax agrees
+    outside TIE_MARGIN near-ties.  Returns the error."""
+    e = float(np.max(np.abs(glog - lg)) / np.max(np.abs(lg)))
+    assert e < logit_tol, (where, e)
+    top = np.sort(lg)[::-1]
+    if top[0] - top[1] > TIE_MARGIN * max(1.0, abs(top[0])):
+        assert got == ref, (where, got, ref)
+    return e
+
+
+def run_compare(cfg, om, s, tokens, max_ctx, logit_tol=LOGIT_TOL, route_margin=ROUTE_MARGIN, st=None):
+    """Teacher-forced decode steps; st continues an existing oracle state."""
+    st = om.state(max_ctx) if st is None else st
     worst, near_ties, checked = 0.0, 0, 0
     got_tokens = []
     for i, t in enumerate(tokens):
@@ -30,23 +61,8 @@ def run_compare(cfg, om, s, tokens, max_ctx, logit_tol=LOGIT_TOL, route_margin=R
         gi, _ = s.routes()
         gi = np.array(gi, np.int32).reshape(-1, cfg.top_k)
         ref, lg, _, sc = st.forward_ex(int(t), forced_idx=gi.ravel())
-        for l in range(gi.shape[0]):
-            sel, margin = own_topk(sc[l], cfg.top_k)
-            if margin > route_margin:
-                # same expert set; each slot holds an expert whose score is
-                # within route_margin of the oracle's expert for that slot
-                # (the order is descending score, so near-equal scores may swap)
-                assert sorted(gi[l].tolist()) == sorted(sel), (i, l, list(gi[l]), sel, margin)
-                for j, e in enumerate(gi[l]):
-                    assert abs(sc[l][e] - sc[l][sel[j]]) <= route_margin, (i, l, j, list(gi[l]), sel)
-                checked += 1
-            else:
-                near_ties += 1
-        glog = s.logits().cpu().numpy()
-        e = float(np.max(np.abs(glog - lg)) / np.max(np.abs(lg)))
-        worst = max(worst, e)
-        assert e < logit_tol, (i, e)
-        top = np.sort(lg)[::-1]
-        if top[0] - top[1] > TIE_MARGIN * max(1.0, abs(top[0])):
-            assert got == ref, (i, got, ref)
+        c, n = check_routes(gi, sc, cfg.top_k, route_margin, i)
+        checked += c
+        near_ties += n
+        worst = max(worst, check_logits(s.logits().cpu().numpy(), lg, got, ref, logit_tol, i))
     return worst, near_ties, checked, got_tokens

@@ -186,3 +186,41 @@ def test_argmax_key_rule_matches_reference_tree():
         n = int(rng.integers(1, 3000))
         v = rng.integers(0, int(rng.integers(1, 6)), n).astype(np.float32)
         assert key_argmax(v) == _argmax_ref_kernel(v)
+
+
+def test_oracle_prefill_semantics(tmp_path):
+    """The oracle's batched prefill (engine.cu:784-917) equals decoding the
+    same ids one by one while no KV group commits inside it (every key is
+    then read from the fp16 tail in both), and differs once one does (the
+    prefill's queries then read their own group's keys as FP8)."""
+    import zlib
+    cfg = weights.make_config(hidden=128, n_layers=3, n_heads=2, n_kv_heads=1, vocab=300, n_dense=1,
+                              n_experts=8, top_k=2, moe_inter=128, dense_inter=128, attn_layers=(1, 2))
+
+    def tensor(name, shape):
+        rng = np.random.default_rng(zlib.crc32(name.encode()))
+        k = weights.init_kind(name)
+        if k == "norm":
+            return (1 + 0.02 * rng.standard_normal(shape)).astype(np.float32)
+        if k == "conv":
+            return rng.uniform(-0.577, 0.577, shape).astype(np.float32)
+        return (0.05 * rng.standard_normal(shape)).astype(np.float32)
+
+    weights.write_model(str(tmp_path), cfg, tensor)
+    om = pyoracle.Model(weights.config_dict(cfg), np.fromfile(tmp_path / "weights.bin", np.uint8),
+                        open(tmp_path / "index.bin", "rb").read())
+    toks = np.random.default_rng(3).integers(0, cfg.vocab, 80)
+    a, b = om.state(128), om.state(128)
+    for t in toks[:20]:
+        a.forward(int(t), want_logits=False)
+        b.forward(int(t), want_logits=False)
+    n1, lg1, sc = a.prefill(toks[20:40])  # positions 20..39: no commit
+    for t in toks[20:40]:
+        n2, lg2, _, _ = b.forward_ex(int(t))
+    assert n1 == n2 and np.array_equal(lg1, lg2) and a.pos == b.pos == 40
+    assert sc.shape == (20, 2, 8)  # [S, moe layers, experts]
+    n1, lg1, _ = a.prefill(toks[40:80])  # commits group 0 at position 64
+    for t in toks[40:80]:
+        n2, lg2, _, _ = b.forward_ex(int(t))
+    assert not np.array_equal(lg1, lg2)
+    assert np.abs(lg1 - lg2).max() < 0.1 * np.abs(lg2).max()

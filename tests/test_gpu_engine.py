@@ -23,7 +23,7 @@ import pytest
 from oracle import pyoracle as orc
 from cuda_inf_b200 import weights
 from cuda_inf_b200.engine import Model, Session, device_error
-from enginecheck import run_compare
+from enginecheck import check_logits, check_routes, run_compare
 
 pytestmark = pytest.mark.gpu
 
@@ -75,6 +75,7 @@ def test_engine_greedy_matches_oracle(tiny):
     cfg, om, gm = tiny
     s = Session(gm, max_ctx=96)
     s.keep_logits(True)
+    s.set_option(Session.OPT_PREFILL, 0)  # the prompt through decode steps
     prompt = [5, 17, 999, 0, 42]
     gen = s.generate(prompt, 40)
     s2 = Session(gm, max_ctx=96)
@@ -110,3 +111,58 @@ def test_engine_options_do_not_change_results(tiny, opt):
     for t in np.random.default_rng(9).integers(0, cfg.vocab, 70):
         assert a.step(int(t)) == b.step(int(t))
         assert np.array_equal(a.logits().cpu().numpy(), b.logits().cpu().numpy())
+
+
+def prefill_compare(cfg, om, s, st, ids):
+    """Engine prefill vs the oracle's prefill forced onto the engine's
+    experts: routing outside near-ties, last-row logits and argmax."""
+    got, gi = s.prefill(ids, routes=True)
+    ref, lg, sc = st.prefill(ids, forced_idx=gi)
+    checked = near = 0
+    for i in range(len(ids)):
+        c, n = check_routes(gi[i], sc[i], cfg.top_k, 1e-3, ("prefill row", i))
+        checked += c
+        near += n
+    e = check_logits(s.logits().cpu().numpy(), lg, got, ref, 1e-2, "prefill")
+    return got, e, checked, near
+
+
+@pytest.mark.parametrize("past,S", [(0, 1), (0, 70), (30, 50), (64, 64)])
+def test_prefill_matches_oracle(tiny, past, S):
+    """Batched prefill of S ids after `past` decode steps (the reference's
+    prefill starts at 0; later starts continue a session), then 20
+    teacher-forced decode steps: the group commits inside the prefill
+    (tokens 64 and 128) and the attention over committed FP8 groups plus the
+    fp16 tail must follow the oracle."""
+    cfg, om, gm = tiny
+    rng = np.random.default_rng(1000 + past + S)
+    lead = rng.integers(0, cfg.vocab, past)
+    ids = rng.integers(0, cfg.vocab, S)
+    tail = rng.integers(0, cfg.vocab, 20)
+    s = Session(gm, max_ctx=192)
+    s.keep_logits(True)
+    st = om.state(192)
+    if past:
+        run_compare(cfg, om, s, lead, 192, st=st)
+    got, e, checked, near = prefill_compare(cfg, om, s, st, ids)
+    assert s.pos == past + S and st.pos == past + S
+    print(f"prefill past={past} S={S}: logits rel err {e:.2e}, routing checked {checked}, near-ties {near}")
+    assert checked > 0.9 * (checked + near)
+    # decoding continues from the prefilled state (first fed token = the argmax)
+    worst, near, checked, _ = run_compare(cfg, om, s, [got] + list(tail), 192, st=st)
+    assert device_error() == 0 and s.error() == 0
+
+
+def test_generate_prefills_prompt(tiny):
+    """generate() consumes its prompt with one prefill, as the reference does."""
+    cfg, om, gm = tiny
+    prompt = [int(t) for t in np.random.default_rng(77).integers(0, cfg.vocab, 66)]
+    s = Session(gm, max_ctx=128)
+    gen = s.generate(prompt, 30)
+    s2 = Session(gm, max_ctx=128)
+    seq = [s2.prefill(prompt)]
+    for _ in range(29):
+        seq.append(s2.step(-1))
+    assert gen == seq
+    s.reset()
+    assert s.generate(prompt, 30) == gen

@@ -2,27 +2,27 @@
 g023/cuda_inf, built unmodified for sm_100a by oracle/Makefile into
 oracle/_ref/ref_engine), on the same random-init full-size weights.
 
-The prompt is one token.  For a longer prompt the reference runs a batched
-prefill whose attention reads the prompt's own keys from the FP8 group that
-the prefill has just committed (attention_fused, engine.cu:236-308, with the
-placement at 831-855), while this engine decodes prompt tokens one by one
-(fp16 tail until a group is full); the two are different computations, so a
-batched prefill is what greedy parity on long prompts needs.  With a
-one-token prompt the reference's first step is its decode step
-(attn_decode_split/combine), and every later step is decode in both engines.
+Both engines consume the prompt with a batched prefill (layer_forward with
+S = prompt length, engine.cu:784-917): every attention layer first places all
+the prompt's keys/values, FP8-committing each full 64-token group, then every
+prompt query attends over them (attention_fused, 236-308); this engine's
+cuinf_prefill does the same.  Prompts of 1 and 64 tokens are run; the
+64-token prompt commits its group inside the prefill, so its queries read
+their own group's keys as FP8.  Then 80 tokens are generated, crossing the
+next commit.
 
-80 tokens are generated, crossing the FP8 commit of the first KV group.  The
-CPU oracle, teacher-forced along the reference's tokens, gives at every
-position the top-2 logit margin and, for each of the 22 MoE layers, the
-margin between the 4th and 5th expert scores.  Two faithful implementations
-differ by fp16 ulps in the residual stream, which moves router scores by up
-to ~1.5e-3; a flipped expert then changes the logits by far more than any
-rounding, so the two greedy trajectories can part at such a routing
-near-tie.  The test walks the reference's tokens: this engine's tokens must
-equal them up to the first difference, that difference must sit on a
-near-tie (logit margin below TIE_MARGIN of the top logit, or a routing
-margin below ROUTE_MARGIN in some layer), and at every clear position the
-reference's token must be the oracle's argmax.  The matched prefix is printed.
+The CPU oracle, teacher-forced along the reference's tokens, gives at every
+position the top-2 logit margin and the margin between the 4th and 5th
+expert scores of each MoE layer (of every prompt row for the prefill).  Two
+faithful implementations differ by fp16 ulps in the residual stream, which
+moves router scores by up to ~1.5e-3; a flipped expert then changes the
+logits by far more than any rounding, so the two greedy trajectories can
+part at such a routing near-tie.  The test walks the reference's tokens:
+this engine's tokens must equal them up to the first difference, that
+difference must sit on a near-tie (logit margin below TIE_MARGIN of the top
+logit, or a routing margin below ROUTE_MARGIN in some layer), and at every
+clear position the reference's token must be the oracle's argmax.  The
+matched prefix is printed.
 """
 import os
 import shutil
@@ -41,17 +41,17 @@ pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF_ENGINE = os.path.join(ROOT, "oracle", "_ref", "ref_engine")
-N_PROMPT = 1
 N_NEW = 80
 TIE_MARGIN = 1e-2  # relative top-2 logit margin below which a greedy pick is a near-tie
 ROUTE_MARGIN = 2e-3  # 4th-vs-5th expert score margin below which routing is a near-tie
 
 
 @pytest.mark.skipif(not os.path.exists(REF_ENGINE), reason="reference engine not built (oracle/_ref)")
-def test_greedy_matches_reference_engine(cuda):
+@pytest.mark.parametrize("n_prompt", [1, 64])
+def test_greedy_matches_reference_engine(cuda, n_prompt):
     cfg = weights.default_config()
     blob, index = weights.synth_device_blob(cfg, seed=97, device=cuda)
-    prompt = [int(t) for t in np.random.default_rng(5).integers(0, cfg.vocab, N_PROMPT)]
+    prompt = [int(t) for t in np.random.default_rng(5).integers(0, cfg.vocab, n_prompt)]
     base = "/dev/shm" if shutil.disk_usage("/dev/shm").free > 6e9 else None
     with tempfile.TemporaryDirectory(dir=base) as d:
         weights.save_blob(blob, index, d)
@@ -65,8 +65,8 @@ def test_greedy_matches_reference_engine(cuda):
     assert 1 <= len(ref) <= N_NEW
 
     gm = Model.from_device_blob(blob, index, cfg)
-    s = Session(gm, max_ctx=N_PROMPT + N_NEW + 8)
-    ours = s.generate(prompt, len(ref))
+    s = Session(gm, max_ctx=n_prompt + N_NEW + 8)
+    ours = s.generate(prompt, len(ref))  # prompt through cuinf_prefill
     s.close()
     gm.close()
     del blob
@@ -74,16 +74,16 @@ def test_greedy_matches_reference_engine(cuda):
 
     orc.set_threads(os.cpu_count() or 1)
     om = orc.Model(weights.config_dict(cfg), host, index)
-    st = om.state(N_PROMPT + N_NEW + 8)
-    for t in prompt[:-1]:
-        st.forward(t, want_logits=False)
+    st = om.state(n_prompt + N_NEW + 8)
     matched = 0
-    feed = prompt[-1]
     for i, tok in enumerate(ref):
-        nxt, lg, _, sc = st.forward_ex(feed)
+        if i == 0:
+            nxt, lg, sc = st.prefill(prompt)  # sc [S, n_moe, E]
+        else:
+            nxt, lg, _, sc = st.forward_ex(ref[i - 1])
         top = np.sort(lg)[::-1]
-        srt = -np.sort(-sc, axis=1)
-        route_margin = float(np.min(srt[:, cfg.top_k - 1] - srt[:, cfg.top_k]))
+        srt = -np.sort(-sc, axis=-1)
+        route_margin = float(np.min(srt[..., cfg.top_k - 1] - srt[..., cfg.top_k]))
         logit_tie = top[0] - top[1] <= TIE_MARGIN * max(1.0, abs(float(top[0])))
         near_tie = logit_tie or route_margin <= ROUTE_MARGIN
         if ours[i] != tok:
@@ -92,7 +92,7 @@ def test_greedy_matches_reference_engine(cuda):
         if not near_tie:
             assert tok == nxt, (i, tok, nxt)
         matched += 1
-        feed = tok
-    print(f"greedy tokens equal to the reference engine's: first {matched} of {len(ref)}; "
+    print(f"prompt {n_prompt}: greedy tokens equal to the reference engine's: first {matched} of {len(ref)}; "
           f"ours {ours[:matched + 1]}, reference {ref[:matched + 1]}")
-    assert matched >= 1
+    if n_prompt == 1:
+        assert matched >= 1
