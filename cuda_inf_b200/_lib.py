@@ -34,6 +34,9 @@ _SIGS = {
     "cuinf_last_error": (ctypes.c_char_p, []),
     "cuinf_version": (ctypes.c_char_p, []),
     "cuinf_gemv_int4": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "cuinf_gemm_int4_tc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "cuinf_gemm_fp16_tc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "cuinf_argmax_key_index": (c_int, [ctypes.c_ulonglong]),
     "cuinf_gemv_fp16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "cuinf_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]),
     "cuinf_rope": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_void_p]),

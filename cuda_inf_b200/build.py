@@ -15,8 +15,8 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libcuinf.so")
-SOURCES = ["ops.cu", "engine.cu"]
-HEADERS = ["common.cuh", "attn.cuh", "engine_kernels.cuh", "route.cuh"]
+SOURCES = ["ops.cu", "engine.cu", "batch.cu"]
+HEADERS = ["common.cuh", "attn.cuh", "engine_kernels.cuh", "route.cuh", "tc_gemm.cuh"]
 
 NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

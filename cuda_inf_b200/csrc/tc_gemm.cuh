@@ -1,0 +1,382 @@
+// INT4 (or fp16) weights x fp16 activations on the 5th-generation tensor
+// cores: the batched-decode / prefill form of gemv_int4 (engine.cu:83-109,
+// y[M,N] = x[M,K] . deq(W[N,K])^T with deq = (nib-8) * scale[n, k/128]).
+//
+// One CTA owns a tile of 128 weight rows (the MMA's M) against up to 128
+// activation rows (the MMA's N; tokens of a batch or of one expert's group)
+// over a K range (split-K across CTAs, reduced in a fixed order).
+//   warp 8   TMA producer of the packed INT4 rows (2-D tensor map, box
+//            64 bytes x 128 rows, 64-byte swizzle) into a 6-deep ring; for
+//            fp16 weights it loads the A operand directly (128-byte swizzle);
+//   warp 9   TMA producer of the activation rows (box 64 halves x 16 rows,
+//            128-byte swizzle, which is the K-major UMMA layout);
+//   warps 0-7 dequantize 128 K per stage: (nib-8) exact in fp16 via the
+//            1024-magic, times the group's fp16 scale (one fp16 rounding per
+//            weight), written in the 128-byte-swizzled K-major layout;
+//   warp 10  allocates the TMEM accumulator (128 lanes x 128 fp32 columns)
+//            and one thread issues tcgen05.mma.kind::f16 (M=128, N=rows
+//            rounded up to 16, K=16), committing each stage to the barrier
+//            that frees its operand slot;
+//   warps 0-3 read the accumulator back with tcgen05.ld (lane = weight row,
+//            column = activation row) for the epilogue.
+// Every wait is bounded; a time-out sets the error word and the CTA drains
+// its copies and MMAs before it frees TMEM and exits.  No cluster multicast.
+#pragma once
+#include <cuda.h>
+#include "common.cuh"
+
+#define TC_ROWS 128
+#define TC_KS 128
+#define TC_NMAX 128
+#define TC_PST 6
+#define TC_OST 2
+#define TC_DQ_WARPS 8
+#define TC_THREADS ((TC_DQ_WARPS + 3) * 32)
+#define TC_A_BYTES (TC_ROWS * TC_KS * 2)  // 32 KB: two 64-K swizzle atoms
+#define TC_X_BYTES (TC_NMAX * TC_KS * 2)  // 32 KB
+#define TC_P_BYTES (TC_ROWS * TC_KS / 2)  // 8 KB packed
+#define TC_MAX_KG 64                      // scale groups per split held in smem (K range <= 8192)
+#define TC_TMEM_COLS 128
+
+struct TcGroup {
+    const CUtensorMap* wmap;  // weights (global-memory tensor map); null = the launch's own map
+    const __half* scales;     // [N, K/128] for INT4 weights
+    float* y;                 // y[j * ldy + n], j < rows
+    int x_row;                // first activation row in the activation tensor map
+    int rows;                 // activation rows, 0..TC_NMAX
+    int N;                    // weight rows
+    int ldy;
+};
+
+struct TcParams {
+    const TcGroup* groups;  // device table, or null: one group, g0
+    TcGroup g0;
+    int n_groups;
+    int K;
+    int splits, kg_per_split;
+    int fp16_w;                    // weights are fp16 [N, K] (no dequantization)
+    float* ws;                     // split-K partials [slot][TC_NMAX][TC_ROWS]
+    unsigned* counters;            // per (group, tile) arrival counters, self-resetting
+    unsigned long long* amax;      // optional per activation row argmax key (lm_head)
+    unsigned* err;
+};
+
+struct TcSmem {
+    uint64_t p_full[TC_PST], p_empty[TC_PST];
+    uint64_t a_full[TC_OST], x_full[TC_OST], op_empty[TC_OST];
+    uint64_t done;
+    uint32_t tmem;
+    int abort_;
+    int last;
+    unsigned long long amax[4][TC_NMAX];
+};
+
+static constexpr size_t TC_SMEM_BYTES =
+    1024 + TC_OST * (size_t)(TC_A_BYTES + TC_X_BYTES) + TC_PST * (size_t)TC_P_BYTES +
+    (size_t)TC_ROWS * TC_MAX_KG * 2 + sizeof(TcSmem);
+
+__device__ __forceinline__ void tc_tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];\n" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tc_tma_2d_hint(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                               uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+        "[%1, {%2, %3}], [%4], %5;\n" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ void tc_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+// UMMA shared-memory descriptor, K-major, 128-byte swizzle: 8-row core
+// groups 1024 bytes apart (SBO), leading offset unused (1), version 1.
+__device__ __forceinline__ uint64_t tc_desc_sw128(const void* p) {
+    const uint64_t a = smem_u32(p);
+    return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::f16: fp32 accumulate, A = B = f16, both
+// K-major, N = n, M = 128.
+__device__ __forceinline__ uint32_t tc_idesc(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_ROWS >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+            d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+// Bounded wait that also gives up as soon as another role of the CTA has.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, TcSmem* S, unsigned* err) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if (*(volatile int*)&S->abort_) return false;
+        if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) break;
+        __nanosleep(20);
+    }
+    *(volatile int*)&S->abort_ = 1;
+    if (err) atomicOr(err, 2u);
+    return false;
+}
+// Final drain: wait for a phase regardless of the abort flag (bounded).
+__device__ __forceinline__ void tc_drain(uint64_t* bar, uint32_t parity, unsigned* err) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_test_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) {
+            if (err) atomicOr(err, 2u);
+            return;
+        }
+        __nanosleep(20);
+    }
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_tc_gemm(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap0, const TcParams P) {
+    extern __shared__ __align__(1024) unsigned char tc_raw[];
+    const TcGroup G = P.groups ? P.groups[blockIdx.z] : P.g0;
+    const int n0 = blockIdx.x * TC_ROWS;
+    if (G.rows <= 0 || n0 >= G.N) return;
+    const CUtensorMap* wmap = G.wmap ? G.wmap : &wmap0;
+    const int KG = P.K / TC_KS;
+    const int split = blockIdx.y;
+    const int kg0 = split * P.kg_per_split;
+    const int nk = min(KG, kg0 + P.kg_per_split) - kg0;
+    const int npad = (G.rows + 15) & ~15;
+
+    unsigned char* sm = tc_raw + ((1024 - (smem_u32(tc_raw) & 1023)) & 1023);
+    unsigned char* A = sm;
+    unsigned char* X = A + TC_OST * TC_A_BYTES;
+    unsigned char* PK = X + TC_OST * TC_X_BYTES;
+    __half* SC = reinterpret_cast<__half*>(PK + TC_PST * TC_P_BYTES);
+    TcSmem* S = reinterpret_cast<TcSmem*>(SC + TC_ROWS * TC_MAX_KG);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (tid == 0) {
+        for (int i = 0; i < TC_PST; i++) {
+            mbar_init(&S->p_full[i], 1);
+            mbar_init(&S->p_empty[i], TC_DQ_WARPS);
+        }
+        for (int i = 0; i < TC_OST; i++) {
+            mbar_init(&S->a_full[i], P.fp16_w ? 1 : TC_DQ_WARPS);
+            mbar_init(&S->x_full[i], 1);
+            mbar_init(&S->op_empty[i], 1);
+        }
+        mbar_init(&S->done, 1);
+        S->abort_ = 0;
+    }
+    if (warp == TC_DQ_WARPS + 2) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(&S->tmem)),
+                     "r"(TC_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = S->tmem;
+
+    if (warp == TC_DQ_WARPS) {
+        // ---- weight producer ----
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            int last[TC_PST > TC_OST ? TC_PST : TC_OST];
+            for (int s = 0; s < TC_PST; s++) last[s] = -1;
+            bool ok = true;
+            for (int i = 0; i < nk && ok; i++) {
+                const int kg = kg0 + i;
+                if (P.fp16_w) {
+                    const int s = i % TC_OST;
+                    if (!(ok = tc_wait(&S->op_empty[s], ((i / TC_OST) & 1) ^ 1, S, P.err))) break;
+                    mbar_arrive_expect_tx(&S->a_full[s], TC_A_BYTES);
+                    tc_tma_2d_hint(A + s * TC_A_BYTES, wmap, kg * TC_KS, n0, &S->a_full[s], pol);
+                    tc_tma_2d_hint(A + s * TC_A_BYTES + TC_A_BYTES / 2, wmap, kg * TC_KS + 64, n0, &S->a_full[s], pol);
+                    last[s] = i;
+                } else {
+                    const int s = i % TC_PST;
+                    if (!(ok = tc_wait(&S->p_empty[s], ((i / TC_PST) & 1) ^ 1, S, P.err))) break;
+                    mbar_arrive_expect_tx(&S->p_full[s], TC_P_BYTES);
+                    tc_tma_2d_hint(PK + s * TC_P_BYTES, wmap, kg * (TC_KS / 2), n0, &S->p_full[s], pol);
+                    last[s] = i;
+                }
+            }
+            // copies still in flight land before the CTA can exit
+            const int depth = P.fp16_w ? TC_OST : TC_PST;
+            for (int s = 0; s < depth; s++)
+                if (last[s] >= 0)
+                    tc_drain(P.fp16_w ? &S->a_full[s] : &S->p_full[s], (last[s] / depth) & 1, P.err);
+        }
+    } else if (warp == TC_DQ_WARPS + 1) {
+        // ---- activation producer ----
+        if (lane == 0) {
+            pdl_wait();
+            int last[TC_OST] = {-1, -1};
+            for (int i = 0; i < nk; i++) {
+                const int s = i % TC_OST;
+                if (!tc_wait(&S->op_empty[s], ((i / TC_OST) & 1) ^ 1, S, P.err)) break;
+                mbar_arrive_expect_tx(&S->x_full[s], (uint32_t)npad * TC_KS * 2);
+                const int kx = (kg0 + i) * TC_KS;
+                for (int a = 0; a < 2; a++)
+                    for (int b = 0; b < npad / 16; b++)
+                        tc_tma_2d(X + s * TC_X_BYTES + a * (TC_X_BYTES / 2) + b * 2048, &xmap, kx + 64 * a,
+                                  G.x_row + 16 * b, &S->x_full[s]);
+                last[s] = i;
+            }
+            for (int s = 0; s < TC_OST; s++)
+                if (last[s] >= 0) tc_drain(&S->x_full[s], (last[s] / TC_OST) & 1, P.err);
+        }
+    } else if (warp == TC_DQ_WARPS + 2) {
+        // ---- MMA issuer ----
+        if (lane == 0) {
+            const uint32_t idesc = tc_idesc(npad);
+            for (int i = 0; i < nk; i++) {
+                const int s = i % TC_OST;
+                const uint32_t ph = (i / TC_OST) & 1;
+                if (!tc_wait(&S->a_full[s], ph, S, P.err) || !tc_wait(&S->x_full[s], ph, S, P.err)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < TC_KS / 16; kk++) {
+                    const int off = (kk >> 2) * (TC_A_BYTES / 2) + (kk & 3) * 32;
+                    const int xoff = (kk >> 2) * (TC_X_BYTES / 2) + (kk & 3) * 32;
+                    tc_mma(tmem, tc_desc_sw128(A + s * TC_A_BYTES + off), tc_desc_sw128(X + s * TC_X_BYTES + xoff),
+                           idesc, (i | kk) != 0);
+                }
+                tc_commit(&S->op_empty[s]);
+            }
+            tc_commit(&S->done);  // tracks every MMA issued above
+        }
+    } else {
+        // ---- dequantization (INT4 weights) ----
+        const int r = tid & (TC_ROWS - 1), h = tid >> 7;
+        if (!P.fp16_w) {
+            for (int i = tid; i < TC_ROWS * nk; i += TC_DQ_WARPS * 32) {
+                const int rr = i / nk, g = i - rr * nk;
+                SC[g * TC_ROWS + rr] = n0 + rr < G.N ? G.scales[(size_t)(n0 + rr) * KG + kg0 + g] : __float2half(0.f);
+            }
+            asm volatile("bar.sync 1, %0;\n" ::"r"(TC_DQ_WARPS * 32) : "memory");
+            for (int i = 0; i < nk; i++) {
+                const int s = i % TC_PST;
+                if (!tc_wait(&S->p_full[s], (i / TC_PST) & 1, S, P.err)) break;
+                const unsigned char* row = PK + s * TC_P_BYTES + r * 64;
+                const int sw = (r >> 1) & 3;
+                const uint4 c0 = *reinterpret_cast<const uint4*>(row + (((2 * h) ^ sw) << 4));
+                const uint4 c1 = *reinterpret_cast<const uint4*>(row + (((2 * h + 1) ^ sw) << 4));
+                __syncwarp();
+                if (lane == 0) tc_arrive(&S->p_empty[s]);
+                const __half sch = SC[i * TC_ROWS + r];
+                const uint32_t sc2 = (uint32_t)__half_as_ushort(sch) * 0x10001u;
+                const int so = i % TC_OST;
+                if (!tc_wait(&S->op_empty[so], ((i / TC_OST) & 1) ^ 1, S, P.err)) break;
+                unsigned char* dst = A + so * TC_A_BYTES + h * (TC_A_BYTES / 2) + r * 128;
+                const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    uint32_t q[4];
+                    dequant8(w[j], q);  // (k0,k4) (k1,k5) (k2,k6) (k3,k7)
+                    uint4 o;
+                    o.x = hmul2_u(__byte_perm(q[0], q[1], 0x5410), sc2);
+                    o.y = hmul2_u(__byte_perm(q[2], q[3], 0x5410), sc2);
+                    o.z = hmul2_u(__byte_perm(q[0], q[1], 0x7632), sc2);
+                    o.w = hmul2_u(__byte_perm(q[2], q[3], 0x7632), sc2);
+                    *reinterpret_cast<uint4*>(dst + ((j ^ (r & 7)) << 4)) = o;
+                }
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                __syncwarp();
+                if (lane == 0) tc_arrive(&S->a_full[so]);
+            }
+        }
+        // ---- epilogue (warps 0-3: TMEM lanes 32w..32w+31 = weight rows) ----
+        if (warp < 4) {
+            const bool ok = tc_wait(&S->done, 0, S, P.err);
+            tc_fence_after();
+            pdl_wait();
+            const int rr = warp * 32 + lane, n = n0 + rr;
+            const bool live = ok && !*(volatile int*)&S->abort_;
+            if (P.splits == 1) {
+                for (int c = 0; c < npad; c += 16) {
+                    float v[16];
+                    tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c, v);
+                    if (!live) continue;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        if (c + j >= G.rows) break;
+                        if (n < G.N && G.y) G.y[(size_t)(c + j) * G.ldy + n] = v[j];
+                        if (P.amax) {
+                            unsigned long long key = n < G.N ? argmax_key(v[j], n) : 0ull;
+#pragma unroll
+                            for (int o = 16; o; o >>= 1) key = umax64_dev(key, __shfl_xor_sync(0xffffffffu, key, o));
+                            if (lane == 0) S->amax[warp][c + j] = key;
+                        }
+                    }
+                }
+                if (P.amax) {
+                    asm volatile("bar.sync 2, 128;\n" ::: "memory");
+                    if (live && tid < G.rows) {
+                        unsigned long long k = S->amax[0][tid];
+                        for (int w = 1; w < 4; w++) k = umax64_dev(k, S->amax[w][tid]);
+                        atomicMax(&P.amax[G.x_row + tid], k);
+                    }
+                }
+            } else {
+                const size_t tile = (size_t)blockIdx.z * gridDim.x + blockIdx.x;
+                float* mine = P.ws + (tile * P.splits + split) * (size_t)(TC_NMAX * TC_ROWS);
+                for (int c = 0; c < npad; c += 16) {
+                    float v[16];
+                    tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c, v);
+#pragma unroll
+                    for (int j = 0; j < 16; j++) __stcg(&mine[(c + j) * TC_ROWS + rr], v[j]);
+                }
+                __threadfence();
+                asm volatile("bar.sync 2, 128;\n" ::: "memory");
+                if (tid == 0) {
+                    const unsigned t = atomicAdd(&P.counters[tile], 1u);
+                    S->last = t == (unsigned)P.splits - 1;
+                    if (S->last) P.counters[tile] = 0;  // ready for the next launch
+                }
+                asm volatile("bar.sync 2, 128;\n" ::: "memory");
+                if (S->last && live && n < G.N) {
+                    __threadfence();
+                    const float* base = P.ws + tile * P.splits * (size_t)(TC_NMAX * TC_ROWS);
+                    for (int j = 0; j < G.rows; j++) {
+                        float acc = 0.f;
+                        for (int sp = 0; sp < P.splits; sp++)
+                            acc += __ldcg(&base[sp * (size_t)(TC_NMAX * TC_ROWS) + j * TC_ROWS + rr]);
+                        G.y[(size_t)j * G.ldy + n] = acc;
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == TC_DQ_WARPS + 2) {
+        tc_fence_after();
+        if (lane == 0) tc_drain(&S->done, 0, P.err);  // all MMAs retired before TMEM is freed
+        __syncwarp();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TC_TMEM_COLS)
+                     : "memory");
+    }
+}

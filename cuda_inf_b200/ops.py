@@ -52,6 +52,31 @@ def gemv_int4(x, packed, scales, y=None):
     return y
 
 
+def gemm_int4_tc(x, packed, scales, y=None):
+    """Tensor-core form of gemv_int4 for M activation rows (tcgen05)."""
+    _dt(x, torch.float16, "x"), _dt(packed, torch.uint8, "packed"), _dt(scales, torch.float16, "scales")
+    N, K = packed.shape[0], packed.shape[1] * 2
+    M = x.numel() // K
+    if y is None:
+        y = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    check(lib().cuinf_gemm_int4_tc(_p(x), _p(packed), _p(scales), _p(y), M, N, K, _stream()))
+    return y
+
+
+def gemm_fp16_tc(x, W, want_logits=True):
+    """Tensor-core x[M,K] . W[N,K]^T with the fused argmax; returns
+    (logits fp32 [M,N] or None, argmax int [M])."""
+    _dt(x, torch.float16, "x"), _dt(W, torch.float16, "W")
+    N, K = W.shape
+    M = x.numel() // K
+    y = torch.empty((M, N), dtype=torch.float32, device=x.device) if want_logits else None
+    keys = torch.zeros(M, dtype=torch.int64, device=x.device)
+    check(lib().cuinf_gemm_fp16_tc(_p(x), _p(W), _p(y) if y is not None else None, M, N, K, _p(keys),
+                                   _stream()))
+    idx = [lib().cuinf_argmax_key_index(int(k) & 0xFFFFFFFFFFFFFFFF) for k in keys.cpu().tolist()]
+    return y, idx
+
+
 def gemv_fp16(x, W, y=None):
     """y[m,n] = sum_k x[m,k] * W[n,k]  (gemv_fp16, engine.cu:112-128)."""
     _dt(x, torch.float16, "x"), _dt(W, torch.float16, "W")

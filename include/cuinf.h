@@ -202,6 +202,23 @@ int cuinf_session_pos(const cuinf_session* s);
  * which never leaves the device.  out_token (host, nullable) receives the
  * argmax after a stream sync.  Asynchronous when out_token == NULL. */
 int cuinf_decode_step(cuinf_session* s, int token, int* out_token);
+/* Tensor-core GEMMs for batched decode and prefill (no counterpart in the
+ * reference, which runs gemv_int4 / gemv_fp16 with grid.y = M,
+ * engine.cu:83-128): tcgen05 MMA with the accumulator in TMEM, weights
+ * streamed by 2-D TMA.  cuinf_gemm_int4_tc computes the same y[M,N] fp32 as
+ * cuinf_gemv_int4, with each dequantized weight (nib-8)*scale rounded once to
+ * fp16 before the fp32-accumulated product (relative error < 1e-3).
+ * cuinf_gemm_fp16_tc: y[M,N] = x[M,K] . W[N,K]^T (y nullable) and, when
+ * argmax_keys (device u64 [M], zeroed by the caller) is given, a fused
+ * per-row argmax with the reference's tie rule (argmax_kernel, 562-572);
+ * decode a key with cuinf_argmax_key_index.  K a multiple of 128, all
+ * pointers 16-byte aligned.  Split-K uses a library-owned workspace, so calls
+ * on a device must not overlap. */
+int cuinf_gemm_int4_tc(const void* x, const uint8_t* packed, const void* scales, float* y, int M, int N, int K,
+                       void* stream);
+int cuinf_gemm_fp16_tc(const void* x, const void* W, float* y, int M, int N, int K,
+                       unsigned long long* argmax_keys, void* stream);
+int cuinf_argmax_key_index(unsigned long long key);
 /* Batched prompt processing, replacing the reference's prefill
  * (src/engine.cu:910-917: layer_forward with S = n_ids, 784-908): every layer
  * runs on all S tokens at positions pos..pos+S-1; each attention layer first
