@@ -85,6 +85,16 @@ _SIGS = {
     "cuinf_session_keep_logits": (c_int, [c_void_p, c_int]),
     "cuinf_session_set_option": (c_int, [c_void_p, c_int, c_int]),
     "cuinf_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "cuinf_batch_create": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "cuinf_batch_free": (c_int, [c_void_p]),
+    "cuinf_batch_reset": (c_int, [c_void_p]),
+    "cuinf_batch_step": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "cuinf_batch_keep_logits": (c_int, [c_void_p, c_int]),
+    "cuinf_batch_logits": (c_void_p, [c_void_p]),
+    "cuinf_batch_routes": (c_int, [c_void_p, c_void_p]),
+    "cuinf_batch_kernels_per_step": (c_int, [c_void_p]),
+    "cuinf_batch_fill_synthetic": (c_int, [c_void_p, c_int, ctypes.c_ulonglong]),
+    "cuinf_batch_error": (c_int, [c_void_p]),
     "cuinf_device_error": (c_int, [ctypes.POINTER(ctypes.c_uint)]),
     "cuinf_session_uses_megakernel": (c_int, [c_void_p]),
     "cuinf_session_trace": (c_int, [c_void_p, c_void_p, c_int, c_void_p, ctypes.POINTER(c_int),

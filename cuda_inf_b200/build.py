@@ -16,7 +16,7 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libcuinf.so")
 SOURCES = ["ops.cu", "engine.cu", "batch.cu"]
-HEADERS = ["common.cuh", "attn.cuh", "engine_kernels.cuh", "route.cuh", "tc_gemm.cuh"]
+HEADERS = ["common.cuh", "attn.cuh", "engine_kernels.cuh", "route.cuh", "tc_gemm.cuh", "model.h"]
 
 NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

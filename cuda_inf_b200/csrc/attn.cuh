@@ -35,6 +35,9 @@ struct AttnParams {
     unsigned* counters;   // [nkv], zero before the first launch; left zero
     int nh, nkv, nsplit;  // nsplit * (nh/nkv) <= ATTN_MAX_PARTS
     L2Ranges next;        // weights of the following kernels, prefetched to L2
+    // batched decode: sequence blockIdx.z reads its q, cache, position and
+    // writes its output at these element strides (counters at b * nkv)
+    size_t bq = 0, bkv8 = 0, bsc = 0, btail = 0, bout = 0, bpart = 0;
 };
 
 #define ATTN_PART_STRIDE 68
@@ -222,13 +225,22 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     const int h = blockIdx.x, sp = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const int nkv = P.nkv, gqa = P.nh / P.nkv;
+    const size_t b = blockIdx.z;
+    const uint8_t* kc8 = P.kc8 + b * P.bkv8;
+    const uint8_t* vc8 = P.vc8 + b * P.bkv8;
+    const __half* ksc = P.ksc + b * P.bsc;
+    const __half* vsc = P.vsc + b * P.bsc;
+    const __half* ktail = P.ktail + b * P.btail;
+    const __half* vtail = P.vtail + b * P.btail;
+    float* const part_b = P.part + b * P.bpart;
+    unsigned* const cnt_b = P.counters + b * nkv;
     if (threadIdx.x == 0 && P.next.count)
         l2_prefetch_share(P.next, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     pdl_trigger();
     pdl_wait();  // q and the cache come from the previous kernel
     int qpos = P.qpos, committed = P.committed;
     if (P.pos_dev) {
-        qpos = *P.pos_dev;
+        qpos = P.pos_dev[b];
         committed = ((qpos + 1) / CUINF_KVGROUP) * CUINF_KVGROUP;
     }
     const int total = qpos + 1;
@@ -243,7 +255,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     uint32_t aq[4][2];
     {
         const bool real = g < gqa;
-        const __half* qh = P.q + (size_t)(h * gqa + (real ? g : 0)) * CUINF_HD + 16 * c;
+        const __half* qh = P.q + b * P.bq + (size_t)(h * gqa + (real ? g : 0)) * CUINF_HD + 16 * c;
 #pragma unroll
         for (int s = 0; s < 4; s++) {
             uint32_t lo = *reinterpret_cast<const uint32_t*>(qh + 4 * s);
@@ -258,7 +270,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
 #pragma unroll
     for (int j = 0; j < 8; j++) O[j][0] = O[j][1] = O[j][2] = O[j][3] = 0.f;
 
-    attn_warp_units<false, ATTN_PARTS>(P.kc8, P.vc8, P.ksc, P.vsc, P.ktail, P.vtail, nkv, h, n_fp8, tail_len,
+    attn_warp_units<false, ATTN_PARTS>(kc8, vc8, ksc, vsc, ktail, vtail, nkv, h, n_fp8, tail_len,
                                        kfac, aq, u0 * ATTN_PARTS + warp, u1 * ATTN_PARTS, ATTN_THREADS / 32,
                                        m_run, l_run, O);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
@@ -275,7 +287,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
         }
     }
     __syncthreads();
-    float* part = P.part + ((size_t)(h * P.nsplit + sp) * gqa) * ATTN_PART_STRIDE;
+    float* part = part_b + ((size_t)(h * P.nsplit + sp) * gqa) * ATTN_PART_STRIDE;
     for (int it = threadIdx.x; it < gqa * 64; it += blockDim.x) {
         const int r = it >> 6, d = it & 63;
         float mm = ATTN_NEG;
@@ -296,14 +308,14 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
-        unsigned prev = atomicAdd(&P.counters[h], 1u);
+        unsigned prev = atomicAdd(&cnt_b[h], 1u);
         s_last = prev == (unsigned)(P.nsplit - 1);
     }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
     // stage (m, l) of every split in shared memory, then one weight per split
-    const float* hp = P.part + (size_t)h * P.nsplit * gqa * ATTN_PART_STRIDE;
+    const float* hp = part_b + (size_t)h * P.nsplit * gqa * ATTN_PART_STRIDE;
     float* s_m = &sm[0][0][0];                 // [nsplit*gqa]
     float* s_l = s_m + ATTN_MAX_PARTS;         // [nsplit*gqa]
     float* s_g = s_l + ATTN_MAX_PARTS;         // [gqa] max, [gqa] sum (at +8)
@@ -341,9 +353,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
             for (int k = 0; k < 8; k++)
                 if (sp0 + k < P.nsplit) o += s_m[(sp0 + k) * gqa + r] * v[k];
         }
-        P.out[(size_t)(h * gqa + r) * CUINF_HD + d] = __float2half_rn(o / s_g[8 + r]);
+        P.out[b * P.bout + (size_t)(h * gqa + r) * CUINF_HD + d] = __float2half_rn(o / s_g[8 + r]);
     }
-    if (threadIdx.x == 0) P.counters[h] = 0u;
+    if (threadIdx.x == 0) cnt_b[h] = 0u;
 }
 
 // Prefill attention (attention_fused, engine.cu:236-308): query token i of

@@ -100,9 +100,16 @@ TcPlan tc_plan(int ctas_without_split, int K, int num_sms) {
     return {(KG + kgps - 1) / kgps, kgps};
 }
 
+// Kernel attribute and error-word address, set up once per process outside
+// any graph capture.
+static unsigned* g_tc_err_ptr = nullptr;
 static int tc_attr_once() {
-    static cudaError_t e = cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                (int)TC_SMEM_BYTES);
+    static cudaError_t e = [] {
+        cudaError_t r = cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)TC_SMEM_BYTES);
+        if (r == cudaSuccess) r = cudaGetSymbolAddress((void**)&g_tc_err_ptr, g_tc_err);
+        return r;
+    }();
     if (e != cudaSuccess) return cuinf_set_cuda_error(e);
     return CUINF_OK;
 }
@@ -111,9 +118,7 @@ int tc_launch(const CUtensorMap& xmap, const CUtensorMap& wmap, TcParams P, int 
               bool pdl) {
     int rc = tc_attr_once();
     if (rc) return rc;
-    unsigned* err = nullptr;
-    CUINF_TRY(cudaGetSymbolAddress((void**)&err, g_tc_err));
-    P.err = err;
+    P.err = g_tc_err_ptr;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(tiles, P.splits, P.n_groups);
     cfg.blockDim = dim3(TC_THREADS);
@@ -223,4 +228,789 @@ extern "C" int cuinf_argmax_key_index(unsigned long long key) {
     uint32_t r = tie >> 23, b = 0;
     for (int i = 0; i < 8; i++) b |= ((r >> i) & 1u) << (7 - i);
     return (int)(((tie & 0x7FFFFFu) << 8) | b);
+}
+
+// ===========================================================================
+// Sequence-batched decode engine: B independent sequences advance one token
+// per step.  Per layer the B tokens go through the same operators as the
+// reference's layer_forward(1) for each sequence (engine.cu:784-908), with
+// every projection on the tensor-core GEMM above, attention batched over the
+// sequences' own FP8 caches, and the MoE experts grouped: a device-side
+// counting sort assigns each (token, slot) a row of its expert's group, one
+// grouped GEMM runs w1/w3 of all experts, one runs w2, and a combine kernel
+// applies the reference's per-token slot order (acc_scaled then add_inplace,
+// engine.cu:894-904).  The step is one CUDA graph.
+// ===========================================================================
+#include "model.h"
+#include "route.cuh"
+
+struct cuinf_batch {
+    cuinf_model* m = nullptr;
+    int B = 0, max_ctx = 0, num_sms = 148;
+    cudaStream_t st = nullptr;
+    bool own_stream = false;
+    std::vector<void*> allocs;
+    // per-sequence state
+    int *tok = nullptr, *pos = nullptr, *pinned = nullptr;
+    std::vector<AttnState> attn;
+    std::vector<__half*> conv_state;
+    size_t kv8_seq = 0, sc_seq = 0, tail_seq = 0;
+    // activations
+    __half *h = nullptr, *xn = nullptr, *qkv16 = nullptr, *attn_out = nullptr, *conv_y = nullptr,
+           *dmid = nullptr, *xg = nullptr, *mmid = nullptr;
+    float *fqkv = nullptr, *fa = nullptr, *fb = nullptr, *fg = nullptr, *fu = nullptr, *fo = nullptr,
+          *rlog = nullptr, *logits = nullptr;
+    int *ridx = nullptr, *inv = nullptr, *src = nullptr;
+    float* rw = nullptr;
+    unsigned long long* amax = nullptr;
+    float* apart = nullptr;
+    unsigned* acnt = nullptr;
+    int nsplit = 1;
+    // tensor-core GEMM state
+    std::vector<CUtensorMap> hmaps;  // weights (host copies)
+    CUtensorMap* dmaps = nullptr;    // same, device
+    TcGroup* dstatic = nullptr;      // q/k/v and dense w1/w3 group tables
+    std::vector<int> qkv_tab, d13_tab;
+    TcGroup *g13 = nullptr, *g2 = nullptr;  // MoE group tables, rewritten per layer
+    CUtensorMap x_h, x_conv, x_attn, x_dmid, x_xg, x_mmid;
+    std::vector<int> mi_in, mi_out, mi_q, mi_k, mi_v, mi_o, mi_w1, mi_w3, mi_w2;
+    std::vector<int> mi_experts;  // per MoE layer: index of expert 0's w1 map (then w3, w2, next expert)
+    int mi_embed = -1;
+    float* ws = nullptr;
+    unsigned* cnt = nullptr;
+    size_t ws_slots = 0, cnt_n = 0;
+    bool keep_logits = false;
+    int kernels = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+};
+
+template <class T>
+static int balloc(cuinf_batch* b, T** p, size_t bytes) {
+    void* d = nullptr;
+    CUINF_TRY(cudaMalloc(&d, bytes < 256 ? 256 : bytes));
+    CUINF_TRY(cudaMemset(d, 0, bytes < 256 ? 256 : bytes));
+    b->allocs.push_back(d);
+    *p = (T*)d;
+    return CUINF_OK;
+}
+
+// ---------------------------------------------------------------------------
+// batched kernels
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint8_t bf32_to_e4m3(float x) {
+    return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+}
+// kv_commit_group for one head of one sequence (engine.cu:202-228): scale =
+// absmax/448 + 1e-12 in fp32, stored as fp16; codes = e4m3(x / scale_f32).
+__device__ void bkv_commit_head(const __half* tail, uint8_t* c8, __half* sc, int h, int nkv, int grp, float* red) {
+    float mx = 0.f;
+    for (int e = threadIdx.x; e < CUINF_KVGROUP * CUINF_HD; e += blockDim.x) {
+        const int t = e >> 6, d = e & 63;
+        mx = fmaxf(mx, fabsf(__half2float(tail[((size_t)t * nkv + h) * CUINF_HD + d])));
+    }
+    mx = warp_max(mx);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    float amax = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) amax = fmaxf(amax, red[i]);
+    const float s = amax / 448.0f + 1e-12f;
+    if (threadIdx.x == 0) sc[grp * nkv + h] = __float2half_rn(s);
+    for (int e = threadIdx.x; e < CUINF_KVGROUP * CUINF_HD; e += blockDim.x) {
+        const int t = e >> 6, d = e & 63;
+        const float v = __half2float(tail[((size_t)t * nkv + h) * CUINF_HD + d]);
+        c8[((size_t)(grp * CUINF_KVGROUP + t) * nkv + h) * CUINF_HD + d] = bf32_to_e4m3(v / s);
+    }
+}
+
+// Placement of each sequence's new K/V row (engine.cu:831-845 with S = 1):
+// tail slot pos % 64; a full tail is committed as FP8 group pos / 64.
+// grid (B, nkv), 256 threads.
+__global__ void __launch_bounds__(256) k_bkv_place(const __half* __restrict__ k16, const __half* __restrict__ v16,
+                                                   const int* __restrict__ pos, __half* ktail, __half* vtail,
+                                                   uint8_t* kc8, uint8_t* vc8, __half* ksc, __half* vsc, int nkv,
+                                                   size_t tail_seq, size_t kv8_seq, size_t sc_seq) {
+    __shared__ float red[8];
+    const int b = blockIdx.x, h = blockIdx.y, p = pos[b], slot = p & (CUINF_KVGROUP - 1);
+    __half* kt = ktail + b * tail_seq;
+    __half* vt = vtail + b * tail_seq;
+    if (threadIdx.x < CUINF_HD) {
+        const size_t src = ((size_t)b * nkv + h) * CUINF_HD + threadIdx.x;
+        const size_t dst = ((size_t)slot * nkv + h) * CUINF_HD + threadIdx.x;
+        kt[dst] = k16[src];
+        vt[dst] = v16[src];
+    }
+    if (slot != CUINF_KVGROUP - 1) return;
+    __syncthreads();
+    bkv_commit_head(kt, kc8 + b * kv8_seq, ksc + b * sc_seq, h, nkv, p / CUINF_KVGROUP, red);
+    __syncthreads();
+    bkv_commit_head(vt, vc8 + b * kv8_seq, vsc + b * sc_seq, h, nkv, p / CUINF_KVGROUP, red);
+}
+
+// Short conv of one token per sequence (conv_pre / conv_apply /
+// conv_update_state with S = 1, engine.cu:483-525): z = in_proj output
+// [B][3H] in the order B | C | x.
+__global__ void k_bconv(const float* __restrict__ z, const __half* __restrict__ w, __half* state, __half* y, int B,
+                        int H) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * H) return;
+    const int b = i / H, c = i - b * H;
+    const float* row = z + (size_t)b * 3 * H;
+    const __half Cx = __float2half_rn(row[H + c]);
+    const __half Bx = __float2half_rn(row[c] * row[2 * H + c]);
+    __half* sb = state + (size_t)b * 2 * H;
+    const float b0 = __half2float(sb[c]), b1 = __half2float(sb[H + c]), b2 = __half2float(Bx);
+    const float w0 = __half2float(w[c * 3 + 0]), w1 = __half2float(w[c * 3 + 1]), w2 = __half2float(w[c * 3 + 2]);
+    y[i] = __float2half_rn(__half2float(Cx) * (b0 * w0 + b1 * w1 + b2 * w2));
+    sb[c] = sb[H + c];
+    sb[H + c] = Bx;
+}
+
+// MoE routing of B tokens (engine.cu:883-892, one warp per token) and the
+// expert grouping: rows of the gathered activation buffer are ordered by
+// expert, then by token; each expert's rows form up to maxch groups of 128.
+// One CTA of 256 threads; E <= 256.
+struct BRouteParams {
+    const float* logits;  // [B][E]
+    const __half* bias;
+    int B, E, topk, I, H, maxch;
+    int* ridx;  // [B][topk] (this layer's slice)
+    float* rw;  // [B][topk]
+    int* inv;   // [B*topk] row of (token, slot)
+    int* src;   // [B*topk] token of row
+    TcGroup* g13;  // [2][E][maxch]
+    TcGroup* g2;   // [E][maxch]
+    const CUtensorMap* maps;  // [E][3]: w1, w3, w2
+    void* const* experts;     // [E][6]: w1 packed, w1 scales, w3 .., w2 ..
+    float *gbuf, *ubuf, *obuf;
+};
+__global__ void __launch_bounds__(256) k_broute(const BRouteParams P) {
+    __shared__ int cnt[256], off[256];
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int b = warp; b < P.B; b += nw)
+        route_select_warp(P.logits + (size_t)b * P.E, P.bias, P.E, P.topk, P.ridx + b * P.topk, P.rw + b * P.topk);
+    __syncthreads();
+    const int n = P.B * P.topk, e = threadIdx.x;
+    if (e < P.E) {
+        int c = 0;
+        for (int j = 0; j < n; j++) c += P.ridx[j] == e;
+        cnt[e] = c;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int s = 0;
+        for (int i = 0; i < P.E; i++) {
+            off[i] = s;
+            s += cnt[i];
+        }
+    }
+    __syncthreads();
+    if (e < P.E) {
+        int k = off[e];
+        for (int j = 0; j < n; j++)
+            if (P.ridx[j] == e) {
+                P.inv[j] = k;
+                P.src[k] = j / P.topk;
+                k++;
+            }
+        for (int c = 0; c < P.maxch; c++) {
+            const int r0 = off[e] + c * TC_NMAX;
+            const int rows = max(0, min(TC_NMAX, cnt[e] - c * TC_NMAX));
+            const int gi = e * P.maxch + c;
+            TcGroup a;
+            a.wmap = P.maps + e * 3 + 0;
+            a.scales = (const __half*)P.experts[e * 6 + 1];
+            a.y = P.gbuf + (size_t)r0 * P.I;
+            a.x_row = r0;
+            a.rows = rows;
+            a.N = P.I;
+            a.ldy = P.I;
+            P.g13[gi] = a;
+            a.wmap = P.maps + e * 3 + 1;
+            a.scales = (const __half*)P.experts[e * 6 + 3];
+            a.y = P.ubuf + (size_t)r0 * P.I;
+            P.g13[P.E * P.maxch + gi] = a;
+            a.wmap = P.maps + e * 3 + 2;
+            a.scales = (const __half*)P.experts[e * 6 + 5];
+            a.y = P.obuf + (size_t)r0 * P.H;
+            a.N = P.H;
+            a.ldy = P.H;
+            P.g2[gi] = a;
+        }
+    }
+}
+
+__global__ void k_bgather(const __half* __restrict__ xn, const int* __restrict__ src, __half* xg, int H) {
+    const int r = blockIdx.x;
+    const uint4* s = reinterpret_cast<const uint4*>(xn + (size_t)src[r] * H);
+    uint4* d = reinterpret_cast<uint4*>(xg + (size_t)r * H);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) d[i] = s[i];
+}
+
+// h[b] += sum over slots in order: acc = half(acc + w_t * o_t) (acc_scaled),
+// then h = half(h + acc) (add_inplace), engine.cu:894-904.
+__global__ void k_bcombine(const float* __restrict__ obuf, const int* __restrict__ inv, const float* __restrict__ rw,
+                           __half* h, int B, int H, int topk) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * H) return;
+    const int b = i / H, c = i - b * H;
+    __half acc = __float2half_rn(0.f);
+    for (int t = 0; t < topk; t++)
+        acc = __float2half_rn(__half2float(acc) + rw[b * topk + t] * obuf[(size_t)inv[b * topk + t] * H + c]);
+    h[i] = __float2half_rn(__half2float(h[i]) + __half2float(acc));
+}
+
+__global__ void k_btok(const unsigned long long* __restrict__ keys, int* tok, int* pos, int B) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    tok[b] = argmax_key_index(keys[b]);
+    pos[b] += 1;
+}
+
+// Synthetic caches for benchmarking at a given context: every sequence's
+// committed groups hold pseudo-random FP8 codes (the lowest exponent bit
+// cleared, so no NaN codes; magnitudes up to 240) with group scales 1/112,
+// and its position is set to ctx.
+__global__ void k_bfill(uint8_t* c8, size_t n, unsigned long long seed) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        unsigned long long z = seed + i * 0x9E3779B97F4A7C15ull;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        z ^= z >> 31;
+        c8[i] = (uint8_t)(z & 0xF7u);  // exponent field <= 14: finite E4M3
+    }
+}
+__global__ void k_bfill_scales(__half* s, size_t n, float v) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        s[i] = __float2half_rn(v);
+}
+__global__ void k_bset(int* p, int B, int v) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) p[b] = v;
+}
+
+// ---------------------------------------------------------------------------
+// host: one step as a sequence of launches (recorded into a graph)
+// ---------------------------------------------------------------------------
+#define BTRY(x)                      \
+    do {                             \
+        int rc_ = (x);               \
+        if (rc_ != CUINF_OK) return rc_; \
+    } while (0)
+
+struct BStep {
+    cuinf_batch* b;
+    bool dry;  // size the split-K workspace only
+    size_t need_slots = 0, need_cnt = 0;
+    int launches = 0;
+
+    int gemm(const CUtensorMap& xm, int wmap_idx, const TcGroup* dg, TcGroup g0, int ngroups, int tiles, int K,
+             int active_ctas, bool fp16w, unsigned long long* amax) {
+        TcPlan pl = amax ? TcPlan{1, K / TC_KS} : tc_plan(active_ctas, K, b->num_sms);
+        REQUIRE(fp16w || pl.kgps <= TC_MAX_KG, "K too large");
+        launches++;
+        if (pl.splits > 1) {
+            need_slots = std::max(need_slots, (size_t)ngroups * tiles * pl.splits);
+            need_cnt = std::max(need_cnt, (size_t)ngroups * tiles);
+        }
+        if (dry) return CUINF_OK;
+        TcParams P = {};
+        P.groups = dg;
+        P.g0 = g0;
+        P.n_groups = ngroups;
+        P.K = K;
+        P.splits = pl.splits;
+        P.kg_per_split = pl.kgps;
+        P.fp16_w = fp16w;
+        P.ws = b->ws;
+        P.counters = b->cnt;
+        P.amax = amax;
+        const CUtensorMap& wm = wmap_idx >= 0 ? b->hmaps[wmap_idx] : b->hmaps[0];
+        return tc_launch(xm, wm, P, tiles, b->st, false);
+    }
+    // single weight matrix, all B rows
+    int gemm1(const CUtensorMap& xm, int wi, const __half* scales, float* y, int N, int K, bool fp16w = false,
+              unsigned long long* amax = nullptr) {
+        TcGroup g = {};
+        g.wmap = nullptr;
+        g.scales = scales;
+        g.y = y;
+        g.x_row = 0;
+        g.rows = b->B;
+        g.N = N;
+        g.ldy = N;
+        const int tiles = (N + TC_ROWS - 1) / TC_ROWS;
+        return gemm(xm, wi, nullptr, g, 1, tiles, K, tiles, fp16w, amax);
+    }
+    int ew(int rc) {
+        launches++;
+        return rc;
+    }
+};
+
+static int batch_record(cuinf_batch* b, BStep& S) {
+    const cuinf_model* m = b->m;
+    const cuinf_config& c = m->cfg;
+    const int B = b->B, H = c.hidden, nh = c.n_heads, nkv = c.n_kv_heads, E = c.n_experts, K = c.top_k;
+    const int NQ = nh * 64, NK = nkv * 64;
+    const int maxch = (B + TC_NMAX - 1) / TC_NMAX;
+    void* vs = (void*)b->st;
+    const bool dry = S.dry;
+    auto run = [&](int rc) { return dry ? CUINF_OK : rc; };
+    BTRY(S.ew(run(cuinf_embed_gather(m->embed, b->tok, b->h, B, H, vs))));
+    int moe_i = 0;
+    for (int l = 0; l < c.n_layers; l++) {
+        const LayerW& L = m->L[l];
+        BTRY(S.ew(run(cuinf_rmsnorm(b->h, L.op_norm, b->xn, B, H, c.norm_eps, vs))));
+        if (c.attn_layer[l]) {
+            const AttnState& A = b->attn[l];
+            float* qf = b->fqkv;
+            float* kf = qf + (size_t)B * NQ;
+            float* vf = kf + (size_t)B * NK;
+            __half* q16 = b->qkv16;
+            __half* k16 = q16 + (size_t)B * NQ;
+            __half* v16 = k16 + (size_t)B * NK;
+            const int tiles = (NQ + TC_ROWS - 1) / TC_ROWS;
+            const int active = tiles + 2 * ((NK + TC_ROWS - 1) / TC_ROWS);
+            BTRY(S.gemm(b->x_h, -1, b->dstatic + b->qkv_tab[l], TcGroup{}, 3, tiles, H, active, false, nullptr));
+            BTRY(S.ew(run(cuinf_f32_to_f16(qf, q16, B * (NQ + 2 * NK), vs))));
+            BTRY(S.ew(run(cuinf_rmsnorm(q16, L.q_ln, q16, B * nh, 64, c.norm_eps, vs))));
+            BTRY(S.ew(run(cuinf_rmsnorm(k16, L.k_ln, k16, B * nkv, 64, c.norm_eps, vs))));
+            BTRY(S.ew(run(cuinf_rope(q16, k16, b->pos, B, nh, nkv, c.rope_theta, vs))));
+            S.launches++;
+            if (!dry) {
+                k_bkv_place<<<dim3(B, nkv), 256, 0, b->st>>>(k16, v16, b->pos, A.ktail, A.vtail, A.kc8, A.vc8, A.ksc,
+                                                             A.vsc, nkv, b->tail_seq, b->kv8_seq, b->sc_seq);
+                BTRY(cuinf_launch_status());
+            }
+            BatchAttnArgs a;
+            a.q = q16;
+            a.kc8 = A.kc8;
+            a.vc8 = A.vc8;
+            a.ksc = A.ksc;
+            a.vsc = A.vsc;
+            a.ktail = A.ktail;
+            a.vtail = A.vtail;
+            a.pos = b->pos;
+            a.out = b->attn_out;
+            a.part = b->apart;
+            a.counters = b->acnt;
+            a.nh = nh;
+            a.nkv = nkv;
+            a.nsplit = b->nsplit;
+            a.n_seqs = B;
+            a.bq = NQ;
+            a.bkv8 = b->kv8_seq;
+            a.bsc = b->sc_seq;
+            a.btail = b->tail_seq;
+            a.bout = NQ;
+            a.bpart = attn_batched_part_floats(nh, nkv, b->nsplit);
+            a.scale = 0.125f;
+            BTRY(S.ew(run(attn_decode_batched(a, b->st))));
+            BTRY(S.gemm1(b->x_attn, b->mi_o[l], L.wo.s, b->fa, H, NQ));
+        } else {
+            BTRY(S.gemm1(b->x_h, b->mi_in[l], L.in_proj.s, b->fa, 3 * H, H));
+            S.launches++;
+            if (!dry) {
+                k_bconv<<<(B * H + 255) / 256, 256, 0, b->st>>>(b->fa, L.conv_w, b->conv_state[l], b->conv_y, B, H);
+                BTRY(cuinf_launch_status());
+            }
+            BTRY(S.gemm1(b->x_conv, b->mi_out[l], L.out_proj.s, b->fa, H, H));
+        }
+        BTRY(S.ew(run(cuinf_add_f32_inplace(b->h, b->fa, B * H, vs))));
+        BTRY(S.ew(run(cuinf_rmsnorm(b->h, L.ffn_norm, b->xn, B, H, c.norm_eps, vs))));
+        if (l < c.n_dense) {
+            const int I = c.dense_inter, tiles = (I + TC_ROWS - 1) / TC_ROWS;
+            BTRY(S.gemm(b->x_h, -1, b->dstatic + b->d13_tab[l], TcGroup{}, 2, tiles, H, 2 * tiles, false, nullptr));
+            BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->dmid, B * I, vs))));
+            BTRY(S.gemm1(b->x_dmid, b->mi_w2[l], L.w2.s, b->fa, H, I));
+            BTRY(S.ew(run(cuinf_add_f32_inplace(b->h, b->fa, B * H, vs))));
+        } else {
+            const int I = c.moe_inter;
+            BTRY(S.ew(run(cuinf_gemv_fp16(b->xn, L.gate, b->rlog, B, E, H, vs))));
+            S.launches++;
+            if (!dry) {
+                BRouteParams R;
+                R.logits = b->rlog;
+                R.bias = L.ebias;
+                R.B = B;
+                R.E = E;
+                R.topk = K;
+                R.I = I;
+                R.H = H;
+                R.maxch = maxch;
+                R.ridx = b->ridx + (size_t)moe_i * B * K;
+                R.rw = b->rw;
+                R.inv = b->inv;
+                R.src = b->src;
+                R.g13 = b->g13;
+                R.g2 = b->g2;
+                R.maps = b->dmaps + b->mi_experts[moe_i];
+                R.experts = (void* const*)(m->d_experts + (size_t)L.moe_index * E * 6);
+                R.gbuf = b->fg;
+                R.ubuf = b->fu;
+                R.obuf = b->fo;
+                k_broute<<<1, 256, 0, b->st>>>(R);
+                BTRY(cuinf_launch_status());
+                k_bgather<<<B * K, 256, 0, b->st>>>(b->xn, b->src, b->xg, H);
+                BTRY(cuinf_launch_status());
+            }
+            S.launches++;
+            const int t13 = (I + TC_ROWS - 1) / TC_ROWS, t2 = (H + TC_ROWS - 1) / TC_ROWS;
+            // about min(E, B*K) experts are hit; each group is one tile row of CTAs
+            const int hit = std::min(E, B * K);
+            BTRY(S.gemm(b->x_xg, -1, b->g13, TcGroup{}, 2 * E * maxch, t13, H, 2 * hit * t13, false, nullptr));
+            BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->mmid, B * K * I, vs))));
+            BTRY(S.gemm(b->x_mmid, -1, b->g2, TcGroup{}, E * maxch, t2, I, hit * t2, false, nullptr));
+            S.launches++;
+            if (!dry) {
+                k_bcombine<<<(B * H + 255) / 256, 256, 0, b->st>>>(b->fo, b->inv, b->rw, b->h, B, H, K);
+                BTRY(cuinf_launch_status());
+            }
+            moe_i++;
+        }
+    }
+    // final norm, lm_head with the fused argmax (compute_logits_last, engine.cu:932-940)
+    BTRY(S.ew(run(cuinf_rmsnorm(b->h, m->emb_norm, b->xn, B, H, c.norm_eps, vs))));
+    if (!dry) CUINF_TRY(cudaMemsetAsync(b->amax, 0, (size_t)B * 8, b->st));
+    BTRY(S.gemm1(b->x_h, b->mi_embed, nullptr, b->keep_logits ? b->logits : nullptr, c.vocab, H, true, b->amax));
+    S.launches++;
+    if (!dry) {
+        k_btok<<<(B + 127) / 128, 128, 0, b->st>>>(b->amax, b->tok, b->pos, B);
+        BTRY(cuinf_launch_status());
+    }
+    return CUINF_OK;
+}
+
+static int batch_build_graph(cuinf_batch* b) {
+    if (b->exec) cudaGraphExecDestroy(b->exec);
+    if (b->graph) cudaGraphDestroy(b->graph);
+    b->exec = nullptr;
+    b->graph = nullptr;
+    BStep D{b, true};
+    BTRY(batch_record(b, D));
+    if (D.need_slots > b->ws_slots) {
+        if (b->ws) cudaFree(b->ws);
+        b->ws = nullptr;
+        CUINF_TRY(cudaMalloc(&b->ws, D.need_slots * TC_NMAX * TC_ROWS * sizeof(float)));
+        b->ws_slots = D.need_slots;
+    }
+    if (D.need_cnt > b->cnt_n) {
+        if (b->cnt) cudaFree(b->cnt);
+        b->cnt = nullptr;
+        CUINF_TRY(cudaMalloc(&b->cnt, D.need_cnt * sizeof(unsigned)));
+        CUINF_TRY(cudaMemset(b->cnt, 0, D.need_cnt * sizeof(unsigned)));
+        b->cnt_n = D.need_cnt;
+    }
+    BTRY(tc_attr_once());
+    CUINF_TRY(cudaStreamSynchronize(b->st));
+    BStep R{b, false};
+    CUINF_TRY(cudaStreamBeginCapture(b->st, cudaStreamCaptureModeThreadLocal));
+    int rc = batch_record(b, R);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(b->st, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    CUINF_TRY(e);
+    b->graph = g;
+    CUINF_TRY(cudaGraphInstantiate(&b->exec, g, 0));
+    b->kernels = R.launches;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_batch_free(cuinf_batch* b) {
+    if (!b) return CUINF_OK;
+    if (b->st) cudaStreamSynchronize(b->st);
+    if (b->exec) cudaGraphExecDestroy(b->exec);
+    if (b->graph) cudaGraphDestroy(b->graph);
+    for (void* p : b->allocs) cudaFree(p);
+    if (b->ws) cudaFree(b->ws);
+    if (b->cnt) cudaFree(b->cnt);
+    if (b->pinned) cudaFreeHost(b->pinned);
+    if (b->own_stream && b->st) cudaStreamDestroy(b->st);
+    delete b;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, cuinf_batch** out) {
+    REQUIRE(m && out, "null pointer");
+    const cuinf_config& c = m->cfg;
+    REQUIRE(n_seqs >= 1 && n_seqs <= TC_NMAX, "n_seqs must be in [1, 128]");
+    REQUIRE(max_ctx >= 1, "max_ctx must be positive");
+    REQUIRE(c.hidden % TC_KS == 0 && c.moe_inter % TC_KS == 0 && c.dense_inter % TC_KS == 0 &&
+                (c.n_heads * 64) % TC_KS == 0,
+            "batched decode needs hidden, intermediates and heads*64 multiples of 128");
+    REQUIRE(c.n_experts <= 256 && c.top_k <= 8, "n_experts <= 256, top_k <= 8");
+    REQUIRE(c.n_heads % c.n_kv_heads == 0 && c.n_heads / c.n_kv_heads <= 8, "GQA ratio <= 8");
+    cuinf_batch* b = new cuinf_batch();
+    b->m = m;
+    b->B = n_seqs;
+    b->max_ctx = max_ctx;
+    int rc = CUINF_OK;
+#define TRYB(x)                     \
+    do {                            \
+        if ((rc = (x)) != CUINF_OK) { \
+            cuinf_batch_free(b);    \
+            return rc;              \
+        }                           \
+    } while (0)
+    if (stream) {
+        b->st = (cudaStream_t)stream;
+    } else {
+        if (cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking) != cudaSuccess) {
+            delete b;
+            return cuinf_set_arg_error("stream creation failed");
+        }
+        b->own_stream = true;
+    }
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&b->num_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    const int B = n_seqs, H = c.hidden, nkv = c.n_kv_heads, NQ = c.n_heads * 64, NK = nkv * 64, K = c.top_k;
+    const int I = c.moe_inter, ID = c.dense_inter, E = c.n_experts;
+    const int n_moe = c.n_layers - c.n_dense;
+    const size_t groups = (size_t)max_ctx / CUINF_KVGROUP + 2;
+    b->kv8_seq = (size_t)max_ctx * NK;
+    b->sc_seq = groups * nkv;
+    b->tail_seq = (size_t)CUINF_KVGROUP * NK;
+    b->attn.assign(c.n_layers, AttnState());
+    b->conv_state.assign(c.n_layers, nullptr);
+    for (int l = 0; l < c.n_layers; l++) {
+        if (c.attn_layer[l]) {
+            AttnState& A = b->attn[l];
+            TRYB(balloc(b, &A.kc8, B * b->kv8_seq));
+            TRYB(balloc(b, &A.vc8, B * b->kv8_seq));
+            TRYB(balloc(b, &A.ksc, B * b->sc_seq * 2));
+            TRYB(balloc(b, &A.vsc, B * b->sc_seq * 2));
+            TRYB(balloc(b, &A.ktail, B * b->tail_seq * 2));
+            TRYB(balloc(b, &A.vtail, B * b->tail_seq * 2));
+        } else {
+            TRYB(balloc(b, &b->conv_state[l], (size_t)B * 2 * H * 2));
+        }
+    }
+    const int maxN = std::max(std::max(3 * H, NQ + 2 * NK), ID);
+    TRYB(balloc(b, &b->tok, (size_t)B * 4));
+    TRYB(balloc(b, &b->pos, (size_t)B * 4));
+    TRYB(balloc(b, &b->h, (size_t)B * H * 2));
+    TRYB(balloc(b, &b->xn, (size_t)B * H * 2));
+    TRYB(balloc(b, &b->qkv16, (size_t)B * (NQ + 2 * NK) * 2));
+    TRYB(balloc(b, &b->attn_out, (size_t)B * NQ * 2));
+    TRYB(balloc(b, &b->conv_y, (size_t)B * H * 2));
+    TRYB(balloc(b, &b->dmid, (size_t)B * std::max(ID, 128) * 2));
+    TRYB(balloc(b, &b->xg, (size_t)B * K * H * 2));
+    TRYB(balloc(b, &b->mmid, (size_t)B * K * I * 2));
+    TRYB(balloc(b, &b->fqkv, (size_t)B * (NQ + 2 * NK) * 4));
+    TRYB(balloc(b, &b->fa, (size_t)B * maxN * 4));
+    TRYB(balloc(b, &b->fb, (size_t)B * maxN * 4));
+    TRYB(balloc(b, &b->fg, (size_t)B * K * std::max(I, ID) * 4));
+    TRYB(balloc(b, &b->fu, (size_t)B * K * std::max(I, ID) * 4));
+    TRYB(balloc(b, &b->fo, (size_t)B * K * H * 4));
+    TRYB(balloc(b, &b->rlog, (size_t)B * std::max(E, 1) * 4));
+    TRYB(balloc(b, &b->logits, (size_t)B * c.vocab * 4));
+    TRYB(balloc(b, &b->ridx, (size_t)std::max(n_moe, 1) * B * K * 4));
+    TRYB(balloc(b, &b->rw, (size_t)B * K * 4));
+    TRYB(balloc(b, &b->inv, (size_t)B * K * 4));
+    TRYB(balloc(b, &b->src, (size_t)B * K * 4));
+    TRYB(balloc(b, &b->amax, (size_t)B * 8));
+    b->nsplit = attn_batched_nsplit(c.n_heads, nkv, max_ctx);
+    TRYB(balloc(b, &b->apart, (size_t)B * attn_batched_part_floats(c.n_heads, nkv, b->nsplit) * 4));
+    TRYB(balloc(b, &b->acnt, (size_t)B * nkv * 4));
+    const int maxch = (B + TC_NMAX - 1) / TC_NMAX;
+    TRYB(balloc(b, &b->g13, (size_t)2 * std::max(E, 1) * maxch * sizeof(TcGroup)));
+    TRYB(balloc(b, &b->g2, (size_t)std::max(E, 1) * maxch * sizeof(TcGroup)));
+    if (cudaHostAlloc(&b->pinned, (size_t)2 * B * 4, cudaHostAllocDefault) != cudaSuccess) {
+        cuinf_batch_free(b);
+        return cuinf_set_arg_error("pinned allocation failed");
+    }
+    // activation maps
+    TRYB(tc_map_act(&b->x_h, b->xn, B, H));
+    TRYB(tc_map_act(&b->x_conv, b->conv_y, B, H));
+    TRYB(tc_map_act(&b->x_attn, b->attn_out, B, NQ));
+    TRYB(tc_map_act(&b->x_dmid, b->dmid, B, std::max(ID, 128)));
+    TRYB(tc_map_act(&b->x_xg, b->xg, B * K, H));
+    TRYB(tc_map_act(&b->x_mmid, b->mmid, B * K, I));
+    // weight maps
+    auto add4 = [&](const Q4& q, int N, int Kd, int* idx) -> int {
+        CUtensorMap mm;
+        int r = tc_map_int4(&mm, q.p, N, Kd);
+        if (r) return r;
+        *idx = (int)b->hmaps.size();
+        b->hmaps.push_back(mm);
+        return CUINF_OK;
+    };
+    const int nl = c.n_layers;
+    b->mi_in.assign(nl, -1), b->mi_out.assign(nl, -1), b->mi_q.assign(nl, -1), b->mi_k.assign(nl, -1);
+    b->mi_v.assign(nl, -1), b->mi_o.assign(nl, -1), b->mi_w1.assign(nl, -1), b->mi_w3.assign(nl, -1);
+    b->mi_w2.assign(nl, -1);
+    b->qkv_tab.assign(nl, -1), b->d13_tab.assign(nl, -1);
+    std::vector<void*> ex((size_t)std::max(n_moe, 1) * E * 6);
+    if (n_moe > 0)
+        if (cudaMemcpy(ex.data(), m->d_experts, ex.size() * sizeof(void*), cudaMemcpyDeviceToHost) != cudaSuccess) {
+            cuinf_batch_free(b);
+            return cuinf_set_arg_error("expert table copy failed");
+        }
+    for (int l = 0; l < nl; l++) {
+        const LayerW& L = m->L[l];
+        if (c.attn_layer[l]) {
+            TRYB(add4(L.wq, NQ, H, &b->mi_q[l]));
+            TRYB(add4(L.wk, NK, H, &b->mi_k[l]));
+            TRYB(add4(L.wv, NK, H, &b->mi_v[l]));
+            TRYB(add4(L.wo, H, NQ, &b->mi_o[l]));
+        } else {
+            TRYB(add4(L.in_proj, 3 * H, H, &b->mi_in[l]));
+            TRYB(add4(L.out_proj, H, H, &b->mi_out[l]));
+        }
+        if (l < c.n_dense) {
+            TRYB(add4(L.w1, ID, H, &b->mi_w1[l]));
+            TRYB(add4(L.w3, ID, H, &b->mi_w3[l]));
+            TRYB(add4(L.w2, H, ID, &b->mi_w2[l]));
+        } else {
+            const int mi = L.moe_index;
+            b->mi_experts.push_back((int)b->hmaps.size());
+            for (int e = 0; e < E; e++) {
+                void* const* t = &ex[((size_t)mi * E + e) * 6];
+                int dummy;
+                TRYB(add4(Q4{(const uint8_t*)t[0], (const __half*)t[1]}, I, H, &dummy));
+                TRYB(add4(Q4{(const uint8_t*)t[2], (const __half*)t[3]}, I, H, &dummy));
+                TRYB(add4(Q4{(const uint8_t*)t[4], (const __half*)t[5]}, H, I, &dummy));
+            }
+        }
+    }
+    {
+        CUtensorMap mm;
+        TRYB(tc_map_f16w(&mm, m->embed, c.vocab, H));
+        b->mi_embed = (int)b->hmaps.size();
+        b->hmaps.push_back(mm);
+    }
+    TRYB(balloc(b, &b->dmaps, b->hmaps.size() * sizeof(CUtensorMap)));
+    if (cudaMemcpy(b->dmaps, b->hmaps.data(), b->hmaps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice) !=
+        cudaSuccess) {
+        cuinf_batch_free(b);
+        return cuinf_set_arg_error("tensor map upload failed");
+    }
+    // static group tables: q/k/v of attention layers, w1/w3 of dense layers
+    std::vector<TcGroup> st;
+    for (int l = 0; l < nl; l++) {
+        const LayerW& L = m->L[l];
+        if (c.attn_layer[l]) {
+            b->qkv_tab[l] = (int)st.size();
+            float* qf = b->fqkv;
+            float* kf = qf + (size_t)B * NQ;
+            float* vf = kf + (size_t)B * NK;
+            st.push_back(TcGroup{b->dmaps + b->mi_q[l], L.wq.s, qf, 0, B, NQ, NQ});
+            st.push_back(TcGroup{b->dmaps + b->mi_k[l], L.wk.s, kf, 0, B, NK, NK});
+            st.push_back(TcGroup{b->dmaps + b->mi_v[l], L.wv.s, vf, 0, B, NK, NK});
+        }
+        if (l < c.n_dense) {
+            b->d13_tab[l] = (int)st.size();
+            st.push_back(TcGroup{b->dmaps + b->mi_w1[l], L.w1.s, b->fg, 0, B, ID, ID});
+            st.push_back(TcGroup{b->dmaps + b->mi_w3[l], L.w3.s, b->fu, 0, B, ID, ID});
+        }
+    }
+    if (!st.empty()) {
+        TRYB(balloc(b, &b->dstatic, st.size() * sizeof(TcGroup)));
+        if (cudaMemcpy(b->dstatic, st.data(), st.size() * sizeof(TcGroup), cudaMemcpyHostToDevice) != cudaSuccess) {
+            cuinf_batch_free(b);
+            return cuinf_set_arg_error("group table upload failed");
+        }
+    }
+    TRYB(batch_build_graph(b));
+    *out = b;
+    return CUINF_OK;
+#undef TRYB
+}
+
+extern "C" int cuinf_batch_reset(cuinf_batch* b) {
+    REQUIRE(b, "null batch");
+    const cuinf_config& c = b->m->cfg;
+    for (int l = 0; l < c.n_layers; l++) {
+        if (c.attn_layer[l]) {
+            const AttnState& A = b->attn[l];
+            CUINF_TRY(cudaMemsetAsync(A.kc8, 0, b->B * b->kv8_seq, b->st));
+            CUINF_TRY(cudaMemsetAsync(A.vc8, 0, b->B * b->kv8_seq, b->st));
+            CUINF_TRY(cudaMemsetAsync(A.ksc, 0, b->B * b->sc_seq * 2, b->st));
+            CUINF_TRY(cudaMemsetAsync(A.vsc, 0, b->B * b->sc_seq * 2, b->st));
+            CUINF_TRY(cudaMemsetAsync(A.ktail, 0, b->B * b->tail_seq * 2, b->st));
+            CUINF_TRY(cudaMemsetAsync(A.vtail, 0, b->B * b->tail_seq * 2, b->st));
+        } else {
+            CUINF_TRY(cudaMemsetAsync(b->conv_state[l], 0, (size_t)b->B * 2 * c.hidden * 2, b->st));
+        }
+    }
+    CUINF_TRY(cudaMemsetAsync(b->pos, 0, (size_t)b->B * 4, b->st));
+    CUINF_TRY(cudaStreamSynchronize(b->st));
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_batch_step(cuinf_batch* b, const int* tokens, int* out_tokens) {
+    REQUIRE(b && b->exec, "null batch");
+    const int B = b->B;
+    if (tokens) {
+        for (int i = 0; i < B; i++) REQUIRE(tokens[i] >= 0 && tokens[i] < b->m->cfg.vocab, "token out of range");
+        CUINF_TRY(cudaStreamSynchronize(b->st));  // the pinned slot is free
+        memcpy(b->pinned, tokens, (size_t)B * 4);
+        CUINF_TRY(cudaMemcpyAsync(b->tok, b->pinned, (size_t)B * 4, cudaMemcpyHostToDevice, b->st));
+    }
+    CUINF_TRY(cudaGraphLaunch(b->exec, b->st));
+    if (out_tokens) {
+        CUINF_TRY(cudaMemcpyAsync(b->pinned + B, b->tok, (size_t)B * 4, cudaMemcpyDeviceToHost, b->st));
+        CUINF_TRY(cudaStreamSynchronize(b->st));
+        memcpy(out_tokens, b->pinned + B, (size_t)B * 4);
+    }
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_batch_keep_logits(cuinf_batch* b, int on) {
+    REQUIRE(b, "null batch");
+    if ((bool)on == b->keep_logits) return CUINF_OK;
+    CUINF_TRY(cudaStreamSynchronize(b->st));
+    b->keep_logits = on != 0;
+    return batch_build_graph(b);
+}
+extern "C" const float* cuinf_batch_logits(const cuinf_batch* b) { return b ? b->logits : nullptr; }
+extern "C" int cuinf_batch_routes(cuinf_batch* b, int* idx) {
+    REQUIRE(b && idx, "null pointer");
+    const cuinf_config& c = b->m->cfg;
+    const size_t n = (size_t)std::max(1, c.n_layers - c.n_dense) * b->B * c.top_k;
+    CUINF_TRY(cudaStreamSynchronize(b->st));
+    CUINF_TRY(cudaMemcpy(idx, b->ridx, n * 4, cudaMemcpyDeviceToHost));
+    return CUINF_OK;
+}
+extern "C" int cuinf_batch_kernels_per_step(const cuinf_batch* b) { return b ? b->kernels : -1; }
+extern "C" int cuinf_batch_error(unsigned* flags) {
+    REQUIRE(flags, "null pointer");
+    unsigned v = 0;
+    CUINF_TRY(cudaMemcpyFromSymbol(&v, g_tc_err, sizeof(v)));
+    *flags = v;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_batch_fill_synthetic(cuinf_batch* b, int ctx, unsigned long long seed) {
+    REQUIRE(b, "null batch");
+    REQUIRE(ctx >= 0 && ctx < b->max_ctx, "ctx must be below max_ctx");
+    REQUIRE(ctx % CUINF_KVGROUP == 0, "ctx must be a multiple of 64 (whole FP8 groups)");
+    const cuinf_config& c = b->m->cfg;
+    const int grid = 4 * b->num_sms;
+    for (int l = 0; l < c.n_layers; l++) {
+        if (!c.attn_layer[l]) continue;
+        const AttnState& A = b->attn[l];
+        for (int s = 0; s < b->B; s++) {
+            const size_t n = (size_t)ctx * c.n_kv_heads * 64;
+            if (n) {
+                k_bfill<<<grid, 256, 0, b->st>>>(A.kc8 + s * b->kv8_seq, n, seed + 977ull * l + 131ull * s);
+                k_bfill<<<grid, 256, 0, b->st>>>(A.vc8 + s * b->kv8_seq, n, seed + 977ull * l + 131ull * s + 7);
+                const size_t ns = (size_t)(ctx / CUINF_KVGROUP) * c.n_kv_heads;
+                k_bfill_scales<<<grid, 256, 0, b->st>>>(A.ksc + s * b->sc_seq, ns, 1.0f / 112.0f);
+                k_bfill_scales<<<grid, 256, 0, b->st>>>(A.vsc + s * b->sc_seq, ns, 1.0f / 112.0f);
+            }
+        }
+    }
+    k_bset<<<(b->B + 127) / 128, 128, 0, b->st>>>(b->pos, b->B, ctx);
+    CUINF_TRY(cudaGetLastError());
+    CUINF_TRY(cudaStreamSynchronize(b->st));
+    return CUINF_OK;
 }

@@ -16,6 +16,7 @@
 #include "attn.cuh"
 #include "engine_kernels.cuh"
 #include "megakernel.cuh"
+#include "model.h"
 
 #define REQUIRE(cond, msg) \
     do {                   \
@@ -106,6 +107,43 @@ extern "C" int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_
     P.next.count = 0;
     if (workspace) CUINF_TRY(cudaMemsetAsync(ws, 0, 256, ST(stream)));
     k_attn_decode<<<dim3(nkv, ns), ATTN_THREADS, 0, ST(stream)>>>(P);
+    return cuinf_launch_status();
+}
+
+// Batched form for the sequence-batched engine (batch.cu).
+int attn_batched_nsplit(int nh, int nkv, int max_ctx) {
+    return attn_engine_nsplit(nh / nkv, (max_ctx + CUINF_KVGROUP - 1) / CUINF_KVGROUP);
+}
+size_t attn_batched_part_floats(int nh, int nkv, int nsplit) {
+    return (size_t)nkv * nsplit * (nh / nkv) * ATTN_PART_STRIDE;
+}
+int attn_decode_batched(const BatchAttnArgs& a, cudaStream_t st) {
+    AttnParams P;
+    P.q = a.q;
+    P.kc8 = a.kc8;
+    P.vc8 = a.vc8;
+    P.ksc = a.ksc;
+    P.vsc = a.vsc;
+    P.ktail = a.ktail;
+    P.vtail = a.vtail;
+    P.pos_dev = a.pos;
+    P.committed = 0;
+    P.qpos = 0;
+    P.scale = a.scale;
+    P.out = a.out;
+    P.part = a.part;
+    P.counters = a.counters;
+    P.nh = a.nh;
+    P.nkv = a.nkv;
+    P.nsplit = a.nsplit;
+    P.next.count = 0;
+    P.bq = a.bq;
+    P.bkv8 = a.bkv8;
+    P.bsc = a.bsc;
+    P.btail = a.btail;
+    P.bout = a.bout;
+    P.bpart = a.bpart;
+    k_attn_decode<<<dim3(a.nkv, a.nsplit, a.n_seqs), ATTN_THREADS, 0, st>>>(P);
     return cuinf_launch_status();
 }
 
@@ -327,35 +365,6 @@ extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* exper
 // ---------------------------------------------------------------------------
 // model
 // ---------------------------------------------------------------------------
-struct TDesc {
-    uint8_t kind;
-    uint64_t offset, packed, scales;
-    int64_t d0, d1;
-};
-struct Q4 {
-    const uint8_t* p = nullptr;
-    const __half* s = nullptr;
-};
-struct LayerW {
-    const __half *op_norm = nullptr, *ffn_norm = nullptr;
-    Q4 wq, wk, wv, wo, in_proj, out_proj, w1, w3, w2;
-    const __half *q_ln = nullptr, *k_ln = nullptr, *conv_w = nullptr, *gate = nullptr,
-                 *ebias = nullptr;
-    int moe_index = -1;  // index into the expert table / route buffers
-};
-
-struct cuinf_model {
-    cuinf_config cfg;
-    uint8_t* d_blob = nullptr;
-    size_t blob_bytes = 0;
-    bool own_blob = false;
-    std::unordered_map<std::string, TDesc> idx;
-    std::vector<LayerW> L;
-    const __half *embed = nullptr, *emb_norm = nullptr;
-    void** d_experts = nullptr;  // [n_moe][E][6]
-    int n_moe = 0;
-};
-
 extern "C" void cuinf_default_config(cuinf_config* c) {
     memset(c, 0, sizeof(*c));
     c->hidden = 2048;
@@ -593,10 +602,6 @@ extern "C" int cuinf_model_free(cuinf_model* m) {
 // ---------------------------------------------------------------------------
 // session
 // ---------------------------------------------------------------------------
-struct AttnState {
-    uint8_t *kc8 = nullptr, *vc8 = nullptr;
-    __half *ksc = nullptr, *vsc = nullptr, *ktail = nullptr, *vtail = nullptr;
-};
 
 struct cuinf_session {
     cuinf_model* m = nullptr;

@@ -10,15 +10,19 @@
 //            fp16 weights it loads the A operand directly (128-byte swizzle);
 //   warp 9   TMA producer of the activation rows (box 64 halves x 16 rows,
 //            128-byte swizzle, which is the K-major UMMA layout);
-//   warps 0-7 dequantize 128 K per stage: (nib-8) exact in fp16 via the
-//            1024-magic, times the group's fp16 scale (one fp16 rounding per
-//            weight), written in the 128-byte-swizzled K-major layout;
-//   warp 10  allocates the TMEM accumulator (128 lanes x 128 fp32 columns)
-//            and one thread issues tcgen05.mma.kind::f16 (M=128, N=rows
-//            rounded up to 16, K=16), committing each stage to the barrier
-//            that frees its operand slot;
-//   warps 0-3 read the accumulator back with tcgen05.ld (lane = weight row,
-//            column = activation row) for the epilogue.
+//   warps 0-7 dequantize 128 K (one scale group) per stage to (nib-8),
+//            exact in fp16 via the 1024-magic, written in the
+//            128-byte-swizzled K-major layout;
+//   warp 10  allocates TMEM and one thread issues tcgen05.mma.kind::f16
+//            (M=128, N=rows rounded up to 16, K=16): each stage's 8 MMAs sum
+//            exact products (nib-8)*x into one of two per-group accumulators
+//            (128 lanes x 128 fp32 columns each);
+//   warps 12-15 (lane = weight row, column = activation row) read each
+//            group's sum with tcgen05.ld, multiply it by the row's fp32
+//            scale and add it into a third TMEM region, so the result is the
+//            reference's fp32 sum of (nib-8)*scale*x up to summation order;
+//            they then run the epilogue.
+// fp16 weights (lm_head) accumulate directly in the first region.
 // Every wait is bounded; a time-out sets the error word and the CTA drains
 // its copies and MMAs before it frees TMEM and exits.  No cluster multicast.
 #pragma once
@@ -31,12 +35,13 @@
 #define TC_PST 6
 #define TC_OST 2
 #define TC_DQ_WARPS 8
-#define TC_THREADS ((TC_DQ_WARPS + 3) * 32)
+#define TC_ACC_WARP0 12
+#define TC_THREADS ((TC_ACC_WARP0 + 4) * 32)
 #define TC_A_BYTES (TC_ROWS * TC_KS * 2)  // 32 KB: two 64-K swizzle atoms
 #define TC_X_BYTES (TC_NMAX * TC_KS * 2)  // 32 KB
 #define TC_P_BYTES (TC_ROWS * TC_KS / 2)  // 8 KB packed
 #define TC_MAX_KG 64                      // scale groups per split held in smem (K range <= 8192)
-#define TC_TMEM_COLS 128
+#define TC_TMEM_COLS 512  // group accumulators at columns 0 and 128, the sum at 256
 
 struct TcGroup {
     const CUtensorMap* wmap;  // weights (global-memory tensor map); null = the launch's own map
@@ -64,6 +69,7 @@ struct TcParams {
 struct TcSmem {
     uint64_t p_full[TC_PST], p_empty[TC_PST];
     uint64_t a_full[TC_OST], x_full[TC_OST], op_empty[TC_OST];
+    uint64_t acc_full[2], acc_empty[2];
     uint64_t done;
     uint32_t tmem;
     int abort_;
@@ -128,6 +134,19 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const float (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+            taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+        : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
 // Bounded wait that also gives up as soon as another role of the CTA has.
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, TcSmem* S, unsigned* err) {
     if (mbar_test_wait(bar, parity)) return true;
@@ -184,6 +203,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&S->a_full[i], P.fp16_w ? 1 : TC_DQ_WARPS);
             mbar_init(&S->x_full[i], 1);
             mbar_init(&S->op_empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&S->acc_full[i], 1);
+            mbar_init(&S->acc_empty[i], 4);
         }
         mbar_init(&S->done, 1);
         S->abort_ = 0;
@@ -256,27 +279,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int s = i % TC_OST;
                 const uint32_t ph = (i / TC_OST) & 1;
                 if (!tc_wait(&S->a_full[s], ph, S, P.err) || !tc_wait(&S->x_full[s], ph, S, P.err)) break;
+                // INT4: the group accumulator i%2 must have been read back (stage i-2)
+                if (!P.fp16_w && !tc_wait(&S->acc_empty[i & 1], ((i >> 1) & 1) ^ 1, S, P.err)) break;
                 tc_fence_after();
+                const uint32_t d = P.fp16_w ? tmem : tmem + (uint32_t)((i & 1) * 128);
 #pragma unroll
                 for (int kk = 0; kk < TC_KS / 16; kk++) {
                     const int off = (kk >> 2) * (TC_A_BYTES / 2) + (kk & 3) * 32;
                     const int xoff = (kk >> 2) * (TC_X_BYTES / 2) + (kk & 3) * 32;
-                    tc_mma(tmem, tc_desc_sw128(A + s * TC_A_BYTES + off), tc_desc_sw128(X + s * TC_X_BYTES + xoff),
-                           idesc, (i | kk) != 0);
+                    tc_mma(d, tc_desc_sw128(A + s * TC_A_BYTES + off), tc_desc_sw128(X + s * TC_X_BYTES + xoff),
+                           idesc, P.fp16_w ? (i | kk) != 0 : kk != 0);
                 }
                 tc_commit(&S->op_empty[s]);
+                if (!P.fp16_w) tc_commit(&S->acc_full[i & 1]);
             }
             tc_commit(&S->done);  // tracks every MMA issued above
         }
-    } else {
-        // ---- dequantization (INT4 weights) ----
+    } else if (warp < TC_DQ_WARPS) {
+        // ---- dequantization (INT4 weights) to exact (nib-8) ----
         const int r = tid & (TC_ROWS - 1), h = tid >> 7;
         if (!P.fp16_w) {
-            for (int i = tid; i < TC_ROWS * nk; i += TC_DQ_WARPS * 32) {
-                const int rr = i / nk, g = i - rr * nk;
-                SC[g * TC_ROWS + rr] = n0 + rr < G.N ? G.scales[(size_t)(n0 + rr) * KG + kg0 + g] : __float2half(0.f);
-            }
-            asm volatile("bar.sync 1, %0;\n" ::"r"(TC_DQ_WARPS * 32) : "memory");
             for (int i = 0; i < nk; i++) {
                 const int s = i % TC_PST;
                 if (!tc_wait(&S->p_full[s], (i / TC_PST) & 1, S, P.err)) break;
@@ -286,8 +308,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const uint4 c1 = *reinterpret_cast<const uint4*>(row + (((2 * h + 1) ^ sw) << 4));
                 __syncwarp();
                 if (lane == 0) tc_arrive(&S->p_empty[s]);
-                const __half sch = SC[i * TC_ROWS + r];
-                const uint32_t sc2 = (uint32_t)__half_as_ushort(sch) * 0x10001u;
                 const int so = i % TC_OST;
                 if (!tc_wait(&S->op_empty[so], ((i / TC_OST) & 1) ^ 1, S, P.err)) break;
                 unsigned char* dst = A + so * TC_A_BYTES + h * (TC_A_BYTES / 2) + r * 128;
@@ -297,10 +317,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     uint32_t q[4];
                     dequant8(w[j], q);  // (k0,k4) (k1,k5) (k2,k6) (k3,k7)
                     uint4 o;
-                    o.x = hmul2_u(__byte_perm(q[0], q[1], 0x5410), sc2);
-                    o.y = hmul2_u(__byte_perm(q[2], q[3], 0x5410), sc2);
-                    o.z = hmul2_u(__byte_perm(q[0], q[1], 0x7632), sc2);
-                    o.w = hmul2_u(__byte_perm(q[2], q[3], 0x7632), sc2);
+                    o.x = __byte_perm(q[0], q[1], 0x5410);
+                    o.y = __byte_perm(q[2], q[3], 0x5410);
+                    o.z = __byte_perm(q[0], q[1], 0x7632);
+                    o.w = __byte_perm(q[2], q[3], 0x7632);
                     *reinterpret_cast<uint4*>(dst + ((j ^ (r & 7)) << 4)) = o;
                 }
                 asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
@@ -308,64 +328,98 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (lane == 0) tc_arrive(&S->a_full[so]);
             }
         }
-        // ---- epilogue (warps 0-3: TMEM lanes 32w..32w+31 = weight rows) ----
-        if (warp < 4) {
-            const bool ok = tc_wait(&S->done, 0, S, P.err);
-            tc_fence_after();
-            pdl_wait();
-            const int rr = warp * 32 + lane, n = n0 + rr;
-            const bool live = ok && !*(volatile int*)&S->abort_;
-            if (P.splits == 1) {
+    } else if (warp >= TC_ACC_WARP0) {
+        // ---- per-group scale-accumulate, then the epilogue ----
+        // warp 12+q reads TMEM lanes 32q..32q+31 = weight rows
+        const int q = warp - TC_ACC_WARP0, atid = tid - TC_ACC_WARP0 * 32;
+        const int rr = q * 32 + lane, n = n0 + rr;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        bool ok = true;
+        if (!P.fp16_w) {
+            for (int i = atid; i < TC_ROWS * nk; i += 128) {
+                const int r2 = i / nk, g = i - r2 * nk;
+                SC[g * TC_ROWS + r2] = n0 + r2 < G.N ? G.scales[(size_t)(n0 + r2) * KG + kg0 + g] : __float2half(0.f);
+            }
+            asm volatile("bar.sync 3, 128;\n" ::: "memory");
+            for (int i = 0; i < nk; i++) {
+                if (!(ok = tc_wait(&S->acc_full[i & 1], (i >> 1) & 1, S, P.err))) break;
+                tc_fence_after();
+                const float sc = __half2float(SC[i * TC_ROWS + rr]);
+                const uint32_t ab = lane_base + (uint32_t)((i & 1) * 128);
                 for (int c = 0; c < npad; c += 16) {
-                    float v[16];
-                    tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c, v);
-                    if (!live) continue;
+                    float a[16], y[16];
+                    tc_ld16(ab + c, a);
+                    if (i == 0) {
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        if (c + j >= G.rows) break;
-                        if (n < G.N && G.y) G.y[(size_t)(c + j) * G.ldy + n] = v[j];
-                        if (P.amax) {
-                            unsigned long long key = n < G.N ? argmax_key(v[j], n) : 0ull;
+                        for (int j = 0; j < 16; j++) y[j] = sc * a[j];
+                    } else {
+                        tc_ld16(lane_base + 256 + c, y);
 #pragma unroll
-                            for (int o = 16; o; o >>= 1) key = umax64_dev(key, __shfl_xor_sync(0xffffffffu, key, o));
-                            if (lane == 0) S->amax[warp][c + j] = key;
-                        }
+                        for (int j = 0; j < 16; j++) y[j] = fmaf(sc, a[j], y[j]);
+                    }
+                    tc_st16(lane_base + 256 + c, y);
+                }
+                tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc_arrive(&S->acc_empty[i & 1]);
+            }
+        }
+        const bool done_ok = tc_wait(&S->done, 0, S, P.err);
+        tc_fence_after();
+        pdl_wait();
+        const bool live = ok && done_ok && !*(volatile int*)&S->abort_;
+        const uint32_t res = P.fp16_w ? lane_base : lane_base + 256;
+        if (P.splits == 1) {
+            for (int c = 0; c < npad; c += 16) {
+                float v[16];
+                tc_ld16(res + c, v);
+                if (!live) continue;
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    if (c + j >= G.rows) break;
+                    if (n < G.N && G.y) G.y[(size_t)(c + j) * G.ldy + n] = v[j];
+                    if (P.amax) {
+                        unsigned long long key = n < G.N ? argmax_key(v[j], n) : 0ull;
+#pragma unroll
+                        for (int o = 16; o; o >>= 1) key = umax64_dev(key, __shfl_xor_sync(0xffffffffu, key, o));
+                        if (lane == 0) S->amax[q][c + j] = key;
                     }
                 }
-                if (P.amax) {
-                    asm volatile("bar.sync 2, 128;\n" ::: "memory");
-                    if (live && tid < G.rows) {
-                        unsigned long long k = S->amax[0][tid];
-                        for (int w = 1; w < 4; w++) k = umax64_dev(k, S->amax[w][tid]);
-                        atomicMax(&P.amax[G.x_row + tid], k);
-                    }
+            }
+            if (P.amax) {
+                asm volatile("bar.sync 2, 128;\n" ::: "memory");
+                if (live && atid < G.rows) {
+                    unsigned long long k = S->amax[0][atid];
+                    for (int w = 1; w < 4; w++) k = umax64_dev(k, S->amax[w][atid]);
+                    atomicMax(&P.amax[G.x_row + atid], k);
                 }
-            } else {
-                const size_t tile = (size_t)blockIdx.z * gridDim.x + blockIdx.x;
-                float* mine = P.ws + (tile * P.splits + split) * (size_t)(TC_NMAX * TC_ROWS);
-                for (int c = 0; c < npad; c += 16) {
-                    float v[16];
-                    tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + c, v);
+            }
+        } else {
+            const size_t tile = (size_t)blockIdx.z * gridDim.x + blockIdx.x;
+            float* mine = P.ws + (tile * P.splits + split) * (size_t)(TC_NMAX * TC_ROWS);
+            for (int c = 0; c < npad; c += 16) {
+                float v[16];
+                tc_ld16(res + c, v);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) __stcg(&mine[(c + j) * TC_ROWS + rr], v[j]);
-                }
+                for (int j = 0; j < 16; j++) __stcg(&mine[(c + j) * TC_ROWS + rr], v[j]);
+            }
+            __threadfence();
+            asm volatile("bar.sync 2, 128;\n" ::: "memory");
+            if (atid == 0) {
+                const unsigned t = atomicAdd(&P.counters[tile], 1u);
+                S->last = t == (unsigned)P.splits - 1;
+                if (S->last) P.counters[tile] = 0;  // ready for the next launch
+            }
+            asm volatile("bar.sync 2, 128;\n" ::: "memory");
+            if (S->last && live && n < G.N) {
                 __threadfence();
-                asm volatile("bar.sync 2, 128;\n" ::: "memory");
-                if (tid == 0) {
-                    const unsigned t = atomicAdd(&P.counters[tile], 1u);
-                    S->last = t == (unsigned)P.splits - 1;
-                    if (S->last) P.counters[tile] = 0;  // ready for the next launch
-                }
-                asm volatile("bar.sync 2, 128;\n" ::: "memory");
-                if (S->last && live && n < G.N) {
-                    __threadfence();
-                    const float* base = P.ws + tile * P.splits * (size_t)(TC_NMAX * TC_ROWS);
-                    for (int j = 0; j < G.rows; j++) {
-                        float acc = 0.f;
-                        for (int sp = 0; sp < P.splits; sp++)
-                            acc += __ldcg(&base[sp * (size_t)(TC_NMAX * TC_ROWS) + j * TC_ROWS + rr]);
-                        G.y[(size_t)j * G.ldy + n] = acc;
-                    }
+                const float* base = P.ws + tile * P.splits * (size_t)(TC_NMAX * TC_ROWS);
+                for (int j = 0; j < G.rows; j++) {
+                    float acc = 0.f;
+                    for (int sp = 0; sp < P.splits; sp++)
+                        acc += __ldcg(&base[sp * (size_t)(TC_NMAX * TC_ROWS) + j * TC_ROWS + rr]);
+                    G.y[(size_t)j * G.ldy + n] = acc;
                 }
             }
         }

@@ -191,3 +191,66 @@ class Session:
                                                ctypes.byref(n)))
         return [(names.raw[i * nl:(i + 1) * nl].split(b"\0")[0].decode(), ms[i], by[i])
                 for i in range(n.value)]
+
+
+class Batch:
+    """Sequence-batched decode (cuinf_batch_*): n_seqs independent sequences
+    advance one token per step, all matmuls on the tensor-core GEMMs."""
+
+    def __init__(self, model, n_seqs, max_ctx, stream=None):
+        self.model = model
+        self.n = n_seqs
+        h = ctypes.c_void_p()
+        st = ctypes.c_void_p(stream.cuda_stream) if stream is not None else None
+        check(lib().cuinf_batch_create(model._h, n_seqs, max_ctx, st, ctypes.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            lib().cuinf_batch_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self):
+        check(lib().cuinf_batch_reset(self._h))
+
+    def step(self, tokens=None, want=True):
+        """One step for every sequence; tokens None feeds back each one's
+        previous argmax.  Returns the new argmax per sequence when want."""
+        t = (ctypes.c_int * self.n)(*[int(x) for x in tokens]) if tokens is not None else None
+        o = (ctypes.c_int * self.n)() if want else None
+        check(lib().cuinf_batch_step(self._h, t, o))
+        return list(o) if want else None
+
+    def keep_logits(self, on=True):
+        check(lib().cuinf_batch_keep_logits(self._h, int(on)))
+
+    def logits(self):
+        ptr = lib().cuinf_batch_logits(self._h)
+        return torch.as_tensor(_DevArray(ptr, (self.n, self.model.cfg.vocab), "<f4"), device="cuda")
+
+    def routes(self):
+        """Experts of the last step, int32 [n_moe_layers, n_seqs, top_k]."""
+        import numpy as np
+        c = self.model.cfg
+        r = np.zeros((max(1, c.n_layers - c.n_dense), self.n, c.top_k), np.int32)
+        check(lib().cuinf_batch_routes(self._h, r.ctypes.data))
+        return r
+
+    def fill_synthetic(self, ctx, seed=1):
+        check(lib().cuinf_batch_fill_synthetic(self._h, int(ctx), int(seed)))
+
+    @property
+    def kernels_per_step(self):
+        return lib().cuinf_batch_kernels_per_step(self._h)
+
+    @staticmethod
+    def error():
+        v = ctypes.c_uint(0)
+        check(lib().cuinf_batch_error(ctypes.byref(v)))
+        return v.value

@@ -206,8 +206,9 @@ int cuinf_decode_step(cuinf_session* s, int token, int* out_token);
  * reference, which runs gemv_int4 / gemv_fp16 with grid.y = M,
  * engine.cu:83-128): tcgen05 MMA with the accumulator in TMEM, weights
  * streamed by 2-D TMA.  cuinf_gemm_int4_tc computes the same y[M,N] fp32 as
- * cuinf_gemv_int4, with each dequantized weight (nib-8)*scale rounded once to
- * fp16 before the fp32-accumulated product (relative error < 1e-3).
+ * cuinf_gemv_int4: the MMA sums exact products (nib-8)*x per 128-K group and
+ * each group's sum is scaled in fp32, so results differ from the reference
+ * only by fp32 summation order.
  * cuinf_gemm_fp16_tc: y[M,N] = x[M,K] . W[N,K]^T (y nullable) and, when
  * argmax_keys (device u64 [M], zeroed by the caller) is given, a fused
  * per-row argmax with the reference's tie rule (argmax_kernel, 562-572);
@@ -219,6 +220,31 @@ int cuinf_gemm_int4_tc(const void* x, const uint8_t* packed, const void* scales,
 int cuinf_gemm_fp16_tc(const void* x, const void* W, float* y, int M, int N, int K,
                        unsigned long long* argmax_keys, void* stream);
 int cuinf_argmax_key_index(unsigned long long key);
+/* Sequence-batched decode (single GPU): n_seqs (<= 128)
+ * independent sequences, each with its own FP8 KV cache and conv state,
+ * advance one token per cuinf_batch_step.  Per sequence the arithmetic is
+ * the reference's decode step (layer_forward with S = 1, engine.cu:784-908;
+ * compute_logits_last, 932-940); the projections run on the tensor-core
+ * GEMMs and the MoE experts as grouped GEMMs over the tokens routed to them.
+ * No counterpart in the reference, which decodes one sequence.
+ * tokens (host [n_seqs], nullable: feed back each sequence's last argmax);
+ * out_tokens (host [n_seqs], nullable; synchronizes).  All sequences start at
+ * position 0; cuinf_batch_fill_synthetic sets every sequence to position
+ * ctx over pseudo-random FP8 caches (benchmarking at a context length).
+ * cuinf_batch_routes: host [n_moe_layers][n_seqs][top_k] experts of the last
+ * step.  cuinf_batch_logits: device [n_seqs][vocab] while keep_logits is on. */
+typedef struct cuinf_batch cuinf_batch;
+int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, cuinf_batch** out);
+int cuinf_batch_free(cuinf_batch* b);
+int cuinf_batch_reset(cuinf_batch* b);
+int cuinf_batch_step(cuinf_batch* b, const int* tokens, int* out_tokens);
+int cuinf_batch_keep_logits(cuinf_batch* b, int on);
+const float* cuinf_batch_logits(const cuinf_batch* b);
+int cuinf_batch_routes(cuinf_batch* b, int* idx);
+int cuinf_batch_kernels_per_step(const cuinf_batch* b);
+int cuinf_batch_fill_synthetic(cuinf_batch* b, int ctx, unsigned long long seed);
+/* Error word of the tensor-core kernels (bit 1: a bounded pipeline wait timed out). */
+int cuinf_batch_error(unsigned* flags);
 /* Batched prompt processing, replacing the reference's prefill
  * (src/engine.cu:910-917: layer_forward with S = n_ids, 784-908): every layer
  * runs on all S tokens at positions pos..pos+S-1; each attention layer first

@@ -15,45 +15,13 @@ recurrent KV/conv state carries fp16 one-ulp differences from step to step)
 and the argmax must agree whenever the oracle's top-2 logit margin exceeds
 TIE_MARGIN.
 """
-import zlib
-
 import numpy as np
 import pytest
 
-from oracle import pyoracle as orc
-from cuda_inf_b200 import weights
-from cuda_inf_b200.engine import Model, Session, device_error
+from cuda_inf_b200.engine import Session, device_error
 from enginecheck import check_logits, check_routes, run_compare
 
 pytestmark = pytest.mark.gpu
-
-TINY = dict(hidden=256, n_layers=6, n_heads=4, n_kv_heads=1, vocab=1000, n_dense=1, n_experts=8,
-            top_k=2, moe_inter=256, dense_inter=384, attn_layers=(1, 4))
-
-
-def tiny_tensor(name, shape):
-    rng = np.random.default_rng(zlib.crc32(name.encode()))
-    k = weights.init_kind(name)
-    if k == "norm":
-        return (1 + 0.02 * rng.standard_normal(shape)).astype(np.float32)
-    if k == "bias":
-        return (0.1 * rng.standard_normal(shape)).astype(np.float32)
-    if k == "conv":
-        return rng.uniform(-0.577, 0.577, shape).astype(np.float32)
-    return (0.05 * rng.standard_normal(shape)).astype(np.float32)
-
-
-@pytest.fixture(scope="module")
-def tiny(tmp_path_factory, cuda):
-    d = tmp_path_factory.mktemp("tiny")
-    cfg = weights.make_config(**TINY)
-    weights.write_model(str(d), cfg, tiny_tensor)
-    blob = np.fromfile(d / "weights.bin", np.uint8)
-    index = open(d / "index.bin", "rb").read()
-    om = orc.Model(weights.config_dict(cfg), blob, index)
-    gm = Model.load(str(d), cfg)
-    return cfg, om, gm
-
 
 @pytest.mark.parametrize("mk", [1, 0], ids=["megakernel", "multikernel"])
 def test_engine_matches_oracle_teacher_forced(tiny, mk):

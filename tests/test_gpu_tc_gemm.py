@@ -3,9 +3,11 @@ same op: the INT4 dequant-GEMM y = x . ((nib-8)*scale)^T (gemv_int4,
 engine.cu:83-109, at M activation rows) and the fp16 lm_head GEMM with its
 fused argmax (gemv_fp16 + argmax_kernel, engine.cu:112-128, 562-572).
 
-Tolerance: max-abs error / max-abs reference < 1e-3 (each dequantized
-weight is rounded once to fp16 before the fp32-accumulated MMA).  Split-K
-reduces in a fixed order, so repeated runs are bit-identical.
+Tolerance: max-abs error / max-abs reference < 1e-3 (the contract); the
+INT4 path is in fact exact up to fp32 summation order (the MMA sums exact
+products (nib-8)*x per 128-K group and the fp32 scale is applied per group),
+which the tests hold to 2e-5.  Split-K reduces in a fixed order, so repeated
+runs are bit-identical.
 """
 import numpy as np
 import pytest
@@ -49,7 +51,7 @@ def test_gemm_int4_tc_vs_torch_fp32(cuda, M, N, K):
     torch.cuda.synchronize()
     e = relerr(y, ref)
     print(f"M={M} N={N} K={K}: rel err {e:.2e}")
-    assert e < TOL
+    assert e < TOL and e < 2e-5
     y2 = ops.gemm_int4_tc(x, packed, scales)
     assert torch.equal(y, y2)  # deterministic split-K
 
