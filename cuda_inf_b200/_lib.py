@@ -95,6 +95,7 @@ _SIGS = {
     "cuinf_batch_kernels_per_step": (c_int, [c_void_p]),
     "cuinf_batch_fill_synthetic": (c_int, [c_void_p, c_int, ctypes.c_ulonglong]),
     "cuinf_batch_error": (c_int, [c_void_p]),
+    "cuinf_batch_profile_step": (c_int, [c_void_p, c_int, c_void_p, ctypes.c_char_p, c_int, c_void_p]),
     "cuinf_device_error": (c_int, [ctypes.POINTER(ctypes.c_uint)]),
     "cuinf_session_uses_megakernel": (c_int, [c_void_p]),
     "cuinf_session_trace": (c_int, [c_void_p, c_void_p, c_int, c_void_p, ctypes.POINTER(c_int),

@@ -3,6 +3,7 @@
 // tensor maps and split-K plans.
 #include <math.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -23,12 +24,12 @@ int cuinf_launch_status();
 
 // Device error word of the tensor-core kernels (bit 1: a bounded pipeline
 // wait timed out).
-static __device__ unsigned g_tc_err;
+static __device__ unsigned g_tc_err[4];
 
 unsigned cuinf_tc_error_word() {
-    unsigned v = 0;
-    cudaMemcpyFromSymbol(&v, g_tc_err, sizeof(v));
-    return v;
+    unsigned v[4] = {0, 0, 0, 0};
+    cudaMemcpyFromSymbol(v, g_tc_err, sizeof(v));
+    return v[0];
 }
 
 // ---------------------------------------------------------------------------
@@ -119,8 +120,13 @@ int tc_launch(const CUtensorMap& xmap, const CUtensorMap& wmap, TcParams P, int 
     int rc = tc_attr_once();
     if (rc) return rc;
     P.err = g_tc_err_ptr;
+    P.tiles = tiles;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long items = (long long)P.n_groups * tiles * P.splits;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(tiles, P.splits, P.n_groups);
+    cfg.gridDim = dim3((unsigned)std::min<long long>(items, sms));  // persistent: one CTA per SM at most
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = TC_SMEM_BYTES;
     cfg.stream = st;
@@ -370,7 +376,7 @@ __global__ void k_bconv(const float* __restrict__ z, const __half* __restrict__ 
 // MoE routing of B tokens (engine.cu:883-892, one warp per token) and the
 // expert grouping: rows of the gathered activation buffer are ordered by
 // expert, then by token; each expert's rows form up to maxch groups of 128.
-// One CTA of 256 threads; E <= 256.
+// One CTA of 1024 threads; E <= 256, B * topk <= 1024.
 struct BRouteParams {
     const float* logits;  // [B][E]
     const __half* bias;
@@ -385,54 +391,67 @@ struct BRouteParams {
     void* const* experts;     // [E][6]: w1 packed, w1 scales, w3 .., w2 ..
     float *gbuf, *ubuf, *obuf;
 };
-__global__ void __launch_bounds__(256) k_broute(const BRouteParams P) {
+__global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
+    __shared__ int sidx[1024];
     __shared__ int cnt[256], off[256];
-    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, n = P.B * P.topk;
+    for (int e = threadIdx.x; e < P.E; e += blockDim.x) cnt[e] = 0;
     for (int b = warp; b < P.B; b += nw)
         route_select_warp(P.logits + (size_t)b * P.E, P.bias, P.E, P.topk, P.ridx + b * P.topk, P.rw + b * P.topk);
     __syncthreads();
-    const int n = P.B * P.topk, e = threadIdx.x;
-    if (e < P.E) {
-        int c = 0;
-        for (int j = 0; j < n; j++) c += P.ridx[j] == e;
-        cnt[e] = c;
+    // rank of entry j among the entries of its expert that come before it
+    int e = -1, rank = 0;
+    if (threadIdx.x < n) {
+        e = P.ridx[threadIdx.x];
+        sidx[threadIdx.x] = e;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int s = 0;
-        for (int i = 0; i < P.E; i++) {
-            off[i] = s;
-            s += cnt[i];
+    if (e >= 0) {
+        for (int j = 0; j < (int)threadIdx.x; j++) rank += sidx[j] == e;
+        atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {  // exclusive prefix over experts, one warp
+        int carry = 0;
+        for (int base = 0; base < P.E; base += 32) {
+            const int i = base + threadIdx.x;
+            const int v = i < P.E ? cnt[i] : 0;
+            int x = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if ((int)threadIdx.x >= o) x += y;
+            }
+            if (i < P.E) off[i] = carry + x - v;
+            carry += __shfl_sync(0xffffffffu, x, 31);
         }
     }
     __syncthreads();
-    if (e < P.E) {
-        int k = off[e];
-        for (int j = 0; j < n; j++)
-            if (P.ridx[j] == e) {
-                P.inv[j] = k;
-                P.src[k] = j / P.topk;
-                k++;
-            }
+    if (e >= 0) {
+        const int row = off[e] + rank;
+        P.inv[threadIdx.x] = row;
+        P.src[row] = threadIdx.x / P.topk;
+    }
+    for (int ex = threadIdx.x; ex < P.E; ex += blockDim.x) {
         for (int c = 0; c < P.maxch; c++) {
-            const int r0 = off[e] + c * TC_NMAX;
-            const int rows = max(0, min(TC_NMAX, cnt[e] - c * TC_NMAX));
-            const int gi = e * P.maxch + c;
+            const int r0 = off[ex] + c * TC_NMAX;
+            const int rows = max(0, min(TC_NMAX, cnt[ex] - c * TC_NMAX));
+            const int gi = ex * P.maxch + c;
             TcGroup a;
-            a.wmap = P.maps + e * 3 + 0;
-            a.scales = (const __half*)P.experts[e * 6 + 1];
+            a.wmap = P.maps + ex * 3 + 0;
+            a.scales = (const __half*)P.experts[ex * 6 + 1];
             a.y = P.gbuf + (size_t)r0 * P.I;
             a.x_row = r0;
             a.rows = rows;
             a.N = P.I;
             a.ldy = P.I;
             P.g13[gi] = a;
-            a.wmap = P.maps + e * 3 + 1;
-            a.scales = (const __half*)P.experts[e * 6 + 3];
+            a.wmap = P.maps + ex * 3 + 1;
+            a.scales = (const __half*)P.experts[ex * 6 + 3];
             a.y = P.ubuf + (size_t)r0 * P.I;
             P.g13[P.E * P.maxch + gi] = a;
-            a.wmap = P.maps + e * 3 + 2;
-            a.scales = (const __half*)P.experts[e * 6 + 5];
+            a.wmap = P.maps + ex * 3 + 2;
+            a.scales = (const __half*)P.experts[ex * 6 + 5];
             a.y = P.obuf + (size_t)r0 * P.H;
             a.N = P.H;
             a.ldy = P.H;
@@ -504,6 +523,22 @@ struct BStep {
     bool dry;  // size the split-K workspace only
     size_t need_slots = 0, need_cnt = 0;
     int launches = 0;
+    // eager profiling: an event after each launch, with the launch's name
+    std::vector<std::pair<const char*, cudaEvent_t>>* prof = nullptr;
+    bool trace = false;  // eager profiling only: synchronize and report each launch
+    int mark(const char* name) {
+        if (dry || !prof) return CUINF_OK;
+        cudaEvent_t e;
+        CUINF_TRY(cudaEventCreate(&e));
+        CUINF_TRY(cudaEventRecord(e, b->st));
+        prof->push_back({name, e});
+        if (trace) {
+            CUINF_TRY(cudaStreamSynchronize(b->st));
+            fprintf(stderr, "[cuinf batch] %3zu %s done\n", prof->size(), name);
+            fflush(stderr);
+        }
+        return CUINF_OK;
+    }
 
     int gemm(const CUtensorMap& xm, int wmap_idx, const TcGroup* dg, TcGroup g0, int ngroups, int tiles, int K,
              int active_ctas, bool fp16w, unsigned long long* amax) {
@@ -559,10 +594,12 @@ static int batch_record(cuinf_batch* b, BStep& S) {
     const bool dry = S.dry;
     auto run = [&](int rc) { return dry ? CUINF_OK : rc; };
     BTRY(S.ew(run(cuinf_embed_gather(m->embed, b->tok, b->h, B, H, vs))));
+    BTRY(S.mark("embed"));
     int moe_i = 0;
     for (int l = 0; l < c.n_layers; l++) {
         const LayerW& L = m->L[l];
         BTRY(S.ew(run(cuinf_rmsnorm(b->h, L.op_norm, b->xn, B, H, c.norm_eps, vs))));
+        BTRY(S.mark("rmsnorm"));
         if (c.attn_layer[l]) {
             const AttnState& A = b->attn[l];
             float* qf = b->fqkv;
@@ -574,15 +611,21 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             const int tiles = (NQ + TC_ROWS - 1) / TC_ROWS;
             const int active = tiles + 2 * ((NK + TC_ROWS - 1) / TC_ROWS);
             BTRY(S.gemm(b->x_h, -1, b->dstatic + b->qkv_tab[l], TcGroup{}, 3, tiles, H, active, false, nullptr));
+            BTRY(S.mark("gemm_qkv"));
             BTRY(S.ew(run(cuinf_f32_to_f16(qf, q16, B * (NQ + 2 * NK), vs))));
+            BTRY(S.mark("f32_to_f16"));
             BTRY(S.ew(run(cuinf_rmsnorm(q16, L.q_ln, q16, B * nh, 64, c.norm_eps, vs))));
+            BTRY(S.mark("rmsnorm_q"));
             BTRY(S.ew(run(cuinf_rmsnorm(k16, L.k_ln, k16, B * nkv, 64, c.norm_eps, vs))));
+            BTRY(S.mark("rmsnorm_k"));
             BTRY(S.ew(run(cuinf_rope(q16, k16, b->pos, B, nh, nkv, c.rope_theta, vs))));
+            BTRY(S.mark("rope"));
             S.launches++;
             if (!dry) {
                 k_bkv_place<<<dim3(B, nkv), 256, 0, b->st>>>(k16, v16, b->pos, A.ktail, A.vtail, A.kc8, A.vc8, A.ksc,
                                                              A.vsc, nkv, b->tail_seq, b->kv8_seq, b->sc_seq);
                 BTRY(cuinf_launch_status());
+                BTRY(S.mark("kv_place"));
             }
             BatchAttnArgs a;
             a.q = q16;
@@ -608,27 +651,39 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             a.bpart = attn_batched_part_floats(nh, nkv, b->nsplit);
             a.scale = 0.125f;
             BTRY(S.ew(run(attn_decode_batched(a, b->st))));
+            BTRY(S.mark("attention"));
             BTRY(S.gemm1(b->x_attn, b->mi_o[l], L.wo.s, b->fa, H, NQ));
+            BTRY(S.mark("gemm_o"));
         } else {
             BTRY(S.gemm1(b->x_h, b->mi_in[l], L.in_proj.s, b->fa, 3 * H, H));
+            BTRY(S.mark("gemm_conv_in"));
             S.launches++;
             if (!dry) {
                 k_bconv<<<(B * H + 255) / 256, 256, 0, b->st>>>(b->fa, L.conv_w, b->conv_state[l], b->conv_y, B, H);
                 BTRY(cuinf_launch_status());
+                BTRY(S.mark("conv"));
             }
             BTRY(S.gemm1(b->x_conv, b->mi_out[l], L.out_proj.s, b->fa, H, H));
+            BTRY(S.mark("gemm_conv_out"));
         }
         BTRY(S.ew(run(cuinf_add_f32_inplace(b->h, b->fa, B * H, vs))));
+        BTRY(S.mark("residual"));
         BTRY(S.ew(run(cuinf_rmsnorm(b->h, L.ffn_norm, b->xn, B, H, c.norm_eps, vs))));
+        BTRY(S.mark("rmsnorm"));
         if (l < c.n_dense) {
             const int I = c.dense_inter, tiles = (I + TC_ROWS - 1) / TC_ROWS;
             BTRY(S.gemm(b->x_h, -1, b->dstatic + b->d13_tab[l], TcGroup{}, 2, tiles, H, 2 * tiles, false, nullptr));
+            BTRY(S.mark("gemm_dense_w13"));
             BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->dmid, B * I, vs))));
+            BTRY(S.mark("swiglu"));
             BTRY(S.gemm1(b->x_dmid, b->mi_w2[l], L.w2.s, b->fa, H, I));
+            BTRY(S.mark("gemm_dense_w2"));
             BTRY(S.ew(run(cuinf_add_f32_inplace(b->h, b->fa, B * H, vs))));
+            BTRY(S.mark("residual"));
         } else {
             const int I = c.moe_inter;
             BTRY(S.ew(run(cuinf_gemv_fp16(b->xn, L.gate, b->rlog, B, E, H, vs))));
+            BTRY(S.mark("router_gemv"));
             S.launches++;
             if (!dry) {
                 BRouteParams R;
@@ -651,34 +706,43 @@ static int batch_record(cuinf_batch* b, BStep& S) {
                 R.gbuf = b->fg;
                 R.ubuf = b->fu;
                 R.obuf = b->fo;
-                k_broute<<<1, 256, 0, b->st>>>(R);
+                k_broute<<<1, 1024, 0, b->st>>>(R);
                 BTRY(cuinf_launch_status());
+                BTRY(S.mark("route_group"));
                 k_bgather<<<B * K, 256, 0, b->st>>>(b->xn, b->src, b->xg, H);
                 BTRY(cuinf_launch_status());
+                BTRY(S.mark("gather"));
             }
             S.launches++;
             const int t13 = (I + TC_ROWS - 1) / TC_ROWS, t2 = (H + TC_ROWS - 1) / TC_ROWS;
             // about min(E, B*K) experts are hit; each group is one tile row of CTAs
             const int hit = std::min(E, B * K);
             BTRY(S.gemm(b->x_xg, -1, b->g13, TcGroup{}, 2 * E * maxch, t13, H, 2 * hit * t13, false, nullptr));
+            BTRY(S.mark("gemm_moe_w13"));
             BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->mmid, B * K * I, vs))));
+            BTRY(S.mark("swiglu_moe"));
             BTRY(S.gemm(b->x_mmid, -1, b->g2, TcGroup{}, E * maxch, t2, I, hit * t2, false, nullptr));
+            BTRY(S.mark("gemm_moe_w2"));
             S.launches++;
             if (!dry) {
                 k_bcombine<<<(B * H + 255) / 256, 256, 0, b->st>>>(b->fo, b->inv, b->rw, b->h, B, H, K);
                 BTRY(cuinf_launch_status());
+                BTRY(S.mark("combine"));
             }
             moe_i++;
         }
     }
     // final norm, lm_head with the fused argmax (compute_logits_last, engine.cu:932-940)
     BTRY(S.ew(run(cuinf_rmsnorm(b->h, m->emb_norm, b->xn, B, H, c.norm_eps, vs))));
+    BTRY(S.mark("rmsnorm_final"));
     if (!dry) CUINF_TRY(cudaMemsetAsync(b->amax, 0, (size_t)B * 8, b->st));
     BTRY(S.gemm1(b->x_h, b->mi_embed, nullptr, b->keep_logits ? b->logits : nullptr, c.vocab, H, true, b->amax));
+    BTRY(S.mark("lm_head"));
     S.launches++;
     if (!dry) {
         k_btok<<<(B + 127) / 128, 128, 0, b->st>>>(b->amax, b->tok, b->pos, B);
         BTRY(cuinf_launch_status());
+        BTRY(S.mark("next_token"));
     }
     return CUINF_OK;
 }
@@ -743,7 +807,7 @@ extern "C" int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void*
     REQUIRE(c.hidden % TC_KS == 0 && c.moe_inter % TC_KS == 0 && c.dense_inter % TC_KS == 0 &&
                 (c.n_heads * 64) % TC_KS == 0,
             "batched decode needs hidden, intermediates and heads*64 multiples of 128");
-    REQUIRE(c.n_experts <= 256 && c.top_k <= 8, "n_experts <= 256, top_k <= 8");
+    REQUIRE(c.n_experts <= 256 && c.top_k <= 8 && n_seqs * c.top_k <= 1024, "n_experts <= 256, top_k <= 8");
     REQUIRE(c.n_heads % c.n_kv_heads == 0 && c.n_heads / c.n_kv_heads <= 8, "GQA ratio <= 8");
     cuinf_batch* b = new cuinf_batch();
     b->m = m;
@@ -817,7 +881,7 @@ extern "C" int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void*
     TRYB(balloc(b, &b->inv, (size_t)B * K * 4));
     TRYB(balloc(b, &b->src, (size_t)B * K * 4));
     TRYB(balloc(b, &b->amax, (size_t)B * 8));
-    b->nsplit = attn_batched_nsplit(c.n_heads, nkv, max_ctx);
+    b->nsplit = attn_batched_nsplit(c.n_heads, nkv, max_ctx, B, b->num_sms);
     TRYB(balloc(b, &b->apart, (size_t)B * attn_batched_part_floats(c.n_heads, nkv, b->nsplit) * 4));
     TRYB(balloc(b, &b->acnt, (size_t)B * nkv * 4));
     const int maxch = (B + TC_NMAX - 1) / TC_NMAX;
@@ -983,9 +1047,7 @@ extern "C" int cuinf_batch_routes(cuinf_batch* b, int* idx) {
 extern "C" int cuinf_batch_kernels_per_step(const cuinf_batch* b) { return b ? b->kernels : -1; }
 extern "C" int cuinf_batch_error(unsigned* flags) {
     REQUIRE(flags, "null pointer");
-    unsigned v = 0;
-    CUINF_TRY(cudaMemcpyFromSymbol(&v, g_tc_err, sizeof(v)));
-    *flags = v;
+    CUINF_TRY(cudaMemcpyFromSymbol(flags, g_tc_err, 4 * sizeof(unsigned)));
     return CUINF_OK;
 }
 
@@ -1012,5 +1074,41 @@ extern "C" int cuinf_batch_fill_synthetic(cuinf_batch* b, int ctx, unsigned long
     k_bset<<<(b->B + 127) / 128, 128, 0, b->st>>>(b->pos, b->B, ctx);
     CUINF_TRY(cudaGetLastError());
     CUINF_TRY(cudaStreamSynchronize(b->st));
+    return CUINF_OK;
+}
+
+// One step launched eagerly with an event after every launch: ms[i] is the
+// duration of launch i (names[i * name_len] its name).  Advances the batch
+// like cuinf_batch_step(b, NULL, NULL).
+extern "C" int cuinf_batch_profile_step(cuinf_batch* b, int max_kernels, float* ms, char* names, int name_len,
+                                        int* n_kernels) {
+    REQUIRE(b && ms && names && n_kernels && name_len > 0, "null pointer");
+    CUINF_TRY(cudaStreamSynchronize(b->st));
+    std::vector<std::pair<const char*, cudaEvent_t>> ev;
+    cudaEvent_t e0;
+    CUINF_TRY(cudaEventCreate(&e0));
+    CUINF_TRY(cudaEventRecord(e0, b->st));
+    BStep S{b, false};
+    S.prof = &ev;
+    S.trace = getenv("CUINF_BATCH_TRACE") != nullptr;
+    int rc = batch_record(b, S);
+    cudaError_t se = cudaStreamSynchronize(b->st);
+    int n = 0;
+    if (rc == CUINF_OK && se == cudaSuccess) {
+        cudaEvent_t prev = e0;
+        for (auto& pe : ev) {
+            if (n < max_kernels) {
+                cudaEventElapsedTime(&ms[n], prev, pe.second);
+                snprintf(names + (size_t)n * name_len, name_len, "%s", pe.first);
+                n++;
+            }
+            prev = pe.second;
+        }
+    }
+    for (auto& pe : ev) cudaEventDestroy(pe.second);
+    cudaEventDestroy(e0);
+    if (rc) return rc;
+    CUINF_TRY(se);
+    *n_kernels = n;
     return CUINF_OK;
 }

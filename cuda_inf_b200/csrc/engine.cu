@@ -111,8 +111,12 @@ extern "C" int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_
 }
 
 // Batched form for the sequence-batched engine (batch.cu).
-int attn_batched_nsplit(int nh, int nkv, int max_ctx) {
-    return attn_engine_nsplit(nh / nkv, (max_ctx + CUINF_KVGROUP - 1) / CUINF_KVGROUP);
+// Splits per (sequence, kv head): about two CTAs per SM over the whole batch,
+// never more than the single-sequence engine uses at this context.
+int attn_batched_nsplit(int nh, int nkv, int max_ctx, int n_seqs, int num_sms) {
+    const int cap = attn_engine_nsplit(nh / nkv, (max_ctx + CUINF_KVGROUP - 1) / CUINF_KVGROUP);
+    const int want = (2 * num_sms + n_seqs * nkv - 1) / (n_seqs * nkv);
+    return std::max(1, std::min(cap, want));
 }
 size_t attn_batched_part_floats(int nh, int nkv, int nsplit) {
     return (size_t)nkv * nsplit * (nh / nkv) * ATTN_PART_STRIDE;

@@ -61,5 +61,5 @@ struct BatchAttnArgs {
     float scale;
 };
 int attn_decode_batched(const BatchAttnArgs& a, cudaStream_t st);
-int attn_batched_nsplit(int nh, int nkv, int max_ctx);
+int attn_batched_nsplit(int nh, int nkv, int max_ctx, int n_seqs, int num_sms);
 size_t attn_batched_part_floats(int nh, int nkv, int nsplit);

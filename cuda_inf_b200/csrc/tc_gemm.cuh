@@ -32,15 +32,17 @@
 #define TC_ROWS 128
 #define TC_KS 128
 #define TC_NMAX 128
-#define TC_PST 6
-#define TC_OST 2
+#define TC_PST 8   // packed-weight ring (INT4)
+#define TC_OST 2   // operand stages (A + X) with INT4 weights
+#define TC_OST16 3 // operand stages with fp16 weights (the packed ring's room)
 #define TC_DQ_WARPS 8
 #define TC_ACC_WARP0 12
 #define TC_THREADS ((TC_ACC_WARP0 + 4) * 32)
 #define TC_A_BYTES (TC_ROWS * TC_KS * 2)  // 32 KB: two 64-K swizzle atoms
 #define TC_X_BYTES (TC_NMAX * TC_KS * 2)  // 32 KB
 #define TC_P_BYTES (TC_ROWS * TC_KS / 2)  // 8 KB packed
-#define TC_MAX_KG 64                      // scale groups per split held in smem (K range <= 8192)
+#define TC_MAX_KG 64                      // scale groups per split (K range <= 8192)
+#define TC_STAGE_BYTES (TC_A_BYTES + TC_X_BYTES)
 #define TC_TMEM_COLS 512  // group accumulators at columns 0 and 128, the sum at 256
 
 struct TcGroup {
@@ -57,6 +59,7 @@ struct TcParams {
     const TcGroup* groups;  // device table, or null: one group, g0
     TcGroup g0;
     int n_groups;
+    int tiles;                     // 128-row tiles per group (of the largest N)
     int K;
     int splits, kg_per_split;
     int fp16_w;                    // weights are fp16 [N, K] (no dequantization)
@@ -68,8 +71,9 @@ struct TcParams {
 
 struct TcSmem {
     uint64_t p_full[TC_PST], p_empty[TC_PST];
-    uint64_t a_full[TC_OST], x_full[TC_OST], op_empty[TC_OST];
+    uint64_t a_full[TC_OST16], x_full[TC_OST16], op_empty[TC_OST16];
     uint64_t acc_full[2], acc_empty[2];
+    uint64_t epi;  // the four epilogue warps' own barrier (bounded, unlike bar.sync)
     uint64_t done;
     uint32_t tmem;
     int abort_;
@@ -77,9 +81,10 @@ struct TcSmem {
     unsigned long long amax[4][TC_NMAX];
 };
 
-static constexpr size_t TC_SMEM_BYTES =
-    1024 + TC_OST * (size_t)(TC_A_BYTES + TC_X_BYTES) + TC_PST * (size_t)TC_P_BYTES +
-    (size_t)TC_ROWS * TC_MAX_KG * 2 + sizeof(TcSmem);
+// INT4: two operand stages then the packed ring; fp16: three operand stages.
+static constexpr size_t TC_RING_BYTES = TC_OST * (size_t)TC_STAGE_BYTES + TC_PST * (size_t)TC_P_BYTES;
+static_assert(TC_OST16 * (size_t)TC_STAGE_BYTES <= TC_RING_BYTES, "fp16 stages must fit the ring");
+static constexpr size_t TC_SMEM_BYTES = 1024 + TC_RING_BYTES + sizeof(TcSmem);
 
 __device__ __forceinline__ void tc_tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -147,51 +152,75 @@ __device__ __forceinline__ void tc_st16(uint32_t taddr, const float (&v)[16]) {
 }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
+// A pipeline wait in these kernels takes microseconds; one that lasts this
+// long has failed.
+#define TC_WAIT_LIMIT_NS 200000000ull
 // Bounded wait that also gives up as soon as another role of the CTA has.
-__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, TcSmem* S, unsigned* err) {
+// The first failure records err[1] = where (barrier code), err[2] = block,
+// err[3] = the waiter's stage counter.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, TcSmem* S, unsigned* err, unsigned where = 0,
+                                        unsigned ctr = 0) {
     if (mbar_test_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
         if (mbar_test_wait(bar, parity)) return true;
         if (*(volatile int*)&S->abort_) return false;
-        if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) break;
+        if (globaltimer_ns() - t0 > TC_WAIT_LIMIT_NS) break;
         __nanosleep(20);
     }
     *(volatile int*)&S->abort_ = 1;
-    if (err) atomicOr(err, 2u);
+    if (err && (atomicOr(err, 2u) & 2u) == 0) {
+        err[1] = where;
+        err[2] = blockIdx.x;
+        err[3] = ctr;
+    }
     return false;
 }
 // Final drain: wait for a phase regardless of the abort flag (bounded).
 __device__ __forceinline__ void tc_drain(uint64_t* bar, uint32_t parity, unsigned* err) {
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_test_wait(bar, parity)) {
-        if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) {
-            if (err) atomicOr(err, 2u);
+        if (globaltimer_ns() - t0 > TC_WAIT_LIMIT_NS) {
+            if (err) atomicOr(err, 4u);
             return;
         }
         __nanosleep(20);
     }
 }
 
+// One work item = (group, 128-row tile, K split); CTA c takes items c,
+// c + gridDim.x, ...  Items of empty groups (rows == 0) or beyond a group's N
+// are skipped by every role alike.
+struct TcItem {
+    TcGroup G;
+    int g, tile, split, n0, kg0, nk, npad;
+};
+__device__ __forceinline__ bool tc_item(const TcParams& P, int it, int KG, TcItem& t) {
+    t.split = it % P.splits;
+    const int gt = it / P.splits;
+    t.tile = gt % P.tiles;
+    t.g = gt / P.tiles;
+    t.G = P.groups ? P.groups[t.g] : P.g0;
+    t.n0 = t.tile * TC_ROWS;
+    if (t.G.rows <= 0 || t.n0 >= t.G.N) return false;
+    t.kg0 = t.split * P.kg_per_split;
+    t.nk = min(KG, t.kg0 + P.kg_per_split) - t.kg0;
+    t.npad = (t.G.rows + 15) & ~15;
+    return t.nk > 0;
+}
+
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap0, const TcParams P) {
     extern __shared__ __align__(1024) unsigned char tc_raw[];
-    const TcGroup G = P.groups ? P.groups[blockIdx.z] : P.g0;
-    const int n0 = blockIdx.x * TC_ROWS;
-    if (G.rows <= 0 || n0 >= G.N) return;
-    const CUtensorMap* wmap = G.wmap ? G.wmap : &wmap0;
     const int KG = P.K / TC_KS;
-    const int split = blockIdx.y;
-    const int kg0 = split * P.kg_per_split;
-    const int nk = min(KG, kg0 + P.kg_per_split) - kg0;
-    const int npad = (G.rows + 15) & ~15;
+    const int n_items = P.n_groups * P.tiles * P.splits;
+    const int ost = P.fp16_w ? TC_OST16 : TC_OST;
 
     unsigned char* sm = tc_raw + ((1024 - (smem_u32(tc_raw) & 1023)) & 1023);
-    unsigned char* A = sm;
-    unsigned char* X = A + TC_OST * TC_A_BYTES;
-    unsigned char* PK = X + TC_OST * TC_X_BYTES;
-    __half* SC = reinterpret_cast<__half*>(PK + TC_PST * TC_P_BYTES);
-    TcSmem* S = reinterpret_cast<TcSmem*>(SC + TC_ROWS * TC_MAX_KG);
+    unsigned char* PK = sm + TC_OST * TC_STAGE_BYTES;  // INT4 only
+    TcSmem* S = reinterpret_cast<TcSmem*>(sm + TC_RING_BYTES);
+    auto A_of = [&](int s) { return sm + (size_t)s * TC_STAGE_BYTES; };
+    auto X_of = [&](int s) { return sm + (size_t)s * TC_STAGE_BYTES + TC_A_BYTES; };
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
@@ -199,7 +228,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&S->p_full[i], 1);
             mbar_init(&S->p_empty[i], TC_DQ_WARPS);
         }
-        for (int i = 0; i < TC_OST; i++) {
+        for (int i = 0; i < TC_OST16; i++) {
             mbar_init(&S->a_full[i], P.fp16_w ? 1 : TC_DQ_WARPS);
             mbar_init(&S->x_full[i], 1);
             mbar_init(&S->op_empty[i], 1);
@@ -208,6 +237,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&S->acc_full[i], 1);
             mbar_init(&S->acc_empty[i], 4);
         }
+        mbar_init(&S->epi, 4);
         mbar_init(&S->done, 1);
         S->abort_ = 0;
     }
@@ -226,72 +256,97 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---- weight producer ----
         if (lane == 0) {
             const uint64_t pol = l2_policy_evict_first();
-            int last[TC_PST > TC_OST ? TC_PST : TC_OST];
+            int last[TC_PST];
             for (int s = 0; s < TC_PST; s++) last[s] = -1;
+            uint32_t pc = 0;
             bool ok = true;
-            for (int i = 0; i < nk && ok; i++) {
-                const int kg = kg0 + i;
-                if (P.fp16_w) {
-                    const int s = i % TC_OST;
-                    if (!(ok = tc_wait(&S->op_empty[s], ((i / TC_OST) & 1) ^ 1, S, P.err))) break;
-                    mbar_arrive_expect_tx(&S->a_full[s], TC_A_BYTES);
-                    tc_tma_2d_hint(A + s * TC_A_BYTES, wmap, kg * TC_KS, n0, &S->a_full[s], pol);
-                    tc_tma_2d_hint(A + s * TC_A_BYTES + TC_A_BYTES / 2, wmap, kg * TC_KS + 64, n0, &S->a_full[s], pol);
-                    last[s] = i;
-                } else {
-                    const int s = i % TC_PST;
-                    if (!(ok = tc_wait(&S->p_empty[s], ((i / TC_PST) & 1) ^ 1, S, P.err))) break;
-                    mbar_arrive_expect_tx(&S->p_full[s], TC_P_BYTES);
-                    tc_tma_2d_hint(PK + s * TC_P_BYTES, wmap, kg * (TC_KS / 2), n0, &S->p_full[s], pol);
-                    last[s] = i;
+            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+                TcItem t;
+                if (!tc_item(P, it, KG, t)) continue;
+                const CUtensorMap* wm = t.G.wmap ? t.G.wmap : &wmap0;
+                for (int i = 0; i < t.nk; i++, pc++) {
+                    const int kg = t.kg0 + i;
+                    if (P.fp16_w) {
+                        const int s = pc % ost;
+                        if (!(ok = tc_wait(&S->op_empty[s], ((pc / ost) & 1) ^ 1, S, P.err, 10 + s, pc))) break;
+                        mbar_arrive_expect_tx(&S->a_full[s], TC_A_BYTES);
+                        tc_tma_2d_hint(A_of(s), wm, kg * TC_KS, t.n0, &S->a_full[s], pol);
+                        tc_tma_2d_hint(A_of(s) + TC_A_BYTES / 2, wm, kg * TC_KS + 64, t.n0, &S->a_full[s], pol);
+                        last[s] = (int)pc;
+                    } else {
+                        const int s = pc % TC_PST;
+                        if (!(ok = tc_wait(&S->p_empty[s], ((pc / TC_PST) & 1) ^ 1, S, P.err, 20 + s, pc))) break;
+                        mbar_arrive_expect_tx(&S->p_full[s], TC_P_BYTES);
+                        tc_tma_2d_hint(PK + s * TC_P_BYTES, wm, kg * (TC_KS / 2), t.n0, &S->p_full[s], pol);
+                        last[s] = (int)pc;
+                    }
                 }
             }
             // copies still in flight land before the CTA can exit
-            const int depth = P.fp16_w ? TC_OST : TC_PST;
+            const int depth = P.fp16_w ? ost : TC_PST;
             for (int s = 0; s < depth; s++)
-                if (last[s] >= 0)
-                    tc_drain(P.fp16_w ? &S->a_full[s] : &S->p_full[s], (last[s] / depth) & 1, P.err);
+                if (last[s] >= 0) tc_drain(P.fp16_w ? &S->a_full[s] : &S->p_full[s], (last[s] / depth) & 1, P.err);
         }
     } else if (warp == TC_DQ_WARPS + 1) {
         // ---- activation producer ----
         if (lane == 0) {
             pdl_wait();
-            int last[TC_OST] = {-1, -1};
-            for (int i = 0; i < nk; i++) {
-                const int s = i % TC_OST;
-                if (!tc_wait(&S->op_empty[s], ((i / TC_OST) & 1) ^ 1, S, P.err)) break;
-                mbar_arrive_expect_tx(&S->x_full[s], (uint32_t)npad * TC_KS * 2);
-                const int kx = (kg0 + i) * TC_KS;
-                for (int a = 0; a < 2; a++)
-                    for (int b = 0; b < npad / 16; b++)
-                        tc_tma_2d(X + s * TC_X_BYTES + a * (TC_X_BYTES / 2) + b * 2048, &xmap, kx + 64 * a,
-                                  G.x_row + 16 * b, &S->x_full[s]);
-                last[s] = i;
+            int last[TC_OST16] = {-1, -1, -1};
+            uint32_t oc = 0;
+            bool ok = true;
+            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+                TcItem t;
+                if (!tc_item(P, it, KG, t)) continue;
+                for (int i = 0; i < t.nk; i++, oc++) {
+                    const int s = oc % ost;
+                    if (!(ok = tc_wait(&S->op_empty[s], ((oc / ost) & 1) ^ 1, S, P.err, 30 + s, oc))) break;
+                    mbar_arrive_expect_tx(&S->x_full[s], (uint32_t)t.npad * TC_KS * 2);
+                    const int kx = (t.kg0 + i) * TC_KS;
+                    for (int a = 0; a < 2; a++)
+                        for (int b = 0; b < t.npad / 16; b++)
+                            tc_tma_2d(X_of(s) + a * (TC_X_BYTES / 2) + b * 2048, &xmap, kx + 64 * a, t.G.x_row + 16 * b,
+                                      &S->x_full[s]);
+                    last[s] = (int)oc;
+                }
             }
-            for (int s = 0; s < TC_OST; s++)
-                if (last[s] >= 0) tc_drain(&S->x_full[s], (last[s] / TC_OST) & 1, P.err);
+            for (int s = 0; s < ost; s++)
+                if (last[s] >= 0) tc_drain(&S->x_full[s], (last[s] / ost) & 1, P.err);
         }
     } else if (warp == TC_DQ_WARPS + 2) {
         // ---- MMA issuer ----
         if (lane == 0) {
-            const uint32_t idesc = tc_idesc(npad);
-            for (int i = 0; i < nk; i++) {
-                const int s = i % TC_OST;
-                const uint32_t ph = (i / TC_OST) & 1;
-                if (!tc_wait(&S->a_full[s], ph, S, P.err) || !tc_wait(&S->x_full[s], ph, S, P.err)) break;
-                // INT4: the group accumulator i%2 must have been read back (stage i-2)
-                if (!P.fp16_w && !tc_wait(&S->acc_empty[i & 1], ((i >> 1) & 1) ^ 1, S, P.err)) break;
-                tc_fence_after();
-                const uint32_t d = P.fp16_w ? tmem : tmem + (uint32_t)((i & 1) * 128);
-#pragma unroll
-                for (int kk = 0; kk < TC_KS / 16; kk++) {
-                    const int off = (kk >> 2) * (TC_A_BYTES / 2) + (kk & 3) * 32;
-                    const int xoff = (kk >> 2) * (TC_X_BYTES / 2) + (kk & 3) * 32;
-                    tc_mma(d, tc_desc_sw128(A + s * TC_A_BYTES + off), tc_desc_sw128(X + s * TC_X_BYTES + xoff),
-                           idesc, P.fp16_w ? (i | kk) != 0 : kk != 0);
+            uint32_t oc = 0, ac = 0, ic = 0;
+            bool ok = true;
+            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+                TcItem t;
+                if (!tc_item(P, it, KG, t)) continue;
+                const uint32_t idesc = tc_idesc(t.npad);
+                uint32_t d = 0;
+                if (P.fp16_w) {  // the item accumulates in region ic&1, free once read back
+                    if (!(ok = tc_wait(&S->acc_empty[ic & 1], ((ic >> 1) & 1) ^ 1, S, P.err, 40 + (ic & 1), ic))) break;
+                    d = tmem + (uint32_t)((ic & 1) * 128);
                 }
-                tc_commit(&S->op_empty[s]);
-                if (!P.fp16_w) tc_commit(&S->acc_full[i & 1]);
+                for (int i = 0; i < t.nk; i++, oc++) {
+                    const int s = oc % ost;
+                    const uint32_t ph = (oc / ost) & 1;
+                    if (!(ok = tc_wait(&S->a_full[s], ph, S, P.err, 50 + s, oc) && tc_wait(&S->x_full[s], ph, S, P.err, 60 + s, oc)))
+                        break;
+                    if (!P.fp16_w) {  // INT4: one accumulator per scale group, read back by the scale warps
+                        if (!(ok = tc_wait(&S->acc_empty[ac & 1], ((ac >> 1) & 1) ^ 1, S, P.err, 70 + (ac & 1), ac))) break;
+                        d = tmem + (uint32_t)((ac & 1) * 128);
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < TC_KS / 16; kk++) {
+                        const int off = (kk >> 2) * (TC_A_BYTES / 2) + (kk & 3) * 32;
+                        const int xoff = (kk >> 2) * (TC_X_BYTES / 2) + (kk & 3) * 32;
+                        tc_mma(d, tc_desc_sw128(A_of(s) + off), tc_desc_sw128(X_of(s) + xoff), idesc,
+                               P.fp16_w ? (i | kk) != 0 : kk != 0);
+                    }
+                    tc_commit(&S->op_empty[s]);
+                    if (!P.fp16_w) tc_commit(&S->acc_full[(ac++) & 1]);
+                }
+                if (ok && P.fp16_w) tc_commit(&S->acc_full[(ic++) & 1]);
             }
             tc_commit(&S->done);  // tracks every MMA issued above
         }
@@ -299,128 +354,172 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---- dequantization (INT4 weights) to exact (nib-8) ----
         const int r = tid & (TC_ROWS - 1), h = tid >> 7;
         if (!P.fp16_w) {
-            for (int i = 0; i < nk; i++) {
-                const int s = i % TC_PST;
-                if (!tc_wait(&S->p_full[s], (i / TC_PST) & 1, S, P.err)) break;
-                const unsigned char* row = PK + s * TC_P_BYTES + r * 64;
-                const int sw = (r >> 1) & 3;
-                const uint4 c0 = *reinterpret_cast<const uint4*>(row + (((2 * h) ^ sw) << 4));
-                const uint4 c1 = *reinterpret_cast<const uint4*>(row + (((2 * h + 1) ^ sw) << 4));
-                __syncwarp();
-                if (lane == 0) tc_arrive(&S->p_empty[s]);
-                const int so = i % TC_OST;
-                if (!tc_wait(&S->op_empty[so], ((i / TC_OST) & 1) ^ 1, S, P.err)) break;
-                unsigned char* dst = A + so * TC_A_BYTES + h * (TC_A_BYTES / 2) + r * 128;
-                const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            uint32_t pc = 0, oc = 0;
+            bool ok = true;
+            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+                TcItem t;
+                if (!tc_item(P, it, KG, t)) continue;
+                for (int i = 0; i < t.nk; i++, pc++, oc++) {
+                    const int s = pc % TC_PST;
+                    if (!(ok = tc_wait(&S->p_full[s], (pc / TC_PST) & 1, S, P.err, 80 + s, pc))) break;
+                    const unsigned char* row = PK + s * TC_P_BYTES + r * 64;
+                    const int sw = (r >> 1) & 3;
+                    const uint4 c0 = *reinterpret_cast<const uint4*>(row + (((2 * h) ^ sw) << 4));
+                    const uint4 c1 = *reinterpret_cast<const uint4*>(row + (((2 * h + 1) ^ sw) << 4));
+                    __syncwarp();
+                    if (lane == 0) tc_arrive(&S->p_empty[s]);
+                    const int so = oc % TC_OST;
+                    if (!(ok = tc_wait(&S->op_empty[so], ((oc / TC_OST) & 1) ^ 1, S, P.err, 90 + so, oc))) break;
+                    unsigned char* dst = A_of(so) + h * (TC_A_BYTES / 2) + r * 128;
+                    const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    uint32_t q[4];
-                    dequant8(w[j], q);  // (k0,k4) (k1,k5) (k2,k6) (k3,k7)
-                    uint4 o;
-                    o.x = __byte_perm(q[0], q[1], 0x5410);
-                    o.y = __byte_perm(q[2], q[3], 0x5410);
-                    o.z = __byte_perm(q[0], q[1], 0x7632);
-                    o.w = __byte_perm(q[2], q[3], 0x7632);
-                    *reinterpret_cast<uint4*>(dst + ((j ^ (r & 7)) << 4)) = o;
+                    for (int j = 0; j < 8; j++) {
+                        uint32_t q[4];
+                        dequant8(w[j], q);  // (k0,k4) (k1,k5) (k2,k6) (k3,k7)
+                        uint4 o;
+                        o.x = __byte_perm(q[0], q[1], 0x5410);
+                        o.y = __byte_perm(q[2], q[3], 0x5410);
+                        o.z = __byte_perm(q[0], q[1], 0x7632);
+                        o.w = __byte_perm(q[2], q[3], 0x7632);
+                        *reinterpret_cast<uint4*>(dst + ((j ^ (r & 7)) << 4)) = o;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) tc_arrive(&S->a_full[so]);
                 }
-                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-                __syncwarp();
-                if (lane == 0) tc_arrive(&S->a_full[so]);
             }
         }
     } else if (warp >= TC_ACC_WARP0) {
-        // ---- per-group scale-accumulate, then the epilogue ----
+        // ---- per-group scale-accumulate, then the epilogue of each item ----
         // warp 12+q reads TMEM lanes 32q..32q+31 = weight rows
         const int q = warp - TC_ACC_WARP0, atid = tid - TC_ACC_WARP0 * 32;
-        const int rr = q * 32 + lane, n = n0 + rr;
+        const int rr = q * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-        bool ok = true;
-        if (!P.fp16_w) {
-            for (int i = atid; i < TC_ROWS * nk; i += 128) {
-                const int r2 = i / nk, g = i - r2 * nk;
-                SC[g * TC_ROWS + r2] = n0 + r2 < G.N ? G.scales[(size_t)(n0 + r2) * KG + kg0 + g] : __float2half(0.f);
-            }
-            asm volatile("bar.sync 3, 128;\n" ::: "memory");
-            for (int i = 0; i < nk; i++) {
-                if (!(ok = tc_wait(&S->acc_full[i & 1], (i >> 1) & 1, S, P.err))) break;
-                tc_fence_after();
-                const float sc = __half2float(SC[i * TC_ROWS + rr]);
-                const uint32_t ab = lane_base + (uint32_t)((i & 1) * 128);
-                for (int c = 0; c < npad; c += 16) {
-                    float a[16], y[16];
-                    tc_ld16(ab + c, a);
-                    if (i == 0) {
+        uint32_t ac = 0, ic = 0, ek = 0;
+        bool ok = true, waited = false;
+        // bounded barrier of the four epilogue warps (gives up on abort)
+        auto sync4 = [&]() -> bool {
+            __syncwarp();
+            if (lane == 0) tc_arrive(&S->epi);
+            const bool r = tc_wait(&S->epi, ek & 1, S, P.err, 120, ek);
+            ek++;
+            return r;
+        };
+        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+            TcItem t;
+            if (!tc_item(P, it, KG, t)) continue;
+            const TcGroup& G = t.G;
+            const int n = t.n0 + rr;
+            uint32_t res;
+            if (!P.fp16_w) {
+                const __half* srow = G.scales + (size_t)min(n, G.N - 1) * KG + t.kg0;
+                float sc_next = n < G.N ? __half2float(__ldg(srow)) : 0.f;
+                for (int i = 0; i < t.nk; i++, ac++) {
+                    const float sc = sc_next;
+                    if (i + 1 < t.nk) sc_next = n < G.N ? __half2float(__ldg(srow + i + 1)) : 0.f;
+                    if (!(ok = tc_wait(&S->acc_full[ac & 1], (ac >> 1) & 1, S, P.err, 100 + (ac & 1), ac))) break;
+                    tc_fence_after();
+                    const uint32_t ab = lane_base + (uint32_t)((ac & 1) * 128);
+                    for (int c = 0; c < t.npad; c += 16) {
+                        float a[16], y[16];
+                        tc_ld16(ab + c, a);
+                        if (i == 0) {
 #pragma unroll
-                        for (int j = 0; j < 16; j++) y[j] = sc * a[j];
-                    } else {
-                        tc_ld16(lane_base + 256 + c, y);
+                            for (int j = 0; j < 16; j++) y[j] = sc * a[j];
+                        } else {
+                            tc_ld16(lane_base + 256 + c, y);
 #pragma unroll
-                        for (int j = 0; j < 16; j++) y[j] = fmaf(sc, a[j], y[j]);
+                            for (int j = 0; j < 16; j++) y[j] = fmaf(sc, a[j], y[j]);
+                        }
+                        tc_st16(lane_base + 256 + c, y);
                     }
-                    tc_st16(lane_base + 256 + c, y);
+                    tc_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc_arrive(&S->acc_empty[ac & 1]);
                 }
-                tc_wait_st();
+                if (!ok) break;
+                res = lane_base + 256;
+            } else {
+                if (!(ok = tc_wait(&S->acc_full[ic & 1], (ic >> 1) & 1, S, P.err, 110 + (ic & 1), ic))) break;
+                tc_fence_after();
+                res = lane_base + (uint32_t)((ic & 1) * 128);
+            }
+            if (!waited) {
+                pdl_wait();
+                waited = true;
+            }
+            const bool live = !*(volatile int*)&S->abort_;
+            if (P.splits == 1) {
+                for (int c = 0; c < t.npad; c += 16) {
+                    float v[16];
+                    tc_ld16(res + c, v);
+                    if (!live) continue;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        if (c + j >= G.rows) break;
+                        if (n < G.N && G.y) G.y[(size_t)(c + j) * G.ldy + n] = v[j];
+                        if (P.amax) {
+                            unsigned long long key = n < G.N ? argmax_key(v[j], n) : 0ull;
+#pragma unroll
+                            for (int o = 16; o; o >>= 1) key = umax64_dev(key, __shfl_xor_sync(0xffffffffu, key, o));
+                            if (lane == 0) S->amax[q][c + j] = key;
+                        }
+                    }
+                }
+                if (P.amax) {
+                    if (!(ok = sync4())) break;
+                    if (live && atid < G.rows) {
+                        unsigned long long k = S->amax[0][atid];
+                        for (int w = 1; w < 4; w++) k = umax64_dev(k, S->amax[w][atid]);
+                        atomicMax(&P.amax[G.x_row + atid], k);
+                    }
+                    if (!(ok = sync4())) break;  // S->amax is reused by the next item
+                }
+            } else {
+                const size_t tile = (size_t)t.g * P.tiles + t.tile;
+                const size_t SLOT = (size_t)TC_NMAX * TC_ROWS;
+                float* mine = P.ws + (tile * P.splits + t.split) * SLOT;
+                for (int c = 0; c < t.npad; c += 16) {
+                    float v[16];
+                    tc_ld16(res + c, v);
+#pragma unroll
+                    for (int j = 0; j < 16; j++) __stcg(&mine[(c + j) * TC_ROWS + rr], v[j]);
+                }
+                __threadfence();
+                if (!(ok = sync4())) break;
+                if (atid == 0) {
+                    const unsigned tk = atomicAdd(&P.counters[tile], 1u);
+                    S->last = tk == (unsigned)P.splits - 1;
+                    if (S->last) P.counters[tile] = 0;  // ready for the next launch
+                }
+                if (!(ok = sync4())) break;
+                if (S->last && live && n < G.N) {
+                    __threadfence();
+                    const float* base = P.ws + tile * P.splits * SLOT;
+                    for (int j0 = 0; j0 < G.rows; j0 += 8) {
+                        float acc[8];
+#pragma unroll
+                        for (int u = 0; u < 8; u++) acc[u] = 0.f;
+                        for (int sp = 0; sp < P.splits; sp++) {
+                            float v[8];
+#pragma unroll
+                            for (int u = 0; u < 8; u++)
+                                v[u] = j0 + u < G.rows ? __ldcg(&base[sp * SLOT + (size_t)(j0 + u) * TC_ROWS + rr]) : 0.f;
+#pragma unroll
+                            for (int u = 0; u < 8; u++) acc[u] += v[u];
+                        }
+#pragma unroll
+                        for (int u = 0; u < 8; u++)
+                            if (j0 + u < G.rows) G.y[(size_t)(j0 + u) * G.ldy + n] = acc[u];
+                    }
+                }
+            }
+            if (P.fp16_w) {  // every lane advances ic; lane 0 arrives for the warp
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) tc_arrive(&S->acc_empty[i & 1]);
-            }
-        }
-        const bool done_ok = tc_wait(&S->done, 0, S, P.err);
-        tc_fence_after();
-        pdl_wait();
-        const bool live = ok && done_ok && !*(volatile int*)&S->abort_;
-        const uint32_t res = P.fp16_w ? lane_base : lane_base + 256;
-        if (P.splits == 1) {
-            for (int c = 0; c < npad; c += 16) {
-                float v[16];
-                tc_ld16(res + c, v);
-                if (!live) continue;
-#pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    if (c + j >= G.rows) break;
-                    if (n < G.N && G.y) G.y[(size_t)(c + j) * G.ldy + n] = v[j];
-                    if (P.amax) {
-                        unsigned long long key = n < G.N ? argmax_key(v[j], n) : 0ull;
-#pragma unroll
-                        for (int o = 16; o; o >>= 1) key = umax64_dev(key, __shfl_xor_sync(0xffffffffu, key, o));
-                        if (lane == 0) S->amax[q][c + j] = key;
-                    }
-                }
-            }
-            if (P.amax) {
-                asm volatile("bar.sync 2, 128;\n" ::: "memory");
-                if (live && atid < G.rows) {
-                    unsigned long long k = S->amax[0][atid];
-                    for (int w = 1; w < 4; w++) k = umax64_dev(k, S->amax[w][atid]);
-                    atomicMax(&P.amax[G.x_row + atid], k);
-                }
-            }
-        } else {
-            const size_t tile = (size_t)blockIdx.z * gridDim.x + blockIdx.x;
-            float* mine = P.ws + (tile * P.splits + split) * (size_t)(TC_NMAX * TC_ROWS);
-            for (int c = 0; c < npad; c += 16) {
-                float v[16];
-                tc_ld16(res + c, v);
-#pragma unroll
-                for (int j = 0; j < 16; j++) __stcg(&mine[(c + j) * TC_ROWS + rr], v[j]);
-            }
-            __threadfence();
-            asm volatile("bar.sync 2, 128;\n" ::: "memory");
-            if (atid == 0) {
-                const unsigned t = atomicAdd(&P.counters[tile], 1u);
-                S->last = t == (unsigned)P.splits - 1;
-                if (S->last) P.counters[tile] = 0;  // ready for the next launch
-            }
-            asm volatile("bar.sync 2, 128;\n" ::: "memory");
-            if (S->last && live && n < G.N) {
-                __threadfence();
-                const float* base = P.ws + tile * P.splits * (size_t)(TC_NMAX * TC_ROWS);
-                for (int j = 0; j < G.rows; j++) {
-                    float acc = 0.f;
-                    for (int sp = 0; sp < P.splits; sp++)
-                        acc += __ldcg(&base[sp * (size_t)(TC_NMAX * TC_ROWS) + j * TC_ROWS + rr]);
-                    G.y[(size_t)j * G.ldy + n] = acc;
-                }
+                if (lane == 0) tc_arrive(&S->acc_empty[ic & 1]);
+                ic++;
             }
         }
     }

@@ -250,7 +250,18 @@ class Batch:
         return lib().cuinf_batch_kernels_per_step(self._h)
 
     @staticmethod
-    def error():
-        v = ctypes.c_uint(0)
-        check(lib().cuinf_batch_error(ctypes.byref(v)))
-        return v.value
+    def error(detail=False):
+        """Tensor-core kernel error flags (0 = none); detail=True returns
+        (flags, barrier code, block, stage counter) of the first failure."""
+        v = (ctypes.c_uint * 4)()
+        check(lib().cuinf_batch_error(v))
+        return tuple(v) if detail else v[0]
+
+    def profile_step(self, max_kernels=4096, name_len=32):
+        """Eager step with per-launch CUDA-event timing: [(name, ms)]."""
+        ms = (ctypes.c_float * max_kernels)()
+        names = ctypes.create_string_buffer(max_kernels * name_len)
+        n = ctypes.c_int(0)
+        check(lib().cuinf_batch_profile_step(self._h, max_kernels, ms, names, name_len, ctypes.byref(n)))
+        raw = names.raw
+        return [(raw[i * name_len:(i + 1) * name_len].split(b"\0")[0].decode(), ms[i]) for i in range(n.value)]

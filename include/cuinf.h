@@ -243,8 +243,14 @@ const float* cuinf_batch_logits(const cuinf_batch* b);
 int cuinf_batch_routes(cuinf_batch* b, int* idx);
 int cuinf_batch_kernels_per_step(const cuinf_batch* b);
 int cuinf_batch_fill_synthetic(cuinf_batch* b, int ctx, unsigned long long seed);
-/* Error word of the tensor-core kernels (bit 1: a bounded pipeline wait timed out). */
+/* Error words of the tensor-core kernels, flags[4]: [0] bit 1 a bounded
+ * pipeline wait timed out, bit 2 a final drain did; [1] the wait's barrier
+ * code, [2] its block, [3] its stage counter (first failure). */
 int cuinf_batch_error(unsigned* flags);
+/* One step launched eagerly with an event after each launch: ms[i] is the
+ * duration of launch i, names[i * name_len] its name; advances the batch. */
+int cuinf_batch_profile_step(cuinf_batch* b, int max_kernels, float* ms, char* names, int name_len,
+                             int* n_kernels);
 /* Batched prompt processing, replacing the reference's prefill
  * (src/engine.cu:910-917: layer_forward with S = n_ids, 784-908): every layer
  * runs on all S tokens at positions pos..pos+S-1; each attention layer first

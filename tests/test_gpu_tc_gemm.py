@@ -7,7 +7,8 @@ Tolerance: max-abs error / max-abs reference < 1e-3 (the contract); the
 INT4 path is in fact exact up to fp32 summation order (the MMA sums exact
 products (nib-8)*x per 128-K group and the fp32 scale is applied per group),
 which the tests hold to 2e-5.  Split-K reduces in a fixed order, so repeated
-runs are bit-identical.
+runs are bit-identical.  Shapes with more than 148 tiles give a CTA several
+work items and more than 8 K stages per item (the packed ring wraps).
 """
 import numpy as np
 import pytest
@@ -15,6 +16,7 @@ import torch
 
 from oracle import pyoracle as orc
 from cuda_inf_b200 import ops
+from cuda_inf_b200.engine import Batch
 
 pytestmark = pytest.mark.gpu
 
@@ -43,7 +45,8 @@ def dequant_f32(packed, scales):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 7168, 2048), (64, 6144, 2048), (64, 2048, 7168), (37, 1000, 256),
-                                   (128, 512, 2048), (200, 1792, 2048), (16, 128, 128), (8, 2048, 1792)])
+                                   (128, 512, 2048), (200, 1792, 2048), (16, 128, 128), (8, 2048, 1792),
+                                   (64, 20480, 2048), (24, 19200, 1536)])
 def test_gemm_int4_tc_vs_torch_fp32(cuda, M, N, K):
     packed, scales, x = int4_case(M * 1000 + N + K, M, N, K, cuda)
     ref = x.float() @ dequant_f32(packed, scales).t()
@@ -54,6 +57,7 @@ def test_gemm_int4_tc_vs_torch_fp32(cuda, M, N, K):
     assert e < TOL and e < 2e-5
     y2 = ops.gemm_int4_tc(x, packed, scales)
     assert torch.equal(y, y2)  # deterministic split-K
+    assert Batch.error() == 0
 
 
 def test_gemm_int4_tc_vs_oracle(cuda):
@@ -64,7 +68,8 @@ def test_gemm_int4_tc_vs_oracle(cuda):
     assert relerr(y, torch.from_numpy(np.asarray(ref))) < TOL
 
 
-@pytest.mark.parametrize("M,N,K", [(64, 4196, 2048), (3, 1000, 256), (128, 640, 128)])
+@pytest.mark.parametrize("M,N,K", [(64, 4196, 2048), (3, 1000, 256), (128, 640, 128), (64, 25600, 2048),
+                                   (64, 64000, 2048)])
 def test_gemm_fp16_tc_argmax(cuda, M, N, K):
     g = torch.Generator().manual_seed(M + N + K)
     W = (0.02 * torch.randn(N, K, generator=g)).half().to(cuda)
@@ -76,3 +81,4 @@ def test_gemm_fp16_tc_argmax(cuda, M, N, K):
     assert idx == torch.argmax(y, dim=1).tolist()  # the argmax of its own logits
     _, idx2 = ops.gemm_fp16_tc(x, W, want_logits=False)
     assert idx2 == idx
+    assert Batch.error() == 0
