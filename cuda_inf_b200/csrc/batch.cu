@@ -26,6 +26,12 @@ int cuinf_launch_status();
 // wait timed out).
 static __device__ unsigned g_tc_err[4];
 
+#ifdef TC_TRACE
+extern "C" int cuinf_tc_trace_read(unsigned long long* out) {
+    return cudaMemcpyFromSymbol(out, g_tc_trace, sizeof(g_tc_trace)) == cudaSuccess ? 0 : 1;
+}
+#endif
+
 unsigned cuinf_tc_error_word() {
     unsigned v[4] = {0, 0, 0, 0};
     cudaMemcpyFromSymbol(v, g_tc_err, sizeof(v));
@@ -75,15 +81,16 @@ int tc_map_int4(CUtensorMap* m, const uint8_t* packed, int N, int K) {
     return tmap_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, packed, (uint64_t)K / 2, N, TC_KS / 2, TC_ROWS,
                    CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 }
+// fp16 activations [rows][K]: box 64 x box_rows (16..128, a multiple of 16),
+// 128-byte swizzle (the B operand)
+int tc_map_act(CUtensorMap* m, const __half* x, int rows, int K, int box_rows) {
+    return tmap_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, rows, 64, box_rows, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
+}
 // fp16 weights [N][K]: box 64 x 128 rows, 128-byte swizzle (the A operand)
 int tc_map_f16w(CUtensorMap* m, const __half* W, int N, int K) {
     return tmap_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, W, K, N, 64, TC_ROWS, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
-}
-// fp16 activations [rows][K]: box 64 x 16 rows, 128-byte swizzle (the B operand)
-int tc_map_act(CUtensorMap* m, const __half* x, int rows, int K) {
-    return tmap_2d(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x, K, rows, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
 }
 
 // Split-K plan: enough CTAs to cover the SMs once, each split holding at
@@ -181,7 +188,8 @@ static int tc_gemm_op(const void* x, const void* w, const void* scales, float* y
     REQUIRE(K % TC_KS == 0, "K must be a multiple of 128");
     REQUIRE(fp16_w || scales, "null scales");
     CUtensorMap xm, wm;
-    int rc = tc_map_act(&xm, (const __half*)x, M, K);
+    const int xmax = (std::min(M, TC_NMAX) + 15) & ~15;  // one box covers a launch's rows
+    int rc = tc_map_act(&xm, (const __half*)x, M, K, xmax);
     if (rc) return rc;
     rc = fp16_w ? tc_map_f16w(&wm, (const __half*)w, N, K) : tc_map_int4(&wm, (const uint8_t*)w, N, K);
     if (rc) return rc;
@@ -209,6 +217,8 @@ static int tc_gemm_op(const void* x, const void* w, const void* scales, float* y
         P.splits = pl.splits;
         P.kg_per_split = pl.kgps;
         P.fp16_w = fp16_w;
+        P.xmax = xmax;
+        P.xbox = xmax;
         P.ws = ws;
         P.counters = cnt;
         P.amax = amax;
@@ -277,8 +287,8 @@ struct cuinf_batch {
     CUtensorMap* dmaps = nullptr;    // same, device
     TcGroup* dstatic = nullptr;      // q/k/v and dense w1/w3 group tables
     std::vector<int> qkv_tab, d13_tab;
+    CUtensorMap x_h, x_conv, x_attn, x_dmid, x_xg, x_mmid;  // activation maps
     TcGroup *g13 = nullptr, *g2 = nullptr;  // MoE group tables, rewritten per layer
-    CUtensorMap x_h, x_conv, x_attn, x_dmid, x_xg, x_mmid;
     std::vector<int> mi_in, mi_out, mi_q, mi_k, mi_v, mi_o, mi_w1, mi_w3, mi_w2;
     std::vector<int> mi_experts;  // per MoE layer: index of expert 0's w1 map (then w3, w2, next expert)
     int mi_embed = -1;
@@ -540,8 +550,8 @@ struct BStep {
         return CUINF_OK;
     }
 
-    int gemm(const CUtensorMap& xm, int wmap_idx, const TcGroup* dg, TcGroup g0, int ngroups, int tiles, int K,
-             int active_ctas, bool fp16w, unsigned long long* amax) {
+    int gemm(const CUtensorMap& xm, int xbox, int wmap_idx, const TcGroup* dg, TcGroup g0, int ngroups, int tiles,
+             int K, int active_ctas, bool fp16w, unsigned long long* amax) {
         TcPlan pl = amax ? TcPlan{1, K / TC_KS} : tc_plan(active_ctas, K, b->num_sms);
         REQUIRE(fp16w || pl.kgps <= TC_MAX_KG, "K too large");
         launches++;
@@ -558,6 +568,8 @@ struct BStep {
         P.splits = pl.splits;
         P.kg_per_split = pl.kgps;
         P.fp16_w = fp16w;
+        P.xmax = (std::min(b->B, TC_NMAX) + 15) & ~15;  // no group has more rows than the batch
+        P.xbox = xbox;
         P.ws = b->ws;
         P.counters = b->cnt;
         P.amax = amax;
@@ -576,7 +588,7 @@ struct BStep {
         g.N = N;
         g.ldy = N;
         const int tiles = (N + TC_ROWS - 1) / TC_ROWS;
-        return gemm(xm, wi, nullptr, g, 1, tiles, K, tiles, fp16w, amax);
+        return gemm(xm, (b->B + 15) & ~15, wi, nullptr, g, 1, tiles, K, tiles, fp16w, amax);
     }
     int ew(int rc) {
         launches++;
@@ -610,7 +622,8 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             __half* v16 = k16 + (size_t)B * NK;
             const int tiles = (NQ + TC_ROWS - 1) / TC_ROWS;
             const int active = tiles + 2 * ((NK + TC_ROWS - 1) / TC_ROWS);
-            BTRY(S.gemm(b->x_h, -1, b->dstatic + b->qkv_tab[l], TcGroup{}, 3, tiles, H, active, false, nullptr));
+            BTRY(S.gemm(b->x_h, (B + 15) & ~15, -1, b->dstatic + b->qkv_tab[l], TcGroup{}, 3, tiles, H, active, false,
+                        nullptr));
             BTRY(S.mark("gemm_qkv"));
             BTRY(S.ew(run(cuinf_f32_to_f16(qf, q16, B * (NQ + 2 * NK), vs))));
             BTRY(S.mark("f32_to_f16"));
@@ -672,7 +685,8 @@ static int batch_record(cuinf_batch* b, BStep& S) {
         BTRY(S.mark("rmsnorm"));
         if (l < c.n_dense) {
             const int I = c.dense_inter, tiles = (I + TC_ROWS - 1) / TC_ROWS;
-            BTRY(S.gemm(b->x_h, -1, b->dstatic + b->d13_tab[l], TcGroup{}, 2, tiles, H, 2 * tiles, false, nullptr));
+            BTRY(S.gemm(b->x_h, (B + 15) & ~15, -1, b->dstatic + b->d13_tab[l], TcGroup{}, 2, tiles, H, 2 * tiles,
+                        false, nullptr));
             BTRY(S.mark("gemm_dense_w13"));
             BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->dmid, B * I, vs))));
             BTRY(S.mark("swiglu"));
@@ -717,11 +731,11 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             const int t13 = (I + TC_ROWS - 1) / TC_ROWS, t2 = (H + TC_ROWS - 1) / TC_ROWS;
             // about min(E, B*K) experts are hit; each group is one tile row of CTAs
             const int hit = std::min(E, B * K);
-            BTRY(S.gemm(b->x_xg, -1, b->g13, TcGroup{}, 2 * E * maxch, t13, H, 2 * hit * t13, false, nullptr));
+            BTRY(S.gemm(b->x_xg, 16, -1, b->g13, TcGroup{}, 2 * E * maxch, t13, H, 2 * hit * t13, false, nullptr));
             BTRY(S.mark("gemm_moe_w13"));
             BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->mmid, B * K * I, vs))));
             BTRY(S.mark("swiglu_moe"));
-            BTRY(S.gemm(b->x_mmid, -1, b->g2, TcGroup{}, E * maxch, t2, I, hit * t2, false, nullptr));
+            BTRY(S.gemm(b->x_mmid, 16, -1, b->g2, TcGroup{}, E * maxch, t2, I, hit * t2, false, nullptr));
             BTRY(S.mark("gemm_moe_w2"));
             S.launches++;
             if (!dry) {
@@ -891,13 +905,14 @@ extern "C" int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void*
         cuinf_batch_free(b);
         return cuinf_set_arg_error("pinned allocation failed");
     }
-    // activation maps
-    TRYB(tc_map_act(&b->x_h, b->xn, B, H));
-    TRYB(tc_map_act(&b->x_conv, b->conv_y, B, H));
-    TRYB(tc_map_act(&b->x_attn, b->attn_out, B, NQ));
-    TRYB(tc_map_act(&b->x_dmid, b->dmid, B, std::max(ID, 128)));
-    TRYB(tc_map_act(&b->x_xg, b->xg, B * K, H));
-    TRYB(tc_map_act(&b->x_mmid, b->mmid, B * K, I));
+    // activation maps: shared layers one box over the batch, expert groups 16-row boxes
+    const int xb = (B + 15) & ~15;
+    TRYB(tc_map_act(&b->x_h, b->xn, B, H, xb));
+    TRYB(tc_map_act(&b->x_conv, b->conv_y, B, H, xb));
+    TRYB(tc_map_act(&b->x_attn, b->attn_out, B, NQ, xb));
+    TRYB(tc_map_act(&b->x_dmid, b->dmid, B, ID, xb));
+    TRYB(tc_map_act(&b->x_xg, b->xg, B * K, H, 16));
+    TRYB(tc_map_act(&b->x_mmid, b->mmid, B * K, I, 16));
     // weight maps
     auto add4 = [&](const Q4& q, int N, int Kd, int* idx) -> int {
         CUtensorMap mm;

@@ -105,6 +105,18 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Potentially blocking test of phase `parity`: the thread may be suspended in
+// hardware until the phase completes or a short system time limit passes, and
+// resumes as soon as the phase completes (no sleep granularity).
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
@@ -118,12 +130,11 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // its math but still waits (bounded) before exiting so no copy targets freed
 // shared memory.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* flag) {
-    if (mbar_test_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    for (;;) {
-        if (mbar_test_wait(bar, parity)) return true;
-        if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) break;
-        __nanosleep(32);
+    for (int k = 1;; k++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((k & 7) == 0 && globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) break;
     }
     if (flag) atomicOr(flag, 1u);
     return false;

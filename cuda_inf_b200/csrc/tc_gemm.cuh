@@ -8,15 +8,15 @@
 //   warp 8   TMA producer of the packed INT4 rows (2-D tensor map, box
 //            64 bytes x 128 rows, 64-byte swizzle) into a 6-deep ring; for
 //            fp16 weights it loads the A operand directly (128-byte swizzle);
-//   warp 9   TMA producer of the activation rows (box 64 halves x 16 rows,
-//            128-byte swizzle, which is the K-major UMMA layout);
+//   warp 9   TMA producer of the activation rows (box 64 halves x xbox
+//            rows, 128-byte swizzle, which is the K-major UMMA layout);
 //   warps 0-7 dequantize 128 K (one scale group) per stage to (nib-8),
 //            exact in fp16 via the 1024-magic, written in the
 //            128-byte-swizzled K-major layout;
 //   warp 10  allocates TMEM and one thread issues tcgen05.mma.kind::f16
 //            (M=128, N=rows rounded up to 16, K=16): each stage's 8 MMAs sum
-//            exact products (nib-8)*x into one of two per-group accumulators
-//            (128 lanes x 128 fp32 columns each);
+//            exact products (nib-8)*x into one of three per-group
+//            accumulators (128 lanes x 128 fp32 columns each);
 //   warps 12-15 (lane = weight row, column = activation row) read each
 //            group's sum with tcgen05.ld, multiply it by the row's fp32
 //            scale and add it into a third TMEM region, so the result is the
@@ -32,18 +32,16 @@
 #define TC_ROWS 128
 #define TC_KS 128
 #define TC_NMAX 128
-#define TC_PST 8   // packed-weight ring (INT4)
-#define TC_OST 2   // operand stages (A + X) with INT4 weights
-#define TC_OST16 3 // operand stages with fp16 weights (the packed ring's room)
+#define TC_PST 8    // packed-weight ring (INT4)
+#define TC_OSTMAX 4 // operand stages (A + X): up to 3 with INT4 weights, 4 with fp16
+#define TC_NACC 3   // INT4 per-group accumulators in TMEM (the sum follows them)
 #define TC_DQ_WARPS 8
 #define TC_ACC_WARP0 12
 #define TC_THREADS ((TC_ACC_WARP0 + 4) * 32)
 #define TC_A_BYTES (TC_ROWS * TC_KS * 2)  // 32 KB: two 64-K swizzle atoms
-#define TC_X_BYTES (TC_NMAX * TC_KS * 2)  // 32 KB
 #define TC_P_BYTES (TC_ROWS * TC_KS / 2)  // 8 KB packed
 #define TC_MAX_KG 64                      // scale groups per split (K range <= 8192)
-#define TC_STAGE_BYTES (TC_A_BYTES + TC_X_BYTES)
-#define TC_TMEM_COLS 512  // group accumulators at columns 0 and 128, the sum at 256
+#define TC_TMEM_COLS 512  // accumulators at columns 0, 128, 256; the INT4 sum at 384
 
 struct TcGroup {
     const CUtensorMap* wmap;  // weights (global-memory tensor map); null = the launch's own map
@@ -63,6 +61,8 @@ struct TcParams {
     int K;
     int splits, kg_per_split;
     int fp16_w;                    // weights are fp16 [N, K] (no dequantization)
+    int xmax;                      // activation rows of the largest group, rounded up to 16
+    int xbox;                      // rows per activation TMA box (the map's box height; divides xmax)
     float* ws;                     // split-K partials [slot][TC_NMAX][TC_ROWS]
     unsigned* counters;            // per (group, tile) arrival counters, self-resetting
     unsigned long long* amax;      // optional per activation row argmax key (lm_head)
@@ -71,8 +71,8 @@ struct TcParams {
 
 struct TcSmem {
     uint64_t p_full[TC_PST], p_empty[TC_PST];
-    uint64_t a_full[TC_OST16], x_full[TC_OST16], op_empty[TC_OST16];
-    uint64_t acc_full[2], acc_empty[2];
+    uint64_t a_full[TC_OSTMAX], x_full[TC_OSTMAX], op_empty[TC_OSTMAX];
+    uint64_t acc_full[TC_NACC], acc_empty[TC_NACC];
     uint64_t epi;  // the four epilogue warps' own barrier (bounded, unlike bar.sync)
     uint64_t done;
     uint32_t tmem;
@@ -81,10 +81,16 @@ struct TcSmem {
     unsigned long long amax[4][TC_NMAX];
 };
 
-// INT4: two operand stages then the packed ring; fp16: three operand stages.
-static constexpr size_t TC_RING_BYTES = TC_OST * (size_t)TC_STAGE_BYTES + TC_PST * (size_t)TC_P_BYTES;
-static_assert(TC_OST16 * (size_t)TC_STAGE_BYTES <= TC_RING_BYTES, "fp16 stages must fit the ring");
+// INT4: operand stages (A 32 KB + X xmax*256 B each) in the first
+// TC_OPS_BYTES, then the packed ring; fp16: operand stages over the whole ring.
+static constexpr size_t TC_OPS_BYTES = 144 * 1024;
+static constexpr size_t TC_RING_BYTES = TC_OPS_BYTES + TC_PST * (size_t)TC_P_BYTES;
 static constexpr size_t TC_SMEM_BYTES = 1024 + TC_RING_BYTES + sizeof(TcSmem);
+__host__ __device__ inline int tc_op_stages(int fp16_w, int xmax) {
+    const size_t st = TC_A_BYTES + (size_t)xmax * TC_KS * 2;
+    const int n = (int)((fp16_w ? TC_RING_BYTES : TC_OPS_BYTES) / st);
+    return n < TC_OSTMAX ? n : TC_OSTMAX;
+}
 
 __device__ __forceinline__ void tc_tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -100,6 +106,9 @@ __device__ __forceinline__ void tc_tma_2d_hint(void* dst, const CUtensorMap* map
         "[%1, {%2, %3}], [%4], %5;\n" ::"r"(smem_u32(dst)),
         "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
+}
+__device__ __forceinline__ void tc_prefetch_map(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(map) : "memory");
 }
 __device__ __forceinline__ void tc_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
@@ -139,6 +148,15 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
+// tcgen05.ld of 16 columns without the wait (tc_wait_ld before use).
+__device__ __forceinline__ void tc_ld16_issue(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_st16(uint32_t taddr, const float (&v)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
@@ -160,13 +178,14 @@ __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sy
 // err[3] = the waiter's stage counter.
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, TcSmem* S, unsigned* err, unsigned where = 0,
                                         unsigned ctr = 0) {
-    if (mbar_test_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
-    for (;;) {
-        if (mbar_test_wait(bar, parity)) return true;
-        if (*(volatile int*)&S->abort_) return false;
-        if (globaltimer_ns() - t0 > TC_WAIT_LIMIT_NS) break;
-        __nanosleep(20);
+    for (int k = 1;; k++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((k & 7) == 0) {
+            if (*(volatile int*)&S->abort_) return false;
+            if (globaltimer_ns() - t0 > TC_WAIT_LIMIT_NS) break;
+        }
     }
     *(volatile int*)&S->abort_ = 1;
     if (err && (atomicOr(err, 2u) & 2u) == 0) {
@@ -179,21 +198,40 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, TcSmem* 
 // Final drain: wait for a phase regardless of the abort flag (bounded).
 __device__ __forceinline__ void tc_drain(uint64_t* bar, uint32_t parity, unsigned* err) {
     const uint64_t t0 = globaltimer_ns();
-    while (!mbar_test_wait(bar, parity)) {
+    while (!mbar_try_wait(bar, parity)) {
         if (globaltimer_ns() - t0 > TC_WAIT_LIMIT_NS) {
             if (err) atomicOr(err, 4u);
             return;
         }
-        __nanosleep(20);
     }
 }
+
+// Diagnostic builds (-DTC_TRACE) record %globaltimer at each pipeline event
+// of CTA 0; product builds compile the hooks away.
+#ifdef TC_TRACE
+static __device__ unsigned long long g_tc_trace[1024];
+#define TC_T(slot)                                                          \
+    do {                                                                    \
+        if (blockIdx.x == 0 && (slot) < 1024) g_tc_trace[(slot)] = globaltimer_ns(); \
+    } while (0)
+#else
+#define TC_T(slot) \
+    do {           \
+    } while (0)
+#endif
 
 // One work item = (group, 128-row tile, K split); CTA c takes items c,
 // c + gridDim.x, ...  Items of empty groups (rows == 0) or beyond a group's N
 // are skipped by every role alike.
 struct TcItem {
     TcGroup G;
-    int g, tile, split, n0, kg0, nk, npad;
+    int g, tile, split, n0, kg0, nk, npad, koff;
+    // scale group of stage i: CTAs walk K from different offsets, so the SMs
+    // do not all request the same activation lines from L2 at once
+    __device__ __forceinline__ int kg(int i) const {
+        const int j = i + koff;
+        return kg0 + (j < nk ? j : j - nk);
+    }
 };
 __device__ __forceinline__ bool tc_item(const TcParams& P, int it, int KG, TcItem& t) {
     t.split = it % P.splits;
@@ -206,6 +244,7 @@ __device__ __forceinline__ bool tc_item(const TcParams& P, int it, int KG, TcIte
     t.kg0 = t.split * P.kg_per_split;
     t.nk = min(KG, t.kg0 + P.kg_per_split) - t.kg0;
     t.npad = (t.G.rows + 15) & ~15;
+    t.koff = t.nk > 0 ? (int)((blockIdx.x * 5u + (unsigned)t.tile) % (unsigned)t.nk) : 0;
     return t.nk > 0;
 }
 
@@ -214,13 +253,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     extern __shared__ __align__(1024) unsigned char tc_raw[];
     const int KG = P.K / TC_KS;
     const int n_items = P.n_groups * P.tiles * P.splits;
-    const int ost = P.fp16_w ? TC_OST16 : TC_OST;
+    const int ost = tc_op_stages(P.fp16_w, P.xmax);
+    const int xatom = P.xmax * 128;  // bytes of one 64-K swizzle atom of activations
+    const size_t stage = TC_A_BYTES + 2 * (size_t)xatom;
 
     unsigned char* sm = tc_raw + ((1024 - (smem_u32(tc_raw) & 1023)) & 1023);
-    unsigned char* PK = sm + TC_OST * TC_STAGE_BYTES;  // INT4 only
+    unsigned char* PK = sm + TC_OPS_BYTES;  // INT4 only
     TcSmem* S = reinterpret_cast<TcSmem*>(sm + TC_RING_BYTES);
-    auto A_of = [&](int s) { return sm + (size_t)s * TC_STAGE_BYTES; };
-    auto X_of = [&](int s) { return sm + (size_t)s * TC_STAGE_BYTES + TC_A_BYTES; };
+    auto A_of = [&](int s) { return sm + (size_t)s * stage; };
+    auto X_of = [&](int s) { return sm + (size_t)s * stage + TC_A_BYTES; };
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
@@ -228,12 +269,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&S->p_full[i], 1);
             mbar_init(&S->p_empty[i], TC_DQ_WARPS);
         }
-        for (int i = 0; i < TC_OST16; i++) {
+        for (int i = 0; i < TC_OSTMAX; i++) {
             mbar_init(&S->a_full[i], P.fp16_w ? 1 : TC_DQ_WARPS);
             mbar_init(&S->x_full[i], 1);
             mbar_init(&S->op_empty[i], 1);
         }
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < TC_NACC; i++) {
             mbar_init(&S->acc_full[i], 1);
             mbar_init(&S->acc_empty[i], 4);
         }
@@ -247,109 +288,149 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
     }
+    if (tid == 0) TC_T(0);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = S->tmem;
+    if (tid == 0) TC_T(1);
 
+    // The producer and MMA warps iterate warp-uniformly (all lanes walk the
+    // items and stages; lane 0 waits and issues, the result is broadcast), so
+    // the issuing lane never runs diverged from a parked warp.
     if (warp == TC_DQ_WARPS) {
         // ---- weight producer ----
-        if (lane == 0) {
-            const uint64_t pol = l2_policy_evict_first();
-            int last[TC_PST];
-            for (int s = 0; s < TC_PST; s++) last[s] = -1;
-            uint32_t pc = 0;
-            bool ok = true;
-            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-                TcItem t;
-                if (!tc_item(P, it, KG, t)) continue;
-                const CUtensorMap* wm = t.G.wmap ? t.G.wmap : &wmap0;
-                for (int i = 0; i < t.nk; i++, pc++) {
-                    const int kg = t.kg0 + i;
+        const uint64_t pol = l2_policy_evict_first();
+        int last[TC_PST];
+        for (int s = 0; s < TC_PST; s++) last[s] = -1;
+        uint32_t pc = 0;
+        bool ok = true;
+        if (lane == 0 && !P.groups) tc_prefetch_map(&wmap0);
+        const CUtensorMap* prev = nullptr;
+        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+            TcItem t;
+            if (!tc_item(P, it, KG, t)) continue;
+            const CUtensorMap* wm = t.G.wmap ? t.G.wmap : &wmap0;
+            if (wm != prev) {
+                if (lane == 0) tc_prefetch_map(wm);
+                prev = wm;
+            }
+            for (int i = 0; i < t.nk; i++, pc++) {
+                const int kg = t.kg(i);
+                const int s = P.fp16_w ? (int)(pc % ost) : (int)(pc % TC_PST);
+                bool w = true;
+                if (lane == 0) {
                     if (P.fp16_w) {
-                        const int s = pc % ost;
-                        if (!(ok = tc_wait(&S->op_empty[s], ((pc / ost) & 1) ^ 1, S, P.err, 10 + s, pc))) break;
-                        mbar_arrive_expect_tx(&S->a_full[s], TC_A_BYTES);
-                        tc_tma_2d_hint(A_of(s), wm, kg * TC_KS, t.n0, &S->a_full[s], pol);
-                        tc_tma_2d_hint(A_of(s) + TC_A_BYTES / 2, wm, kg * TC_KS + 64, t.n0, &S->a_full[s], pol);
-                        last[s] = (int)pc;
+                        w = tc_wait(&S->op_empty[s], ((pc / ost) & 1) ^ 1, S, P.err, 10 + s, pc);
+                        if (w) {
+                            mbar_arrive_expect_tx(&S->a_full[s], TC_A_BYTES);
+                            tc_tma_2d_hint(A_of(s), wm, kg * TC_KS, t.n0, &S->a_full[s], pol);
+                            tc_tma_2d_hint(A_of(s) + TC_A_BYTES / 2, wm, kg * TC_KS + 64, t.n0, &S->a_full[s], pol);
+                        }
                     } else {
-                        const int s = pc % TC_PST;
-                        if (!(ok = tc_wait(&S->p_empty[s], ((pc / TC_PST) & 1) ^ 1, S, P.err, 20 + s, pc))) break;
-                        mbar_arrive_expect_tx(&S->p_full[s], TC_P_BYTES);
-                        tc_tma_2d_hint(PK + s * TC_P_BYTES, wm, kg * (TC_KS / 2), t.n0, &S->p_full[s], pol);
-                        last[s] = (int)pc;
+                        w = tc_wait(&S->p_empty[s], ((pc / TC_PST) & 1) ^ 1, S, P.err, 20 + s, pc);
+                        if (w) {
+                            mbar_arrive_expect_tx(&S->p_full[s], TC_P_BYTES);
+                            tc_tma_2d_hint(PK + s * TC_P_BYTES, wm, kg * (TC_KS / 2), t.n0, &S->p_full[s], pol);
+                            if (pc < 64) TC_T(16 + pc);
+                        }
                     }
                 }
+                if (!(ok = __shfl_sync(0xffffffffu, (int)w, 0) != 0)) break;
+                last[s] = (int)pc;
             }
-            // copies still in flight land before the CTA can exit
+        }
+        // copies still in flight land before the CTA can exit
+        if (lane == 0) {
             const int depth = P.fp16_w ? ost : TC_PST;
             for (int s = 0; s < depth; s++)
                 if (last[s] >= 0) tc_drain(P.fp16_w ? &S->a_full[s] : &S->p_full[s], (last[s] / depth) & 1, P.err);
         }
+        __syncwarp();
     } else if (warp == TC_DQ_WARPS + 1) {
         // ---- activation producer ----
-        if (lane == 0) {
-            pdl_wait();
-            int last[TC_OST16] = {-1, -1, -1};
-            uint32_t oc = 0;
-            bool ok = true;
-            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-                TcItem t;
-                if (!tc_item(P, it, KG, t)) continue;
-                for (int i = 0; i < t.nk; i++, oc++) {
-                    const int s = oc % ost;
-                    if (!(ok = tc_wait(&S->op_empty[s], ((oc / ost) & 1) ^ 1, S, P.err, 30 + s, oc))) break;
-                    mbar_arrive_expect_tx(&S->x_full[s], (uint32_t)t.npad * TC_KS * 2);
-                    const int kx = (t.kg0 + i) * TC_KS;
-                    for (int a = 0; a < 2; a++)
-                        for (int b = 0; b < t.npad / 16; b++)
-                            tc_tma_2d(X_of(s) + a * (TC_X_BYTES / 2) + b * 2048, &xmap, kx + 64 * a, t.G.x_row + 16 * b,
-                                      &S->x_full[s]);
-                    last[s] = (int)oc;
+        if (lane == 0) tc_prefetch_map(&xmap);
+        pdl_wait();
+        int last[TC_OSTMAX] = {-1, -1, -1, -1};
+        uint32_t oc = 0;
+        bool ok = true;
+        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+            TcItem t;
+            if (!tc_item(P, it, KG, t)) continue;
+            for (int i = 0; i < t.nk; i++, oc++) {
+                const int s = oc % ost;
+                bool w = true;
+                if (lane == 0) {
+                    w = tc_wait(&S->op_empty[s], ((oc / ost) & 1) ^ 1, S, P.err, 30 + s, oc);
+                    if (w) {
+                        const int nb = (t.npad + P.xbox - 1) / P.xbox;
+                        mbar_arrive_expect_tx(&S->x_full[s], (uint32_t)(nb * P.xbox) * TC_KS * 2);
+                        if (oc < 64) TC_T(80 + oc);
+                        const int kx = t.kg(i) * TC_KS;
+                        for (int a = 0; a < 2; a++)
+                            for (int b = 0; b < nb; b++)
+                                tc_tma_2d(X_of(s) + a * xatom + b * P.xbox * 128, &xmap, kx + 64 * a,
+                                          t.G.x_row + P.xbox * b, &S->x_full[s]);
+                    }
                 }
+                if (!(ok = __shfl_sync(0xffffffffu, (int)w, 0) != 0)) break;
+                last[s] = (int)oc;
             }
+        }
+        if (lane == 0)
             for (int s = 0; s < ost; s++)
                 if (last[s] >= 0) tc_drain(&S->x_full[s], (last[s] / ost) & 1, P.err);
-        }
+        __syncwarp();
     } else if (warp == TC_DQ_WARPS + 2) {
         // ---- MMA issuer ----
-        if (lane == 0) {
-            uint32_t oc = 0, ac = 0, ic = 0;
-            bool ok = true;
-            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-                TcItem t;
-                if (!tc_item(P, it, KG, t)) continue;
-                const uint32_t idesc = tc_idesc(t.npad);
-                uint32_t d = 0;
-                if (P.fp16_w) {  // the item accumulates in region ic&1, free once read back
-                    if (!(ok = tc_wait(&S->acc_empty[ic & 1], ((ic >> 1) & 1) ^ 1, S, P.err, 40 + (ic & 1), ic))) break;
-                    d = tmem + (uint32_t)((ic & 1) * 128);
-                }
-                for (int i = 0; i < t.nk; i++, oc++) {
-                    const int s = oc % ost;
-                    const uint32_t ph = (oc / ost) & 1;
-                    if (!(ok = tc_wait(&S->a_full[s], ph, S, P.err, 50 + s, oc) && tc_wait(&S->x_full[s], ph, S, P.err, 60 + s, oc)))
-                        break;
-                    if (!P.fp16_w) {  // INT4: one accumulator per scale group, read back by the scale warps
-                        if (!(ok = tc_wait(&S->acc_empty[ac & 1], ((ac >> 1) & 1) ^ 1, S, P.err, 70 + (ac & 1), ac))) break;
-                        d = tmem + (uint32_t)((ac & 1) * 128);
-                    }
-                    tc_fence_after();
-#pragma unroll
-                    for (int kk = 0; kk < TC_KS / 16; kk++) {
-                        const int off = (kk >> 2) * (TC_A_BYTES / 2) + (kk & 3) * 32;
-                        const int xoff = (kk >> 2) * (TC_X_BYTES / 2) + (kk & 3) * 32;
-                        tc_mma(d, tc_desc_sw128(A_of(s) + off), tc_desc_sw128(X_of(s) + xoff), idesc,
-                               P.fp16_w ? (i | kk) != 0 : kk != 0);
-                    }
-                    tc_commit(&S->op_empty[s]);
-                    if (!P.fp16_w) tc_commit(&S->acc_full[(ac++) & 1]);
-                }
-                if (ok && P.fp16_w) tc_commit(&S->acc_full[(ic++) & 1]);
+        uint32_t oc = 0, ac = 0, ic = 0;
+        bool ok = true;
+        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+            TcItem t;
+            if (!tc_item(P, it, KG, t)) continue;
+            const uint32_t idesc = tc_idesc(t.npad);
+            uint32_t d = 0;
+            if (P.fp16_w) {  // the item accumulates in region ic%3, free once read back
+                const uint32_t a3 = ic % TC_NACC;
+                bool w = true;
+                if (lane == 0) w = tc_wait(&S->acc_empty[a3], ((ic / TC_NACC) & 1) ^ 1, S, P.err, 40 + a3, ic);
+                if (!(ok = __shfl_sync(0xffffffffu, (int)w, 0) != 0)) break;
+                d = tmem + a3 * 128;
             }
-            tc_commit(&S->done);  // tracks every MMA issued above
+            for (int i = 0; i < t.nk; i++, oc++) {
+                const int s = oc % ost;
+                const uint32_t ph = (oc / ost) & 1;
+                const uint32_t a3 = ac % TC_NACC;
+                bool w = true;
+                if (lane == 0) {
+                    w = tc_wait(&S->a_full[s], ph, S, P.err, 50 + s, oc) && tc_wait(&S->x_full[s], ph, S, P.err, 60 + s, oc);
+                    // INT4: one accumulator per scale group, read back by the scale warps
+                    if (w && !P.fp16_w) w = tc_wait(&S->acc_empty[a3], ((ac / TC_NACC) & 1) ^ 1, S, P.err, 70 + a3, ac);
+                    if (w) {
+                        if (!P.fp16_w) d = tmem + a3 * 128;
+                        tc_fence_after();
+                        if (oc < 64) TC_T(272 + oc);
+#pragma unroll
+                        for (int kk = 0; kk < TC_KS / 16; kk++) {
+                            const int off = (kk >> 2) * (TC_A_BYTES / 2) + (kk & 3) * 32;
+                            const int xoff = (kk >> 2) * xatom + (kk & 3) * 32;
+                            tc_mma(d, tc_desc_sw128(A_of(s) + off), tc_desc_sw128(X_of(s) + xoff), idesc,
+                                   P.fp16_w ? (i | kk) != 0 : kk != 0);
+                        }
+                        tc_commit(&S->op_empty[s]);
+                        if (!P.fp16_w) tc_commit(&S->acc_full[a3]);
+                    }
+                }
+                if (!(ok = __shfl_sync(0xffffffffu, (int)w, 0) != 0)) break;
+                if (!P.fp16_w) ac++;
+            }
+            if (ok && P.fp16_w) {
+                if (lane == 0) tc_commit(&S->acc_full[ic % TC_NACC]);
+                ic++;
+            }
         }
+        if (lane == 0) tc_commit(&S->done);  // tracks every MMA issued above
+        __syncwarp();
     } else if (warp < TC_DQ_WARPS) {
         // ---- dequantization (INT4 weights) to exact (nib-8) ----
         const int r = tid & (TC_ROWS - 1), h = tid >> 7;
@@ -362,14 +443,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 for (int i = 0; i < t.nk; i++, pc++, oc++) {
                     const int s = pc % TC_PST;
                     if (!(ok = tc_wait(&S->p_full[s], (pc / TC_PST) & 1, S, P.err, 80 + s, pc))) break;
+                    if (tid == 0 && pc < 64) TC_T(144 + pc);
                     const unsigned char* row = PK + s * TC_P_BYTES + r * 64;
                     const int sw = (r >> 1) & 3;
                     const uint4 c0 = *reinterpret_cast<const uint4*>(row + (((2 * h) ^ sw) << 4));
                     const uint4 c1 = *reinterpret_cast<const uint4*>(row + (((2 * h + 1) ^ sw) << 4));
                     __syncwarp();
                     if (lane == 0) tc_arrive(&S->p_empty[s]);
-                    const int so = oc % TC_OST;
-                    if (!(ok = tc_wait(&S->op_empty[so], ((oc / TC_OST) & 1) ^ 1, S, P.err, 90 + so, oc))) break;
+                    const int so = oc % ost;
+                    if (!(ok = tc_wait(&S->op_empty[so], ((oc / ost) & 1) ^ 1, S, P.err, 90 + so, oc))) break;
                     unsigned char* dst = A_of(so) + h * (TC_A_BYTES / 2) + r * 128;
                     const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
@@ -386,6 +468,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
                     __syncwarp();
                     if (lane == 0) tc_arrive(&S->a_full[so]);
+                    if (tid == 0 && oc < 64) TC_T(208 + oc);
                 }
             }
         }
@@ -412,38 +495,47 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int n = t.n0 + rr;
             uint32_t res;
             if (!P.fp16_w) {
-                const __half* srow = G.scales + (size_t)min(n, G.N - 1) * KG + t.kg0;
-                float sc_next = n < G.N ? __half2float(__ldg(srow)) : 0.f;
+                const __half* srow = G.scales + (size_t)min(n, G.N - 1) * KG;
+                float sc_next = n < G.N ? __half2float(__ldg(srow + t.kg(0))) : 0.f;
                 for (int i = 0; i < t.nk; i++, ac++) {
                     const float sc = sc_next;
-                    if (i + 1 < t.nk) sc_next = n < G.N ? __half2float(__ldg(srow + i + 1)) : 0.f;
-                    if (!(ok = tc_wait(&S->acc_full[ac & 1], (ac >> 1) & 1, S, P.err, 100 + (ac & 1), ac))) break;
+                    if (i + 1 < t.nk) sc_next = n < G.N ? __half2float(__ldg(srow + t.kg(i + 1))) : 0.f;
+                    const uint32_t a3 = ac % TC_NACC;
+                    if (!(ok = tc_wait(&S->acc_full[a3], (ac / TC_NACC) & 1, S, P.err, 100 + a3, ac))) break;
+                    if (atid == 0 && ac < 64) TC_T(336 + ac);
                     tc_fence_after();
-                    const uint32_t ab = lane_base + (uint32_t)((ac & 1) * 128);
-                    for (int c = 0; c < t.npad; c += 16) {
-                        float a[16], y[16];
-                        tc_ld16(ab + c, a);
-                        if (i == 0) {
-#pragma unroll
-                            for (int j = 0; j < 16; j++) y[j] = sc * a[j];
-                        } else {
-                            tc_ld16(lane_base + 256 + c, y);
-#pragma unroll
-                            for (int j = 0; j < 16; j++) y[j] = fmaf(sc, a[j], y[j]);
+                    const uint32_t ab = lane_base + a3 * 128, yb = lane_base + 384;
+                    // 32 columns per round: both loads issued, one wait
+                    for (int c = 0; c < t.npad; c += 32) {
+                        const bool two = c + 16 < t.npad;
+                        uint32_t a[32], y[32];
+                        tc_ld16_issue(ab + c, a);
+                        if (two) tc_ld16_issue(ab + c + 16, a + 16);
+                        if (i > 0) {
+                            tc_ld16_issue(yb + c, y);
+                            if (two) tc_ld16_issue(yb + c + 16, y + 16);
                         }
-                        tc_st16(lane_base + 256 + c, y);
+                        tc_wait_ld();
+                        float o[32];
+#pragma unroll
+                        for (int j = 0; j < 32; j++)
+                            o[j] = i == 0 ? sc * __uint_as_float(a[j]) : fmaf(sc, __uint_as_float(a[j]), __uint_as_float(y[j]));
+                        tc_st16(yb + c, *reinterpret_cast<const float(*)[16]>(o));
+                        if (two) tc_st16(yb + c + 16, *reinterpret_cast<const float(*)[16]>(o + 16));
                     }
                     tc_wait_st();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) tc_arrive(&S->acc_empty[ac & 1]);
+                    if (lane == 0) tc_arrive(&S->acc_empty[a3]);
+                    if (atid == 0 && ac < 64) TC_T(400 + ac);
                 }
                 if (!ok) break;
-                res = lane_base + 256;
+                res = lane_base + 384;
             } else {
-                if (!(ok = tc_wait(&S->acc_full[ic & 1], (ic >> 1) & 1, S, P.err, 110 + (ic & 1), ic))) break;
+                const uint32_t a3 = ic % TC_NACC;
+                if (!(ok = tc_wait(&S->acc_full[a3], (ic / TC_NACC) & 1, S, P.err, 110 + a3, ic))) break;
                 tc_fence_after();
-                res = lane_base + (uint32_t)((ic & 1) * 128);
+                res = lane_base + a3 * 128;
             }
             if (!waited) {
                 pdl_wait();
@@ -515,16 +607,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                 }
             }
+            if (atid == 0) TC_T(464 + (it / gridDim.x < 32 ? it / gridDim.x : 31));
             if (P.fp16_w) {  // every lane advances ic; lane 0 arrives for the warp
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) tc_arrive(&S->acc_empty[ic & 1]);
+                if (lane == 0) tc_arrive(&S->acc_empty[ic % TC_NACC]);
                 ic++;
             }
         }
     }
     tc_fence_before();
     __syncthreads();
+    if (tid == 0) TC_T(500);
     if (warp == TC_DQ_WARPS + 2) {
         tc_fence_after();
         if (lane == 0) tc_drain(&S->done, 0, P.err);  // all MMAs retired before TMEM is freed
