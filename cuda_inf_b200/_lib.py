@@ -96,6 +96,9 @@ _SIGS = {
     "cuinf_batch_fill_synthetic": (c_int, [c_void_p, c_int, ctypes.c_ulonglong]),
     "cuinf_batch_error": (c_int, [c_void_p]),
     "cuinf_batch_profile_step": (c_int, [c_void_p, c_int, c_void_p, ctypes.c_char_p, c_int, c_void_p]),
+    "cuinf_batch_create_ep": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "cuinf_ep_unique_id": (c_int, [c_void_p, c_int]),
+    "cuinf_ep_unique_id_bytes": (c_int, []),
     "cuinf_device_error": (c_int, [ctypes.POINTER(ctypes.c_uint)]),
     "cuinf_session_uses_megakernel": (c_int, [c_void_p]),
     "cuinf_session_trace": (c_int, [c_void_p, c_void_p, c_int, c_void_p, ctypes.POINTER(c_int),
@@ -121,6 +124,10 @@ def lib():
             raise RuntimeError(
                 f"{LIB_PATH} is missing; build it with `python -m cuda_inf_b200.build` "
                 "(there is no CPU fallback)")
+        # torch first: its NCCL (libnccl.so.2) is then the one the library's
+        # NCCL dependency resolves to, so both share one NCCL in the process
+        import torch  # noqa: F401
+        import torch.distributed  # noqa: F401
         L = ctypes.CDLL(LIB_PATH)
         for name, (res, args) in _SIGS.items():
             fn = getattr(L, name)

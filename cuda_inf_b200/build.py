@@ -56,7 +56,7 @@ def build(force=False, jobs=4, extra=()):
         raise RuntimeError("nvcc failed:\n" + "\n".join(errs))
     objs = [o for o, _ in results]
     if force or _newer(LIB, objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart_static"]
+        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart_static", "-lnccl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n" + r.stderr + r.stdout)

@@ -257,6 +257,8 @@ extern "C" int cuinf_argmax_key_index(unsigned long long key) {
 // applies the reference's per-token slot order (acc_scaled then add_inplace,
 // engine.cu:894-904).  The step is one CUDA graph.
 // ===========================================================================
+#include <nccl.h>
+
 #include "model.h"
 #include "route.cuh"
 
@@ -299,6 +301,13 @@ struct cuinf_batch {
     int kernels = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    // expert parallelism: this rank hosts experts [e_lo, e_lo + e_loc) and
+    // exchanges (token, slot) rows with the other ranks through NCCL
+    int ep_rank = 0, ep_world = 1, e_lo = 0, e_loc = 0, cap = 0;
+    ncclComm_t comm = nullptr;
+    __half *send_x = nullptr, *recv_x = nullptr;
+    int *send_meta = nullptr, *recv_meta = nullptr, *dest_pos = nullptr;
+    float *back_o = nullptr, *recv_back = nullptr;
 };
 
 template <class T>
@@ -393,26 +402,36 @@ struct BRouteParams {
     int B, E, topk, I, H, maxch;
     int* ridx;  // [B][topk] (this layer's slice)
     float* rw;  // [B][topk]
-    int* inv;   // [B*topk] row of (token, slot)
-    int* src;   // [B*topk] token of row
-    TcGroup* g13;  // [2][E][maxch]
-    TcGroup* g2;   // [E][maxch]
-    const CUtensorMap* maps;  // [E][3]: w1, w3, w2
-    void* const* experts;     // [E][6]: w1 packed, w1 scales, w3 .., w2 ..
+    // grouping of n entries by key (an expert of this rank, -1 = none): with
+    // keys null the entries are this batch's (token, slot) choices (n = B*topk,
+    // source row = token); otherwise received rows (source row = entry)
+    const int* keys;
+    int n, n_local;  // entries; experts in the group tables (E, or E/world)
+    int group;       // 0: route only
+    int* inv;   // [n] row of entry (-1: none)
+    int* src;   // [rows] source row of each grouped row
+    TcGroup* g13;  // [2][n_local][maxch]
+    TcGroup* g2;   // [n_local][maxch]
+    const CUtensorMap* maps;  // [n_local][3]: w1, w3, w2
+    void* const* experts;     // [n_local][6]: w1 packed, w1 scales, w3 .., w2 ..
     float *gbuf, *ubuf, *obuf;
 };
 __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
     __shared__ int sidx[1024];
     __shared__ int cnt[256], off[256];
-    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5, n = P.B * P.topk;
-    for (int e = threadIdx.x; e < P.E; e += blockDim.x) cnt[e] = 0;
-    for (int b = warp; b < P.B; b += nw)
-        route_select_warp(P.logits + (size_t)b * P.E, P.bias, P.E, P.topk, P.ridx + b * P.topk, P.rw + b * P.topk);
+    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int n = P.keys ? P.n : P.B * P.topk, NE = P.keys ? P.n_local : P.E;
+    for (int e = threadIdx.x; e < NE; e += blockDim.x) cnt[e] = 0;
+    if (!P.keys)
+        for (int b = warp; b < P.B; b += nw)
+            route_select_warp(P.logits + (size_t)b * P.E, P.bias, P.E, P.topk, P.ridx + b * P.topk,
+                              P.rw + b * P.topk);
+    if (!P.group) return;
     __syncthreads();
     // rank of entry j among the entries of its expert that come before it
     int e = -1, rank = 0;
     if (threadIdx.x < n) {
-        e = P.ridx[threadIdx.x];
+        e = P.keys ? P.keys[threadIdx.x] : P.ridx[threadIdx.x];
         sidx[threadIdx.x] = e;
     }
     __syncthreads();
@@ -423,26 +442,23 @@ __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
     __syncthreads();
     if (threadIdx.x < 32) {  // exclusive prefix over experts, one warp
         int carry = 0;
-        for (int base = 0; base < P.E; base += 32) {
+        for (int base = 0; base < NE; base += 32) {
             const int i = base + threadIdx.x;
-            const int v = i < P.E ? cnt[i] : 0;
+            const int v = i < NE ? cnt[i] : 0;
             int x = v;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const int y = __shfl_up_sync(0xffffffffu, x, o);
                 if ((int)threadIdx.x >= o) x += y;
             }
-            if (i < P.E) off[i] = carry + x - v;
+            if (i < NE) off[i] = carry + x - v;
             carry += __shfl_sync(0xffffffffu, x, 31);
         }
     }
     __syncthreads();
-    if (e >= 0) {
-        const int row = off[e] + rank;
-        P.inv[threadIdx.x] = row;
-        P.src[row] = threadIdx.x / P.topk;
-    }
-    for (int ex = threadIdx.x; ex < P.E; ex += blockDim.x) {
+    if (threadIdx.x < n) P.inv[threadIdx.x] = e >= 0 ? off[e] + rank : -1;
+    if (e >= 0) P.src[off[e] + rank] = P.keys ? (int)threadIdx.x : (int)threadIdx.x / P.topk;
+    for (int ex = threadIdx.x; ex < NE; ex += blockDim.x) {
         for (int c = 0; c < P.maxch; c++) {
             const int r0 = off[ex] + c * TC_NMAX;
             const int rows = max(0, min(TC_NMAX, cnt[ex] - c * TC_NMAX));
@@ -459,7 +475,7 @@ __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
             a.wmap = P.maps + ex * 3 + 1;
             a.scales = (const __half*)P.experts[ex * 6 + 3];
             a.y = P.ubuf + (size_t)r0 * P.I;
-            P.g13[P.E * P.maxch + gi] = a;
+            P.g13[NE * P.maxch + gi] = a;
             a.wmap = P.maps + ex * 3 + 2;
             a.scales = (const __half*)P.experts[ex * 6 + 5];
             a.y = P.obuf + (size_t)r0 * P.H;
@@ -519,6 +535,46 @@ __global__ void k_bset(int* p, int B, int v) {
     if (b < B) p[b] = v;
 }
 
+// Expert-parallel dispatch plan (one CTA, n = B*topk <= 1024 entries): entry
+// j = (token, slot) goes to rank d = expert / e_loc at position rank-of-j
+// among the entries for d (in entry order); dest_pos[j] = d * cap + position,
+// meta[d * cap + position] = the expert's index on d, unused positions -1.
+__global__ void __launch_bounds__(1024) k_ep_plan(const int* __restrict__ ridx, int n, int e_loc, int world,
+                                                  int cap, int* dest_pos, int* meta) {
+    __shared__ int sd[1024];
+    const int j = threadIdx.x;
+    for (int i = j; i < world * cap; i += blockDim.x) meta[i] = -1;
+    int d = -1, e = -1;
+    if (j < n) {
+        e = ridx[j];
+        d = e / e_loc;
+        sd[j] = d;
+    }
+    __syncthreads();
+    if (j < n) {
+        int r = 0;
+        for (int i = 0; i < j; i++) r += sd[i] == d;
+        dest_pos[j] = d * cap + r;
+        meta[d * cap + r] = e - d * e_loc;
+    }
+}
+// send_x[dest_pos[j]] = xn[j / topk]
+__global__ void k_ep_pack(const __half* __restrict__ xn, const int* __restrict__ dest_pos, __half* send_x, int H,
+                          int topk) {
+    const int j = blockIdx.x;
+    const uint4* s = reinterpret_cast<const uint4*>(xn + (size_t)(j / topk) * H);
+    uint4* d = reinterpret_cast<uint4*>(send_x + (size_t)dest_pos[j] * H);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) d[i] = s[i];
+}
+// back_o[j] = fo[inv[j]] for received entries that hold a row
+__global__ void k_ep_unpack(const float* __restrict__ fo, const int* __restrict__ inv, float* back_o, int H) {
+    const int j = blockIdx.x, r = inv[j];
+    if (r < 0) return;
+    const float4* s = reinterpret_cast<const float4*>(fo + (size_t)r * H);
+    float4* d = reinterpret_cast<float4*>(back_o + (size_t)j * H);
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) d[i] = s[i];
+}
+
 // ---------------------------------------------------------------------------
 // host: one step as a sequence of launches (recorded into a graph)
 // ---------------------------------------------------------------------------
@@ -550,8 +606,9 @@ struct BStep {
         return CUINF_OK;
     }
 
-    int gemm(const CUtensorMap& xm, int xbox, int wmap_idx, const TcGroup* dg, TcGroup g0, int ngroups, int tiles,
-             int K, int active_ctas, bool fp16w, unsigned long long* amax) {
+    // xrows: most activation rows any group of the launch can have
+    int gemm(const CUtensorMap& xm, int xbox, int xrows, int wmap_idx, const TcGroup* dg, TcGroup g0, int ngroups,
+             int tiles, int K, int active_ctas, bool fp16w, unsigned long long* amax) {
         TcPlan pl = amax ? TcPlan{1, K / TC_KS} : tc_plan(active_ctas, K, b->num_sms);
         REQUIRE(fp16w || pl.kgps <= TC_MAX_KG, "K too large");
         launches++;
@@ -568,7 +625,7 @@ struct BStep {
         P.splits = pl.splits;
         P.kg_per_split = pl.kgps;
         P.fp16_w = fp16w;
-        P.xmax = (std::min(b->B, TC_NMAX) + 15) & ~15;  // no group has more rows than the batch
+        P.xmax = (std::min(xrows, TC_NMAX) + 15) & ~15;
         P.xbox = xbox;
         P.ws = b->ws;
         P.counters = b->cnt;
@@ -588,7 +645,7 @@ struct BStep {
         g.N = N;
         g.ldy = N;
         const int tiles = (N + TC_ROWS - 1) / TC_ROWS;
-        return gemm(xm, (b->B + 15) & ~15, wi, nullptr, g, 1, tiles, K, tiles, fp16w, amax);
+        return gemm(xm, (b->B + 15) & ~15, b->B, wi, nullptr, g, 1, tiles, K, tiles, fp16w, amax);
     }
     int ew(int rc) {
         launches++;
@@ -601,7 +658,6 @@ static int batch_record(cuinf_batch* b, BStep& S) {
     const cuinf_config& c = m->cfg;
     const int B = b->B, H = c.hidden, nh = c.n_heads, nkv = c.n_kv_heads, E = c.n_experts, K = c.top_k;
     const int NQ = nh * 64, NK = nkv * 64;
-    const int maxch = (B + TC_NMAX - 1) / TC_NMAX;
     void* vs = (void*)b->st;
     const bool dry = S.dry;
     auto run = [&](int rc) { return dry ? CUINF_OK : rc; };
@@ -622,8 +678,8 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             __half* v16 = k16 + (size_t)B * NK;
             const int tiles = (NQ + TC_ROWS - 1) / TC_ROWS;
             const int active = tiles + 2 * ((NK + TC_ROWS - 1) / TC_ROWS);
-            BTRY(S.gemm(b->x_h, (B + 15) & ~15, -1, b->dstatic + b->qkv_tab[l], TcGroup{}, 3, tiles, H, active, false,
-                        nullptr));
+            BTRY(S.gemm(b->x_h, (B + 15) & ~15, B, -1, b->dstatic + b->qkv_tab[l], TcGroup{}, 3, tiles, H, active,
+                        false, nullptr));
             BTRY(S.mark("gemm_qkv"));
             BTRY(S.ew(run(cuinf_f32_to_f16(qf, q16, B * (NQ + 2 * NK), vs))));
             BTRY(S.mark("f32_to_f16"));
@@ -685,8 +741,8 @@ static int batch_record(cuinf_batch* b, BStep& S) {
         BTRY(S.mark("rmsnorm"));
         if (l < c.n_dense) {
             const int I = c.dense_inter, tiles = (I + TC_ROWS - 1) / TC_ROWS;
-            BTRY(S.gemm(b->x_h, (B + 15) & ~15, -1, b->dstatic + b->d13_tab[l], TcGroup{}, 2, tiles, H, 2 * tiles,
-                        false, nullptr));
+            BTRY(S.gemm(b->x_h, (B + 15) & ~15, B, -1, b->dstatic + b->d13_tab[l], TcGroup{}, 2, tiles, H,
+                        2 * tiles, false, nullptr));
             BTRY(S.mark("gemm_dense_w13"));
             BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->dmid, B * I, vs))));
             BTRY(S.mark("swiglu"));
@@ -696,50 +752,116 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             BTRY(S.mark("residual"));
         } else {
             const int I = c.moe_inter;
+            const bool ep = b->ep_world > 1;
+            const int EL = ep ? b->e_loc : E;           // experts in this rank's group tables
+            const int NR = ep ? b->ep_world * b->cap : B * K;  // rows grouped here
+            const int mch = (NR + TC_NMAX - 1) / TC_NMAX;
             BTRY(S.ew(run(cuinf_gemv_fp16(b->xn, L.gate, b->rlog, B, E, H, vs))));
             BTRY(S.mark("router_gemv"));
-            S.launches++;
-            if (!dry) {
-                BRouteParams R;
-                R.logits = b->rlog;
-                R.bias = L.ebias;
-                R.B = B;
-                R.E = E;
-                R.topk = K;
-                R.I = I;
-                R.H = H;
-                R.maxch = maxch;
-                R.ridx = b->ridx + (size_t)moe_i * B * K;
-                R.rw = b->rw;
-                R.inv = b->inv;
-                R.src = b->src;
-                R.g13 = b->g13;
-                R.g2 = b->g2;
-                R.maps = b->dmaps + b->mi_experts[moe_i];
-                R.experts = (void* const*)(m->d_experts + (size_t)L.moe_index * E * 6);
-                R.gbuf = b->fg;
-                R.ubuf = b->fu;
-                R.obuf = b->fo;
-                k_broute<<<1, 1024, 0, b->st>>>(R);
-                BTRY(cuinf_launch_status());
-                BTRY(S.mark("route_group"));
-                k_bgather<<<B * K, 256, 0, b->st>>>(b->xn, b->src, b->xg, H);
-                BTRY(cuinf_launch_status());
-                BTRY(S.mark("gather"));
+            BRouteParams R;
+            R.logits = b->rlog;
+            R.bias = L.ebias;
+            R.B = B;
+            R.E = E;
+            R.topk = K;
+            R.I = I;
+            R.H = H;
+            R.maxch = mch;
+            R.ridx = b->ridx + (size_t)moe_i * B * K;
+            R.rw = b->rw;
+            R.keys = nullptr;
+            R.n = B * K;
+            R.n_local = EL;
+            R.group = 1;
+            R.inv = b->inv;
+            R.src = b->src;
+            R.g13 = b->g13;
+            R.g2 = b->g2;
+            R.maps = b->dmaps + b->mi_experts[moe_i] + 3 * b->e_lo;
+            R.experts = (void* const*)(m->d_experts + ((size_t)L.moe_index * E + b->e_lo) * 6);
+            R.gbuf = b->fg;
+            R.ubuf = b->fu;
+            R.obuf = b->fo;
+            if (!ep) {
+                S.launches += 2;
+                if (!dry) {
+                    k_broute<<<1, 1024, 0, b->st>>>(R);
+                    BTRY(cuinf_launch_status());
+                    BTRY(S.mark("route_group"));
+                    k_bgather<<<B * K, 256, 0, b->st>>>(b->xn, b->src, b->xg, H);
+                    BTRY(cuinf_launch_status());
+                    BTRY(S.mark("gather"));
+                }
+            } else {
+                // route this rank's tokens, pack each (token, slot) row for its
+                // expert's rank, exchange, group the received rows by local expert
+                S.launches += 5;
+                if (!dry) {
+                    R.group = 0;
+                    k_broute<<<1, 1024, 0, b->st>>>(R);
+                    BTRY(cuinf_launch_status());
+                    BTRY(S.mark("route"));
+                    k_ep_plan<<<1, 1024, 0, b->st>>>(R.ridx, B * K, b->e_loc, b->ep_world, b->cap, b->dest_pos,
+                                                      b->send_meta);
+                    BTRY(cuinf_launch_status());
+                    k_ep_pack<<<B * K, 256, 0, b->st>>>(b->xn, b->dest_pos, b->send_x, H, K);
+                    BTRY(cuinf_launch_status());
+                    BTRY(S.mark("ep_pack"));
+                    const size_t cx = (size_t)b->cap * H;
+                    if (ncclGroupStart() != ncclSuccess) return cuinf_set_arg_error("ncclGroupStart failed");
+                    for (int d = 0; d < b->ep_world; d++) {
+                        ncclSend(b->send_x + d * cx, cx, ncclFloat16, d, b->comm, b->st);
+                        ncclRecv(b->recv_x + d * cx, cx, ncclFloat16, d, b->comm, b->st);
+                        ncclSend(b->send_meta + d * b->cap, b->cap, ncclInt32, d, b->comm, b->st);
+                        ncclRecv(b->recv_meta + d * b->cap, b->cap, ncclInt32, d, b->comm, b->st);
+                    }
+                    if (ncclGroupEnd() != ncclSuccess) return cuinf_set_arg_error("NCCL dispatch failed");
+                    BTRY(S.mark("ep_dispatch"));
+                    R.keys = b->recv_meta;
+                    R.n = NR;
+                    R.group = 1;
+                    k_broute<<<1, 1024, 0, b->st>>>(R);
+                    BTRY(cuinf_launch_status());
+                    k_bgather<<<NR, 256, 0, b->st>>>(b->recv_x, b->src, b->xg, H);
+                    BTRY(cuinf_launch_status());
+                    BTRY(S.mark("ep_group"));
+                }
             }
             S.launches++;
             const int t13 = (I + TC_ROWS - 1) / TC_ROWS, t2 = (H + TC_ROWS - 1) / TC_ROWS;
-            // about min(E, B*K) experts are hit; each group is one tile row of CTAs
-            const int hit = std::min(E, B * K);
-            BTRY(S.gemm(b->x_xg, 16, -1, b->g13, TcGroup{}, 2 * E * maxch, t13, H, 2 * hit * t13, false, nullptr));
+            // about min(experts, rows) experts are hit; each group is one tile row of CTAs
+            const int hit = std::min(EL, NR);
+            // an expert's group holds at most one row per token of every rank
+            const int grows = B * b->ep_world;
+            BTRY(S.gemm(b->x_xg, 16, grows, -1, b->g13, TcGroup{}, 2 * EL * mch, t13, H, 2 * hit * t13, false,
+                        nullptr));
             BTRY(S.mark("gemm_moe_w13"));
-            BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->mmid, B * K * I, vs))));
+            BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->mmid, NR * I, vs))));
             BTRY(S.mark("swiglu_moe"));
-            BTRY(S.gemm(b->x_mmid, 16, -1, b->g2, TcGroup{}, E * maxch, t2, I, hit * t2, false, nullptr));
+            BTRY(S.gemm(b->x_mmid, 16, grows, -1, b->g2, TcGroup{}, EL * mch, t2, I, hit * t2, false, nullptr));
             BTRY(S.mark("gemm_moe_w2"));
+            const float* ob = b->fo;
+            const int* oi = b->inv;
+            if (ep) {
+                S.launches++;
+                if (!dry) {
+                    k_ep_unpack<<<NR, 256, 0, b->st>>>(b->fo, b->inv, b->back_o, H);
+                    BTRY(cuinf_launch_status());
+                    const size_t co = (size_t)b->cap * H;
+                    if (ncclGroupStart() != ncclSuccess) return cuinf_set_arg_error("ncclGroupStart failed");
+                    for (int d = 0; d < b->ep_world; d++) {
+                        ncclSend(b->back_o + d * co, co, ncclFloat32, d, b->comm, b->st);
+                        ncclRecv(b->recv_back + d * co, co, ncclFloat32, d, b->comm, b->st);
+                    }
+                    if (ncclGroupEnd() != ncclSuccess) return cuinf_set_arg_error("NCCL combine failed");
+                    BTRY(S.mark("ep_return"));
+                }
+                ob = b->recv_back;
+                oi = b->dest_pos;
+            }
             S.launches++;
             if (!dry) {
-                k_bcombine<<<(B * H + 255) / 256, 256, 0, b->st>>>(b->fo, b->inv, b->rw, b->h, B, H, K);
+                k_bcombine<<<(B * H + 255) / 256, 256, 0, b->st>>>(ob, oi, b->rw, b->h, B, H, K);
                 BTRY(cuinf_launch_status());
                 BTRY(S.mark("combine"));
             }
@@ -808,14 +930,20 @@ extern "C" int cuinf_batch_free(cuinf_batch* b) {
     if (b->ws) cudaFree(b->ws);
     if (b->cnt) cudaFree(b->cnt);
     if (b->pinned) cudaFreeHost(b->pinned);
+    if (b->comm) ncclCommDestroy(b->comm);  // after the graph that holds its calls
     if (b->own_stream && b->st) cudaStreamDestroy(b->st);
     delete b;
     return CUINF_OK;
 }
 
-extern "C" int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, cuinf_batch** out) {
+static int batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, const unsigned char* nccl_id,
+                        int rank, int world, cuinf_batch** out) {
     REQUIRE(m && out, "null pointer");
     const cuinf_config& c = m->cfg;
+    REQUIRE(world >= 1 && rank >= 0 && rank < world, "bad rank / world");
+    REQUIRE(world == 1 || (nccl_id && c.n_experts % world == 0),
+            "expert parallelism needs an NCCL id and n_experts divisible by the world size");
+    REQUIRE(world == 1 || (size_t)n_seqs * c.top_k * world <= 1024, "n_seqs * top_k * world must be <= 1024");
     REQUIRE(n_seqs >= 1 && n_seqs <= TC_NMAX, "n_seqs must be in [1, 128]");
     REQUIRE(max_ctx >= 1, "max_ctx must be positive");
     REQUIRE(c.hidden % TC_KS == 0 && c.moe_inter % TC_KS == 0 && c.dense_inter % TC_KS == 0 &&
@@ -826,6 +954,11 @@ extern "C" int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void*
     cuinf_batch* b = new cuinf_batch();
     b->m = m;
     b->B = n_seqs;
+    b->ep_rank = rank;
+    b->ep_world = world;
+    b->e_loc = c.n_experts / world;
+    b->e_lo = rank * b->e_loc;
+    b->cap = n_seqs * c.top_k;
     b->max_ctx = max_ctx;
     int rc = CUINF_OK;
 #define TRYB(x)                     \
@@ -880,25 +1013,43 @@ extern "C" int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void*
     TRYB(balloc(b, &b->attn_out, (size_t)B * NQ * 2));
     TRYB(balloc(b, &b->conv_y, (size_t)B * H * 2));
     TRYB(balloc(b, &b->dmid, (size_t)B * std::max(ID, 128) * 2));
-    TRYB(balloc(b, &b->xg, (size_t)B * K * H * 2));
-    TRYB(balloc(b, &b->mmid, (size_t)B * K * I * 2));
+    const int NR = world > 1 ? world * b->cap : B * K;  // rows the expert GEMMs group
+    TRYB(balloc(b, &b->xg, (size_t)NR * H * 2));
+    TRYB(balloc(b, &b->mmid, (size_t)NR * I * 2));
     TRYB(balloc(b, &b->fqkv, (size_t)B * (NQ + 2 * NK) * 4));
     TRYB(balloc(b, &b->fa, (size_t)B * maxN * 4));
     TRYB(balloc(b, &b->fb, (size_t)B * maxN * 4));
-    TRYB(balloc(b, &b->fg, (size_t)B * K * std::max(I, ID) * 4));
-    TRYB(balloc(b, &b->fu, (size_t)B * K * std::max(I, ID) * 4));
-    TRYB(balloc(b, &b->fo, (size_t)B * K * H * 4));
+    TRYB(balloc(b, &b->fg, (size_t)std::max(NR * I, B * ID) * 4));
+    TRYB(balloc(b, &b->fu, (size_t)std::max(NR * I, B * ID) * 4));
+    TRYB(balloc(b, &b->fo, (size_t)NR * H * 4));
     TRYB(balloc(b, &b->rlog, (size_t)B * std::max(E, 1) * 4));
     TRYB(balloc(b, &b->logits, (size_t)B * c.vocab * 4));
     TRYB(balloc(b, &b->ridx, (size_t)std::max(n_moe, 1) * B * K * 4));
     TRYB(balloc(b, &b->rw, (size_t)B * K * 4));
-    TRYB(balloc(b, &b->inv, (size_t)B * K * 4));
-    TRYB(balloc(b, &b->src, (size_t)B * K * 4));
+    TRYB(balloc(b, &b->inv, (size_t)NR * 4));
+    TRYB(balloc(b, &b->src, (size_t)NR * 4));
+    if (world > 1) {
+        const size_t rows = (size_t)world * b->cap;
+        TRYB(balloc(b, &b->send_x, rows * H * 2));
+        TRYB(balloc(b, &b->recv_x, rows * H * 2));
+        TRYB(balloc(b, &b->send_meta, rows * 4));
+        TRYB(balloc(b, &b->recv_meta, rows * 4));
+        TRYB(balloc(b, &b->dest_pos, (size_t)B * K * 4));
+        TRYB(balloc(b, &b->back_o, rows * H * 4));
+        TRYB(balloc(b, &b->recv_back, rows * H * 4));
+        ncclUniqueId id;
+        memcpy(&id, nccl_id, sizeof(id));
+        if (ncclCommInitRank(&b->comm, world, id, rank) != ncclSuccess) {
+            b->comm = nullptr;
+            cuinf_batch_free(b);
+            return cuinf_set_arg_error("ncclCommInitRank failed");
+        }
+    }
     TRYB(balloc(b, &b->amax, (size_t)B * 8));
     b->nsplit = attn_batched_nsplit(c.n_heads, nkv, max_ctx, B, b->num_sms);
     TRYB(balloc(b, &b->apart, (size_t)B * attn_batched_part_floats(c.n_heads, nkv, b->nsplit) * 4));
     TRYB(balloc(b, &b->acnt, (size_t)B * nkv * 4));
-    const int maxch = (B + TC_NMAX - 1) / TC_NMAX;
+    const int maxch = (NR + TC_NMAX - 1) / TC_NMAX;
     TRYB(balloc(b, &b->g13, (size_t)2 * std::max(E, 1) * maxch * sizeof(TcGroup)));
     TRYB(balloc(b, &b->g2, (size_t)std::max(E, 1) * maxch * sizeof(TcGroup)));
     if (cudaHostAlloc(&b->pinned, (size_t)2 * B * 4, cudaHostAllocDefault) != cudaSuccess) {
@@ -911,8 +1062,8 @@ extern "C" int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void*
     TRYB(tc_map_act(&b->x_conv, b->conv_y, B, H, xb));
     TRYB(tc_map_act(&b->x_attn, b->attn_out, B, NQ, xb));
     TRYB(tc_map_act(&b->x_dmid, b->dmid, B, ID, xb));
-    TRYB(tc_map_act(&b->x_xg, b->xg, B * K, H, 16));
-    TRYB(tc_map_act(&b->x_mmid, b->mmid, B * K, I, 16));
+    TRYB(tc_map_act(&b->x_xg, b->xg, NR, H, 16));
+    TRYB(tc_map_act(&b->x_mmid, b->mmid, NR, I, 16));
     // weight maps
     auto add4 = [&](const Q4& q, int N, int Kd, int* idx) -> int {
         CUtensorMap mm;
@@ -1003,6 +1154,22 @@ extern "C" int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void*
     return CUINF_OK;
 #undef TRYB
 }
+
+extern "C" int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, cuinf_batch** out) {
+    return batch_create(m, n_seqs, max_ctx, stream, nullptr, 0, 1, out);
+}
+extern "C" int cuinf_batch_create_ep(cuinf_model* m, int n_seqs, int max_ctx, void* stream,
+                                     const unsigned char* nccl_id, int rank, int world, cuinf_batch** out) {
+    return batch_create(m, n_seqs, max_ctx, stream, nccl_id, rank, world, out);
+}
+extern "C" int cuinf_ep_unique_id(unsigned char* id, int id_bytes) {
+    REQUIRE(id && id_bytes >= (int)sizeof(ncclUniqueId), "id buffer too small");
+    ncclUniqueId u;
+    if (ncclGetUniqueId(&u) != ncclSuccess) return cuinf_set_arg_error("ncclGetUniqueId failed");
+    memcpy(id, &u, sizeof(u));
+    return CUINF_OK;
+}
+extern "C" int cuinf_ep_unique_id_bytes(void) { return (int)sizeof(ncclUniqueId); }
 
 extern "C" int cuinf_batch_reset(cuinf_batch* b) {
     REQUIRE(b, "null batch");

@@ -244,6 +244,10 @@ __device__ __forceinline__ bool tc_item(const TcParams& P, int it, int KG, TcIte
     t.kg0 = t.split * P.kg_per_split;
     t.nk = min(KG, t.kg0 + P.kg_per_split) - t.kg0;
     t.npad = (t.G.rows + 15) & ~15;
+    if (t.npad > P.xmax) {  // more rows than the activation stage holds: skip, report
+        if (threadIdx.x == 0 && P.err) atomicOr(P.err, 8u);
+        return false;
+    }
     t.koff = t.nk > 0 ? (int)((blockIdx.x * 5u + (unsigned)t.tile) % (unsigned)t.nk) : 0;
     return t.nk > 0;
 }

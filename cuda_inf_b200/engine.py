@@ -197,12 +197,18 @@ class Batch:
     """Sequence-batched decode (cuinf_batch_*): n_seqs independent sequences
     advance one token per step, all matmuls on the tensor-core GEMMs."""
 
-    def __init__(self, model, n_seqs, max_ctx, stream=None):
+    def __init__(self, model, n_seqs, max_ctx, stream=None, ep=None):
+        """ep = (nccl_id bytes, rank, world) for expert parallelism."""
         self.model = model
         self.n = n_seqs
         h = ctypes.c_void_p()
         st = ctypes.c_void_p(stream.cuda_stream) if stream is not None else None
-        check(lib().cuinf_batch_create(model._h, n_seqs, max_ctx, st, ctypes.byref(h)))
+        if ep is None:
+            check(lib().cuinf_batch_create(model._h, n_seqs, max_ctx, st, ctypes.byref(h)))
+        else:
+            uid, rank, world = ep
+            buf = (ctypes.c_ubyte * len(uid)).from_buffer_copy(bytes(uid))
+            check(lib().cuinf_batch_create_ep(model._h, n_seqs, max_ctx, st, buf, rank, world, ctypes.byref(h)))
         self._h = h
 
     def close(self):
@@ -265,3 +271,24 @@ class Batch:
         check(lib().cuinf_batch_profile_step(self._h, max_kernels, ms, names, name_len, ctypes.byref(n)))
         raw = names.raw
         return [(raw[i * name_len:(i + 1) * name_len].split(b"\0")[0].decode(), ms[i]) for i in range(n.value)]
+
+
+def ep_unique_id():
+    """A fresh NCCL unique id (bytes) for cuinf_batch_create_ep."""
+    n = lib().cuinf_ep_unique_id_bytes()
+    buf = (ctypes.c_ubyte * n)()
+    check(lib().cuinf_ep_unique_id(buf, n))
+    return bytes(buf)
+
+
+def ep_unique_id_shared(group=None):
+    """Rank 0's NCCL id broadcast over torch.distributed (any backend)."""
+    import torch.distributed as dist
+    n = lib().cuinf_ep_unique_id_bytes()
+    backend = dist.get_backend(group)
+    dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
+    t = torch.zeros(n, dtype=torch.uint8, device=dev)
+    if dist.get_rank(group) == 0:
+        t.copy_(torch.frombuffer(bytearray(ep_unique_id()), dtype=torch.uint8))
+    dist.broadcast(t, src=0, group=group)
+    return bytes(t.cpu().numpy().tobytes())

@@ -235,6 +235,17 @@ int cuinf_argmax_key_index(unsigned long long key);
  * step.  cuinf_batch_logits: device [n_seqs][vocab] while keep_logits is on. */
 typedef struct cuinf_batch cuinf_batch;
 int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, cuinf_batch** out);
+/* Expert-parallel form (BASELINE config 5 on `world` GPUs, one process per
+ * GPU): this rank decodes its own n_seqs sequences and hosts experts
+ * [rank*E/world, (rank+1)*E/world); per MoE layer each (token, slot) row goes
+ * to its expert's rank and the fp32 expert output comes back, by NCCL
+ * send/recv on the batch stream inside the step graph (fixed capacity
+ * n_seqs*top_k rows per peer).  nccl_id: cuinf_ep_unique_id on rank 0,
+ * broadcast to all ranks.  Every rank steps together. */
+int cuinf_batch_create_ep(cuinf_model* m, int n_seqs, int max_ctx, void* stream, const unsigned char* nccl_id,
+                          int rank, int world, cuinf_batch** out);
+int cuinf_ep_unique_id(unsigned char* id, int id_bytes);
+int cuinf_ep_unique_id_bytes(void);
 int cuinf_batch_free(cuinf_batch* b);
 int cuinf_batch_reset(cuinf_batch* b);
 int cuinf_batch_step(cuinf_batch* b, const int* tokens, int* out_tokens);
@@ -244,7 +255,8 @@ int cuinf_batch_routes(cuinf_batch* b, int* idx);
 int cuinf_batch_kernels_per_step(const cuinf_batch* b);
 int cuinf_batch_fill_synthetic(cuinf_batch* b, int ctx, unsigned long long seed);
 /* Error words of the tensor-core kernels, flags[4]: [0] bit 1 a bounded
- * pipeline wait timed out, bit 2 a final drain did; [1] the wait's barrier
+ * pipeline wait timed out, bit 2 a final drain did, bit 3 a group had more
+ * rows than its launch allowed (skipped); [1] the wait's barrier
  * code, [2] its block, [3] its stage counter (first failure). */
 int cuinf_batch_error(unsigned* flags);
 /* One step launched eagerly with an event after each launch: ms[i] is the
