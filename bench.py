@@ -336,8 +336,69 @@ def run_ours(a, ws, rank):
     if rank == 0 and ws == 1 and not a.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(cfg, blob, idx, a.cpu_budget)
     sess.close()
+    if a.batch > 0 and not a.profile_small:
+        out["batched_ep"] = run_batched(a, ws, rank, model, cfg)
     model.close()
     return out
+
+
+def run_batched(a, ws, rank, model, cfg):
+    """Config 5: a.batch sequences at context 2048 decoding together, split
+    over the ranks with the experts sharded (E/ws per GPU) and the (token,
+    slot) rows exchanged over NCCL each MoE layer; one GPU runs them all with
+    every expert local.  value = all sequences' tokens / max-over-ranks time."""
+    from cuda_inf_b200.engine import Batch, ep_unique_id_shared
+    if a.batch % ws or cfg.n_experts % ws:
+        return {"skipped": f"batch {a.batch} or {cfg.n_experts} experts not divisible by {ws} GPUs"}
+    B = a.batch // ws
+    ctx = 2048
+    stream = torch.cuda.Stream()
+    ep = (ep_unique_id_shared(), rank, ws) if ws > 1 else None
+    bt = Batch(model, B, max_ctx=ctx + a.batch_warmup + 2 * a.batch_steps + 64, stream=stream, ep=ep)
+    bt.fill_synthetic(ctx, seed=a.seed + rank)
+    toks = prompt_ids(a.seed, B, cfg.vocab, rank)
+    bt.step(toks)
+    for _ in range(a.batch_warmup):
+        bt.step(None, want=False)
+    torch.cuda.synchronize()
+    barrier(ws)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ev0.record(stream)
+        for _ in range(a.batch_steps):
+            bt.step(None, want=False)
+        ev1.record(stream)
+        stream.synchronize()
+    barrier(ws)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), ws)
+    # end to end through the public API: tokens in from the host, argmaxes out
+    cur = bt.step(None, want=True)
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(a.batch_steps):
+        cur = bt.step(cur, want=True)
+    e1.record(stream)
+    stream.synchronize()
+    barrier(ws)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), ws)
+    err = Batch.error()
+    kps = bt.kernels_per_step
+    bt.close()  # its step graph holds NCCL calls: released before the process group
+    return {
+        "workload": f"config 5: {a.batch} sequences at context {ctx}, batched decode",
+        "parallelism": f"expert-parallel x{ws} ({cfg.n_experts // ws} experts per GPU, NCCL send/recv)"
+                       if ws > 1 else "single GPU, all experts local",
+        "value": round(a.batch * a.batch_steps / (ms / 1e3), 1), "unit": "tok/s",
+        "ms_per_step": round(ms / a.batch_steps, 4), "steps": a.batch_steps, "warmup": a.batch_warmup,
+        "scaling": "strong", "sequences_per_gpu": B,
+        "e2e": {"value": round(a.batch * a.batch_steps / (e2e_ms / 1e3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
+        "gpu_launches": kps * a.batch_steps, "device_errors": err,
+        "data": "synthetic FP8 caches at context 2048 (seeded), random-init weights",
+        "clocks": clk.summary(),
+    }
 
 
 def run_reference(a, ws, rank):
@@ -397,6 +458,10 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the config-1 INT4 GEMV measurement (for profiler captures)")
+    ap.add_argument("--batch", type=int, default=64,
+                    help="config 5 batched decode: total sequences (0 = skip)")
+    ap.add_argument("--batch-steps", type=int, default=20)
+    ap.add_argument("--batch-warmup", type=int, default=3)
     ap.add_argument("--profile-small", action="store_true",
                     help="6-layer, 32k-vocab model of the same shapes, for profiler captures only")
     a = ap.parse_args()
