@@ -204,6 +204,51 @@ def gemv_config1(copies=24, graphs=10):
             "calls_timed": graphs * copies}
 
 
+def gemm_tc_batch(M=64, copies=24, graphs=10):
+    """The tensor-core INT4 GEMM (cuinf_gemm_int4_tc, tcgen05) on the config-1
+    weight shape at M activation rows (a config-5 batch): rotating `copies`
+    weight copies (> L2), launches captured in a CUDA graph.  Algorithmic
+    bytes per call: packed + scales + x (M x 2048 fp16) + y (M x 7168 fp32)."""
+    from cuda_inf_b200 import ops
+    N, K = 7168, 2048
+    g = torch.Generator(device="cuda")
+    g.manual_seed(13)
+    packed = [torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda", generator=g)
+              for _ in range(copies)]
+    scales = [torch.exp(torch.empty(N, K // 128, device="cuda").uniform_(np.log(0.005), np.log(0.05),
+                                                                          generator=g)).half()
+              for _ in range(copies)]
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    y = torch.empty(M, N, dtype=torch.float32, device="cuda")
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        for i in range(copies):  # warm-up: kernel load, split-K workspace
+            ops.gemm_int4_tc(x, packed[i], scales[i], y)
+        st.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            for i in range(copies):
+                ops.gemm_int4_tc(x, packed[i], scales[i], y)
+        graph.replay()
+        st.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(graphs):
+            graph.replay()
+        e1.record(st)
+        st.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (graphs * copies)
+    bpc = N * K // 2 + N * (K // 128) * 2 + M * K * 2 + M * N * 4
+    flops = 2 * M * N * K
+    peak, kind = hbm_peak()
+    gbps = bpc / (us * 1e-6) / 1e9
+    del graph
+    return {"kernel": "k_tc_gemm", "shape": f"7168x2048 INT4 G=128, {M} activation rows", "us_per_call": round(us, 3),
+            "bytes_per_call": bpc, "achieved": round(gbps, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(gbps / peak, 4), "peak_source": kind, "tflops": round(flops / (us * 1e-6) / 1e12, 2),
+            "weight_copies": copies, "calls_timed": graphs * copies}
+
+
 def cpu_baseline(cfg, blob, idx, budget_s=20.0):
     """The CPU oracle (scalar C restatement, OpenMP over output rows) decoding
     the same model on this host: a bounded sample of the first positions."""
@@ -383,6 +428,13 @@ def run_batched(a, ws, rank, model, cfg):
     stream.synchronize()
     barrier(ws)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), ws)
+    # one step launched kernel by kernel (CUDA events between launches)
+    agg = {}
+    for name, kms in bt.profile_step():
+        d = agg.setdefault(name, [0, 0.0])
+        d[0] += 1
+        d[1] += kms
+    tot = sum(v[1] for v in agg.values())
     err = Batch.error()
     kps = bt.kernels_per_step
     bt.close()  # its step graph holds NCCL calls: released before the process group
@@ -396,6 +448,8 @@ def run_batched(a, ws, rank, model, cfg):
         "e2e": {"value": round(a.batch * a.batch_steps / (e2e_ms / 1e3), 1), "unit": "tok/s",
                 "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
         "gpu_launches": kps * a.batch_steps, "device_errors": err,
+        "kernel_breakdown_eager": {k: {"launches": v[0], "ms": round(v[1], 4), "share": round(v[1] / tot, 3)}
+                                   for k, v in sorted(agg.items(), key=lambda kv: -kv[1][1])},
         "data": "synthetic FP8 caches at context 2048 (seeded), random-init weights",
         "clocks": clk.summary(),
     }
@@ -458,6 +512,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the config-1 INT4 GEMV measurement (for profiler captures)")
+    ap.add_argument("--tc-gemm-only", action="store_true",
+                    help="only the tensor-core INT4 GEMM at 64 rows (for profiler captures)")
     ap.add_argument("--batch", type=int, default=64,
                     help="config 5 batched decode: total sequences (0 = skip)")
     ap.add_argument("--batch-steps", type=int, default=20)
@@ -479,11 +535,18 @@ def main():
         if ws > 1:
             torch.distributed.destroy_process_group()
         return
+    if a.tc_gemm_only:
+        if rank == 0:
+            print(json.dumps({"profiling_only": True, "gemm_int4_tc_batch64": gemm_tc_batch()}), flush=True)
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+        return
     if a.profile_small:
         a.no_cpu_baseline = True
     out = run_ours(a, ws, rank)
     if not a.profile_small:
         out["gemv_int4_config1"] = gemv_config1()
+        out["gemm_int4_tc_batch64"] = gemm_tc_batch()
     if a.profile_small:
         out = {"profiling_only": True, "ms_per_step": out["ms_per_step"],
                "kernel_breakdown": out["kernel_breakdown"]}
