@@ -249,6 +249,109 @@ def gemm_tc_batch(M=64, copies=24, graphs=10):
             "weight_copies": copies, "calls_timed": graphs * copies}
 
 
+def _graph_time(fn, n_inner, graphs=10):
+    """Capture fn() (n_inner launches) in a CUDA graph after a warm-up call,
+    replay it `graphs` times; returns us per inner launch (CUDA events)."""
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        fn()
+        st.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            fn()
+        graph.replay()
+        st.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(graphs):
+            graph.replay()
+        e1.record(st)
+        st.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (graphs * n_inner)
+    del graph
+    return us
+
+
+def moe_config2(layers=8):
+    """Config 2: one MoE FFN decode layer, batch 1 (cuinf_moe_ffn: router,
+    sigmoid + bias top-4, norm_topk_prob, 4 x SwiGLU experts, weighted sum and
+    residual), over `layers` distinct layers of 32 random INT4 experts (the
+    selected experts' weights, 8 x 22.7 MB, exceed L2).  Algorithmic bytes
+    per call: 4 experts x 5,677,056 + gate 131,072 + bias 64 + x 4,096 +
+    h read/write 8,192."""
+    from cuda_inf_b200 import ops
+    H, I, E, K = 2048, 1792, 32, 4
+    g = torch.Generator(device="cuda")
+    g.manual_seed(21)
+
+    def q4(n, k):
+        p = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device="cuda", generator=g)
+        sc = torch.exp(torch.empty(n, k // 128, device="cuda").uniform_(np.log(0.005), np.log(0.05),
+                                                                        generator=g)).half()
+        return p, sc
+    keep, tables, gates, biases = [], [], [], []
+    for _ in range(layers):
+        experts = [q4(I, H) + q4(I, H) + q4(H, I) for _ in range(E)]
+        keep.append(experts)
+        tables.append(ops.expert_table([(a, b, c, d, e, f) for a, b, c, d, e, f in experts]))
+        gates.append((0.02 * torch.randn(E, H, device="cuda", generator=g)).half())
+        biases.append((0.1 * torch.randn(E, device="cuda", generator=g)).half())
+    xs = [torch.randn(H, device="cuda", generator=g).half() for _ in range(layers)]
+    h = torch.zeros(H, device="cuda").half()
+
+    def run():
+        for i in range(layers):
+            ops.moe_ffn(xs[i], gates[i], biases[i], tables[i], h, K, I)
+    us = _graph_time(run, layers)
+    bpc = 4 * 5_677_056 + 131_072 + 64 + 4_096 + 8_192
+    peak, kind = hbm_peak()
+    gbps = bpc / (us * 1e-6) / 1e9
+    return {"kernels": "k_moe_up + k_moe_down", "shape": "H 2048, 32 experts, I 1792, top-4, batch 1",
+            "us_per_layer": round(us, 3), "bytes_per_layer": bpc, "achieved": round(gbps, 1), "peak": peak,
+            "unit": "GB/s", "frac": round(gbps / peak, 4), "peak_source": kind, "layers_rotated": layers}
+
+
+def attn_config3(ctxs=(2048, 8192, 32768)):
+    """Config 3: FP8 E4M3 KV flash-decoding attention for one GQA layer (32 q /
+    8 kv heads, head_dim 64) at each context, over enough distinct caches to
+    exceed L2; tail = ctx mod 64 (0 here).  QK-norm and RoPE of the query run
+    in the engine's q/k/v kernel, not here.  Algorithmic bytes per call:
+    1024*C + (C/64)*32 + 2048*(ctx - C) + q/out 8,192."""
+    from cuda_inf_b200 import ops
+    nh, nkv = 32, 8
+    out = {}
+    peak, kind = hbm_peak()
+    for ctx in ctxs:
+        C = (ctx // 64) * 64
+        per = 1024 * C + (C // 64) * 32 + 2048 * (ctx - C) + 8192
+        copies = max(2, int(np.ceil(160e6 / per)))
+        g = torch.Generator(device="cuda")
+        g.manual_seed(ctx)
+        caches = []
+        for _ in range(copies):
+            kc = (torch.randint(0, 256, (ctx, nkv, 64), dtype=torch.uint8, device="cuda", generator=g) & 0x77)
+            vc = (torch.randint(0, 256, (ctx, nkv, 64), dtype=torch.uint8, device="cuda", generator=g) & 0x77)
+            ks = torch.full((C // 64 + 1, nkv), 1.0 / 64, dtype=torch.float16, device="cuda")
+            vs = torch.full((C // 64 + 1, nkv), 1.0 / 64, dtype=torch.float16, device="cuda")
+            kt = torch.randn(64, nkv, 64, device="cuda", generator=g).half()
+            vt = torch.randn(64, nkv, 64, device="cuda", generator=g).half()
+            caches.append((kc, vc, ks, vs, kt, vt))
+        q = torch.randn(nh, 64, device="cuda", generator=g).half()
+        o = torch.empty_like(q)
+
+        def run():
+            for kc, vc, ks, vs, kt, vt in caches:
+                ops.attn_decode(q, kc, vc, ks, vs, kt, vt, C, ctx - 1, 0.125, o)
+        us = _graph_time(run, copies)
+        gbps = per / (us * 1e-6) / 1e9
+        out[str(ctx)] = {"us_per_call": round(us, 3), "bytes_per_call": per, "achieved": round(gbps, 1),
+                         "frac": round(gbps / peak, 4), "caches_rotated": copies}
+        del caches
+        torch.cuda.empty_cache()
+    return {"kernel": "k_attn_decode", "shape": "32 q / 8 kv heads, hd 64, FP8 groups of 64 + fp16 tail",
+            "peak": peak, "unit": "GB/s", "peak_source": kind, "by_context": out}
+
+
 def cpu_baseline(cfg, blob, idx, budget_s=20.0):
     """The CPU oracle (scalar C restatement, OpenMP over output rows) decoding
     the same model on this host: a bounded sample of the first positions."""
@@ -512,6 +615,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the config-1 INT4 GEMV measurement (for profiler captures)")
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="only the config-2 MoE layer and config-3 attention measurements")
     ap.add_argument("--tc-gemm-only", action="store_true",
                     help="only the tensor-core INT4 GEMM at 64 rows (for profiler captures)")
     ap.add_argument("--batch", type=int, default=64,
@@ -535,6 +640,13 @@ def main():
         if ws > 1:
             torch.distributed.destroy_process_group()
         return
+    if a.kernels_only:
+        if rank == 0:
+            print(json.dumps({"profiling_only": True, "moe_ffn_config2": moe_config2(),
+                              "attention_config3": attn_config3()}), flush=True)
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+        return
     if a.tc_gemm_only:
         if rank == 0:
             print(json.dumps({"profiling_only": True, "gemm_int4_tc_batch64": gemm_tc_batch()}), flush=True)
@@ -547,6 +659,11 @@ def main():
     if not a.profile_small:
         out["gemv_int4_config1"] = gemv_config1()
         out["gemm_int4_tc_batch64"] = gemm_tc_batch()
+        for key, fn in (("moe_ffn_config2", moe_config2), ("attention_config3", attn_config3)):
+            try:
+                out[key] = fn()
+            except Exception as e:  # a side measurement never takes the headline line down
+                out[key] = {"error": str(e)[:300]}
     if a.profile_small:
         out = {"profiling_only": True, "ms_per_step": out["ms_per_step"],
                "kernel_breakdown": out["kernel_breakdown"]}
