@@ -85,6 +85,8 @@ _SIGS = {
     "cuinf_session_keep_logits": (c_int, [c_void_p, c_int]),
     "cuinf_session_set_option": (c_int, [c_void_p, c_int, c_int]),
     "cuinf_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "cuinf_session_set_kv_budget": (c_int, [c_void_p, c_int, c_int]),
+    "cuinf_session_h2o_state": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "cuinf_batch_create": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "cuinf_batch_free": (c_int, [c_void_p]),
     "cuinf_batch_reset": (c_int, [c_void_p]),

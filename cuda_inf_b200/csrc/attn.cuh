@@ -425,3 +425,183 @@ static inline int attn_default_nsplit(int nkv, int gqa, int max_units, int num_s
     if (ns < 1) ns = 1;
     return ns;
 }
+
+// ---------------------------------------------------------------------------
+// H2O eviction mode (engine.cu:310-384, 803-828): a circular buffer of C
+// per-token FP8 slots per attention layer, each with its own per-head fp16
+// scale, its logical position and its cumulative attention mass.
+// ---------------------------------------------------------------------------
+#define H2O_MAX_SLOTS 8192
+struct H2oParams {
+    const __half *k_new, *v_new;  // [S][nkv][64] the fresh tokens' K/V
+    const __half* q;              // [S][nh][64]
+    __half* out;                  // [S][nh][64]
+    const int* pos_dev;           // decode: the token's position (S = 1); null: past
+    int past, S, C, W, nh, nkv;
+    float scale;
+    uint8_t *hk8, *hv8;  // [C][nkv][64]
+    __half *hks, *hvs;   // [C][nkv]
+    int* slot_pos;       // [C]
+    float* attn_sum;     // [C]
+    int* n_live;         // [1]
+    int* dst;            // [S] slot of each fresh token
+};
+
+// Slot choice for the S fresh tokens in order (the reference's host loop,
+// engine.cu:808-823): append while there is room; else the least cumulative
+// attention among slots outside the local window (pos <= p - W), first such
+// minimum; else the least overall; slots picked earlier in the same batch are
+// excluded.  A reused slot's mass restarts at 0.  Then kv_quant_write
+// (317-333): per token and head, scale = absmax/448 + 1e-12, codes
+// e4m3(x / scale).  One CTA of 256 threads.
+__global__ void __launch_bounds__(256) k_h2o_place(H2oParams P) {
+    __shared__ unsigned char banned[H2O_MAX_SLOTS];
+    __shared__ float rv[8];
+    __shared__ int ri[8];
+    __shared__ int s_live, s_slot;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int t = tid; t < P.C; t += blockDim.x) banned[t] = 0;
+    pdl_wait();
+    if (tid == 0) s_live = *P.n_live;
+    __syncthreads();
+    const int base = P.pos_dev ? *P.pos_dev : P.past;
+    for (int j = 0; j < P.S; j++) {
+        const int pos = base + j;
+        if (s_live < P.C) {
+            if (tid == 0) s_slot = s_live;
+        } else {
+            for (int pass = 0; pass < 2; pass++) {
+                float v = 1e30f;
+                int idx = 0x7fffffff;
+                for (int t = tid; t < P.C; t += blockDim.x) {
+                    const float a = banned[t] ? 1e30f : P.attn_sum[t];
+                    if ((pass == 1 || P.slot_pos[t] <= pos - P.W) && a < v) {
+                        v = a;
+                        idx = t;
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+                    if (ov < v || (ov == v && oi < idx)) {
+                        v = ov;
+                        idx = oi;
+                    }
+                }
+                if (lane == 0) {
+                    rv[warp] = v;
+                    ri[warp] = idx;
+                }
+                __syncthreads();
+                if (tid == 0) {
+                    float bv = rv[0];
+                    int bi = ri[0];
+                    for (int w = 1; w < 8; w++)
+                        if (rv[w] < bv || (rv[w] == bv && ri[w] < bi)) {
+                            bv = rv[w];
+                            bi = ri[w];
+                        }
+                    s_slot = bi;
+                }
+                __syncthreads();
+                if (s_slot != 0x7fffffff) break;
+            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const int slot = s_slot;
+            if (s_live < P.C && slot == s_live) s_live++;
+            banned[slot] = 1;
+            P.attn_sum[slot] = 0.f;
+            P.slot_pos[slot] = pos;
+            P.dst[j] = slot;
+        }
+        __syncthreads();
+    }
+    if (tid == 0) *P.n_live = s_live;
+    // quantize every (token, head, K|V) row of 64 into its slot: one warp per row
+    for (int r = warp; r < P.S * P.nkv * 2; r += 8) {
+        const int which = r & 1, jh = r >> 1, j = jh / P.nkv, h = jh - j * P.nkv;
+        const __half* src = (which ? P.v_new : P.k_new) + ((size_t)j * P.nkv + h) * CUINF_HD;
+        const float x0 = __half2float(src[2 * lane]), x1 = __half2float(src[2 * lane + 1]);
+        const float mx = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
+        const float sc = mx / 448.0f + 1e-12f;
+        const int slot = P.dst[j];
+        uint8_t* d8 = (which ? P.hv8 : P.hk8) + ((size_t)slot * P.nkv + h) * CUINF_HD;
+        d8[2 * lane] = (uint8_t)__nv_cvt_float_to_fp8(x0 / sc, __NV_SATFINITE, __NV_E4M3);
+        d8[2 * lane + 1] = (uint8_t)__nv_cvt_float_to_fp8(x1 / sc, __NV_SATFINITE, __NV_E4M3);
+        if (lane == 0) (which ? P.hvs : P.hks)[slot * P.nkv + h] = __float2half_rn(sc);
+    }
+}
+
+// attention_h2o (engine.cu:337-384): query i of S (position base + i), head
+// h, over the live slots with position <= the query's; exact two-pass
+// softmax; each slot's normalized probability is added to its cumulative
+// attention.  grid (S, nh), 256 threads, dynamic smem C floats.
+__global__ void __launch_bounds__(256) k_h2o_attn(H2oParams P) {
+    extern __shared__ float h2o_sm[];
+    __shared__ float qs[CUINF_HD];
+    __shared__ float red[32];
+    __shared__ float part[4][CUINF_HD];
+    const int i = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const int kvh = h / (P.nh / P.nkv);
+    pdl_wait();
+    const int qpos = (P.pos_dev ? *P.pos_dev : P.past) + i;
+    const int n = *P.n_live;
+    if (tid < CUINF_HD) qs[tid] = __half2float(P.q[((size_t)i * P.nh + h) * CUINF_HD + tid]);
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int t = tid; t < n; t += blockDim.x) {
+        float s = -INFINITY;
+        if (P.slot_pos[t] <= qpos) {
+            const float ks = __half2float(P.hks[t * P.nkv + kvh]);
+            const uint8_t* kp = P.hk8 + ((size_t)t * P.nkv + kvh) * CUINF_HD;
+            float acc = 0.f;
+#pragma unroll
+            for (int d = 0; d < CUINF_HD; d += 2) {
+                const uint32_t kb = fp8x2_to_h2(*reinterpret_cast<const uint16_t*>(kp + d));
+                const __half2 k2 = *reinterpret_cast<const __half2*>(&kb);
+                acc += qs[d] * (__low2float(k2) * ks) + qs[d + 1] * (__high2float(k2) * ks);
+            }
+            s = acc * P.scale;
+        }
+        h2o_sm[t] = s;
+        mx = fmaxf(mx, s);
+    }
+    mx = warp_max(mx);
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    float m = -INFINITY;
+    for (int w = 0; w < 8; w++) m = fmaxf(m, red[w]);
+    __syncthreads();
+    float l = 0.f;
+    for (int t = tid; t < n; t += blockDim.x) {
+        const float p = h2o_sm[t] == -INFINITY ? 0.f : __expf(h2o_sm[t] - m);
+        h2o_sm[t] = p;
+        l += p;
+    }
+    const float L = block_sum(l, red);
+    __syncthreads();
+    const float inv = 1.f / L;
+    for (int t = tid; t < n; t += blockDim.x)
+        if (h2o_sm[t] > 0.f) atomicAdd(&P.attn_sum[t], h2o_sm[t] * inv);
+    // o[d] = sum_t p_t v_t[d]: four groups of 64 threads over t mod 4
+    const int g = tid >> 6, d = tid & 63;
+    float o = 0.f;
+    for (int t = g; t < n; t += 4) {
+        const float p = h2o_sm[t];
+        if (p > 0.f) {
+            const float vs = __half2float(P.hvs[t * P.nkv + kvh]);
+            const uint8_t vb = P.hv8[((size_t)t * P.nkv + kvh) * CUINF_HD + d];
+            const __half vh = __ushort_as_half((unsigned short)(fp8x2_to_h2(vb) & 0xFFFFu));
+            o += p * (__half2float(vh) * vs);
+        }
+    }
+    part[g][d] = o;
+    __syncthreads();
+    if (tid < CUINF_HD) {
+        const float s = part[0][tid] + part[1][tid] + part[2][tid] + part[3][tid];
+        P.out[((size_t)i * P.nh + h) * CUINF_HD + tid] = __float2half_rn(s * inv);
+    }
+}

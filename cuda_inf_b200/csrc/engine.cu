@@ -651,6 +651,18 @@ struct cuinf_session {
     // prefill scratch, grown to the longest prompt seen (freed with the session)
     int pf_cap = 0;
     void* pf_buf = nullptr;
+    // H2O eviction mode (0 slots = off): per attention layer C per-token FP8 slots
+    int h2o_C = 0, h2o_W = 0;
+    struct H2o {
+        uint8_t *hk8 = nullptr, *hv8 = nullptr;
+        __half *hks = nullptr, *hvs = nullptr;
+        int* slot_pos = nullptr;
+        float* attn_sum = nullptr;
+        int* n_live = nullptr;
+    };
+    std::vector<H2o> h2o;
+    __half* kv_new = nullptr;  // the decode token's K then V, [2][nkv][64]
+    int* h2o_dst = nullptr;    // [n_layers] slot chosen in the last step
 };
 
 template <class T>
@@ -875,8 +887,36 @@ static int record_step_mk(cuinf_session* s) {
 
 // Records one decode step into the session stream (under capture, or eagerly
 // with per-kernel events when prof is set).
+static H2oParams h2o_params(cuinf_session* s, int l, const __half* k_new, const __half* v_new, const __half* q,
+                            __half* out, const int* pos_dev, int past, int S, int* dst) {
+    const cuinf_config& c = s->m->cfg;
+    const cuinf_session::H2o& Z = s->h2o[l];
+    H2oParams P;
+    P.k_new = k_new;
+    P.v_new = v_new;
+    P.q = q;
+    P.out = out;
+    P.pos_dev = pos_dev;
+    P.past = past;
+    P.S = S;
+    P.C = s->h2o_C;
+    P.W = s->h2o_W;
+    P.nh = c.n_heads;
+    P.nkv = c.n_kv_heads;
+    P.scale = 1.0f / sqrtf((float)c.head_dim);
+    P.hk8 = Z.hk8;
+    P.hv8 = Z.hv8;
+    P.hks = Z.hks;
+    P.hvs = Z.hvs;
+    P.slot_pos = Z.slot_pos;
+    P.attn_sum = Z.attn_sum;
+    P.n_live = Z.n_live;
+    P.dst = dst;
+    return P;
+}
+
 static int record_step(cuinf_session* s, Prof* prof = nullptr) {
-    if (s->use_mk && s->mk_ok && !prof) return record_step_mk(s);
+    if (s->use_mk && s->mk_ok && !prof && !s->h2o_C) return record_step_mk(s);
     const cuinf_model* m = s->m;
     const cuinf_config& c = m->cfg;
     const int H = c.hidden;
@@ -904,6 +944,7 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
             Q.ktail = A.ktail; Q.vtail = A.vtail;
             Q.kc8 = A.kc8; Q.vc8 = A.vc8;
             Q.ksc = A.ksc; Q.vsc = A.vsc;
+            Q.kv_new = s->h2o_C ? s->kv_new : nullptr;
             Q.H = H; Q.nh = nh; Q.nkv = nkv;
             Q.eps = c.norm_eps; Q.theta = c.rope_theta;
             const int heads = nh + 2 * nkv;
@@ -927,12 +968,27 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
             P.nh = nh; P.nkv = nkv; P.nsplit = s->nsplit;
             const double ctx = s->host_pos + 1, cm = 64.0 * floor(ctx / 64.0);
             const int nsplit = s->nsplit;
-            Ls.push_back({"attn_decode", cm * nkv * 128 + cm / 64 * nkv * 4 + (ctx - cm) * nkv * 256 + nh * 256.0,
-                          {},
-                          [=](const L2Ranges& nx, bool pdl) mutable {
-                              P.next = nx;
-                              return launch_k(k_attn_decode, dim3(nkv, nsplit), dim3(ATTN_THREADS), 0, st, pdl, P);
-                          }});
+            if (s->h2o_C) {  // H2O: slot choice + quantized write, then attention over the slots
+                H2oParams Z = h2o_params(s, l, s->kv_new, s->kv_new + nkv * 64, s->q, s->attn_out, s->pos, 0, 1,
+                                         s->h2o_dst + l);
+                const double live = std::min<double>(ctx, s->h2o_C);
+                Ls.push_back({"h2o_place", 12.0 * s->h2o_C + nkv * 256.0, {},
+                              [=](const L2Ranges&, bool pdl) mutable {
+                                  return launch_k(k_h2o_place, dim3(1), dim3(256), 0, st, pdl, Z);
+                              }});
+                const size_t smz = (size_t)s->h2o_C * 4;
+                Ls.push_back({"h2o_attention", live * (nkv * 132.0 + 12.0) * 1.0 + nh * 256.0, {},
+                              [=](const L2Ranges&, bool pdl) mutable {
+                                  return launch_k(k_h2o_attn, dim3(1, nh), dim3(256), smz, st, pdl, Z);
+                              }});
+            } else {
+                Ls.push_back({"attn_decode", cm * nkv * 128 + cm / 64 * nkv * 4 + (ctx - cm) * nkv * 256 + nh * 256.0,
+                              {},
+                              [=](const L2Ranges& nx, bool pdl) mutable {
+                                  P.next = nx;
+                                  return launch_k(k_attn_decode, dim3(nkv, nsplit), dim3(ATTN_THREADS), 0, st, pdl, P);
+                              }});
+            }
             ResParams R;
             R.act = s->attn_out; R.wp = L.wo.p; R.ws = L.wo.s; R.h = s->h; R.N = H; R.K = nh * 64;
             Ls.push_back({"attn_out_proj", q4_bytes(H, nh * 64) + nh * 128 + 4.0 * H,
@@ -1093,6 +1149,12 @@ extern "C" int cuinf_session_free(cuinf_session* s) {
     if (!s) return CUINF_OK;
     if (s->st) cudaStreamSynchronize(s->st);
     if (s->pf_buf) cudaFree(s->pf_buf);
+    for (auto& Z : s->h2o) {
+        cudaFree(Z.hk8); cudaFree(Z.hv8); cudaFree(Z.hks); cudaFree(Z.hvs);
+        cudaFree(Z.slot_pos); cudaFree(Z.attn_sum); cudaFree(Z.n_live);
+    }
+    if (s->kv_new) cudaFree(s->kv_new);
+    if (s->h2o_dst) cudaFree(s->h2o_dst);
     if (s->exec) cudaGraphExecDestroy(s->exec);
     if (s->graph) cudaGraphDestroy(s->graph);
     for (void* p : s->allocs) cudaFree(p);
@@ -1186,6 +1248,12 @@ extern "C" int cuinf_session_reset(cuinf_session* s) {
             CUINF_TRY(cudaMemsetAsync(s->conv_state[l], 0, (size_t)2 * c.hidden * 2, s->st));
         }
     }
+    for (auto& Z : s->h2o)
+        if (Z.n_live) {
+            CUINF_TRY(cudaMemsetAsync(Z.n_live, 0, 4, s->st));
+            CUINF_TRY(cudaMemsetAsync(Z.attn_sum, 0, (size_t)s->h2o_C * 4, s->st));
+            CUINF_TRY(cudaMemsetAsync(Z.slot_pos, 0, (size_t)s->h2o_C * 4, s->st));
+        }
     CUINF_TRY(cudaMemsetAsync(s->pos, 0, 4, s->st));
     if (s->mk_words) CUINF_TRY(cudaMemsetAsync(s->mk_words, 0, 64, s->st));
     CUINF_TRY(cudaStreamSynchronize(s->st));
@@ -1233,6 +1301,7 @@ extern "C" int cuinf_prefill(cuinf_session* s, const int* ids, int S, int* out_t
     const cuinf_model* m = s->m;
     const cuinf_config& c = m->cfg;
     REQUIRE(s->host_pos + S <= s->max_ctx, "context too long for max_ctx");
+    REQUIRE(!s->h2o_C || S <= s->h2o_C, "with a KV budget the prompt must fit the budget (engine.cu:753)");
     for (int i = 0; i < S; i++) REQUIRE(ids[i] >= 0 && ids[i] < c.vocab, "token out of range");
     const int H = c.hidden, nh = c.n_heads, nkv = c.n_kv_heads, hd = 64, E = c.n_experts, K = c.top_k;
     const int NQ = nh * hd, NK = nkv * hd;
@@ -1296,6 +1365,18 @@ extern "C" int cuinf_prefill(cuinf_session* s, const int* ids, int S, int* out_t
             PF(cuinf_rmsnorm(q16, L.q_ln, q16, S * nh, hd, c.norm_eps, vs));
             PF(cuinf_rmsnorm(k16, L.k_ln, k16, S * nkv, hd, c.norm_eps, vs));
             PF(cuinf_rope(q16, k16, d_pos, S, nh, nkv, c.rope_theta, vs));
+            if (s->h2o_C) {  // H2O: every fresh token's slot, then every query over the slots
+                // d_ids (consumed by the embedding gather) holds the chosen slots
+                H2oParams Z = h2o_params(s, l, k16, v16, q16, ao, nullptr, past, S, d_ids);
+                k_h2o_place<<<1, 256, 0, st>>>(Z);
+                PF(cuinf_launch_status());
+                k_h2o_attn<<<dim3(S, nh), 256, (size_t)s->h2o_C * 4, st>>>(Z);
+                PF(cuinf_launch_status());
+                PF(cuinf_gemv_int4(ao, L.wo.p, L.wo.s, fa, S, H, NQ, vs));
+                PF(cuinf_add_f32_inplace(hs, fa, S * H, vs));
+                goto ffn;
+            }
+            {
             int committed = (past / CUINF_KVGROUP) * CUINF_KVGROUP;
             for (int placed = 0; placed < S;) {
                 const int slot = past + placed - committed;
@@ -1314,6 +1395,7 @@ extern "C" int cuinf_prefill(cuinf_session* s, const int* ids, int S, int* out_t
             PF(cuinf_launch_status());
             PF(cuinf_gemv_int4(ao, L.wo.p, L.wo.s, fa, S, H, NQ, vs));
             PF(cuinf_add_f32_inplace(hs, fa, S * H, vs));
+            }
         } else {
             PF(cuinf_gemv_int4(xn, L.in_proj.p, L.in_proj.s, fa, S, 3 * H, H, vs));
             PF(cuinf_conv_pre(fa, t16, t16b, S, H, vs));
@@ -1322,6 +1404,7 @@ extern "C" int cuinf_prefill(cuinf_session* s, const int* ids, int S, int* out_t
             PF(cuinf_gemv_int4(acc, L.out_proj.p, L.out_proj.s, fa, S, H, H, vs));
             PF(cuinf_add_f32_inplace(hs, fa, S * H, vs));
         }
+    ffn:
         PF(cuinf_rmsnorm(hs, L.ffn_norm, xn, S, H, c.norm_eps, vs));
         if (l < c.n_dense) {
             const int I = c.dense_inter;
@@ -1390,6 +1473,68 @@ extern "C" int cuinf_generate(cuinf_session* s, const int* prompt, int n_prompt,
     return CUINF_OK;
 }
 
+// H2O eviction mode (engine.cu:579-581, 753-756): budget slots per attention
+// layer, local window W (<= 0: budget/2).  Only before the first token.
+extern "C" int cuinf_session_set_kv_budget(cuinf_session* s, int budget, int window) {
+    REQUIRE(s, "null session");
+    REQUIRE(s->host_pos == 0, "set the KV budget before the first token");
+    REQUIRE(budget >= 0 && budget <= H2O_MAX_SLOTS, "budget must be in [0, 8192]");
+    const cuinf_config& c = s->m->cfg;
+    CUINF_TRY(cudaStreamSynchronize(s->st));
+    for (auto& Z : s->h2o) {
+        cudaFree(Z.hk8); cudaFree(Z.hv8); cudaFree(Z.hks); cudaFree(Z.hvs);
+        cudaFree(Z.slot_pos); cudaFree(Z.attn_sum); cudaFree(Z.n_live);
+    }
+    s->h2o.clear();
+    if (s->kv_new) cudaFree(s->kv_new);
+    if (s->h2o_dst) cudaFree(s->h2o_dst);
+    s->kv_new = nullptr;
+    s->h2o_dst = nullptr;
+    s->h2o_C = 0;
+    if (budget > 0) {
+        if (window <= 0) window = budget / 2;
+        if (window >= budget) window = budget - 1;
+        REQUIRE(window >= 1, "budget must be at least 2");
+        const size_t row = (size_t)c.n_kv_heads * 64;
+        s->h2o.assign(c.n_layers, cuinf_session::H2o());
+        for (int l = 0; l < c.n_layers; l++) {
+            if (!c.attn_layer[l]) continue;
+            cuinf_session::H2o& Z = s->h2o[l];
+            CUINF_TRY(cudaMalloc(&Z.hk8, budget * row));
+            CUINF_TRY(cudaMalloc(&Z.hv8, budget * row));
+            CUINF_TRY(cudaMalloc(&Z.hks, (size_t)budget * c.n_kv_heads * 2));
+            CUINF_TRY(cudaMalloc(&Z.hvs, (size_t)budget * c.n_kv_heads * 2));
+            CUINF_TRY(cudaMalloc(&Z.slot_pos, (size_t)budget * 4));
+            CUINF_TRY(cudaMalloc(&Z.attn_sum, (size_t)budget * 4));
+            CUINF_TRY(cudaMalloc(&Z.n_live, 4));
+            CUINF_TRY(cudaMemset(Z.slot_pos, 0, (size_t)budget * 4));
+            CUINF_TRY(cudaMemset(Z.attn_sum, 0, (size_t)budget * 4));
+            CUINF_TRY(cudaMemset(Z.n_live, 0, 4));
+        }
+        CUINF_TRY(cudaMalloc(&s->kv_new, 2 * row * 2));
+        CUINF_TRY(cudaMalloc(&s->h2o_dst, (size_t)c.n_layers * 4));
+        CUINF_TRY(cudaMemset(s->h2o_dst, 0xff, (size_t)c.n_layers * 4));
+        s->h2o_C = budget;
+        s->h2o_W = window;
+    }
+    return build_graph(s);
+}
+
+// H2O state of one attention layer (host copies): slot positions and
+// cumulative attention [budget], live slots, the slot of the last step.
+extern "C" int cuinf_session_h2o_state(cuinf_session* s, int layer, int* slot_pos, float* attn_sum, int* n_live,
+                                       int* last_slot) {
+    REQUIRE(s && s->h2o_C, "no KV budget set");
+    REQUIRE(layer >= 0 && layer < s->m->cfg.n_layers && s->m->cfg.attn_layer[layer], "not an attention layer");
+    CUINF_TRY(cudaStreamSynchronize(s->st));
+    const cuinf_session::H2o& Z = s->h2o[layer];
+    if (slot_pos) CUINF_TRY(cudaMemcpy(slot_pos, Z.slot_pos, (size_t)s->h2o_C * 4, cudaMemcpyDeviceToHost));
+    if (attn_sum) CUINF_TRY(cudaMemcpy(attn_sum, Z.attn_sum, (size_t)s->h2o_C * 4, cudaMemcpyDeviceToHost));
+    if (n_live) CUINF_TRY(cudaMemcpy(n_live, Z.n_live, 4, cudaMemcpyDeviceToHost));
+    if (last_slot) CUINF_TRY(cudaMemcpy(last_slot, s->h2o_dst + layer, 4, cudaMemcpyDeviceToHost));
+    return CUINF_OK;
+}
+
 extern "C" int cuinf_session_keep_logits(cuinf_session* s, int on) {
     REQUIRE(s, "null session");
     if ((bool)on == s->keep_logits) return CUINF_OK;
@@ -1432,7 +1577,7 @@ extern "C" int cuinf_session_trace(cuinf_session* s, unsigned long long* buf, in
 }
 
 extern "C" int cuinf_session_uses_megakernel(const cuinf_session* s) {
-    return s && s->use_mk && s->mk_ok ? 1 : 0;
+    return s && !s->h2o_C && s->use_mk && s->mk_ok ? 1 : 0;
 }
 
 extern "C" int cuinf_session_error(cuinf_session* s, unsigned* flags) {

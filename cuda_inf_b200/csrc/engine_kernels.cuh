@@ -159,6 +159,7 @@ struct QkvParams {
     __half *ktail, *vtail;
     uint8_t *kc8, *vc8;
     __half *ksc, *vsc;
+    __half* kv_new;  // H2O mode: the token's K [nkv][64] then V [nkv][64] here, no tail/commit
     int H, nh, nkv;
     float eps, theta;
     L2Ranges next;
@@ -255,6 +256,10 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256) k_attn_qkv(QkvP
         return;
     }
     const int kvh = is_k ? hh - P.nh : hh - P.nh - P.nkv;
+    if (P.kv_new) {
+        if (d < 64) P.kv_new[((is_k ? 0 : P.nkv) + kvh) * CUINF_HD + d] = hv[d];
+        return;
+    }
     __half* tail = is_k ? P.ktail : P.vtail;
     if (d < 64) tail[((size_t)slot * P.nkv + kvh) * CUINF_HD + d] = hv[d];  // kv_write_tail
     if (slot == CUINF_KVGROUP - 1) {  // kv_commit_group for this head

@@ -104,6 +104,24 @@ class Session:
                                   r.ctypes.data if routes else None))
         return (out.value, r) if routes else out.value
 
+    def set_kv_budget(self, budget, window=0):
+        """H2O eviction mode: `budget` FP8 slots per attention layer, local
+        window (0: budget/2); before the first token."""
+        check(lib().cuinf_session_set_kv_budget(self._h, int(budget), int(window)))
+        self._kv_budget = int(budget)
+
+    def h2o_state(self, layer):
+        """(slot_pos int32 [budget], attn_sum float32 [budget], n_live, last slot)."""
+        import numpy as np
+        b = self._kv_budget
+        sp = np.zeros(b, np.int32)
+        a = np.zeros(b, np.float32)
+        n = ctypes.c_int(0)
+        last = ctypes.c_int(-1)
+        check(lib().cuinf_session_h2o_state(self._h, int(layer), sp.ctypes.data, a.ctypes.data,
+                                            ctypes.byref(n), ctypes.byref(last)))
+        return sp, a, n.value, last.value
+
     def generate(self, prompt, n_new, eos=-1):
         p = (ctypes.c_int * len(prompt))(*prompt)
         o = (ctypes.c_int * n_new)()

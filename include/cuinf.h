@@ -302,6 +302,20 @@ int cuinf_session_keep_logits(cuinf_session* s, int on);
  * as the reference does (default 1); 0 feeds it through decode steps. */
 #define CUINF_OPT_PREFILL 5
 int cuinf_session_set_option(cuinf_session* s, int option, int value);
+/* H2O eviction mode (the reference's --kv-budget / --kv-window,
+ * engine.cu:310-384, 579-581, 753-756, 803-828): each attention layer keeps
+ * `budget` per-token FP8 slots (own per-head fp16 scale, logical position,
+ * cumulative attention mass); once full, a fresh token takes the slot with
+ * the least mass outside the last `window` positions (first minimum), else
+ * the least overall.  window <= 0: budget/2.  budget 0 turns it off.  Only
+ * before the first token; budget <= 8192; prompts must fit the budget.  The
+ * slot choice runs on the device, inside the step graph.  The decode step
+ * then uses the multi-kernel graph (not the megakernel). */
+int cuinf_session_set_kv_budget(cuinf_session* s, int budget, int window);
+/* Host copies of one attention layer's H2O state: slot positions and
+ * cumulative attention [budget], live slots, slot of the last step. */
+int cuinf_session_h2o_state(cuinf_session* s, int layer, int* slot_pos, float* attn_sum, int* n_live,
+                            int* last_slot);
 /* Device error flags of the engine kernels (bit 0: a bounded wait on a
  * weight-staging barrier timed out and the kernel skipped its math). */
 int cuinf_device_error(unsigned* flags);

@@ -428,6 +428,17 @@ struct orc_state {
     int* committed;
     int* route_idx;
     float* route_w;
+    /* H2O eviction mode (engine.cu:310-384, 803-828): per attention layer a
+     * circular buffer of `budget` per-token FP8 slots */
+    int h2o_budget, h2o_window;
+    uint8_t **hk8, **hv8;
+    uint16_t **hks, **hvs;
+    int** slot_pos;
+    float** attn_sum;
+    int* n_live;
+    int* own_slot;     /* [nl] the slot this oracle chose in the last step */
+    int* used_slot;    /* [nl] the slot it used (own, or forced) */
+    int* forced_slot;  /* [nl] next step's forced slots, -1 = none */
 };
 
 static const orc_tensor* find_t(const orc_model* m, const char* name) {
@@ -564,6 +575,11 @@ orc_state* orc_state_new(const orc_model* m, int max_ctx) {
     s->committed = (int*)calloc((size_t)nl, sizeof(int));
     s->route_idx = (int*)calloc((size_t)nl * (c->top_k > 0 ? c->top_k : 1), sizeof(int));
     s->route_w = (float*)calloc((size_t)nl * (c->top_k > 0 ? c->top_k : 1), sizeof(float));
+    s->n_live = (int*)calloc((size_t)nl, sizeof(int));
+    s->own_slot = (int*)calloc((size_t)nl, sizeof(int));
+    s->used_slot = (int*)calloc((size_t)nl, sizeof(int));
+    s->forced_slot = (int*)malloc((size_t)nl * sizeof(int));
+    for (int l = 0; l < nl; l++) s->own_slot[l] = s->used_slot[l] = s->forced_slot[l] = -1;
     for (int l = 0; l < nl; l++) {
         if (c->attn_layer[l]) {
             s->kc8[l] = (uint8_t*)calloc((size_t)max_ctx * row, 1);
@@ -585,6 +601,14 @@ void orc_state_free(orc_state* s) {
         free(s->kc8[l]); free(s->vc8[l]); free(s->ksc[l]); free(s->vsc[l]);
         free(s->ktail[l]); free(s->vtail[l]); free(s->conv_state[l]);
     }
+    if (s->h2o_budget > 0) {
+        for (int l = 0; l < s->nl; l++) {
+            free(s->hk8[l]); free(s->hv8[l]); free(s->hks[l]); free(s->hvs[l]);
+            free(s->slot_pos[l]); free(s->attn_sum[l]);
+        }
+        free(s->hk8); free(s->hv8); free(s->hks); free(s->hvs); free(s->slot_pos); free(s->attn_sum);
+    }
+    free(s->n_live); free(s->own_slot); free(s->used_slot); free(s->forced_slot);
     free(s->h);
     free(s->committed);
     free(s->route_idx);
@@ -595,6 +619,138 @@ void orc_state_free(orc_state* s) {
 }
 
 int orc_state_pos(const orc_state* s) { return s->pos; }
+
+/* H2O mode: budget slots per attention layer, local window W (the reference's
+ * defaults: budget >= prompt, W = budget/2, W < budget; engine.cu:753-756). */
+int orc_state_set_h2o(const orc_model* m, orc_state* s, int budget, int window) {
+    const orc_config* c = &m->cfg;
+    if (budget <= 0 || window <= 0 || window >= budget || s->pos != 0 || s->h2o_budget) return -1;
+    const size_t row = (size_t)c->n_kv_heads * c->head_dim;
+    s->h2o_budget = budget;
+    s->h2o_window = window;
+    s->hk8 = (uint8_t**)calloc((size_t)s->nl, sizeof(void*));
+    s->hv8 = (uint8_t**)calloc((size_t)s->nl, sizeof(void*));
+    s->hks = (uint16_t**)calloc((size_t)s->nl, sizeof(void*));
+    s->hvs = (uint16_t**)calloc((size_t)s->nl, sizeof(void*));
+    s->slot_pos = (int**)calloc((size_t)s->nl, sizeof(void*));
+    s->attn_sum = (float**)calloc((size_t)s->nl, sizeof(void*));
+    for (int l = 0; l < s->nl; l++) {
+        if (!c->attn_layer[l]) continue;
+        s->hk8[l] = (uint8_t*)calloc((size_t)budget * row, 1);
+        s->hv8[l] = (uint8_t*)calloc((size_t)budget * row, 1);
+        s->hks[l] = (uint16_t*)calloc((size_t)budget * c->n_kv_heads, 2);
+        s->hvs[l] = (uint16_t*)calloc((size_t)budget * c->n_kv_heads, 2);
+        s->slot_pos[l] = (int*)calloc((size_t)budget, sizeof(int));
+        s->attn_sum[l] = (float*)calloc((size_t)budget, sizeof(float));
+    }
+    return 0;
+}
+const int* orc_state_h2o_own_slots(const orc_state* s) { return s->own_slot; }
+const int* orc_state_h2o_used_slots(const orc_state* s) { return s->used_slot; }
+const float* orc_state_h2o_attn_sum(const orc_state* s, int layer) {
+    return s->h2o_budget && s->attn_sum[layer] ? s->attn_sum[layer] : NULL;
+}
+const int* orc_state_h2o_slot_pos(const orc_state* s, int layer) {
+    return s->h2o_budget && s->slot_pos[layer] ? s->slot_pos[layer] : NULL;
+}
+int orc_state_h2o_n_live(const orc_state* s, int layer) { return s->n_live[layer]; }
+void orc_state_force_h2o_slots(orc_state* s, const int* slots) {
+    for (int l = 0; l < s->nl; l++) s->forced_slot[l] = slots ? slots[l] : -1;
+}
+
+/* The reference's slot choice for a fresh token at position pos (host loop,
+ * engine.cu:808-823): append while there is room; else the slot with the
+ * least cumulative attention among those outside the local window (first
+ * such minimum), else the least overall.  `banned` slots (picked earlier in
+ * the same batch) count as +inf. */
+static int h2o_choose(const orc_state* s, int l, int pos, const unsigned char* banned) {
+    const int C = s->h2o_budget, W = s->h2o_window;
+    if (s->n_live[l] < C) return s->n_live[l];
+    int best = -1;
+    float bv = 1e30f;
+    for (int t = 0; t < C; t++) {
+        float a = banned && banned[t] ? 1e30f : s->attn_sum[l][t];
+        if (s->slot_pos[l][t] <= pos - W && a < bv) { bv = a; best = t; }
+    }
+    if (best < 0)
+        for (int t = 0; t < C; t++) {
+            float a = banned && banned[t] ? 1e30f : s->attn_sum[l][t];
+            if (a < bv) { bv = a; best = t; }
+        }
+    return best;
+}
+
+/* kv_quant_write, engine.cu:317-333: one token's K/V per head into a slot,
+ * scale = absmax/448 + 1e-12 (fp32 for the quantization, stored fp16). */
+static void h2o_write(orc_state* s, int l, int slot, const uint16_t* k, const uint16_t* v, int nkv, int hd) {
+    for (int h = 0; h < nkv; h++) {
+        for (int which = 0; which < 2; which++) {
+            const uint16_t* src = (which ? v : k) + (size_t)h * hd;
+            float mx = 0.f;
+            for (int d = 0; d < hd; d++) {
+                float a = fabsf(orc_h2f(src[d]));
+                if (a > mx) mx = a;
+            }
+            float sc = mx / 448.0f + 1e-12f;
+            uint8_t* dst = (which ? s->hv8[l] : s->hk8[l]) + ((size_t)slot * nkv + h) * hd;
+            for (int d = 0; d < hd; d++) dst[d] = orc_f32_to_e4m3_sat(orc_h2f(src[d]) / sc);
+            (which ? s->hvs[l] : s->hks[l])[slot * nkv + h] = orc_f2h(sc);
+        }
+    }
+}
+
+/* attention_h2o, engine.cu:337-384: exact softmax over the live slots with
+ * slot position <= qpos; each slot's normalized probability is added to its
+ * cumulative attention (summed over query heads). */
+static void h2o_attend(orc_state* s, int l, const uint16_t* q, int qpos, float scale, uint16_t* out, int nh,
+                       int nkv, int hd) {
+    const int n = s->n_live[l], gqa = nh / nkv;
+    double* sc = (double*)malloc(sizeof(double) * (size_t)(n > 0 ? n : 1));
+    double* o = (double*)malloc(sizeof(double) * (size_t)hd);
+    for (int h = 0; h < nh; h++) {
+        const int kvh = h / gqa;
+        const uint16_t* qh = q + (size_t)h * hd;
+        double mx = -INFINITY;
+        for (int t = 0; t < n; t++) {
+            if (s->slot_pos[l][t] > qpos) continue;
+            const float ks = orc_h2f(s->hks[l][t * nkv + kvh]);
+            const uint8_t* kp = s->hk8[l] + ((size_t)t * nkv + kvh) * hd;
+            double acc = 0.0;
+            for (int d = 0; d < hd; d++) acc += (double)orc_h2f(qh[d]) * (double)(orc_e4m3_to_f32(kp[d]) * ks);
+            sc[t] = acc * scale;
+            if (sc[t] > mx) mx = sc[t];
+        }
+        double L = 0.0;
+        for (int d = 0; d < hd; d++) o[d] = 0.0;
+        for (int t = 0; t < n; t++) {
+            if (s->slot_pos[l][t] > qpos) continue;
+            const double p = exp(sc[t] - mx);
+            L += p;
+            const float vs = orc_h2f(s->hvs[l][t * nkv + kvh]);
+            const uint8_t* vp = s->hv8[l] + ((size_t)t * nkv + kvh) * hd;
+            for (int d = 0; d < hd; d++) o[d] += p * (double)(orc_e4m3_to_f32(vp[d]) * vs);
+        }
+        for (int d = 0; d < hd; d++) out[(size_t)h * hd + d] = orc_f2h((float)(o[d] / L));
+        for (int t = 0; t < n; t++)
+            if (s->slot_pos[l][t] <= qpos) s->attn_sum[l][t] += (float)(exp(sc[t] - mx) / L);
+    }
+    free(sc);
+    free(o);
+}
+
+/* One token's H2O placement and attention in layer l (decode, S = 1). */
+static void h2o_step(orc_state* s, int l, int pos, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                     float scale, uint16_t* out, int nh, int nkv, int hd) {
+    int own = h2o_choose(s, l, pos, NULL);
+    int slot = s->forced_slot[l] >= 0 ? s->forced_slot[l] : own;
+    s->own_slot[l] = own;
+    s->used_slot[l] = slot;
+    if (s->n_live[l] < s->h2o_budget && slot == s->n_live[l]) s->n_live[l]++;
+    s->attn_sum[l][slot] = 0.f;
+    s->slot_pos[l][slot] = pos;
+    h2o_write(s, l, slot, k, v, nkv, hd);
+    h2o_attend(s, l, q, pos, scale, out, nh, nkv, hd);
+}
 const int* orc_state_route_idx(const orc_state* s) { return s->route_idx; }
 const float* orc_state_route_w(const orc_state* s) { return s->route_w; }
 
@@ -645,6 +801,12 @@ int orc_forward_token_ex(const orc_model* m, orc_state* s, int token, const int*
             orc_rmsnorm(q16, L->q_ln, q16, nh, hd, eps);
             orc_rmsnorm(k16, L->k_ln, k16, nkv, hd, eps);
             orc_rope(q16, k16, &pos, 1, nh, nkv, hd, c->rope_theta);
+            if (s->h2o_budget > 0) {
+                h2o_step(s, l, pos, q16, k16, v16, 1.0f / sqrtf((float)hd), ao, nh, nkv, hd);
+                orc_gemv_int4(ao, L->wo.p, L->wo.s, fa, 1, H, nh * hd);
+                orc_add_f32_inplace(s->h, fa, H);
+                goto ffn;
+            }
             int slot = pos - s->committed[l];
             orc_kv_write_tail(k16, v16, s->ktail[l], s->vtail[l], slot, 1, nkv, hd);
             if (slot + 1 == 64) {
@@ -668,6 +830,7 @@ int orc_forward_token_ex(const orc_model* m, orc_state* s, int token, const int*
             orc_gemv_int4(acc, L->out_proj.p, L->out_proj.s, fa, 1, H, H);
             orc_add_f32_inplace(s->h, fa, H);
         }
+    ffn:
         orc_rmsnorm(s->h, L->ffn_norm, xn, 1, H, eps);
         if (l < c->n_dense) {
             int I = c->dense_inter;
@@ -780,6 +943,32 @@ int orc_prefill_ex(const orc_model* m, orc_state* s, const int* tokens, int S, c
             orc_rmsnorm(q16, L->q_ln, q16, S * nh, hd, eps);
             orc_rmsnorm(k16, L->k_ln, k16, S * nkv, hd, eps);
             orc_rope(q16, k16, pos, S, nh, nkv, hd, c->rope_theta);
+            if (s->h2o_budget > 0) {
+                /* H2O (engine.cu:804-828): choose every fresh token's slot
+                 * (earlier picks of this batch excluded), write them all,
+                 * then every query attends over the live slots */
+                unsigned char* banned = (unsigned char*)calloc((size_t)s->h2o_budget, 1);
+                int* dst = (int*)malloc((size_t)S * sizeof(int));
+                for (int j = 0; j < S; j++) {
+                    int slot = h2o_choose(s, l, past + j, banned);
+                    if (s->n_live[l] < s->h2o_budget && slot == s->n_live[l]) s->n_live[l]++;
+                    banned[slot] = 1;
+                    s->attn_sum[l][slot] = 0.f;
+                    s->slot_pos[l][slot] = past + j;
+                    dst[j] = slot;
+                    s->own_slot[l] = s->used_slot[l] = slot;
+                }
+                for (int j = 0; j < S; j++)
+                    h2o_write(s, l, dst[j], k16 + (size_t)j * nkv * hd, v16 + (size_t)j * nkv * hd, nkv, hd);
+                for (int i = 0; i < S; i++)
+                    h2o_attend(s, l, q16 + (size_t)i * nh * hd, past + i, 1.0f / sqrtf((float)hd),
+                               ao + (size_t)i * nh * hd, nh, nkv, hd);
+                free(banned);
+                free(dst);
+                orc_gemv_int4(ao, L->wo.p, L->wo.s, fa, S, H, nh * hd);
+                orc_add_f32_inplace(hs, fa, S * H);
+                goto ffn_pf;
+            }
             int placed = 0;
             while (placed < S) {  /* engine.cu:831-845 */
                 int slot = past + placed - s->committed[l];
@@ -808,6 +997,7 @@ int orc_prefill_ex(const orc_model* m, orc_state* s, const int* tokens, int S, c
             orc_gemv_int4(acc, L->out_proj.p, L->out_proj.s, fa, S, H, H);
             orc_add_f32_inplace(hs, fa, S * H);
         }
+    ffn_pf:
         orc_rmsnorm(hs, L->ffn_norm, xn, S, H, eps);
         if (l < c->n_dense) {
             int I = c->dense_inter;

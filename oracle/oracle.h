@@ -114,6 +114,18 @@ int        orc_prefill(const orc_model* m, orc_state* s, const int* tokens, int 
  * selection scores written to scores [S][n_moe][E]. */
 int        orc_prefill_ex(const orc_model* m, orc_state* s, const int* tokens, int S,
                           const int* forced_idx, float* scores, float* logits_out);
+/* H2O eviction mode (engine.cu:310-384, 803-828), set before the first
+ * token: `budget` per-token FP8 slots per attention layer, local window W.
+ * own/used slots: per layer, the slot this oracle chose / used in the last
+ * step (-1 for other layers); force: the next decode step uses these slots
+ * per layer (-1 or NULL: its own choice). */
+int          orc_state_set_h2o(const orc_model* m, orc_state* s, int budget, int window);
+const int*   orc_state_h2o_own_slots(const orc_state* s);
+const int*   orc_state_h2o_used_slots(const orc_state* s);
+const float* orc_state_h2o_attn_sum(const orc_state* s, int layer);
+const int*   orc_state_h2o_slot_pos(const orc_state* s, int layer);
+int          orc_state_h2o_n_live(const orc_state* s, int layer);
+void         orc_state_force_h2o_slots(orc_state* s, const int* slots);
 /* Router decisions of the last forward_token: [n_moe_layers][top_k]. */
 const int*   orc_state_route_idx(const orc_state* s);
 const float* orc_state_route_w(const orc_state* s);

@@ -62,6 +62,13 @@ _SIGS = {
     "orc_prefill": (I, [P, P, P, I, P]),
     "orc_prefill_ex": (I, [P, P, P, I, P, P, P]),
     "orc_state_route_idx": (P, [P]),
+    "orc_state_set_h2o": (I, [P, P, I, I]),
+    "orc_state_h2o_own_slots": (P, [P]),
+    "orc_state_h2o_used_slots": (P, [P]),
+    "orc_state_h2o_attn_sum": (P, [P, I]),
+    "orc_state_h2o_slot_pos": (P, [P, I]),
+    "orc_state_h2o_n_live": (I, [P, I]),
+    "orc_state_force_h2o_slots": (None, [P, P]),
     "orc_state_route_w": (P, [P]),
     "orc_set_threads": (None, [I]),
     "orc_get_threads": (I, []),
@@ -305,6 +312,40 @@ class State:
         nxt = lib().orc_forward_token_ex(self.model._h, self._h, int(token), _ptr(fi), _ptr(sc),
                                          _ptr(lg), _ptr(hid))
         return nxt, lg, hid, sc
+
+    def set_h2o(self, budget, window):
+        """H2O eviction mode: `budget` per-token FP8 slots per attention layer,
+        local window `window` (engine.cu:310-384, 803-828)."""
+        if lib().orc_state_set_h2o(self.model._h, self._h, int(budget), int(window)) != 0:
+            raise ValueError("bad H2O budget/window (or the state already advanced)")
+        self._h2o_budget = int(budget)
+
+    def h2o_slots(self):
+        """(own, used): per layer, the slot chosen by this oracle and the slot
+        used (forced or own) in the last step; -1 for non-attention layers."""
+        nl = self.model.cfg.n_layers
+        own = np.ctypeslib.as_array(ctypes.cast(lib().orc_state_h2o_own_slots(self._h),
+                                                ctypes.POINTER(ctypes.c_int)), (nl,)).copy()
+        used = np.ctypeslib.as_array(ctypes.cast(lib().orc_state_h2o_used_slots(self._h),
+                                                 ctypes.POINTER(ctypes.c_int)), (nl,)).copy()
+        return own, used
+
+    def h2o_layer(self, layer):
+        """(attn_sum float32 [budget], slot_pos int32 [budget], n_live) of layer."""
+        b = self._h2o_budget
+        a = np.ctypeslib.as_array(ctypes.cast(lib().orc_state_h2o_attn_sum(self._h, layer),
+                                              ctypes.POINTER(ctypes.c_float)), (b,)).copy()
+        sp = np.ctypeslib.as_array(ctypes.cast(lib().orc_state_h2o_slot_pos(self._h, layer),
+                                               ctypes.POINTER(ctypes.c_int)), (b,)).copy()
+        return a, sp, lib().orc_state_h2o_n_live(self._h, layer)
+
+    def force_h2o_slots(self, slots):
+        """The next decode step uses these slots per layer (None: own choice)."""
+        if slots is None:
+            lib().orc_state_force_h2o_slots(self._h, None)
+        else:
+            self._forced = np.ascontiguousarray(slots, np.int32)
+            lib().orc_state_force_h2o_slots(self._h, self._forced.ctypes.data)
 
     def routes(self):
         c = self.model.cfg

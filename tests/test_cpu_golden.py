@@ -224,3 +224,52 @@ def test_oracle_prefill_semantics(tmp_path):
         n2, lg2, _, _ = b.forward_ex(int(t))
     assert not np.array_equal(lg1, lg2)
     assert np.abs(lg1 - lg2).max() < 0.1 * np.abs(lg2).max()
+
+
+def test_oracle_h2o_policy(tmp_path):
+    """The oracle's H2O slot choice (engine.cu:808-823): append while there is
+    room, then the least cumulative attention outside the local window (first
+    minimum), else the least overall; the chosen slot's mass restarts at 0 and
+    its position becomes the token's.  Without eviction a prefill equals
+    decoding the same ids."""
+    import zlib
+    cfg = weights.make_config(hidden=128, n_layers=3, n_heads=2, n_kv_heads=1, vocab=300, n_dense=1,
+                              n_experts=8, top_k=2, moe_inter=128, dense_inter=128, attn_layers=(1, 2))
+
+    def tensor(name, shape):
+        rng = np.random.default_rng(zlib.crc32(name.encode()))
+        k = weights.init_kind(name)
+        if k == "norm":
+            return (1 + 0.02 * rng.standard_normal(shape)).astype(np.float32)
+        if k == "conv":
+            return rng.uniform(-0.577, 0.577, shape).astype(np.float32)
+        return (0.05 * rng.standard_normal(shape)).astype(np.float32)
+
+    weights.write_model(str(tmp_path), cfg, tensor)
+    om = pyoracle.Model(weights.config_dict(cfg), np.fromfile(tmp_path / "weights.bin", np.uint8),
+                        open(tmp_path / "index.bin", "rb").read())
+    C, W = 8, 3
+    st = om.state(64)
+    st.set_h2o(C, W)
+    toks = np.random.default_rng(9).integers(0, cfg.vocab, 30)
+    for pos, t in enumerate(toks):
+        a, sp, n = st.h2o_layer(1)
+        if n < C:
+            want = n
+        else:
+            elig = [i for i in range(C) if sp[i] <= pos - W]
+            pool = elig if elig else list(range(C))
+            want = min(pool, key=lambda i: (a[i], i))
+        st.forward_ex(int(t))
+        own, used = st.h2o_slots()
+        assert own[1] == used[1] == want, (pos, own[1], want)
+        a2, sp2, n2 = st.h2o_layer(1)
+        assert sp2[want] == pos and n2 == min(pos + 1, C)
+    # prefill == decode while nothing is evicted
+    s1, s2 = om.state(64), om.state(64)
+    s1.set_h2o(16, 8)
+    s2.set_h2o(16, 8)
+    n1, lg1, _ = s1.prefill(toks[:12])
+    for t in toks[:12]:
+        n2, lg2, _, _ = s2.forward_ex(int(t))
+    assert n1 == n2 and np.array_equal(lg1, lg2)
