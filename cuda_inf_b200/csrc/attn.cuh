@@ -605,3 +605,139 @@ __global__ void __launch_bounds__(256) k_h2o_attn(H2oParams P) {
         P.out[((size_t)i * P.nh + h) * CUINF_HD + tid] = __float2half_rn(s * inv);
     }
 }
+
+// Prefill attention for long prompts (attention_fused, engine.cu:236-308),
+// the same keys and arithmetic as k_attn_prefill: grid (S, nh), 256 threads;
+// thread j takes keys j, j+256, ... of the query's range with its own online
+// softmax (q and its 64 outputs in registers, one full 64-dim dot per key),
+// and the block merges the 256 partial states at the end.
+__global__ void __launch_bounds__(256) k_attn_prefill_wide(const __half* __restrict__ q,
+                                                            const uint8_t* __restrict__ kc8,
+                                                            const uint8_t* __restrict__ vc8,
+                                                            const __half* __restrict__ ksc,
+                                                            const __half* __restrict__ vsc,
+                                                            const __half* __restrict__ ktail,
+                                                            const __half* __restrict__ vtail, int committed,
+                                                            int past, float scale, __half* __restrict__ out, int nh,
+                                                            int nkv) {
+    __shared__ float wm[8], wl[8];
+    __shared__ float wo[8][CUINF_HD];
+    const int i = blockIdx.x, hq = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int kvh = hq / (nh / nkv), qpos = past + i;
+    const int cend = committed < qpos + 1 ? committed : qpos + 1;
+    float qr[CUINF_HD];
+    {
+        const uint4* qp = reinterpret_cast<const uint4*>(q + ((size_t)i * nh + hq) * CUINF_HD);
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const uint4 u = qp[c];
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const __half2 h2 = *reinterpret_cast<const __half2*>(&w[j]);
+                qr[c * 8 + 2 * j] = __low2float(h2) * scale;
+                qr[c * 8 + 2 * j + 1] = __high2float(h2) * scale;
+            }
+        }
+    }
+    float m = -1e30f, l = 0.f, o[CUINF_HD];
+#pragma unroll
+    for (int d = 0; d < CUINF_HD; d++) o[d] = 0.f;
+    for (int t = tid; t <= qpos; t += blockDim.x) {
+        // score first (K converted on the fly), then V folded into the outputs
+        float s = 0.f, cf, p;
+        if (t < cend) {
+            const float ks = __half2float(ksc[(t / CUINF_KVGROUP) * nkv + kvh]);
+            const uint4* kp = reinterpret_cast<const uint4*>(kc8 + ((size_t)t * nkv + kvh) * CUINF_HD);
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const uint4 ku = kp[c];
+                const uint32_t kw[4] = {ku.x, ku.y, ku.z, ku.w};
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const uint32_t kb = fp8x2_to_h2(kw[j >> 1] >> (16 * (j & 1)));
+                    const __half2 k2 = *reinterpret_cast<const __half2*>(&kb);
+                    const int d = c * 16 + j * 2;
+                    s = fmaf(qr[d], __low2float(k2) * ks, s);
+                    s = fmaf(qr[d + 1], __high2float(k2) * ks, s);
+                }
+            }
+        } else {
+            const uint4* kp = reinterpret_cast<const uint4*>(ktail + ((size_t)(t - committed) * nkv + kvh) * CUINF_HD);
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const uint4 ku = kp[c];
+                const uint32_t kw[4] = {ku.x, ku.y, ku.z, ku.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const __half2 k2 = *reinterpret_cast<const __half2*>(&kw[j]);
+                    s = fmaf(qr[c * 8 + 2 * j], __low2float(k2), s);
+                    s = fmaf(qr[c * 8 + 2 * j + 1], __high2float(k2), s);
+                }
+            }
+        }
+        const float mn = fmaxf(m, s);
+        cf = __expf(m - mn);
+        p = __expf(s - mn);
+        l = l * cf + p;
+        m = mn;
+        if (t < cend) {
+            const float pv = p * __half2float(vsc[(t / CUINF_KVGROUP) * nkv + kvh]);
+            const uint4* vp = reinterpret_cast<const uint4*>(vc8 + ((size_t)t * nkv + kvh) * CUINF_HD);
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const uint4 vu = vp[c];
+                const uint32_t vw[4] = {vu.x, vu.y, vu.z, vu.w};
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const uint32_t vb = fp8x2_to_h2(vw[j >> 1] >> (16 * (j & 1)));
+                    const __half2 v2 = *reinterpret_cast<const __half2*>(&vb);
+                    const int d = c * 16 + j * 2;
+                    o[d] = fmaf(pv, __low2float(v2), o[d] * cf);
+                    o[d + 1] = fmaf(pv, __high2float(v2), o[d + 1] * cf);
+                }
+            }
+        } else {
+            const uint4* vp = reinterpret_cast<const uint4*>(vtail + ((size_t)(t - committed) * nkv + kvh) * CUINF_HD);
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const uint4 vu = vp[c];
+                const uint32_t vw[4] = {vu.x, vu.y, vu.z, vu.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const __half2 v2 = *reinterpret_cast<const __half2*>(&vw[j]);
+                    o[c * 8 + 2 * j] = fmaf(p, __low2float(v2), o[c * 8 + 2 * j] * cf);
+                    o[c * 8 + 2 * j + 1] = fmaf(p, __high2float(v2), o[c * 8 + 2 * j + 1] * cf);
+                }
+            }
+        }
+    }
+    // merge: lanes of a warp, then the 8 warps
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, m, off), ol = __shfl_xor_sync(0xffffffffu, l, off);
+        const float mn = fmaxf(m, om), a = __expf(m - mn), b = __expf(om - mn);
+#pragma unroll
+        for (int d = 0; d < CUINF_HD; d++) o[d] = o[d] * a + __shfl_xor_sync(0xffffffffu, o[d], off) * b;
+        l = l * a + ol * b;
+        m = mn;
+    }
+    if (lane == 0) {
+        wm[warp] = m;
+        wl[warp] = l;
+#pragma unroll
+        for (int d = 0; d < CUINF_HD; d++) wo[warp][d] = o[d];
+    }
+    __syncthreads();
+    if (tid < CUINF_HD) {
+        float M = -1e30f;
+        for (int w = 0; w < 8; w++) M = fmaxf(M, wm[w]);
+        float L = 0.f, O = 0.f;
+        for (int w = 0; w < 8; w++) {
+            const float e = __expf(wm[w] - M);
+            L += wl[w] * e;
+            O += wo[w][tid] * e;
+        }
+        out[((size_t)i * nh + hq) * CUINF_HD + tid] = __float2half_rn(O / L);
+    }
+}

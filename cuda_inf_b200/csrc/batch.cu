@@ -1294,3 +1294,158 @@ extern "C" int cuinf_batch_profile_step(cuinf_batch* b, int max_kernels, float* 
     *n_kernels = n;
     return CUINF_OK;
 }
+
+// ===========================================================================
+// Grouped MoE for prefill: the S tokens of one prompt go through the same
+// routing / grouping / grouped-GEMM / combine kernels as a decode batch, in
+// chunks of up to 1024/top_k tokens (one routing CTA handles 1024 entries).
+// ===========================================================================
+struct TcCache {
+    std::mutex mu;
+    std::vector<CUtensorMap> hmaps;
+    CUtensorMap* dmaps = nullptr;  // [n_moe][E][3]
+    int chunk = 0;
+    float *rlog = nullptr, *rw = nullptr, *fg = nullptr, *fu = nullptr, *fo = nullptr;
+    int *inv = nullptr, *src = nullptr, *ridx = nullptr;
+    __half *xg = nullptr, *mmid = nullptr;
+    TcGroup *g13 = nullptr, *g2 = nullptr;
+    CUtensorMap x_xg, x_mmid;
+    std::vector<void*> allocs;
+};
+
+void tc_cache_free(cuinf_model* m) {
+    TcCache* c = (TcCache*)m->tc_cache;
+    if (!c) return;
+    for (void* p : c->allocs) cudaFree(p);
+    delete c;
+    m->tc_cache = nullptr;
+}
+
+static int tc_cache_get(cuinf_model* m, TcCache** out) {
+    if (m->tc_cache) {
+        *out = (TcCache*)m->tc_cache;
+        return CUINF_OK;
+    }
+    const cuinf_config& c = m->cfg;
+    REQUIRE(c.hidden % TC_KS == 0 && c.moe_inter % TC_KS == 0, "grouped MoE needs H and I multiples of 128");
+    const int E = c.n_experts, K = c.top_k, H = c.hidden, I = c.moe_inter;
+    const int n_moe = c.n_layers - c.n_dense;
+    TcCache* tc = new TcCache();
+    auto fail = [&](int rc) {
+        for (void* p : tc->allocs) cudaFree(p);
+        delete tc;
+        return rc;
+    };
+    auto al = [&](void** p, size_t bytes) -> int {
+        if (cudaMalloc(p, bytes) != cudaSuccess) return cuinf_set_arg_error("prefill scratch allocation failed");
+        tc->allocs.push_back(*p);
+        return CUINF_OK;
+    };
+    std::vector<void*> ex((size_t)n_moe * E * 6);
+    if (cudaMemcpy(ex.data(), m->d_experts, ex.size() * sizeof(void*), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return fail(cuinf_set_arg_error("expert table copy failed"));
+    for (size_t e = 0; e < (size_t)n_moe * E; e++) {
+        CUtensorMap a, b, d;
+        int rc = tc_map_int4(&a, (const uint8_t*)ex[e * 6 + 0], I, H);
+        if (!rc) rc = tc_map_int4(&b, (const uint8_t*)ex[e * 6 + 2], I, H);
+        if (!rc) rc = tc_map_int4(&d, (const uint8_t*)ex[e * 6 + 4], H, I);
+        if (rc) return fail(rc);
+        tc->hmaps.push_back(a);
+        tc->hmaps.push_back(b);
+        tc->hmaps.push_back(d);
+    }
+    int rc = al((void**)&tc->dmaps, tc->hmaps.size() * sizeof(CUtensorMap));
+    if (rc) return fail(rc);
+    if (cudaMemcpy(tc->dmaps, tc->hmaps.data(), tc->hmaps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice) !=
+        cudaSuccess)
+        return fail(cuinf_set_arg_error("tensor map upload failed"));
+    const int C = 1024 / K, R = C * K, maxch = (C + TC_NMAX - 1) / TC_NMAX;
+    tc->chunk = C;
+    if ((rc = al((void**)&tc->rlog, (size_t)C * E * 4)) || (rc = al((void**)&tc->rw, (size_t)R * 4)) ||
+        (rc = al((void**)&tc->fg, (size_t)R * I * 4)) || (rc = al((void**)&tc->fu, (size_t)R * I * 4)) ||
+        (rc = al((void**)&tc->fo, (size_t)R * H * 4)) || (rc = al((void**)&tc->inv, (size_t)R * 4)) ||
+        (rc = al((void**)&tc->src, (size_t)R * 4)) || (rc = al((void**)&tc->ridx, (size_t)R * 4)) ||
+        (rc = al((void**)&tc->xg, (size_t)R * H * 2)) || (rc = al((void**)&tc->mmid, (size_t)R * I * 2)) ||
+        (rc = al((void**)&tc->g13, (size_t)2 * E * maxch * sizeof(TcGroup))) ||
+        (rc = al((void**)&tc->g2, (size_t)E * maxch * sizeof(TcGroup))))
+        return fail(rc);
+    if ((rc = tc_map_act(&tc->x_xg, tc->xg, R, H, 16)) || (rc = tc_map_act(&tc->x_mmid, tc->mmid, R, I, 16)))
+        return fail(rc);
+    m->tc_cache = tc;
+    *out = tc;
+    return CUINF_OK;
+}
+
+int moe_grouped_prefill(cuinf_model* m, int layer, const __half* xn, __half* h, int S, int* ridx_out,
+                        cudaStream_t st) {
+    TcCache* tc = nullptr;
+    int rc = tc_cache_get(m, &tc);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(tc->mu);
+    rc = tc_attr_once();
+    if (rc) return rc;
+    const cuinf_config& c = m->cfg;
+    const LayerW& L = m->L[layer];
+    const int E = c.n_experts, K = c.top_k, H = c.hidden, I = c.moe_inter;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    for (int c0 = 0; c0 < S; c0 += tc->chunk) {
+        const int n = std::min(tc->chunk, S - c0), maxch = (n + TC_NMAX - 1) / TC_NMAX;
+        rc = cuinf_gemv_fp16(xn + (size_t)c0 * H, L.gate, tc->rlog, n, E, H, st);
+        if (rc) return rc;
+        BRouteParams R;
+        R.logits = tc->rlog;
+        R.bias = L.ebias;
+        R.B = n;
+        R.E = E;
+        R.topk = K;
+        R.I = I;
+        R.H = H;
+        R.maxch = maxch;
+        R.ridx = ridx_out ? ridx_out + (size_t)c0 * K : tc->ridx;
+        R.rw = tc->rw;
+        R.keys = nullptr;
+        R.n = n * K;
+        R.n_local = E;
+        R.group = 1;
+        R.inv = tc->inv;
+        R.src = tc->src;
+        R.g13 = tc->g13;
+        R.g2 = tc->g2;
+        R.maps = tc->dmaps + (size_t)L.moe_index * E * 3;
+        R.experts = (void* const*)(m->d_experts + (size_t)L.moe_index * E * 6);
+        R.gbuf = tc->fg;
+        R.ubuf = tc->fu;
+        R.obuf = tc->fo;
+        k_broute<<<1, 1024, 0, st>>>(R);
+        k_bgather<<<n * K, 256, 0, st>>>(xn + (size_t)c0 * H, tc->src, tc->xg, H);
+        if ((rc = cuinf_launch_status())) return rc;
+        const int t13 = (I + TC_ROWS - 1) / TC_ROWS, t2 = (H + TC_ROWS - 1) / TC_ROWS;
+        const int hit = std::min(E, n * K);
+        for (int pass = 0; pass < 2; pass++) {
+            const int ng = pass ? E * maxch : 2 * E * maxch, tiles = pass ? t2 : t13, Kd = pass ? I : H;
+            TcPlan pl = tc_plan((pass ? 1 : 2) * hit * tiles, Kd, sms);
+            float* ws = nullptr;
+            unsigned* cnt = nullptr;
+            if (pl.splits > 1 && (rc = tc_workspace((size_t)ng * tiles * pl.splits, (size_t)ng * tiles, &ws, &cnt)))
+                return rc;
+            TcParams P = {};
+            P.groups = pass ? tc->g2 : tc->g13;
+            P.n_groups = ng;
+            P.K = Kd;
+            P.splits = pl.splits;
+            P.kg_per_split = pl.kgps;
+            P.fp16_w = 0;
+            P.xmax = (std::min(n, TC_NMAX) + 15) & ~15;  // a group holds at most one row per token
+            P.xbox = 16;
+            P.ws = ws;
+            P.counters = cnt;
+            if ((rc = tc_launch(pass ? tc->x_mmid : tc->x_xg, tc->hmaps[0], P, tiles, st, false))) return rc;
+            if (!pass && (rc = cuinf_swiglu(tc->fg, tc->fu, tc->mmid, n * K * I, st))) return rc;
+        }
+        k_bcombine<<<(n * H + 255) / 256, 256, 0, st>>>(tc->fo, tc->inv, tc->rw, h + (size_t)c0 * H, n, H, K);
+        if ((rc = cuinf_launch_status())) return rc;
+    }
+    return CUINF_OK;
+}

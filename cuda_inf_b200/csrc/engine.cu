@@ -597,6 +597,7 @@ extern "C" int cuinf_model_load(const char* dir, const cuinf_config* cfg, cuinf_
 
 extern "C" int cuinf_model_free(cuinf_model* m) {
     if (!m) return CUINF_OK;
+    tc_cache_free(m);
     if (m->d_experts) cudaFree(m->d_experts);
     if (m->own_blob && m->d_blob) cudaFree(m->d_blob);
     delete m;
@@ -1296,6 +1297,16 @@ extern "C" int cuinf_decode_step(cuinf_session* s, int token, int* out_token) {
 // token.  Kernel by kernel on the session stream (not captured); afterwards
 // the session continues with decode steps from position pos + S.
 // ---------------------------------------------------------------------------
+// From this many prompt rows on, prefill runs its projections on the
+// tensor-core GEMM and its MoE as grouped expert GEMMs; shorter prompts use
+// the batch-1 GEMV kernels.
+#define PF_TC_MIN_ROWS 16
+static int pf_gemm(const void* x, const uint8_t* packed, const void* scales, float* y, int M, int N, int K,
+                   void* stream) {
+    if (M >= PF_TC_MIN_ROWS) return cuinf_gemm_int4_tc(x, packed, scales, y, M, N, K, stream);
+    return cuinf_gemv_int4(x, packed, scales, y, M, N, K, stream);
+}
+
 extern "C" int cuinf_prefill(cuinf_session* s, const int* ids, int S, int* out_token, int* routes_out) {
     REQUIRE(s && ids && S > 0, "bad arguments");
     const cuinf_model* m = s->m;
@@ -1356,11 +1367,11 @@ extern "C" int cuinf_prefill(cuinf_session* s, const int* ids, int S, int* out_t
         PF(cuinf_rmsnorm(hs, L.op_norm, xn, S, H, c.norm_eps, vs));
         if (c.attn_layer[l]) {
             AttnState& A = s->attn[l];
-            PF(cuinf_gemv_int4(xn, L.wq.p, L.wq.s, fa, S, NQ, H, vs));
+            PF(pf_gemm(xn, L.wq.p, L.wq.s, fa, S, NQ, H, vs));
             PF(cuinf_f32_to_f16(fa, q16, S * NQ, vs));
-            PF(cuinf_gemv_int4(xn, L.wk.p, L.wk.s, fa, S, NK, H, vs));
+            PF(pf_gemm(xn, L.wk.p, L.wk.s, fa, S, NK, H, vs));
             PF(cuinf_f32_to_f16(fa, k16, S * NK, vs));
-            PF(cuinf_gemv_int4(xn, L.wv.p, L.wv.s, fa, S, NK, H, vs));
+            PF(pf_gemm(xn, L.wv.p, L.wv.s, fa, S, NK, H, vs));
             PF(cuinf_f32_to_f16(fa, v16, S * NK, vs));
             PF(cuinf_rmsnorm(q16, L.q_ln, q16, S * nh, hd, c.norm_eps, vs));
             PF(cuinf_rmsnorm(k16, L.k_ln, k16, S * nkv, hd, c.norm_eps, vs));
@@ -1372,7 +1383,7 @@ extern "C" int cuinf_prefill(cuinf_session* s, const int* ids, int S, int* out_t
                 PF(cuinf_launch_status());
                 k_h2o_attn<<<dim3(S, nh), 256, (size_t)s->h2o_C * 4, st>>>(Z);
                 PF(cuinf_launch_status());
-                PF(cuinf_gemv_int4(ao, L.wo.p, L.wo.s, fa, S, H, NQ, vs));
+                PF(pf_gemm(ao, L.wo.p, L.wo.s, fa, S, H, NQ, vs));
                 PF(cuinf_add_f32_inplace(hs, fa, S * H, vs));
                 goto ffn;
             }
@@ -1390,29 +1401,41 @@ extern "C" int cuinf_prefill(cuinf_session* s, const int* ids, int S, int* out_t
                     committed += CUINF_KVGROUP;
                 }
             }
-            k_attn_prefill<<<dim3(S, nh), 32, 0, st>>>(q16, A.kc8, A.vc8, A.ksc, A.vsc, A.ktail, A.vtail,
-                                                       committed, past, 1.0f / sqrtf((float)hd), ao, nh, nkv);
+            if (S >= PF_TC_MIN_ROWS)
+                k_attn_prefill_wide<<<dim3(S, nh), 256, 0, st>>>(q16, A.kc8, A.vc8, A.ksc, A.vsc, A.ktail, A.vtail,
+                                                                 committed, past, 1.0f / sqrtf((float)hd), ao, nh,
+                                                                 nkv);
+            else
+                k_attn_prefill<<<dim3(S, nh), 32, 0, st>>>(q16, A.kc8, A.vc8, A.ksc, A.vsc, A.ktail, A.vtail,
+                                                           committed, past, 1.0f / sqrtf((float)hd), ao, nh, nkv);
             PF(cuinf_launch_status());
-            PF(cuinf_gemv_int4(ao, L.wo.p, L.wo.s, fa, S, H, NQ, vs));
+            PF(pf_gemm(ao, L.wo.p, L.wo.s, fa, S, H, NQ, vs));
             PF(cuinf_add_f32_inplace(hs, fa, S * H, vs));
             }
         } else {
-            PF(cuinf_gemv_int4(xn, L.in_proj.p, L.in_proj.s, fa, S, 3 * H, H, vs));
+            PF(pf_gemm(xn, L.in_proj.p, L.in_proj.s, fa, S, 3 * H, H, vs));
             PF(cuinf_conv_pre(fa, t16, t16b, S, H, vs));
             PF(cuinf_conv_apply(t16b, t16, L.conv_w, s->conv_state[l], acc, S, H, vs));
             PF(cuinf_conv_update_state(t16b, s->conv_state[l], S, H, vs));
-            PF(cuinf_gemv_int4(acc, L.out_proj.p, L.out_proj.s, fa, S, H, H, vs));
+            PF(pf_gemm(acc, L.out_proj.p, L.out_proj.s, fa, S, H, H, vs));
             PF(cuinf_add_f32_inplace(hs, fa, S * H, vs));
         }
     ffn:
         PF(cuinf_rmsnorm(hs, L.ffn_norm, xn, S, H, c.norm_eps, vs));
         if (l < c.n_dense) {
             const int I = c.dense_inter;
-            PF(cuinf_gemv_int4(xn, L.w1.p, L.w1.s, fa, S, I, H, vs));
-            PF(cuinf_gemv_int4(xn, L.w3.p, L.w3.s, fb, S, I, H, vs));
+            PF(pf_gemm(xn, L.w1.p, L.w1.s, fa, S, I, H, vs));
+            PF(pf_gemm(xn, L.w3.p, L.w3.s, fb, S, I, H, vs));
             PF(cuinf_swiglu(fa, fb, t16, S * I, vs));
-            PF(cuinf_gemv_int4(t16, L.w2.p, L.w2.s, fa, S, H, I, vs));
+            PF(pf_gemm(t16, L.w2.p, L.w2.s, fa, S, H, I, vs));
             PF(cuinf_add_f32_inplace(hs, fa, S * H, vs));
+        } else if (S >= PF_TC_MIN_ROWS) {
+            // the prompt's tokens grouped by expert (each expert's weights streamed once per chunk);
+            // experts of this layer into rw (free here), then into the [S][n_moe][K] layout
+            int* rl = reinterpret_cast<int*>(rw);
+            PF(moe_grouped_prefill(const_cast<cuinf_model*>(m), l, xn, hs, S, rl, st));
+            CUINF_TRY(cudaMemcpy2DAsync(ridx + (size_t)L.moe_index * K, (size_t)n_moe * K * 4, rl, (size_t)K * 4,
+                                        (size_t)K * 4, S, cudaMemcpyDeviceToDevice, st));
         } else {
             const void* const* ex = (const void* const*)(m->d_experts + (size_t)L.moe_index * E * 6);
             for (int i = 0; i < S; i++) {  // one token at a time, h_i += its expert mix (882-904)

@@ -38,7 +38,16 @@ struct cuinf_model {
     const __half *embed = nullptr, *emb_norm = nullptr;
     void** d_experts = nullptr;  // [n_moe][E][6]
     int n_moe = 0;
+    void* tc_cache = nullptr;    // tensor-core prefill state (expert tensor maps, scratch), built on first use
 };
+
+// Grouped MoE FFN of S tokens of one sequence (prefill): h[S][H] += the
+// reference's per-token expert mix, with the experts' weights streamed once
+// per chunk of tokens by the tensor-core GEMM.  ridx (device, nullable)
+// receives the experts [S][top_k].  Calls on one model must not overlap.
+int moe_grouped_prefill(cuinf_model* m, int layer, const __half* xn, __half* h, int S, int* ridx,
+                        cudaStream_t st);
+void tc_cache_free(cuinf_model* m);
 
 struct AttnState {
     uint8_t *kc8 = nullptr, *vc8 = nullptr;
