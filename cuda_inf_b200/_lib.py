@@ -85,6 +85,12 @@ _SIGS = {
     "cuinf_session_keep_logits": (c_int, [c_void_p, c_int]),
     "cuinf_session_set_option": (c_int, [c_void_p, c_int, c_int]),
     "cuinf_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
+    "cuinf_tokenizer_load": (c_int, [ctypes.c_char_p, c_void_p]),
+    "cuinf_tokenizer_free": (c_int, [c_void_p]),
+    "cuinf_tokenizer_vocab_size": (c_int, [c_void_p]),
+    "cuinf_tokenizer_encode": (c_int, [c_void_p, ctypes.c_char_p, c_size_t, c_void_p, c_int, c_void_p]),
+    "cuinf_tokenizer_decode": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "cuinf_chat_prompt": (c_int, [ctypes.c_char_p, c_void_p, c_size_t, c_void_p]),
     "cuinf_session_set_kv_budget": (c_int, [c_void_p, c_int, c_int]),
     "cuinf_session_h2o_state": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "cuinf_batch_create": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),

@@ -15,7 +15,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libcuinf.so")
-SOURCES = ["ops.cu", "engine.cu", "batch.cu"]
+SOURCES = ["ops.cu", "engine.cu", "batch.cu", "tokenizer.cpp"]
 HEADERS = ["common.cuh", "attn.cuh", "engine_kernels.cuh", "route.cuh", "tc_gemm.cuh", "model.h"]
 
 NVCC = os.environ.get("NVCC", "nvcc")

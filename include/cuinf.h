@@ -263,6 +263,20 @@ int cuinf_batch_error(unsigned* flags);
  * duration of launch i, names[i * name_len] its name; advances the batch. */
 int cuinf_batch_profile_step(cuinf_batch* b, int max_kernels, float* ms, char* names, int name_len,
                              int* n_kernels);
+/* Tokenizer (the reference's src/tokenizer.h and its files from
+ * tools/export_tokenizer.py: vocab.tsv, merges.tsv, special.tsv in `dir`):
+ * GPT-2 byte-level BPE with the reference's pre-tokenizer rules and literal
+ * special tokens.  encode: *n_out = the full count (ids holds the first cap);
+ * decode: *len_out = the full byte length (out holds the first cap).
+ * cuinf_chat_prompt: the reference's single-turn template (engine.cu:697-699). */
+typedef struct cuinf_tokenizer cuinf_tokenizer;
+int cuinf_tokenizer_load(const char* dir, cuinf_tokenizer** out);
+int cuinf_tokenizer_free(cuinf_tokenizer* t);
+int cuinf_tokenizer_vocab_size(const cuinf_tokenizer* t);
+int cuinf_tokenizer_encode(const cuinf_tokenizer* t, const char* text, size_t len, int* ids, int cap, int* n_out);
+int cuinf_tokenizer_decode(const cuinf_tokenizer* t, const int* ids, int n, int skip_special, char* out, size_t cap,
+                           size_t* len_out);
+int cuinf_chat_prompt(const char* user, char* out, size_t cap, size_t* len_out);
 /* Batched prompt processing, replacing the reference's prefill
  * (src/engine.cu:910-917: layer_forward with S = n_ids, 784-908): every layer
  * runs on all S tokens at positions pos..pos+S-1; each attention layer first
