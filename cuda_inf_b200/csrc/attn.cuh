@@ -314,46 +314,46 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // stage (m, l) of every split in shared memory, then one weight per split
+    // Thread (r, d) merges output d of query row r over the splits, 32 splits
+    // per round with all their (m, l, o) requested at once (one L2 round trip
+    // per round), rescaled online; with nsplit <= 32 this is exactly
+    // gm = max m, L = sum l*2^(m-gm), o = sum o*2^(m-gm) in split order.
     const float* hp = part_b + (size_t)h * P.nsplit * gqa * ATTN_PART_STRIDE;
-    float* s_m = &sm[0][0][0];                 // [nsplit*gqa]
-    float* s_l = s_m + ATTN_MAX_PARTS;         // [nsplit*gqa]
-    float* s_g = s_l + ATTN_MAX_PARTS;         // [gqa] max, [gqa] sum (at +8)
-    const int np = P.nsplit * gqa;
-    for (int i = threadIdx.x; i < np; i += blockDim.x) {
-        s_m[i] = __ldcg(hp + (size_t)i * ATTN_PART_STRIDE);
-        s_l[i] = __ldcg(hp + (size_t)i * ATTN_PART_STRIDE + 1);
-    }
-    __syncthreads();
-    if (threadIdx.x < gqa) {
-        const int r = threadIdx.x;
-        float gm = ATTN_NEG;
-        for (int sp2 = 0; sp2 < P.nsplit; sp2++)
-            if (s_l[sp2 * gqa + r] > 0.f) gm = fmaxf(gm, s_m[sp2 * gqa + r]);
-        float L = 0.f;
-        for (int sp2 = 0; sp2 < P.nsplit; sp2++) {
-            const int i = sp2 * gqa + r;
-            const float e = s_l[i] > 0.f ? exp2f(s_m[i] - gm) : 0.f;
-            s_m[i] = e;  // now the split's weight
-            L += s_l[i] * e;
-        }
-        s_g[8 + r] = L;
-    }
-    __syncthreads();
     for (int it = threadIdx.x; it < gqa * 64; it += blockDim.x) {
         const int r = it >> 6, d = it & 63;
-        float o = 0.f;
-        // eight splits' values requested at a time, then summed in split order
-        for (int sp0 = 0; sp0 < P.nsplit; sp0 += 8) {
-            float v[8];
+        float gm = ATTN_NEG, L = 0.f, o = 0.f;
+        for (int sp0 = 0; sp0 < P.nsplit; sp0 += 32) {
+            float vm[32], vl[32], vo[32];
 #pragma unroll
-            for (int k = 0; k < 8; k++)
-                v[k] = sp0 + k < P.nsplit ? __ldcg(hp + (size_t)((sp0 + k) * gqa + r) * ATTN_PART_STRIDE + 4 + d) : 0.f;
+            for (int k = 0; k < 32; k++) {
+                vm[k] = ATTN_NEG;
+                vl[k] = 0.f;
+                vo[k] = 0.f;
+                if (sp0 + k < P.nsplit) {
+                    const float* pr = hp + (size_t)((sp0 + k) * gqa + r) * ATTN_PART_STRIDE;
+                    vm[k] = __ldcg(pr);
+                    vl[k] = __ldcg(pr + 1);
+                    vo[k] = __ldcg(pr + 4 + d);
+                }
+            }
+            float cm = gm;
 #pragma unroll
-            for (int k = 0; k < 8; k++)
-                if (sp0 + k < P.nsplit) o += s_m[(sp0 + k) * gqa + r] * v[k];
+            for (int k = 0; k < 32; k++)
+                if (vl[k] > 0.f) cm = fmaxf(cm, vm[k]);
+            if (cm > gm) {
+                const float sc = exp2f(gm - cm);
+                L *= sc;
+                o *= sc;
+                gm = cm;
+            }
+#pragma unroll
+            for (int k = 0; k < 32; k++) {
+                const float e = vl[k] > 0.f ? exp2f(vm[k] - gm) : 0.f;
+                L += vl[k] * e;
+                o += e * vo[k];
+            }
         }
-        P.out[b * P.bout + (size_t)(h * gqa + r) * CUINF_HD + d] = __float2half_rn(o / s_g[8 + r]);
+        P.out[b * P.bout + (size_t)(h * gqa + r) * CUINF_HD + d] = __float2half_rn(o / L);
     }
     if (threadIdx.x == 0) cnt_b[h] = 0u;
 }

@@ -290,6 +290,19 @@ static cudaError_t launch_kc(Kern kernel, dim3 grid, dim3 block, size_t smem, cu
 
 static int set_kernel_attrs(const cuinf_config& c);
 
+// Dynamic shared memory for a kernel whose grid fits on the SMs and whose
+// CTAs should each hold an SM alone: more than half of the SM's 228 KB, so
+// no second CTA of the kernel fits.  A launch that follows another kernel
+// (programmatic dependent launch) otherwise gets its CTAs packed 2-3 to an
+// SM on whichever SMs have room at that moment, and the per-CTA dot
+// (dequantize + mma.sync, bound by the SM's issue rate) then runs 2-3 times
+// in sequence there while other SMs idle.  Used for k_conv_in and
+// k_gemv_residual (128 CTAs each at H = 2048).
+#define ONE_PER_SM_SMEM ((size_t)116 * 1024)
+static inline size_t one_per_sm(size_t bytes, int grid, int sms) {
+    return grid <= sms ? std::max(bytes, ONE_PER_SM_SMEM) : bytes;
+}
+
 // k_moe_up + k_moe_down for one token: xn already normalized, h += the
 // rank-ordered expert mix; mid [topk*I] fp16 and the routes are scratch.
 static int moe_ffn_launch(const __half* xn, const __half* gate, const __half* bias, const void* const* experts,
@@ -923,6 +936,7 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
     const int H = c.hidden;
     cudaStream_t st = s->st;
     const int nh = c.n_heads, nkv = c.n_kv_heads;
+    const int sms = s->num_sms;
     std::vector<Launch> Ls;
     for (int l = 0; l < c.n_layers; l++) {
         const LayerW& L = m->L[l];
@@ -996,7 +1010,7 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
                           {q4_range(L.wo, H, nh * 64)},
                           [=](const L2Ranges& nx, bool pdl) mutable {
                               R.next = nx;
-                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), res_smem(nh * 64), st, pdl, R);
+                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), one_per_sm(res_smem(nh * 64), H / 16, sms), st, pdl, R);
                           }});
         } else {
             ConvParams C;
@@ -1013,14 +1027,14 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
             Ls.push_back({"conv_in", q4_bytes(3 * H, H) + 18.0 * H, {q4_range(L.in_proj, 3 * H, H)},
                           [=](const L2Ranges& nx, bool pdl) mutable {
                               C.next = nx;
-                              return launch_k(k_conv_in, dim3(H / 16), dim3(384), conv_smem(H), st, pdl, C);
+                              return launch_k(k_conv_in, dim3(H / 16), dim3(384), one_per_sm(conv_smem(H), H / 16, sms), st, pdl, C);
                           }});
             ResParams R;
             R.act = s->conv_y; R.wp = L.out_proj.p; R.ws = L.out_proj.s; R.h = s->h; R.N = H; R.K = H;
             Ls.push_back({"conv_out_proj", q4_bytes(H, H) + 6.0 * H, {q4_range(L.out_proj, H, H)},
                           [=](const L2Ranges& nx, bool pdl) mutable {
                               R.next = nx;
-                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), res_smem(H), st, pdl, R);
+                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), one_per_sm(res_smem(H), H / 16, sms), st, pdl, R);
                           }});
         }
         if (l < c.n_dense) {
@@ -1040,7 +1054,7 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
             Ls.push_back({"dense_down", q4_bytes(H, I) + 2.0 * I + 4.0 * H, {q4_range(L.w2, H, I)},
                           [=](const L2Ranges& nx, bool pdl) mutable {
                               R.next = nx;
-                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), res_smem(I), st, pdl, R);
+                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), one_per_sm(res_smem(I), H / 16, sms), st, pdl, R);
                           }});
         } else {
             const int mi = L.moe_index;
@@ -1090,12 +1104,13 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
     LM.H = H;
     LM.V = c.vocab;
     LM.eps = c.norm_eps;
-    const int lm_grid = ((c.vocab + 15) / 16 + 7) / 8;
+    const int lm_stages = (c.vocab + lmhead_rows_per_stage(H) - 1) / lmhead_rows_per_stage(H);
+    const int lm_grid = std::min(s->num_sms, lm_stages);
     Ls.push_back({"lm_head_argmax", (double)c.vocab * H * 2 + 6.0 * H,
                   {{(const char*)m->embed, (unsigned long long)c.vocab * H * 2}},
                   [=](const L2Ranges& nx, bool pdl) mutable {
                       LM.next = nx;
-                      return launch_k(k_lmhead, dim3(lm_grid), dim3(256), (size_t)H * 2 + 64 * 4, st, pdl, LM);
+                      return launch_k(k_lmhead, dim3(lm_grid), dim3(LM_THREADS), lmhead_smem(H), st, pdl, LM);
                   }});
 
     std::vector<L2Ranges> plans;
@@ -1131,12 +1146,13 @@ static int set_kernel_attrs(const cuinf_config& c) {
 
     struct { const void* k; size_t bytes; } need[] = {
         {(const void*)k_attn_qkv, qkv_smem(H)},
-        {(const void*)k_conv_in, conv_smem(H)},
+        {(const void*)k_conv_in, std::max(conv_smem(H), ONE_PER_SM_SMEM)},
         {(const void*)k_ffn_up, ffn_up_smem(H)},
         {(const void*)k_moe_up, moe_up_smem(H, std::max(1, c.n_experts))},
         {(const void*)k_moe_down, moe_down_smem(c.moe_inter, std::max(1, c.top_k))},
+        {(const void*)k_lmhead, lmhead_smem(H)},
         {(const void*)k_gemv_residual,
-         std::max(res_smem(H), std::max(res_smem(c.n_heads * 64), res_smem(c.dense_inter)))},
+         std::max(ONE_PER_SM_SMEM, std::max(res_smem(H), std::max(res_smem(c.n_heads * 64), res_smem(c.dense_inter))))},
     };
     for (auto& n : need) {
         if (n.bytes > 227 * 1024) return cuinf_set_arg_error("model dims too large for shared memory");
@@ -1200,7 +1216,9 @@ extern "C" int cuinf_session_create(cuinf_model* m, int max_ctx, void* stream, c
     TRYS(dalloc(s, &s->am_key, 16));
     TRYS(dalloc(s, &s->am_ticket, 16));
     const int units = max_ctx / CUINF_KVGROUP + 1;
-    s->nsplit = attn_engine_nsplit(gqa, units);
+    // k_attn_decode holds one CTA per SM (its registers): keep every split
+    // of every kv head in one wave
+    s->nsplit = std::min(attn_engine_nsplit(gqa, units), std::max(1, s->num_sms / nkv));
     TRYS(dalloc(s, &s->attn_part, (size_t)nkv * s->nsplit * gqa * ATTN_PART_STRIDE * 4));
     TRYS(dalloc(s, &s->attn_cnt, (size_t)nkv * 4));
     s->attn.assign(c.n_layers, AttnState());

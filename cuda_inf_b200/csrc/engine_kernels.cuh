@@ -509,8 +509,11 @@ __host__ __device__ inline size_t moe_up_stage_bytes(int H, int E) {
     const size_t gate = (size_t)((E + 7) / 8) * H * 2, tiles = 2 * (size_t)int4_tile_bytes(H);
     return gate > tiles ? gate : tiles;
 }
+// + the router bias (E <= 256 halves) and the expert pointer table [E][6],
+// both static, copied to shared memory before the dependency wait so the
+// selection and the route-dependent copies read no global memory.
 __host__ __device__ inline size_t moe_up_smem(int H, int E) {
-    return moe_up_stage_bytes(H, E) + (size_t)H * 4 + (160 + 32 + 256 + 32) * 4;
+    return moe_up_stage_bytes(H, E) + (size_t)H * 4 + (160 + 32 + 256 + 32) * 4 + 512 + (size_t)E * 6 * 8;
 }
 
 __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpParams P) {
@@ -527,6 +530,8 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     float* lg_all = lg_mine + 32;                     // [256]
     int* sidx = reinterpret_cast<int*>(lg_all + 256);  // [16]
     float* sw = reinterpret_cast<float*>(sidx + 16);   // [16]
+    __half* sbias = reinterpret_cast<__half*>(sw + 16);  // [E]
+    const void** stab = reinterpret_cast<const void**>(reinterpret_cast<unsigned char*>(sbias) + 512);  // [E][6]
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -545,6 +550,8 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     }
     NormW nw;
     if (!P.xn) norm_w_load(nw, P.norm_w, P.H);
+    for (int i = threadIdx.x; i < P.E; i += blockDim.x) sbias[i] = P.bias[i];
+    for (int i = threadIdx.x; i < P.E * 6; i += blockDim.x) stab[i] = P.experts[i];
     pdl_trigger();
     pdl_wait();
     if (P.xn) {
@@ -591,7 +598,7 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     cluster.sync();
     // scratch for the selection: the gate rows' region, consumed by now (the
     // expert tiles are staged into it only after the selection)
-    route_select_block(lg_all, P.bias, P.E, P.topk, sidx, sw, reinterpret_cast<float*>(gs));
+    route_select_block(lg_all, sbias, P.E, P.topk, sidx, sw, reinterpret_cast<float*>(gs));
     if (blockIdx.x == 0 && threadIdx.x < P.topk) {
         P.route_idx[threadIdx.x] = sidx[threadIdx.x];
         P.route_w[threadIdx.x] = sw[threadIdx.x];
@@ -600,19 +607,20 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     const int item = blockIdx.x;
     const bool active = item < P.topk * tiles_per;
     const int t = active ? item / tiles_per : 0, row0 = active ? (item % tiles_per) * 16 : 0;
-    const void* const* ex = P.experts + (size_t)sidx[t] * 6;
+    const void* const* ex = stab + (size_t)sidx[t] * 6;
     if (threadIdx.x == 0 && active) {
         mbar_arrive_expect_tx(&bar[1], 2 * TB);
         tma_tile_int4((const uint8_t*)ex[0], (const __half*)ex[1], P.H, row0, tiles, &bar[1]);
         tma_tile_int4((const uint8_t*)ex[2], (const __half*)ex[3], P.H, row0, tiles + TB, &bar[1]);
     }
-    // the selected experts' w2 (read by moe_down next) into L2, over the grid
+    // the selected experts' w2 (read by moe_down next) into L2, over the
+    // grid, issued by another warp than the one that issued the tiles
     auto prefetch_w2 = [&]() {
-        if (threadIdx.x != 0) return;
+        if (threadIdx.x != 32) return;
         L2Ranges R;
         R.count = 0;
         for (int k = 0; k < P.topk && R.count < 7; k++) {
-            const void* const* e2 = P.experts + (size_t)sidx[k] * 6;
+            const void* const* e2 = stab + (size_t)sidx[k] * 6;
             R.p[R.count] = (const char*)e2[4];
             R.n[R.count++] = (unsigned long long)P.H * (P.I >> 1);
             R.p[R.count] = (const char*)e2[5];
@@ -729,12 +737,15 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeDownParams P) {
 
 // ---------------------------------------------------------------------------
 // Final norm + tied lm_head (fp16 [V,H]) + argmax + next-token bookkeeping
-// (engine.cu:932-940).  One 16-row tile per warp, all tiles resident in one
-// wave, weights streamed with 16-byte loads that ask L2 for 256-byte blocks
-// (each row is read front to back, so the rest of the block is used by the
-// same warp's next loads).  Argmax: 64-bit keys (argmax_key) reduced per
-// CTA, then atomicMax; the last CTA (atomic ticket) publishes the token,
-// advances pos and resets.
+// (engine.cu:932-940).  Persistent: one CTA per SM owns a contiguous run of
+// vocabulary rows.  Warp 8 streams the rows into a ring of LM_NST 32 KB
+// stages with bulk copies; it starts before the dependency wait (the
+// weights are static), so the first stages are in flight while the
+// previous kernel finishes.  Warps 0-7 normalise h and take the stage's
+// rows round-robin: one row per warp at a time, 16-byte chunks per lane,
+// fp32 products (exact for fp16 operands) summed in fp32.  Argmax: 64-bit
+// keys (argmax_key) reduced per CTA, then atomicMax; the last CTA (atomic
+// ticket) publishes the token, advances pos and resets.
 // ---------------------------------------------------------------------------
 struct LmHeadParams {
     const __half* h;
@@ -753,54 +764,146 @@ struct LmHeadParams {
     L2Ranges next;  // the first kernels of the next step
 };
 
-__global__ void __launch_bounds__(256) k_lmhead(LmHeadParams P) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __half* xs = reinterpret_cast<__half*>(smem);
-    float* red = reinterpret_cast<float*>(xs + P.H);
-    __shared__ unsigned long long kred[8];
+#define LM_STAGE_BYTES 32768
+#define LM_NST 4
+#define LM_WARPS 8  // row warps; warp LM_WARPS streams the weights
+#define LM_THREADS ((LM_WARPS + 1) * 32)
+// Rows per stage (H <= 16384, H % 8 == 0: the host checks).
+__host__ __device__ inline int lmhead_rows_per_stage(int H) { return LM_STAGE_BYTES / (2 * H); }
+__host__ __device__ inline size_t lmhead_smem(int H) {
+    return (size_t)LM_NST * LM_STAGE_BYTES + (size_t)H * 2 + 64 * 4;
+}
+// barrier of the row warps only (the streaming warp is not part of it)
+__device__ __forceinline__ void lm_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(LM_WARPS * 32) : "memory"); }
+
+__global__ void __launch_bounds__(LM_THREADS, 1) k_lmhead(LmHeadParams P) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t full[LM_NST], empty[LM_NST];
+    __shared__ unsigned long long kred[LM_WARPS];
     __shared__ int s_last;
+    unsigned char* ring = smem;
+    __half* xs = reinterpret_cast<__half*>(smem + (size_t)LM_NST * LM_STAGE_BYTES);
+    float* red = reinterpret_cast<float*>(xs + P.H);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntiles = (P.V + 15) / 16;
-    const int tile0 = blockIdx.x * 8 + warp;
-    if (threadIdx.x == 0) l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
-    pdl_trigger();
-    pdl_wait();
-    for (int i = threadIdx.x; i < P.H; i += blockDim.x) xs[i] = P.h[i];
-    __syncthreads();
-    if (blockIdx.x == 0 && P.hidden_out)
-        for (int i = threadIdx.x; i < P.H; i += blockDim.x) P.hidden_out[i] = xs[i];
-    rmsnorm_smem(xs, P.norm_w, xs, P.H, P.eps, red);
-    __syncthreads();
-    unsigned long long best = 0ull;
-    for (int tile = tile0; tile < ntiles; tile += gridDim.x * 8) {
-        float y0 = 0.f, y1 = 0.f;
-        f16_tile_dot<4>(P.W, P.V, P.H, tile * 16, 0, P.H >> 5, 1, xs, y0, y1);
-        const int r0 = tile * 16 + (lane >> 2), r1 = r0 + 8;
-        if ((lane & 3) == 0) {
-            if (r0 < P.V) {
-                if (P.logits) P.logits[r0] = y0;
-                if (y0 > -1e30f) best = umax64_dev(best, argmax_key(y0 == 0.f ? 0.f : y0, r0));
-            }
-            if (r1 < P.V) {
-                if (P.logits) P.logits[r1] = y1;
-                if (y1 > -1e30f) best = umax64_dev(best, argmax_key(y1 == 0.f ? 0.f : y1, r1));
-            }
+    const int rps = lmhead_rows_per_stage(P.H);
+    const int nst = (P.V + rps - 1) / rps;
+    const int s0 = (int)((long long)nst * blockIdx.x / gridDim.x);
+    const int s1 = (int)((long long)nst * (blockIdx.x + 1) / gridDim.x);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < LM_NST; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], LM_WARPS);
         }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) best = umax64_dev(best, __shfl_xor_sync(0xffffffffu, best, o));
-    if (lane == 0) kred[warp] = best;
     __syncthreads();
+    pdl_trigger();
+    if (warp == LM_WARPS) {
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            int last[LM_NST];
+            for (int i = 0; i < LM_NST; i++) last[i] = -1;
+            for (int j = 0; j < s1 - s0; j++) {
+                const int slot = j % LM_NST;
+                if (j >= LM_NST && !mbar_wait_bounded(&empty[slot], ((j / LM_NST) - 1) & 1, &g_engine_err)) break;
+                const int r0 = (s0 + j) * rps, nr = min(rps, P.V - r0);
+                mbar_arrive_expect_tx(&full[slot], (uint32_t)nr * P.H * 2);
+                tma_load_1d_hint(ring + (size_t)slot * LM_STAGE_BYTES, P.W + (size_t)r0 * P.H,
+                                 (uint32_t)nr * P.H * 2, &full[slot], pol);
+                last[slot] = j;
+                if (j == LM_NST - 1) l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
+            }
+            if (s1 - s0 < LM_NST) l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
+            // copies still in flight land before the CTA can exit
+            for (int i = 0; i < LM_NST; i++)
+                if (last[i] >= 0) mbar_wait_bounded(&full[i], (last[i] / LM_NST) & 1, &g_engine_err);
+        }
+        return;
+    }
+    // the norm weight (static) is read before the dependency wait; h and the
+    // weight move in 16-byte chunks, two per thread at H <= 4096
+    const int n8 = P.H >> 3;
+    uint4 nwv[2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int i = threadIdx.x + r * LM_WARPS * 32;
+        nwv[r] = i < n8 ? ldg_stream(P.norm_w + 8 * i) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    pdl_wait();
+    {  // rmsnorm (engine.cu:131-144) into xs; block 0 also keeps the raw h
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < n8; i += LM_WARPS * 32) {
+            const uint4 v = *reinterpret_cast<const uint4*>(P.h + 8 * i);
+            *reinterpret_cast<uint4*>(xs + 8 * i) = v;
+            if (blockIdx.x == 0 && P.hidden_out) *reinterpret_cast<uint4*>(P.hidden_out + 8 * i) = v;
+            const __half* e = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                const float f = __half2float(e[q]);
+                ss = fmaf(f, f, ss);
+            }
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) red[warp] = ss;
+        lm_sync();
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < LM_WARPS; w++) t += red[w];
+        const float inv = rsqrtf(t / (float)P.H + P.eps);
+        for (int i = threadIdx.x, r = 0; i < n8; i += LM_WARPS * 32, r++) {
+            const uint4 v = *reinterpret_cast<const uint4*>(xs + 8 * i);
+            const uint4 wv = r == 0 ? nwv[0] : r == 1 ? nwv[1] : ldg_stream(P.norm_w + 8 * i);
+            const __half* xe = reinterpret_cast<const __half*>(&v);
+            const __half* we = reinterpret_cast<const __half*>(&wv);
+            __align__(16) __half o[8];
+#pragma unroll
+            for (int q = 0; q < 8; q++) o[q] = __float2half_rn(__half2float(xe[q]) * inv * __half2float(we[q]));
+            *reinterpret_cast<uint4*>(xs + 8 * i) = *reinterpret_cast<const uint4*>(o);
+        }
+        lm_sync();
+    }
+    unsigned long long best = 0ull;
+    for (int j = 0; j < s1 - s0; j++) {
+        const int slot = j % LM_NST;
+        if (!mbar_wait_bounded(&full[slot], (j / LM_NST) & 1, &g_engine_err)) break;
+        const int r0 = (s0 + j) * rps, nr = min(rps, P.V - r0);
+        const __half* st = reinterpret_cast<const __half*>(ring + (size_t)slot * LM_STAGE_BYTES);
+        for (int r = warp; r < nr; r += LM_WARPS) {
+            const __half* wr = st + (size_t)r * P.H;
+            float acc = 0.f;
+            for (int k = lane * 8; k < P.H; k += 256) {
+                const uint4 wv = *reinterpret_cast<const uint4*>(wr + k);
+                const uint4 xv = *reinterpret_cast<const uint4*>(xs + k);
+                const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
+                const __half2* x2 = reinterpret_cast<const __half2*>(&xv);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const float2 a = __half22float2(w2[q]), b = __half22float2(x2[q]);
+                    acc = fmaf(a.x, b.x, acc);
+                    acc = fmaf(a.y, b.y, acc);
+                }
+            }
+            acc = warp_sum(acc);
+            const int row = r0 + r;
+            if (lane == 0) {
+                if (P.logits) P.logits[row] = acc;
+                if (acc > -1e30f) best = umax64_dev(best, argmax_key(acc == 0.f ? 0.f : acc, row));
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (lane == 0) kred[warp] = best;
+    lm_sync();
     if (threadIdx.x == 0) {
         unsigned long long b = 0ull;
 #pragma unroll
-        for (int w = 0; w < 8; w++) b = umax64_dev(b, kred[w]);
+        for (int w = 0; w < LM_WARPS; w++) b = umax64_dev(b, kred[w]);
         if (b) atomicMax(P.key, b);
         __threadfence();
         unsigned prev = atomicAdd(P.ticket, 1u);
         s_last = prev == gridDim.x - 1;
     }
-    __syncthreads();
+    lm_sync();
     if (!s_last || threadIdx.x != 0) return;
     __threadfence();
     const unsigned long long k = atomicExch(P.key, 0ull);

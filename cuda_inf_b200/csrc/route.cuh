@@ -92,10 +92,11 @@ __device__ __forceinline__ void route_select_block(const float* logits, const __
                 const float score = sig + __half2float(bias[e]);
                 key = (score > -1e30f) ? score : -INFINITY;
             }
-            int rank = 0;
-            for (int o = 0; o < n_exp; o++) {
+            int rank = 0;  // 32 independent shuffles, unrolled so they pipeline
+#pragma unroll
+            for (int o = 0; o < 32; o++) {
                 const float ko = __shfl_sync(0xffffffffu, key, o);
-                rank += (ko > key || (ko == key && o < e)) ? 1 : 0;
+                rank += (o < n_exp && (ko > key || (ko == key && o < e))) ? 1 : 0;
             }
             if (e < n_exp && rank < topk) {
                 idx[rank] = e;
