@@ -635,6 +635,74 @@ def run_reference(a, ws, rank):
     }
 
 
+PHASES = {  # kernel id (csrc/common.cuh PH_*) -> (name, {slot: phase reached})
+    0: ("k_attn_qkv", {0: "start", 1: "dependency wait done", 2: "norm done", 4: "dot done",
+                       5: "head gathered (rank 0)", 9: "end (rank 0 of k/v heads)"}),
+    1: ("k_gemv_residual", {0: "start", 1: "dependency wait done", 2: "x staged", 4: "dot done", 9: "end"}),
+    2: ("k_conv_in", {0: "start", 1: "dependency wait done", 2: "norm done", 4: "dot done", 9: "end"}),
+    3: ("k_ffn_up", {0: "start", 1: "dependency wait done", 2: "norm done", 4: "dot done", 9: "end"}),
+    4: ("k_moe_up", {0: "start", 1: "dependency wait done", 2: "norm done", 3: "gate rows in",
+                     4: "logits exchanged", 5: "experts selected", 6: "expert copies issued",
+                     7: "expert tiles in", 8: "dot done", 9: "end"}),
+    5: ("k_moe_down", {0: "start", 1: "dependency wait done", 2: "mid staged", 4: "cluster sum done",
+                       9: "end"}),
+    6: ("k_lmhead", {0: "start", 1: "dependency wait done", 2: "norm done", 3: "rows done",
+                     9: "token published (last CTA)"}),
+    7: ("k_attn_decode", {0: "start", 1: "dependency wait done", 2: "keys done (warp 0)",
+                          3: "combining CTA elected", 4: "combine done"}),
+}
+
+
+def phase_trace(a):
+    """Diagnostic: run the decode step built with phase timestamps
+    (libcuinf_trace.so, `python -m cuda_inf_b200.build --trace`) to context
+    a.ctx and report, for the latest launch of each kernel, when its CTAs
+    reached each phase (microseconds after the earliest kernel start of the
+    last step's traced launches; min / median / max over CTAs)."""
+    import ctypes
+    import cuda_inf_b200._lib as L
+    L.LIB_PATH = os.path.join(ROOT, "cuda_inf_b200", "libcuinf_trace.so")
+    from cuda_inf_b200 import weights as W
+    from cuda_inf_b200.engine import Model, Session
+    cfg = W.default_config()
+    blob, idx = W.synth_device_blob(cfg, seed=a.seed)
+    model = Model.from_device_blob(blob, idx, cfg)
+    stream = torch.cuda.Stream()
+    sess = Session(model, max_ctx=a.ctx + a.warmup + 16, stream=stream)
+    with torch.cuda.stream(stream):
+        for t in prompt_ids(a.seed, a.prompt_len, cfg.vocab, 0):
+            sess.step(t, want=False)
+        while sess.pos < a.ctx + a.warmup:
+            sess.step(-1, want=False)
+    stream.synchronize()
+    buf = np.zeros((8, 1024, 12), dtype=np.uint64)
+    rc = L.lib().cuinf_phase_trace_read(buf.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(buf.nbytes))
+    if rc != 0:
+        raise RuntimeError(f"cuinf_phase_trace_read failed ({rc})")
+    t = buf.astype(np.int64)
+    starts = [t[k][t[k][:, 0] > 0, 0] for k in range(8)]
+    t0 = min(int(x.min()) for x in starts if len(x))
+    out = {}
+    for k, (name, slots) in PHASES.items():
+        live = t[k][:, 0] > 0
+        if not live.any():
+            continue
+        rows = t[k][live]
+        ent = {"ctas": int(live.sum()), "sms": int(len(np.unique(rows[:, 11]))), "phases": {}}
+        for sl, what in slots.items():
+            # a mark older than its CTA's start is from an earlier launch (the
+            # CTA did not reach that phase this time): dropped
+            col = rows[:, sl]
+            col = col[col >= rows[:, 0]] - t0
+            if len(col):
+                ent["phases"][f"{sl} {what}"] = [round(float(col.min()) / 1e3, 2),
+                                                  round(float(np.median(col)) / 1e3, 2),
+                                                  round(float(col.max()) / 1e3, 2)]
+        out[name] = ent
+    return {"profiling_only": True, "phase_trace_us_min_med_max": out,
+            "context": int(sess.pos), "note": "latest launch of each kernel in the last step"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -658,6 +726,8 @@ def main():
     ap.add_argument("--prefill-len", type=int, default=4096,
                     help="config 5b prefill length (0 = skip)")
     ap.add_argument("--batch-warmup", type=int, default=3)
+    ap.add_argument("--phase-trace", action="store_true",
+                    help="diagnostic: per-phase timestamps of the decode kernels (needs build --trace)")
     ap.add_argument("--profile-small", action="store_true",
                     help="6-layer, 32k-vocab model of the same shapes, for profiler captures only")
     a = ap.parse_args()
@@ -666,6 +736,12 @@ def main():
     if a.impl == "reference":
         if rank == 0:
             print(json.dumps(run_reference(a, ws, rank)), flush=True)
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+        return
+    if a.phase_trace:
+        if rank == 0:
+            print(json.dumps(phase_trace(a)), flush=True)
         if ws > 1:
             torch.distributed.destroy_process_group()
         return

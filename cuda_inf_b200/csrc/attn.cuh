@@ -234,10 +234,12 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     const __half* vtail = P.vtail + b * P.btail;
     float* const part_b = P.part + b * P.bpart;
     unsigned* const cnt_b = P.counters + b * nkv;
+    PHASE(PH_ATTN, 0);
     if (threadIdx.x == 0 && P.next.count)
         l2_prefetch_share(P.next, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     pdl_trigger();
     pdl_wait();  // q and the cache come from the previous kernel
+    PHASE(PH_ATTN, 1);
     int qpos = P.qpos, committed = P.committed;
     if (P.pos_dev) {
         qpos = P.pos_dev[b];
@@ -273,6 +275,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     attn_warp_units<false, ATTN_PARTS>(kc8, vc8, ksc, vsc, ktail, vtail, nkv, h, n_fp8, tail_len,
                                        kfac, aq, u0 * ATTN_PARTS + warp, u1 * ATTN_PARTS, ATTN_THREADS / 32,
                                        m_run, l_run, O);
+    PHASE(PH_ATTN, 2);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
 
@@ -313,6 +316,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
     }
     __syncthreads();
     if (!s_last) return;
+    PHASE(PH_ATTN, 3);
     __threadfence();
     // Thread (r, d) merges output d of query row r over the splits, 32 splits
     // per round with all their (m, l, o) requested at once (one L2 round trip
@@ -356,6 +360,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
         P.out[b * P.bout + (size_t)(h * gqa + r) * CUINF_HD + d] = __float2half_rn(o / L);
     }
     if (threadIdx.x == 0) cnt_b[h] = 0u;
+    PHASE(PH_ATTN, 4);
 }
 
 // Prefill attention (attention_fused, engine.cu:236-308): query token i of

@@ -125,6 +125,41 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
     return t;
 }
+// Phase timestamps of the decode-step kernels, for diagnostic builds only
+// (-DCUINF_PHASE_TRACE, `python -m cuda_inf_b200.build --trace`): thread 0
+// of every CTA stores %globaltimer at each marked phase of its kernel's
+// latest launch (kernel id k, phase i < 10; slot 11 = the CTA's SM).
+// Product builds compile the marks away.
+#define PH_QKV 0
+#define PH_RES 1
+#define PH_CONV 2
+#define PH_FFN 3
+#define PH_MOE_UP 4
+#define PH_MOE_DOWN 5
+#define PH_LMHEAD 6
+#define PH_ATTN 7
+#ifdef CUINF_PHASE_TRACE
+static __device__ unsigned long long g_phase[8][1024][12];
+__device__ __forceinline__ void phase_mark(int k, int i) {
+    if (threadIdx.x == 0) {
+        const unsigned cta = blockIdx.x + blockIdx.y * gridDim.x;
+        if (cta < 1024) {
+            g_phase[k][cta][i] = globaltimer_ns();
+            if (i == 0) {
+                unsigned sm;
+                asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+                g_phase[k][cta][11] = sm;
+            }
+        }
+    }
+}
+#define PHASE(k, i) phase_mark(k, i)
+#else
+#define PHASE(k, i) \
+    do {            \
+    } while (0)
+#endif
+
 // Every wait in these kernels gives up after this long (wall time), sets an
 // error flag and lets the kernel finish.
 #define CUINF_WAIT_LIMIT_NS 4000000000ull

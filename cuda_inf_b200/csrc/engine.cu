@@ -1687,3 +1687,13 @@ extern "C" int cuinf_session_profile_step(cuinf_session* s, int token, int max_k
     *n_kernels = n;
     return rc;
 }
+
+#ifdef CUINF_PHASE_TRACE
+// Diagnostic builds only: copies the phase timestamps of the latest launch of
+// every decode-step kernel ([8 kernels][1024 CTAs][12] u64) to host memory.
+extern "C" int cuinf_phase_trace_read(void* dst, size_t bytes) {
+    REQUIRE(dst && bytes >= sizeof(g_phase), "buffer too small");
+    CUINF_TRY(cudaMemcpyFromSymbol(dst, g_phase, sizeof(g_phase)));
+    return CUINF_OK;
+}
+#endif

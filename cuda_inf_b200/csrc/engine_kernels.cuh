@@ -183,6 +183,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256) k_attn_qkv(QkvP
     const int rank = (int)cluster.block_rank();
     const int hh = blockIdx.x >> 2;
     const int warp = threadIdx.x >> 5;
+    PHASE(PH_QKV, 0);
 
     const uint8_t* wp;
     const __half* ws;
@@ -201,12 +202,15 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256) k_attn_qkv(QkvP
     norm_w_load(nw, P.norm_w, P.H);
     pdl_trigger();
     pdl_wait();
+    PHASE(PH_QKV, 1);
     norm_prologue_fast(nw, P.h, P.embed, P.tok, P.h_store, P.H, P.eps, xs, xB, red + 128);
+    PHASE(PH_QKV, 2);
     float y0 = 0.f, y1 = 0.f;
     if (stage_wait(&bar))
         int4_tile_dot_smem<2>(tile, P.H, warp, P.H >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
     warp_partials(red, warp, y0, y1);
     __syncthreads();
+    PHASE(PH_QKV, 4);
     if (threadIdx.x < 16) {
         float s = 0.f;
 #pragma unroll
@@ -220,6 +224,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256) k_attn_qkv(QkvP
     }
     cluster.sync();
     if (rank != 0) return;
+    PHASE(PH_QKV, 5);
 
     const int pos = *P.pos;
     const int committed = (pos / CUINF_KVGROUP) * CUINF_KVGROUP;
@@ -287,6 +292,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(256) k_attn_qkv(QkvP
                 (uint8_t)__nv_cvt_float_to_fp8(v / s, __NV_SATFINITE, __NV_E4M3);
         }
     }
+    PHASE(PH_QKV, 9);
 }
 
 // ---------------------------------------------------------------------------
@@ -314,6 +320,7 @@ __global__ void __launch_bounds__(256) k_gemv_residual(ResParams P) {
     __half* xB = reinterpret_cast<__half*>(smem + int4_tile_bytes(P.K));
     float* red = reinterpret_cast<float*>(xB + P.K);
     const int warp = threadIdx.x >> 5, row0 = blockIdx.x * 16;
+    PHASE(PH_RES, 0);
     stage_begin(&bar);
     if (threadIdx.x == 0) {
         mbar_arrive_expect_tx(&bar, int4_tile_bytes(P.K));
@@ -322,13 +329,16 @@ __global__ void __launch_bounds__(256) k_gemv_residual(ResParams P) {
     }
     pdl_trigger();
     pdl_wait();
+    PHASE(PH_RES, 1);
     for (int e = threadIdx.x; e < P.K / 4; e += blockDim.x) build_xB_entry(P.act, xB, e);
     __syncthreads();
+    PHASE(PH_RES, 2);
     float y0 = 0.f, y1 = 0.f;
     if (stage_wait(&bar))
         int4_tile_dot_smem<2>(tile, P.K, warp, P.K >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
     warp_partials(red, warp, y0, y1);
     __syncthreads();
+    PHASE(PH_RES, 4);
     if (threadIdx.x < 16) {
         float s = 0.f;
 #pragma unroll
@@ -336,6 +346,7 @@ __global__ void __launch_bounds__(256) k_gemv_residual(ResParams P) {
         const int n = row0 + threadIdx.x;
         if (n < P.N) P.h[n] = __float2half_rn(__half2float(P.h[n]) + s);
     }
+    PHASE(PH_RES, 9);
 }
 
 // ---------------------------------------------------------------------------
@@ -373,6 +384,7 @@ __global__ void __launch_bounds__(384) k_conv_in(ConvParams P) {
     float* red = reinterpret_cast<float*>(xB + P.H);  // [12][16] + 32
     const int warp = threadIdx.x >> 5;
     const int tile = warp >> 2, c0 = blockIdx.x * 16;
+    PHASE(PH_CONV, 0);
     stage_begin(&bar);
     if (threadIdx.x == 0) {
         mbar_arrive_expect_tx(&bar, 3 * TB);
@@ -396,13 +408,16 @@ __global__ void __launch_bounds__(384) k_conv_in(ConvParams P) {
     }
     pdl_trigger();
     pdl_wait();
+    PHASE(PH_CONV, 1);
     norm_prologue_fast(nw, P.h, P.embed, P.tok, P.h_store, P.H, P.eps, xs, xB, red + 192);
+    PHASE(PH_CONV, 2);
     float y0 = 0.f, y1 = 0.f;
     if (stage_wait(&bar))
         int4_tile_dot_smem<2>(tiles + tile * TB, P.H, warp & 3, P.H >> 7, 4,
                               reinterpret_cast<const uint2*>(xB), y0, y1);
     warp_partials(red, warp, y0, y1);
     __syncthreads();
+    PHASE(PH_CONV, 4);
     if (threadIdx.x < 16) {
         const int i = threadIdx.x, c = c0 + i;
         float v[3];
@@ -417,6 +432,7 @@ __global__ void __launch_bounds__(384) k_conv_in(ConvParams P) {
         P.state[c] = cs1;
         P.state[P.H + c] = Bx;
     }
+    PHASE(PH_CONV, 9);
 }
 
 // ---------------------------------------------------------------------------
@@ -450,6 +466,7 @@ __global__ void __launch_bounds__(256) k_ffn_up(FfnUpParams P) {
     float* red = reinterpret_cast<float*>(xB + P.H);
     const int warp = threadIdx.x >> 5, row0 = blockIdx.x * 16;
     const int tile = warp & 1;
+    PHASE(PH_FFN, 0);
     stage_begin(&bar);
     if (threadIdx.x == 0) {
         mbar_arrive_expect_tx(&bar, 2 * TB);
@@ -461,13 +478,16 @@ __global__ void __launch_bounds__(256) k_ffn_up(FfnUpParams P) {
     norm_w_load(nw, P.norm_w, P.H);
     pdl_trigger();
     pdl_wait();
+    PHASE(PH_FFN, 1);
     norm_prologue_fast(nw, P.h, nullptr, nullptr, nullptr, P.H, P.eps, xs, xB, red + 128);
+    PHASE(PH_FFN, 2);
     float y0 = 0.f, y1 = 0.f;
     if (stage_wait(&bar))
         int4_tile_dot_smem<2>(tiles + tile * TB, P.H, warp >> 1, P.H >> 7, 4,
                               reinterpret_cast<const uint2*>(xB), y0, y1);
     warp_partials(red, warp, y0, y1);
     __syncthreads();
+    PHASE(PH_FFN, 4);
     if (threadIdx.x < 16) {
         const int i = threadIdx.x, r = row0 + i;
         float g = 0.f, u = 0.f;
@@ -478,6 +498,7 @@ __global__ void __launch_bounds__(256) k_ffn_up(FfnUpParams P) {
         }
         if (r < P.I) P.mid[r] = __float2half_rn(silu_fast(g) * u);
     }
+    PHASE(PH_FFN, 9);
 }
 
 // ---------------------------------------------------------------------------
@@ -537,6 +558,7 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e0 = rank * rpc, ne = max(0, min(P.E - e0, rpc));
     cluster_arrive_started();
+    PHASE(PH_MOE_UP, 0);
 
     if (threadIdx.x == 0) {
         mbar_init(&bar[0], 1);
@@ -554,6 +576,7 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     for (int i = threadIdx.x; i < P.E * 6; i += blockDim.x) stab[i] = P.experts[i];
     pdl_trigger();
     pdl_wait();
+    PHASE(PH_MOE_UP, 1);
     if (P.xn) {
         for (int i = threadIdx.x; i < P.H; i += blockDim.x) xs[i] = P.xn[i];
         __syncthreads();
@@ -562,8 +585,10 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     } else {
         norm_prologue_fast(nw, P.h, nullptr, nullptr, nullptr, P.H, P.eps, xs, xB, red + 128);
     }
+    PHASE(PH_MOE_UP, 2);
     // router rows of this cluster member: one warp per half row, from smem
     const bool gate_ok = stage_wait(&bar[0]);
+    PHASE(PH_MOE_UP, 3);
     float* lgp = red;  // [2*rpc] half-row partials
     for (int item = warp; item < 2 * rpc; item += 8) {
         const int j = item >> 1;
@@ -596,6 +621,7 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
         if (j < ne) cluster.map_shared_rank(lg_all, r)[e0 + j] = lgp[2 * j] + lgp[2 * j + 1];
     }
     cluster.sync();
+    PHASE(PH_MOE_UP, 4);
     // scratch for the selection: the gate rows' region, consumed by now (the
     // expert tiles are staged into it only after the selection)
     route_select_block(lg_all, sbias, P.E, P.topk, sidx, sw, reinterpret_cast<float*>(gs));
@@ -603,6 +629,7 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
         P.route_idx[threadIdx.x] = sidx[threadIdx.x];
         P.route_w[threadIdx.x] = sw[threadIdx.x];
     }
+    PHASE(PH_MOE_UP, 5);
     const int tiles_per = P.I / 16;
     const int item = blockIdx.x;
     const bool active = item < P.topk * tiles_per;
@@ -613,6 +640,7 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
         tma_tile_int4((const uint8_t*)ex[0], (const __half*)ex[1], P.H, row0, tiles, &bar[1]);
         tma_tile_int4((const uint8_t*)ex[2], (const __half*)ex[3], P.H, row0, tiles + TB, &bar[1]);
     }
+    PHASE(PH_MOE_UP, 6);
     // the selected experts' w2 (read by moe_down next) into L2, over the
     // grid, issued by another warp than the one that issued the tiles
     auto prefetch_w2 = [&]() {
@@ -633,12 +661,14 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
     const int tile = warp & 1;
     float y0 = 0.f, y1 = 0.f;
     const bool tiles_ok = stage_wait(&bar[1]);
+    PHASE(PH_MOE_UP, 7);
     if (tiles_ok)
         int4_tile_dot_smem<2>(tiles + tile * TB, P.H, warp >> 1, P.H >> 7, 4,
                               reinterpret_cast<const uint2*>(xB), y0, y1);
     __syncthreads();
     warp_partials(red, warp, y0, y1);
     __syncthreads();
+    PHASE(PH_MOE_UP, 8);
     if (threadIdx.x < 16) {
         const int i = threadIdx.x;
         float g = 0.f, u = 0.f;
@@ -649,6 +679,7 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(256) k_moe_up(MoeUpP
         }
         P.mid[(size_t)t * P.I + row0 + i] = __float2half_rn(silu_fast(g) * u);
     }
+    PHASE(PH_MOE_UP, 9);
 }
 
 // ---------------------------------------------------------------------------
@@ -689,10 +720,12 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeDownParams P) {
     const int row0 = (blockIdx.x / P.topk) * 16;
     const int warp = threadIdx.x >> 5;
     cluster_arrive_started();
+    PHASE(PH_MOE_DOWN, 0);
     stage_begin(&bar);
     if (threadIdx.x == 0) l2_prefetch_share(P.next, blockIdx.x, gridDim.x);
     pdl_trigger();
     pdl_wait();
+    PHASE(PH_MOE_DOWN, 1);
     if (threadIdx.x == 0) {
         mbar_arrive_expect_tx(&bar, TB);
         const void* const* ex = P.experts + (size_t)P.route_idx[t] * 6;
@@ -712,6 +745,7 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeDownParams P) {
         e1[1] = __halves2half2(o[3], o[7]);
     }
     __syncthreads();
+    PHASE(PH_MOE_DOWN, 2);
     float y0 = 0.f, y1 = 0.f;
     if (stage_wait(&bar))
         int4_tile_dot_smem<2>(tile, P.I, warp, P.I >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
@@ -726,6 +760,7 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeDownParams P) {
         dst[t * 16 + threadIdx.x] = o;
     }
     cluster.sync();
+    PHASE(PH_MOE_DOWN, 4);
     if (t == 0 && threadIdx.x < 16) {
         const int n = row0 + threadIdx.x;
         __half acc = __float2half_rn(0.f);
@@ -733,6 +768,7 @@ __global__ void __launch_bounds__(256) k_moe_down(MoeDownParams P) {
             acc = __float2half_rn(__half2float(acc) + P.route_w[k] * slots[k * 16 + threadIdx.x]);
         P.h[n] = __float2half_rn(__half2float(P.h[n]) + __half2float(acc));
     }
+    PHASE(PH_MOE_DOWN, 9);
 }
 
 // ---------------------------------------------------------------------------
@@ -797,6 +833,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) k_lmhead(LmHeadParams P) {
     }
     __syncthreads();
     pdl_trigger();
+    PHASE(PH_LMHEAD, 0);
     if (warp == LM_WARPS) {
         if (lane == 0) {
             const uint64_t pol = l2_policy_evict_first();
@@ -829,6 +866,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) k_lmhead(LmHeadParams P) {
         nwv[r] = i < n8 ? ldg_stream(P.norm_w + 8 * i) : make_uint4(0u, 0u, 0u, 0u);
     }
     pdl_wait();
+    PHASE(PH_LMHEAD, 1);
     {  // rmsnorm (engine.cu:131-144) into xs; block 0 also keeps the raw h
         float ss = 0.f;
         for (int i = threadIdx.x; i < n8; i += LM_WARPS * 32) {
@@ -861,6 +899,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) k_lmhead(LmHeadParams P) {
         }
         lm_sync();
     }
+    PHASE(PH_LMHEAD, 2);
     unsigned long long best = 0ull;
     for (int j = 0; j < s1 - s0; j++) {
         const int slot = j % LM_NST;
@@ -893,6 +932,7 @@ __global__ void __launch_bounds__(LM_THREADS, 1) k_lmhead(LmHeadParams P) {
         if (lane == 0) mbar_arrive(&empty[slot]);
     }
     if (lane == 0) kred[warp] = best;
+    PHASE(PH_LMHEAD, 3);
     lm_sync();
     if (threadIdx.x == 0) {
         unsigned long long b = 0ull;
@@ -913,4 +953,5 @@ __global__ void __launch_bounds__(LM_THREADS, 1) k_lmhead(LmHeadParams P) {
     if (P.out_ring) P.out_ring[pos % P.ring] = token;
     *P.pos = pos + 1;
     *P.ticket = 0u;
+    PHASE(PH_LMHEAD, 9);
 }
