@@ -670,9 +670,7 @@ static int batch_record(cuinf_batch* b, BStep& S) {
         BTRY(S.mark("rmsnorm"));
         if (c.attn_layer[l]) {
             const AttnState& A = b->attn[l];
-            float* qf = b->fqkv;
-            float* kf = qf + (size_t)B * NQ;
-            float* vf = kf + (size_t)B * NK;
+            float* qf = b->fqkv;  // q | k | v rows, converted together below
             __half* q16 = b->qkv16;
             __half* k16 = q16 + (size_t)B * NQ;
             __half* v16 = k16 + (size_t)B * NK;

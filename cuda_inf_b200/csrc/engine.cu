@@ -689,8 +689,6 @@ static int dalloc(cuinf_session* s, T** p, size_t bytes) {
     return CUINF_OK;
 }
 
-static size_t smem_norm_gemv(int H, int warps) { return (size_t)H * 4 + (warps * 16 + 32) * 4; }
-
 // Per-kernel timing of an eagerly launched step: an event after each launch
 // plus the kernel's algorithmic bytes (weights + activations it must move).
 struct Prof {

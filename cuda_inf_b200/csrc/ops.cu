@@ -120,7 +120,7 @@ extern "C" int cuinf_gemv_int4(const void* x, const uint8_t* packed, const void*
 __global__ void __launch_bounds__(256) k_gemv_fp16(const __half* __restrict__ x,
                                                    const __half* __restrict__ W,
                                                    float* __restrict__ y, int N, int K) {
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     __half* xs = reinterpret_cast<__half*>(smem);
     float* red = reinterpret_cast<float*>(smem + (size_t)K * 2);
     const int m = blockIdx.y, row0 = blockIdx.x * 16;
