@@ -36,6 +36,7 @@ sys.path.insert(0, ROOT)
 METRIC = "decode tok/s (bs1, context 4096)"
 PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM = 6650.0
+FALLBACK_TFLOPS, FALLBACK_TFLOPS_SUSTAINED = 1590.0, 1400.0
 PUBLISHED = {"value": 97.3, "unit": "tok/s", "hardware": "RTX 3060 (sm_86)",
              "source": "kb/03_status.md:21-24 (decode at 1.9k context)"}
 
@@ -46,6 +47,33 @@ def hbm_peak():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM, "fallback"
+
+
+def tensor_peak(sustained):
+    """Dense bf16 TFLOP/s: the burst figure for a kernel timed alone, the
+    sustained one (power cap) for work timed over a long run."""
+    try:
+        p = json.load(open(PEAKS))
+        return float(p["bf16_tflops_sustained" if sustained else "bf16_tflops"]), "measured"
+    except Exception:
+        return (FALLBACK_TFLOPS_SUSTAINED if sustained else FALLBACK_TFLOPS), "fallback"
+
+
+def linear_macs_per_token(cfg):
+    """Multiply-adds of one token's linear layers (projections, router and
+    the top-k experts' FFN; not attention's QK/PV or the lm_head)."""
+    H, hd = cfg.hidden, cfg.head_dim
+    macs = 0
+    for L in range(cfg.n_layers):
+        if cfg.attn_layer[L]:
+            macs += (cfg.n_heads + 2 * cfg.n_kv_heads) * hd * H + H * cfg.n_heads * hd
+        else:
+            macs += 3 * H * H + H * H
+        if L < cfg.n_dense:
+            macs += 3 * cfg.dense_inter * H
+        else:
+            macs += cfg.n_experts * H + cfg.top_k * 3 * cfg.moe_inter * H
+    return macs
 
 
 class ClockSampler:
@@ -241,11 +269,14 @@ def gemm_tc_batch(M=64, copies=24, graphs=10):
     bpc = N * K // 2 + N * (K // 128) * 2 + M * K * 2 + M * N * 4
     flops = 2 * M * N * K
     peak, kind = hbm_peak()
+    tpeak, tkind = tensor_peak(sustained=False)
     gbps = bpc / (us * 1e-6) / 1e9
+    tflops = flops / (us * 1e-6) / 1e12
     del graph
     return {"kernel": "k_tc_gemm", "shape": f"7168x2048 INT4 G=128, {M} activation rows", "us_per_call": round(us, 3),
             "bytes_per_call": bpc, "achieved": round(gbps, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(gbps / peak, 4), "peak_source": kind, "tflops": round(flops / (us * 1e-6) / 1e12, 2),
+            "frac": round(gbps / peak, 4), "peak_source": kind, "tflops": round(tflops, 2),
+            "tensor_peak_tflops": tpeak, "tensor_frac": round(tflops / tpeak, 4), "tensor_peak_source": tkind,
             "weight_copies": copies, "calls_timed": graphs * copies}
 
 
@@ -518,8 +549,13 @@ def run_prefill(a, model, cfg):
         times.append(e0.elapsed_time(e1))
     sess.close()
     ms = min(times)
+    flops = 2.0 * S * linear_macs_per_token(cfg)
+    tflops = flops / (ms / 1e3) / 1e12
+    tpeak, tkind = tensor_peak(sustained=True)
     return {"workload": f"config 5b: prefill of {S} prompt tokens, batch 1", "value": round(S / (ms / 1e3), 1),
             "unit": "tok/s", "ms": round(ms, 3), "runs": len(times), "next_token": tok,
+            "linear_tflop": round(flops / 1e12, 3), "tflops": round(tflops, 2),
+            "tensor_peak_tflops": tpeak, "tensor_frac": round(tflops / tpeak, 4), "tensor_peak_source": tkind,
             "data": "synthetic random prompt ids, random-init weights"}
 
 
@@ -574,6 +610,9 @@ def run_batched(a, ws, rank, model, cfg):
     err = Batch.error()
     kps = bt.kernels_per_step
     bt.close()  # its step graph holds NCCL calls: released before the process group
+    step_flops = 2.0 * a.batch * (linear_macs_per_token(cfg) + cfg.vocab * cfg.hidden)
+    tf_gpu = step_flops / (ms / a.batch_steps / 1e3) / 1e12 / ws
+    tpeak, tkind = tensor_peak(sustained=True)
     return {
         "workload": f"config 5: {a.batch} sequences at context {ctx}, batched decode",
         "parallelism": f"expert-parallel x{ws} ({cfg.n_experts // ws} experts per GPU, NCCL send/recv)"
@@ -584,6 +623,9 @@ def run_batched(a, ws, rank, model, cfg):
         "e2e": {"value": round(a.batch * a.batch_steps / (e2e_ms / 1e3), 1), "unit": "tok/s",
                 "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
         "gpu_launches": kps * a.batch_steps, "device_errors": err,
+        # all ranks' linear layers + lm_head per step over the step time (per GPU)
+        "tflops_per_gpu": round(tf_gpu, 2), "tensor_peak_tflops": tpeak,
+        "tensor_frac": round(tf_gpu / tpeak, 4), "tensor_peak_source": tkind,
         "kernel_breakdown_eager": {k: {"launches": v[0], "ms": round(v[1], 4), "share": round(v[1] / tot, 3)}
                                    for k, v in sorted(agg.items(), key=lambda kv: -kv[1][1])},
         "data": "synthetic FP8 caches at context 2048 (seeded), random-init weights",

@@ -81,31 +81,25 @@ def _hf_model(torch, cfg, T):
     return m
 
 
-def test_oracle_matches_hf_lfm2_moe(tmp_path):
+@pytest.fixture(scope="module")
+def models(tmp_path_factory):
+    """(config, oracle model, HF model) of the TINY test model."""
     pytest.importorskip("transformers")
     import torch
     from cuda_inf_b200 import weights
     from oracle import pyoracle as orc
 
+    d = tmp_path_factory.mktemp("hf_tiny")
     cfg = weights.make_config(**TINY)
-    weights.write_model(str(tmp_path), cfg, tiny_tensor)
-    blob = np.fromfile(tmp_path / "weights.bin", np.uint8)
-    om = orc.Model(weights.config_dict(cfg), blob, open(tmp_path / "index.bin", "rb").read())
-    m = _hf_model(torch, cfg, _dequant_tensors(weights, orc, cfg, blob))
+    weights.write_model(str(d), cfg, tiny_tensor)
+    blob = np.fromfile(d / "weights.bin", np.uint8)
+    om = orc.Model(weights.config_dict(cfg), blob, open(d / "index.bin", "rb").read())
+    return cfg, om, _hf_model(torch, cfg, _dequant_tensors(weights, orc, cfg, blob))
 
-    n_moe, k = cfg.n_layers - cfg.n_dense, cfg.top_k
-    ids = np.random.default_rng(S).integers(0, cfg.vocab, S)
-    st = om.state(S + 8)
-    olog, osc = [], np.zeros((n_moe, S, cfg.n_experts))
-    oidx = np.zeros((n_moe, S, k), np.int64)
-    for i, t in enumerate(ids):
-        _, lg, _, sc = st.forward_ex(int(t))
-        olog.append(lg)
-        for j in range(n_moe):
-            osc[j, i] = sc[j]
-            oidx[j, i] = _topk_ref(sc[j], k)
 
-    # HF with the oracle's expert choices; its own router scores are recorded
+def _hf_forced(torch, cfg, m, ids, oidx):
+    """HF logits [S, V] with the experts of oidx [n_moe, S, k]; returns them
+    and HF's own router scores {moe layer: [S, E]}."""
     hsc = {}
     for j, L in enumerate(range(cfg.n_dense, cfg.n_layers)):
         blk = m.model.layers[L].feed_forward
@@ -120,6 +114,26 @@ def test_oracle_matches_hf_lfm2_moe(tmp_path):
         blk.route_tokens_to_experts = route.__get__(blk)
     with torch.no_grad():
         hl = m(torch.from_numpy(ids)[None].long()).logits[0].numpy()
+    return hl, hsc
+
+
+def test_oracle_matches_hf_lfm2_moe(models):
+    import torch
+    cfg, om, m = models
+    n_moe, k = cfg.n_layers - cfg.n_dense, cfg.top_k
+    ids = np.random.default_rng(S).integers(0, cfg.vocab, S)
+    st = om.state(S + 8)
+    olog, osc = [], np.zeros((n_moe, S, cfg.n_experts))
+    oidx = np.zeros((n_moe, S, k), np.int64)
+    for i, t in enumerate(ids):
+        _, lg, _, sc = st.forward_ex(int(t))
+        olog.append(lg)
+        for j in range(n_moe):
+            osc[j, i] = sc[j]
+            oidx[j, i] = _topk_ref(sc[j], k)
+
+    # HF with the oracle's expert choices; its own router scores are recorded
+    hl, hsc = _hf_forced(torch, cfg, m, ids, oidx)
 
     committed_from = 63  # the token whose step commits the first FP8 group
     for i in range(S):
@@ -139,3 +153,24 @@ def test_oracle_matches_hf_lfm2_moe(tmp_path):
                 assert np.array_equal(_topk_ref(hs, k), oidx[j, i]), (j, i, gap)
                 checked += 1
     assert checked > 0.9 * n_moe * S, checked
+
+
+@pytest.mark.parametrize("n", [50, 70])
+def test_oracle_prefill_matches_hf_lfm2_moe(models, n):
+    """The oracle's batched prefill (layer_forward(S), engine.cu:784-908 and
+    attention_fused 236-308) of n prompt tokens from position 0: its
+    last-row logits against HF's on the same expert choices.  At n = 70 the
+    first 64 keys are committed to FP8 inside the prompt and the queries read
+    them from the FP8 group, as the reference does."""
+    import torch
+    cfg, om, m = models
+    n_moe, k = cfg.n_layers - cfg.n_dense, cfg.top_k
+    ids = np.random.default_rng(1000 + n).integers(0, cfg.vocab, n)
+    nxt, lg, sc = om.state(n + 8).prefill(ids)
+    oidx = np.stack([[_topk_ref(sc[i, j], k) for i in range(n)] for j in range(n_moe)]).astype(np.int64)
+    hl, _ = _hf_forced(torch, cfg, m, ids, oidx)
+    err = float(np.abs(lg - hl[-1]).max() / np.abs(hl[-1]).max())
+    assert err < (FP16_TOL if n < 64 else FP8_TOL), err
+    top2 = np.sort(hl[-1])[-2:]
+    if top2[1] - top2[0] > 2 * float(np.abs(lg - hl[-1]).max()):
+        assert nxt == int(np.argmax(hl[-1]))
