@@ -25,6 +25,10 @@ import pytest
 from enginecheck import TINY, tiny_tensor
 
 S = 80  # crosses the first FP8 commit (token 63)
+# the small test model (1 kv head, top-2 of 8) and one with the real model's
+# GQA ratio and top-4 routing (8 query / 2 kv heads, top-4 of 16 experts)
+GQA = dict(hidden=512, n_layers=4, n_heads=8, n_kv_heads=2, vocab=600, n_dense=1, n_experts=16,
+           top_k=4, moe_inter=256, dense_inter=512, attn_layers=(1, 3))
 FP16_TOL = 1e-2
 FP8_TOL = 6e-2
 
@@ -81,16 +85,16 @@ def _hf_model(torch, cfg, T):
     return m
 
 
-@pytest.fixture(scope="module")
-def models(tmp_path_factory):
-    """(config, oracle model, HF model) of the TINY test model."""
+@pytest.fixture(scope="module", params=["tiny", "gqa4_top4"])
+def models(request, tmp_path_factory):
+    """(config, oracle model, HF model) of a small test model."""
     pytest.importorskip("transformers")
     import torch
     from cuda_inf_b200 import weights
     from oracle import pyoracle as orc
 
-    d = tmp_path_factory.mktemp("hf_tiny")
-    cfg = weights.make_config(**TINY)
+    d = tmp_path_factory.mktemp("hf_" + request.param)
+    cfg = weights.make_config(**(TINY if request.param == "tiny" else GQA))
     weights.write_model(str(d), cfg, tiny_tensor)
     blob = np.fromfile(d / "weights.bin", np.uint8)
     om = orc.Model(weights.config_dict(cfg), blob, open(d / "index.bin", "rb").read())
@@ -152,7 +156,7 @@ def test_oracle_matches_hf_lfm2_moe(models):
             if gap > 2 * float(np.abs(hs - osc[j, i]).max()):
                 assert np.array_equal(_topk_ref(hs, k), oidx[j, i]), (j, i, gap)
                 checked += 1
-    assert checked > 0.9 * n_moe * S, checked
+    assert checked > 0.75 * n_moe * S, checked  # the check is not vacuous (top-4 of 16: ~90 % clear)
 
 
 @pytest.mark.parametrize("n", [50, 70])
