@@ -7,13 +7,22 @@ greedy decode at context 4096: a 64-token random prompt is fed, the model
 decodes until position 4096, then W warm-up and K timed steps follow.  One
 step = one token through all layers + lm_head + argmax.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W]
+                  [--impl ours|reference|reference-engine]
 
 Under torchrun each rank decodes its own independent sequence on its GPU
 (bs1 decode does not shard: replicas, weak scaling); value = total tokens/s
-over the max per-rank time.  The reference arm runs the reference engine
-(src/engine.cu of g023/cuda_inf, unmodified, rebuilt for sm_100a in
-oracle/_ref) on the same weights, rank 0 only.
+over the max per-rank time.  The same line carries config 5 (batched,
+expert-parallel decode over the ranks), 5b (prefill), 1-3 (kernel
+measurements) and a compact `summary` as its last key.
+
+--impl reference: the reference has no CPU implementation of this path (all
+of src/engine.cu's math is CUDA), so its arm is the CPU restatement of the
+same decode step (oracle.c built as the fp32 baseline, -O3, all host threads)
+at context 4096 on weights synthesized without this library; rank 0 only.
+Its line also reports the reference's own CUDA engine (src/engine.cu rebuilt
+unmodified for sm_100a) on the same GPU as `reference_engine_gpu`.
+--impl reference-engine: only that GPU engine run.
 """
 import argparse
 import json
@@ -384,27 +393,54 @@ def attn_config3(ctxs=(2048, 8192, 32768)):
             "peak": peak, "unit": "GB/s", "peak_source": kind, "by_context": out}
 
 
-def cpu_baseline(cfg, blob, idx, budget_s=20.0):
-    """The CPU oracle (scalar C restatement, OpenMP over output rows) decoding
-    the same model on this host: a bounded sample of the first positions."""
+def _baseline_oracle():
+    """pyoracle bound to the timed CPU baseline build of oracle.c (fp32
+    accumulation, -O3, this host's ISA)."""
+    import oracle
     from oracle import pyoracle as orc
-    host = blob.cpu().numpy()
-    from cuda_inf_b200 import weights as W
-    om = orc.Model(W.config_dict(cfg), host, idx)
-    st = om.state(64)
-    toks = prompt_ids(1, 64, cfg.vocab)
+    orc.use_library(oracle.baseline_library())
+    return orc
+
+
+def _time_cpu_steps(orc, om, snap, threads, warm, max_steps, budget_s, seed):
+    """Decode steps of the CPU baseline from a state snapshot: `warm` untimed,
+    then up to max_steps timed ones, stopped once budget_s is spent.
+    Returns (steps, seconds)."""
+    orc.set_threads(threads)
+    st = om.state(4096 + 64 + warm + max_steps)
+    st.load_state(snap)
+    toks = np.random.default_rng(seed).integers(0, om.cfg.vocab, warm + max_steps)
+    for i in range(warm):
+        st.forward(int(toks[i]), want_logits=False)
     t0 = time.perf_counter()
     n = 0
-    while n < len(toks):
-        st.forward(toks[n], want_logits=False)
+    while n < max_steps:
+        st.forward(int(toks[warm + n]), want_logits=False)
         n += 1
         if time.perf_counter() - t0 > budget_s:
             break
-    dt = time.perf_counter() - t0
-    return {"value": n / dt, "unit": "tok/s", "cores": orc.get_threads(), "kind": "port",
-            "sample": f"{n} decode steps at positions 0..{n - 1} of the same model "
-                      f"(oracle/oracle.c, OpenMP, {dt:.1f} s; at context 4096 the KV cache adds "
-                      f"~2% more bytes per step)"}
+    return n, time.perf_counter() - t0
+
+
+def cpu_baseline(cfg, host_blob, idx, ctx, budget_s=20.0):
+    """The CPU baseline (oracle.c restatement of the decode step, fp32, -O3,
+    OpenMP over output rows and heads) on this host, from a state snapshot at
+    context ctx - 6: single-threaded and on all host threads, each over a
+    bounded sample of the same workload."""
+    from cuda_inf_b200 import weights as W
+    from oracle.snapshot import random_snapshot
+    orc = _baseline_oracle()
+    om = orc.Model(W.config_dict(cfg), host_blob, idx)
+    snap = random_snapshot(cfg, ctx - 6, seed=ctx)
+    threads = len(os.sched_getaffinity(0))
+    n1, t1 = _time_cpu_steps(orc, om, snap, 1, 1, 64, budget_s * 0.4, 3)
+    nN, tN = _time_cpu_steps(orc, om, snap, threads, 1, 256, budget_s * 0.6, 4)
+    return {"value": round(nN / tN, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+            "single_thread": {"value": round(n1 / t1, 3), "unit": "tok/s", "cores": 1, "steps": n1,
+                              "seconds": round(t1, 2)},
+            "sample": f"{nN} decode steps from position {ctx - 5} on {threads} threads ({tN:.1f} s) and {n1} "
+                      f"on 1 thread ({t1:.1f} s): oracle.c built as the fp32 baseline (-O3, native ISA, "
+                      f"OpenMP), from a random KV/conv state snapshot at position {ctx - 6}"}
 
 
 def run_ours(a, ws, rank):
@@ -514,7 +550,7 @@ def run_ours(a, ws, rank):
         "setup_s": round(t_synth, 1),
     }
     if rank == 0 and ws == 1 and not a.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(cfg, blob, idx, a.cpu_budget)
+        out["cpu_baseline"] = cpu_baseline(cfg, blob.cpu().numpy(), idx, a.ctx, a.cpu_budget)
     sess.close()
     if a.batch > 0 and not a.profile_small:
         out["batched_ep"] = run_batched(a, ws, rank, model, cfg)
@@ -634,43 +670,67 @@ def run_batched(a, ws, rank, model, cfg):
     }
 
 
+def synth_host_blob(cfg, seed):
+    """The seeded random-init model of weights.synth_device_blob without this
+    library: the same torch generator draws (on the GPU when there is one),
+    quantized on the host by oracle.c's restatement of the exporter's
+    quantizer (tools/export_weights.py:64-79), so the reference arm never
+    loads libcuinf.  Returns (host uint8 blob, index bytes)."""
+    import concurrent.futures as cf
+    from cuda_inf_b200 import weights as W
+    from oracle import pyoracle as orc
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    ents = W.layout(cfg)
+    blob = np.empty(ents[-1].offset + ents[-1].nbytes, np.uint8)
+
+    def quant(e, w):
+        p, sc = orc.quant_int4_group(w)
+        blob[e.offset:e.offset + e.packed] = p.reshape(-1)
+        blob[e.offset + e.packed:e.offset + e.nbytes] = sc.view(np.uint8).reshape(-1)
+
+    with cf.ThreadPoolExecutor(len(os.sched_getaffinity(0))) as ex:
+        futs = []
+        for e in ents:
+            w = W.synth_tensor_torch(e.name, e.shape, seed, dev).cpu().numpy()
+            if e.kind == W.FP16:
+                blob[e.offset:e.offset + e.nbytes] = w.reshape(-1).astype(np.float16).view(np.uint8)
+            else:
+                futs.append(ex.submit(quant, e, w))
+        for f in futs:
+            f.result()
+    return blob, W.index_bytes(ents)
+
+
 def run_reference(a, ws, rank):
     """Reference arm: the reference has no CPU implementation of this path
     (all of src/engine.cu's math is CUDA), so it is the CPU restatement of
-    the same decode (oracle/oracle.c, OpenMP over all host threads) on the
-    same seeded model and prompt: W untimed steps, then up to K timed steps,
-    stopped early once about REF_BUDGET_S seconds are spent."""
-    from oracle import pyoracle as orc
+    the same decode step (oracle.c built as the fp32 baseline) on all host
+    threads, at context 4096 (from a random KV/conv snapshot at a.ctx - 6),
+    on the same seeded model synthesized without this library: W untimed
+    steps, then up to K timed steps, stopped early after about REF_BUDGET_S
+    seconds.  Then the reference's own CUDA engine on the same weights."""
     from cuda_inf_b200 import weights as W
-    cfg = W.default_config()
-    blob, idx = W.synth_device_blob(cfg, seed=a.seed)
-    host = blob.cpu().numpy()
-    del blob
-    torch.cuda.empty_cache()
+    from oracle.snapshot import random_snapshot
+    cfg = W.make_config()  # the default LFM2.5-8B-A1B shape (no library call)
+    orc = _baseline_oracle()
+    t0 = time.time()
+    host, idx = synth_host_blob(cfg, a.seed)
+    t_synth = time.time() - t0
     threads = len(os.sched_getaffinity(0))
-    orc.set_threads(threads)
     om = orc.Model(W.config_dict(cfg), host, idx)
-    st = om.state(a.warmup + a.steps + 8)
-    toks = prompt_ids(a.seed, a.warmup + a.steps, cfg.vocab, rank)
-    for i in range(a.warmup):
-        st.forward(int(toks[i]), want_logits=False)
-    t0 = time.perf_counter()
-    n = 0
-    while n < a.steps:
-        st.forward(int(toks[a.warmup + n]), want_logits=False)
-        n += 1
-        if time.perf_counter() - t0 > REF_BUDGET_S:
-            break
-    dt = time.perf_counter() - t0
+    snap = random_snapshot(cfg, a.ctx - 6, seed=a.ctx)
+    n, dt = _time_cpu_steps(orc, om, snap, threads, min(a.warmup, 3), a.steps, REF_BUDGET_S, a.seed)
     tps = n / dt
-    sample = (f"{n} decode steps at positions {a.warmup}..{a.warmup + n - 1} after {a.warmup} untimed "
-              f"(oracle/oracle.c, OpenMP, {threads} threads, {dt:.1f} s; at context 4096 the KV cache "
-              f"adds ~2% more bytes per step)")
-    return {
+    sample = (f"{n} decode steps from position {a.ctx - 6 + min(a.warmup, 3)} after {min(a.warmup, 3)} untimed "
+              f"(oracle.c fp32 baseline, -O3 native ISA, OpenMP, {threads} threads, {dt:.1f} s), from a random "
+              f"KV/conv state snapshot at position {a.ctx - 6}")
+    del om
+    out = {
         "metric": METRIC, "value": round(tps, 3), "unit": "tok/s", "n_gpus": ws, "steps": n,
         "warmup": a.warmup, "ms_per_step": round(dt / n * 1e3, 2), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int4xfp16->fp32",
-        "data": "synthetic (same seeded weights and prompt as the ours arm)", "impl": "reference",
+        "data": "synthetic (the ours arm's seeded weights, synthesized and quantized on the host)",
+        "impl": "reference",
         "config": {"workload": "config 4: full 24-layer decode, batch 1, context 4096",
                    "model": "LFM2.5-8B-A1B-shaped random init (INT4 G=128, fp16 tied lm_head)",
                    "global_batch": 1, "seq_len": a.ctx, "prompt_len": a.prompt_len,
@@ -678,24 +738,41 @@ def run_reference(a, ws, rank):
         "cpu_baseline": {"kind": "port", "value": round(tps, 3), "unit": "tok/s", "cores": threads,
                          "sample": sample},
         "e2e": {"value": round(tps, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "setup_s": round(t_synth, 1),
     }
+    if not a.no_reference_engine:
+        try:
+            eng = run_reference_engine(a, ws, rank, host=(host, idx))
+            out["reference_engine_gpu"] = {k: eng.get(k) for k in ("value", "unit", "ms_per_step", "steps",
+                                                                   "unavailable", "clocks")
+                                           if k in eng}
+            if "config" in eng:
+                out["reference_engine_gpu"]["timed"] = eng["config"]["timed"]
+        except Exception as e:  # the GPU side run never takes the CPU arm's line down
+            out["reference_engine_gpu"] = {"unavailable": str(e)[:300]}
+    return out
 
 
-def run_reference_engine(a, ws, rank):
+def run_reference_engine(a, ws, rank, host=None):
     """The reference's own engine (src/engine.cu, built unmodified for sm_100a
     into oracle/_ref/ref_engine) on the GPU, same weights and prompt, timed by
-    its own decode-loop clock: the GPU-to-GPU comparison."""
+    its own decode-loop clock: the GPU-to-GPU comparison.  host = (blob,
+    index) of run_reference's host-synthesized model, else synthesized here."""
     eng = os.path.join(ROOT, "oracle", "_ref", "ref_engine")
     if not os.path.exists(eng):
         return {"impl": "reference-engine", "unavailable": "oracle/_ref/ref_engine not built (reference tree absent at build time)"}
     from cuda_inf_b200 import weights as W
-    cfg = W.default_config()
-    blob, idx = W.synth_device_blob(cfg, seed=a.seed)
+    cfg = W.make_config()
+    if host is None:
+        _baseline_oracle()
+        host = synth_host_blob(cfg, a.seed)
+    blob, idx = host
     base = "/dev/shm" if shutil.disk_usage("/dev/shm").free > 6e9 else None
     with tempfile.TemporaryDirectory(dir=base) as d:
-        W.save_blob(blob, idx, d)
-        del blob
-        torch.cuda.empty_cache()
+        with open(os.path.join(d, "weights.bin"), "wb") as f:
+            f.write(memoryview(blob))
+        with open(os.path.join(d, "index.bin"), "wb") as f:
+            f.write(idx)
         ids = np.array(prompt_ids(a.seed, a.prompt_len, cfg.vocab, rank), np.int32)
         ids.tofile(os.path.join(d, "ids.i32"))
         os.makedirs(os.path.join(d, "scratch"), exist_ok=True)
@@ -792,6 +869,34 @@ def phase_trace(a):
             "context": int(sess.pos), "note": "latest launch of each kernel in the last step"}
 
 
+def summary(out):
+    """The headline figures of every configuration in one short object, put
+    last on the line (a record that keeps only the line's tail still shows
+    them)."""
+    def g(*path):
+        d = out
+        for k in path:
+            if not isinstance(d, dict) or k not in d:
+                return None
+            d = d[k]
+        return d
+    return {
+        "bs1_tok_s": g("value"), "bs1_e2e_tok_s": g("e2e", "value"), "bs1_ms_per_step": g("ms_per_step"),
+        "bs1_step_frac": g("roofline_step", "frac"), "top_kernel": g("roofline", "kernel"),
+        "top_kernel_frac": g("roofline", "frac"),
+        "batched_tok_s": g("batched_ep", "value"), "batched_e2e_tok_s": g("batched_ep", "e2e", "value"),
+        "batched_ms_per_step": g("batched_ep", "ms_per_step"), "batched_parallelism": g("batched_ep", "parallelism"),
+        "batched_clocks_mhz": g("batched_ep", "clocks", "sm_mhz"),
+        "prefill_tok_s": g("prefill_config5b", "value"), "prefill_tensor_frac": g("prefill_config5b", "tensor_frac"),
+        "gemv_int4_frac": g("gemv_int4_config1", "frac"), "tc_gemm_frac": g("gemm_int4_tc_batch64", "frac"),
+        "moe_ffn_frac": g("moe_ffn_config2", "frac"),
+        "attn_frac_2k_8k_32k": [g("attention_config3", "by_context", c, "frac") for c in ("2048", "8192", "32768")],
+        "cpu_baseline_tok_s": g("cpu_baseline", "value"),
+        "cpu_baseline_1thread_tok_s": g("cpu_baseline", "single_thread", "value"),
+        "clocks_mhz": g("clocks", "sm_mhz"), "clock_reasons": g("clocks", "reasons"),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -805,6 +910,8 @@ def main():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--no-reference-engine", action="store_true",
+                    help="reference arm: skip the reference's CUDA engine run")
     ap.add_argument("--gemv-only", action="store_true",
                     help="only the config-1 INT4 GEMV measurement (for profiler captures)")
     ap.add_argument("--kernels-only", action="store_true",
@@ -870,6 +977,8 @@ def main():
     if a.profile_small:
         out = {"profiling_only": True, "ms_per_step": out["ms_per_step"],
                "kernel_breakdown": out["kernel_breakdown"]}
+    else:
+        out["summary"] = summary(out)
     if rank == 0:
         print(json.dumps(out), flush=True)
     if ws > 1:

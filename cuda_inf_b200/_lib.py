@@ -79,6 +79,9 @@ _SIGS = {
     "cuinf_session_free": (c_int, [c_void_p]),
     "cuinf_session_reset": (c_int, [c_void_p]),
     "cuinf_session_pos": (c_int, [c_void_p]),
+    "cuinf_session_state_bytes": (c_size_t, [c_void_p]),
+    "cuinf_session_save_state": (c_int, [c_void_p, c_void_p, c_size_t]),
+    "cuinf_session_load_state": (c_int, [c_void_p, c_void_p, c_size_t]),
     "cuinf_decode_step": (c_int, [c_void_p, c_int, ctypes.POINTER(c_int)]),
     "cuinf_generate": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
                                ctypes.POINTER(c_int)]),
@@ -102,6 +105,9 @@ _SIGS = {
     "cuinf_batch_routes": (c_int, [c_void_p, c_void_p]),
     "cuinf_batch_kernels_per_step": (c_int, [c_void_p]),
     "cuinf_batch_fill_synthetic": (c_int, [c_void_p, c_int, ctypes.c_ulonglong]),
+    "cuinf_batch_seq_state_bytes": (c_size_t, [c_void_p, c_int]),
+    "cuinf_batch_save_seq": (c_int, [c_void_p, c_int, c_void_p, c_size_t]),
+    "cuinf_batch_load_seq": (c_int, [c_void_p, c_int, c_void_p, c_size_t]),
     "cuinf_batch_error": (c_int, [c_void_p]),
     "cuinf_batch_profile_step": (c_int, [c_void_p, c_int, c_void_p, ctypes.c_char_p, c_int, c_void_p]),
     "cuinf_batch_create_ep": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),

@@ -1257,6 +1257,63 @@ extern "C" int cuinf_batch_fill_synthetic(cuinf_batch* b, int ctx, unsigned long
     return CUINF_OK;
 }
 
+// Sequence `seq`'s own slices of the batch's stacked caches and conv states.
+static void batch_seq_views(const cuinf_batch* b, int seq, std::vector<AttnState>& A, std::vector<__half*>& C) {
+    const cuinf_config& c = b->m->cfg;
+    A.assign(c.n_layers, AttnState());
+    C.assign(c.n_layers, nullptr);
+    for (int l = 0; l < c.n_layers; l++) {
+        if (c.attn_layer[l]) {
+            const AttnState& S = b->attn[l];
+            A[l].kc8 = S.kc8 + seq * b->kv8_seq;
+            A[l].vc8 = S.vc8 + seq * b->kv8_seq;
+            A[l].ksc = S.ksc + seq * b->sc_seq;
+            A[l].vsc = S.vsc + seq * b->sc_seq;
+            A[l].ktail = S.ktail + seq * b->tail_seq;
+            A[l].vtail = S.vtail + seq * b->tail_seq;
+        } else {
+            C[l] = b->conv_state[l] + (size_t)seq * 2 * c.hidden;
+        }
+    }
+}
+
+extern "C" size_t cuinf_batch_seq_state_bytes(cuinf_batch* b, int seq) {
+    if (!b || seq < 0 || seq >= b->B) return 0;
+    int pos = 0;
+    if (cudaStreamSynchronize(b->st) != cudaSuccess ||
+        cudaMemcpy(&pos, b->pos + seq, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return 0;
+    return seq_state_bytes(b->m->cfg, pos);
+}
+
+extern "C" int cuinf_batch_save_seq(cuinf_batch* b, int seq, void* host, size_t n) {
+    REQUIRE(b && host, "null pointer");
+    REQUIRE(seq >= 0 && seq < b->B, "sequence index out of range");
+    int pos = 0;
+    CUINF_TRY(cudaStreamSynchronize(b->st));
+    CUINF_TRY(cudaMemcpy(&pos, b->pos + seq, 4, cudaMemcpyDeviceToHost));
+    std::vector<AttnState> A;
+    std::vector<__half*> C;
+    batch_seq_views(b, seq, A, C);
+    return seq_state_copy(b->m->cfg, pos, A.data(), C.data(), host, n, true, b->st);
+}
+
+extern "C" int cuinf_batch_load_seq(cuinf_batch* b, int seq, const void* host, size_t n) {
+    REQUIRE(b && host, "null pointer");
+    REQUIRE(seq >= 0 && seq < b->B, "sequence index out of range");
+    int pos = 0;
+    int rc = seq_state_header(b->m->cfg, host, n, b->max_ctx, &pos);
+    if (rc) return rc;
+    CUINF_TRY(cudaStreamSynchronize(b->st));
+    std::vector<AttnState> A;
+    std::vector<__half*> C;
+    batch_seq_views(b, seq, A, C);
+    rc = seq_state_copy(b->m->cfg, pos, A.data(), C.data(), const_cast<void*>(host), n, false, b->st);
+    if (rc) return rc;
+    CUINF_TRY(cudaMemcpy(b->pos + seq, &pos, 4, cudaMemcpyHostToDevice));
+    return CUINF_OK;
+}
+
 // One step launched eagerly with an event after every launch: ms[i] is the
 // duration of launch i (names[i * name_len] its name).  Advances the batch
 // like cuinf_batch_step(b, NULL, NULL).

@@ -1280,6 +1280,105 @@ extern "C" int cuinf_session_reset(cuinf_session* s) {
 
 extern "C" int cuinf_session_pos(const cuinf_session* s) { return s ? s->host_pos : -1; }
 
+// ---------------------------------------------------------------------------
+// sequence state snapshots (KV cache + conv state at a position)
+// ---------------------------------------------------------------------------
+static const uint32_t kStateMagic = 0x54534943u;  // "CIST"
+static const uint32_t kStateVersion = 1;
+struct StateHeader {
+    uint32_t magic, version;
+    int32_t pos, n_layers, hidden, n_kv_heads, reserved[2];
+};
+
+size_t seq_state_bytes(const cuinf_config& c, int pos) {
+    const size_t row = (size_t)c.n_kv_heads * CUINF_HD;
+    const size_t C = (size_t)(pos / CUINF_KVGROUP) * CUINF_KVGROUP;
+    size_t n = sizeof(StateHeader);
+    for (int l = 0; l < c.n_layers; l++) {
+        if (c.attn_layer[l])
+            n += 2 * C * row + 2 * (C / CUINF_KVGROUP) * c.n_kv_heads * 2 + 2 * (size_t)CUINF_KVGROUP * row * 2;
+        else
+            n += (size_t)2 * c.hidden * 2;
+    }
+    return n;
+}
+
+int seq_state_header(const cuinf_config& c, const void* host, size_t n, int max_ctx, int* pos) {
+    REQUIRE(host && n >= sizeof(StateHeader), "state snapshot too short");
+    StateHeader hd;
+    memcpy(&hd, host, sizeof(hd));
+    REQUIRE(hd.magic == kStateMagic && hd.version == kStateVersion, "not a cuinf state snapshot (v1)");
+    REQUIRE(hd.n_layers == c.n_layers && hd.hidden == c.hidden && hd.n_kv_heads == c.n_kv_heads,
+            "state snapshot of another model shape");
+    REQUIRE(hd.pos >= 0 && hd.pos < max_ctx, "state snapshot position beyond max_ctx");
+    REQUIRE(n == seq_state_bytes(c, hd.pos), "state snapshot size does not match its position");
+    *pos = hd.pos;
+    return CUINF_OK;
+}
+
+int seq_state_copy(const cuinf_config& c, int pos, const AttnState* attn, __half* const* conv, void* host,
+                   size_t n, bool save, cudaStream_t st) {
+    REQUIRE(n == seq_state_bytes(c, pos), "state buffer size does not match the position");
+    const size_t row = (size_t)c.n_kv_heads * CUINF_HD;
+    const size_t C = (size_t)(pos / CUINF_KVGROUP) * CUINF_KVGROUP;
+    uint8_t* p = (uint8_t*)host;
+    if (save) {
+        StateHeader hd = {kStateMagic, kStateVersion, pos, c.n_layers, c.hidden, c.n_kv_heads, {0, 0}};
+        memcpy(p, &hd, sizeof(hd));
+    }
+    p += sizeof(StateHeader);
+    auto piece = [&](void* dev, size_t bytes) -> cudaError_t {
+        cudaError_t e = bytes == 0 ? cudaSuccess
+                        : save     ? cudaMemcpyAsync(p, dev, bytes, cudaMemcpyDeviceToHost, st)
+                                   : cudaMemcpyAsync(dev, p, bytes, cudaMemcpyHostToDevice, st);
+        p += bytes;
+        return e;
+    };
+    for (int l = 0; l < c.n_layers; l++) {
+        if (c.attn_layer[l]) {
+            const AttnState& A = attn[l];
+            const size_t sc = (C / CUINF_KVGROUP) * c.n_kv_heads * 2, tail = (size_t)CUINF_KVGROUP * row * 2;
+            CUINF_TRY(piece(A.kc8, C * row));
+            CUINF_TRY(piece(A.vc8, C * row));
+            CUINF_TRY(piece(A.ksc, sc));
+            CUINF_TRY(piece(A.vsc, sc));
+            CUINF_TRY(piece(A.ktail, tail));
+            CUINF_TRY(piece(A.vtail, tail));
+        } else {
+            CUINF_TRY(piece(conv[l], (size_t)2 * c.hidden * 2));
+        }
+    }
+    CUINF_TRY(cudaStreamSynchronize(st));
+    return CUINF_OK;
+}
+
+extern "C" size_t cuinf_session_state_bytes(const cuinf_session* s) {
+    return s ? seq_state_bytes(s->m->cfg, s->host_pos) : 0;
+}
+
+extern "C" int cuinf_session_save_state(cuinf_session* s, void* host, size_t n) {
+    REQUIRE(s && host, "null pointer");
+    REQUIRE(!s->h2o_C, "state snapshots are not available in H2O eviction mode");
+    CUINF_TRY(cudaStreamSynchronize(s->st));
+    return seq_state_copy(s->m->cfg, s->host_pos, s->attn.data(), s->conv_state.data(), host, n, true, s->st);
+}
+
+extern "C" int cuinf_session_load_state(cuinf_session* s, const void* host, size_t n) {
+    REQUIRE(s && host, "null pointer");
+    REQUIRE(!s->h2o_C, "state snapshots are not available in H2O eviction mode");
+    int pos = 0;
+    int rc = seq_state_header(s->m->cfg, host, n, s->max_ctx, &pos);
+    if (rc) return rc;
+    CUINF_TRY(cudaStreamSynchronize(s->st));
+    rc = seq_state_copy(s->m->cfg, pos, s->attn.data(), s->conv_state.data(), const_cast<void*>(host), n,
+                        false, s->st);
+    if (rc) return rc;
+    CUINF_TRY(cudaMemcpy(s->pos, &pos, 4, cudaMemcpyHostToDevice));
+    if (s->mk_words) CUINF_TRY(cudaMemset(s->mk_words, 0, 64));
+    s->host_pos = pos;
+    return CUINF_OK;
+}
+
 extern "C" int cuinf_decode_step(cuinf_session* s, int token, int* out_token) {
     REQUIRE(s && s->exec, "null session");
     REQUIRE(s->host_pos < s->max_ctx, "context full (max_ctx reached)");

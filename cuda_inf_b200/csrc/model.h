@@ -54,6 +54,17 @@ struct AttnState {
     __half *ksc = nullptr, *vsc = nullptr, *ktail = nullptr, *vtail = nullptr;
 };
 
+
+// One sequence's recurrent state in the snapshot layout of
+// cuinf_session_save_state (include/cuinf.h): copies between a host buffer
+// and the device pieces (attn[l] / conv[l], per layer; null where the layer
+// has no such piece) on `st`, synchronously.  save: device -> host.
+size_t seq_state_bytes(const cuinf_config& c, int pos);
+int seq_state_copy(const cuinf_config& c, int pos, const AttnState* attn, __half* const* conv, void* host,
+                   size_t n, bool save, cudaStream_t st);
+// Reads and checks a snapshot's header; returns its position through *pos.
+int seq_state_header(const cuinf_config& c, const void* host, size_t n, int max_ctx, int* pos);
+
 // Decode attention over B sequences (grid z), each at its own device
 // position: q [B][nh*64], caches at the given per-sequence element strides,
 // partials [B][part_floats], counters [B][nkv] (zero, left zero).

@@ -83,6 +83,22 @@ class Session:
     def reset(self):
         check(lib().cuinf_session_reset(self._h))
 
+    def save_state(self):
+        """Snapshot of the KV cache and conv state at the current position
+        (bytes, the layout of cuinf_session_save_state)."""
+        import numpy as np
+        n = lib().cuinf_session_state_bytes(self._h)
+        buf = np.empty(n, np.uint8)
+        check(lib().cuinf_session_save_state(self._h, buf.ctypes.data, n))
+        return buf.tobytes()
+
+    def load_state(self, snap):
+        """Resume from a snapshot: the session moves to its position; the
+        next step() must pass a token."""
+        import numpy as np
+        buf = np.frombuffer(snap, np.uint8)
+        check(lib().cuinf_session_load_state(self._h, buf.ctypes.data, buf.size))
+
     def step(self, token=-1, want=True):
         """One decode step; token < 0 feeds back the previous argmax on the
         device.  Returns the argmax (synchronizes) when want is true."""
@@ -268,6 +284,22 @@ class Batch:
 
     def fill_synthetic(self, ctx, seed=1):
         check(lib().cuinf_batch_fill_synthetic(self._h, int(ctx), int(seed)))
+
+    def save_seq(self, seq):
+        """State snapshot of sequence seq (the session snapshot layout)."""
+        import numpy as np
+        n = lib().cuinf_batch_seq_state_bytes(self._h, int(seq))
+        if n == 0:
+            raise ValueError("bad sequence index or device error")
+        buf = np.empty(n, np.uint8)
+        check(lib().cuinf_batch_save_seq(self._h, int(seq), buf.ctypes.data, n))
+        return buf.tobytes()
+
+    def load_seq(self, seq, snap):
+        """Put sequence seq at a snapshot's state and position."""
+        import numpy as np
+        buf = np.frombuffer(snap, np.uint8)
+        check(lib().cuinf_batch_load_seq(self._h, int(seq), buf.ctypes.data, buf.size))
 
     @property
     def kernels_per_step(self):

@@ -196,6 +196,28 @@ int cuinf_session_free(cuinf_session* s);
 int cuinf_session_reset(cuinf_session* s);
 int cuinf_session_pos(const cuinf_session* s);
 
+/* Snapshots of a sequence's recurrent state at its position p: the FP8 KV
+ * cache of every attention layer (C = 64*floor(p/64) committed tokens, their
+ * group scales, the fp16 tails) and the conv state of every short-conv layer.
+ * The reference keeps this state only in device buffers for the life of the
+ * process (Buffers, engine.cu:590-623); a snapshot lets a caller park a
+ * sequence on the host and resume it later (or start a session at a long
+ * context from a stored prompt state).  Layout (little-endian):
+ *   u32 magic 0x54534943, u32 version 1, i32 pos, i32 n_layers, i32 hidden,
+ *   i32 n_kv_heads, i32 reserved[2]; then per layer in order:
+ *   attention: kc8 u8 [C][nkv][64], vc8 same, ksc fp16 [C/64][nkv], vsc same,
+ *              ktail fp16 [64][nkv][64] (slots 0..p-C-1 hold tokens C..p-1),
+ *              vtail same;
+ *   short-conv: state fp16 [2][hidden].
+ * cuinf_session_state_bytes gives the size at the session's position.  save
+ * copies device -> host; load checks the header against the model, copies
+ * host -> device and moves the session to the snapshot's position (the next
+ * cuinf_decode_step must pass its token explicitly).  Both synchronize the
+ * session's stream.  Not available in H2O eviction mode. */
+size_t cuinf_session_state_bytes(const cuinf_session* s);
+int cuinf_session_save_state(cuinf_session* s, void* host, size_t n);
+int cuinf_session_load_state(cuinf_session* s, const void* host, size_t n);
+
 /* One token through all layers + final norm + lm_head + argmax, at the
  * session's position (then position + 1).  token >= 0 is the input token
  * (copied host->device); token < 0 feeds back the previous step's argmax,
@@ -254,6 +276,14 @@ const float* cuinf_batch_logits(const cuinf_batch* b);
 int cuinf_batch_routes(cuinf_batch* b, int* idx);
 int cuinf_batch_kernels_per_step(const cuinf_batch* b);
 int cuinf_batch_fill_synthetic(cuinf_batch* b, int ctx, unsigned long long seed);
+/* Per-sequence state snapshots of a batch, in the layout of
+ * cuinf_session_save_state (a snapshot moves freely between sessions and
+ * batches of the same model): the size at sequence seq's position, save
+ * (device -> host) and load (host -> device, which also sets that sequence's
+ * position; its next token must be passed explicitly).  Synchronous. */
+size_t cuinf_batch_seq_state_bytes(cuinf_batch* b, int seq);
+int cuinf_batch_save_seq(cuinf_batch* b, int seq, void* host, size_t n);
+int cuinf_batch_load_seq(cuinf_batch* b, int seq, const void* host, size_t n);
 /* Error words of the tensor-core kernels, flags[4]: [0] bit 1 a bounded
  * pipeline wait timed out, bit 2 a final drain did, bit 3 a group had more
  * rows than its launch allowed (skipped); [1] the wait's barrier

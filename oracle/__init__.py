@@ -13,14 +13,34 @@ import os
 import subprocess
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_TREE = os.environ.get("CUINF_REFERENCE", "/root/reference")
+
+
+def reference_tree():
+    """The g023/cuda_inf source tree: $CUINF_REFERENCE, else a checkout named
+    `reference` beside this repository; None when neither exists."""
+    cand = os.environ.get("CUINF_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isdir(os.path.join(cand, "src")) else None
 
 
 def build(with_ref=None):
-    """Build liboracle.so, and _ref/ when the reference tree is present."""
-    subprocess.run(["make", "-C", HERE, "liboracle.so"], check=True, capture_output=True)
+    """Build liboracle.so and libcpubase.so, and _ref/ when the reference
+    tree is found (reference_tree())."""
+    subprocess.run(["make", "-C", HERE, "liboracle.so", "libcpubase.so"], check=True, capture_output=True)
+    ref = reference_tree()
     if with_ref is None:
-        with_ref = os.path.isdir(os.path.join(REF_TREE, "src"))
+        with_ref = ref is not None
     if with_ref:
-        subprocess.run(["make", "-C", HERE, "ref", f"REF={REF_TREE}"], check=True,
-                       capture_output=True)
+        if ref is None:
+            raise RuntimeError("reference tree not found: set CUINF_REFERENCE")
+        subprocess.run(["make", "-C", HERE, "ref", f"REF={ref}"], check=True, capture_output=True)
+
+
+def baseline_library():
+    """Path of the timed CPU baseline (oracle.c built with -DORC_BASELINE):
+    built for this host's own ISA (-march=native) when gcc is at hand, else
+    the prebuilt portable x86-64-v3 library."""
+    native = os.path.join(HERE, "_native", "libcpubase.so")
+    r = subprocess.run(["make", "-B", "-C", HERE, "native"], capture_output=True)
+    if r.returncode == 0 and os.path.exists(native):
+        return native
+    return os.path.join(HERE, "libcpubase.so")

@@ -14,6 +14,20 @@
  */
 #include "oracle.h"
 
+/* ORC_BASELINE builds the same restatement as the timed CPU baseline
+ * (oracle/Makefile libcpubase.so: -O3, native ISA, FMA contraction allowed):
+ * dot products and softmax sums accumulate in fp32 (eight partial sums per
+ * dot product, which the compiler vectorizes), exp in float.  The checker
+ * build (liboracle.so) keeps double accumulation and a fixed summation
+ * order. */
+#ifdef ORC_BASELINE
+typedef float orc_acc;
+#define ORC_EXP expf
+#else
+typedef double orc_acc;
+#define ORC_EXP exp
+#endif
+
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -46,6 +60,12 @@ float orc_e4m3_to_f32(uint8_t b) {
     if (e == 0) v = ldexpf((float)m, -9);
     else        v = ldexpf(1.0f + (float)m / 8.0f, e - 7);
     return s ? -v : v;
+}
+
+/* All 256 E4M3 codes decoded once (the same values as orc_e4m3_to_f32). */
+static float g_e4m3[256];
+__attribute__((constructor)) static void orc_init_e4m3(void) {
+    for (int b = 0; b < 256; b++) g_e4m3[b] = orc_e4m3_to_f32((uint8_t)b);
 }
 
 /* Round-to-nearest-even at E4M3 precision with satfinite (|x| >= 448 -> 448). */
@@ -110,27 +130,44 @@ void orc_dequant_int4(const uint8_t* packed, const uint16_t* scales,
 /* gemv_int4, engine.cu:83-109: y[m,n] = sum_k x[m,k] * (nib-8)*scale[n,k/128] */
 void orc_gemv_int4(const uint16_t* x, const uint8_t* packed, const uint16_t* scales,
                    float* y, int M, int N, int K) {
-    for (int m = 0; m < M; m++) {
-        float* xs = (float*)malloc(sizeof(float) * (size_t)K);
-        for (int k = 0; k < K; k++) xs[k] = orc_h2f(x[(size_t)m * K + k]);
-#pragma omp parallel for schedule(static) if ((size_t)N * K > (1u << 18))
+    /* Each weight row is dequantized once (exact fp32 (nib-8)*scale) and
+     * dotted with every x row; per (m, n) the double sum runs over k in
+     * order, the same arithmetic as one row at a time. */
+    float* xs = (float*)malloc(sizeof(float) * (size_t)M * K);
+    for (size_t i = 0; i < (size_t)M * K; i++) xs[i] = orc_h2f(x[i]);
+#pragma omp parallel if ((size_t)N * K * M > (1u << 18))
+    {
+        float* wr = (float*)malloc(sizeof(float) * (size_t)K);
+#pragma omp for schedule(static)
         for (int n = 0; n < N; n++) {
             const uint8_t* prow = packed + (size_t)n * (K / 2);
             const uint16_t* srow = scales + (size_t)n * (K / 128);
-            double acc = 0.0;
             for (int g = 0; g < K / 128; g++) {
                 float sc = orc_h2f(srow[g]);
                 for (int j = g * 64; j < g * 64 + 64; j++) {
                     uint8_t b = prow[j];
-                    float w0 = (float)((int)(b & 15) - 8) * sc;
-                    float w1 = (float)((int)(b >> 4) - 8) * sc;
-                    acc += (double)w0 * xs[2 * j] + (double)w1 * xs[2 * j + 1];
+                    wr[2 * j] = (float)((int)(b & 15) - 8) * sc;
+                    wr[2 * j + 1] = (float)((int)(b >> 4) - 8) * sc;
                 }
             }
-            y[(size_t)m * N + n] = (float)acc;
+            for (int m = 0; m < M; m++) {
+                const float* xm = xs + (size_t)m * K;
+#ifdef ORC_BASELINE
+                float a8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                for (int k = 0; k < K; k += 8)
+                    for (int u = 0; u < 8; u++) a8[u] += wr[k + u] * xm[k + u];
+                y[(size_t)m * N + n] = ((a8[0] + a8[1]) + (a8[2] + a8[3])) + ((a8[4] + a8[5]) + (a8[6] + a8[7]));
+#else
+                double acc = 0.0;
+                for (int j = 0; j < K / 2; j++)
+                    acc += (double)wr[2 * j] * xm[2 * j] + (double)wr[2 * j + 1] * xm[2 * j + 1];
+                y[(size_t)m * N + n] = (float)acc;
+#endif
+            }
         }
-        free(xs);
+        free(wr);
     }
+    free(xs);
 }
 
 /* gemv_fp16, engine.cu:112-128 */
@@ -141,9 +178,18 @@ void orc_gemv_fp16(const uint16_t* x, const uint16_t* W, float* y, int M, int N,
 #pragma omp parallel for schedule(static) if ((size_t)N * K > (1u << 18))
         for (int n = 0; n < N; n++) {
             const uint16_t* wr = W + (size_t)n * K;
+#ifdef ORC_BASELINE
+            float a8[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int k = 0; k + 8 <= K; k += 8)
+                for (int u = 0; u < 8; u++) a8[u] += orc_h2f(wr[k + u]) * xs[k + u];
+            float acc = ((a8[0] + a8[1]) + (a8[2] + a8[3])) + ((a8[4] + a8[5]) + (a8[6] + a8[7]));
+            for (int k = K & ~7; k < K; k++) acc += orc_h2f(wr[k]) * xs[k];
+            y[(size_t)m * N + n] = acc;
+#else
             double acc = 0.0;
             for (int k = 0; k < K; k++) acc += (double)orc_h2f(wr[k]) * xs[k];
             y[(size_t)m * N + n] = (float)acc;
+#endif
         }
         free(xs);
     }
@@ -236,44 +282,46 @@ void orc_attn_decode(const uint16_t* q, const uint8_t* kc8, const uint8_t* vc8,
     int total = qpos + 1;
     int cend = committed < total ? committed : total;
     int gqa = nh / nkv;
-    double* s = (double*)malloc(sizeof(double) * (size_t)total);
-    double* o = (double*)malloc(sizeof(double) * (size_t)hd);
+#pragma omp parallel for schedule(static) if ((size_t)nh * total > 65536)
     for (int h = 0; h < nh; h++) {
+        orc_acc* s = (orc_acc*)malloc(sizeof(orc_acc) * (size_t)total);
+        orc_acc o[256];
         int kvh = h / gqa;
         const uint16_t* qh = q + (size_t)h * hd;
-        double mx = -INFINITY;
+        float qf[256];
+        for (int d = 0; d < hd; d++) qf[d] = orc_h2f(qh[d]);
+        orc_acc mx = -INFINITY;
         for (int t = 0; t < total; t++) {
-            double acc = 0.0;
+            orc_acc acc = 0.0;
             if (t < cend) {
                 float kscl = orc_h2f(ksc[(t / 64) * nkv + kvh]);
                 const uint8_t* kp = kc8 + ((size_t)t * nkv + kvh) * hd;
                 for (int d = 0; d < hd; d++)
-                    acc += (double)orc_h2f(qh[d]) * (double)(orc_e4m3_to_f32(kp[d]) * kscl);
+                    acc += (orc_acc)qf[d] * (orc_acc)(g_e4m3[kp[d]] * kscl);
             } else {
                 const uint16_t* kp = ktail + ((size_t)(t - committed) * nkv + kvh) * hd;
-                for (int d = 0; d < hd; d++) acc += (double)orc_h2f(qh[d]) * orc_h2f(kp[d]);
+                for (int d = 0; d < hd; d++) acc += (orc_acc)qf[d] * orc_h2f(kp[d]);
             }
             s[t] = acc * scale;
             if (s[t] > mx) mx = s[t];
         }
-        double l = 0.0;
+        orc_acc l = 0.0;
         for (int d = 0; d < hd; d++) o[d] = 0.0;
         for (int t = 0; t < total; t++) {
-            double p = exp(s[t] - mx);
+            orc_acc p = ORC_EXP(s[t] - mx);
             l += p;
             if (t < cend) {
                 float vscl = orc_h2f(vsc[(t / 64) * nkv + kvh]);
                 const uint8_t* vp = vc8 + ((size_t)t * nkv + kvh) * hd;
-                for (int d = 0; d < hd; d++) o[d] += p * (double)(orc_e4m3_to_f32(vp[d]) * vscl);
+                for (int d = 0; d < hd; d++) o[d] += p * (orc_acc)(g_e4m3[vp[d]] * vscl);
             } else {
                 const uint16_t* vp = vtail + ((size_t)(t - committed) * nkv + kvh) * hd;
                 for (int d = 0; d < hd; d++) o[d] += p * orc_h2f(vp[d]);
             }
         }
         for (int d = 0; d < hd; d++) out[(size_t)h * hd + d] = orc_f2h((float)(o[d] / l));
+        free(s);
     }
-    free(s);
-    free(o);
 }
 
 /* conv_pre, engine.cu:483-494: inproj rows are B | C | x */
@@ -619,6 +667,45 @@ void orc_state_free(orc_state* s) {
 }
 
 int orc_state_pos(const orc_state* s) { return s->pos; }
+
+int orc_state_load(const orc_model* m, orc_state* s, const uint8_t* buf, size_t n) {
+    const orc_config* c = &m->cfg;
+    int32_t hd[8];
+    uint32_t magic, version;
+    if (n < 32) return -1;
+    memcpy(&magic, buf, 4);
+    memcpy(&version, buf + 4, 4);
+    memcpy(hd, buf + 8, 24);
+    const int pos = hd[0];
+    if (magic != 0x54534943u || version != 1 || hd[1] != c->n_layers || hd[2] != c->hidden ||
+        hd[3] != c->n_kv_heads || pos < 0 || pos >= s->max_ctx || s->h2o_budget > 0)
+        return -1;
+    const size_t row = (size_t)c->n_kv_heads * c->head_dim;
+    const size_t C = (size_t)(pos / 64) * 64;
+    size_t need = 32;
+    for (int l = 0; l < c->n_layers; l++)
+        need += c->attn_layer[l] ? 2 * C * row + 2 * (C / 64) * c->n_kv_heads * 2 + 2 * 64 * row * 2
+                                 : (size_t)2 * c->hidden * 2;
+    if (n != need) return -1;
+    const uint8_t* p = buf + 32;
+    for (int l = 0; l < c->n_layers; l++) {
+        if (c->attn_layer[l]) {
+            const size_t sc = (C / 64) * c->n_kv_heads * 2, tail = 64 * row * 2;
+            memcpy(s->kc8[l], p, C * row); p += C * row;
+            memcpy(s->vc8[l], p, C * row); p += C * row;
+            memcpy(s->ksc[l], p, sc); p += sc;
+            memcpy(s->vsc[l], p, sc); p += sc;
+            memcpy(s->ktail[l], p, tail); p += tail;
+            memcpy(s->vtail[l], p, tail); p += tail;
+            s->committed[l] = (int)C;
+        } else {
+            memcpy(s->conv_state[l], p, (size_t)2 * c->hidden * 2);
+            p += (size_t)2 * c->hidden * 2;
+        }
+    }
+    s->pos = pos;
+    return 0;
+}
 
 /* H2O mode: budget slots per attention layer, local window W (the reference's
  * defaults: budget >= prompt, W = budget/2, W < budget; engine.cu:753-756). */
@@ -983,6 +1070,7 @@ int orc_prefill_ex(const orc_model* m, orc_state* s, const int* tokens, int S, c
                 }
             }
             float scale = 1.0f / sqrtf((float)hd);
+#pragma omp parallel for schedule(dynamic, 4) if (S > 8)
             for (int i = 0; i < S; i++)
                 orc_attn_decode(q16 + (size_t)i * nh * hd, s->kc8[l], s->vc8[l], s->ksc[l], s->vsc[l],
                                 s->ktail[l], s->vtail[l], s->committed[l], past + i, scale,
@@ -1013,6 +1101,8 @@ int orc_prefill_ex(const orc_model* m, orc_state* s, const int* tokens, int S, c
             for (int e = 0; e < E; e++) eb[e] = orc_h2f(L->ebias[e]);
             memset(acc, 0, (size_t)S * H * 2);  /* expert_out_acc, engine.cu:882 */
             const int n_moe = c->n_layers - c->n_dense;
+            int* idx_all = (int*)malloc((size_t)S * K * sizeof(int));
+            float* w_all = (float*)malloc((size_t)S * K * sizeof(float));
             for (int i = 0; i < S; i++) {
                 const uint16_t* xi = xn + (size_t)i * H;
                 orc_gemv_fp16(xi, L->gate, rl, 1, E, H);
@@ -1032,16 +1122,38 @@ int orc_prefill_ex(const orc_model* m, orc_state* s, const int* tokens, int S, c
                 for (int t = 0; t < K; t++) {
                     s->route_idx[moe_i * K + t] = idx[t];
                     s->route_w[moe_i * K + t] = w[t];
-                }
-                for (int t = 0; t < K; t++) {
-                    int e = idx[t];
-                    orc_gemv_int4(xi, L->ew1[e].p, L->ew1[e].s, fa, 1, I, H);
-                    orc_gemv_int4(xi, L->ew3[e].p, L->ew3[e].s, fb, 1, I, H);
-                    orc_swiglu(fa, fb, t16, I);
-                    orc_gemv_int4(t16, L->ew2[e].p, L->ew2[e].s, fa, 1, H, I);
-                    orc_acc_scaled(acc + (size_t)i * H, fa, w[t], H);
+                    idx_all[i * K + t] = idx[t];
+                    w_all[i * K + t] = w[t];
                 }
             }
+            /* every (token, slot) row's expert output o = W2e . swiglu(W1e x, W3e x)
+             * (engine.cu:894-902), the rows of one expert in one multi-row GEMV
+             * (per row the same arithmetic as a single-row call) */
+            float* o_all = (float*)malloc((size_t)S * K * H * sizeof(float));
+            int* rows = (int*)malloc((size_t)S * K * sizeof(int));
+            uint16_t* xg = (uint16_t*)malloc((size_t)S * K * H * 2);
+            float* ga = (float*)malloc((size_t)S * K * I * 4);
+            float* gb = (float*)malloc((size_t)S * K * I * 4);
+            uint16_t* mid = (uint16_t*)malloc((size_t)S * K * I * 2);
+            float* og = (float*)malloc((size_t)S * K * H * 4);
+            for (int e = 0; e < E; e++) {
+                int n_e = 0;
+                for (int j = 0; j < S * K; j++)
+                    if (idx_all[j] == e) rows[n_e++] = j;
+                if (!n_e) continue;
+                for (int r = 0; r < n_e; r++)
+                    memcpy(xg + (size_t)r * H, xn + (size_t)(rows[r] / K) * H, (size_t)H * 2);
+                orc_gemv_int4(xg, L->ew1[e].p, L->ew1[e].s, ga, n_e, I, H);
+                orc_gemv_int4(xg, L->ew3[e].p, L->ew3[e].s, gb, n_e, I, H);
+                orc_swiglu(ga, gb, mid, n_e * I);
+                orc_gemv_int4(mid, L->ew2[e].p, L->ew2[e].s, og, n_e, H, I);
+                for (int r = 0; r < n_e; r++)
+                    memcpy(o_all + (size_t)rows[r] * H, og + (size_t)r * H, (size_t)H * 4);
+            }
+            for (int i = 0; i < S; i++)
+                for (int t = 0; t < K; t++)  /* acc_scaled in rank order, engine.cu:901 */
+                    orc_acc_scaled(acc + (size_t)i * H, o_all + ((size_t)i * K + t) * H, w_all[i * K + t], H);
+            free(idx_all); free(w_all); free(o_all); free(rows); free(xg); free(ga); free(gb); free(mid); free(og);
             orc_add_inplace(hs, acc, S * H);
             moe_i++;
         }

@@ -94,6 +94,12 @@ void       orc_model_free(orc_model* m);
 orc_state* orc_state_new(const orc_model* m, int max_ctx);
 void       orc_state_free(orc_state* s);
 int        orc_state_pos(const orc_state* s);
+/* Resume from a sequence-state snapshot in the layout documented at
+ * cuinf_session_save_state (KV cache, group scales, fp16 tails and conv state
+ * at a position; the reference keeps this state only in its device Buffers,
+ * engine.cu:590-623).  Returns 0, or -1 when the snapshot does not fit this
+ * model or state. */
+int        orc_state_load(const orc_model* m, orc_state* s, const uint8_t* buf, size_t n);
 /* One token through all layers at position state->pos, then the final norm,
  * lm_head and argmax.  Writes fp32 logits when logits != NULL and the final
  * hidden state (pre-norm, fp16) when hidden != NULL.  Returns the argmax. */

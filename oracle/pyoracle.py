@@ -57,6 +57,7 @@ _SIGS = {
     "orc_state_new": (P, [P, I]),
     "orc_state_free": (None, [P]),
     "orc_state_pos": (I, [P]),
+    "orc_state_load": (I, [P, P, P, ctypes.c_size_t]),
     "orc_forward_token": (I, [P, P, I, P, P]),
     "orc_forward_token_ex": (I, [P, P, I, P, P, P, P]),
     "orc_prefill": (I, [P, P, P, I, P]),
@@ -75,10 +76,22 @@ _SIGS = {
 }
 
 
+_PATH = os.path.join(HERE, "liboracle.so")
+
+
+def use_library(path):
+    """Bind this module to another build of oracle.c (the timed CPU baseline,
+    libcpubase.so) instead of the checker; only before the first call."""
+    global _PATH
+    if _L is not None and path != _PATH:
+        raise RuntimeError("pyoracle already bound to " + _PATH)
+    _PATH = path
+
+
 def lib():
     global _L
     if _L is None:
-        path = os.path.join(HERE, "liboracle.so")
+        path = _PATH
         if not os.path.exists(path):
             from . import build
             build(with_ref=False)
@@ -355,6 +368,13 @@ class State:
         idx = np.ctypeslib.as_array(ctypes.cast(ip, ctypes.POINTER(ctypes.c_int)), (n,)).copy()
         w = np.ctypeslib.as_array(ctypes.cast(wp, ctypes.POINTER(ctypes.c_float)), (n,)).copy()
         return idx, w
+
+    def load_state(self, snap):
+        """Resume from a sequence-state snapshot (bytes in the layout of
+        cuinf_session_save_state)."""
+        buf = np.frombuffer(snap, np.uint8)
+        if lib().orc_state_load(self.model._h, self._h, buf.ctypes.data, buf.size) != 0:
+            raise ValueError("state snapshot does not fit this model/state")
 
     @property
     def pos(self):

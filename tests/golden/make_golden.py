@@ -2,7 +2,7 @@
 
 Run here (where the reference tree is mounted), not on the GPU box:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref <g023/cuda_inf source tree>]
 
 Writes:
   quant_int4.npz    inputs/outputs of quant_int4_group (tools/export_weights.py:64-79),
@@ -128,7 +128,10 @@ def make_format(ref, out):
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from oracle import reference_tree
+    ap.add_argument("--ref", default=reference_tree(),
+                    help="the g023/cuda_inf source tree (default: $CUINF_REFERENCE or ../reference)")
     ap.add_argument("--out", default=HERE)
     a = ap.parse_args()
     make_quant(a.ref, a.out)

@@ -95,29 +95,31 @@ def prefill_compare(cfg, om, s, st, ids):
     return got, e, checked, near
 
 
-@pytest.mark.parametrize("past,S", [(0, 1), (0, 70), (30, 50), (64, 64)])
+@pytest.mark.parametrize("past,S", [(0, 1), (0, 70), (30, 50), (64, 64), (0, 600)])
 def test_prefill_matches_oracle(tiny, past, S):
     """Batched prefill of S ids after `past` decode steps (the reference's
     prefill starts at 0; later starts continue a session), then 20
     teacher-forced decode steps: the group commits inside the prefill
     (tokens 64 and 128) and the attention over committed FP8 groups plus the
-    fp16 tail must follow the oracle."""
+    fp16 tail must follow the oracle.  S = 600 runs the grouped expert GEMMs
+    over two chunks of 1024/top_k tokens."""
     cfg, om, gm = tiny
     rng = np.random.default_rng(1000 + past + S)
     lead = rng.integers(0, cfg.vocab, past)
     ids = rng.integers(0, cfg.vocab, S)
     tail = rng.integers(0, cfg.vocab, 20)
-    s = Session(gm, max_ctx=192)
+    mc = max(192, past + S + 32)
+    s = Session(gm, max_ctx=mc)
     s.keep_logits(True)
-    st = om.state(192)
+    st = om.state(mc)
     if past:
-        run_compare(cfg, om, s, lead, 192, st=st)
+        run_compare(cfg, om, s, lead, mc, st=st)
     got, e, checked, near = prefill_compare(cfg, om, s, st, ids)
     assert s.pos == past + S and st.pos == past + S
     print(f"prefill past={past} S={S}: logits rel err {e:.2e}, routing checked {checked}, near-ties {near}")
     assert checked > 0.9 * (checked + near)
     # decoding continues from the prefilled state (first fed token = the argmax)
-    worst, near, checked, _ = run_compare(cfg, om, s, [got] + list(tail), 192, st=st)
+    worst, near, checked, _ = run_compare(cfg, om, s, [got] + list(tail), mc, st=st)
     assert device_error() == 0 and s.error() == 0
 
 

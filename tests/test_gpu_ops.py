@@ -164,7 +164,7 @@ def test_kv_write_tail(cuda):
     assert kt[:10].abs().sum().item() == 0 and kt[13:].abs().sum().item() == 0
 
 
-@pytest.mark.parametrize("n_tok", [1, 5, 63, 64, 65, 127, 128, 200, 2048, 4113, 8192])
+@pytest.mark.parametrize("n_tok", [1, 5, 63, 64, 65, 127, 128, 200, 2048, 4113, 8192, 32768])
 def test_attn_decode(cuda, n_tok):
     rng = np.random.default_rng(n_tok)
     K, V, kc8, vc8, ksc, vsc, ktail, vtail, committed = _kv_cache(rng, n_tok, zero_head=n_tok == 200)

@@ -11,6 +11,16 @@ cuinf_prefill does the same.  Prompts of 1 and 64 tokens are run; the
 their own group's keys as FP8.  Then 80 tokens are generated, crossing the
 next commit.
 
+Two models are run.  On the plain random-init model (expert bias
+N(0, 0.1)) routing near-ties occur at most positions, so the comparison
+walks the trajectories up to their first parting and requires it to sit on
+a near-tie.  On the same model with a spaced router bias (each MoE layer's
+expert bias set to 1.0 x a random permutation of 0..31, so the 4th vs 5th
+expert score margin is at least 1.0 - 0.7: sigmoid values of these logits
+stay inside (0.15, 0.85)) no routing decision is near a tie, and the greedy
+tokens must be identical to the reference engine's for the first
+MIN_PREFIX tokens.
+
 The CPU oracle, teacher-forced along the reference's tokens, gives at every
 position the top-2 logit margin and the margin between the 4th and 5th
 expert scores of each MoE layer (of every prompt row for the prefill).  Two
@@ -42,15 +52,29 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF_ENGINE = os.path.join(ROOT, "oracle", "_ref", "ref_engine")
 N_NEW = 80
+MIN_PREFIX = 32
 TIE_MARGIN = 1e-2  # relative top-2 logit margin below which a greedy pick is a near-tie
 ROUTE_MARGIN = 2e-3  # 4th-vs-5th expert score margin below which routing is a near-tie
 
 
+def space_router_bias(blob, cfg, seed):
+    """Overwrite every MoE layer's expert bias in the device blob with
+    1.0 x a random permutation of 0..E-1 (fp16, exact)."""
+    rng = np.random.default_rng(seed)
+    for e in weights.layout(cfg):
+        if e.name.endswith("feed_forward.expert_bias"):
+            b = rng.permutation(cfg.n_experts).astype(np.float16)
+            blob[e.offset:e.offset + e.nbytes].copy_(torch.from_numpy(b.view(np.uint8)).to(blob.device))
+
+
 @pytest.mark.skipif(not os.path.exists(REF_ENGINE), reason="reference engine not built (oracle/_ref)")
+@pytest.mark.parametrize("spaced", [False, True], ids=["plain", "spaced_bias"])
 @pytest.mark.parametrize("n_prompt", [1, 64])
-def test_greedy_matches_reference_engine(cuda, n_prompt):
+def test_greedy_matches_reference_engine(cuda, n_prompt, spaced):
     cfg = weights.default_config()
     blob, index = weights.synth_device_blob(cfg, seed=97, device=cuda)
+    if spaced:
+        space_router_bias(blob, cfg, seed=11)
     prompt = [int(t) for t in np.random.default_rng(5).integers(0, cfg.vocab, n_prompt)]
     base = "/dev/shm" if shutil.disk_usage("/dev/shm").free > 6e9 else None
     with tempfile.TemporaryDirectory(dir=base) as d:
@@ -76,6 +100,7 @@ def test_greedy_matches_reference_engine(cuda, n_prompt):
     om = orc.Model(weights.config_dict(cfg), host, index)
     st = om.state(n_prompt + N_NEW + 8)
     matched = 0
+    min_route_margin = np.inf
     for i, tok in enumerate(ref):
         if i == 0:
             nxt, lg, sc = st.prefill(prompt)  # sc [S, n_moe, E]
@@ -84,6 +109,7 @@ def test_greedy_matches_reference_engine(cuda, n_prompt):
         top = np.sort(lg)[::-1]
         srt = -np.sort(-sc, axis=-1)
         route_margin = float(np.min(srt[..., cfg.top_k - 1] - srt[..., cfg.top_k]))
+        min_route_margin = min(min_route_margin, route_margin)
         logit_tie = top[0] - top[1] <= TIE_MARGIN * max(1.0, abs(float(top[0])))
         near_tie = logit_tie or route_margin <= ROUTE_MARGIN
         if ours[i] != tok:
@@ -92,7 +118,10 @@ def test_greedy_matches_reference_engine(cuda, n_prompt):
         if not near_tie:
             assert tok == nxt, (i, tok, nxt)
         matched += 1
-    print(f"prompt {n_prompt}: greedy tokens equal to the reference engine's: first {matched} of {len(ref)}; "
-          f"ours {ours[:matched + 1]}, reference {ref[:matched + 1]}")
-    if n_prompt == 1:
+    print(f"prompt {n_prompt} ({'spaced' if spaced else 'plain'} bias): greedy tokens equal to the reference "
+          f"engine's: first {matched} of {len(ref)}; ours {ours[:matched + 1]}, reference {ref[:matched + 1]}")
+    if spaced:
+        assert min_route_margin > 0.1
+        assert matched >= min(MIN_PREFIX, len(ref))
+    elif n_prompt == 1:
         assert matched >= 1
