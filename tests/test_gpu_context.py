@@ -124,7 +124,7 @@ def test_prefill_4090_then_decode(wide3):
         near += n
     e = check_logits(s.logits().cpu().numpy(), lg, got, ref, 1e-2, "prefill")
     print(f"prefill {S}: last-row logits rel err {e:.2e}; routing checked {checked}, near-ties {near}")
-    assert checked > 0.9 * (checked + near)
+    assert checked > 0.8 * (checked + near)
     assert s.pos == S and st.pos == S
     tail = rng.integers(0, cfg.vocab, 9)
     worst, near, checked, _ = run_compare(cfg, om, s, [got] + list(tail), 4160, route_margin=ROUTE_MARGIN_FULL,
