@@ -65,6 +65,7 @@ _SIGS = {
     "cuinf_argmax": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
     "cuinf_moe_route": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
                                 c_void_p]),
+    "cuinf_moe_ffn_workspace_size": (c_size_t, [c_int, c_int, c_int]),
     "cuinf_moe_ffn": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                               c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "cuinf_quantize_int4": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),

@@ -17,6 +17,7 @@
 #include "engine_kernels.cuh"
 #include "megakernel.cuh"
 #include "model.h"
+#include "moe_fused.cuh"
 
 #define REQUIRE(cond, msg) \
     do {                   \
@@ -27,33 +28,50 @@
 // ---------------------------------------------------------------------------
 // standalone flash-decoding attention (attn_decode_split/combine, 396-480)
 // ---------------------------------------------------------------------------
+static int current_sms() {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return 148;
+    return sms;
+}
+
 extern "C" size_t cuinf_attn_decode_workspace_size(int nh, int nkv, int max_ctx) {
     if (nh <= 0 || nkv <= 0 || max_ctx <= 0) return 0;
     int units = (max_ctx + CUINF_KVGROUP - 1) / CUINF_KVGROUP + 1;
-    int ns = attn_default_nsplit(nkv, nh / nkv, units, 148);
+    int ns = attn_default_nsplit(nkv, nh / nkv, units, current_sms());
     return (size_t)nkv * ns * (nh / nkv) * ATTN_PART_STRIDE * 4 + 256;
 }
 
+// Library-owned scratch for calls that pass no workspace, one buffer per
+// device ordinal and kind (grown on demand; zero-filled when allocated).  A
+// kernel that needs zeroed words (tickets, accumulators) leaves them zero.
+// Growing waits for the whole device, so no launch still uses the old buffer.
+#define WS_MAX_DEVICES 64
+enum { WS_ATTN = 0, WS_MOE = 1, WS_KINDS = 2 };
 static std::mutex g_ws_mu;
-static void* g_ws = nullptr;
-static size_t g_ws_bytes = 0;
+static void* g_ws[WS_KINDS][WS_MAX_DEVICES];
+static size_t g_ws_bytes[WS_KINDS][WS_MAX_DEVICES];
 
-// Library-owned scratch for calls that pass no workspace (grown on demand;
-// its first 256 bytes are the zero-initialised per-kv-head tickets).
-static int shared_workspace(size_t need, void** out, cudaStream_t st) {
+static int shared_workspace(int kind, size_t need, void** out) {
+    int dev = 0;
+    CUINF_TRY(cudaGetDevice(&dev));
+    REQUIRE(dev >= 0 && dev < WS_MAX_DEVICES, "device ordinal beyond the library's table");
     std::lock_guard<std::mutex> lk(g_ws_mu);
-    if (g_ws_bytes < need) {
-        if (g_ws) {
-            CUINF_TRY(cudaStreamSynchronize(st));
-            CUINF_TRY(cudaFree(g_ws));
-            g_ws = nullptr;
-            g_ws_bytes = 0;
+    void*& p = g_ws[kind][dev];
+    size_t& have = g_ws_bytes[kind][dev];
+    if (have < need) {
+        if (p) {
+            CUINF_TRY(cudaDeviceSynchronize());
+            CUINF_TRY(cudaFree(p));
+            p = nullptr;
+            have = 0;
         }
-        CUINF_TRY(cudaMalloc(&g_ws, need));
-        CUINF_TRY(cudaMemsetAsync(g_ws, 0, 256, st));
-        g_ws_bytes = need;
+        CUINF_TRY(cudaMalloc(&p, need));
+        CUINF_TRY(cudaMemset(p, 0, need));
+        have = need;
     }
-    *out = g_ws;
+    *out = p;
     return CUINF_OK;
 }
 
@@ -80,7 +98,7 @@ extern "C" int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_
     const size_t need = (size_t)nkv * ns * (nh / nkv) * ATTN_PART_STRIDE * 4 + 256;
     void* ws = workspace;
     if (!ws) {
-        int rc = shared_workspace(need, &ws, ST(stream));
+        int rc = shared_workspace(WS_ATTN, need, &ws);
         if (rc) return rc;
     } else {
         REQUIRE(workspace_bytes >= need, "workspace too small");
@@ -350,6 +368,15 @@ static int moe_ffn_launch(const __half* xn, const __half* gate, const __half* bi
     return cuinf_launch_status();
 }
 
+// Workspace of cuinf_moe_ffn: [0, 256) tickets, then the fused kernel's
+// fixed-point accumulators [topk][H], then mid [topk][I] and the routes of
+// the two-kernel form.  The first 256 + topk*H*8 bytes must be zero before the
+// first call; every call leaves them zero.
+extern "C" size_t cuinf_moe_ffn_workspace_size(int H, int I, int topk) {
+    if (H <= 0 || I <= 0 || topk <= 0) return 0;
+    return 256 + (size_t)topk * H * 8 + (size_t)topk * I * 2 + 256;
+}
+
 extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* expert_bias,
                              const void* const* experts, void* h, int H, int I, int n_exp, int topk,
                              int* idx, float* w, void* workspace, size_t workspace_bytes,
@@ -358,22 +385,49 @@ extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* exper
     REQUIRE(H > 0 && H % 128 == 0 && I > 0 && I % 128 == 0, "H and I must be multiples of 128");
     REQUIRE(n_exp > 0 && n_exp <= 256 && topk > 0 && topk <= 8 && topk <= n_exp,
             "n_exp <= 256, topk <= 8");
-    const size_t need = (size_t)topk * I * 2 + 256;
+    const size_t need = cuinf_moe_ffn_workspace_size(H, I, topk);
     void* ws = workspace;
     if (!ws) {
-        int rc = shared_workspace(need + 256, &ws, ST(stream));
+        int rc = shared_workspace(WS_MOE, need, &ws);
         if (rc) return rc;
-        ws = (char*)ws + 256;
     } else {
-        REQUIRE(workspace_bytes >= need, "workspace too small");
+        REQUIRE(workspace_bytes >= need, "workspace too small (cuinf_moe_ffn_workspace_size)");
+        REQUIRE(((uintptr_t)ws & 15) == 0, "workspace must be 16-byte aligned");
     }
-    __half* mid = (__half*)ws;
-    int* ridx = idx ? idx : (int*)((char*)ws + (size_t)topk * I * 2);
-    float* rw = w ? w : (float*)((char*)ws + (size_t)topk * I * 2 + 128);
-    {   // TMA sources must be 16-byte aligned
+    unsigned* tickets = (unsigned*)ws;
+    unsigned long long* acc = (unsigned long long*)((char*)ws + 256);
+    __half* mid = (__half*)((char*)ws + 256 + (size_t)topk * H * 8);
+    char* rbuf = (char*)mid + (size_t)topk * I * 2;
+    int* ridx = idx ? idx : (int*)rbuf;
+    float* rw = w ? w : (float*)(rbuf + 128);
+    {   // TMA / async-copy sources must be 16-byte aligned
         std::vector<uintptr_t> tab((size_t)n_exp * 6);
         CUINF_TRY(cudaMemcpy(tab.data(), experts, tab.size() * sizeof(uintptr_t), cudaMemcpyDeviceToHost));
         for (uintptr_t a : tab) REQUIRE(a && (a & 15) == 0, "expert tensors must be 16-byte aligned");
+    }
+    if (moef_supported(H, I, n_exp, topk)) {
+        MoeFusedParams F;
+        F.h = (const __half*)h;
+        F.xn = (const __half*)xn;
+        F.h_out = (__half*)h;
+        F.norm_w = nullptr;
+        F.gate = (const __half*)gate;
+        F.bias = (const __half*)expert_bias;
+        F.experts = experts;
+        F.route_idx = ridx;
+        F.route_w = rw;
+        F.acc = acc;
+        F.tickets = tickets;
+        F.H = H;
+        F.I = I;
+        F.E = n_exp;
+        F.topk = topk;
+        F.eps = 0.f;
+        F.next.count = 0;
+        const size_t sm = moef_layout(H, n_exp).total;
+        CUINF_TRY(cudaFuncSetAttribute(k_moe_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        k_moe_fused<<<topk * (I / MOEF_CHUNK), MOEF_THREADS, sm, ST(stream)>>>(F);
+        return cuinf_launch_status();
     }
     return moe_ffn_launch((const __half*)xn, (const __half*)gate, (const __half*)expert_bias, experts,
                           (__half*)h, H, I, n_exp, topk, mid, ridx, rw, ST(stream));
@@ -677,6 +731,11 @@ struct cuinf_session {
     std::vector<H2o> h2o;
     __half* kv_new = nullptr;  // the decode token's K then V, [2][nkv][64]
     int* h2o_dst = nullptr;    // [n_layers] slot chosen in the last step
+    // fused MoE layer (k_moe_fused): fixed-point down accumulators and
+    // tickets, zero between launches (each launch leaves them zero)
+    bool moe_fused = false;
+    unsigned long long* moe_acc = nullptr;
+    unsigned* moe_tick = nullptr;
 };
 
 template <class T>
@@ -1056,10 +1115,31 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
                           }});
         } else {
             const int mi = L.moe_index;
+            const void* const* ex = (const void* const*)(m->d_experts + (size_t)mi * c.n_experts * 6);
+            const double moe_bytes = 2.0 * c.top_k * q4_bytes(c.moe_inter, H) + c.top_k * q4_bytes(H, c.moe_inter) +
+                                     (double)c.n_experts * H * 2 + c.n_experts * 2 + 4.0 * H;
+            if (s->moe_fused) {
+                MoeFusedParams F;
+                F.h = s->h; F.xn = nullptr; F.h_out = s->h; F.norm_w = L.ffn_norm;
+                F.gate = L.gate; F.bias = L.ebias; F.experts = ex;
+                F.route_idx = s->route_idx + mi * c.top_k;
+                F.route_w = s->route_w + mi * c.top_k;
+                F.acc = s->moe_acc; F.tickets = s->moe_tick;
+                F.H = H; F.I = c.moe_inter; F.E = c.n_experts; F.topk = c.top_k; F.eps = c.norm_eps;
+                const int grid = c.top_k * (c.moe_inter / MOEF_CHUNK);
+                const size_t sm = moef_layout(H, c.n_experts).total;
+                Ls.push_back({"moe_ffn", moe_bytes,
+                              {{(const char*)L.gate, (unsigned long long)c.n_experts * H * 2}},
+                              [=](const L2Ranges& nx, bool pdl) mutable {
+                                  F.next = nx;
+                                  return launch_k(k_moe_fused, dim3(grid), dim3(MOEF_THREADS), sm, st, pdl, F);
+                              }});
+                continue;
+            }
             MoeUpParams U;
             U.h = s->h; U.xn = nullptr; U.norm_w = L.ffn_norm;
             U.gate = L.gate; U.bias = L.ebias;
-            U.experts = (const void* const*)(m->d_experts + (size_t)mi * c.n_experts * 6);
+            U.experts = ex;
             U.mid = s->mid;
             U.route_idx = s->route_idx + mi * c.top_k;
             U.route_w = s->route_w + mi * c.top_k;
@@ -1149,6 +1229,8 @@ static int set_kernel_attrs(const cuinf_config& c) {
         {(const void*)k_moe_up, moe_up_smem(H, std::max(1, c.n_experts))},
         {(const void*)k_moe_down, moe_down_smem(c.moe_inter, std::max(1, c.top_k))},
         {(const void*)k_lmhead, lmhead_smem(H)},
+        {(const void*)k_moe_fused, moef_supported(H, c.moe_inter, c.n_experts, c.top_k)
+                                       ? moef_layout(H, c.n_experts).total : (size_t)0},
         {(const void*)k_gemv_residual,
          std::max(ONE_PER_SM_SMEM, std::max(res_smem(H), std::max(res_smem(c.n_heads * 64), res_smem(c.dense_inter))))},
     };
@@ -1219,6 +1301,11 @@ extern "C" int cuinf_session_create(cuinf_model* m, int max_ctx, void* stream, c
     s->nsplit = std::min(attn_engine_nsplit(gqa, units), std::max(1, s->num_sms / nkv));
     TRYS(dalloc(s, &s->attn_part, (size_t)nkv * s->nsplit * gqa * ATTN_PART_STRIDE * 4));
     TRYS(dalloc(s, &s->attn_cnt, (size_t)nkv * 4));
+    if (m->n_moe > 0 && moef_supported(H, c.moe_inter, c.n_experts, c.top_k)) {
+        TRYS(dalloc(s, &s->moe_acc, (size_t)c.top_k * H * 8));
+        TRYS(dalloc(s, &s->moe_tick, 256));
+        s->moe_fused = true;
+    }
     s->attn.assign(c.n_layers, AttnState());
     s->conv_state.assign(c.n_layers, nullptr);
     const size_t row = (size_t)nkv * 64;

@@ -147,7 +147,11 @@ int cuinf_moe_route(const float* logits, const void* bias, int S, int n_exp, int
  * w3.packed, w3.scales, w2.packed, w2.scales} (w1,w3 [I,H], w2 [H,I]).
  * h fp16 [H] is updated in place: h = half(h + acc), acc accumulated in fp16
  * over the selected experts in rank order.  idx/w (device, may be NULL)
- * receive the routing decision.  workspace: 2*topk*I*2 bytes or NULL. */
+ * receive the routing decision.  workspace: cuinf_moe_ffn_workspace_size
+ * bytes, 16-byte aligned, whose first 256 + topk*H*8 bytes are zero before
+ * the first call (every call leaves them zero), or NULL for a library-owned
+ * buffer per device.  Calls sharing a workspace must not overlap. */
+size_t cuinf_moe_ffn_workspace_size(int H, int I, int topk);
 int cuinf_moe_ffn(const void* xn, const void* gate, const void* expert_bias,
                   const void* const* experts, void* h, int H, int I, int n_exp, int topk,
                   int* idx, float* w, void* workspace, size_t workspace_bytes, void* stream);

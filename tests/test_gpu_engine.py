@@ -59,7 +59,9 @@ def test_kernels_per_step(tiny):
     cfg, om, gm = tiny
     s = Session(gm, max_ctx=64)
     assert not s.uses_megakernel  # the captured multi-kernel graph is the default
-    assert s.kernels_per_step == 2 * 4 + 3 * 2 + 2 * 6 + 1
+    # conv layers 2 kernels, attention 3, the dense FFN 2, each MoE FFN 1
+    # (k_moe_fused), the lm_head 1
+    assert s.kernels_per_step == 2 * 4 + 3 * 2 + 2 * 1 + 1 * 5 + 1
     s.set_option(Session.OPT_MEGAKERNEL, 1)
     assert s.kernels_per_step == 1  # one persistent launch
 
