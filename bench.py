@@ -807,9 +807,10 @@ PHASES = {  # kernel id (csrc/common.cuh PH_*) -> (name, {slot: phase reached})
     1: ("k_gemv_residual", {0: "start", 1: "dependency wait done", 2: "x staged", 4: "dot done", 9: "end"}),
     2: ("k_conv_in", {0: "start", 1: "dependency wait done", 2: "norm done", 4: "dot done", 9: "end"}),
     3: ("k_ffn_up", {0: "start", 1: "dependency wait done", 2: "norm done", 4: "dot done", 9: "end"}),
-    4: ("k_moe_up", {0: "start", 1: "dependency wait done", 2: "norm done", 3: "gate rows in",
-                     4: "logits exchanged", 5: "experts selected", 6: "expert copies issued",
-                     7: "expert tiles in", 8: "dot done", 9: "end"}),
+    4: ("k_moe_fused", {0: "start", 1: "dependency wait done", 2: "norm done", 3: "logits exchanged",
+                        4: "experts selected", 5: "expert weights requested", 6: "w1/w3 dot done",
+                        7: "SwiGLU values gathered (cluster)", 8: "w2 partial added, ticket taken",
+                        9: "eighth finalized (last cluster)"}),
     5: ("k_moe_down", {0: "start", 1: "dependency wait done", 2: "mid staged", 4: "cluster sum done",
                        9: "end"}),
     6: ("k_lmhead", {0: "start", 1: "dependency wait done", 2: "norm done", 3: "rows done",

@@ -21,7 +21,7 @@ LIB = os.path.join(PKG, "libcuinf.so")
 BUILD_TRACE = os.path.join(PKG, "_build_trace")
 LIB_TRACE = os.path.join(PKG, "libcuinf_trace.so")
 SOURCES = ["ops.cu", "engine.cu", "batch.cu", "tokenizer.cpp"]
-HEADERS = ["common.cuh", "attn.cuh", "engine_kernels.cuh", "route.cuh", "tc_gemm.cuh", "model.h"]
+HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith((".cuh", ".h")))
 
 NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

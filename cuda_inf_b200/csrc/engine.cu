@@ -405,7 +405,7 @@ extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* exper
         CUINF_TRY(cudaMemcpy(tab.data(), experts, tab.size() * sizeof(uintptr_t), cudaMemcpyDeviceToHost));
         for (uintptr_t a : tab) REQUIRE(a && (a & 15) == 0, "expert tensors must be 16-byte aligned");
     }
-    if (moef_supported(H, I, n_exp, topk)) {
+    if (moef_supported(H, I, n_exp, topk) && ((uintptr_t)expert_bias & 15) == 0) {
         MoeFusedParams F;
         F.h = (const __half*)h;
         F.xn = (const __half*)xn;
@@ -426,7 +426,7 @@ extern "C" int cuinf_moe_ffn(const void* xn, const void* gate, const void* exper
         F.next.count = 0;
         const size_t sm = moef_layout(H, n_exp).total;
         CUINF_TRY(cudaFuncSetAttribute(k_moe_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        k_moe_fused<<<topk * (I / MOEF_CHUNK), MOEF_THREADS, sm, ST(stream)>>>(F);
+        k_moe_fused<<<topk * (I / 16), MOEF_THREADS, sm, ST(stream)>>>(F);
         return cuinf_launch_status();
     }
     return moe_ffn_launch((const __half*)xn, (const __half*)gate, (const __half*)expert_bias, experts,
@@ -1126,7 +1126,7 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
                 F.route_w = s->route_w + mi * c.top_k;
                 F.acc = s->moe_acc; F.tickets = s->moe_tick;
                 F.H = H; F.I = c.moe_inter; F.E = c.n_experts; F.topk = c.top_k; F.eps = c.norm_eps;
-                const int grid = c.top_k * (c.moe_inter / MOEF_CHUNK);
+                const int grid = c.top_k * (c.moe_inter / 16);
                 const size_t sm = moef_layout(H, c.n_experts).total;
                 Ls.push_back({"moe_ffn", moe_bytes,
                               {{(const char*)L.gate, (unsigned long long)c.n_experts * H * 2}},
@@ -1301,7 +1301,9 @@ extern "C" int cuinf_session_create(cuinf_model* m, int max_ctx, void* stream, c
     s->nsplit = std::min(attn_engine_nsplit(gqa, units), std::max(1, s->num_sms / nkv));
     TRYS(dalloc(s, &s->attn_part, (size_t)nkv * s->nsplit * gqa * ATTN_PART_STRIDE * 4));
     TRYS(dalloc(s, &s->attn_cnt, (size_t)nkv * 4));
-    if (m->n_moe > 0 && moef_supported(H, c.moe_inter, c.n_experts, c.top_k)) {
+    bool bias16 = true;  // the fused MoE kernel copies each router bias with 16-byte async copies
+    for (int l = c.n_dense; l < c.n_layers; l++) bias16 = bias16 && ((uintptr_t)m->L[l].ebias & 15) == 0;
+    if (m->n_moe > 0 && bias16 && moef_supported(H, c.moe_inter, c.n_experts, c.top_k)) {
         TRYS(dalloc(s, &s->moe_acc, (size_t)c.top_k * H * 8));
         TRYS(dalloc(s, &s->moe_tick, 256));
         s->moe_fused = true;

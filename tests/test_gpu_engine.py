@@ -83,6 +83,13 @@ def test_engine_options_do_not_change_results(tiny, opt):
         assert np.array_equal(a.logits().cpu().numpy(), b.logits().cpu().numpy())
 
 
+# Prefill rows run through the tensor-core GEMMs and the prefill attention,
+# whose fp32 sums differ from decode's in order; over hundreds of rows the
+# engine-vs-oracle router score difference reaches ~1.2e-3 (observed at row
+# 233 of a 600-token prompt), so prompt routing is compared outside 2e-3.
+PREFILL_ROUTE_MARGIN = 2e-3
+
+
 def prefill_compare(cfg, om, s, st, ids):
     """Engine prefill vs the oracle's prefill forced onto the engine's
     experts: routing outside near-ties, last-row logits and argmax."""
@@ -90,7 +97,7 @@ def prefill_compare(cfg, om, s, st, ids):
     ref, lg, sc = st.prefill(ids, forced_idx=gi)
     checked = near = 0
     for i in range(len(ids)):
-        c, n = check_routes(gi[i], sc[i], cfg.top_k, 1e-3, ("prefill row", i))
+        c, n = check_routes(gi[i], sc[i], cfg.top_k, PREFILL_ROUTE_MARGIN, ("prefill row", i))
         checked += c
         near += n
     e = check_logits(s.logits().cpu().numpy(), lg, got, ref, 1e-2, "prefill")
