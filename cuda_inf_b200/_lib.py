@@ -114,7 +114,14 @@ _SIGS = {
     "cuinf_batch_create_ep": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "cuinf_ep_unique_id": (c_int, [c_void_p, c_int]),
     "cuinf_ep_unique_id_bytes": (c_int, []),
+    "cuinf_batch_sync": (c_int, [c_void_p]),
+    "cuinf_ep_plan_host": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "cuinf_batch_abort": (c_int, [c_void_p]),
+    "cuinf_batch_set_timeout": (c_int, [c_void_p, c_int]),
+    "cuinf_batch_failed": (c_int, [c_void_p]),
     "cuinf_device_error": (c_int, [ctypes.POINTER(ctypes.c_uint)]),
+    "cuinf_selftest_wait_timeout": (c_int, [ctypes.c_uint, ctypes.POINTER(ctypes.c_uint),
+                                            ctypes.POINTER(ctypes.c_ulonglong)]),
     "cuinf_session_uses_megakernel": (c_int, [c_void_p]),
     "cuinf_session_trace": (c_int, [c_void_p, c_void_p, c_int, c_void_p, ctypes.POINTER(c_int),
                                     ctypes.POINTER(c_int)]),

@@ -259,6 +259,10 @@ extern "C" int cuinf_argmax_key_index(unsigned long long key) {
 // ===========================================================================
 #include <nccl.h>
 
+#include <chrono>
+#include <string>
+#include <thread>
+
 #include "model.h"
 #include "route.cuh"
 
@@ -305,6 +309,8 @@ struct cuinf_batch {
     // exchanges (token, slot) rows with the other ranks through NCCL
     int ep_rank = 0, ep_world = 1, e_lo = 0, e_loc = 0, cap = 0;
     ncclComm_t comm = nullptr;
+    int ep_timeout_ms = 120000;  // host-side limit on a step's (and the setup's) collectives
+    bool ep_failed = false;      // the communicator was aborted: the batch takes no more steps
     __half *send_x = nullptr, *recv_x = nullptr;
     int *send_meta = nullptr, *recv_meta = nullptr, *dest_pos = nullptr;
     float *back_o = nullptr, *recv_back = nullptr;
@@ -558,6 +564,24 @@ __global__ void __launch_bounds__(1024) k_ep_plan(const int* __restrict__ ridx, 
         meta[d * cap + r] = e - d * e_loc;
     }
 }
+// The same plan on the host (for checking the exchange protocol without a
+// GPU): identical outputs to k_ep_plan for the same routes.
+extern "C" int cuinf_ep_plan_host(const int* ridx, int n, int e_loc, int world, int cap, int* dest_pos, int* meta) {
+    REQUIRE(ridx && dest_pos && meta, "null pointer");
+    REQUIRE(n >= 0 && e_loc > 0 && world > 0 && cap >= 0, "bad plan sizes");
+    for (int i = 0; i < world * cap; i++) meta[i] = -1;
+    std::vector<int> fill(world, 0);
+    for (int j = 0; j < n; j++) {
+        const int e = ridx[j], d = e / e_loc;
+        REQUIRE(e >= 0 && d < world, "expert id out of range");
+        const int r = fill[d]++;
+        REQUIRE(r < cap, "more rows for one rank than the capacity");
+        dest_pos[j] = d * cap + r;
+        meta[d * cap + r] = e - d * e_loc;
+    }
+    return CUINF_OK;
+}
+
 // send_x[dest_pos[j]] = xn[j / topk]
 __global__ void k_ep_pack(const __half* __restrict__ xn, const int* __restrict__ dest_pos, __half* send_x, int H,
                           int topk) {
@@ -652,6 +676,56 @@ struct BStep {
         return rc;
     }
 };
+
+// ---------------------------------------------------------------------------
+// expert-parallel failure handling: the communicator is non-blocking, every
+// host wait on NCCL work polls its asynchronous error state under a time
+// limit, and a failure aborts the communicator (NCCL then releases the
+// kernels still waiting for peers) and marks the batch unusable.
+// ---------------------------------------------------------------------------
+static double now_ms() {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+static int ep_fail(cuinf_batch* b, const char* what) {
+    if (b->comm) ncclCommAbort(b->comm);
+    b->comm = nullptr;
+    b->ep_failed = true;
+    return cuinf_set_arg_error(what);
+}
+// Wait until a non-blocking NCCL call (init, group end) has been accepted.
+static int ep_settle(cuinf_batch* b, ncclResult_t r, const char* what) {
+    if (r != ncclSuccess && r != ncclInProgress) return ep_fail(b, what);
+    const double t0 = now_ms();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        if (ncclCommGetAsyncError(b->comm, &st) != ncclSuccess) return ep_fail(b, what);
+        if (st == ncclSuccess) return CUINF_OK;
+        if (st != ncclInProgress) return ep_fail(b, what);
+        if (now_ms() - t0 > b->ep_timeout_ms) return ep_fail(b, "NCCL call timed out (a peer did not join)");
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+// Synchronize the batch stream; for an expert-parallel batch, poll the
+// communicator's error state meanwhile and give up after the time limit.
+static int batch_sync(cuinf_batch* b) {
+    if (!b->comm) {
+        if (b->ep_failed) return cuinf_set_arg_error("expert-parallel batch was aborted");
+        CUINF_TRY(cudaStreamSynchronize(b->st));
+        return CUINF_OK;
+    }
+    const double t0 = now_ms();
+    for (int k = 0;; k++) {
+        const cudaError_t e = cudaStreamQuery(b->st);
+        if (e == cudaSuccess) return CUINF_OK;
+        if (e != cudaErrorNotReady) return cuinf_set_cuda_error(e);
+        ncclResult_t st = ncclSuccess;
+        if (ncclCommGetAsyncError(b->comm, &st) != ncclSuccess || (st != ncclSuccess && st != ncclInProgress))
+            return ep_fail(b, "expert-parallel step failed: NCCL reported an asynchronous error");
+        if (now_ms() - t0 > b->ep_timeout_ms)
+            return ep_fail(b, "expert-parallel step timed out (a peer did not complete it); communicator aborted");
+        if (k > 64) std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
 
 static int batch_record(cuinf_batch* b, BStep& S) {
     const cuinf_model* m = b->m;
@@ -813,7 +887,7 @@ static int batch_record(cuinf_batch* b, BStep& S) {
                         ncclSend(b->send_meta + d * b->cap, b->cap, ncclInt32, d, b->comm, b->st);
                         ncclRecv(b->recv_meta + d * b->cap, b->cap, ncclInt32, d, b->comm, b->st);
                     }
-                    if (ncclGroupEnd() != ncclSuccess) return cuinf_set_arg_error("NCCL dispatch failed");
+                    BTRY(ep_settle(b, ncclGroupEnd(), "NCCL dispatch failed"));
                     BTRY(S.mark("ep_dispatch"));
                     R.keys = b->recv_meta;
                     R.n = NR;
@@ -851,7 +925,7 @@ static int batch_record(cuinf_batch* b, BStep& S) {
                         ncclSend(b->back_o + d * co, co, ncclFloat32, d, b->comm, b->st);
                         ncclRecv(b->recv_back + d * co, co, ncclFloat32, d, b->comm, b->st);
                     }
-                    if (ncclGroupEnd() != ncclSuccess) return cuinf_set_arg_error("NCCL combine failed");
+                    BTRY(ep_settle(b, ncclGroupEnd(), "NCCL combine failed"));
                     BTRY(S.mark("ep_return"));
                 }
                 ob = b->recv_back;
@@ -928,7 +1002,7 @@ extern "C" int cuinf_batch_free(cuinf_batch* b) {
     if (b->ws) cudaFree(b->ws);
     if (b->cnt) cudaFree(b->cnt);
     if (b->pinned) cudaFreeHost(b->pinned);
-    if (b->comm) ncclCommDestroy(b->comm);  // after the graph that holds its calls
+    if (b->comm) ncclCommDestroy(b->comm);  // after the graph that holds its calls (an aborted one is gone)
     if (b->own_stream && b->st) cudaStreamDestroy(b->st);
     delete b;
     return CUINF_OK;
@@ -1037,10 +1111,14 @@ static int batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, c
         TRYB(balloc(b, &b->recv_back, rows * H * 4));
         ncclUniqueId id;
         memcpy(&id, nccl_id, sizeof(id));
-        if (ncclCommInitRank(&b->comm, world, id, rank) != ncclSuccess) {
-            b->comm = nullptr;
+        ncclConfig_t ncfg = NCCL_CONFIG_INITIALIZER;
+        ncfg.blocking = 0;  // init and every group end are polled under b->ep_timeout_ms
+        const ncclResult_t r = ncclCommInitRankConfig(&b->comm, world, id, rank, &ncfg);
+        if (r != ncclSuccess && r != ncclInProgress) b->comm = nullptr;
+        if (!b->comm || ep_settle(b, r, "ncclCommInitRankConfig failed")) {
+            const std::string msg = cuinf_last_error();
             cuinf_batch_free(b);
-            return cuinf_set_arg_error("ncclCommInitRank failed");
+            return cuinf_set_arg_error(msg.c_str());
         }
     }
     TRYB(balloc(b, &b->amax, (size_t)B * 8));
@@ -1192,21 +1270,44 @@ extern "C" int cuinf_batch_reset(cuinf_batch* b) {
 
 extern "C" int cuinf_batch_step(cuinf_batch* b, const int* tokens, int* out_tokens) {
     REQUIRE(b && b->exec, "null batch");
+    REQUIRE(!b->ep_failed, "expert-parallel batch was aborted");
     const int B = b->B;
     if (tokens) {
         for (int i = 0; i < B; i++) REQUIRE(tokens[i] >= 0 && tokens[i] < b->m->cfg.vocab, "token out of range");
-        CUINF_TRY(cudaStreamSynchronize(b->st));  // the pinned slot is free
+        BTRY(batch_sync(b));  // the pinned slot is free
         memcpy(b->pinned, tokens, (size_t)B * 4);
         CUINF_TRY(cudaMemcpyAsync(b->tok, b->pinned, (size_t)B * 4, cudaMemcpyHostToDevice, b->st));
     }
     CUINF_TRY(cudaGraphLaunch(b->exec, b->st));
     if (out_tokens) {
         CUINF_TRY(cudaMemcpyAsync(b->pinned + B, b->tok, (size_t)B * 4, cudaMemcpyDeviceToHost, b->st));
-        CUINF_TRY(cudaStreamSynchronize(b->st));
+        BTRY(batch_sync(b));
         memcpy(out_tokens, b->pinned + B, (size_t)B * 4);
     }
     return CUINF_OK;
 }
+
+extern "C" int cuinf_batch_sync(cuinf_batch* b) {
+    REQUIRE(b, "null batch");
+    return batch_sync(b);
+}
+
+extern "C" int cuinf_batch_abort(cuinf_batch* b) {
+    REQUIRE(b, "null batch");
+    if (b->ep_world <= 1) return CUINF_OK;
+    if (b->comm) ncclCommAbort(b->comm);
+    b->comm = nullptr;
+    b->ep_failed = true;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_batch_set_timeout(cuinf_batch* b, int timeout_ms) {
+    REQUIRE(b && timeout_ms > 0, "null batch or non-positive timeout");
+    b->ep_timeout_ms = timeout_ms;
+    return CUINF_OK;
+}
+
+extern "C" int cuinf_batch_failed(const cuinf_batch* b) { return b && b->ep_failed ? 1 : 0; }
 
 extern "C" int cuinf_batch_keep_logits(cuinf_batch* b, int on) {
     REQUIRE(b, "null batch");

@@ -167,15 +167,19 @@ __device__ __forceinline__ void phase_mark(int k, int i) {
 // the flag word (if given) is set and false returned; the caller then skips
 // its math but still waits (bounded) before exiting so no copy targets freed
 // shared memory.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* flag) {
+__device__ __forceinline__ bool mbar_wait_bounded_ns(uint64_t* bar, uint32_t parity, unsigned* flag,
+                                                     uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (int k = 1;; k++) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((k & 7) == 0 && globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) break;
+        if ((k & 7) == 0 && globaltimer_ns() - t0 > limit_ns) break;
     }
     if (flag) atomicOr(flag, 1u);
     return false;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* flag) {
+    return mbar_wait_bounded_ns(bar, parity, flag, CUINF_WAIT_LIMIT_NS);
 }
 // PDL: let the next kernel in the stream start launching, and wait until the
 // previous kernel has completed and its writes are visible.  Both are no-ops

@@ -1829,6 +1829,41 @@ extern "C" int cuinf_device_error(unsigned* flags) {
     return CUINF_OK;
 }
 
+// Failure-path self test: one CTA arms an mbarrier for 16 bytes that no copy
+// will ever deliver and waits on it with the given limit (the same bounded
+// wait every staging kernel uses, there with a 4 s limit).  The wait gives
+// up, records bit 0 in its own word and the kernel returns normally.
+__global__ void k_wait_selftest(unsigned long long limit_ns, unsigned* word, unsigned long long* waited_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    mbar_arrive_expect_tx(&bar, 16);  // arrival done, 16 transaction bytes outstanding forever
+    const uint64_t t0 = globaltimer_ns();
+    const bool ok = mbar_wait_bounded_ns(&bar, 0, word, limit_ns);
+    *waited_ns = globaltimer_ns() - t0;
+    if (ok) atomicOr(word, 2u);  // the phase completed: must not happen
+}
+
+extern "C" int cuinf_selftest_wait_timeout(unsigned limit_us, unsigned* flags, unsigned long long* waited_ns) {
+    REQUIRE(flags && waited_ns, "null pointer");
+    REQUIRE(limit_us > 0 && limit_us <= 2000000u, "limit_us must be in (0, 2 s]");
+    unsigned* d = nullptr;
+    CUINF_TRY(cudaMalloc(&d, 16));
+    cudaError_t e = cudaMemset(d, 0, 16);
+    if (e == cudaSuccess) {
+        k_wait_selftest<<<1, 32>>>((unsigned long long)limit_us * 1000ull, d, (unsigned long long*)(d + 2));
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    unsigned h[4] = {0, 0, 0, 0};
+    if (e == cudaSuccess) e = cudaMemcpy(h, d, 16, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    CUINF_TRY(e);
+    *flags = h[0];
+    memcpy(waited_ns, &h[2], 8);
+    return CUINF_OK;
+}
+
 extern "C" const float* cuinf_session_logits(const cuinf_session* s) { return s ? s->logits : nullptr; }
 extern "C" const void* cuinf_session_hidden(const cuinf_session* s) { return s ? s->hidden : nullptr; }
 

@@ -57,7 +57,7 @@ __device__ __forceinline__ void norm_prologue_fast(const NormW& nw, const __half
     const __half* src = h;
     if (embed) {
         src = embed + (size_t)(*tok) * H;
-        if (blockIdx.x == 0 && blockIdx.y == 0)
+        if (h_store && blockIdx.x == 0 && blockIdx.y == 0)
             for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8)
                 *reinterpret_cast<uint4*>(h_store + i) = *reinterpret_cast<const uint4*>(src + i);
     }

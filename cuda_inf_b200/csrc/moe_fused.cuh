@@ -89,13 +89,18 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 __device__ __forceinline__ void red_add_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
 }
+__device__ __forceinline__ void prefetch_l2_line(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p));
+}
 __device__ __forceinline__ unsigned long long ld_cg_u64(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.global.cg.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
-__global__ void __cluster_dims__(MOEF_CL, 1, 1) __launch_bounds__(MOEF_THREADS) k_moe_fused(MoeFusedParams P) {
+// (4 CTAs per SM, so that a whole grid of topk * I/16 = 448 CTAs is resident
+// at once on 148 SMs: a second wave would hold up every ticket)
+__global__ void __cluster_dims__(MOEF_CL, 1, 1) __launch_bounds__(MOEF_THREADS, 4) k_moe_fused(MoeFusedParams P) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t bar[2];  // [0] router rows, [1] w1/w3 tiles
     __shared__ int s_last;
@@ -216,13 +221,11 @@ __global__ void __cluster_dims__(MOEF_CL, 1, 1) __launch_bounds__(MOEF_THREADS) 
         tma_tile_int4((const uint8_t*)ex[0], (const __half*)ex[1], H, row0, tiles, &bar[1]);
         tma_tile_int4((const uint8_t*)ex[2], (const __half*)ex[3], H, row0, tiles + TB, &bar[1]);
     }
-    for (int j = threadIdx.x; j < rows; j += blockDim.x)
-        prefetch_l2_bulk(w2p + (size_t)(n0 + j) * (I >> 1) + grp * 64, 64);
-    if (threadIdx.x == 32) {
-        // scales of rows [n0, n0 + rows): one contiguous span, 16-byte aligned
-        const uintptr_t b = (uintptr_t)(w2s + (size_t)n0 * (I >> 7)) & ~(uintptr_t)15;
-        const uintptr_t e = ((uintptr_t)(w2s + (size_t)(n0 + rows) * (I >> 7)) + 15) & ~(uintptr_t)15;
-        for (uintptr_t p = b; p < e; p += 65536) prefetch_l2_bulk((const void*)p, (uint32_t)min((uintptr_t)65536, e - p));
+    // (per-thread prefetches through the load/store unit: hundreds of tiny
+    // bulk prefetches would queue ahead of the tile copies in the TMA unit)
+    for (int j = threadIdx.x; j < rows; j += blockDim.x) {
+        prefetch_l2_line(w2p + (size_t)(n0 + j) * (I >> 1) + grp * 64);
+        prefetch_l2_line(w2s + (size_t)(n0 + j) * (I >> 7) + grp);
     }
     PHASE(PH_MOE_UP, 5);
 
@@ -281,15 +284,20 @@ __global__ void __cluster_dims__(MOEF_CL, 1, 1) __launch_bounds__(MOEF_THREADS) 
     __threadfence();
     for (int i = threadIdx.x; i < rows; i += blockDim.x) {
         const int n = n0 + i;
+        long long q[8];  // topk <= 8; fully unrolled so the array stays in registers
+#pragma unroll
+        for (int k = 0; k < 8; k++) q[k] = k < P.topk ? (long long)ld_cg_u64(P.acc + (size_t)k * H + n) : 0ll;
+        const float hn = __half2float(P.h[n]);
         __half acc = __float2half_rn(0.f);
-        for (int k = 0; k < P.topk; k++) {
-            unsigned long long* a = P.acc + (size_t)k * H + n;
-            const long long q = (long long)ld_cg_u64(a);
-            const float o = (float)((double)q * (1.0 / 4294967296.0));
-            acc = __float2half_rn(__half2float(acc) + sw[k] * o);
-            *a = 0ull;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            if (k < P.topk) {
+                const float o = (float)((double)q[k] * (1.0 / 4294967296.0));
+                acc = __float2half_rn(__half2float(acc) + sw[k] * o);
+                P.acc[(size_t)k * H + n] = 0ull;
+            }
         }
-        P.h_out[n] = __float2half_rn(__half2float(P.h[n]) + __half2float(acc));
+        P.h_out[n] = __float2half_rn(hn + __half2float(acc));
     }
     if (threadIdx.x == 0) P.tickets[rank] = 0u;
     PHASE(PH_MOE_UP, 9);

@@ -270,6 +270,23 @@ class Batch:
     def keep_logits(self, on=True):
         check(lib().cuinf_batch_keep_logits(self._h, int(on)))
 
+    def sync(self):
+        """Wait for the queued steps (expert parallel: polling NCCL errors
+        under the batch's time limit)."""
+        check(lib().cuinf_batch_sync(self._h))
+
+    def abort(self):
+        """Abort the expert-parallel communicator (a peer failed); the batch
+        takes no more steps."""
+        check(lib().cuinf_batch_abort(self._h))
+
+    def set_timeout(self, ms):
+        check(lib().cuinf_batch_set_timeout(self._h, int(ms)))
+
+    @property
+    def failed(self):
+        return bool(lib().cuinf_batch_failed(self._h))
+
     def logits(self):
         ptr = lib().cuinf_batch_logits(self._h)
         return torch.as_tensor(_DevArray(ptr, (self.n, self.model.cfg.vocab), "<f4"), device="cuda")

@@ -272,6 +272,27 @@ int cuinf_batch_create_ep(cuinf_model* m, int n_seqs, int max_ctx, void* stream,
                           int rank, int world, cuinf_batch** out);
 int cuinf_ep_unique_id(unsigned char* id, int id_bytes);
 int cuinf_ep_unique_id_bytes(void);
+/* Failure handling of the expert-parallel form (the reference runs on one
+ * GPU and has none).  The communicator is non-blocking: its setup, every
+ * group of sends/receives and every host wait on a step (cuinf_batch_step
+ * with out_tokens or tokens, cuinf_batch_sync) poll NCCL's asynchronous
+ * error state and give up after the batch's time limit (default 120 s,
+ * cuinf_batch_set_timeout).  On an NCCL error or a time-out, or on
+ * cuinf_batch_abort (a host that learned a peer failed), the communicator is
+ * aborted, which releases kernels still waiting for peers; the batch then
+ * refuses further steps (cuinf_batch_failed returns 1) and must be freed. */
+/* The dispatch plan of one MoE layer, on the host (the device computes the
+ * same inside the step): entry j = token j/top_k, slot j%top_k, routed to
+ * expert ridx[j], goes to rank d = ridx[j] / e_loc at position r = the count
+ * of earlier entries for d; dest_pos[j] = d*cap + r and meta[d*cap + r] =
+ * the expert's index on d, -1 where a position is unused.  The expert's
+ * output row returns to back[dest_pos[j]], and token j/top_k combines its
+ * slots in slot order (acc_scaled, engine.cu:900-902). */
+int cuinf_ep_plan_host(const int* ridx, int n, int e_loc, int world, int cap, int* dest_pos, int* meta);
+int cuinf_batch_sync(cuinf_batch* b);
+int cuinf_batch_abort(cuinf_batch* b);
+int cuinf_batch_set_timeout(cuinf_batch* b, int timeout_ms);
+int cuinf_batch_failed(const cuinf_batch* b);
 int cuinf_batch_free(cuinf_batch* b);
 int cuinf_batch_reset(cuinf_batch* b);
 int cuinf_batch_step(cuinf_batch* b, const int* tokens, int* out_tokens);
@@ -367,6 +388,12 @@ int cuinf_session_h2o_state(cuinf_session* s, int layer, int* slot_pos, float* a
 /* Device error flags of the engine kernels (bit 0: a bounded wait on a
  * weight-staging barrier timed out and the kernel skipped its math). */
 int cuinf_device_error(unsigned* flags);
+/* Self test of the failure path of those bounded waits (no counterpart in
+ * the reference, whose kernels have no waits): one CTA arms a barrier for
+ * bytes that never arrive and waits at most limit_us microseconds; flags
+ * receives bit 0 when the wait gave up (expected) and bit 1 if the barrier
+ * completed; waited_ns the time the wait took.  The context stays usable. */
+int cuinf_selftest_wait_timeout(unsigned limit_us, unsigned* flags, unsigned long long* waited_ns);
 /* Per-stage timestamps of the last traced megakernel step: buf receives
  * [n_stages][n_ctas][16]: %globaltimer ns at the stage start, prologue end
  * and end (words 0, 1, 3); SM cycles spent waiting for weight slabs (2); SM cycles
