@@ -314,6 +314,14 @@ struct cuinf_batch {
     __half *send_x = nullptr, *recv_x = nullptr;
     int *send_meta = nullptr, *recv_meta = nullptr, *dest_pos = nullptr;
     float *back_o = nullptr, *recv_back = nullptr;
+    // vocabulary-sharded lm_head (expert-parallel form, logits not kept): this
+    // rank multiplies every rank's final rows by vocabulary rows
+    // [rank*V/world, (rank+1)*V/world); the argmax keys are max-reduced
+    __half* xall = nullptr;            // [world*B][H] final normed rows of all ranks
+    unsigned long long* kall = nullptr;  // [world*B] argmax keys
+    CUtensorMap x_all;
+    int mi_embed_shard = -1;
+    bool vocab_shard = false;
 };
 
 template <class T>
@@ -632,7 +640,7 @@ struct BStep {
 
     // xrows: most activation rows any group of the launch can have
     int gemm(const CUtensorMap& xm, int xbox, int xrows, int wmap_idx, const TcGroup* dg, TcGroup g0, int ngroups,
-             int tiles, int K, int active_ctas, bool fp16w, unsigned long long* amax) {
+             int tiles, int K, int active_ctas, bool fp16w, unsigned long long* amax, int n_base = 0) {
         TcPlan pl = amax ? TcPlan{1, K / TC_KS} : tc_plan(active_ctas, K, b->num_sms);
         REQUIRE(fp16w || pl.kgps <= TC_MAX_KG, "K too large");
         launches++;
@@ -654,6 +662,7 @@ struct BStep {
         P.ws = b->ws;
         P.counters = b->cnt;
         P.amax = amax;
+        P.n_base = n_base;
         const CUtensorMap& wm = wmap_idx >= 0 ? b->hmaps[wmap_idx] : b->hmaps[0];
         return tc_launch(xm, wm, P, tiles, b->st, false);
     }
@@ -943,6 +952,37 @@ static int batch_record(cuinf_batch* b, BStep& S) {
     // final norm, lm_head with the fused argmax (compute_logits_last, engine.cu:932-940)
     BTRY(S.ew(run(cuinf_rmsnorm(b->h, m->emb_norm, b->xn, B, H, c.norm_eps, vs))));
     BTRY(S.mark("rmsnorm_final"));
+    if (b->vocab_shard && !b->keep_logits) {
+        // every rank's final rows, then this rank's vocabulary shard for all
+        // of them, then the max over the ranks' argmax keys (the keys order
+        // by value, then by the reference's tie rule on the global index)
+        const int W = b->ep_world, GB = W * B, Vs = c.vocab / W;
+        if (!dry) {
+            BTRY(ep_settle(b, ncclAllGather(b->xn, b->xall, (size_t)B * H, ncclFloat16, b->comm, b->st),
+                           "NCCL all-gather of the final rows failed"));
+            CUINF_TRY(cudaMemsetAsync(b->kall, 0, (size_t)GB * 8, b->st));
+        }
+        BTRY(S.mark("ep_gather_rows"));
+        TcGroup g = {};
+        g.rows = GB;
+        g.N = Vs;
+        g.ldy = Vs;
+        const int tiles = (Vs + TC_ROWS - 1) / TC_ROWS;
+        BTRY(S.gemm(b->x_all, (GB + 15) & ~15, GB, b->mi_embed_shard, nullptr, g, 1, tiles, H, tiles, true, b->kall,
+                    b->ep_rank * Vs));
+        BTRY(S.mark("lm_head"));
+        if (!dry)
+            BTRY(ep_settle(b, ncclAllReduce(b->kall, b->kall, GB, ncclUint64, ncclMax, b->comm, b->st),
+                           "NCCL all-reduce of the argmax keys failed"));
+        BTRY(S.mark("ep_argmax_reduce"));
+        S.launches++;
+        if (!dry) {
+            k_btok<<<(B + 127) / 128, 128, 0, b->st>>>(b->kall + (size_t)b->ep_rank * B, b->tok, b->pos, B);
+            BTRY(cuinf_launch_status());
+            BTRY(S.mark("next_token"));
+        }
+        return CUINF_OK;
+    }
     if (!dry) CUINF_TRY(cudaMemsetAsync(b->amax, 0, (size_t)B * 8, b->st));
     BTRY(S.gemm1(b->x_h, b->mi_embed, nullptr, b->keep_logits ? b->logits : nullptr, c.vocab, H, true, b->amax));
     BTRY(S.mark("lm_head"));
@@ -1192,6 +1232,20 @@ static int batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, c
         TRYB(tc_map_f16w(&mm, m->embed, c.vocab, H));
         b->mi_embed = (int)b->hmaps.size();
         b->hmaps.push_back(mm);
+    }
+    // the vocabulary shard of this rank (expert-parallel form), when the
+    // shards are equal and every rank's rows fit one GEMM (<= 128 rows)
+    if (world > 1 && c.vocab % world == 0 && (size_t)world * B <= TC_NMAX &&
+        (((uintptr_t)(m->embed + (size_t)rank * (c.vocab / world) * H)) & 15) == 0) {
+        const int Vs = c.vocab / world, GB = world * B;
+        CUtensorMap mm;
+        TRYB(tc_map_f16w(&mm, m->embed + (size_t)rank * Vs * H, Vs, H));
+        b->mi_embed_shard = (int)b->hmaps.size();
+        b->hmaps.push_back(mm);
+        TRYB(balloc(b, &b->xall, (size_t)GB * H * 2));
+        TRYB(balloc(b, &b->kall, (size_t)GB * 8));
+        TRYB(tc_map_act(&b->x_all, b->xall, GB, H, (GB + 15) & ~15));
+        b->vocab_shard = true;
     }
     TRYB(balloc(b, &b->dmaps, b->hmaps.size() * sizeof(CUtensorMap)));
     if (cudaMemcpy(b->dmaps, b->hmaps.data(), b->hmaps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice) !=

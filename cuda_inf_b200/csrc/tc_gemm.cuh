@@ -66,6 +66,7 @@ struct TcParams {
     float* ws;                     // split-K partials [slot][TC_NMAX][TC_ROWS]
     unsigned* counters;            // per (group, tile) arrival counters, self-resetting
     unsigned long long* amax;      // optional per activation row argmax key (lm_head)
+    int n_base;                    // weight row n is vocabulary index n_base + n in the argmax keys
     unsigned* err;
 };
 
@@ -556,7 +557,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         if (c + j >= G.rows) break;
                         if (n < G.N && G.y) G.y[(size_t)(c + j) * G.ldy + n] = v[j];
                         if (P.amax) {
-                            unsigned long long key = n < G.N ? argmax_key(v[j], n) : 0ull;
+                            unsigned long long key = n < G.N ? argmax_key(v[j], P.n_base + n) : 0ull;
 #pragma unroll
                             for (int o = 16; o; o >>= 1) key = umax64_dev(key, __shfl_xor_sync(0xffffffffu, key, o));
                             if (lane == 0) S->amax[q][c + j] = key;

@@ -3,7 +3,8 @@ tests/test_gpu_ep.py through torch.distributed.run, one process per GPU).
 
 Each rank decodes its own sequences with experts sharded across the ranks
 (cuinf_batch_create_ep) and checks every one of them against the CPU oracle,
-teacher-forced, exactly as the single-GPU batch test does.  Prints one line
+teacher-forced, exactly as the single-GPU batch test does; a second batch
+with the vocabulary-sharded lm_head must produce the same tokens.  Prints one line
 "EP rank R: ..." and exits non-zero on a mismatch."""
 import datetime
 import os
@@ -43,9 +44,15 @@ def main():
     toks = np.random.default_rng(4242).integers(0, cfg.vocab, (steps, n_local * world))
     mine = toks[:, rank * n_local:(rank + 1) * n_local]
     states = [om.state(160) for _ in range(n_local)]
+    # a second batch on the same tokens without kept logits: its lm_head is
+    # sharded by vocabulary over the ranks (argmax keys max-reduced), and its
+    # tokens must equal the replicated lm_head's bit for bit
+    bt2 = Batch(gm, n_local, max_ctx=160, ep=(ep_unique_id_shared(), rank, world))  # its own communicator
     worst, checked, near = 0.0, 0, 0
     for i in range(steps):
         got = bt.step(mine[i])
+        got2 = bt2.step(mine[i])
+        assert got2 == got, (rank, i, got, got2)
         routes = bt.routes()
         glog = bt.logits().cpu().numpy()
         for b in range(n_local):
@@ -60,6 +67,7 @@ def main():
     print(f"EP rank {rank}/{world}: {n_local} sequences x {steps} steps, worst logits rel err {worst:.2e}, "
           f"routing checked {checked}, near-ties {near}", flush=True)
     bt.close()  # the step graph holds NCCL calls: release it before the process group
+    bt2.close()
     dist.barrier()
     dist.destroy_process_group()
 
