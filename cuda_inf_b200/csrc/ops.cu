@@ -48,6 +48,10 @@ extern "C" const char* cuinf_version(void) { return "cuinf-b200 0.1 (sm_100a)"; 
 // stages the tile (packed rows + scales) into shared memory with TMA bulk
 // copies while the CTA permutes x into B-fragment order; the 8 warps then
 // take the K groups w, w+8, ... (ragged or unaligned tiles use direct loads).
+// Launched with programmatic stream serialization: the weights (which no
+// earlier kernel writes) are requested before the dependency wait, so a
+// GEMV that follows another kernel streams its tile while that kernel
+// finishes; x is read, and y written, only after the wait.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_gemv_int4(const __half* __restrict__ x,
                                                    const uint8_t* __restrict__ packed,
@@ -68,6 +72,8 @@ __global__ void __launch_bounds__(256) k_gemv_int4(const __half* __restrict__ x,
             tma_tile_int4(packed, scales, K, row0, tile, &bar);
         }
     }
+    pdl_trigger();
+    pdl_wait();
     const __half* xm = x + (size_t)m * K;
     for (int e = threadIdx.x; e < K / 4; e += blockDim.x) build_xB_entry(xm, xB, e);
     __syncthreads();
@@ -108,9 +114,18 @@ extern "C" int cuinf_gemv_int4(const void* x, const uint8_t* packed, const void*
     if (smem > 48 * 1024)
         CUINF_TRY(cudaFuncSetAttribute(k_gemv_int4, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem));
-    dim3 grid((N + 15) / 16, M);
-    k_gemv_int4<<<grid, 256, smem, ST(stream)>>>((const __half*)x, packed, (const __half*)scales,
-                                                 y, N, K, use_tma);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((N + 15) / 16, M);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ST(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CUINF_TRY(cudaLaunchKernelEx(&cfg, k_gemv_int4, (const __half*)x, packed, (const __half*)scales, y, N, K,
+                                 use_tma));
     return cuinf_launch_status();
 }
 

@@ -103,6 +103,9 @@ int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_t* vc8, con
  * must not overlap: issue them on one stream or order them with events;
  * overlapping calls race on the scratch.  The scratch's 256-byte ticket area
  * must start at zero; each call clears it on the stream before its launch.
+ * The looked-up address is kept per device for the life of the process: a
+ * device that uses this entry point must not be reset (cudaDeviceReset)
+ * while the library is loaded, since the array's address may then change.
  * No counterpart in the reference. */
 size_t cuinf_attn_decode_static_scratch_bytes(void);
 int cuinf_attn_decode_noalloc(const void* q, const uint8_t* kc8, const uint8_t* vc8,
