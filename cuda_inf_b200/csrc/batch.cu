@@ -479,6 +479,7 @@ __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
             const int gi = ex * P.maxch + c;
             TcGroup a;
             a.wmap = P.maps + ex * 3 + 0;
+            a.packed = (const uint8_t*)P.experts[ex * 6 + 0];
             a.scales = (const __half*)P.experts[ex * 6 + 1];
             a.y = P.gbuf + (size_t)r0 * P.I;
             a.x_row = r0;
@@ -487,10 +488,12 @@ __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
             a.ldy = P.I;
             P.g13[gi] = a;
             a.wmap = P.maps + ex * 3 + 1;
+            a.packed = (const uint8_t*)P.experts[ex * 6 + 2];
             a.scales = (const __half*)P.experts[ex * 6 + 3];
             a.y = P.ubuf + (size_t)r0 * P.I;
             P.g13[NE * P.maxch + gi] = a;
             a.wmap = P.maps + ex * 3 + 2;
+            a.packed = (const uint8_t*)P.experts[ex * 6 + 4];
             a.scales = (const __half*)P.experts[ex * 6 + 5];
             a.y = P.obuf + (size_t)r0 * P.H;
             a.N = P.H;
@@ -605,6 +608,121 @@ __global__ void k_ep_unpack(const float* __restrict__ fo, const int* __restrict_
     const float4* s = reinterpret_cast<const float4*>(fo + (size_t)r * H);
     float4* d = reinterpret_cast<float4*>(back_o + (size_t)j * H);
     for (int i = threadIdx.x; i < H / 4; i += blockDim.x) d[i] = s[i];
+}
+
+// ---------------------------------------------------------------------------
+// Grouped INT4 GEMV for the batched MoE: every group (an expert's rows of the
+// gathered activations, up to 128) times that expert's weight matrix, 8
+// activation rows per pass.  About top_k*B/E rows reach an expert (8 for 64
+// sequences), far too few to amortise the dequantized 128x128 operand tile of
+// the tensor-core GEMM: here the INT4 tile is dequantized in registers and
+// fed to mma.sync m16n8k16 whose 8 columns are 8 activation rows, so one
+// dequantization serves 8 rows and the kernel streams the weights at the pace
+// of the batch-1 decode kernels.  Per 128-K group the products (nib-8)*x are
+// exact and summed in fp32, then scaled in fp32 (as the reference's gemv_int4
+// sums dequantized products in fp32, engine.cu:83-109).
+// grid (N / (16*G8_TILES), groups), 256 threads: warps 4t..4t+3 take tile t
+// (16 weight rows), each a quarter of the K groups.
+// ---------------------------------------------------------------------------
+#define G8_TILES 2
+__host__ __device__ inline size_t g8_smem(int K) {
+    return (size_t)G8_TILES * int4_tile_bytes(K) + (size_t)K * 16 + 8 * 16 * 8 * 4;
+}
+__global__ void __launch_bounds__(256) k_grouped_gemv8(const TcGroup* __restrict__ groups, const __half* __restrict__ x,
+                                                       int ldx, int K, unsigned* err) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ uint64_t bar;
+    const TcGroup G = groups[blockIdx.y];
+    const int rbase = blockIdx.x * 16 * G8_TILES;
+    if (G.rows <= 0 || rbase >= G.N) return;
+    const uint32_t TB = int4_tile_bytes(K);
+    uint2* xb = reinterpret_cast<uint2*>(smem + G8_TILES * TB);  // [K/16][32] B fragments of 8 rows
+    float* red = reinterpret_cast<float*>(smem + G8_TILES * TB + (size_t)K * 16);  // [8][16][8]
+    const int ntile = min(G8_TILES, (G.N - rbase) / 16);
+    if (threadIdx.x == 0) mbar_init(&bar, 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar, ntile * TB);
+        for (int t = 0; t < ntile; t++) tma_tile_int4(G.packed, G.scales, K, rbase + 16 * t, smem + t * TB, &bar);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int tile = warp >> 2, q = warp & 3, KG = K >> 7, KH = K >> 1;
+    bool ok = true;
+    for (int p0 = 0; p0 < G.rows; p0 += 8) {
+        const int np = min(8, G.rows - p0);
+        // B fragments: entry (group Gk, mma m, lane 4g+c) = row g's x[k], x[k+4],
+        // x[k+1], x[k+5], k = 128Gk + 32c + 8(m/2) + 2(m%2); zero past np rows
+        for (int e = threadIdx.x; e < (K >> 4) * 32; e += blockDim.x) {
+            const int ln = e & 31, gm = e >> 5, m = gm & 7, Gk = gm >> 3, rg = ln >> 2, cq = ln & 3;
+            const int k = 128 * Gk + 32 * cq + 8 * (m >> 1) + ((m & 1) ? 2 : 0);
+            uint2 v = make_uint2(0u, 0u);
+            if (rg < np) {
+                const __half* xr = x + (size_t)(G.x_row + p0 + rg) * ldx + k;
+                const __half2 lo = __halves2half2(xr[0], xr[4]), hi = __halves2half2(xr[1], xr[5]);
+                v.x = *reinterpret_cast<const uint32_t*>(&lo);
+                v.y = *reinterpret_cast<const uint32_t*>(&hi);
+            }
+            xb[e] = v;
+        }
+        __syncthreads();
+        if (p0 == 0) ok = mbar_wait_bounded(&bar, 0, err);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (ok && tile < ntile) {
+            const uint8_t* tb = smem + tile * TB;
+            const uint8_t* pa = tb + g * KH + c * 16;
+            const uint8_t* pb = tb + (g + 8) * KH + c * 16;
+            const __half* sc = reinterpret_cast<const __half*>(tb + 16 * KH);
+            for (int Gk = q; Gk < KG; Gk += 4) {
+                const uint4 wa = *reinterpret_cast<const uint4*>(pa + Gk * 64);
+                const uint4 wb = *reinterpret_cast<const uint4*>(pb + Gk * 64);
+                const float fa = __half2float(sc[g * KG + Gk]), fb = __half2float(sc[(g + 8) * KG + Gk]);
+                const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w}, wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+                float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    uint32_t ha[4], hb[4];
+                    dequant8(wav[j], ha);
+                    dequant8(wbv[j], hb);
+                    const uint2 b0 = xb[(Gk * 8 + 2 * j) * 32 + lane], b1 = xb[(Gk * 8 + 2 * j + 1) * 32 + lane];
+                    mma_16816(d, ha[0], hb[0], ha[1], hb[1], b0.x, b0.y);
+                    mma_16816(d, ha[2], hb[2], ha[3], hb[3], b1.x, b1.y);
+                }
+                acc[0] = fmaf(fa, d[0], acc[0]);
+                acc[1] = fmaf(fa, d[1], acc[1]);
+                acc[2] = fmaf(fb, d[2], acc[2]);
+                acc[3] = fmaf(fb, d[3], acc[3]);
+            }
+        }
+        // red[warp][row][token]: row g / g+8 of the warp's tile, tokens 2c, 2c+1
+        red[(warp * 16 + g) * 8 + 2 * c] = acc[0];
+        red[(warp * 16 + g) * 8 + 2 * c + 1] = acc[1];
+        red[(warp * 16 + g + 8) * 8 + 2 * c] = acc[2];
+        red[(warp * 16 + g + 8) * 8 + 2 * c + 1] = acc[3];
+        __syncthreads();
+        for (int i = threadIdx.x; i < ntile * 128; i += blockDim.x) {
+            const int t = i >> 7, r = (i >> 3) & 15, tok = i & 7;
+            if (tok < np) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < 4; w++) v += red[((4 * t + w) * 16 + r) * 8 + tok];
+                G.y[(size_t)(p0 + tok) * G.ldy + rbase + 16 * t + r] = v;
+            }
+        }
+        __syncthreads();  // xb and red are rebuilt by the next pass
+    }
+}
+
+// Shapes the grouped small-row GEMV takes (whole 32-row CTA tiles, and its
+// shared memory within one SM's limit).
+static bool g8_fits(int H, int I) {
+    return H % (16 * G8_TILES) == 0 && I % (16 * G8_TILES) == 0 && H % 128 == 0 && I % 128 == 0 &&
+           g8_smem(std::max(H, I)) <= 227 * 1024;
+}
+static int g8_attr_once() {
+    static cudaError_t e = cudaFuncSetAttribute(k_grouped_gemv8, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                227 * 1024);
+    if (e != cudaSuccess) return cuinf_set_cuda_error(e);
+    return CUINF_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -909,18 +1027,38 @@ static int batch_record(cuinf_batch* b, BStep& S) {
                 }
             }
             S.launches++;
-            const int t13 = (I + TC_ROWS - 1) / TC_ROWS, t2 = (H + TC_ROWS - 1) / TC_ROWS;
-            // about min(experts, rows) experts are hit; each group is one tile row of CTAs
-            const int hit = std::min(EL, NR);
-            // an expert's group holds at most one row per token of every rank
-            const int grows = B * b->ep_world;
-            BTRY(S.gemm(b->x_xg, 16, grows, -1, b->g13, TcGroup{}, 2 * EL * mch, t13, H, 2 * hit * t13, false,
-                        nullptr));
-            BTRY(S.mark("gemm_moe_w13"));
-            BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->mmid, NR * I, vs))));
-            BTRY(S.mark("swiglu_moe"));
-            BTRY(S.gemm(b->x_mmid, 16, grows, -1, b->g2, TcGroup{}, EL * mch, t2, I, hit * t2, false, nullptr));
-            BTRY(S.mark("gemm_moe_w2"));
+            if (g8_fits(H, I)) {
+                // few rows per expert: the grouped small-row GEMV (k_grouped_gemv8)
+                S.launches++;
+                if (!dry) {
+                    k_grouped_gemv8<<<dim3(I / (16 * G8_TILES), 2 * EL * mch), 256, g8_smem(H), b->st>>>(
+                        b->g13, b->xg, H, H, g_tc_err_ptr);
+                    BTRY(cuinf_launch_status());
+                }
+                BTRY(S.mark("gemv8_moe_w13"));
+                BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->mmid, NR * I, vs))));
+                BTRY(S.mark("swiglu_moe"));
+                S.launches++;
+                if (!dry) {
+                    k_grouped_gemv8<<<dim3(H / (16 * G8_TILES), EL * mch), 256, g8_smem(I), b->st>>>(
+                        b->g2, b->mmid, I, I, g_tc_err_ptr);
+                    BTRY(cuinf_launch_status());
+                }
+                BTRY(S.mark("gemv8_moe_w2"));
+            } else {
+                const int t13 = (I + TC_ROWS - 1) / TC_ROWS, t2 = (H + TC_ROWS - 1) / TC_ROWS;
+                // about min(experts, rows) experts are hit; each group is one tile row of CTAs
+                const int hit = std::min(EL, NR);
+                // an expert's group holds at most one row per token of every rank
+                const int grows = B * b->ep_world;
+                BTRY(S.gemm(b->x_xg, 16, grows, -1, b->g13, TcGroup{}, 2 * EL * mch, t13, H, 2 * hit * t13, false,
+                            nullptr));
+                BTRY(S.mark("gemm_moe_w13"));
+                BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->mmid, NR * I, vs))));
+                BTRY(S.mark("swiglu_moe"));
+                BTRY(S.gemm(b->x_mmid, 16, grows, -1, b->g2, TcGroup{}, EL * mch, t2, I, hit * t2, false, nullptr));
+                BTRY(S.mark("gemm_moe_w2"));
+            }
             const float* ob = b->fo;
             const int* oi = b->inv;
             if (ep) {
@@ -1016,6 +1154,7 @@ static int batch_build_graph(cuinf_batch* b) {
         b->cnt_n = D.need_cnt;
     }
     BTRY(tc_attr_once());
+    BTRY(g8_attr_once());
     CUINF_TRY(cudaStreamSynchronize(b->st));
     BStep R{b, false};
     CUINF_TRY(cudaStreamBeginCapture(b->st, cudaStreamCaptureModeThreadLocal));
@@ -1262,14 +1401,14 @@ static int batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, c
             float* qf = b->fqkv;
             float* kf = qf + (size_t)B * NQ;
             float* vf = kf + (size_t)B * NK;
-            st.push_back(TcGroup{b->dmaps + b->mi_q[l], L.wq.s, qf, 0, B, NQ, NQ});
-            st.push_back(TcGroup{b->dmaps + b->mi_k[l], L.wk.s, kf, 0, B, NK, NK});
-            st.push_back(TcGroup{b->dmaps + b->mi_v[l], L.wv.s, vf, 0, B, NK, NK});
+            st.push_back(TcGroup{b->dmaps + b->mi_q[l], L.wq.p, L.wq.s, qf, 0, B, NQ, NQ});
+            st.push_back(TcGroup{b->dmaps + b->mi_k[l], L.wk.p, L.wk.s, kf, 0, B, NK, NK});
+            st.push_back(TcGroup{b->dmaps + b->mi_v[l], L.wv.p, L.wv.s, vf, 0, B, NK, NK});
         }
         if (l < c.n_dense) {
             b->d13_tab[l] = (int)st.size();
-            st.push_back(TcGroup{b->dmaps + b->mi_w1[l], L.w1.s, b->fg, 0, B, ID, ID});
-            st.push_back(TcGroup{b->dmaps + b->mi_w3[l], L.w3.s, b->fu, 0, B, ID, ID});
+            st.push_back(TcGroup{b->dmaps + b->mi_w1[l], L.w1.p, L.w1.s, b->fg, 0, B, ID, ID});
+            st.push_back(TcGroup{b->dmaps + b->mi_w3[l], L.w3.p, L.w3.s, b->fu, 0, B, ID, ID});
         }
     }
     if (!st.empty()) {

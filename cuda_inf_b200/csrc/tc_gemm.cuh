@@ -45,6 +45,7 @@
 
 struct TcGroup {
     const CUtensorMap* wmap;  // weights (global-memory tensor map); null = the launch's own map
+    const uint8_t* packed;    // the same weights' packed rows (the grouped small-row GEMV reads them)
     const __half* scales;     // [N, K/128] for INT4 weights
     float* y;                 // y[j * ldy + n], j < rows
     int x_row;                // first activation row in the activation tensor map
