@@ -625,53 +625,57 @@ __global__ void k_ep_unpack(const float* __restrict__ fo, const int* __restrict_
 // (16 weight rows), each a quarter of the K groups.
 // ---------------------------------------------------------------------------
 #define G8_TILES 2
+// x rows in shared memory at a pitch of 32 mod 128 bytes: the 16-byte loads
+// of one 8-lane phase (rows g, g+1; chunks c = 0..3) then hit at most two
+// lanes per 16-byte bank slot.
+__host__ __device__ inline unsigned g8_pitch(int K) {
+    const unsigned b = 2u * (unsigned)K;
+    return b + ((32u - (b & 127u)) & 127u);
+}
 __host__ __device__ inline size_t g8_smem(int K) {
-    return (size_t)G8_TILES * int4_tile_bytes(K) + (size_t)K * 16 + 8 * 16 * 8 * 4;
+    return (size_t)G8_TILES * int4_tile_bytes(K) + (size_t)8 * g8_pitch(K) + 8 * 16 * 8 * 4;
 }
 __global__ void __launch_bounds__(256) k_grouped_gemv8(const TcGroup* __restrict__ groups, const __half* __restrict__ x,
                                                        int ldx, int K, unsigned* err) {
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ uint64_t bar;
+    __shared__ uint64_t bar_w, bar_x;
     const TcGroup G = groups[blockIdx.y];
     const int rbase = blockIdx.x * 16 * G8_TILES;
     if (G.rows <= 0 || rbase >= G.N) return;
-    const uint32_t TB = int4_tile_bytes(K);
-    uint2* xb = reinterpret_cast<uint2*>(smem + G8_TILES * TB);  // [K/16][32] B fragments of 8 rows
-    float* red = reinterpret_cast<float*>(smem + G8_TILES * TB + (size_t)K * 16);  // [8][16][8]
+    const uint32_t TB = int4_tile_bytes(K), XP = g8_pitch(K), XB = 2u * (uint32_t)K;
+    uint8_t* xs = smem + G8_TILES * TB;                                              // [8][XP] x rows
+    float* red = reinterpret_cast<float*>(smem + G8_TILES * TB + (size_t)8 * XP);  // [8][16][8]
     const int ntile = min(G8_TILES, (G.N - rbase) / 16);
-    if (threadIdx.x == 0) mbar_init(&bar, 1);
-    __syncthreads();
     if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(&bar, ntile * TB);
-        for (int t = 0; t < ntile; t++) tma_tile_int4(G.packed, G.scales, K, rbase + 16 * t, smem + t * TB, &bar);
+        mbar_init(&bar_w, 1);
+        mbar_init(&bar_x, 1);
+        mbar_arrive_expect_tx(&bar_w, ntile * TB);
+        for (int t = 0; t < ntile; t++) tma_tile_int4(G.packed, G.scales, K, rbase + 16 * t, smem + t * TB, &bar_w);
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const int tile = warp >> 2, q = warp & 3, KG = K >> 7, KH = K >> 1;
     bool ok = true;
-    for (int p0 = 0; p0 < G.rows; p0 += 8) {
+    int pass = 0;
+    for (int p0 = 0; p0 < G.rows; p0 += 8, pass++) {
         const int np = min(8, G.rows - p0);
-        // B fragments: entry (group Gk, mma m, lane 4g+c) = row g's x[k], x[k+4],
-        // x[k+1], x[k+5], k = 128Gk + 32c + 8(m/2) + 2(m%2); zero past np rows
-        for (int e = threadIdx.x; e < (K >> 4) * 32; e += blockDim.x) {
-            const int ln = e & 31, gm = e >> 5, m = gm & 7, Gk = gm >> 3, rg = ln >> 2, cq = ln & 3;
-            const int k = 128 * Gk + 32 * cq + 8 * (m >> 1) + ((m & 1) ? 2 : 0);
-            uint2 v = make_uint2(0u, 0u);
-            if (rg < np) {
-                const __half* xr = x + (size_t)(G.x_row + p0 + rg) * ldx + k;
-                const __half2 lo = __halves2half2(xr[0], xr[4]), hi = __halves2half2(xr[1], xr[5]);
-                v.x = *reinterpret_cast<const uint32_t*>(&lo);
-                v.y = *reinterpret_cast<const uint32_t*>(&hi);
-            }
-            xb[e] = v;
+        if (threadIdx.x == 0) {
+            // this pass's activation rows (rows past np keep stale values: their
+            // mma columns are independent of the others and are never stored)
+            mbar_arrive_expect_tx(&bar_x, np * XB);
+            for (int r = 0; r < np; r++)
+                tma_load_1d(xs + r * XP, x + (size_t)(G.x_row + p0 + r) * ldx, XB, &bar_x);
         }
-        __syncthreads();
-        if (p0 == 0) ok = mbar_wait_bounded(&bar, 0, err);
+        __syncthreads();  // barrier inits are visible before anyone waits
+        if (pass == 0) ok = mbar_wait_bounded(&bar_w, 0, err);
+        ok = mbar_wait_bounded(&bar_x, pass & 1, err) && ok;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         if (ok && tile < ntile) {
             const uint8_t* tb = smem + tile * TB;
             const uint8_t* pa = tb + g * KH + c * 16;
             const uint8_t* pb = tb + (g + 8) * KH + c * 16;
             const __half* sc = reinterpret_cast<const __half*>(tb + 16 * KH);
+            // lane (g, c) feeds x row g, k = 128Gk + 32c + 8j .. +7 for mma pair j
+            const uint8_t* xr = xs + g * XP + c * 64;
             for (int Gk = q; Gk < KG; Gk += 4) {
                 const uint4 wa = *reinterpret_cast<const uint4*>(pa + Gk * 64);
                 const uint4 wb = *reinterpret_cast<const uint4*>(pb + Gk * 64);
@@ -683,9 +687,13 @@ __global__ void __launch_bounds__(256) k_grouped_gemv8(const TcGroup* __restrict
                     uint32_t ha[4], hb[4];
                     dequant8(wav[j], ha);
                     dequant8(wbv[j], hb);
-                    const uint2 b0 = xb[(Gk * 8 + 2 * j) * 32 + lane], b1 = xb[(Gk * 8 + 2 * j + 1) * 32 + lane];
-                    mma_16816(d, ha[0], hb[0], ha[1], hb[1], b0.x, b0.y);
-                    mma_16816(d, ha[2], hb[2], ha[3], hb[3], b1.x, b1.y);
+                    // x[k..k+7] as words (k,k+1) (k+2,k+3) (k+4,k+5) (k+6,k+7);
+                    // the fragments want (k,k+4) (k+1,k+5) and (k+2,k+6) (k+3,k+7)
+                    const uint4 xv = *reinterpret_cast<const uint4*>(xr + Gk * 256 + j * 16);
+                    mma_16816(d, ha[0], hb[0], ha[1], hb[1], __byte_perm(xv.x, xv.z, 0x5410),
+                              __byte_perm(xv.x, xv.z, 0x7632));
+                    mma_16816(d, ha[2], hb[2], ha[3], hb[3], __byte_perm(xv.y, xv.w, 0x5410),
+                              __byte_perm(xv.y, xv.w, 0x7632));
                 }
                 acc[0] = fmaf(fa, d[0], acc[0]);
                 acc[1] = fmaf(fa, d[1], acc[1]);
@@ -708,19 +716,20 @@ __global__ void __launch_bounds__(256) k_grouped_gemv8(const TcGroup* __restrict
                 G.y[(size_t)(p0 + tok) * G.ldy + rbase + 16 * t + r] = v;
             }
         }
-        __syncthreads();  // xb and red are rebuilt by the next pass
+        __syncthreads();  // xs and red are refilled by the next pass
     }
 }
 
 // Shapes the grouped small-row GEMV takes (whole 32-row CTA tiles, and its
 // shared memory within one SM's limit).
+#define G8_SMEM_MAX (200 * 1024)
 static bool g8_fits(int H, int I) {
     return H % (16 * G8_TILES) == 0 && I % (16 * G8_TILES) == 0 && H % 128 == 0 && I % 128 == 0 &&
-           g8_smem(std::max(H, I)) <= 227 * 1024;
+           g8_smem(std::max(H, I)) <= G8_SMEM_MAX;
 }
 static int g8_attr_once() {
     static cudaError_t e = cudaFuncSetAttribute(k_grouped_gemv8, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                227 * 1024);
+                                                G8_SMEM_MAX);
     if (e != cudaSuccess) return cuinf_set_cuda_error(e);
     return CUINF_OK;
 }
