@@ -646,13 +646,15 @@ def run_batched(a, ws, rank, model, cfg):
     tot = sum(v[1] for v in agg.values())
     err = Batch.error()
     kps = bt.kernels_per_step
+    exch = bt.exchange
     bt.close()  # its step graph holds NCCL calls: released before the process group
     step_flops = 2.0 * a.batch * (linear_macs_per_token(cfg) + cfg.vocab * cfg.hidden)
     tf_gpu = step_flops / (ms / a.batch_steps / 1e3) / 1e12 / ws
     tpeak, tkind = tensor_peak(sustained=True)
     return {
         "workload": f"config 5: {a.batch} sequences at context {ctx}, batched decode",
-        "parallelism": f"expert-parallel x{ws} ({cfg.n_experts // ws} experts per GPU, NCCL send/recv)"
+        "parallelism": f"expert-parallel x{ws} ({cfg.n_experts // ws} experts per GPU, rows exchanged by "
+                       f"{'peer-memory stores over NVLink' if exch == 'peer_memory' else 'NCCL send/recv'})"
                        if ws > 1 else "single GPU, all experts local",
         "value": round(a.batch * a.batch_steps / (ms / 1e3), 1), "unit": "tok/s",
         "ms_per_step": round(ms / a.batch_steps, 4), "steps": a.batch_steps, "warmup": a.batch_warmup,
@@ -808,7 +810,7 @@ PHASES = {  # kernel id (csrc/common.cuh PH_*) -> (name, {slot: phase reached})
     2: ("k_conv_in", {0: "start", 1: "dependency wait done", 2: "norm done", 4: "dot done", 9: "end"}),
     3: ("k_ffn_up", {0: "start", 1: "dependency wait done", 2: "norm done", 4: "dot done", 9: "end"}),
     4: ("k_moe_fused", {0: "start", 1: "dependency wait done", 2: "norm done", 3: "logits exchanged",
-                        4: "experts selected", 5: "expert weights requested", 6: "w1/w3 dot done",
+                        10: "sigmoids done (warp 0)", 4: "experts selected", 5: "expert weights requested", 6: "w1/w3 dot done",
                         7: "SwiGLU values gathered (cluster)", 8: "w2 partial added, ticket taken",
                         9: "eighth finalized (last cluster)"}),
     5: ("k_moe_down", {0: "start", 1: "dependency wait done", 2: "mid staged", 4: "cluster sum done",

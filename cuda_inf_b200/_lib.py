@@ -119,6 +119,8 @@ _SIGS = {
     "cuinf_batch_abort": (c_int, [c_void_p]),
     "cuinf_batch_set_timeout": (c_int, [c_void_p, c_int]),
     "cuinf_batch_failed": (c_int, [c_void_p]),
+    "cuinf_batch_ep_exchange": (c_int, [c_void_p]),
+    "cuinf_batch_set_ep_exchange": (c_int, [c_void_p, c_int]),
     "cuinf_device_error": (c_int, [ctypes.POINTER(ctypes.c_uint)]),
     "cuinf_selftest_wait_timeout": (c_int, [ctypes.c_uint, ctypes.POINTER(ctypes.c_uint),
                                             ctypes.POINTER(ctypes.c_ulonglong)]),

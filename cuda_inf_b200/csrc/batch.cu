@@ -266,6 +266,19 @@ extern "C" int cuinf_argmax_key_index(unsigned long long key) {
 #include "model.h"
 #include "route.cuh"
 
+// Peer-memory exchange of the expert-parallel batch (kernels below).
+#define EP_MAX_WORLD 8
+struct EpLinks {
+    char* base[EP_MAX_WORLD];  // every rank's exchange arena as mapped in this process (own included)
+    size_t off_x, off_meta, off_back, off_flag;
+    int rank, world, cap, H;
+};
+struct EpWait {
+    const unsigned long long* flags;  // this rank's flags row ([0] dispatch or [1] return); null: no wait
+    const unsigned long long* step;   // the device step counter
+    int world, tag;                   // tag: 2 * MoE layer + direction
+    unsigned* err;                    // bit 2: a peer's flag did not come within the wait limit
+};
 struct cuinf_batch {
     cuinf_model* m = nullptr;
     int B = 0, max_ctx = 0, num_sms = 148;
@@ -314,6 +327,13 @@ struct cuinf_batch {
     __half *send_x = nullptr, *recv_x = nullptr;
     int *send_meta = nullptr, *recv_meta = nullptr, *dest_pos = nullptr;
     float *back_o = nullptr, *recv_back = nullptr;
+    // peer-memory exchange (the default when every peer's arena maps here;
+    // otherwise the rows travel by NCCL send/recv through the buffers above)
+    bool p2p = false, p2p_ok = false;
+    EpLinks links = {};
+    std::vector<void*> peer_open;         // the peers' arenas opened in this process
+    unsigned long long* ep_step = nullptr;  // device step counter of the flag values
+    unsigned* ep_ticket = nullptr;          // [2] tickets of the sending kernels
     // vocabulary-sharded lm_head (expert-parallel form, logits not kept): this
     // rank multiplies every rank's final rows by vocabulary rows
     // [rank*V/world, (rank+1)*V/world); the argmax keys are max-reduced
@@ -406,6 +426,124 @@ __global__ void k_bconv(const float* __restrict__ z, const __half* __restrict__ 
     sb[H + c] = Bx;
 }
 
+// ---------------------------------------------------------------------------
+// Expert-parallel exchange through peer memory.  Every rank exports one
+// "exchange arena" (cudaIpc) that the others map:
+//   rx_x    [world][cap][H] fp16   rows sent to this rank, segment p from rank p
+//   rx_meta [world][cap]    int    their local expert index (-1: unused slot)
+//   rx_back [world][cap][H] fp32   expert outputs returned to this rank, segment d from rank d
+//   flags   [2][world]      u64    arrival flags: [0][p] rows from p, [1][d] outputs from d
+// A sender writes its rows straight into the receivers' arenas over NVLink
+// (plain stores, no bulk copies), fences, and the last of its CTAs (atomic
+// ticket) raises its flag in every receiver with a system-scope release
+// store.  The receiver's next kernel waits (bounded) for every peer's flag
+// with acquire loads.  Flag values grow monotonically: (step << 8) + 2 *
+// (MoE layer) + 1 (+1 for returns), the step counter advanced on the device
+// at the start of every step.  One buffer per direction suffices: a rank can
+// send layer L+1's rows only after it has every peer's outputs of layer L,
+// which each peer returns only after it has consumed layer L's rows (and
+// read its metadata); likewise for the returned outputs.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned long long ep_flag_value(unsigned long long step, int tag) {
+    return (step << 8) + (unsigned long long)tag + 1ull;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+// One thread: wait until every peer's flag reached this step's value, at
+// most CUINF_WAIT_LIMIT_NS in total; on time-out set the error bit and return
+// (the kernel then runs on stale rows; the host reports the error).
+__device__ void ep_wait_flags(const EpWait& W) {
+    if (*(volatile unsigned*)W.err & 4u) return;  // an earlier wait gave up: do not wait again
+    const unsigned long long want = ep_flag_value(*W.step, W.tag);
+    const unsigned long long t0 = globaltimer_ns();
+    for (int p = 0; p < W.world; p++) {
+        while (ld_acquire_sys_u64(W.flags + p) < want) {
+            if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) {
+                atomicOr(W.err, 4u);
+                return;
+            }
+            __nanosleep(32);
+        }
+    }
+}
+// Every CTA of a sending kernel ends here: fence its stores, take a ticket;
+// the last CTA raises this rank's flag (row `dir`) in every rank's arena.
+__device__ void ep_send_done(const EpLinks& L, unsigned* ticket, const unsigned long long* step, int tag, int dir) {
+    __shared__ bool last;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const unsigned long long v = ep_flag_value(*step, tag);
+        for (int d = 0; d < L.world; d++)
+            st_release_sys_u64(reinterpret_cast<unsigned long long*>(L.base[d] + L.off_flag) + dir * L.world + L.rank,
+                               v);
+        *ticket = 0u;  // the next sending kernel starts after this one ends (stream order)
+    }
+}
+// Dispatch of this rank's (token, slot) entries (n = B * topk): entry j goes
+// to rank d = expert / e_loc at position rank-of-j among the entries for d
+// (the plan of cuinf_ep_plan_host); its row xn[j / topk] and the expert's
+// local index are written into d's arena at segment `rank`.  CTAs n..n+world-1
+// mark the unused slots of each receiver's segment with -1.
+// grid n + world, 256 threads.
+__global__ void __launch_bounds__(256) k_ep_send(EpLinks L, const int* __restrict__ ridx, int n, int e_loc,
+                                                 const __half* __restrict__ xn, int topk, int* dest_pos,
+                                                 unsigned* ticket, const unsigned long long* step, int tag) {
+    __shared__ int s_cnt;
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    const bool entry = (int)blockIdx.x < n;
+    const int d = entry ? ridx[blockIdx.x] / e_loc : (int)blockIdx.x - n;
+    const int lim = entry ? (int)blockIdx.x : n;  // count the entries for d before j (or all of them)
+    int c = 0;
+    for (int i = threadIdx.x; i < lim; i += blockDim.x) c += ridx[i] / e_loc == d;
+    if (c) atomicAdd(&s_cnt, c);
+    __syncthreads();
+    const int pos = s_cnt;
+    int* meta = reinterpret_cast<int*>(L.base[d] + L.off_meta) + (size_t)L.rank * L.cap;
+    if (entry) {
+        const int j = blockIdx.x;
+        if (threadIdx.x == 0) {
+            dest_pos[j] = d * L.cap + pos;
+            meta[pos] = ridx[j] - d * e_loc;
+        }
+        const uint4* s = reinterpret_cast<const uint4*>(xn + (size_t)(j / topk) * L.H);
+        uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(L.base[d] + L.off_x) +
+                                            ((size_t)L.rank * L.cap + pos) * L.H);
+        for (int i = threadIdx.x; i < L.H / 8; i += blockDim.x) o[i] = s[i];
+    } else {
+        for (int i = pos + threadIdx.x; i < L.cap; i += blockDim.x) meta[i] = -1;
+    }
+    ep_send_done(L, ticket, step, tag, 0);
+}
+// Return of the expert outputs: slot i of this rank's received rows (from
+// rank p = i / cap, its position i % cap) goes back to p's arena at segment
+// `rank`, same position.  grid world * cap, 256 threads.
+__global__ void __launch_bounds__(256) k_ep_send_back(EpLinks L, const float* __restrict__ fo,
+                                                      const int* __restrict__ inv, unsigned* ticket,
+                                                      const unsigned long long* step, int tag) {
+    const int i = blockIdx.x, p = i / L.cap, pos = i - p * L.cap;
+    const int r = inv[i];
+    if (r >= 0) {
+        const float4* s = reinterpret_cast<const float4*>(fo + (size_t)r * L.H);
+        float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(L.base[p] + L.off_back) +
+                                              ((size_t)L.rank * L.cap + pos) * L.H);
+        for (int k = threadIdx.x; k < L.H / 4; k += blockDim.x) o[k] = s[k];
+    }
+    ep_send_done(L, ticket, step, tag, 1);
+}
+__global__ void k_ep_tick(unsigned long long* step) { *step += 1ull; }
+
 // MoE routing of B tokens (engine.cu:883-892, one warp per token) and the
 // expert grouping: rows of the gathered activation buffer are ordered by
 // expert, then by token; each expert's rows form up to maxch groups of 128.
@@ -429,10 +567,15 @@ struct BRouteParams {
     const CUtensorMap* maps;  // [n_local][3]: w1, w3, w2
     void* const* experts;     // [n_local][6]: w1 packed, w1 scales, w3 .., w2 ..
     float *gbuf, *ubuf, *obuf;
+    EpWait wait;  // expert-parallel peer exchange: the rows' arrival (flags null: none)
 };
 __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
     __shared__ int sidx[1024];
     __shared__ int cnt[256], off[256];
+    if (P.wait.flags) {
+        if (threadIdx.x == 0) ep_wait_flags(P.wait);
+        __syncthreads();
+    }
     const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int n = P.keys ? P.n : P.B * P.topk, NE = P.keys ? P.n_local : P.E;
     for (int e = threadIdx.x; e < NE; e += blockDim.x) cnt[e] = 0;
@@ -445,7 +588,7 @@ __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
     // rank of entry j among the entries of its expert that come before it
     int e = -1, rank = 0;
     if (threadIdx.x < n) {
-        e = P.keys ? P.keys[threadIdx.x] : P.ridx[threadIdx.x];
+        e = P.keys ? __ldcg(P.keys + threadIdx.x) : P.ridx[threadIdx.x];  // keys: written by peers (L2 loads)
         sidx[threadIdx.x] = e;
     }
     __syncthreads();
@@ -513,13 +656,17 @@ __global__ void k_bgather(const __half* __restrict__ xn, const int* __restrict__
 // h[b] += sum over slots in order: acc = half(acc + w_t * o_t) (acc_scaled),
 // then h = half(h + acc) (add_inplace), engine.cu:894-904.
 __global__ void k_bcombine(const float* __restrict__ obuf, const int* __restrict__ inv, const float* __restrict__ rw,
-                           __half* h, int B, int H, int topk) {
+                           __half* h, int B, int H, int topk, EpWait wait) {
+    if (wait.flags) {  // expert-parallel: the peers' outputs have arrived
+        if (threadIdx.x == 0) ep_wait_flags(wait);
+        __syncthreads();
+    }
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= B * H) return;
     const int b = i / H, c = i - b * H;
     __half acc = __float2half_rn(0.f);
-    for (int t = 0; t < topk; t++)
-        acc = __float2half_rn(__half2float(acc) + rw[b * topk + t] * obuf[(size_t)inv[b * topk + t] * H + c]);
+    for (int t = 0; t < topk; t++)  // (L2 loads: rows another GPU wrote during this kernel's wait)
+        acc = __float2half_rn(__half2float(acc) + rw[b * topk + t] * __ldcg(obuf + (size_t)inv[b * topk + t] * H + c));
     h[i] = __float2half_rn(__half2float(h[i]) + __half2float(acc));
 }
 
@@ -871,6 +1018,13 @@ static int batch_record(cuinf_batch* b, BStep& S) {
     void* vs = (void*)b->st;
     const bool dry = S.dry;
     auto run = [&](int rc) { return dry ? CUINF_OK : rc; };
+    if (b->p2p) {
+        S.launches++;
+        if (!dry) {
+            k_ep_tick<<<1, 1, 0, b->st>>>(b->ep_step);
+            BTRY(cuinf_launch_status());
+        }
+    }
     BTRY(S.ew(run(cuinf_embed_gather(m->embed, b->tok, b->h, B, H, vs))));
     BTRY(S.mark("embed"));
     int moe_i = 0;
@@ -966,7 +1120,7 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             const int mch = (NR + TC_NMAX - 1) / TC_NMAX;
             BTRY(S.ew(run(cuinf_gemv_fp16(b->xn, L.gate, b->rlog, B, E, H, vs))));
             BTRY(S.mark("router_gemv"));
-            BRouteParams R;
+            BRouteParams R = {};
             R.logits = b->rlog;
             R.bias = L.ebias;
             R.B = B;
@@ -999,6 +1153,37 @@ static int batch_record(cuinf_batch* b, BStep& S) {
                     k_bgather<<<B * K, 256, 0, b->st>>>(b->xn, b->src, b->xg, H);
                     BTRY(cuinf_launch_status());
                     BTRY(S.mark("gather"));
+                }
+            } else if (b->p2p) {
+                // route this rank's tokens, write each (token, slot) row into its
+                // expert's rank, wait for every peer's rows, group them by local expert
+                S.launches += 4;
+                if (!dry) {
+                    R.group = 0;
+                    k_broute<<<1, 1024, 0, b->st>>>(R);
+                    BTRY(cuinf_launch_status());
+                    BTRY(S.mark("route"));
+                    k_ep_send<<<B * K + b->ep_world, 256, 0, b->st>>>(b->links, R.ridx, B * K, b->e_loc, b->xn, K,
+                                                                      b->dest_pos, b->ep_ticket, b->ep_step,
+                                                                      2 * moe_i);
+                    BTRY(cuinf_launch_status());
+                    BTRY(S.mark("ep_dispatch"));
+                    R.keys = reinterpret_cast<const int*>(b->links.base[b->ep_rank] + b->links.off_meta);
+                    R.n = NR;
+                    R.group = 1;
+                    R.wait.flags = reinterpret_cast<const unsigned long long*>(b->links.base[b->ep_rank] +
+                                                                               b->links.off_flag);
+                    R.wait.step = b->ep_step;
+                    R.wait.world = b->ep_world;
+                    R.wait.tag = 2 * moe_i;
+                    R.wait.err = g_tc_err_ptr;
+                    k_broute<<<1, 1024, 0, b->st>>>(R);
+                    BTRY(cuinf_launch_status());
+                    k_bgather<<<NR, 256, 0, b->st>>>(
+                        reinterpret_cast<const __half*>(b->links.base[b->ep_rank] + b->links.off_x), b->src, b->xg,
+                        H);
+                    BTRY(cuinf_launch_status());
+                    BTRY(S.mark("ep_group"));
                 }
             } else {
                 // route this rank's tokens, pack each (token, slot) row for its
@@ -1070,7 +1255,24 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             }
             const float* ob = b->fo;
             const int* oi = b->inv;
-            if (ep) {
+            EpWait cw = {};
+            if (ep && b->p2p) {
+                S.launches++;
+                if (!dry) {
+                    k_ep_send_back<<<NR, 256, 0, b->st>>>(b->links, b->fo, b->inv, b->ep_ticket + 1, b->ep_step,
+                                                         2 * moe_i + 1);
+                    BTRY(cuinf_launch_status());
+                    BTRY(S.mark("ep_return"));
+                }
+                ob = reinterpret_cast<const float*>(b->links.base[b->ep_rank] + b->links.off_back);
+                oi = b->dest_pos;
+                cw.flags = reinterpret_cast<const unsigned long long*>(b->links.base[b->ep_rank] + b->links.off_flag) +
+                           b->ep_world;
+                cw.step = b->ep_step;
+                cw.world = b->ep_world;
+                cw.tag = 2 * moe_i + 1;
+                cw.err = g_tc_err_ptr;
+            } else if (ep) {
                 S.launches++;
                 if (!dry) {
                     k_ep_unpack<<<NR, 256, 0, b->st>>>(b->fo, b->inv, b->back_o, H);
@@ -1089,7 +1291,7 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             }
             S.launches++;
             if (!dry) {
-                k_bcombine<<<(B * H + 255) / 256, 256, 0, b->st>>>(ob, oi, b->rw, b->h, B, H, K);
+                k_bcombine<<<(B * H + 255) / 256, 256, 0, b->st>>>(ob, oi, b->rw, b->h, B, H, K, cw);
                 BTRY(cuinf_launch_status());
                 BTRY(S.mark("combine"));
             }
@@ -1186,6 +1388,7 @@ extern "C" int cuinf_batch_free(cuinf_batch* b) {
     if (b->st) cudaStreamSynchronize(b->st);
     if (b->exec) cudaGraphExecDestroy(b->exec);
     if (b->graph) cudaGraphDestroy(b->graph);
+    for (void* p : b->peer_open) cudaIpcCloseMemHandle(p);
     for (void* p : b->allocs) cudaFree(p);
     if (b->ws) cudaFree(b->ws);
     if (b->cnt) cudaFree(b->cnt);
@@ -1193,6 +1396,67 @@ extern "C" int cuinf_batch_free(cuinf_batch* b) {
     if (b->comm) ncclCommDestroy(b->comm);  // after the graph that holds its calls (an aborted one is gone)
     if (b->own_stream && b->st) cudaStreamDestroy(b->st);
     delete b;
+    return CUINF_OK;
+}
+
+// Map every rank's exchange arena into this process (cudaIpc over the NCCL
+// communicator).  All ranks take the same collective steps whatever happens
+// locally; the peer-memory exchange is used only when every rank mapped
+// every arena, otherwise the batch keeps the NCCL send/recv exchange.
+static int ep_map_peers(cuinf_batch* b) {
+    const int W = b->ep_world, H = b->m->cfg.hidden;
+    const size_t rows = (size_t)W * b->cap;
+    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    EpLinks& L = b->links;
+    L.off_x = 0;
+    L.off_meta = al(rows * H * 2);
+    L.off_back = L.off_meta + al(rows * 4);
+    L.off_flag = L.off_back + al(rows * H * 4);
+    L.rank = b->ep_rank;
+    L.world = W;
+    L.cap = b->cap;
+    L.H = H;
+    char* arena = nullptr;
+    BTRY(balloc(b, &arena, L.off_flag + al((size_t)2 * W * 8)));  // zeroed: every flag starts at 0
+    BTRY(balloc(b, &b->ep_step, 8));
+    BTRY(balloc(b, &b->ep_ticket, 8));
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    cudaIpcMemHandle_t mine;
+    memset(&mine, 0, sizeof(mine));
+    int ok = cudaIpcGetMemHandle(&mine, arena) == cudaSuccess;
+    if (!ok) cudaGetLastError();
+    unsigned char* dh = nullptr;
+    int* dok = nullptr;
+    BTRY(balloc(b, &dh, (size_t)W * hb));
+    BTRY(balloc(b, &dok, 4));
+    CUINF_TRY(cudaMemcpy(dh + (size_t)b->ep_rank * hb, &mine, hb, cudaMemcpyHostToDevice));
+    BTRY(ep_settle(b, ncclAllGather(dh + (size_t)b->ep_rank * hb, dh, hb, ncclUint8, b->comm, b->st),
+                   "NCCL all-gather of the exchange handles failed"));
+    BTRY(batch_sync(b));
+    std::vector<cudaIpcMemHandle_t> hs(W);
+    CUINF_TRY(cudaMemcpy(hs.data(), dh, (size_t)W * hb, cudaMemcpyDeviceToHost));
+    for (int p = 0; p < W; p++) {
+        if (p == b->ep_rank) {
+            L.base[p] = arena;
+            continue;
+        }
+        void* ptr = nullptr;
+        if (ok && cudaIpcOpenMemHandle(&ptr, hs[p], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess) {
+            b->peer_open.push_back(ptr);
+            L.base[p] = (char*)ptr;
+        } else {
+            cudaGetLastError();
+            ok = 0;
+        }
+    }
+    CUINF_TRY(cudaMemcpy(dok, &ok, 4, cudaMemcpyHostToDevice));
+    BTRY(ep_settle(b, ncclAllReduce(dok, dok, 1, ncclInt32, ncclMin, b->comm, b->st),
+                   "NCCL all-reduce of the mapping status failed"));
+    BTRY(batch_sync(b));
+    int all = 0;
+    CUINF_TRY(cudaMemcpy(&all, dok, 4, cudaMemcpyDeviceToHost));
+    b->p2p_ok = all != 0;
+    b->p2p = b->p2p_ok;
     return CUINF_OK;
 }
 
@@ -1204,6 +1468,8 @@ static int batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, c
     REQUIRE(world == 1 || (nccl_id && c.n_experts % world == 0),
             "expert parallelism needs an NCCL id and n_experts divisible by the world size");
     REQUIRE(world == 1 || (size_t)n_seqs * c.top_k * world <= 1024, "n_seqs * top_k * world must be <= 1024");
+    REQUIRE(world <= EP_MAX_WORLD, "at most 8 ranks");
+    REQUIRE(c.n_layers - c.n_dense <= 127, "at most 127 MoE layers");
     REQUIRE(n_seqs >= 1 && n_seqs <= TC_NMAX, "n_seqs must be in [1, 128]");
     REQUIRE(max_ctx >= 1, "max_ctx must be positive");
     REQUIRE(c.hidden % TC_KS == 0 && c.moe_inter % TC_KS == 0 && c.dense_inter % TC_KS == 0 &&
@@ -1308,6 +1574,7 @@ static int batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, c
             cuinf_batch_free(b);
             return cuinf_set_arg_error(msg.c_str());
         }
+        TRYB(ep_map_peers(b));
     }
     TRYB(balloc(b, &b->amax, (size_t)B * 8));
     b->nsplit = attn_batched_nsplit(c.n_heads, nkv, max_ctx, B, b->num_sms);
@@ -1510,6 +1777,20 @@ extern "C" int cuinf_batch_set_timeout(cuinf_batch* b, int timeout_ms) {
 }
 
 extern "C" int cuinf_batch_failed(const cuinf_batch* b) { return b && b->ep_failed ? 1 : 0; }
+
+extern "C" int cuinf_batch_ep_exchange(const cuinf_batch* b) {
+    if (!b || b->ep_world <= 1) return -1;
+    return b->p2p ? 1 : 0;
+}
+extern "C" int cuinf_batch_set_ep_exchange(cuinf_batch* b, int peer_memory) {
+    REQUIRE(b && b->ep_world > 1, "not an expert-parallel batch");
+    REQUIRE(!b->ep_failed, "expert-parallel batch was aborted");
+    REQUIRE(!peer_memory || b->p2p_ok, "the peers' exchange arenas could not be mapped");
+    if ((bool)peer_memory == b->p2p) return CUINF_OK;
+    BTRY(batch_sync(b));
+    b->p2p = peer_memory != 0;
+    return batch_build_graph(b);
+}
 
 extern "C" int cuinf_batch_keep_logits(cuinf_batch* b, int on) {
     REQUIRE(b, "null batch");
@@ -1752,7 +2033,7 @@ int moe_grouped_prefill(cuinf_model* m, int layer, const __half* xn, __half* h, 
         const int n = std::min(tc->chunk, S - c0), maxch = (n + TC_NMAX - 1) / TC_NMAX;
         rc = cuinf_gemv_fp16(xn + (size_t)c0 * H, L.gate, tc->rlog, n, E, H, st);
         if (rc) return rc;
-        BRouteParams R;
+        BRouteParams R = {};
         R.logits = tc->rlog;
         R.bias = L.ebias;
         R.B = n;
@@ -1802,7 +2083,8 @@ int moe_grouped_prefill(cuinf_model* m, int layer, const __half* xn, __half* h, 
             if ((rc = tc_launch(pass ? tc->x_mmid : tc->x_xg, tc->hmaps[0], P, tiles, st, false))) return rc;
             if (!pass && (rc = cuinf_swiglu(tc->fg, tc->fu, tc->mmid, n * K * I, st))) return rc;
         }
-        k_bcombine<<<(n * H + 255) / 256, 256, 0, st>>>(tc->fo, tc->inv, tc->rw, h + (size_t)c0 * H, n, H, K);
+        k_bcombine<<<(n * H + 255) / 256, 256, 0, st>>>(tc->fo, tc->inv, tc->rw, h + (size_t)c0 * H, n, H, K,
+                                                         EpWait{});
         if ((rc = cuinf_launch_status())) return rc;
     }
     return CUINF_OK;

@@ -128,7 +128,7 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // Phase timestamps of the decode-step kernels, for diagnostic builds only
 // (-DCUINF_PHASE_TRACE, `python -m cuda_inf_b200.build --trace`): thread 0
 // of every CTA stores %globaltimer at each marked phase of its kernel's
-// latest launch (kernel id k, phase i < 10; slot 11 = the CTA's SM).
+// latest launch (kernel id k, phase i < 11; slot 11 = the CTA's SM).
 // Product builds compile the marks away.
 #define PH_QKV 0
 #define PH_RES 1

@@ -204,7 +204,7 @@ __global__ void __cluster_dims__(MOEF_CL, 1, 1) __launch_bounds__(MOEF_THREADS, 
     PHASE(PH_MOE_UP, 3);
 
     // ---- selection (engine.cu:883-892) ----
-    route_select_block(lg_all, sbias, P.E, P.topk, sidx, sw, lgp);
+    route_select_block(lg_all, sbias, P.E, P.topk, sidx, sw, lgp, PH_MOE_UP);
     if (blockIdx.x == 0 && threadIdx.x < P.topk) {
         P.route_idx[threadIdx.x] = sidx[threadIdx.x];
         P.route_w[threadIdx.x] = sw[threadIdx.x];

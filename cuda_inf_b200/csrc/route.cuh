@@ -81,8 +81,10 @@ __device__ __forceinline__ void route_select_warp(const float* logits, const __h
 // index), as the scan never picks them before the smallest unused index.
 // Weights are the unbiased sigmoids over (their sum in slot order + 1e-6).
 // scratch: 2*E floats of shared memory.  Ends with a block barrier.
+// trace_kernel: phase-trace kernel id that receives mark 10 after the
+// sigmoids (diagnostic builds only; -1 = none).
 __device__ __forceinline__ void route_select_block(const float* logits, const __half* bias, int n_exp, int topk,
-                                                   int* idx, float* w, float* scratch) {
+                                                   int* idx, float* w, float* scratch, int trace_kernel = -1) {
     const int e = threadIdx.x;
     if (n_exp <= 32) {  // one warp: the keys travel by shuffle, one block barrier
         if (e < 32) {
@@ -92,6 +94,7 @@ __device__ __forceinline__ void route_select_block(const float* logits, const __
                 const float score = sig + __half2float(bias[e]);
                 key = (score > -1e30f) ? score : -INFINITY;
             }
+            if (trace_kernel >= 0) PHASE(trace_kernel, 10);
             int rank = 0;  // 32 independent shuffles, unrolled so they pipeline
 #pragma unroll
             for (int o = 0; o < 32; o++) {

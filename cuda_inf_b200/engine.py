@@ -287,6 +287,17 @@ class Batch:
     def failed(self):
         return bool(lib().cuinf_batch_failed(self._h))
 
+    @property
+    def exchange(self):
+        """Expert-parallel row exchange: "peer_memory", "nccl", or None (one GPU)."""
+        v = lib().cuinf_batch_ep_exchange(self._h)
+        return None if v < 0 else ("peer_memory" if v == 1 else "nccl")
+
+    def set_exchange(self, kind):
+        """Select the expert-parallel exchange ("peer_memory" or "nccl"); every
+        rank must make the same choice between the same two steps."""
+        check(lib().cuinf_batch_set_ep_exchange(self._h, 1 if kind == "peer_memory" else 0))
+
     def logits(self):
         ptr = lib().cuinf_batch_logits(self._h)
         return torch.as_tensor(_DevArray(ptr, (self.n, self.model.cfg.vocab), "<f4"), device="cuda")

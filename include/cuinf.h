@@ -264,15 +264,26 @@ int cuinf_argmax_key_index(unsigned long long key);
  * step.  cuinf_batch_logits: device [n_seqs][vocab] while keep_logits is on. */
 typedef struct cuinf_batch cuinf_batch;
 int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, cuinf_batch** out);
-/* Expert-parallel form (BASELINE config 5 on `world` GPUs, one process per
- * GPU): this rank decodes its own n_seqs sequences and hosts experts
- * [rank*E/world, (rank+1)*E/world); per MoE layer each (token, slot) row goes
- * to its expert's rank and the fp32 expert output comes back, by NCCL
- * send/recv on the batch stream inside the step graph (fixed capacity
- * n_seqs*top_k rows per peer).  nccl_id: cuinf_ep_unique_id on rank 0,
- * broadcast to all ranks.  Every rank steps together. */
+/* Expert-parallel form (BASELINE config 5 on `world` <= 8 GPUs of one node,
+ * one process per GPU): this rank decodes its own n_seqs sequences and hosts
+ * experts [rank*E/world, (rank+1)*E/world); per MoE layer each (token, slot)
+ * row goes to its expert's rank and the fp32 expert output comes back.
+ * The exchange writes the rows straight into the receiving rank's memory
+ * (every rank's exchange arena is mapped into every process with cudaIpc;
+ * only the rows that exist cross NVLink, the sender's own rows stay local)
+ * and raises a flag there that the receiver's next kernel waits for (at most
+ * 4 s, then bit 2 of cuinf_batch_error is set).  When an arena cannot be
+ * mapped on some rank, every rank uses NCCL send/recv of fixed capacity
+ * (n_seqs*top_k rows per peer) instead.  nccl_id: cuinf_ep_unique_id on
+ * rank 0, broadcast to all ranks.  Every rank steps together. */
 int cuinf_batch_create_ep(cuinf_model* m, int n_seqs, int max_ctx, void* stream, const unsigned char* nccl_id,
                           int rank, int world, cuinf_batch** out);
+/* The exchange an expert-parallel batch uses: 1 peer memory, 0 NCCL
+ * send/recv, -1 not expert-parallel. */
+int cuinf_batch_ep_exchange(const cuinf_batch* b);
+/* Select the exchange (1 peer memory, 0 NCCL) and rebuild the step graph.
+ * All ranks must make the same choice between the same two steps. */
+int cuinf_batch_set_ep_exchange(cuinf_batch* b, int peer_memory);
 int cuinf_ep_unique_id(unsigned char* id, int id_bytes);
 int cuinf_ep_unique_id_bytes(void);
 /* Failure handling of the expert-parallel form (the reference runs on one

@@ -2,10 +2,11 @@
 tests/test_gpu_ep.py through torch.distributed.run, one process per GPU).
 
 Each rank decodes its own sequences with experts sharded across the ranks
-(cuinf_batch_create_ep) and checks every one of them against the CPU oracle,
-teacher-forced, exactly as the single-GPU batch test does; a second batch
-with the vocabulary-sharded lm_head must produce the same tokens.  Prints one line
-"EP rank R: ..." and exits non-zero on a mismatch."""
+(cuinf_batch_create_ep, rows exchanged through peer memory) and checks every
+one of them against the CPU oracle, teacher-forced, exactly as the
+single-GPU batch test does; a second batch with the vocabulary-sharded
+lm_head and the NCCL send/recv exchange must produce the same tokens.
+Prints one line "EP rank R: ..." and exits non-zero on a mismatch."""
 import datetime
 import os
 import sys
@@ -48,6 +49,9 @@ def main():
     # sharded by vocabulary over the ranks (argmax keys max-reduced), and its
     # tokens must equal the replicated lm_head's bit for bit
     bt2 = Batch(gm, n_local, max_ctx=160, ep=(ep_unique_id_shared(), rank, world))  # its own communicator
+    assert bt.exchange == "peer_memory", bt.exchange
+    bt2.set_exchange("nccl")
+    assert bt2.exchange == "nccl"
     worst, checked, near = 0.0, 0, 0
     for i in range(steps):
         got = bt.step(mine[i])
@@ -65,7 +69,7 @@ def main():
     assert checked > 0.9 * (checked + near), (checked, near)
     assert Batch.error() == 0
     print(f"EP rank {rank}/{world}: {n_local} sequences x {steps} steps, worst logits rel err {worst:.2e}, "
-          f"routing checked {checked}, near-ties {near}", flush=True)
+          f"routing checked {checked}, near-ties {near}; peer-memory and NCCL exchanges agree", flush=True)
     bt.close()  # the step graph holds NCCL calls: release it before the process group
     bt2.close()
     dist.barrier()

@@ -1,4 +1,5 @@
-"""Expert-parallel batched decode on 2 GPUs (one process per GPU over NCCL):
+"""Expert-parallel batched decode on 2 GPUs (one process per GPU; rows
+exchanged through peer memory, and by NCCL send/recv in a second batch):
 each rank's sequences must follow the CPU oracle.  Skipped with fewer than 2
 GPUs.  The host-side NCCL id exchange is covered on CPU by
 test_cpu_ep_id.py."""
