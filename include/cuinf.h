@@ -94,7 +94,8 @@ int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_t* vc8, con
  * front).  It allocates nothing: its split-K scratch is a static device array
  * of cuinf_attn_decode_static_scratch_bytes() (512 KiB) bytes inside the
  * library.  The first call on a device sets up (looks up that array's
- * address).  Shapes
+ * address); make that first call before any stream capture on the device.
+ * Shapes
  * whose scratch would exceed 512 KiB are rejected with CUINF_ERR_ARG: on a
  * B200, 8 kv heads x 4 query heads each (the model's shape) need at most
  * 0.31 MiB; 8 kv heads x 8 query heads need more than 512 KiB past 1920
