@@ -611,138 +611,209 @@ __global__ void __launch_bounds__(256) k_h2o_attn(H2oParams P) {
     }
 }
 
-// Prefill attention for long prompts (attention_fused, engine.cu:236-308),
-// the same keys and arithmetic as k_attn_prefill: grid (S, nh), 256 threads;
-// thread j takes keys j, j+256, ... of the query's range with its own online
-// softmax (q and its 64 outputs in registers, one full 64-dim dot per key),
-// and the block merges the 256 partial states at the end.
-__global__ void __launch_bounds__(256) k_attn_prefill_wide(const __half* __restrict__ q,
-                                                            const uint8_t* __restrict__ kc8,
-                                                            const uint8_t* __restrict__ vc8,
-                                                            const __half* __restrict__ ksc,
-                                                            const __half* __restrict__ vsc,
-                                                            const __half* __restrict__ ktail,
-                                                            const __half* __restrict__ vtail, int committed,
-                                                            int past, float scale, __half* __restrict__ out, int nh,
-                                                            int nkv) {
-    __shared__ float wm[8], wl[8];
-    __shared__ float wo[8][CUINF_HD];
-    const int i = blockIdx.x, hq = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int kvh = hq / (nh / nkv), qpos = past + i;
-    const int cend = committed < qpos + 1 ? committed : qpos + 1;
-    float qr[CUINF_HD];
+// Prefill attention for long prompts (attention_fused, engine.cu:236-308) on
+// the tensor cores: flash attention with mma.sync m16n8k16 (fp16 operands,
+// fp32 accumulation).  One CTA = 64 query tokens x the GQA query heads of
+// one kv head (16 rows per warp: one head, 16 tokens), so every K/V tile
+// staged in shared memory serves all the heads that read it.  Keys come in
+// tiles of 64 = one FP8 commit group, so a committed tile has one K and one
+// V scale and both factor out of the products:
+//   s = (q . k8) * (k_scale * scale)      k8: the E4M3 value, exact in fp16
+//   o += (p * v_scale) . v8, l += p       p = exp(s - m), online over tiles
+// which is the reference's fp32 arithmetic up to summation order (and p * v
+// rounded to fp16 for the MMA).  The tail group (keys >= committed, fp16)
+// has scale 1.  Keys beyond a query's position are masked, as the
+// reference's loop bounds exclude them.  Tiles are double-buffered: the next
+// tile's bytes are loaded into registers while the current one multiplies.
+// grid (ceil(S/64), nkv) (longest key ranges first), 128 * GQA threads, GQA
+// (query heads per kv head) in {1, 2, 4}.
+#define APF_TOK 64
+#define APF_KT 64
+#define APF_PITCH 72  // halves per shared row: the 32-bit fragment loads of a warp hit 32 banks
+template <int GQA>
+__global__ void __launch_bounds__(128 * GQA, 1) k_attn_prefill_mma(const __half* __restrict__ q,
+                                                                   const uint8_t* __restrict__ kc8,
+                                                                   const uint8_t* __restrict__ vc8,
+                                                                   const __half* __restrict__ ksc,
+                                                                   const __half* __restrict__ vsc,
+                                                                   const __half* __restrict__ ktail,
+                                                                   const __half* __restrict__ vtail, int committed,
+                                                                   int past, int S, float scale,
+                                                                   __half* __restrict__ out, int nh, int nkv) {
+    __shared__ __align__(16) __half Ks[2][APF_KT][APF_PITCH];
+    __shared__ __align__(16) __half Vt[2][CUINF_HD][APF_PITCH];  // V transposed: [dim][key]
+    __shared__ float kvs[2][2];                                  // per buffer: k_scale * scale, v_scale
+    constexpr int nthr = 128 * GQA;
+    const int nblk = (S + APF_TOK - 1) / APF_TOK;
+    const int blk = nblk - 1 - (int)blockIdx.x, kvh = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+    const int hq = kvh * GQA + (warp >> 2), sub = warp & 3;
+    const int i0 = blk * APF_TOK, tok0 = i0 + sub * 16;
+    const int last_tok = min(i0 + APF_TOK, S) - 1;
+    const int ntile = (past + last_tok + 1 + APF_KT - 1) / APF_KT;
+    const int tailn = past + S - committed;  // keys in the fp16 tail (< 64)
+    const int warp_last_key = tok0 < S ? past + min(tok0 + 15, S - 1) : -1;
+
+    // query fragments (A operand, 16 tokens x 64 dims), zero past S
+    uint32_t qa[4][4];
     {
-        const uint4* qp = reinterpret_cast<const uint4*>(q + ((size_t)i * nh + hq) * CUINF_HD);
+        const int r0 = tok0 + g, r1 = tok0 + g + 8;
+        const uint32_t* q0 = reinterpret_cast<const uint32_t*>(q + ((size_t)min(r0, S - 1) * nh + hq) * CUINF_HD);
+        const uint32_t* q1 = reinterpret_cast<const uint32_t*>(q + ((size_t)min(r1, S - 1) * nh + hq) * CUINF_HD);
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
-            const uint4 u = qp[c];
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const __half2 h2 = *reinterpret_cast<const __half2*>(&w[j]);
-                qr[c * 8 + 2 * j] = __low2float(h2) * scale;
-                qr[c * 8 + 2 * j + 1] = __high2float(h2) * scale;
-            }
+        for (int kk = 0; kk < 4; kk++) {
+            qa[kk][0] = r0 < S ? q0[8 * kk + c] : 0u;
+            qa[kk][1] = r1 < S ? q1[8 * kk + c] : 0u;
+            qa[kk][2] = r0 < S ? q0[8 * kk + 4 + c] : 0u;
+            qa[kk][3] = r1 < S ? q1[8 * kk + 4 + c] : 0u;
         }
     }
-    float m = -1e30f, l = 0.f, o[CUINF_HD];
+
+    // tile loader: task = (key, 8-dim chunk); K by key-major tasks (16-byte
+    // row stores), V by dim-chunk-major tasks (consecutive keys per warp, so
+    // the transposed 2-byte stores are conflict-free)
+    constexpr int ntask = (APF_KT * CUINF_HD / 8) / nthr;
+    uint4 kr[ntask], vr[ntask];
+    auto load = [&](int j) {
+        const bool tail = j * APF_KT >= committed;
 #pragma unroll
-    for (int d = 0; d < CUINF_HD; d++) o[d] = 0.f;
-    for (int t = tid; t <= qpos; t += blockDim.x) {
-        // score first (K converted on the fly), then V folded into the outputs
-        float s = 0.f, cf, p;
-        if (t < cend) {
-            const float ks = __half2float(ksc[(t / CUINF_KVGROUP) * nkv + kvh]);
-            const uint4* kp = reinterpret_cast<const uint4*>(kc8 + ((size_t)t * nkv + kvh) * CUINF_HD);
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const uint4 ku = kp[c];
-                const uint32_t kw[4] = {ku.x, ku.y, ku.z, ku.w};
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    const uint32_t kb = fp8x2_to_h2(kw[j >> 1] >> (16 * (j & 1)));
-                    const __half2 k2 = *reinterpret_cast<const __half2*>(&kb);
-                    const int d = c * 16 + j * 2;
-                    s = fmaf(qr[d], __low2float(k2) * ks, s);
-                    s = fmaf(qr[d + 1], __high2float(k2) * ks, s);
-                }
-            }
-        } else {
-            const uint4* kp = reinterpret_cast<const uint4*>(ktail + ((size_t)(t - committed) * nkv + kvh) * CUINF_HD);
-#pragma unroll
-            for (int c = 0; c < 8; c++) {
-                const uint4 ku = kp[c];
-                const uint32_t kw[4] = {ku.x, ku.y, ku.z, ku.w};
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const __half2 k2 = *reinterpret_cast<const __half2*>(&kw[j]);
-                    s = fmaf(qr[c * 8 + 2 * j], __low2float(k2), s);
-                    s = fmaf(qr[c * 8 + 2 * j + 1], __high2float(k2), s);
-                }
+        for (int u = 0; u < ntask; u++) {
+            const int task = tid + u * nthr;
+            const int kk = task >> 3, ch = task & 7;    // K task
+            const int vk = task & 63, vch = task >> 6;  // V task
+            if (!tail) {
+                const size_t kt = (size_t)(j * APF_KT + kk), vt = (size_t)(j * APF_KT + vk);
+                const uint2 k2 = *reinterpret_cast<const uint2*>(kc8 + (kt * nkv + kvh) * CUINF_HD + 8 * ch);
+                const uint2 v2 = *reinterpret_cast<const uint2*>(vc8 + (vt * nkv + kvh) * CUINF_HD + 8 * vch);
+                kr[u] = make_uint4(k2.x, k2.y, 0u, 0u);
+                vr[u] = make_uint4(v2.x, v2.y, 0u, 0u);
+            } else {
+                kr[u] = kk < tailn ? *reinterpret_cast<const uint4*>(ktail + ((size_t)kk * nkv + kvh) * CUINF_HD + 8 * ch)
+                                   : make_uint4(0u, 0u, 0u, 0u);
+                vr[u] = vk < tailn ? *reinterpret_cast<const uint4*>(vtail + ((size_t)vk * nkv + kvh) * CUINF_HD + 8 * vch)
+                                   : make_uint4(0u, 0u, 0u, 0u);
             }
         }
-        const float mn = fmaxf(m, s);
-        cf = __expf(m - mn);
-        p = __expf(s - mn);
-        l = l * cf + p;
-        m = mn;
-        if (t < cend) {
-            const float pv = p * __half2float(vsc[(t / CUINF_KVGROUP) * nkv + kvh]);
-            const uint4* vp = reinterpret_cast<const uint4*>(vc8 + ((size_t)t * nkv + kvh) * CUINF_HD);
+    };
+    auto store = [&](int j, int b) {
+        const bool tail = j * APF_KT >= committed;
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const uint4 vu = vp[c];
-                const uint32_t vw[4] = {vu.x, vu.y, vu.z, vu.w};
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    const uint32_t vb = fp8x2_to_h2(vw[j >> 1] >> (16 * (j & 1)));
-                    const __half2 v2 = *reinterpret_cast<const __half2*>(&vb);
-                    const int d = c * 16 + j * 2;
-                    o[d] = fmaf(pv, __low2float(v2), o[d] * cf);
-                    o[d + 1] = fmaf(pv, __high2float(v2), o[d + 1] * cf);
-                }
+        for (int u = 0; u < ntask; u++) {
+            const int task = tid + u * nthr;
+            const int kk = task >> 3, ch = task & 7;
+            const int vk = task & 63, vch = task >> 6;
+            uint4 kh = kr[u], vh = vr[u];
+            if (!tail) {
+                kh = make_uint4(fp8x2_to_h2(kr[u].x), fp8x2_to_h2(kr[u].x >> 16), fp8x2_to_h2(kr[u].y),
+                                fp8x2_to_h2(kr[u].y >> 16));
+                vh = make_uint4(fp8x2_to_h2(vr[u].x), fp8x2_to_h2(vr[u].x >> 16), fp8x2_to_h2(vr[u].y),
+                                fp8x2_to_h2(vr[u].y >> 16));
             }
-        } else {
-            const uint4* vp = reinterpret_cast<const uint4*>(vtail + ((size_t)(t - committed) * nkv + kvh) * CUINF_HD);
+            *reinterpret_cast<uint4*>(&Ks[b][kk][8 * ch]) = kh;
+            const __half* v8 = reinterpret_cast<const __half*>(&vh);
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
-                const uint4 vu = vp[c];
-                const uint32_t vw[4] = {vu.x, vu.y, vu.z, vu.w};
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const __half2 v2 = *reinterpret_cast<const __half2*>(&vw[j]);
-                    o[c * 8 + 2 * j] = fmaf(p, __low2float(v2), o[c * 8 + 2 * j] * cf);
-                    o[c * 8 + 2 * j + 1] = fmaf(p, __high2float(v2), o[c * 8 + 2 * j + 1] * cf);
-                }
-            }
+            for (int e = 0; e < 8; e++) Vt[b][8 * vch + e][vk] = v8[e];
         }
-    }
-    // merge: lanes of a warp, then the 8 warps
+        if (tid == 0) {
+            kvs[b][0] = tail ? scale : __half2float(ksc[(size_t)j * nkv + kvh]) * scale;
+            kvs[b][1] = tail ? 1.f : __half2float(vsc[(size_t)j * nkv + kvh]);
+        }
+    };
+
+    float o[8][4], m0 = -1e30f, m1 = -1e30f, l0 = 0.f, l1 = 0.f;
 #pragma unroll
-    for (int off = 16; off; off >>= 1) {
-        const float om = __shfl_xor_sync(0xffffffffu, m, off), ol = __shfl_xor_sync(0xffffffffu, l, off);
-        const float mn = fmaxf(m, om), a = __expf(m - mn), b = __expf(om - mn);
-#pragma unroll
-        for (int d = 0; d < CUINF_HD; d++) o[d] = o[d] * a + __shfl_xor_sync(0xffffffffu, o[d], off) * b;
-        l = l * a + ol * b;
-        m = mn;
-    }
-    if (lane == 0) {
-        wm[warp] = m;
-        wl[warp] = l;
-#pragma unroll
-        for (int d = 0; d < CUINF_HD; d++) wo[warp][d] = o[d];
-    }
+    for (int nd = 0; nd < 8; nd++) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+    load(0);
+    store(0, 0);
     __syncthreads();
-    if (tid < CUINF_HD) {
-        float M = -1e30f;
-        for (int w = 0; w < 8; w++) M = fmaxf(M, wm[w]);
-        float L = 0.f, O = 0.f;
-        for (int w = 0; w < 8; w++) {
-            const float e = __expf(wm[w] - M);
-            L += wl[w] * e;
-            O += wo[w][tid] * e;
+    for (int j = 0; j < ntile; j++) {
+        const int b = j & 1;
+        if (j + 1 < ntile) load(j + 1);
+        if (j * APF_KT <= warp_last_key) {
+            // S = Q K^T for 64 keys
+            float sc[8][4];
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+                sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+                const __half* kr0 = &Ks[b][8 * nt + g][2 * c];
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr0 + 16 * kk);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr0 + 16 * kk + 8);
+                    mma_16816(sc[nt], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+                }
+            }
+            const float ks = kvs[b][0], vs = kvs[b][1];
+            const int q0pos = past + tok0 + g, q1pos = q0pos + 8;
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+                const int key = j * APF_KT + 8 * nt + 2 * c;
+                sc[nt][0] = key <= q0pos ? sc[nt][0] * ks : -INFINITY;
+                sc[nt][1] = key + 1 <= q0pos ? sc[nt][1] * ks : -INFINITY;
+                sc[nt][2] = key <= q1pos ? sc[nt][2] * ks : -INFINITY;
+                sc[nt][3] = key + 1 <= q1pos ? sc[nt][3] * ks : -INFINITY;
+                mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
+                mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
+            }
+#pragma unroll
+            for (int off = 1; off <= 2; off <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+            }
+            const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+            const float cf0 = __expf(m0 - mn0), cf1 = __expf(m1 - mn1);
+            m0 = mn0;
+            m1 = mn1;
+            l0 *= cf0;
+            l1 *= cf1;
+#pragma unroll
+            for (int nd = 0; nd < 8; nd++) {
+                o[nd][0] *= cf0;
+                o[nd][1] *= cf0;
+                o[nd][2] *= cf1;
+                o[nd][3] *= cf1;
+            }
+            // P (scaled by the tile's V scale) as the A operand of O += P V
+            uint32_t pa[4][4];
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+                const float p0 = __expf(sc[nt][0] - mn0), p1 = __expf(sc[nt][1] - mn0);
+                const float p2 = __expf(sc[nt][2] - mn1), p3 = __expf(sc[nt][3] - mn1);
+                l0 += p0 + p1;
+                l1 += p2 + p3;
+                const __half2 h01 = __floats2half2_rn(p0 * vs, p1 * vs), h23 = __floats2half2_rn(p2 * vs, p3 * vs);
+                pa[nt >> 1][(nt & 1) * 2 + 0] = *reinterpret_cast<const uint32_t*>(&h01);
+                pa[nt >> 1][(nt & 1) * 2 + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+            }
+#pragma unroll
+            for (int nd = 0; nd < 8; nd++) {
+                const __half* vr0 = &Vt[b][8 * nd + g][2 * c];
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(vr0 + 16 * kk);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(vr0 + 16 * kk + 8);
+                    mma_16816(o[nd], pa[kk][0], pa[kk][1], pa[kk][2], pa[kk][3], b0, b1);
+                }
+            }
         }
-        out[((size_t)i * nh + hq) * CUINF_HD + tid] = __float2half_rn(O / L);
+        if (j + 1 < ntile) store(j + 1, b ^ 1);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+    const int r0 = tok0 + g, r1 = tok0 + g + 8;
+#pragma unroll
+    for (int nd = 0; nd < 8; nd++) {
+        if (r0 < S)
+            *reinterpret_cast<__half2*>(out + ((size_t)r0 * nh + hq) * CUINF_HD + 8 * nd + 2 * c) =
+                __floats2half2_rn(o[nd][0] * inv0, o[nd][1] * inv0);
+        if (r1 < S)
+            *reinterpret_cast<__half2*>(out + ((size_t)r1 * nh + hq) * CUINF_HD + 8 * nd + 2 * c) =
+                __floats2half2_rn(o[nd][2] * inv1, o[nd][3] * inv1);
     }
 }

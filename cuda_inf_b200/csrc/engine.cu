@@ -1605,11 +1605,19 @@ extern "C" int cuinf_prefill(cuinf_session* s, const int* ids, int S, int* out_t
                     committed += CUINF_KVGROUP;
                 }
             }
-            if (S >= PF_TC_MIN_ROWS)
-                k_attn_prefill_wide<<<dim3(S, nh), 256, 0, st>>>(q16, A.kc8, A.vc8, A.ksc, A.vsc, A.ktail, A.vtail,
-                                                                 committed, past, 1.0f / sqrtf((float)hd), ao, nh,
-                                                                 nkv);
-            else
+            if (S >= PF_TC_MIN_ROWS && (nh / nkv == 1 || nh / nkv == 2 || nh / nkv == 4)) {
+                const dim3 grid((S + APF_TOK - 1) / APF_TOK, nkv);
+                const float sc = 1.0f / sqrtf((float)hd);
+                if (nh / nkv == 4)
+                    k_attn_prefill_mma<4><<<grid, 512, 0, st>>>(q16, A.kc8, A.vc8, A.ksc, A.vsc, A.ktail, A.vtail,
+                                                                committed, past, S, sc, ao, nh, nkv);
+                else if (nh / nkv == 2)
+                    k_attn_prefill_mma<2><<<grid, 256, 0, st>>>(q16, A.kc8, A.vc8, A.ksc, A.vsc, A.ktail, A.vtail,
+                                                                committed, past, S, sc, ao, nh, nkv);
+                else
+                    k_attn_prefill_mma<1><<<grid, 128, 0, st>>>(q16, A.kc8, A.vc8, A.ksc, A.vsc, A.ktail, A.vtail,
+                                                                committed, past, S, sc, ao, nh, nkv);
+            } else
                 k_attn_prefill<<<dim3(S, nh), 32, 0, st>>>(q16, A.kc8, A.vc8, A.ksc, A.vsc, A.ktail, A.vtail,
                                                            committed, past, 1.0f / sqrtf((float)hd), ao, nh, nkv);
             PF(cuinf_launch_status());
