@@ -180,7 +180,7 @@ static int num_sms_now() {
     return n;
 }
 
-// One standalone launch per 128 activation rows.
+// One standalone launch: every 128 activation rows form a group of items.
 static int tc_gemm_op(const void* x, const void* w, const void* scales, float* y, int M, int N, int K,
                       unsigned long long* amax, bool fp16_w, void* stream) {
     REQUIRE(x && w && (y || amax), "null pointer");
@@ -193,38 +193,37 @@ static int tc_gemm_op(const void* x, const void* w, const void* scales, float* y
     if (rc) return rc;
     rc = fp16_w ? tc_map_f16w(&wm, (const __half*)w, N, K) : tc_map_int4(&wm, (const uint8_t*)w, N, K);
     if (rc) return rc;
-    const int tiles = (N + TC_ROWS - 1) / TC_ROWS;
-    TcPlan pl = amax ? TcPlan{1, K / TC_KS} : tc_plan(tiles, K, num_sms_now());
+    const int tiles = (N + TC_ROWS - 1) / TC_ROWS, ng = (M + TC_NMAX - 1) / TC_NMAX;
+    TcPlan pl = amax ? TcPlan{1, K / TC_KS} : tc_plan(tiles * ng, K, num_sms_now());
     REQUIRE(pl.kgps <= TC_MAX_KG || fp16_w, "K too large for one split");
     float* ws = nullptr;
     unsigned* cnt = nullptr;
     if (pl.splits > 1) {
-        rc = tc_workspace((size_t)tiles * pl.splits, tiles, &ws, &cnt);
+        rc = tc_workspace((size_t)ng * tiles * pl.splits, (size_t)ng * tiles, &ws, &cnt);
         if (rc) return rc;
     }
-    for (int m0 = 0; m0 < M; m0 += TC_NMAX) {
-        TcParams P = {};
-        P.groups = nullptr;
-        P.g0.wmap = nullptr;
-        P.g0.scales = (const __half*)scales;
-        P.g0.y = y ? y + (size_t)m0 * N : nullptr;
-        P.g0.x_row = m0;
-        P.g0.rows = std::min(TC_NMAX, M - m0);
-        P.g0.N = N;
-        P.g0.ldy = N;
-        P.n_groups = 1;
-        P.K = K;
-        P.splits = pl.splits;
-        P.kg_per_split = pl.kgps;
-        P.fp16_w = fp16_w;
-        P.xmax = xmax;
-        P.xbox = xmax;
-        P.ws = ws;
-        P.counters = cnt;
-        P.amax = amax;
-        rc = tc_launch(xm, wm, P, tiles, ST(stream), false);
-        if (rc) return rc;
-    }
+    TcParams P = {};
+    P.groups = nullptr;
+    P.g0.wmap = nullptr;
+    P.g0.scales = (const __half*)scales;
+    P.g0.y = y;
+    P.g0.x_row = 0;
+    P.g0.rows = std::min(TC_NMAX, M);
+    P.g0.N = N;
+    P.g0.ldy = N;
+    P.n_groups = ng;
+    P.m_rows = M;
+    P.K = K;
+    P.splits = pl.splits;
+    P.kg_per_split = pl.kgps;
+    P.fp16_w = fp16_w;
+    P.xmax = xmax;
+    P.xbox = xmax;
+    P.ws = ws;
+    P.counters = cnt;
+    P.amax = amax;
+    rc = tc_launch(xm, wm, P, tiles, ST(stream), false);
+    if (rc) return rc;
     return cuinf_launch_status();
 }
 
@@ -277,7 +276,7 @@ struct EpWait {
     const unsigned long long* flags;  // this rank's flags row ([0] dispatch or [1] return); null: no wait
     const unsigned long long* step;   // the device step counter
     int world, tag;                   // tag: 2 * MoE layer + direction
-    unsigned* err;                    // bit 2: a peer's flag did not come within the wait limit
+    unsigned* err;                    // bit 4 (16): a peer's flag did not come within the wait limit
 };
 struct cuinf_batch {
     cuinf_model* m = nullptr;
@@ -459,13 +458,13 @@ __device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsign
 // most CUINF_WAIT_LIMIT_NS in total; on time-out set the error bit and return
 // (the kernel then runs on stale rows; the host reports the error).
 __device__ void ep_wait_flags(const EpWait& W) {
-    if (*(volatile unsigned*)W.err & 4u) return;  // an earlier wait gave up: do not wait again
+    if (*(volatile unsigned*)W.err & 16u) return;  // an earlier wait gave up: do not wait again
     const unsigned long long want = ep_flag_value(*W.step, W.tag);
     const unsigned long long t0 = globaltimer_ns();
     for (int p = 0; p < W.world; p++) {
         while (ld_acquire_sys_u64(W.flags + p) < want) {
             if (globaltimer_ns() - t0 > CUINF_WAIT_LIMIT_NS) {
-                atomicOr(W.err, 4u);
+                atomicOr(W.err, 16u);
                 return;
             }
             __nanosleep(32);
@@ -568,7 +567,16 @@ struct BRouteParams {
     void* const* experts;     // [n_local][6]: w1 packed, w1 scales, w3 .., w2 ..
     float *gbuf, *ubuf, *obuf;
     EpWait wait;  // expert-parallel peer exchange: the rows' arrival (flags null: none)
+    int routed;   // 1: ridx / rw already hold this batch's choices (k_broute_tokens)
 };
+// Routing alone, one warp per token (engine.cu:883-892): many tokens (a
+// prefill chunk) are routed by many CTAs instead of k_broute's 32 warps.
+// grid ceil(B/8), 256 threads.
+__global__ void __launch_bounds__(256) k_broute_tokens(const float* __restrict__ logits, const __half* __restrict__ bias,
+                                                       int B, int E, int topk, int* ridx, float* rw) {
+    const int b = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (b < B) route_select_warp(logits + (size_t)b * E, bias, E, topk, ridx + b * topk, rw + b * topk);
+}
 __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
     __shared__ int sidx[1024];
     __shared__ int cnt[256], off[256];
@@ -579,7 +587,7 @@ __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
     const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int n = P.keys ? P.n : P.B * P.topk, NE = P.keys ? P.n_local : P.E;
     for (int e = threadIdx.x; e < NE; e += blockDim.x) cnt[e] = 0;
-    if (!P.keys)
+    if (!P.keys && !P.routed)
         for (int b = warp; b < P.B; b += nw)
             route_select_warp(P.logits + (size_t)b * P.E, P.bias, P.E, P.topk, P.ridx + b * P.topk,
                               P.rw + b * P.topk);
@@ -2057,6 +2065,8 @@ int moe_grouped_prefill(cuinf_model* m, int layer, const __half* xn, __half* h, 
         R.gbuf = tc->fg;
         R.ubuf = tc->fu;
         R.obuf = tc->fo;
+        R.routed = 1;
+        k_broute_tokens<<<(n + 7) / 8, 256, 0, st>>>(tc->rlog, L.ebias, n, E, K, R.ridx, R.rw);
         k_broute<<<1, 1024, 0, st>>>(R);
         k_bgather<<<n * K, 256, 0, st>>>(xn + (size_t)c0 * H, tc->src, tc->xg, H);
         if ((rc = cuinf_launch_status())) return rc;

@@ -55,9 +55,10 @@ struct TcGroup {
 };
 
 struct TcParams {
-    const TcGroup* groups;  // device table, or null: one group, g0
+    const TcGroup* groups;  // device table, or null: g0, or (n_groups > 1) g0 cut into 128-row groups
     TcGroup g0;
     int n_groups;
+    int m_rows;                    // without a table: g0's activation rows in all (group g = rows 128g..)
     int tiles;                     // 128-row tiles per group (of the largest N)
     int K;
     int splits, kg_per_split;
@@ -240,7 +241,16 @@ __device__ __forceinline__ bool tc_item(const TcParams& P, int it, int KG, TcIte
     const int gt = it / P.splits;
     t.tile = gt % P.tiles;
     t.g = gt / P.tiles;
-    t.G = P.groups ? P.groups[t.g] : P.g0;
+    if (P.groups) {
+        t.G = P.groups[t.g];
+    } else {
+        t.G = P.g0;
+        if (P.n_groups > 1) {
+            t.G.x_row = P.g0.x_row + t.g * TC_NMAX;
+            t.G.rows = min(TC_NMAX, P.m_rows - t.g * TC_NMAX);
+            if (t.G.y) t.G.y += (size_t)t.g * TC_NMAX * t.G.ldy;
+        }
+    }
     t.n0 = t.tile * TC_ROWS;
     if (t.G.rows <= 0 || t.n0 >= t.G.N) return false;
     t.kg0 = t.split * P.kg_per_split;
@@ -307,8 +317,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == TC_DQ_WARPS) {
         // ---- weight producer ----
         const uint64_t pol = l2_policy_evict_first();
-        int last[TC_PST];
-        for (int s = 0; s < TC_PST; s++) last[s] = -1;
+        // last copy issued per stage: the INT4 ring (TC_PST) or, for fp16
+        // weights, the operand stages (up to TC_OSTMAX)
+        constexpr int NLAST = TC_PST > TC_OSTMAX ? TC_PST : TC_OSTMAX;
+        int last[NLAST];
+        for (int s = 0; s < NLAST; s++) last[s] = -1;
         uint32_t pc = 0;
         bool ok = true;
         if (lane == 0 && !P.groups) tc_prefetch_map(&wmap0);

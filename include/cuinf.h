@@ -273,7 +273,7 @@ int cuinf_batch_create(cuinf_model* m, int n_seqs, int max_ctx, void* stream, cu
  * (every rank's exchange arena is mapped into every process with cudaIpc;
  * only the rows that exist cross NVLink, the sender's own rows stay local)
  * and raises a flag there that the receiver's next kernel waits for (at most
- * 4 s, then bit 2 of cuinf_batch_error is set).  When an arena cannot be
+ * 4 s, then bit 4 (value 16) of cuinf_batch_error's first word is set).  When an arena cannot be
  * mapped on some rank, every rank uses NCCL send/recv of fixed capacity
  * (n_seqs*top_k rows per peer) instead.  nccl_id: cuinf_ep_unique_id on
  * rank 0, broadcast to all ranks.  Every rank steps together. */
