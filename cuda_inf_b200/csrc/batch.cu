@@ -577,6 +577,40 @@ __global__ void __launch_bounds__(256) k_broute_tokens(const float* __restrict__
     const int b = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (b < B) route_select_warp(logits + (size_t)b * E, bias, E, topk, ridx + b * topk, rw + b * topk);
 }
+// The grouped GEMMs' tables from the per-expert row counts and offsets:
+// expert ex's rows [off, off + cnt) of the gathered buffer form up to maxch
+// groups of TC_NMAX rows (w1, w3 into gbuf / ubuf; w2 into obuf).
+__device__ void bgroup_tables(const BRouteParams& P, const int* cnt, const int* off, int NE) {
+    for (int ex = threadIdx.x; ex < NE; ex += blockDim.x) {
+        for (int c = 0; c < P.maxch; c++) {
+            const int r0 = off[ex] + c * TC_NMAX;
+            const int rows = max(0, min(TC_NMAX, cnt[ex] - c * TC_NMAX));
+            const int gi = ex * P.maxch + c;
+            TcGroup a;
+            a.wmap = P.maps + ex * 3 + 0;
+            a.packed = (const uint8_t*)P.experts[ex * 6 + 0];
+            a.scales = (const __half*)P.experts[ex * 6 + 1];
+            a.y = P.gbuf + (size_t)r0 * P.I;
+            a.x_row = r0;
+            a.rows = rows;
+            a.N = P.I;
+            a.ldy = P.I;
+            P.g13[gi] = a;
+            a.wmap = P.maps + ex * 3 + 1;
+            a.packed = (const uint8_t*)P.experts[ex * 6 + 2];
+            a.scales = (const __half*)P.experts[ex * 6 + 3];
+            a.y = P.ubuf + (size_t)r0 * P.I;
+            P.g13[NE * P.maxch + gi] = a;
+            a.wmap = P.maps + ex * 3 + 2;
+            a.packed = (const uint8_t*)P.experts[ex * 6 + 4];
+            a.scales = (const __half*)P.experts[ex * 6 + 5];
+            a.y = P.obuf + (size_t)r0 * P.H;
+            a.N = P.H;
+            a.ldy = P.H;
+            P.g2[gi] = a;
+        }
+    }
+}
 __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
     __shared__ int sidx[1024];
     __shared__ int cnt[256], off[256];
@@ -623,35 +657,43 @@ __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
     __syncthreads();
     if (threadIdx.x < n) P.inv[threadIdx.x] = e >= 0 ? off[e] + rank : -1;
     if (e >= 0) P.src[off[e] + rank] = P.keys ? (int)threadIdx.x : (int)threadIdx.x / P.topk;
-    for (int ex = threadIdx.x; ex < NE; ex += blockDim.x) {
-        for (int c = 0; c < P.maxch; c++) {
-            const int r0 = off[ex] + c * TC_NMAX;
-            const int rows = max(0, min(TC_NMAX, cnt[ex] - c * TC_NMAX));
-            const int gi = ex * P.maxch + c;
-            TcGroup a;
-            a.wmap = P.maps + ex * 3 + 0;
-            a.packed = (const uint8_t*)P.experts[ex * 6 + 0];
-            a.scales = (const __half*)P.experts[ex * 6 + 1];
-            a.y = P.gbuf + (size_t)r0 * P.I;
-            a.x_row = r0;
-            a.rows = rows;
-            a.N = P.I;
-            a.ldy = P.I;
-            P.g13[gi] = a;
-            a.wmap = P.maps + ex * 3 + 1;
-            a.packed = (const uint8_t*)P.experts[ex * 6 + 2];
-            a.scales = (const __half*)P.experts[ex * 6 + 3];
-            a.y = P.ubuf + (size_t)r0 * P.I;
-            P.g13[NE * P.maxch + gi] = a;
-            a.wmap = P.maps + ex * 3 + 2;
-            a.packed = (const uint8_t*)P.experts[ex * 6 + 4];
-            a.scales = (const __half*)P.experts[ex * 6 + 5];
-            a.y = P.obuf + (size_t)r0 * P.H;
-            a.N = P.H;
-            a.ldy = P.H;
-            P.g2[gi] = a;
+    bgroup_tables(P, cnt, off, NE);
+}
+
+// Grouping of n entries (any n; the prefill's (token, slot) choices, already
+// routed): per-expert counts, offsets, then each entry takes the next row of
+// its expert.  Rows of one expert are ordered by arrival, not by token: each
+// row's products are independent of its place in the group, so the results
+// are the same in any order.  One CTA of 1024 threads; E <= 256.
+__global__ void __launch_bounds__(1024) k_bgroup_many(const BRouteParams P) {
+    __shared__ int cnt[256], off[256], fill[256];
+    const int n = P.n, NE = P.E;
+    for (int e = threadIdx.x; e < NE; e += blockDim.x) cnt[e] = fill[e] = 0;
+    __syncthreads();
+    for (int j = threadIdx.x; j < n; j += blockDim.x) atomicAdd(&cnt[P.ridx[j]], 1);
+    __syncthreads();
+    if (threadIdx.x < 32) {  // exclusive prefix over experts, one warp
+        int carry = 0;
+        for (int base = 0; base < NE; base += 32) {
+            const int i = base + threadIdx.x;
+            const int v = i < NE ? cnt[i] : 0;
+            int x = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if ((int)threadIdx.x >= o) x += y;
+            }
+            if (i < NE) off[i] = carry + x - v;
+            carry += __shfl_sync(0xffffffffu, x, 31);
         }
     }
+    __syncthreads();
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        const int e = P.ridx[j], pos = off[e] + atomicAdd(&fill[e], 1);
+        P.inv[j] = pos;
+        P.src[pos] = j / P.topk;
+    }
+    bgroup_tables(P, cnt, off, NE);
 }
 
 __global__ void k_bgather(const __half* __restrict__ xn, const int* __restrict__ src, __half* xg, int H) {
@@ -1944,8 +1986,9 @@ extern "C" int cuinf_batch_profile_step(cuinf_batch* b, int max_kernels, float* 
 
 // ===========================================================================
 // Grouped MoE for prefill: the S tokens of one prompt go through the same
-// routing / grouping / grouped-GEMM / combine kernels as a decode batch, in
-// chunks of up to 1024/top_k tokens (one routing CTA handles 1024 entries).
+// routing / grouped-GEMM / combine kernels as a decode batch, in chunks of up
+// to PF_MOE_ROWS/top_k tokens: routed one warp per token, grouped by
+// k_bgroup_many.
 // ===========================================================================
 struct TcCache {
     std::mutex mu;
@@ -1968,6 +2011,10 @@ void tc_cache_free(cuinf_model* m) {
     m->tc_cache = nullptr;
 }
 
+// (token, slot) rows per prefill MoE chunk: every expert's weights are read
+// once per chunk, so larger chunks read them fewer times (4096 rows = 1024
+// tokens at top-4 hold about 120 MB of gathered rows and expert outputs)
+#define PF_MOE_ROWS 4096
 static int tc_cache_get(cuinf_model* m, TcCache** out) {
     if (m->tc_cache) {
         *out = (TcCache*)m->tc_cache;
@@ -2006,7 +2053,7 @@ static int tc_cache_get(cuinf_model* m, TcCache** out) {
     if (cudaMemcpy(tc->dmaps, tc->hmaps.data(), tc->hmaps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice) !=
         cudaSuccess)
         return fail(cuinf_set_arg_error("tensor map upload failed"));
-    const int C = 1024 / K, R = C * K, maxch = (C + TC_NMAX - 1) / TC_NMAX;
+    const int C = PF_MOE_ROWS / K, R = C * K, maxch = (C + TC_NMAX - 1) / TC_NMAX;
     tc->chunk = C;
     if ((rc = al((void**)&tc->rlog, (size_t)C * E * 4)) || (rc = al((void**)&tc->rw, (size_t)R * 4)) ||
         (rc = al((void**)&tc->fg, (size_t)R * I * 4)) || (rc = al((void**)&tc->fu, (size_t)R * I * 4)) ||
@@ -2067,7 +2114,7 @@ int moe_grouped_prefill(cuinf_model* m, int layer, const __half* xn, __half* h, 
         R.obuf = tc->fo;
         R.routed = 1;
         k_broute_tokens<<<(n + 7) / 8, 256, 0, st>>>(tc->rlog, L.ebias, n, E, K, R.ridx, R.rw);
-        k_broute<<<1, 1024, 0, st>>>(R);
+        k_bgroup_many<<<1, 1024, 0, st>>>(R);
         k_bgather<<<n * K, 256, 0, st>>>(xn + (size_t)c0 * H, tc->src, tc->xg, H);
         if ((rc = cuinf_launch_status())) return rc;
         const int t13 = (I + TC_ROWS - 1) / TC_ROWS, t2 = (H + TC_ROWS - 1) / TC_ROWS;

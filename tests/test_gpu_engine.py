@@ -104,14 +104,14 @@ def prefill_compare(cfg, om, s, st, ids):
     return got, e, checked, near
 
 
-@pytest.mark.parametrize("past,S", [(0, 1), (0, 70), (30, 50), (64, 64), (0, 600)])
+@pytest.mark.parametrize("past,S", [(0, 1), (0, 70), (30, 50), (64, 64), (0, 600), (0, 2100)])
 def test_prefill_matches_oracle(tiny, past, S):
     """Batched prefill of S ids after `past` decode steps (the reference's
     prefill starts at 0; later starts continue a session), then 20
     teacher-forced decode steps: the group commits inside the prefill
     (tokens 64 and 128) and the attention over committed FP8 groups plus the
-    fp16 tail must follow the oracle.  S = 600 runs the grouped expert GEMMs
-    over two chunks of 1024/top_k tokens."""
+    fp16 tail must follow the oracle.  S = 2100 runs the grouped expert GEMMs
+    over two chunks of 4096/top_k tokens."""
     cfg, om, gm = tiny
     rng = np.random.default_rng(1000 + past + S)
     lead = rng.integers(0, cfg.vocab, past)
