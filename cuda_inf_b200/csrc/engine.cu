@@ -1592,19 +1592,28 @@ extern "C" int cuinf_prefill(cuinf_session* s, const int* ids, int S, int* out_t
                 goto ffn;
             }
             {
-            int committed = (past / CUINF_KVGROUP) * CUINF_KVGROUP;
-            for (int placed = 0; placed < S;) {
-                const int slot = past + placed - committed;
-                const int can = std::min(S - placed, CUINF_KVGROUP - slot);
-                PF(cuinf_kv_write_tail(k16 + (size_t)placed * NK, v16 + (size_t)placed * NK, A.ktail, A.vtail,
-                                       slot, can, nkv, vs));
-                placed += can;
+            // the group already begun in the tail is completed there; whole
+            // groups of new rows are committed straight from the rows (one
+            // launch); the remainder starts the new tail
+            int committed = (past / CUINF_KVGROUP) * CUINF_KVGROUP, placed = 0;
+            if (past > committed) {
+                const int slot = past - committed, can = std::min(S, CUINF_KVGROUP - slot);
+                PF(cuinf_kv_write_tail(k16, v16, A.ktail, A.vtail, slot, can, nkv, vs));
+                placed = can;
                 if (slot + can == CUINF_KVGROUP) {
                     PF(cuinf_kv_commit_group(A.ktail, A.vtail, A.kc8, A.vc8, A.ksc, A.vsc, committed,
                                              committed / CUINF_KVGROUP, nkv, vs));
                     committed += CUINF_KVGROUP;
                 }
             }
+            const int whole = (S - placed) / CUINF_KVGROUP;
+            PF(kv_commit_rows(k16 + (size_t)placed * NK, v16 + (size_t)placed * NK, A.kc8, A.vc8, A.ksc, A.vsc,
+                              whole, committed, committed / CUINF_KVGROUP, nkv, st));
+            committed += whole * CUINF_KVGROUP;
+            placed += whole * CUINF_KVGROUP;
+            if (placed < S)
+                PF(cuinf_kv_write_tail(k16 + (size_t)placed * NK, v16 + (size_t)placed * NK, A.ktail, A.vtail, 0,
+                                       S - placed, nkv, vs));
             if (S >= PF_TC_MIN_ROWS && (nh / nkv == 1 || nh / nkv == 2 || nh / nkv == 4)) {
                 const dim3 grid((S + APF_TOK - 1) / APF_TOK, nkv);
                 const float sc = 1.0f / sqrtf((float)hd);

@@ -48,6 +48,8 @@ struct cuinf_model {
 int moe_grouped_prefill(cuinf_model* m, int layer, const __half* xn, __half* h, int S, int* ridx,
                         cudaStream_t st);
 void tc_cache_free(cuinf_model* m);
+int kv_commit_rows(const __half* k, const __half* v, uint8_t* kc8, uint8_t* vc8, __half* ksc, __half* vsc,
+                   int n_groups, int tok_base, int grp0, int nkv, cudaStream_t st);
 
 struct AttnState {
     uint8_t *kc8 = nullptr, *vc8 = nullptr;

@@ -315,6 +315,25 @@ extern "C" int cuinf_kv_commit_group(const void* ktail, const void* vtail, uint8
     return cuinf_launch_status();
 }
 
+// Prefill: n whole groups committed straight from rows [64n][nkv][64] of new
+// keys and values (each group's rows have the tail's layout, so the result
+// is what writing them to the tail and committing would give).  grid (n, nkv).
+__global__ void k_kv_commit_rows(const __half* __restrict__ k, const __half* __restrict__ v, uint8_t* kc8,
+                                 uint8_t* vc8, __half* ksc, __half* vsc, int tok_base, int grp0, int nkv) {
+    __shared__ float red[32];
+    const int g = blockIdx.x, h = blockIdx.y;
+    const size_t off = (size_t)g * CUINF_KVGROUP * nkv * CUINF_HD;
+    kv_commit_head(k + off, kc8, ksc, h, nkv, tok_base + g * CUINF_KVGROUP, grp0 + g, red);
+    __syncthreads();
+    kv_commit_head(v + off, vc8, vsc, h, nkv, tok_base + g * CUINF_KVGROUP, grp0 + g, red);
+}
+int kv_commit_rows(const __half* k, const __half* v, uint8_t* kc8, uint8_t* vc8, __half* ksc, __half* vsc,
+                   int n_groups, int tok_base, int grp0, int nkv, cudaStream_t st) {
+    if (n_groups <= 0) return CUINF_OK;
+    k_kv_commit_rows<<<dim3(n_groups, nkv), 256, 0, st>>>(k, v, kc8, vc8, ksc, vsc, tok_base, grp0, nkv);
+    return cuinf_launch_status();
+}
+
 // ---------------------------------------------------------------------------
 // short conv (engine.cu:483-525)
 // ---------------------------------------------------------------------------
