@@ -818,7 +818,8 @@ PHASES = {  # kernel id (csrc/common.cuh PH_*) -> (name, {slot: phase reached})
     6: ("k_lmhead", {0: "start", 1: "dependency wait done", 2: "norm done", 3: "rows done",
                      9: "token published (last CTA)"}),
     7: ("k_attn_decode", {0: "start", 1: "dependency wait done", 2: "keys done (warp 0)",
-                          3: "combining CTA elected", 4: "combine done"}),
+                          3: "splits merged (cluster) / combining CTA elected (global)",
+                          4: "cluster released / combine done (global)"}),
 }
 
 

@@ -88,6 +88,7 @@ _SIGS = {
                                ctypes.POINTER(c_int)]),
     "cuinf_session_keep_logits": (c_int, [c_void_p, c_int]),
     "cuinf_session_set_option": (c_int, [c_void_p, c_int, c_int]),
+    "cuinf_session_attn_cluster": (c_int, [c_void_p]),
     "cuinf_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "cuinf_tokenizer_load": (c_int, [ctypes.c_char_p, c_void_p]),
     "cuinf_tokenizer_free": (c_int, [c_void_p]),

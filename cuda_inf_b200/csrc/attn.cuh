@@ -16,7 +16,12 @@
 // Online softmax in base 2 with finite sentinels; per-unit V scale applied
 // to a fresh accumulator.  Partials (m, l, O) per (h, sp, query head) go to
 // the workspace; the last CTA of each kv head (atomic ticket) merges them.
+// Cluster form (P.cluster = nsplit, launched with clusters of (1, nsplit)):
+// the partials stay in each CTA's shared memory and the cluster's CTAs merge
+// them over DSMEM, each a slice of the outputs, in the same split order and
+// arithmetic (no workspace, no ticket).
 #pragma once
+#include <cooperative_groups.h>
 #include "common.cuh"
 
 struct AttnParams {
@@ -35,6 +40,7 @@ struct AttnParams {
     unsigned* counters;   // [nkv], zero before the first launch; left zero
     int nh, nkv, nsplit;  // nsplit * (nh/nkv) <= ATTN_MAX_PARTS
     L2Ranges next;        // weights of the following kernels, prefetched to L2
+    int cluster = 0;      // > 0: the nsplit (= cluster) CTAs of a kv head merge over DSMEM
     // batched decode: sequence blockIdx.z reads its q, cache, position and
     // writes its output at these element strides (counters at b * nkv)
     size_t bq = 0, bkv8 = 0, bsc = 0, btail = 0, bout = 0, bpart = 0;
@@ -219,7 +225,10 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
     }
 }
 
-__global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
+// MINB: CTAs per SM the register budget is cut for (1: no spills; 2: the
+// standalone operator, whose default split count assumes two CTAs per SM).
+template <int MINB>
+__global__ void __launch_bounds__(ATTN_THREADS, MINB) k_attn_decode(AttnParams P) {
     __shared__ __align__(16) float sm[ATTN_THREADS / 32][16][ATTN_PART_STRIDE];
     __shared__ int s_last;
     const int h = blockIdx.x, sp = blockIdx.y;
@@ -290,6 +299,49 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnParams P) {
         }
     }
     __syncthreads();
+    if (P.cluster) {
+        // ---- cluster form: this CTA's partial in shared memory, merged over DSMEM ----
+        __shared__ __align__(16) float cpart[8][ATTN_PART_STRIDE];
+        for (int it = threadIdx.x; it < gqa * 64; it += blockDim.x) {
+            const int r = it >> 6, d = it & 63;
+            float mm = ATTN_NEG;
+#pragma unroll
+            for (int w = 0; w < ATTN_THREADS / 32; w++) mm = fmaxf(mm, sm[w][r][0]);
+            float l = 0.f, o = 0.f;
+#pragma unroll
+            for (int w = 0; w < ATTN_THREADS / 32; w++) {
+                const float e = exp2f(sm[w][r][0] - mm);
+                l += sm[w][r][1] * e;
+                o += sm[w][r][4 + d] * e;
+            }
+            cpart[r][4 + d] = o;
+            if (d == 0) { cpart[r][0] = mm; cpart[r][1] = l; }
+        }
+        cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
+        cl.sync();  // every split's partial is in its CTA
+        const int ncl = (int)cl.num_blocks(), rank = (int)cl.block_rank();
+        const int per = (gqa * 64 + ncl - 1) / ncl, end = min(gqa * 64, (rank + 1) * per);
+        for (int it = rank * per + (int)threadIdx.x; it < end; it += blockDim.x) {
+            const int r = it >> 6, d = it & 63;
+            float gm = ATTN_NEG, L = 0.f, o = 0.f;
+            for (int s2 = 0; s2 < ncl; s2++) {
+                const float* pr = cl.map_shared_rank(&cpart[r][0], s2);
+                if (pr[1] > 0.f) gm = fmaxf(gm, pr[0]);
+            }
+            for (int s2 = 0; s2 < ncl; s2++) {
+                const float* pr = cl.map_shared_rank(&cpart[r][0], s2);
+                const float vl = pr[1];
+                const float e = vl > 0.f ? exp2f(pr[0] - gm) : 0.f;
+                L += vl * e;
+                o += e * pr[4 + d];
+            }
+            P.out[b * P.bout + (size_t)(h * gqa + r) * CUINF_HD + d] = __float2half_rn(o / L);
+        }
+        PHASE(PH_ATTN, 3);
+        cl.sync();  // no CTA leaves while another reads its partial
+        PHASE(PH_ATTN, 4);
+        return;
+    }
     float* part = part_b + ((size_t)(h * P.nsplit + sp) * gqa) * ATTN_PART_STRIDE;
     for (int it = threadIdx.x; it < gqa * 64; it += blockDim.x) {
         const int r = it >> 6, d = it & 63;

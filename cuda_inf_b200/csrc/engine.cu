@@ -124,7 +124,7 @@ extern "C" int cuinf_attn_decode(const void* q, const uint8_t* kc8, const uint8_
     P.nsplit = ns;
     P.next.count = 0;
     if (workspace) CUINF_TRY(cudaMemsetAsync(ws, 0, 256, ST(stream)));
-    k_attn_decode<<<dim3(nkv, ns), ATTN_THREADS, 0, ST(stream)>>>(P);
+    k_attn_decode<2><<<dim3(nkv, ns), ATTN_THREADS, 0, ST(stream)>>>(P);
     return cuinf_launch_status();
 }
 
@@ -165,7 +165,7 @@ int attn_decode_batched(const BatchAttnArgs& a, cudaStream_t st) {
     P.btail = a.btail;
     P.bout = a.bout;
     P.bpart = a.bpart;
-    k_attn_decode<<<dim3(a.nkv, a.nsplit, a.n_seqs), ATTN_THREADS, 0, st>>>(P);
+    k_attn_decode<1><<<dim3(a.nkv, a.nsplit, a.n_seqs), ATTN_THREADS, 0, st>>>(P);
     return cuinf_launch_status();
 }
 
@@ -259,7 +259,7 @@ extern "C" int cuinf_attn_decode_noalloc(const void* q, const uint8_t* kc8, cons
     // zero; clearing them here on the stream (a memset, no allocation) also
     // covers a launch that an earlier error cut short.
     CUINF_TRY(cudaMemsetAsync(ws, 0, 256, ST(stream)));
-    k_attn_decode<<<dim3(nkv, ns), ATTN_THREADS, 0, ST(stream)>>>(P);
+    k_attn_decode<2><<<dim3(nkv, ns), ATTN_THREADS, 0, ST(stream)>>>(P);
     return cuinf_launch_status();
 }
 
@@ -304,6 +304,54 @@ static cudaError_t launch_kc(Kern kernel, dim3 grid, dim3 block, size_t smem, cu
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
+// Same, with thread-block clusters of cluster_y CTAs along y.
+template <typename Kern, typename Par>
+static cudaError_t launch_kcy(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                              int cluster_y, const Par& params) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = cluster_y;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
+// Largest cluster (<= 16 CTAs, one per split) with which the decode
+// attention's nkv clusters all fit on the device at once; 0 if none.
+static int attn_cluster_size(int nkv, int nsplit) {
+    const int cl = std::min(nsplit, 16);
+    if (cl < 2) return 0;
+    if (cl > 8 && cudaFuncSetAttribute(k_attn_decode<1>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nkv, cl);
+    cfg.blockDim = dim3(ATTN_THREADS);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = cl;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, k_attn_decode<1>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n >= nkv ? cl : 0;
 }
 
 static int set_kernel_attrs(const cuinf_config& c);
@@ -704,6 +752,8 @@ struct cuinf_session {
     int tok_slot = 0;
     int host_pos = 0;
     int num_sms = 148;
+    int attn_cluster = 0;        // cluster size of the DSMEM split merge (0: not available)
+    bool attn_use_cluster = true;  // CUINF_OPT_ATTN_CLUSTER
     bool prefetch = true;  // L2 prefetch plans (cross-kernel weight streaming)
     bool pdl = true;       // programmatic dependent launch between the step's kernels
     bool prefill = true;   // cuinf_generate prefills its prompt
@@ -1040,6 +1090,7 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
             P.nh = nh; P.nkv = nkv; P.nsplit = s->nsplit;
             const double ctx = s->host_pos + 1, cm = 64.0 * floor(ctx / 64.0);
             const int nsplit = s->nsplit;
+            const int cluster = s->attn_use_cluster ? s->attn_cluster : 0;
             if (s->h2o_C) {  // H2O: slot choice + quantized write, then attention over the slots
                 H2oParams Z = h2o_params(s, l, s->kv_new, s->kv_new + nkv * 64, s->q, s->attn_out, s->pos, 0, 1,
                                          s->h2o_dst + l);
@@ -1058,7 +1109,12 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
                               {},
                               [=](const L2Ranges& nx, bool pdl) mutable {
                                   P.next = nx;
-                                  return launch_k(k_attn_decode, dim3(nkv, nsplit), dim3(ATTN_THREADS), 0, st, pdl, P);
+                                  if (cluster) {
+                                      P.cluster = cluster;
+                                      return launch_kcy(k_attn_decode<1>, dim3(nkv, nsplit), dim3(ATTN_THREADS), 0,
+                                                        st, pdl, cluster, P);
+                                  }
+                                  return launch_k(k_attn_decode<1>, dim3(nkv, nsplit), dim3(ATTN_THREADS), 0, st, pdl, P);
                               }});
             }
             ResParams R;
@@ -1299,6 +1355,11 @@ extern "C" int cuinf_session_create(cuinf_model* m, int max_ctx, void* stream, c
     // k_attn_decode holds one CTA per SM (its registers): keep every split
     // of every kv head in one wave
     s->nsplit = std::min(attn_engine_nsplit(gqa, units), std::max(1, s->num_sms / nkv));
+    // with clusters the splits of a kv head merge over DSMEM: at most 16
+    // splits (both merge paths then use the same splits, so they agree bit
+    // for bit)
+    s->attn_cluster = attn_cluster_size(nkv, s->nsplit);
+    if (s->attn_cluster) s->nsplit = s->attn_cluster;
     TRYS(dalloc(s, &s->attn_part, (size_t)nkv * s->nsplit * gqa * ATTN_PART_STRIDE * 4));
     TRYS(dalloc(s, &s->attn_cnt, (size_t)nkv * 4));
     bool bias16 = true;  // the fused MoE kernel copies each router bias with 16-byte async copies
@@ -1797,6 +1858,7 @@ extern "C" int cuinf_session_set_option(cuinf_session* s, int option, int value)
             : option == CUINF_OPT_PDL      ? &s->pdl
             : option == CUINF_OPT_MEGAKERNEL ? &s->use_mk
             : option == CUINF_OPT_TRACE      ? &s->trace
+            : option == CUINF_OPT_ATTN_CLUSTER ? &s->attn_use_cluster
                                              : nullptr;
     REQUIRE(f, "unknown option");
     if ((bool)value == *f) return CUINF_OK;
@@ -1804,6 +1866,8 @@ extern "C" int cuinf_session_set_option(cuinf_session* s, int option, int value)
     *f = value != 0;
     return build_graph(s);
 }
+
+extern "C" int cuinf_session_attn_cluster(const cuinf_session* s) { return s && s->attn_cluster ? 1 : 0; }
 
 extern "C" int cuinf_session_trace(cuinf_session* s, unsigned long long* buf, int cap, int* kinds,
                                    int* n_stages, int* n_ctas) {

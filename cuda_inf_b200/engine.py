@@ -145,7 +145,7 @@ class Session:
         check(lib().cuinf_generate(self._h, p, len(prompt), n_new, eos, o, ctypes.byref(n)))
         return list(o[:n.value])
 
-    OPT_PREFETCH, OPT_PDL, OPT_MEGAKERNEL, OPT_TRACE, OPT_PREFILL = 1, 2, 3, 4, 5
+    OPT_PREFETCH, OPT_PDL, OPT_MEGAKERNEL, OPT_TRACE, OPT_PREFILL, OPT_ATTN_CLUSTER = 1, 2, 3, 4, 5, 6
     STAGE_KINDS = ("conv_in", "residual", "qkv", "attention", "dense_up", "moe_up", "moe_down",
                    "lm_head")
 
@@ -187,6 +187,11 @@ class Session:
         dependent launch between the step's kernels (both default on)."""
         check(lib().cuinf_session_set_option(self._h, int(option), int(value)))
 
+
+    @property
+    def attn_cluster(self):
+        """True if decode attention can merge its splits over a cluster."""
+        return bool(lib().cuinf_session_attn_cluster(self._h))
     def keep_logits(self, on=True):
         check(lib().cuinf_session_keep_logits(self._h, 1 if on else 0))
 

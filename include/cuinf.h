@@ -385,6 +385,14 @@ int cuinf_session_keep_logits(cuinf_session* s, int on);
 /* CUINF_OPT_PREFILL: cuinf_generate consumes its prompt with cuinf_prefill,
  * as the reference does (default 1); 0 feeds it through decode steps. */
 #define CUINF_OPT_PREFILL 5
+/* CUINF_OPT_ATTN_CLUSTER: decode attention merges the splits of a kv head
+ * over distributed shared memory inside a thread-block cluster (default 1;
+ * used when the device holds all kv heads' clusters at once); 0 merges them
+ * through global memory with an atomic ticket.  Both use the same splits and
+ * give the same results. */
+#define CUINF_OPT_ATTN_CLUSTER 6
+/* 1 if this session's decode attention can merge over clusters. */
+int cuinf_session_attn_cluster(const cuinf_session* s);
 int cuinf_session_set_option(cuinf_session* s, int option, int value);
 /* H2O eviction mode (the reference's --kv-budget / --kv-window,
  * engine.cu:310-384, 579-581, 753-756, 803-828): each attention layer keeps

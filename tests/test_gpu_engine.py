@@ -83,6 +83,23 @@ def test_engine_options_do_not_change_results(tiny, opt):
         assert np.array_equal(a.logits().cpu().numpy(), b.logits().cpu().numpy())
 
 
+def test_attention_cluster_merge_matches_global_merge(tiny):
+    """Decode attention merging its splits over DSMEM in a cluster gives the
+    same logits, bit for bit, as the global-memory merge of the same splits
+    (600 positions: several 64-token groups, so several splits)."""
+    cfg, om, gm = tiny
+    a = Session(gm, max_ctx=600)
+    b = Session(gm, max_ctx=600)
+    assert a.attn_cluster, "the device should hold the attention clusters"
+    b.set_option(Session.OPT_ATTN_CLUSTER, 0)
+    a.keep_logits(True)
+    b.keep_logits(True)
+    for t in np.random.default_rng(10).integers(0, cfg.vocab, 300):
+        assert a.step(int(t)) == b.step(int(t))
+        assert np.array_equal(a.logits().cpu().numpy(), b.logits().cpu().numpy())
+    assert device_error() == 0
+
+
 # Prefill rows run through the tensor-core GEMMs and the prefill attention,
 # whose fp32 sums differ from decode's in order; over hundreds of rows the
 # engine-vs-oracle router score difference reaches ~1.2e-3 (observed at row
