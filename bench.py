@@ -930,6 +930,9 @@ def main():
     ap.add_argument("--batch-warmup", type=int, default=3)
     ap.add_argument("--phase-trace", action="store_true",
                     help="diagnostic: per-phase timestamps of the decode kernels (needs build --trace)")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="only the config-5b prefill of --prefill-len tokens (with --profile-small: on the 6-layer "
+                         "model, for profiler captures)")
     ap.add_argument("--batch-only", action="store_true",
                     help="only the config-5 batched decode (with --profile-small: on the 6-layer model, for "
                          "profiler captures)")
@@ -967,6 +970,18 @@ def main():
     if a.tc_gemm_only:
         if rank == 0:
             print(json.dumps({"profiling_only": True, "gemm_int4_tc_batch64": gemm_tc_batch()}), flush=True)
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+        return
+    if a.prefill_only:
+        from cuda_inf_b200 import weights as W
+        from cuda_inf_b200.engine import Model
+        cfg = (W.make_config(n_layers=6, n_dense=1, vocab=32000, attn_layers=(2, 5)) if a.profile_small
+               else W.default_config())
+        blob, idx = W.synth_device_blob(cfg, seed=a.seed)
+        res = run_prefill(a, Model.from_device_blob(blob, idx, cfg), cfg)
+        if rank == 0:
+            print(json.dumps({"profiling_only": a.profile_small, "prefill_config5b": res}), flush=True)
         if ws > 1:
             torch.distributed.destroy_process_group()
         return
