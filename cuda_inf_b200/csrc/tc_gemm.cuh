@@ -6,10 +6,13 @@
 // activation rows (the MMA's N; tokens of a batch or of one expert's group)
 // over a K range (split-K across CTAs, reduced in a fixed order).
 //   warp 8   TMA producer of the packed INT4 rows (2-D tensor map, box
-//            64 bytes x 128 rows, 64-byte swizzle) into a 6-deep ring; for
-//            fp16 weights it loads the A operand directly (128-byte swizzle);
+//            64 bytes x 128 rows, 64-byte swizzle) into a 4-deep ring; for
+//            fp16 weights it loads the A operand directly into the three
+//            A stages (128-byte swizzle);
 //   warp 9   TMA producer of the activation rows (box 64 halves x xbox
-//            rows, 128-byte swizzle, which is the K-major UMMA layout);
+//            rows, 128-byte swizzle, which is the K-major UMMA layout) into
+//            their own ring of up to 8 stages, so they are requested several
+//            stages ahead of the A stages they meet in the MMA;
 //   warps 0-7 dequantize 128 K (one scale group) per stage to (nib-8),
 //            exact in fp16 via the 1024-magic, written in the
 //            128-byte-swizzled K-major layout;
@@ -32,8 +35,9 @@
 #define TC_ROWS 128
 #define TC_KS 128
 #define TC_NMAX 128
-#define TC_PST 8    // packed-weight ring (INT4)
-#define TC_OSTMAX 4 // operand stages (A + X): up to 3 with INT4 weights, 4 with fp16
+#define TC_PST 4     // packed-weight ring (INT4)
+#define TC_NA 3      // A operand stages (dequantized INT4 or fp16 weights), 32 KB each
+#define TC_XSTMAX 8  // activation stages: their own ring, so their copies run ahead of the A stages
 #define TC_NACC 3   // INT4 per-group accumulators in TMEM (the sum follows them)
 #define TC_DQ_WARPS 8
 #define TC_ACC_WARP0 12
@@ -74,7 +78,7 @@ struct TcParams {
 
 struct TcSmem {
     uint64_t p_full[TC_PST], p_empty[TC_PST];
-    uint64_t a_full[TC_OSTMAX], x_full[TC_OSTMAX], op_empty[TC_OSTMAX];
+    uint64_t a_full[TC_NA], a_empty[TC_NA], x_full[TC_XSTMAX], x_empty[TC_XSTMAX];
     uint64_t acc_full[TC_NACC], acc_empty[TC_NACC];
     uint64_t epi;  // the four epilogue warps' own barrier (bounded, unlike bar.sync)
     uint64_t done;
@@ -84,15 +88,14 @@ struct TcSmem {
     unsigned long long amax[4][TC_NMAX];
 };
 
-// INT4: operand stages (A 32 KB + X xmax*256 B each) in the first
-// TC_OPS_BYTES, then the packed ring; fp16: operand stages over the whole ring.
-static constexpr size_t TC_OPS_BYTES = 144 * 1024;
+// The A stages (TC_NA x 32 KB), then the activation stages (xmax*256 B each,
+// as many as fit up to TC_XSTMAX), then the packed-weight ring (INT4).
+static constexpr size_t TC_OPS_BYTES = 176 * 1024;
 static constexpr size_t TC_RING_BYTES = TC_OPS_BYTES + TC_PST * (size_t)TC_P_BYTES;
 static constexpr size_t TC_SMEM_BYTES = 1024 + TC_RING_BYTES + sizeof(TcSmem);
-__host__ __device__ inline int tc_op_stages(int fp16_w, int xmax) {
-    const size_t st = TC_A_BYTES + (size_t)xmax * TC_KS * 2;
-    const int n = (int)((fp16_w ? TC_RING_BYTES : TC_OPS_BYTES) / st);
-    return n < TC_OSTMAX ? n : TC_OSTMAX;
+__host__ __device__ inline int tc_x_stages(int xmax) {
+    const int n = (int)((TC_OPS_BYTES - (size_t)TC_NA * TC_A_BYTES) / ((size_t)xmax * TC_KS * 2));
+    return n < TC_XSTMAX ? n : TC_XSTMAX;
 }
 
 __device__ __forceinline__ void tc_tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -269,15 +272,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     extern __shared__ __align__(1024) unsigned char tc_raw[];
     const int KG = P.K / TC_KS;
     const int n_items = P.n_groups * P.tiles * P.splits;
-    const int ost = tc_op_stages(P.fp16_w, P.xmax);
+    const int nx = tc_x_stages(P.xmax);
     const int xatom = P.xmax * 128;  // bytes of one 64-K swizzle atom of activations
-    const size_t stage = TC_A_BYTES + 2 * (size_t)xatom;
 
     unsigned char* sm = tc_raw + ((1024 - (smem_u32(tc_raw) & 1023)) & 1023);
     unsigned char* PK = sm + TC_OPS_BYTES;  // INT4 only
     TcSmem* S = reinterpret_cast<TcSmem*>(sm + TC_RING_BYTES);
-    auto A_of = [&](int s) { return sm + (size_t)s * stage; };
-    auto X_of = [&](int s) { return sm + (size_t)s * stage + TC_A_BYTES; };
+    auto A_of = [&](int s) { return sm + (size_t)s * TC_A_BYTES; };
+    auto X_of = [&](int s) { return sm + (size_t)TC_NA * TC_A_BYTES + (size_t)s * 2 * xatom; };
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
@@ -285,10 +287,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&S->p_full[i], 1);
             mbar_init(&S->p_empty[i], TC_DQ_WARPS);
         }
-        for (int i = 0; i < TC_OSTMAX; i++) {
+        for (int i = 0; i < TC_NA; i++) {
             mbar_init(&S->a_full[i], P.fp16_w ? 1 : TC_DQ_WARPS);
+            mbar_init(&S->a_empty[i], 1);
+        }
+        for (int i = 0; i < TC_XSTMAX; i++) {
             mbar_init(&S->x_full[i], 1);
-            mbar_init(&S->op_empty[i], 1);
+            mbar_init(&S->x_empty[i], 1);
         }
         for (int i = 0; i < TC_NACC; i++) {
             mbar_init(&S->acc_full[i], 1);
@@ -318,8 +323,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---- weight producer ----
         const uint64_t pol = l2_policy_evict_first();
         // last copy issued per stage: the INT4 ring (TC_PST) or, for fp16
-        // weights, the operand stages (up to TC_OSTMAX)
-        constexpr int NLAST = TC_PST > TC_OSTMAX ? TC_PST : TC_OSTMAX;
+        // weights, the A stages (TC_NA)
+        constexpr int NLAST = TC_PST > TC_NA ? TC_PST : TC_NA;
         int last[NLAST];
         for (int s = 0; s < NLAST; s++) last[s] = -1;
         uint32_t pc = 0;
@@ -336,11 +341,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
             for (int i = 0; i < t.nk; i++, pc++) {
                 const int kg = t.kg(i);
-                const int s = P.fp16_w ? (int)(pc % ost) : (int)(pc % TC_PST);
+                const int s = P.fp16_w ? (int)(pc % TC_NA) : (int)(pc % TC_PST);
                 bool w = true;
                 if (lane == 0) {
                     if (P.fp16_w) {
-                        w = tc_wait(&S->op_empty[s], ((pc / ost) & 1) ^ 1, S, P.err, 10 + s, pc);
+                        w = tc_wait(&S->a_empty[s], ((pc / TC_NA) & 1) ^ 1, S, P.err, 10 + s, pc);
                         if (w) {
                             mbar_arrive_expect_tx(&S->a_full[s], TC_A_BYTES);
                             tc_tma_2d_hint(A_of(s), wm, kg * TC_KS, t.n0, &S->a_full[s], pol);
@@ -361,7 +366,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         // copies still in flight land before the CTA can exit
         if (lane == 0) {
-            const int depth = P.fp16_w ? ost : TC_PST;
+            const int depth = P.fp16_w ? TC_NA : TC_PST;
             for (int s = 0; s < depth; s++)
                 if (last[s] >= 0) tc_drain(P.fp16_w ? &S->a_full[s] : &S->p_full[s], (last[s] / depth) & 1, P.err);
         }
@@ -370,17 +375,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---- activation producer ----
         if (lane == 0) tc_prefetch_map(&xmap);
         pdl_wait();
-        int last[TC_OSTMAX] = {-1, -1, -1, -1};
+        int last[TC_XSTMAX];
+        for (int s = 0; s < TC_XSTMAX; s++) last[s] = -1;
         uint32_t oc = 0;
         bool ok = true;
         for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
             TcItem t;
             if (!tc_item(P, it, KG, t)) continue;
             for (int i = 0; i < t.nk; i++, oc++) {
-                const int s = oc % ost;
+                const int s = oc % nx;
                 bool w = true;
                 if (lane == 0) {
-                    w = tc_wait(&S->op_empty[s], ((oc / ost) & 1) ^ 1, S, P.err, 30 + s, oc);
+                    w = tc_wait(&S->x_empty[s], ((oc / nx) & 1) ^ 1, S, P.err, 30 + s, oc);
                     if (w) {
                         const int nb = (t.npad + P.xbox - 1) / P.xbox;
                         mbar_arrive_expect_tx(&S->x_full[s], (uint32_t)(nb * P.xbox) * TC_KS * 2);
@@ -397,8 +403,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
         }
         if (lane == 0)
-            for (int s = 0; s < ost; s++)
-                if (last[s] >= 0) tc_drain(&S->x_full[s], (last[s] / ost) & 1, P.err);
+            for (int s = 0; s < nx; s++)
+                if (last[s] >= 0) tc_drain(&S->x_full[s], (last[s] / nx) & 1, P.err);
         __syncwarp();
     } else if (warp == TC_DQ_WARPS + 2) {
         // ---- MMA issuer ----
@@ -417,12 +423,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 d = tmem + a3 * 128;
             }
             for (int i = 0; i < t.nk; i++, oc++) {
-                const int s = oc % ost;
-                const uint32_t ph = (oc / ost) & 1;
+                const int s = oc % TC_NA, sx = oc % nx;
+                const uint32_t ph = (oc / TC_NA) & 1, phx = (oc / nx) & 1;
                 const uint32_t a3 = ac % TC_NACC;
                 bool w = true;
                 if (lane == 0) {
-                    w = tc_wait(&S->a_full[s], ph, S, P.err, 50 + s, oc) && tc_wait(&S->x_full[s], ph, S, P.err, 60 + s, oc);
+                    w = tc_wait(&S->a_full[s], ph, S, P.err, 50 + s, oc) && tc_wait(&S->x_full[sx], phx, S, P.err, 60 + sx, oc);
                     // INT4: one accumulator per scale group, read back by the scale warps
                     if (w && !P.fp16_w) w = tc_wait(&S->acc_empty[a3], ((ac / TC_NACC) & 1) ^ 1, S, P.err, 70 + a3, ac);
                     if (w) {
@@ -433,10 +439,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         for (int kk = 0; kk < TC_KS / 16; kk++) {
                             const int off = (kk >> 2) * (TC_A_BYTES / 2) + (kk & 3) * 32;
                             const int xoff = (kk >> 2) * xatom + (kk & 3) * 32;
-                            tc_mma(d, tc_desc_sw128(A_of(s) + off), tc_desc_sw128(X_of(s) + xoff), idesc,
+                            tc_mma(d, tc_desc_sw128(A_of(s) + off), tc_desc_sw128(X_of(sx) + xoff), idesc,
                                    P.fp16_w ? (i | kk) != 0 : kk != 0);
                         }
-                        tc_commit(&S->op_empty[s]);
+                        tc_commit(&S->a_empty[s]);
+                        tc_commit(&S->x_empty[sx]);
                         if (!P.fp16_w) tc_commit(&S->acc_full[a3]);
                     }
                 }
@@ -469,8 +476,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const uint4 c1 = *reinterpret_cast<const uint4*>(row + (((2 * h + 1) ^ sw) << 4));
                     __syncwarp();
                     if (lane == 0) tc_arrive(&S->p_empty[s]);
-                    const int so = oc % ost;
-                    if (!(ok = tc_wait(&S->op_empty[so], ((oc / ost) & 1) ^ 1, S, P.err, 90 + so, oc))) break;
+                    const int so = oc % TC_NA;
+                    if (!(ok = tc_wait(&S->a_empty[so], ((oc / TC_NA) & 1) ^ 1, S, P.err, 90 + so, oc))) break;
                     unsigned char* dst = A_of(so) + h * (TC_A_BYTES / 2) + r * 128;
                     const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
