@@ -347,7 +347,7 @@ def moe_config2(layers=8):
     bpc = 4 * 5_677_056 + 131_072 + 64 + 4_096 + 8_192
     peak, kind = hbm_peak()
     gbps = bpc / (us * 1e-6) / 1e9
-    return {"kernels": "k_moe_up + k_moe_down", "shape": "H 2048, 32 experts, I 1792, top-4, batch 1",
+    return {"kernels": "k_moe_fused (cuinf_moe_ffn)", "shape": "H 2048, 32 experts, I 1792, top-4, batch 1",
             "us_per_layer": round(us, 3), "bytes_per_layer": bpc, "achieved": round(gbps, 1), "peak": peak,
             "unit": "GB/s", "frac": round(gbps / peak, 4), "peak_source": kind, "layers_rotated": layers}
 
