@@ -720,6 +720,95 @@ __global__ void k_bcombine(const float* __restrict__ obuf, const int* __restrict
     h[i] = __float2half_rn(__half2float(h[i]) + __half2float(acc));
 }
 
+// Residual add then the next RMSNorm, one CTA (256 threads) per sequence:
+// h = half(h + f) (add_inplace, engine.cu:532-535), then xn = half(h *
+// rsqrt(mean(h^2) + eps) * w) (rmsnorm, engine.cu:131-144).  Thread t takes
+// elements t, t+256, ... as the separate rmsnorm kernel does (same rounding
+// points and summation order); each round's loads are all issued first.
+#define BRN_PER 8
+__global__ void __launch_bounds__(256) k_bres_norm(__half* h, const float* __restrict__ f,
+                                                   const __half* __restrict__ w, __half* xn, int H, float eps) {
+    __shared__ float red[32];
+    __half* row = h + (size_t)blockIdx.x * H;
+    const float* fr = f + (size_t)blockIdx.x * H;
+    float ss = 0.f;
+    for (int base = 0; base < H; base += BRN_PER * 256) {
+        float hv[BRN_PER], fv[BRN_PER];
+#pragma unroll
+        for (int e = 0; e < BRN_PER; e++) {
+            const int i = base + e * 256 + (int)threadIdx.x;
+            hv[e] = i < H ? __half2float(row[i]) : 0.f;
+            fv[e] = i < H ? fr[i] : 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < BRN_PER; e++) {
+            const int i = base + e * 256 + (int)threadIdx.x;
+            if (i < H) {
+                const __half v = __float2half_rn(hv[e] + fv[e]);
+                row[i] = v;
+                const float x = __half2float(v);
+                ss += x * x;
+            }
+        }
+    }
+    ss = block_sum(ss, red);
+    const float inv = rsqrtf(ss / (float)H + eps);
+    for (int i = threadIdx.x; i < H; i += 256)
+        xn[(size_t)blockIdx.x * H + i] = __float2half_rn(__half2float(row[i]) * inv * __half2float(w[i]));
+}
+// The MoE combine (k_bcombine's arithmetic: acc = half(acc + w_t * o_t) in
+// slot order, then h = half(h + acc)) then the next RMSNorm, one CTA (256
+// threads) per sequence, the same element mapping as k_bres_norm.
+__global__ void __launch_bounds__(256) k_bcombine_norm(const float* __restrict__ obuf, const int* __restrict__ inv,
+                                                       const float* __restrict__ rw, __half* h, int H, int topk,
+                                                       EpWait wait, const __half* __restrict__ w, __half* xn,
+                                                       float eps) {
+    __shared__ float red[32];
+    if (wait.flags) {  // expert-parallel: the peers' outputs have arrived
+        if (threadIdx.x == 0) ep_wait_flags(wait);
+        __syncthreads();
+    }
+    const int b = blockIdx.x;
+    __half* row = h + (size_t)b * H;
+    const float* src[8];
+    float wt[8];
+#pragma unroll
+    for (int t = 0; t < 8; t++) {
+        src[t] = t < topk ? obuf + (size_t)inv[b * topk + t] * H : obuf;
+        wt[t] = t < topk ? rw[b * topk + t] : 0.f;
+    }
+    float ss = 0.f;
+    for (int base = 0; base < H; base += 4 * 256) {
+        float o[4][8], hv[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int c = base + e * 256 + (int)threadIdx.x;
+            hv[e] = c < H ? __half2float(row[c]) : 0.f;
+#pragma unroll
+            for (int t = 0; t < 8; t++)  // (L2 loads: rows another GPU may have written during the wait)
+                o[e][t] = (c < H && t < topk) ? __ldcg(src[t] + c) : 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int c = base + e * 256 + (int)threadIdx.x;
+            if (c < H) {
+                __half acc = __float2half_rn(0.f);
+#pragma unroll
+                for (int t = 0; t < 8; t++)
+                    if (t < topk) acc = __float2half_rn(__half2float(acc) + wt[t] * o[e][t]);
+                const __half v = __float2half_rn(hv[e] + __half2float(acc));
+                row[c] = v;
+                const float x = __half2float(v);
+                ss += x * x;
+            }
+        }
+    }
+    ss = block_sum(ss, red);
+    const float r = rsqrtf(ss / (float)H + eps);
+    for (int c = threadIdx.x; c < H; c += 256)
+        xn[(size_t)b * H + c] = __float2half_rn(__half2float(row[c]) * r * __half2float(w[c]));
+}
+
 __global__ void k_btok(const unsigned long long* __restrict__ keys, int* tok, int* pos, int B) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
@@ -1078,10 +1167,16 @@ static int batch_record(cuinf_batch* b, BStep& S) {
     BTRY(S.ew(run(cuinf_embed_gather(m->embed, b->tok, b->h, B, H, vs))));
     BTRY(S.mark("embed"));
     int moe_i = 0;
+    bool xn_ready = false;  // the previous layer's last kernel already normalised h
     for (int l = 0; l < c.n_layers; l++) {
         const LayerW& L = m->L[l];
-        BTRY(S.ew(run(cuinf_rmsnorm(b->h, L.op_norm, b->xn, B, H, c.norm_eps, vs))));
-        BTRY(S.mark("rmsnorm"));
+        // the RMSNorm that follows this layer's FFN: the next layer's, or the final one
+        const __half* next_norm = l + 1 < c.n_layers ? m->L[l + 1].op_norm : m->emb_norm;
+        if (!xn_ready) {
+            BTRY(S.ew(run(cuinf_rmsnorm(b->h, L.op_norm, b->xn, B, H, c.norm_eps, vs))));
+            BTRY(S.mark("rmsnorm"));
+        }
+        xn_ready = false;
         if (c.attn_layer[l]) {
             const AttnState& A = b->attn[l];
             float* qf = b->fqkv;  // q | k | v rows, converted together below
@@ -1147,10 +1242,12 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             BTRY(S.gemm1(b->x_conv, b->mi_out[l], L.out_proj.s, b->fa, H, H));
             BTRY(S.mark("gemm_conv_out"));
         }
-        BTRY(S.ew(run(cuinf_add_f32_inplace(b->h, b->fa, B * H, vs))));
-        BTRY(S.mark("residual"));
-        BTRY(S.ew(run(cuinf_rmsnorm(b->h, L.ffn_norm, b->xn, B, H, c.norm_eps, vs))));
-        BTRY(S.mark("rmsnorm"));
+        S.launches++;
+        if (!dry) {
+            k_bres_norm<<<B, 256, 0, b->st>>>(b->h, b->fa, L.ffn_norm, b->xn, H, c.norm_eps);
+            BTRY(cuinf_launch_status());
+            BTRY(S.mark("residual_norm"));
+        }
         if (l < c.n_dense) {
             const int I = c.dense_inter, tiles = (I + TC_ROWS - 1) / TC_ROWS;
             BTRY(S.gemm(b->x_h, (B + 15) & ~15, B, -1, b->dstatic + b->d13_tab[l], TcGroup{}, 2, tiles, H,
@@ -1160,8 +1257,13 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             BTRY(S.mark("swiglu"));
             BTRY(S.gemm1(b->x_dmid, b->mi_w2[l], L.w2.s, b->fa, H, I));
             BTRY(S.mark("gemm_dense_w2"));
-            BTRY(S.ew(run(cuinf_add_f32_inplace(b->h, b->fa, B * H, vs))));
-            BTRY(S.mark("residual"));
+            S.launches++;
+            if (!dry) {
+                k_bres_norm<<<B, 256, 0, b->st>>>(b->h, b->fa, next_norm, b->xn, H, c.norm_eps);
+                BTRY(cuinf_launch_status());
+                BTRY(S.mark("residual_norm"));
+            }
+            xn_ready = true;
         } else {
             const int I = c.moe_inter;
             const bool ep = b->ep_world > 1;
@@ -1341,16 +1443,20 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             }
             S.launches++;
             if (!dry) {
-                k_bcombine<<<(B * H + 255) / 256, 256, 0, b->st>>>(ob, oi, b->rw, b->h, B, H, K, cw);
+                k_bcombine_norm<<<B, 256, 0, b->st>>>(ob, oi, b->rw, b->h, H, K, cw, next_norm, b->xn, c.norm_eps);
                 BTRY(cuinf_launch_status());
-                BTRY(S.mark("combine"));
+                BTRY(S.mark("combine_norm"));
             }
+            xn_ready = true;
             moe_i++;
         }
     }
-    // final norm, lm_head with the fused argmax (compute_logits_last, engine.cu:932-940)
-    BTRY(S.ew(run(cuinf_rmsnorm(b->h, m->emb_norm, b->xn, B, H, c.norm_eps, vs))));
-    BTRY(S.mark("rmsnorm_final"));
+    // final norm (done by the last layer's closing kernel), lm_head with the
+    // fused argmax (compute_logits_last, engine.cu:932-940)
+    if (!xn_ready) {
+        BTRY(S.ew(run(cuinf_rmsnorm(b->h, m->emb_norm, b->xn, B, H, c.norm_eps, vs))));
+        BTRY(S.mark("rmsnorm_final"));
+    }
     if (b->vocab_shard && !b->keep_logits) {
         // every rank's final rows, then this rank's vocabulary shard for all
         // of them, then the max over the ranks' argmax keys (the keys order
