@@ -720,6 +720,50 @@ __global__ void k_bcombine(const float* __restrict__ obuf, const int* __restrict
     h[i] = __float2half_rn(__half2float(h[i]) + __half2float(acc));
 }
 
+// The attention prologue after the q/k/v GEMM, one CTA of 64 threads per
+// (sequence, head): fp32 -> fp16 of q, k and v; QK-RMSNorm of q and k
+// (engine.cu:146-158, as cuinf_rmsnorm over 64 dims: one element per thread,
+// the same block sum); RoPE of q and k at the sequence's position
+// (engine.cu:161-182, as cuinf_rope).  grid (B, nh + 2*nkv): y < nh query
+// heads, then key heads, then value heads (conversion only).
+__global__ void __launch_bounds__(64) k_bqkv_post(const float* __restrict__ qkv, __half* q16, __half* k16, __half* v16,
+                                                  const __half* __restrict__ qw, const __half* __restrict__ kw,
+                                                  const int* __restrict__ pos, int nh, int nkv, float eps,
+                                                  float theta) {
+    __shared__ float red[2];
+    __shared__ float y[CUINF_HD];
+    const int b = blockIdx.x, j = blockIdx.y, d = threadIdx.x, B = gridDim.x;
+    const size_t NQ = (size_t)nh * CUINF_HD, NK = (size_t)nkv * CUINF_HD;
+    const float* src;
+    __half* dst;
+    const __half* w;
+    if (j < nh) {
+        src = qkv + b * NQ + (size_t)j * CUINF_HD;
+        dst = q16 + b * NQ + (size_t)j * CUINF_HD;
+        w = qw;
+    } else if (j < nh + nkv) {
+        src = qkv + B * NQ + b * NK + (size_t)(j - nh) * CUINF_HD;
+        dst = k16 + b * NK + (size_t)(j - nh) * CUINF_HD;
+        w = kw;
+    } else {
+        const size_t o = b * NK + (size_t)(j - nh - nkv) * CUINF_HD;
+        v16[o + d] = __float2half_rn(qkv[B * (NQ + NK) + o + d]);
+        return;
+    }
+    const float x = __half2float(__float2half_rn(src[d]));
+    const float ss = block_sum(x * x, red);
+    const float inv = rsqrtf(ss / (float)CUINF_HD + eps);
+    y[d] = __half2float(__float2half_rn(x * inv * __half2float(w[d])));
+    __syncthreads();
+    if (d < CUINF_HD / 2) {
+        float cs, sn;
+        rope_pair_angle(pos[b], d, theta, cs, sn);
+        const float x0 = y[d], x1 = y[d + CUINF_HD / 2];
+        dst[d] = __float2half_rn(x0 * cs - x1 * sn);
+        dst[d + CUINF_HD / 2] = __float2half_rn(x1 * cs + x0 * sn);
+    }
+}
+
 // Residual add then the next RMSNorm, one CTA (256 threads) per sequence:
 // h = half(h + f) (add_inplace, engine.cu:532-535), then xn = half(h *
 // rsqrt(mean(h^2) + eps) * w) (rmsnorm, engine.cu:131-144).  Thread t takes
@@ -1188,14 +1232,13 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             BTRY(S.gemm(b->x_h, (B + 15) & ~15, B, -1, b->dstatic + b->qkv_tab[l], TcGroup{}, 3, tiles, H, active,
                         false, nullptr));
             BTRY(S.mark("gemm_qkv"));
-            BTRY(S.ew(run(cuinf_f32_to_f16(qf, q16, B * (NQ + 2 * NK), vs))));
-            BTRY(S.mark("f32_to_f16"));
-            BTRY(S.ew(run(cuinf_rmsnorm(q16, L.q_ln, q16, B * nh, 64, c.norm_eps, vs))));
-            BTRY(S.mark("rmsnorm_q"));
-            BTRY(S.ew(run(cuinf_rmsnorm(k16, L.k_ln, k16, B * nkv, 64, c.norm_eps, vs))));
-            BTRY(S.mark("rmsnorm_k"));
-            BTRY(S.ew(run(cuinf_rope(q16, k16, b->pos, B, nh, nkv, c.rope_theta, vs))));
-            BTRY(S.mark("rope"));
+            S.launches++;
+            if (!dry) {
+                k_bqkv_post<<<dim3(B, nh + 2 * nkv), CUINF_HD, 0, b->st>>>(qf, q16, k16, v16, L.q_ln, L.k_ln, b->pos, nh,
+                                                                        nkv, c.norm_eps, c.rope_theta);
+                BTRY(cuinf_launch_status());
+                BTRY(S.mark("qkv_norm_rope"));
+            }
             S.launches++;
             if (!dry) {
                 k_bkv_place<<<dim3(B, nkv), 256, 0, b->st>>>(k16, v16, b->pos, A.ktail, A.vtail, A.kc8, A.vc8, A.ksc,

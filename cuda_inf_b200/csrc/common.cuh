@@ -498,6 +498,14 @@ __device__ __forceinline__ void f16_tile_dot(const __half* __restrict__ W, int N
 // ---------------------------------------------------------------------------
 // reductions
 // ---------------------------------------------------------------------------
+// RoPE angle of rotation pair d at position pos (rope, engine.cu:161-182):
+// inv_freq = theta^(-2d/64), in float as the reference computes it.
+__device__ __forceinline__ void rope_pair_angle(int pos, int d, float theta, float& cs, float& sn) {
+    float invf = powf(theta, -(float)(2 * d) / (float)CUINF_HD);
+    float ang = (float)pos * invf;
+    cs = cosf(ang);
+    sn = sinf(ang);
+}
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

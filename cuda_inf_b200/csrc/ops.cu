@@ -208,12 +208,6 @@ extern "C" int cuinf_rmsnorm(const void* in, const void* w, void* out, int M, in
 // ---------------------------------------------------------------------------
 // RoPE (engine.cu:161-182): grid S, 32 threads (one per rotation pair)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void rope_pair_angle(int pos, int d, float theta, float& cs, float& sn) {
-    float invf = powf(theta, -(float)(2 * d) / (float)CUINF_HD);
-    float ang = (float)pos * invf;
-    cs = cosf(ang);
-    sn = sinf(ang);
-}
 
 __global__ void k_rope(__half* q, __half* k, const int* __restrict__ pos, int nq, int nk,
                        float theta) {
