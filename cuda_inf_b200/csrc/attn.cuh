@@ -225,8 +225,9 @@ __device__ __forceinline__ void attn_warp_units(const uint8_t* __restrict__ kc8,
     }
 }
 
-// MINB: CTAs per SM the register budget is cut for (1: no spills; 2: the
-// standalone operator, whose default split count assumes two CTAs per SM).
+// MINB: CTAs per SM the register budget is cut for (1: no spills, the
+// batch-1 engine; 2: the standalone operator, whose default split count
+// assumes two CTAs per SM, and the batched engine's many CTAs).
 template <int MINB>
 __global__ void __launch_bounds__(ATTN_THREADS, MINB) k_attn_decode(AttnParams P) {
     __shared__ __align__(16) float sm[ATTN_THREADS / 32][16][ATTN_PART_STRIDE];
