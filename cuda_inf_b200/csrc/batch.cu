@@ -558,6 +558,7 @@ struct BRouteParams {
     // source row = token); otherwise received rows (source row = entry)
     const int* keys;
     int n, n_local;  // entries; experts in the group tables (E, or E/world)
+    int rowcap;      // rows per group (TC_NMAX for the tensor-core GEMM; the small-row GEMV takes any)
     int group;       // 0: route only
     int* inv;   // [n] row of entry (-1: none)
     int* src;   // [rows] source row of each grouped row
@@ -583,8 +584,9 @@ __global__ void __launch_bounds__(256) k_broute_tokens(const float* __restrict__
 __device__ void bgroup_tables(const BRouteParams& P, const int* cnt, const int* off, int NE) {
     for (int ex = threadIdx.x; ex < NE; ex += blockDim.x) {
         for (int c = 0; c < P.maxch; c++) {
-            const int r0 = off[ex] + c * TC_NMAX;
-            const int rows = max(0, min(TC_NMAX, cnt[ex] - c * TC_NMAX));
+            const int cap = P.rowcap > 0 ? P.rowcap : TC_NMAX;
+            const int r0 = off[ex] + c * cap;
+            const int rows = max(0, min(cap, cnt[ex] - c * cap));
             const int gi = ex * P.maxch + c;
             TcGroup a;
             a.wmap = P.maps + ex * 3 + 0;
@@ -1312,7 +1314,10 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             const bool ep = b->ep_world > 1;
             const int EL = ep ? b->e_loc : E;           // experts in this rank's group tables
             const int NR = ep ? b->ep_world * b->cap : B * K;  // rows grouped here
-            const int mch = (NR + TC_NMAX - 1) / TC_NMAX;
+            // the small-row GEMV takes each expert's rows as one group (any count,
+            // in passes of 8); the tensor-core GEMM takes groups of TC_NMAX
+            const bool g8 = g8_fits(H, I);
+            const int mch = g8 ? 1 : (NR + TC_NMAX - 1) / TC_NMAX;
             BTRY(S.ew(run(cuinf_gemv_fp16(b->xn, L.gate, b->rlog, B, E, H, vs))));
             BTRY(S.mark("router_gemv"));
             BRouteParams R = {};
@@ -1324,6 +1329,7 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             R.I = I;
             R.H = H;
             R.maxch = mch;
+            R.rowcap = g8 ? NR : TC_NMAX;
             R.ridx = b->ridx + (size_t)moe_i * B * K;
             R.rw = b->rw;
             R.keys = nullptr;
@@ -1416,7 +1422,7 @@ static int batch_record(cuinf_batch* b, BStep& S) {
                 }
             }
             S.launches++;
-            if (g8_fits(H, I)) {
+            if (g8) {
                 // few rows per expert: the grouped small-row GEMV (k_grouped_gemv8)
                 S.launches++;
                 if (!dry) {
