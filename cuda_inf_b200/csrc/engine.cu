@@ -1125,7 +1125,7 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
                           {q4_range(L.wo, H, nh * 64)},
                           [=](const L2Ranges& nx, bool pdl) mutable {
                               R.next = nx;
-                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), one_per_sm(res_smem(nh * 64), H / 16, sms), st, pdl, R);
+                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(RES_WARPS * 32), one_per_sm(res_smem(nh * 64), H / 16, sms), st, pdl, R);
                           }});
         } else {
             ConvParams C;
@@ -1142,14 +1142,14 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
             Ls.push_back({"conv_in", q4_bytes(3 * H, H) + 18.0 * H, {q4_range(L.in_proj, 3 * H, H)},
                           [=](const L2Ranges& nx, bool pdl) mutable {
                               C.next = nx;
-                              return launch_k(k_conv_in, dim3(H / 16), dim3(384), one_per_sm(conv_smem(H), H / 16, sms), st, pdl, C);
+                              return launch_k(k_conv_in, dim3(H / 16), dim3(CONV_WARPS * 32), one_per_sm(conv_smem(H), H / 16, sms), st, pdl, C);
                           }});
             ResParams R;
             R.act = s->conv_y; R.wp = L.out_proj.p; R.ws = L.out_proj.s; R.h = s->h; R.N = H; R.K = H;
             Ls.push_back({"conv_out_proj", q4_bytes(H, H) + 6.0 * H, {q4_range(L.out_proj, H, H)},
                           [=](const L2Ranges& nx, bool pdl) mutable {
                               R.next = nx;
-                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), one_per_sm(res_smem(H), H / 16, sms), st, pdl, R);
+                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(RES_WARPS * 32), one_per_sm(res_smem(H), H / 16, sms), st, pdl, R);
                           }});
         }
         if (l < c.n_dense) {
@@ -1169,7 +1169,7 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
             Ls.push_back({"dense_down", q4_bytes(H, I) + 2.0 * I + 4.0 * H, {q4_range(L.w2, H, I)},
                           [=](const L2Ranges& nx, bool pdl) mutable {
                               R.next = nx;
-                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(256), one_per_sm(res_smem(I), H / 16, sms), st, pdl, R);
+                              return launch_k(k_gemv_residual, dim3(H / 16), dim3(RES_WARPS * 32), one_per_sm(res_smem(I), H / 16, sms), st, pdl, R);
                           }});
         } else {
             const int mi = L.moe_index;

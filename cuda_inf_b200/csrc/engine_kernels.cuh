@@ -309,11 +309,12 @@ struct ResParams {
     L2Ranges next;
 };
 
+#define RES_WARPS 16  // 16 warps per SM keep the mma.sync dot fed (8 warps reach ~3/4 of the pace)
 __host__ __device__ inline size_t res_smem(int K) {
-    return int4_tile_bytes(K) + (size_t)K * 2 + 8 * 16 * 4;
+    return int4_tile_bytes(K) + (size_t)K * 2 + RES_WARPS * 16 * 4;
 }
 
-__global__ void __launch_bounds__(256) k_gemv_residual(ResParams P) {
+__global__ void __launch_bounds__(RES_WARPS * 32) k_gemv_residual(ResParams P) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t bar;
     uint8_t* tile = smem;
@@ -335,14 +336,14 @@ __global__ void __launch_bounds__(256) k_gemv_residual(ResParams P) {
     PHASE(PH_RES, 2);
     float y0 = 0.f, y1 = 0.f;
     if (stage_wait(&bar))
-        int4_tile_dot_smem<2>(tile, P.K, warp, P.K >> 7, 8, reinterpret_cast<const uint2*>(xB), y0, y1);
+        int4_tile_dot_smem<2>(tile, P.K, warp, P.K >> 7, RES_WARPS, reinterpret_cast<const uint2*>(xB), y0, y1);
     warp_partials(red, warp, y0, y1);
     __syncthreads();
     PHASE(PH_RES, 4);
     if (threadIdx.x < 16) {
         float s = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; w++) s += red[w * 16 + threadIdx.x];
+        for (int w = 0; w < RES_WARPS; w++) s += red[w * 16 + threadIdx.x];
         const int n = row0 + threadIdx.x;
         if (n < P.N) P.h[n] = __float2half_rn(__half2float(P.h[n]) + s);
     }
@@ -352,7 +353,7 @@ __global__ void __launch_bounds__(256) k_gemv_residual(ResParams P) {
 // ---------------------------------------------------------------------------
 // Short-conv layer input: in_proj rows {c, H+c, 2H+c} for 16 channels
 // (B | C | x, engine.cu:861), then conv_pre/conv_apply/conv_update_state
-// (engine.cu:483-525) in the epilogue.  12 warps: 4 per row tile.
+// (engine.cu:483-525) in the epilogue.  24 warps: 8 per row tile.
 // ---------------------------------------------------------------------------
 struct ConvParams {
     const __half* h;
@@ -370,20 +371,21 @@ struct ConvParams {
     L2Ranges next;
 };
 
+#define CONV_WARPS 24
 __host__ __device__ inline size_t conv_smem(int H) {
-    return 3 * (size_t)int4_tile_bytes(H) + (size_t)H * 4 + (192 + 32) * 4;
+    return 3 * (size_t)int4_tile_bytes(H) + (size_t)H * 4 + (CONV_WARPS * 16 + 32) * 4;
 }
 
-__global__ void __launch_bounds__(384) k_conv_in(ConvParams P) {
+__global__ void __launch_bounds__(CONV_WARPS * 32) k_conv_in(ConvParams P) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t bar;
     const uint32_t TB = int4_tile_bytes(P.H);
     uint8_t* tiles = smem;
     __half* xs = reinterpret_cast<__half*>(smem + 3 * TB);
     __half* xB = xs + P.H;
-    float* red = reinterpret_cast<float*>(xB + P.H);  // [12][16] + 32
+    float* red = reinterpret_cast<float*>(xB + P.H);  // [24][16] + 32
     const int warp = threadIdx.x >> 5;
-    const int tile = warp >> 2, c0 = blockIdx.x * 16;
+    const int tile = warp >> 3, c0 = blockIdx.x * 16;
     PHASE(PH_CONV, 0);
     stage_begin(&bar);
     if (threadIdx.x == 0) {
@@ -409,11 +411,11 @@ __global__ void __launch_bounds__(384) k_conv_in(ConvParams P) {
     pdl_trigger();
     pdl_wait();
     PHASE(PH_CONV, 1);
-    norm_prologue_fast(nw, P.h, P.embed, P.tok, P.h_store, P.H, P.eps, xs, xB, red + 192);
+    norm_prologue_fast(nw, P.h, P.embed, P.tok, P.h_store, P.H, P.eps, xs, xB, red + CONV_WARPS * 16);
     PHASE(PH_CONV, 2);
     float y0 = 0.f, y1 = 0.f;
     if (stage_wait(&bar))
-        int4_tile_dot_smem<2>(tiles + tile * TB, P.H, warp & 3, P.H >> 7, 4,
+        int4_tile_dot_smem<2>(tiles + tile * TB, P.H, warp & 7, P.H >> 7, 8,
                               reinterpret_cast<const uint2*>(xB), y0, y1);
     warp_partials(red, warp, y0, y1);
     __syncthreads();
@@ -422,9 +424,11 @@ __global__ void __launch_bounds__(384) k_conv_in(ConvParams P) {
         const int i = threadIdx.x, c = c0 + i;
         float v[3];
 #pragma unroll
-        for (int t = 0; t < 3; t++)
-            v[t] = red[(4 * t + 0) * 16 + i] + red[(4 * t + 1) * 16 + i] + red[(4 * t + 2) * 16 + i] +
-                   red[(4 * t + 3) * 16 + i];
+        for (int t = 0; t < 3; t++) {
+            v[t] = 0.f;
+#pragma unroll
+            for (int w = 0; w < 8; w++) v[t] += red[(8 * t + w) * 16 + i];
+        }
         const __half Cb = __float2half_rn(v[1]);
         const __half Bx = __float2half_rn(v[0] * v[2]);
         const float co = cs0 * cw0 + __half2float(cs1) * cw1 + __half2float(Bx) * cw2;
