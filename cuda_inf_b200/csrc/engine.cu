@@ -757,6 +757,8 @@ struct cuinf_session {
     int attn_cluster = 0;        // cluster size of the DSMEM split merge (0: not available)
     bool attn_use_cluster = true;  // CUINF_OPT_ATTN_CLUSTER
     bool prefetch = true;  // L2 prefetch plans (cross-kernel weight streaming)
+    int prefetch_mb = 12;     // CUINF_OPT_PREFETCH_MB: bytes a kernel prefetches for the next ones
+    int prefetch_ahead = 3;   // CUINF_OPT_PREFETCH_AHEAD: how many launches ahead it looks
     bool pdl = true;       // programmatic dependent launch between the step's kernels
     bool prefill = true;   // cuinf_generate prefills its prompt
     // persistent megakernel (one cooperative launch per step)
@@ -831,11 +833,11 @@ static std::pair<const char*, unsigned long long> q4_range(const Q4& w, int64_t 
     return {(const char*)w.p, (unsigned long long)(N * K / 2 + N * (K / 128) * 2)};
 }
 
-// Weight bytes a kernel prefetches for the kernels after it: each static
-// range is scheduled once, as early as the budget allows.
-static const unsigned long long kPrefetchBudget = 12ull << 20;
-
-static void plan_prefetch(const std::vector<Launch>& L, std::vector<L2Ranges>& plans) {
+// Weight bytes a kernel prefetches for the kernels after it (at most `budget`
+// bytes, from kernels at most `ahead` launches later): each static range is
+// scheduled once, as early as the budget allows.
+static void plan_prefetch(const std::vector<Launch>& L, std::vector<L2Ranges>& plans, unsigned long long budget,
+                          int ahead) {
     const int n = (int)L.size();
     plans.assign(n, L2Ranges());
     // (kernel, range) in execution order, wrapping once into the next step
@@ -850,9 +852,9 @@ static void plan_prefetch(const std::vector<Launch>& L, std::vector<L2Ranges>& p
         R.count = 0;
         while (next < q.size() && q[next].first <= i) { next++; off = 0; }  // too late
         unsigned long long acc = 0;
-        while (next < q.size() && R.count < 8 && acc < kPrefetchBudget && q[next].first <= i + 3) {
+        while (next < q.size() && R.count < 8 && acc < budget && q[next].first <= i + ahead) {
             const unsigned long long left = q[next].second.second - off;
-            unsigned long long len = std::min(left, kPrefetchBudget - acc);
+            unsigned long long len = std::min(left, budget - acc);
             len = (len + 15) & ~15ull;
             if (len > left) len = left;
             R.p[R.count] = q[next].second.first + off;
@@ -1250,7 +1252,7 @@ static int record_step(cuinf_session* s, Prof* prof = nullptr) {
                   }});
 
     std::vector<L2Ranges> plans;
-    if (s->prefetch) plan_prefetch(Ls, plans);
+    if (s->prefetch) plan_prefetch(Ls, plans, (unsigned long long)s->prefetch_mb << 20, s->prefetch_ahead);
     else plans.assign(Ls.size(), L2Ranges{{}, {}, 0});
     prof_mark(prof, st, "start", 0);
     for (size_t i = 0; i < Ls.size(); i++) {
@@ -1855,6 +1857,15 @@ extern "C" int cuinf_session_set_option(cuinf_session* s, int option, int value)
     if (option == CUINF_OPT_PREFILL) {  // host-side only, no graph rebuild
         s->prefill = value != 0;
         return CUINF_OK;
+    }
+    if (option == CUINF_OPT_PREFETCH_MB || option == CUINF_OPT_PREFETCH_AHEAD) {
+        REQUIRE(option == CUINF_OPT_PREFETCH_MB ? (value >= 1 && value <= 1024) : (value >= 1 && value <= 64),
+                "prefetch budget must be 1..1024 MB, look-ahead 1..64 launches");
+        int& f = option == CUINF_OPT_PREFETCH_MB ? s->prefetch_mb : s->prefetch_ahead;
+        if (f == value) return CUINF_OK;
+        CUINF_TRY(cudaStreamSynchronize(s->st));
+        f = value;
+        return build_graph(s);
     }
     bool* f = option == CUINF_OPT_PREFETCH ? &s->prefetch
             : option == CUINF_OPT_PDL      ? &s->pdl

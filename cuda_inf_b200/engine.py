@@ -145,7 +145,8 @@ class Session:
         check(lib().cuinf_generate(self._h, p, len(prompt), n_new, eos, o, ctypes.byref(n)))
         return list(o[:n.value])
 
-    OPT_PREFETCH, OPT_PDL, OPT_MEGAKERNEL, OPT_TRACE, OPT_PREFILL, OPT_ATTN_CLUSTER = 1, 2, 3, 4, 5, 6
+    (OPT_PREFETCH, OPT_PDL, OPT_MEGAKERNEL, OPT_TRACE, OPT_PREFILL, OPT_ATTN_CLUSTER,
+     OPT_PREFETCH_MB, OPT_PREFETCH_AHEAD) = 1, 2, 3, 4, 5, 6, 7, 8
     STAGE_KINDS = ("conv_in", "residual", "qkv", "attention", "dense_up", "moe_up", "moe_down",
                    "lm_head")
 

@@ -391,6 +391,12 @@ int cuinf_session_keep_logits(cuinf_session* s, int on);
  * through global memory with an atomic ticket.  Both use the same splits and
  * give the same results. */
 #define CUINF_OPT_ATTN_CLUSTER 6
+/* CUINF_OPT_PREFETCH_MB / CUINF_OPT_PREFETCH_AHEAD: the L2 prefetch plan of
+ * CUINF_OPT_PREFETCH: each kernel asks L2 for at most `value` MB (default 12,
+ * 1..1024) of the weights of the kernels at most `value` launches after it
+ * (default 3, 1..64).  Scheduling only: results do not change. */
+#define CUINF_OPT_PREFETCH_MB 7
+#define CUINF_OPT_PREFETCH_AHEAD 8
 /* 1 if this session's decode attention can merge over clusters. */
 int cuinf_session_attn_cluster(const cuinf_session* s);
 int cuinf_session_set_option(cuinf_session* s, int option, int value);

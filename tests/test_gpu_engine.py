@@ -66,10 +66,11 @@ def test_kernels_per_step(tiny):
     assert s.kernels_per_step == 1  # one persistent launch
 
 
-@pytest.mark.parametrize("opt", [(1, 0), (2, 0)])
+@pytest.mark.parametrize("opt", [(1, 0), (2, 0), (7, 48), (8, 6)])
 def test_engine_options_do_not_change_results(tiny, opt):
-    """On the multi-kernel path, turning the L2 prefetch plan or PDL off
-    changes scheduling only: results are bit-identical."""
+    """On the multi-kernel path, turning the L2 prefetch plan or PDL off, or
+    resizing the prefetch plan (budget, look-ahead), changes scheduling only:
+    results are bit-identical."""
     cfg, om, gm = tiny
     a = Session(gm, max_ctx=80)
     b = Session(gm, max_ctx=80)
