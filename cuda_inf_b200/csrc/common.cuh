@@ -337,6 +337,20 @@ __device__ __forceinline__ void build_xB_entry(const __half* x, __half* xB, int 
     o[2] = x[k + 1];
     o[3] = x[k + 5];
 }
+// Chunk i of x (elements 8i..8i+7, one 16-byte load; x 16-byte aligned)
+// into its two B-fragment entries: entry m = 2j and m = 2j+1 of quad c of
+// group G for 8i = 128G + 32c + 8j, the same layout build_xB_entry writes.
+__device__ __forceinline__ void build_xB_chunk(const __half* x, __half* xB, int i) {
+    const uint4 v = *reinterpret_cast<const uint4*>(x + 8 * i);
+    const __half* o = reinterpret_cast<const __half*>(&v);
+    const int G = i >> 4, c = (i >> 2) & 3, j = i & 3;
+    __half2* e0 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j) * 4 + c) * 4);
+    __half2* e1 = reinterpret_cast<__half2*>(xB + (size_t)((G * 8 + 2 * j + 1) * 4 + c) * 4);
+    e0[0] = __halves2half2(o[0], o[4]);
+    e0[1] = __halves2half2(o[1], o[5]);
+    e1[0] = __halves2half2(o[2], o[6]);
+    e1[1] = __halves2half2(o[3], o[7]);
+}
 // Same, reading x from shared memory with a float source.
 __device__ __forceinline__ void build_xB_entry_f(const float* x, __half* xB, int e) {
     int c = e & 3, m = (e >> 2) & 7, G = e >> 5;

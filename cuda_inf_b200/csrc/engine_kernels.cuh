@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(RES_WARPS * 32) k_gemv_residual(ResParams P) {
     pdl_trigger();
     pdl_wait();
     PHASE(PH_RES, 1);
-    for (int e = threadIdx.x; e < P.K / 4; e += blockDim.x) build_xB_entry(P.act, xB, e);
+    for (int i = threadIdx.x; i < P.K / 8; i += blockDim.x) build_xB_chunk(P.act, xB, i);
     __syncthreads();
     PHASE(PH_RES, 2);
     float y0 = 0.f, y1 = 0.f;

@@ -56,7 +56,7 @@ extern "C" const char* cuinf_version(void) { return "cuinf-b200 0.1 (sm_100a)"; 
 __global__ void __launch_bounds__(256) k_gemv_int4(const __half* __restrict__ x,
                                                    const uint8_t* __restrict__ packed,
                                                    const __half* __restrict__ scales,
-                                                   float* __restrict__ y, int N, int K, int use_tma) {
+                                                   float* __restrict__ y, int N, int K, int use_tma, int xvec) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t bar;
     const int m = blockIdx.y, row0 = blockIdx.x * 16;
@@ -75,7 +75,10 @@ __global__ void __launch_bounds__(256) k_gemv_int4(const __half* __restrict__ x,
     pdl_trigger();
     pdl_wait();
     const __half* xm = x + (size_t)m * K;
-    for (int e = threadIdx.x; e < K / 4; e += blockDim.x) build_xB_entry(xm, xB, e);
+    if (xvec)  // x 16-byte aligned: one 16-byte load per 8 elements
+        for (int i = threadIdx.x; i < K / 8; i += blockDim.x) build_xB_chunk(xm, xB, i);
+    else
+        for (int e = threadIdx.x; e < K / 4; e += blockDim.x) build_xB_entry(xm, xB, e);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float y0 = 0.f, y1 = 0.f;
@@ -109,6 +112,7 @@ extern "C" int cuinf_gemv_int4(const void* x, const uint8_t* packed, const void*
     REQUIRE(((uintptr_t)scales & 1) == 0 && ((uintptr_t)x & 1) == 0, "misaligned fp16 pointer");
     REQUIRE(M <= 65535, "M too large");
     const int use_tma = ((uintptr_t)scales & 15) == 0;
+    const int xvec = ((uintptr_t)x & 15) == 0;  // K % 128 == 0 keeps every row aligned too
     size_t smem = (size_t)K * 2 + 8 * 16 * 4 + (use_tma ? int4_tile_bytes(K) : 0);
     REQUIRE(smem <= 227 * 1024, "K too large");
     if (smem > 48 * 1024)
@@ -125,7 +129,7 @@ extern "C" int cuinf_gemv_int4(const void* x, const uint8_t* packed, const void*
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     CUINF_TRY(cudaLaunchKernelEx(&cfg, k_gemv_int4, (const __half*)x, packed, (const __half*)scales, y, N, K,
-                                 use_tma));
+                                 use_tma, xvec));
     return cuinf_launch_status();
 }
 
