@@ -614,33 +614,42 @@ __device__ void bgroup_tables(const BRouteParams& P, const int* cnt, const int* 
     }
 }
 __global__ void __launch_bounds__(1024) k_broute(const BRouteParams P) {
-    __shared__ int sidx[1024];
     __shared__ int cnt[256], off[256];
+    __shared__ int wcnt[32][256];  // per warp and expert: its entries, then their offset among the warps
     if (P.wait.flags) {
         if (threadIdx.x == 0) ep_wait_flags(P.wait);
         __syncthreads();
     }
     const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int n = P.keys ? P.n : P.B * P.topk, NE = P.keys ? P.n_local : P.E;
-    for (int e = threadIdx.x; e < NE; e += blockDim.x) cnt[e] = 0;
+    for (int i = threadIdx.x; i < 32 * NE; i += blockDim.x) wcnt[i / NE][i % NE] = 0;
     if (!P.keys && !P.routed)
         for (int b = warp; b < P.B; b += nw)
             route_select_warp(P.logits + (size_t)b * P.E, P.bias, P.E, P.topk, P.ridx + b * P.topk,
                               P.rw + b * P.topk);
     if (!P.group) return;
     __syncthreads();
-    // rank of entry j among the entries of its expert that come before it
-    int e = -1, rank = 0;
-    if (threadIdx.x < n) {
-        e = P.keys ? __ldcg(P.keys + threadIdx.x) : P.ridx[threadIdx.x];  // keys: written by peers (L2 loads)
-        sidx[threadIdx.x] = e;
+    // rank of entry j among the entries of its expert that come before it:
+    // the earlier lanes of its warp with the same expert (match), plus the
+    // entries of that expert in the earlier warps (prefix over the warps)
+    const int lane = threadIdx.x & 31;
+    int e = -1;
+    if (threadIdx.x < n) e = P.keys ? __ldcg(P.keys + threadIdx.x) : P.ridx[threadIdx.x];  // keys: written by peers
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    int rank = __popc(peers & ((1u << lane) - 1u));
+    if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(peers);
+    __syncthreads();
+    for (int x = threadIdx.x; x < NE; x += blockDim.x) {
+        int acc = 0;
+        for (int w = 0; w < nw; w++) {
+            const int v = wcnt[w][x];
+            wcnt[w][x] = acc;
+            acc += v;
+        }
+        cnt[x] = acc;
     }
     __syncthreads();
-    if (e >= 0) {
-        for (int j = 0; j < (int)threadIdx.x; j++) rank += sidx[j] == e;
-        atomicAdd(&cnt[e], 1);
-    }
-    __syncthreads();
+    if (e >= 0) rank += wcnt[warp][e];
     if (threadIdx.x < 32) {  // exclusive prefix over experts, one warp
         int carry = 0;
         for (int base = 0; base < NE; base += 32) {

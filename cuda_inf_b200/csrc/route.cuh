@@ -12,8 +12,9 @@ __device__ __forceinline__ float route_sigmoid(float z) {
 // selection below calls it from an unrolled loop.
 static __device__ __noinline__ float route_sigmoid_call(float z) { return route_sigmoid(z); }
 
-// One warp per token; n_exp <= 32*8.  idx/w receive the topk choices
-// (written by lane 0; w is normalised in place at the end).
+// One warp per token; n_exp <= 32*8, topk <= 32.  idx/w receive the topk
+// choices: lane t keeps slot t's expert and sigmoid in registers and writes
+// both once the sum is known (no read-back of w from global memory).
 __device__ __forceinline__ void route_select_warp(const float* logits, const __half* bias, int n_exp, int topk,
                                                   int* idx, float* w) {
     const int lane = threadIdx.x & 31;
@@ -31,6 +32,8 @@ __device__ __forceinline__ void route_select_warp(const float* logits, const __h
         }
     }
     float wsum = 0.f;  // summed in selection order, as the reference does
+    int my_idx = 0;
+    float my_w = 0.f;
 #pragma unroll 1
     for (int t = 0; t < topk; t++) {
         // max score, lowest index on ties (the reference scans e ascending with '>')
@@ -64,13 +67,15 @@ __device__ __forceinline__ void route_select_warp(const float* logits, const __h
             if (lane + 32 * j == be) { used[j] = true; sv = sig[j]; }
         sv = __shfl_sync(0xffffffffu, sv, be & 31);
         wsum += sv;
-        if (lane == 0) {
-            idx[t] = be;
-            w[t] = sv;
+        if (lane == t) {
+            my_idx = be;
+            my_w = sv;
         }
     }
-    if (lane == 0)
-        for (int t = 0; t < topk; t++) w[t] = w[t] / (wsum + 1e-6f);
+    if (lane < topk) {
+        idx[lane] = my_idx;
+        w[lane] = my_w / (wsum + 1e-6f);
+    }
     __syncwarp();
 }
 
