@@ -779,7 +779,9 @@ __global__ void __launch_bounds__(64) k_bqkv_post(const float* __restrict__ qkv,
 // h = half(h + f) (add_inplace, engine.cu:532-535), then xn = half(h *
 // rsqrt(mean(h^2) + eps) * w) (rmsnorm, engine.cu:131-144).  Thread t takes
 // elements t, t+256, ... as the separate rmsnorm kernel does (same rounding
-// points and summation order); each round's loads are all issued first.
+// points and summation order); each round's loads, the norm weights
+// included, are all issued first, and with H <= BRN_PER * 256 (one round)
+// the normalisation uses the values still in registers.
 #define BRN_PER 8
 __global__ void __launch_bounds__(256) k_bres_norm(__half* h, const float* __restrict__ f,
                                                    const __half* __restrict__ w, __half* xn, int H, float eps) {
@@ -787,6 +789,7 @@ __global__ void __launch_bounds__(256) k_bres_norm(__half* h, const float* __res
     __half* row = h + (size_t)blockIdx.x * H;
     const float* fr = f + (size_t)blockIdx.x * H;
     float ss = 0.f;
+    __half hn[BRN_PER], wv[BRN_PER];
     for (int base = 0; base < H; base += BRN_PER * 256) {
         float hv[BRN_PER], fv[BRN_PER];
 #pragma unroll
@@ -794,22 +797,31 @@ __global__ void __launch_bounds__(256) k_bres_norm(__half* h, const float* __res
             const int i = base + e * 256 + (int)threadIdx.x;
             hv[e] = i < H ? __half2float(row[i]) : 0.f;
             fv[e] = i < H ? fr[i] : 0.f;
+            wv[e] = i < H ? w[i] : __float2half_rn(0.f);
         }
 #pragma unroll
         for (int e = 0; e < BRN_PER; e++) {
             const int i = base + e * 256 + (int)threadIdx.x;
+            hn[e] = __float2half_rn(hv[e] + fv[e]);
             if (i < H) {
-                const __half v = __float2half_rn(hv[e] + fv[e]);
-                row[i] = v;
-                const float x = __half2float(v);
+                row[i] = hn[e];
+                const float x = __half2float(hn[e]);
                 ss += x * x;
             }
         }
     }
     ss = block_sum(ss, red);
     const float inv = rsqrtf(ss / (float)H + eps);
-    for (int i = threadIdx.x; i < H; i += 256)
-        xn[(size_t)blockIdx.x * H + i] = __float2half_rn(__half2float(row[i]) * inv * __half2float(w[i]));
+    if (H <= BRN_PER * 256) {
+#pragma unroll
+        for (int e = 0; e < BRN_PER; e++) {
+            const int i = e * 256 + (int)threadIdx.x;
+            if (i < H) xn[(size_t)blockIdx.x * H + i] = __float2half_rn(__half2float(hn[e]) * inv * __half2float(wv[e]));
+        }
+    } else {
+        for (int i = threadIdx.x; i < H; i += 256)
+            xn[(size_t)blockIdx.x * H + i] = __float2half_rn(__half2float(row[i]) * inv * __half2float(w[i]));
+    }
 }
 // The MoE combine (k_bcombine's arithmetic: acc = half(acc + w_t * o_t) in
 // slot order, then h = half(h + acc)) then the next RMSNorm, one CTA (256
@@ -833,6 +845,43 @@ __global__ void __launch_bounds__(256) k_bcombine_norm(const float* __restrict__
         wt[t] = t < topk ? rw[b * topk + t] : 0.f;
     }
     float ss = 0.f;
+    if (H <= 8 * 256) {
+        // every element of the thread in one round: all its loads (the norm
+        // weights included) issued together, the normalisation from registers
+        float o[8][8], hv[8];
+        __half wv[8], hn[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int c = e * 256 + (int)threadIdx.x;
+            hv[e] = c < H ? __half2float(row[c]) : 0.f;
+            wv[e] = c < H ? w[c] : __float2half_rn(0.f);
+#pragma unroll
+            for (int t = 0; t < 8; t++)  // (L2 loads: rows another GPU may have written during the wait)
+                o[e][t] = (c < H && t < topk) ? __ldcg(src[t] + c) : 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int c = e * 256 + (int)threadIdx.x;
+            __half acc = __float2half_rn(0.f);
+#pragma unroll
+            for (int t = 0; t < 8; t++)
+                if (t < topk) acc = __float2half_rn(__half2float(acc) + wt[t] * o[e][t]);
+            hn[e] = __float2half_rn(hv[e] + __half2float(acc));
+            if (c < H) {
+                row[c] = hn[e];
+                const float x = __half2float(hn[e]);
+                ss += x * x;
+            }
+        }
+        ss = block_sum(ss, red);
+        const float r = rsqrtf(ss / (float)H + eps);
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int c = e * 256 + (int)threadIdx.x;
+            if (c < H) xn[(size_t)b * H + c] = __float2half_rn(__half2float(hn[e]) * r * __half2float(wv[e]));
+        }
+        return;
+    }
     for (int base = 0; base < H; base += 4 * 256) {
         float o[4][8], hv[4];
 #pragma unroll
@@ -840,7 +889,7 @@ __global__ void __launch_bounds__(256) k_bcombine_norm(const float* __restrict__
             const int c = base + e * 256 + (int)threadIdx.x;
             hv[e] = c < H ? __half2float(row[c]) : 0.f;
 #pragma unroll
-            for (int t = 0; t < 8; t++)  // (L2 loads: rows another GPU may have written during the wait)
+            for (int t = 0; t < 8; t++)
                 o[e][t] = (c < H && t < topk) ? __ldcg(src[t] + c) : 0.f;
         }
 #pragma unroll
