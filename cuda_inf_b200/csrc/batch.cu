@@ -1025,8 +1025,11 @@ __host__ __device__ inline unsigned g8_pitch(int K) {
 __host__ __device__ inline size_t g8_smem(int K) {
     return (size_t)G8_TILES * int4_tile_bytes(K) + (size_t)8 * g8_pitch(K) + 8 * 16 * 8 * 4;
 }
+// xsrc (nullable): activation row of each grouped row (x holds the
+// ungrouped rows, so no gathered copy is needed); null: row = grouped row.
 __global__ void __launch_bounds__(256) k_grouped_gemv8(const TcGroup* __restrict__ groups, const __half* __restrict__ x,
-                                                       int ldx, int K, unsigned* err) {
+                                                       int ldx, int K, unsigned* err,
+                                                       const int* __restrict__ xsrc = nullptr) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t bar_w, bar_x;
     const TcGroup G = groups[blockIdx.y];
@@ -1052,8 +1055,13 @@ __global__ void __launch_bounds__(256) k_grouped_gemv8(const TcGroup* __restrict
             // this pass's activation rows (rows past np keep stale values: their
             // mma columns are independent of the others and are never stored)
             mbar_arrive_expect_tx(&bar_x, np * XB);
-            for (int r = 0; r < np; r++)
-                tma_load_1d(xs + r * XP, x + (size_t)(G.x_row + p0 + r) * ldx, XB, &bar_x);
+            int sr[8];
+#pragma unroll
+            for (int r = 0; r < 8; r++) {
+                const int gr = G.x_row + p0 + r;
+                sr[r] = r < np ? (xsrc ? xsrc[gr] : gr) : 0;
+            }
+            for (int r = 0; r < np; r++) tma_load_1d(xs + r * XP, x + (size_t)sr[r] * ldx, XB, &bar_x);
         }
         __syncthreads();  // barrier inits are visible before anyone waits
         if (pass == 0) ok = mbar_wait_bounded(&bar_w, 0, err);
@@ -1404,14 +1412,18 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             R.ubuf = b->fu;
             R.obuf = b->fo;
             if (!ep) {
-                S.launches += 2;
+                // (the small-row GEMV reads each grouped row straight from xn
+                // through src; the tensor-core GEMM's map wants a gathered copy)
+                S.launches += g8 ? 1 : 2;
                 if (!dry) {
                     k_broute<<<1, 1024, 0, b->st>>>(R);
                     BTRY(cuinf_launch_status());
                     BTRY(S.mark("route_group"));
-                    k_bgather<<<B * K, 256, 0, b->st>>>(b->xn, b->src, b->xg, H);
-                    BTRY(cuinf_launch_status());
-                    BTRY(S.mark("gather"));
+                    if (!g8) {
+                        k_bgather<<<B * K, 256, 0, b->st>>>(b->xn, b->src, b->xg, H);
+                        BTRY(cuinf_launch_status());
+                        BTRY(S.mark("gather"));
+                    }
                 }
             } else if (b->p2p) {
                 // route this rank's tokens, write each (token, slot) row into its
@@ -1485,7 +1497,7 @@ static int batch_record(cuinf_batch* b, BStep& S) {
                 S.launches++;
                 if (!dry) {
                     k_grouped_gemv8<<<dim3(I / (16 * G8_TILES), 2 * EL * mch), 256, g8_smem(H), b->st>>>(
-                        b->g13, b->xg, H, H, g_tc_err_ptr);
+                        b->g13, ep ? b->xg : b->xn, H, H, g_tc_err_ptr, ep ? nullptr : b->src);
                     BTRY(cuinf_launch_status());
                 }
                 BTRY(S.mark("gemv8_moe_w13"));
