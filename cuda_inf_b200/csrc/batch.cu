@@ -1025,25 +1025,42 @@ __host__ __device__ inline unsigned g8_pitch(int K) {
 __host__ __device__ inline size_t g8_smem(int K) {
     return (size_t)G8_TILES * int4_tile_bytes(K) + (size_t)8 * g8_pitch(K) + 8 * 16 * 8 * 4;
 }
+// SwiGLU of the expert's w1 and w3 outputs (swiglu, engine.cu:542-547), the
+// arithmetic of the standalone k_swiglu.
+__device__ __forceinline__ float g8_silu(float x) { return x / (1.f + __expf(-x)); }
 // xsrc (nullable): activation row of each grouped row (x holds the
 // ungrouped rows, so no gathered copy is needed); null: row = grouped row.
+// PAIR (the w1/w3 pass): CTA (x, y) takes rows [16x, 16x+16) of group y
+// (w1, tile 0) and of group y + npair (w3, tile 1), whose activation rows
+// are the same, and writes mid = half(silu(w1 . x) * (w3 . x)) at a row
+// pitch of ldm instead of the two fp32 outputs (each sum as without PAIR,
+// so mid is the same bits as the separate SwiGLU kernel's).
+template <bool PAIR>
 __global__ void __launch_bounds__(256) k_grouped_gemv8(const TcGroup* __restrict__ groups, const __half* __restrict__ x,
                                                        int ldx, int K, unsigned* err,
-                                                       const int* __restrict__ xsrc = nullptr) {
+                                                       const int* __restrict__ xsrc = nullptr, int npair = 0,
+                                                       __half* mid = nullptr, int ldm = 0) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ uint64_t bar_w, bar_x;
     const TcGroup G = groups[blockIdx.y];
-    const int rbase = blockIdx.x * 16 * G8_TILES;
+    const int rbase = blockIdx.x * 16 * (PAIR ? 1 : G8_TILES);
     if (G.rows <= 0 || rbase >= G.N) return;
     const uint32_t TB = int4_tile_bytes(K), XP = g8_pitch(K), XB = 2u * (uint32_t)K;
     uint8_t* xs = smem + G8_TILES * TB;                                              // [8][XP] x rows
     float* red = reinterpret_cast<float*>(smem + G8_TILES * TB + (size_t)8 * XP);  // [8][16][8]
-    const int ntile = min(G8_TILES, (G.N - rbase) / 16);
+    const int ntile = PAIR ? 2 : min(G8_TILES, (G.N - rbase) / 16);
     if (threadIdx.x == 0) {
         mbar_init(&bar_w, 1);
         mbar_init(&bar_x, 1);
         mbar_arrive_expect_tx(&bar_w, ntile * TB);
-        for (int t = 0; t < ntile; t++) tma_tile_int4(G.packed, G.scales, K, rbase + 16 * t, smem + t * TB, &bar_w);
+        if (PAIR) {
+            const TcGroup G3 = groups[blockIdx.y + npair];
+            tma_tile_int4(G.packed, G.scales, K, rbase, smem, &bar_w);
+            tma_tile_int4(G3.packed, G3.scales, K, rbase, smem + TB, &bar_w);
+        } else {
+            for (int t = 0; t < ntile; t++)
+                tma_tile_int4(G.packed, G.scales, K, rbase + 16 * t, smem + t * TB, &bar_w);
+        }
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const int tile = warp >> 2, q = warp & 3, KG = K >> 7, KH = K >> 1;
@@ -1105,13 +1122,27 @@ __global__ void __launch_bounds__(256) k_grouped_gemv8(const TcGroup* __restrict
         red[(warp * 16 + g + 8) * 8 + 2 * c] = acc[2];
         red[(warp * 16 + g + 8) * 8 + 2 * c + 1] = acc[3];
         __syncthreads();
-        for (int i = threadIdx.x; i < ntile * 128; i += blockDim.x) {
-            const int t = i >> 7, r = (i >> 3) & 15, tok = i & 7;
-            if (tok < np) {
-                float v = 0.f;
+        if (PAIR) {
+            if (threadIdx.x < 128) {
+                const int r = (threadIdx.x >> 3) & 15, tok = threadIdx.x & 7;
+                if (tok < np) {
+                    float gv = 0.f, uv = 0.f;
 #pragma unroll
-                for (int w = 0; w < 4; w++) v += red[((4 * t + w) * 16 + r) * 8 + tok];
-                G.y[(size_t)(p0 + tok) * G.ldy + rbase + 16 * t + r] = v;
+                    for (int w = 0; w < 4; w++) gv += red[(w * 16 + r) * 8 + tok];
+#pragma unroll
+                    for (int w = 0; w < 4; w++) uv += red[((4 + w) * 16 + r) * 8 + tok];
+                    mid[(size_t)(G.x_row + p0 + tok) * ldm + rbase + r] = __float2half_rn(g8_silu(gv) * uv);
+                }
+            }
+        } else {
+            for (int i = threadIdx.x; i < ntile * 128; i += blockDim.x) {
+                const int t = i >> 7, r = (i >> 3) & 15, tok = i & 7;
+                if (tok < np) {
+                    float v = 0.f;
+#pragma unroll
+                    for (int w = 0; w < 4; w++) v += red[((4 * t + w) * 16 + r) * 8 + tok];
+                    G.y[(size_t)(p0 + tok) * G.ldy + rbase + 16 * t + r] = v;
+                }
             }
         }
         __syncthreads();  // xs and red are refilled by the next pass
@@ -1126,9 +1157,12 @@ static bool g8_fits(int H, int I) {
            g8_smem(std::max(H, I)) <= G8_SMEM_MAX;
 }
 static int g8_attr_once() {
-    static cudaError_t e = cudaFuncSetAttribute(k_grouped_gemv8, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    static cudaError_t e = cudaFuncSetAttribute(k_grouped_gemv8<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 G8_SMEM_MAX);
     if (e != cudaSuccess) return cuinf_set_cuda_error(e);
+    static cudaError_t e1 = cudaFuncSetAttribute(k_grouped_gemv8<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 G8_SMEM_MAX);
+    if (e1 != cudaSuccess) return cuinf_set_cuda_error(e1);
     return CUINF_OK;
 }
 
@@ -1493,19 +1527,18 @@ static int batch_record(cuinf_batch* b, BStep& S) {
             }
             S.launches++;
             if (g8) {
-                // few rows per expert: the grouped small-row GEMV (k_grouped_gemv8)
+                // few rows per expert: the grouped small-row GEMV (k_grouped_gemv8),
+                // w1 and w3 of the same rows in one CTA with the SwiGLU applied there
                 S.launches++;
                 if (!dry) {
-                    k_grouped_gemv8<<<dim3(I / (16 * G8_TILES), 2 * EL * mch), 256, g8_smem(H), b->st>>>(
-                        b->g13, ep ? b->xg : b->xn, H, H, g_tc_err_ptr, ep ? nullptr : b->src);
+                    k_grouped_gemv8<true><<<dim3(I / 16, EL * mch), 256, g8_smem(H), b->st>>>(
+                        b->g13, ep ? b->xg : b->xn, H, H, g_tc_err_ptr, ep ? nullptr : b->src, EL * mch, b->mmid, I);
                     BTRY(cuinf_launch_status());
                 }
-                BTRY(S.mark("gemv8_moe_w13"));
-                BTRY(S.ew(run(cuinf_swiglu(b->fg, b->fu, b->mmid, NR * I, vs))));
-                BTRY(S.mark("swiglu_moe"));
+                BTRY(S.mark("gemv8_moe_w13_swiglu"));
                 S.launches++;
                 if (!dry) {
-                    k_grouped_gemv8<<<dim3(H / (16 * G8_TILES), EL * mch), 256, g8_smem(I), b->st>>>(
+                    k_grouped_gemv8<false><<<dim3(H / (16 * G8_TILES), EL * mch), 256, g8_smem(I), b->st>>>(
                         b->g2, b->mmid, I, I, g_tc_err_ptr);
                     BTRY(cuinf_launch_status());
                 }
