@@ -1530,7 +1530,6 @@ static int batch_record(cuinf_batch* b, BStep& S) {
                     BTRY(S.mark("ep_group"));
                 }
             }
-            S.launches++;
             if (g8) {
                 // few rows per expert: the grouped small-row GEMV (k_grouped_gemv8),
                 // w1 and w3 of the same rows in one CTA with the SwiGLU applied there
