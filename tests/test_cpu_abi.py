@@ -63,3 +63,14 @@ def test_product_does_not_use_oracle():
                 src = open(os.path.join(dp, f)).read()
                 assert "oracle" not in src.replace("oracle/", ""), f
                 assert "import oracle" not in src and "liboracle" not in src, f
+
+
+def test_session_option_constants_match_header():
+    """The Python mirror's option numbers are the header's CUINF_OPT_* values."""
+    from cuda_inf_b200.engine import Session
+    hdr = open(os.path.join(ROOT, "include", "cuinf.h")).read()
+    defs = {m.group(1): int(m.group(2)) for m in re.finditer(r"#define CUINF_(OPT_[A-Z_]+)\s+(\d+)", hdr)}
+    assert len(defs) >= 8
+    for name, value in defs.items():
+        assert getattr(Session, name) == value, name
+    assert len(set(defs.values())) == len(defs)  # no two options share a number
